@@ -1,0 +1,145 @@
+/*
+ * rdet — B200-native deterministic integer-weight transformer path.
+ *
+ * C ABI of the drop-in CUDA executor for casettek/raster-inference's det
+ * path.  A Rust executor `src/runtime/executors/cuda.rs` beside the
+ * reference's `native.rs` binds these symbols.  Every
+ * call returns an int32 status (RDET_OK or a negative RDET_E_* code); the
+ * message of the last failure on the calling thread is available from
+ * rdet_last_error().  No exception or panic crosses this boundary.  All
+ * results are bit-exact with the reference det path (det_num spec v1).
+ *
+ * Threading: one host thread drives one context at a time.
+ */
+#ifndef RDET_H_
+#define RDET_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RDET_OK 0
+#define RDET_NONE 1 /* commitment is None (reference returns Option::None) */
+#define RDET_E_INVALID (-1)
+#define RDET_E_IO (-2)
+#define RDET_E_FORMAT (-3)
+#define RDET_E_CUDA (-4)
+#define RDET_E_STATE (-5)
+#define RDET_E_RANGE (-6)
+#define RDET_E_OOM (-7)
+
+typedef struct rdet_ctx rdet_ctx;
+typedef struct rdet_seq rdet_seq;
+
+/* Options for rdet_open / rdet_open_synthetic. */
+typedef struct rdet_opts {
+  int32_t device;        /* CUDA device ordinal */
+  uint32_t max_prefill;  /* largest prompt per prefill call (workspace sizing); 0 -> 4096 */
+  uint32_t flags;        /* RDET_FLAG_* */
+} rdet_opts;
+#define RDET_FLAG_LAYER_COMMITMENTS 1u /* keep per-layer prefill commitments */
+
+typedef struct rdet_model_info {
+  uint32_t hidden_size, vocab_size, num_layers, num_heads, ple_dim, intermediate_size;
+  uint64_t weight_bytes; /* bytes of all weight tensors resident in HBM */
+} rdet_model_info;
+
+/* Buffers readable with rdet_read / rdet_commitment. */
+#define RDET_BUF_EMBEDDING 0    /* [S,H] embedded prompt of the last prefill */
+#define RDET_BUF_HIDDEN 1       /* [S,H] final hidden states (prefill) or [1,H] (decode) */
+#define RDET_BUF_LOGITS 2       /* [V] last logits */
+#define RDET_BUF_LAYER_OUTPUT 3 /* layer `layer` output of the last prefill ([S,H]) or decode ([1,H]) */
+#define RDET_BUF_KV 4           /* whole KV cache (commitment only) */
+#define RDET_BUF_KV_K 5         /* [rows,d] logical K rows of (layer, kv head = arg) */
+#define RDET_BUF_KV_V 6
+
+/* ---- model ---------------------------------------------------------------
+ * Replaces load_transformer_state_model_from_det_num_wgt_path
+ * (reference src/shared/model/gemma/io.rs:1043-1123): parses
+ * <model_dir>/config.json and the fail-closed detwgt v2 artifact
+ * <model_dir>/model.detwgt (io.rs:230-395) and uploads every tensor to HBM
+ * once. */
+int32_t rdet_open(const char* model_dir, const rdet_opts* opts, rdet_ctx** out);
+/* Seeded random-init model of a config (JSON text); weights are generated in
+ * HBM by the counter-based generator documented in detwgt.py, identical to
+ * the artifact that detwgt.write_synthetic_model writes.  width: 16 or 32. */
+int32_t rdet_open_synthetic(const char* config_json, uint64_t seed, int32_t width, const rdet_opts* opts,
+                            rdet_ctx** out);
+int32_t rdet_close(rdet_ctx* ctx);
+int32_t rdet_get_model_info(rdet_ctx* ctx, rdet_model_info* out);
+
+/* ---- sequences (TransformerDecodeState: per-layer KV cache in HBM) --------
+ * Replaces TransformerDecodeState / LayerKvCache (model/transformer.rs:278-399). */
+int32_t rdet_seq_new(rdet_ctx* ctx, uint32_t max_ctx, rdet_seq** out);
+int32_t rdet_seq_free(rdet_seq* seq);
+int32_t rdet_seq_position(rdet_seq* seq, uint32_t* position);
+
+/* ---- routines ---------------------------------------------------------------
+ * input.embedding (src/routines/input_embedding/mod.rs:17; io.rs:2446-2518). */
+int32_t rdet_embed(rdet_ctx* ctx, const uint32_t* ids, size_t n, int32_t* act_out);
+
+/* prefill_layer: input.embedding + prefill.prepare_aux + prefill.range over all
+ * layers + prefill.finalize (native.rs:153-257 ->
+ * prefill_range/native/deterministic_tiles.rs:69-199,
+ * prefill_finalize/native/tiles.rs:11-107).  Logits stay resident. */
+int32_t rdet_prefill(rdet_ctx* ctx, rdet_seq* seq, const uint32_t* ids, size_t n);
+/* Routine-granular prefill: begin (embedding + PLE inputs), range over
+ * [layer_start, layer_end), finalize (final norm, lm_head, softcap). */
+int32_t rdet_prefill_begin(rdet_ctx* ctx, rdet_seq* seq, const uint32_t* ids, size_t n);
+int32_t rdet_prefill_range(rdet_ctx* ctx, rdet_seq* seq, uint32_t layer_start, uint32_t layer_end);
+int32_t rdet_prefill_finalize(rdet_ctx* ctx, rdet_seq* seq);
+
+/* select_output_token: argmax_first over the resident logits, lowest index on
+ * ties (decode_select_token/native/tiles.rs:22-38, det_num/ops.rs:463). */
+int32_t rdet_select(rdet_ctx* ctx, rdet_seq* seq, uint32_t* token_out);
+
+/* decode_transition for a (ragged) batch: for each sequence, embed its token
+ * at its own position, run every layer (appending to its KV cache) and
+ * project to logits (decode_layer_range/native/tiles.rs:133-197,
+ * decode_transition_finalize/native/tiles.rs:9-65). */
+int32_t rdet_decode(rdet_ctx* ctx, rdet_seq* const* seqs, const uint32_t* tokens, size_t nseq);
+/* Routine-granular decode for one sequence (decode_layer_range init_state /
+ * run_range / decode_transition_finalize). */
+int32_t rdet_decode_begin(rdet_ctx* ctx, rdet_seq* seq, uint32_t token);
+int32_t rdet_decode_range(rdet_ctx* ctx, rdet_seq* seq, uint32_t layer_start, uint32_t layer_end);
+int32_t rdet_decode_finalize(rdet_ctx* ctx, rdet_seq* seq);
+
+/* Greedy generation on the device (native.rs:265-450 loop: select ->
+ * decode_transition), replayed as one CUDA graph per token.  Writes
+ * n_tokens selected ids; the last selected token is not decoded. */
+int32_t rdet_generate(rdet_ctx* ctx, rdet_seq* seq, uint32_t n_tokens, uint32_t* tokens_out);
+
+/* ---- canonical bytes and commitments ----------------------------------------
+ * rdet_read copies the canonical little-endian i32 values of a buffer into
+ * dst (up to `bytes`) and reports the full size in *size_out.
+ * rdet_commitment computes the reference's SHA-256 det commitment
+ * (transformer_kernels.rs:1395-1482) as 64 lowercase hex chars + NUL:
+ *   EMBEDDING, HIDDEN, LAYER_OUTPUT: build_det_activation_commitment (rows)
+ *   LOGITS: build_det_vector_commitment
+ *   KV: build_det_kv_cache_commitment; returns RDET_NONE when a layer has no
+ *       cache of its own (KV-sharing layers), like the reference's None. */
+int32_t rdet_read(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t layer, int32_t arg, void* dst, size_t bytes,
+                  size_t* size_out);
+int32_t rdet_commitment(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t layer, char* hex_out);
+
+/* ---- kernel-level entry points on caller-owned device memory -----------------
+ * det GEMV / linear: y[s, r] = requantize(sum_k x[s, k] * w[r, k]) with exact
+ * wrapping i64 accumulation (det_kernels.rs:108-203 det_linear_rows_into /
+ * det_linear_slab).  w is row-major [rows, cols], i16 (width 16) or i32
+ * (width 32).  stream: a cudaStream_t or NULL. */
+int32_t rdet_det_gemv(const int32_t* x, const void* w, int32_t width, uint32_t rows, uint32_t cols, int32_t* y,
+                      void* stream);
+int32_t rdet_det_linear(const int32_t* x, uint32_t n_rows_x, const void* w, int32_t width, uint32_t rows,
+                        uint32_t cols, int32_t* y, void* stream);
+
+int32_t rdet_last_error(char* buf, size_t len);
+const char* rdet_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RDET_H_ */

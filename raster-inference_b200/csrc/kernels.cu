@@ -1,0 +1,814 @@
+// det kernels for B200 (sm_100a): GEMV, CUDA-core linear, norms, RoPE,
+// attention, embedding, PLE, argmax.  Every kernel computes the reference
+// det_num v1 arithmetic exactly (see det_dev.cuh); integer MAC reductions are
+// split across lanes/warps/CTAs freely because wrapping i64 addition is
+// associative (reference docs/plans/DET_NUM_SPEC.md, "Parallelism legality").
+#include <cstdio>
+
+#include "det_dev.cuh"
+#include "kernels.h"
+
+namespace rdet {
+
+static int g_sms = 0;
+int sm_count() {
+  if (g_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_sms <= 0) g_sms = 148;
+  }
+  return g_sms;
+}
+
+// ---------------------------------------------------------------------------
+// block reductions
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int64_t warp_sum64(int64_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+// saturating sum of non-negative i64 terms (order-free: min(true sum, MAX))
+__device__ __forceinline__ uint64_t sat_add_u(uint64_t a, uint64_t b) {
+  uint64_t s = a + b;
+  return (s < a || s > (uint64_t)INT64_MAX) ? (uint64_t)INT64_MAX : s;
+}
+__device__ __forceinline__ uint64_t warp_satsum(uint64_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = sat_add_u(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// rms_norm_scale (ops.rs:406) of n values in shared memory, computed by the
+// whole block; every thread gets the scale.  `red` is >= 33 u64 of smem.
+__device__ int32_t block_norm_scale(const int32_t* xs, int n, int64_t eps, uint64_t* red) {
+  uint64_t s = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    int64_t v = xs[i];
+    s = sat_add_u(s, (uint64_t)(v * v));
+  }
+  s = warp_satsum(s);
+  int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t t = 0;
+    for (int i = 0; i < nw; ++i) t = sat_add_u(t, red[i]);
+    int64_t mean = div_acc_by_u32((int64_t)t, (uint32_t)n);
+    red[32] = (uint64_t)(uint32_t)inv_sqrt_acc(acc_add_sat(mean, eps));
+  }
+  __syncthreads();
+  return (int32_t)(uint32_t)red[32];
+}
+// same for one warp over n values (lane-strided); returns scale to all lanes
+__device__ int32_t warp_norm_scale(const int32_t* xs, int n, int64_t eps) {
+  uint64_t s = 0;
+  for (int i = threadIdx.x & 31; i < n; i += 32) {
+    int64_t v = xs[i];
+    s = sat_add_u(s, (uint64_t)(v * v));
+  }
+  s = warp_satsum(s);
+  int32_t sc = 0;
+  if ((threadIdx.x & 31) == 0) sc = inv_sqrt_acc(acc_add_sat(div_acc_by_u32((int64_t)s, (uint32_t)n), eps));
+  return __shfl_sync(0xffffffffu, sc, 0);
+}
+
+// ---------------------------------------------------------------------------
+// decode GEMV
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int32_t lo16(uint32_t w) { return (int32_t)(int16_t)(w & 0xffffu); }
+__device__ __forceinline__ int32_t hi16(uint32_t w) { return ((int32_t)w) >> 16; }
+
+__device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// dot of one weight row with xs (smem), warp-cooperative, returns the full
+// wrapping i64 sum on every lane.
+template <int UNR>
+__device__ __forceinline__ int64_t row_dot16(const int16_t* row, const int32_t* xs, int K, int lane) {
+  int64_t acc = 0;
+  if ((K & 7) == 0) {
+    const uint4* wr = reinterpret_cast<const uint4*>(row);
+    int nc = K >> 3;
+    for (int c0 = lane; c0 < nc; c0 += 32 * UNR) {
+      uint4 w[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        int c = c0 + 32 * u;
+        w[u] = c < nc ? ldg_stream(wr + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        int c = c0 + 32 * u;
+        if (c < nc) {
+          const int4* xp = reinterpret_cast<const int4*>(xs + 8 * c);
+          int4 a = xp[0], b = xp[1];
+          acc += (int64_t)a.x * lo16(w[u].x) + (int64_t)a.y * hi16(w[u].x);
+          acc += (int64_t)a.z * lo16(w[u].y) + (int64_t)a.w * hi16(w[u].y);
+          acc += (int64_t)b.x * lo16(w[u].z) + (int64_t)b.y * hi16(w[u].z);
+          acc += (int64_t)b.z * lo16(w[u].w) + (int64_t)b.w * hi16(w[u].w);
+        }
+      }
+    }
+  } else {
+    for (int k = lane; k < K; k += 32) acc += (int64_t)xs[k] * (int64_t)row[k];
+  }
+  return warp_sum64(acc);
+}
+template <int UNR>
+__device__ __forceinline__ int64_t row_dot32(const int32_t* row, const int32_t* xs, int K, int lane) {
+  int64_t acc = 0;
+  if ((K & 3) == 0) {
+    const uint4* wr = reinterpret_cast<const uint4*>(row);
+    int nc = K >> 2;
+    for (int c0 = lane; c0 < nc; c0 += 32 * UNR) {
+      uint4 w[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        int c = c0 + 32 * u;
+        w[u] = c < nc ? ldg_stream(wr + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        int c = c0 + 32 * u;
+        if (c < nc) {
+          int4 a = reinterpret_cast<const int4*>(xs)[c];
+          acc += (int64_t)a.x * (int32_t)w[u].x + (int64_t)a.y * (int32_t)w[u].y;
+          acc += (int64_t)a.z * (int32_t)w[u].z + (int64_t)a.w * (int32_t)w[u].w;
+        }
+      }
+    }
+  } else {
+    for (int k = lane; k < K; k += 32) acc += (int64_t)xs[k] * (int64_t)row[k];
+  }
+  return warp_sum64(acc);
+}
+__device__ __forceinline__ int64_t mat_row_dot(const DevMat& m, int r, const int32_t* xs, int K, int lane) {
+  if (m.width == 16) return row_dot16<8>(static_cast<const int16_t*>(m.p) + (size_t)r * K, xs, K, lane);
+  return row_dot32<8>(static_cast<const int32_t*>(m.p) + (size_t)r * K, xs, K, lane);
+}
+
+constexpr int kGemvThreads = 256;
+
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int32_t* xs = reinterpret_cast<int32_t*>(smem_raw);
+  __shared__ uint64_t red[33];
+  const int K = a.K;
+  // ---- prologue: build x in shared memory
+  for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = a.a[i];
+  __syncthreads();
+  if (a.pro != kProNone) {
+    int32_t sc = block_norm_scale(xs, K, a.eps, red);
+    if (a.pro == kProNorm) {
+      for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = mul_sat(mul_sat(xs[i], sc), a.g1[i]);
+    } else {
+      for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        int32_t t = add_sat(a.res[i], mul_sat(mul_sat(xs[i], sc), a.g1[i]));
+        if (a.has_scalar) t = mul_sat(t, a.scalar);
+        xs[i] = t;
+        if (blockIdx.x == 0 && a.t_out) a.t_out[i] = t;
+      }
+      __syncthreads();
+      if (a.pro == kProResNorm || a.pro == kProResScaleNorm) {
+        int32_t sc2 = block_norm_scale(xs, K, a.eps, red);
+        for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = mul_sat(mul_sat(xs[i], sc2), a.g2[i]);
+      }
+    }
+  }
+  __syncthreads();
+  // ---- rows
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  const int gw = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int nw = gridDim.x * warps;
+  if (a.pair_geglu) {
+    const int R = a.seg[0].w.rows;
+    for (int r = gw; r < R; r += nw) {
+      int64_t g = mat_row_dot(a.seg[0].w, r, xs, K, lane);
+      int64_t u = mat_row_dot(a.seg[1].w, r, xs, K, lane);
+      if (lane == 0) a.seg[0].y[r] = mul_sat(gelu_act(requantize(g)), requantize(u));
+    }
+    return;
+  }
+  int total = 0;
+  for (int s = 0; s < a.nseg; ++s) total += a.seg[s].w.rows;
+  for (int gr = gw; gr < total; gr += nw) {
+    int s = 0, r = gr;
+    while (r >= a.seg[s].w.rows) { r -= a.seg[s].w.rows; ++s; }
+    const GemvSeg& sg = a.seg[s];
+    int64_t acc = mat_row_dot(sg.w, r, xs, K, lane);
+    if (lane == 0) {
+      int32_t v = requantize(acc);
+      if (sg.epi == kEpiSoftcap) v = softcap_act(v, a.softcap);
+      else if (sg.epi == kEpiGeluMul) v = mul_sat(gelu_act(v), sg.vec[r]);
+      sg.y[r] = v;
+    }
+  }
+}
+
+void launch_gemv(const GemvArgs& a, cudaStream_t s) {
+  int rows = 0;
+  if (a.pair_geglu) rows = a.seg[0].w.rows;
+  else for (int i = 0; i < a.nseg; ++i) rows += a.seg[i].w.rows;
+  int warps = kGemvThreads / 32;
+  int blocks = (rows + warps - 1) / warps;
+  int cap = sm_count() * 4;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  size_t smem = (size_t)a.K * 4;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  gemv_kernel<<<blocks, kGemvThreads, smem, s>>>(a);
+}
+
+// ---------------------------------------------------------------------------
+// prefill linear on CUDA cores: Y[S,N] = requantize(X[S,K] W[N,K]^T)
+// 64x64 output tile, 256 threads, 4x4 i64 accumulators per thread.
+// ---------------------------------------------------------------------------
+constexpr int LT_BM = 64, LT_BN = 64, LT_BK = 32;
+
+template <bool PAIR>
+__global__ void __launch_bounds__(256) linear_kernel(const int32_t* __restrict__ X, int S, DevMat w, DevMat wu,
+                                                     int32_t* __restrict__ Y, int epi, const int32_t* __restrict__ vec) {
+  __shared__ int32_t xs[LT_BK][LT_BM + 1];
+  __shared__ int32_t ws[LT_BK][LT_BN + 1];
+  __shared__ int32_t us[PAIR ? LT_BK : 1][PAIR ? LT_BN + 1 : 1];
+  const int N = w.rows, K = w.cols;
+  const int s0 = blockIdx.y * LT_BM, n0 = blockIdx.x * LT_BN;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  int64_t acc[4][4] = {};
+  int64_t accu[PAIR ? 4 : 1][PAIR ? 4 : 1] = {};
+  for (int k0 = 0; k0 < K; k0 += LT_BK) {
+    for (int e = threadIdx.x; e < LT_BM * LT_BK; e += 256) {
+      int r = e / LT_BK, c = e % LT_BK;
+      int gs = s0 + r, gk = k0 + c;
+      xs[c][r] = (gs < S && gk < K) ? X[(size_t)gs * K + gk] : 0;
+      int gn = n0 + r;
+      int32_t wv = 0, uv = 0;
+      if (gn < N && gk < K) {
+        size_t off = (size_t)gn * K + gk;
+        wv = w.width == 16 ? (int32_t) static_cast<const int16_t*>(w.p)[off] : static_cast<const int32_t*>(w.p)[off];
+        if (PAIR) uv = wu.width == 16 ? (int32_t) static_cast<const int16_t*>(wu.p)[off] : static_cast<const int32_t*>(wu.p)[off];
+      }
+      ws[c][r] = wv;
+      if (PAIR) us[c][r] = uv;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int c = 0; c < LT_BK; ++c) {
+      int32_t xv[4], wv[4], uv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) { xv[i] = xs[c][ty + 16 * i]; wv[i] = ws[c][tx + 16 * i]; }
+      if (PAIR) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) uv[i] = us[c][tx + 16 * i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[i][j] += (int64_t)xv[i] * wv[j];
+          if (PAIR) accu[i][j] += (int64_t)xv[i] * uv[j];
+        }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int gs = s0 + ty + 16 * i, gn = n0 + tx + 16 * j;
+      if (gs < S && gn < N) {
+        int32_t v = requantize(acc[i][j]);
+        if (PAIR) v = mul_sat(gelu_act(v), requantize(accu[i][j]));
+        else if (epi == kEpiGeluMul) v = mul_sat(gelu_act(v), vec[(size_t)gs * N + gn]);
+        Y[(size_t)gs * N + gn] = v;
+      }
+    }
+}
+
+void launch_linear(const int32_t* X, int32_t S, const DevMat& w, int32_t* Y, int32_t epi, const int32_t* vec,
+                   cudaStream_t s) {
+  dim3 grid((w.rows + LT_BN - 1) / LT_BN, (S + LT_BM - 1) / LT_BM);
+  linear_kernel<false><<<grid, 256, 0, s>>>(X, S, w, w, Y, epi, vec);
+}
+void launch_linear_geglu(const int32_t* X, int32_t S, const DevMat& wg, const DevMat& wu, int32_t* Y,
+                         cudaStream_t s) {
+  dim3 grid((wg.rows + LT_BN - 1) / LT_BN, (S + LT_BM - 1) / LT_BM);
+  linear_kernel<true><<<grid, 256, 0, s>>>(X, S, wg, wu, Y, kEpiPlain, nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// row norms
+// ---------------------------------------------------------------------------
+__global__ void rmsnorm_rows_kernel(const int32_t* x, int n, const int32_t* g, int64_t eps, int32_t* y) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int32_t* xs = reinterpret_cast<int32_t*>(smem_raw);
+  __shared__ uint64_t red[33];
+  const int32_t* xr = x + (size_t)blockIdx.x * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = xr[i];
+  __syncthreads();
+  int32_t sc = block_norm_scale(xs, n, eps, red);
+  int32_t* yr = y + (size_t)blockIdx.x * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    int32_t v = mul_sat(xs[i], sc);
+    yr[i] = g ? mul_sat(v, g[i]) : v;
+  }
+}
+void launch_rmsnorm_rows(const int32_t* x, int32_t S, int32_t n, const int32_t* g, int64_t eps, int32_t* y,
+                         cudaStream_t s) {
+  size_t smem = (size_t)n * 4;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(rmsnorm_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  rmsnorm_rows_kernel<<<S, 256, smem, s>>>(x, n, g, eps, y);
+}
+
+__global__ void norm_residual_kernel(const int32_t* a, const int32_t* res, int n, const int32_t* g, int64_t eps,
+                                     bool has_scalar, int32_t scalar, int32_t* out) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int32_t* xs = reinterpret_cast<int32_t*>(smem_raw);
+  __shared__ uint64_t red[33];
+  size_t base = (size_t)blockIdx.x * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = a[base + i];
+  __syncthreads();
+  int32_t sc = block_norm_scale(xs, n, eps, red);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    int32_t t = add_sat(res[base + i], mul_sat(mul_sat(xs[i], sc), g[i]));
+    if (has_scalar) t = mul_sat(t, scalar);
+    out[base + i] = t;
+  }
+}
+void launch_norm_residual_rows(const int32_t* a, const int32_t* res, int32_t S, int32_t n, const int32_t* g,
+                               int64_t eps, bool has_scalar, int32_t scalar, int32_t* out, cudaStream_t s) {
+  size_t smem = (size_t)n * 4;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(norm_residual_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  norm_residual_kernel<<<S, 256, smem, s>>>(a, res, n, g, eps, has_scalar, scalar, out);
+}
+
+// ---------------------------------------------------------------------------
+// q/k head norms, RoPE, value norm, KV-cache write.  One block per (row, head).
+// ---------------------------------------------------------------------------
+__device__ void rope_inplace(int32_t* v, int rotary, const int64_t* inv_freq, uint32_t pos) {
+  if (rotary == 0 || pos == 0) return;
+  int half = rotary >> 1;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    int32_t c, s;
+    sin_cos_acc(pos_angle(pos, inv_freq[i]), &c, &s);
+    int32_t l = v[i], r = v[i + half];
+    v[i] = sub_sat(mul_sat(l, c), mul_sat(r, s));
+    v[i + half] = add_sat(mul_sat(r, c), mul_sat(l, s));
+  }
+}
+
+__global__ void qkv_post_kernel(const QkvPostArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int32_t* vs = reinterpret_cast<int32_t*>(smem_raw);
+  __shared__ uint64_t red[33];
+  const int s = blockIdx.x, head = blockIdx.y, d = a.d;
+  const uint32_t pos = (uint32_t)(*a.pos + s);
+  if (head < a.Hq) {
+    const int32_t* src = a.q_in + ((size_t)s * a.Hq + head) * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) vs[i] = src[i];
+    __syncthreads();
+    int32_t sc = block_norm_scale(vs, d, a.eps, red);
+    for (int i = threadIdx.x; i < d; i += blockDim.x) vs[i] = mul_sat(mul_sat(vs[i], sc), a.q_norm[i]);
+    __syncthreads();
+    rope_inplace(vs, a.rotary, a.inv_freq, pos);
+    __syncthreads();
+    int32_t* dst = a.q_out + ((size_t)s * a.Hq + head) * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) dst[i] = vs[i];
+    return;
+  }
+  if (!a.k_in) return;
+  const int h = head - a.Hq;
+  // K: head norm + RoPE
+  const int32_t* ks = a.k_in + ((size_t)s * a.Hkv + h) * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) vs[i] = ks[i];
+  __syncthreads();
+  int32_t sc = block_norm_scale(vs, d, a.eps, red);
+  for (int i = threadIdx.x; i < d; i += blockDim.x) vs[i] = mul_sat(mul_sat(vs[i], sc), a.k_norm[i]);
+  __syncthreads();
+  rope_inplace(vs, a.rotary, a.inv_freq, pos);
+  __syncthreads();
+  int32_t* kd = a.k_cache + ((size_t)h * a.cap + pos) * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) kd[i] = vs[i];
+  __syncthreads();
+  // V: weightless value norm of the raw projection
+  const int32_t* vsrc = a.v_in + ((size_t)s * a.Hkv + h) * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) vs[i] = vsrc[i];
+  __syncthreads();
+  int32_t sv = block_norm_scale(vs, d, a.eps, red);
+  int32_t* vd = a.v_cache + ((size_t)h * a.cap + pos) * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) vd[i] = mul_sat(vs[i], sv);
+}
+void launch_qkv_post(const QkvPostArgs& a, cudaStream_t s) {
+  dim3 grid(a.S, a.Hq + (a.k_in ? a.Hkv : 0));
+  qkv_post_kernel<<<grid, 128, (size_t)a.d * 4, s>>>(a);
+}
+
+// ---------------------------------------------------------------------------
+// decode attention: exact softmax in four grid-wide phases over splits of the
+// key window (attention_output_into, det_kernels.rs:340-367).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void decode_window(const AttnDecodeArgs& a, int* start, int* n) {
+  int len = *a.pos + 1;
+  int st = (a.window > 0 && len > a.window) ? len - a.window : 0;
+  *start = st;
+  *n = len - st;
+}
+
+// phase 1: scores for the G query heads of one KV head over one split.
+__global__ void attn_dec_scores(const AttnDecodeArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int32_t* qs = reinterpret_cast<int32_t*>(smem_raw);  // [G, d]
+  __shared__ int32_t wmax[8][8];
+  __shared__ int32_t widx[8][8];
+  const int kvh = blockIdx.x, split = blockIdx.y, d = a.d;
+  const int G = a.Hq / a.Hkv;
+  int start, n;
+  decode_window(a, &start, &n);
+  const int lo = split * a.rows_per_split, hi = min(n, lo + a.rows_per_split);
+  for (int i = threadIdx.x; i < G * d; i += blockDim.x) qs[i] = a.q[(size_t)kvh * G * d + i];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+  int32_t bm[8];
+  int32_t bi[8];
+  for (int g = 0; g < G; ++g) { bm[g] = INT32_MIN; bi[g] = INT32_MAX; }
+  for (int j = lo + warp; j < hi; j += nwarp) {
+    const int32_t* kr = a.k_cache + ((size_t)kvh * a.cap + start + j) * d;
+    int64_t acc[8];
+    for (int g = 0; g < G; ++g) acc[g] = 0;
+    for (int i = lane; i < d; i += 32) {
+      int64_t kv = kr[i];
+      for (int g = 0; g < G; ++g) acc[g] += kv * qs[g * d + i];
+    }
+    for (int g = 0; g < G; ++g) {
+      int32_t sc = requantize(warp_sum64(acc[g]));
+      if (lane == 0) a.sc.scores[(size_t)(kvh * G + g) * a.cap + j] = sc;
+      if (sc > bm[g]) { bm[g] = sc; bi[g] = j; }  // j increases: first max kept
+    }
+  }
+  if (lane == 0)
+    for (int g = 0; g < G; ++g) { wmax[warp][g] = bm[g]; widx[warp][g] = bi[g]; }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    int g = threadIdx.x;
+    int32_t m = INT32_MIN, mi = INT32_MAX;
+    for (int w = 0; w < nwarp; ++w) {
+      int32_t v = wmax[w][g], ix = widx[w][g];
+      if (ix == INT32_MAX) continue;
+      if (v > m || (v == m && ix < mi)) { m = v; mi = ix; }
+    }
+    size_t o = (size_t)(kvh * G + g) * a.sc.max_splits + split;
+    a.sc.pmax[o] = m;
+    a.sc.pidx[o] = mi;
+  }
+}
+
+__device__ __forceinline__ void global_max(const AttnDecodeArgs& a, int h, int nsplit, int32_t* m, int32_t* mi) {
+  int32_t bm = INT32_MIN, bi = INT32_MAX;
+  for (int s = 0; s < nsplit; ++s) {
+    size_t o = (size_t)h * a.sc.max_splits + s;
+    int32_t v = a.sc.pmax[o], ix = a.sc.pidx[o];
+    if (ix == INT32_MAX) continue;
+    if (v > bm || (v == bm && ix < bi)) { bm = v; bi = ix; }
+  }
+  *m = bm;
+  *mi = bi;
+}
+
+// phase 2: exp terms and partial sums
+__global__ void attn_dec_exp(const AttnDecodeArgs a) {
+  __shared__ int32_t gmax[8];
+  __shared__ uint64_t red[8][8];
+  const int kvh = blockIdx.x, split = blockIdx.y;
+  const int G = a.Hq / a.Hkv;
+  int start, n;
+  decode_window(a, &start, &n);
+  const int nsplit = (n + a.rows_per_split - 1) / a.rows_per_split;
+  const int lo = split * a.rows_per_split, hi = min(n, lo + a.rows_per_split);
+  if (threadIdx.x < G) {
+    int32_t m, mi;
+    global_max(a, kvh * G + threadIdx.x, nsplit, &m, &mi);
+    gmax[threadIdx.x] = m;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+  for (int g = 0; g < G; ++g) {
+    int h = kvh * G + g;
+    uint64_t s = 0;
+    for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) {
+      int64_t e = exp_term(a.sc.scores[(size_t)h * a.cap + j], gmax[g]);
+      a.sc.exps[(size_t)h * a.cap + j] = e;
+      s += (uint64_t)e;
+    }
+    s = (uint64_t)warp_sum64((int64_t)s);
+    if (lane == 0) red[warp][g] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    uint64_t t = 0;
+    for (int w = 0; w < nwarp; ++w) t += red[w][threadIdx.x];
+    a.sc.psum[(size_t)(kvh * G + threadIdx.x) * a.sc.max_splits + split] = (int64_t)t;
+  }
+}
+
+// phase 3: weights and partial weighted sums over V
+__global__ void attn_dec_wsum(const AttnDecodeArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int32_t* ws = reinterpret_cast<int32_t*>(smem_raw);  // [G, rows_per_split]
+  __shared__ int64_t tsum[8];
+  __shared__ int64_t red[8][8];
+  const int kvh = blockIdx.x, split = blockIdx.y, d = a.d;
+  const int G = a.Hq / a.Hkv, R = a.rows_per_split;
+  int start, n;
+  decode_window(a, &start, &n);
+  const int nsplit = (n + R - 1) / R;
+  const int lo = split * R, hi = min(n, lo + R);
+  if (threadIdx.x < G) {
+    int64_t t = 0;
+    for (int s = 0; s < nsplit; ++s) t += a.sc.psum[(size_t)(kvh * G + threadIdx.x) * a.sc.max_splits + s];
+    tsum[threadIdx.x] = t;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+  for (int g = 0; g < G; ++g) {
+    int h = kvh * G + g;
+    int64_t wsum = 0;
+    for (int j = lo + threadIdx.x; j < lo + R; j += blockDim.x) {
+      int32_t w = 0;
+      if (j < hi) w = softmax_weight(a.sc.exps[(size_t)h * a.cap + j], tsum[g]);
+      ws[g * R + (j - lo)] = w;
+      wsum += w;
+    }
+    wsum = warp_sum64(wsum);
+    if (lane == 0) red[warp][g] = wsum;
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    int64_t t = 0;
+    for (int w = 0; w < nwarp; ++w) t += red[w][threadIdx.x];
+    a.sc.pwsum[(size_t)(kvh * G + threadIdx.x) * a.sc.max_splits + split] = t;
+  }
+  // partial weighted sum: thread per dim, loop over rows
+  for (int dim = threadIdx.x; dim < d; dim += blockDim.x) {
+    int64_t acc[8];
+    for (int g = 0; g < G; ++g) acc[g] = 0;
+    for (int j = lo; j < hi; ++j) {
+      int64_t v = a.v_cache[((size_t)kvh * a.cap + start + j) * d + dim];
+      for (int g = 0; g < G; ++g) acc[g] += v * ws[g * R + (j - lo)];
+    }
+    for (int g = 0; g < G; ++g) a.sc.pacc[((size_t)(kvh * G + g) * a.sc.max_splits + split) * d + dim] = acc[g];
+  }
+}
+
+// phase 4: combine splits, residual to the first max, requantize.
+__global__ void attn_dec_final(const AttnDecodeArgs a) {
+  const int h = blockIdx.x, d = a.d, G = a.Hq / a.Hkv, kvh = h / G;
+  int start, n;
+  decode_window(a, &start, &n);
+  const int nsplit = (n + a.rows_per_split - 1) / a.rows_per_split;
+  __shared__ int32_t s_res, s_mi;
+  if (threadIdx.x == 0) {
+    int32_t m, mi;
+    global_max(a, h, nsplit, &m, &mi);
+    int64_t ws = 0;
+    for (int s = 0; s < nsplit; ++s) ws += a.sc.pwsum[(size_t)h * a.sc.max_splits + s];
+    int32_t wsum = ws > INT32_MAX ? INT32_MAX : (int32_t)ws;
+    s_res = sub_sat(kOneAct, wsum);
+    s_mi = mi;
+  }
+  __syncthreads();
+  for (int dim = threadIdx.x; dim < d; dim += blockDim.x) {
+    int64_t acc = 0;
+    for (int s = 0; s < nsplit; ++s) acc += a.sc.pacc[((size_t)h * a.sc.max_splits + s) * d + dim];
+    acc += (int64_t)a.v_cache[((size_t)kvh * a.cap + start + s_mi) * d + dim] * s_res;
+    a.out[(size_t)h * d + dim] = requantize(acc);
+  }
+}
+
+void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
+  const int G = a.Hq / a.Hkv;
+  dim3 grid(a.Hkv, a.sc.max_splits);
+  attn_dec_scores<<<grid, 256, (size_t)G * a.d * 4, s>>>(a);
+  attn_dec_exp<<<grid, 256, 0, s>>>(a);
+  attn_dec_wsum<<<grid, 256, (size_t)G * a.rows_per_split * 4, s>>>(a);
+  attn_dec_final<<<a.Hq, 256, 0, s>>>(a);
+}
+
+// ---------------------------------------------------------------------------
+// prefill attention (causal + optional sliding window), one block per
+// (head, query).  Scores live in global scratch rows of length `rowlen`.
+// ---------------------------------------------------------------------------
+__global__ void attn_prefill_kernel(const AttnPrefillArgs a, int rowlen) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int32_t* qs = reinterpret_cast<int32_t*>(smem_raw);
+  __shared__ int32_t wm[32], wi[32];
+  __shared__ uint64_t wr[32];
+  __shared__ int32_t s_max, s_mi, s_res;
+  __shared__ int64_t s_sum;
+  const int h = blockIdx.x, i = blockIdx.y, d = a.d;
+  const int G = a.Hq / a.Hkv, kvh = h / G;
+  const int start = (a.window > 0 && i + 1 > a.window) ? i + 1 - a.window : 0;
+  const int n = i + 1 - start;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+  for (int t = threadIdx.x; t < d; t += blockDim.x) qs[t] = a.q[((size_t)i * a.Hq + h) * d + t];
+  __syncthreads();
+  int32_t* sc = a.scores + ((size_t)h * a.S + i) * rowlen;
+  int64_t* ex = a.exps + ((size_t)h * a.S + i) * rowlen;
+  // scores + first max
+  int32_t bm = INT32_MIN, bi = INT32_MAX;
+  for (int j = warp; j < n; j += nwarp) {
+    const int32_t* kr = a.k_cache + ((size_t)kvh * a.cap + start + j) * d;
+    int64_t acc = 0;
+    for (int t = lane; t < d; t += 32) acc += (int64_t)kr[t] * qs[t];
+    int32_t v = requantize(warp_sum64(acc));
+    if (lane == 0) sc[j] = v;
+    if (v > bm) { bm = v; bi = j; }
+  }
+  if (lane == 0) { wm[warp] = bm; wi[warp] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int32_t m = INT32_MIN, mi = INT32_MAX;
+    for (int w = 0; w < nwarp; ++w) {
+      if (wi[w] == INT32_MAX) continue;
+      if (wm[w] > m || (wm[w] == m && wi[w] < mi)) { m = wm[w]; mi = wi[w]; }
+    }
+    s_max = m;
+    s_mi = mi;
+  }
+  __syncthreads();
+  // exp terms + sum
+  uint64_t sum = 0;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    int64_t e = exp_term(sc[j], s_max);
+    ex[j] = e;
+    sum += (uint64_t)e;
+  }
+  sum = (uint64_t)warp_sum64((int64_t)sum);
+  if (lane == 0) wr[warp] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t t = 0;
+    for (int w = 0; w < nwarp; ++w) t += wr[w];
+    s_sum = (int64_t)t;
+  }
+  __syncthreads();
+  // weights (stored over the scores) + weight sum
+  int64_t wsum = 0;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    int32_t w = softmax_weight(ex[j], s_sum);
+    sc[j] = w;
+    wsum += w;
+  }
+  wsum = warp_sum64(wsum);
+  if (lane == 0) wr[warp] = (uint64_t)wsum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t t = 0;
+    for (int w = 0; w < nwarp; ++w) t += (int64_t)wr[w];
+    s_res = sub_sat(kOneAct, t > INT32_MAX ? INT32_MAX : (int32_t)t);
+    sc[s_mi] = add_sat(sc[s_mi], s_res);
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < d; t += blockDim.x) {
+    int64_t acc = 0;
+    const int32_t* vb = a.v_cache + ((size_t)kvh * a.cap + start) * d + t;
+    for (int j = 0; j < n; ++j) acc += (int64_t)vb[(size_t)j * d] * sc[j];
+    a.out[((size_t)i * a.Hq + h) * d + t] = requantize(acc);
+  }
+}
+void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t s) {
+  int rowlen = a.window > 0 ? (a.window < a.S ? a.window : a.S) : a.S;
+  dim3 grid(a.Hq, a.S);
+  attn_prefill_kernel<<<grid, 256, (size_t)a.d * 4, s>>>(a, rowlen);
+}
+
+// ---------------------------------------------------------------------------
+// embedding gather (io.rs:2446-2518), PLE inputs (prefill_prepare_aux)
+// ---------------------------------------------------------------------------
+__global__ void embed_kernel(const uint32_t* ids, DevMat emb, int32_t scale, int32_t* out, int32_t* err) {
+  const int s = blockIdx.x, H = emb.cols;
+  uint32_t id = ids[s];
+  if (id >= (uint32_t)emb.rows) {
+    if (threadIdx.x == 0) atomicExch(err, 1);
+    return;
+  }
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    size_t off = (size_t)id * H + i;
+    int32_t v = emb.width == 16 ? (int32_t) static_cast<const int16_t*>(emb.p)[off] : static_cast<const int32_t*>(emb.p)[off];
+    out[(size_t)s * H + i] = mul_sat(v, scale);
+  }
+}
+void launch_embed(const uint32_t* ids, int32_t S, const DevMat& emb, int32_t scale, int32_t* out, int32_t* err,
+                  cudaStream_t s) {
+  embed_kernel<<<S, 256, 0, s>>>(ids, emb, scale, out, err);
+}
+
+__global__ void ple_kernel(const PleArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int32_t* vs = reinterpret_cast<int32_t*>(smem_raw);
+  __shared__ uint64_t red[33];
+  const int s = blockIdx.x, l = blockIdx.y, P = a.P;
+  uint32_t id = a.ids[s];
+  if (id >= (uint32_t)a.table.rows) {
+    if (threadIdx.x == 0) atomicExch(a.err, 1);
+    return;
+  }
+  const int32_t* pr = a.proj + (size_t)s * a.L * P + (size_t)l * P;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) vs[i] = mul_sat(pr[i], a.proj_scale);
+  __syncthreads();
+  int32_t sc = block_norm_scale(vs, P, a.eps, red);
+  int32_t* o = a.out + ((size_t)l * a.S + s) * P;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    int32_t nv = mul_sat(mul_sat(vs[i], sc), a.norm[i]);
+    size_t off = (size_t)id * a.table.cols + (size_t)l * P + i;
+    int32_t tv = a.table.width == 16 ? (int32_t) static_cast<const int16_t*>(a.table.p)[off]
+                                     : static_cast<const int32_t*>(a.table.p)[off];
+    o[i] = mul_sat(add_sat(mul_sat(tv, a.emb_scale), nv), a.in_scale);
+  }
+}
+void launch_ple(const PleArgs& a, cudaStream_t s) {
+  dim3 grid(a.S, a.L);
+  ple_kernel<<<grid, 128, (size_t)a.P * 4, s>>>(a);
+}
+
+// ---------------------------------------------------------------------------
+// argmax_first (ops.rs:463): larger value wins; ties keep the lower index
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void better(int32_t& v, int32_t& i, int32_t v2, int32_t i2) {
+  if (v2 > v || (v2 == v && i2 < i)) { v = v2; i = i2; }
+}
+__global__ void argmax_part_kernel(const int32_t* x, int n, int32_t* part) {
+  __shared__ int32_t sv[32], si[32];
+  int32_t bv = INT32_MIN, bi = INT32_MAX;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) better(bv, bi, x[j], j);
+  for (int o = 16; o > 0; o >>= 1) {
+    int32_t v2 = __shfl_xor_sync(0xffffffffu, bv, o), i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+    better(bv, bi, v2, i2);
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) better(bv, bi, sv[w], si[w]);
+    part[2 * blockIdx.x] = bv;
+    part[2 * blockIdx.x + 1] = bi;
+  }
+}
+__global__ void argmax_final_kernel(const int32_t* part, int blocks, uint32_t* idx) {
+  int32_t bv = INT32_MIN, bi = INT32_MAX;
+  for (int b = 0; b < blocks; ++b) better(bv, bi, part[2 * b], part[2 * b + 1]);
+  *idx = (uint32_t)bi;
+}
+void launch_argmax(const int32_t* x, int32_t n, int32_t* part, int32_t blocks, uint32_t* idx, cudaStream_t s) {
+  argmax_part_kernel<<<blocks, 256, 0, s>>>(x, n, part);
+  argmax_final_kernel<<<1, 1, 0, s>>>(part, blocks, idx);
+}
+__global__ void softcap_kernel(int32_t* x, int n, int32_t cap) {
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) x[j] = softcap_act(x[j], cap);
+}
+void launch_softcap(int32_t* x, int32_t n, int32_t cap, cudaStream_t s) {
+  softcap_kernel<<<(n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024, 256, 0, s>>>(x, n, cap);
+}
+
+// ---------------------------------------------------------------------------
+// misc
+// ---------------------------------------------------------------------------
+__global__ void add_i32_kernel(int32_t* p, int32_t v) { *p += v; }
+void launch_add_i32(int32_t* p, int32_t v, cudaStream_t s) { add_i32_kernel<<<1, 1, 0, s>>>(p, v); }
+void launch_copy_rows(const int32_t* src, int32_t* dst, size_t n, cudaStream_t s) {
+  cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToDevice, s);
+}
+
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+__global__ void synth_kernel(void* dst, int width, int rank, int64_t n, int64_t cols, uint64_t key) {
+  const uint64_t GOLD = 0x9E3779B97F4A7C15ull;
+  int64_t bound = cols > 0 ? (int64_t)(0x7fffffffLL / cols) : 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    uint64_t z = mix64(key + (uint64_t)(i + 1) * GOLD);
+    int32_t v;
+    if (rank == 1) v = 32768 + (int32_t)(z >> 48);
+    else if (width == 16) v = (int32_t)(z >> 48) - 32768;
+    else v = (int32_t)((int64_t)(z % (uint64_t)(2 * bound + 1)) - bound);
+    if (width == 16) static_cast<int16_t*>(dst)[i] = (int16_t)v;
+    else static_cast<int32_t*>(dst)[i] = v;
+  }
+}
+void launch_synth(void* dst, int32_t width, int32_t rank, int64_t n, int64_t cols, uint64_t key, cudaStream_t s) {
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 65536) blocks = 65536;
+  if (blocks < 1) blocks = 1;
+  synth_kernel<<<(unsigned)blocks, 256, 0, s>>>(dst, width, rank, n, cols, key);
+}
+
+}  // namespace rdet

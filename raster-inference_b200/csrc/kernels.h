@@ -1,0 +1,161 @@
+// Launch interface of the det kernels (sm_100a).  Host code in runtime.cu
+// composes these into the prefill / decode / select routines.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace rdet {
+
+enum WeightWidth : int32_t { kW16 = 16, kW32 = 32 };
+
+// A weight matrix resident in HBM: row-major [rows, cols], i16 or i32.
+struct DevMat {
+  const void* p = nullptr;
+  int32_t width = 16;
+  int32_t rows = 0, cols = 0;
+};
+
+// ---- decode GEMV -----------------------------------------------------------
+// Epilogues applied to requantize(dot) of output row r.
+enum GemvEpi : int32_t {
+  kEpiPlain = 0,      // y[r] = v
+  kEpiSoftcap = 1,    // y[r] = softcap(v, cap)
+  kEpiGeluMul = 2,    // y[r] = mul_sat(gelu(v), vec[r])
+};
+// Prologues that build the input vector x (length K) in shared memory.
+enum GemvPro : int32_t {
+  kProNone = 0,       // x = a
+  kProNorm = 1,       // x = rmsnorm(a, g1)
+  kProResNorm = 2,    // t = add_sat(res, rmsnorm(a, g1)); x = rmsnorm(t, g2); block 0 stores t
+  kProResScale = 3,   // t = scale?(add_sat(res, rmsnorm(a, g1))); x = t; block 0 stores t
+  kProResScaleNorm = 4,  // t as kProResScale; x = rmsnorm(t, g2); block 0 stores t
+};
+struct GemvSeg {
+  DevMat w;
+  int32_t* y = nullptr;
+  int32_t epi = kEpiPlain;
+  const int32_t* vec = nullptr;
+};
+struct GemvArgs {
+  int32_t K = 0;
+  int32_t nseg = 1;
+  GemvSeg seg[3];
+  bool pair_geglu = false;  // seg[0]=gate, seg[1]=up: seg[0].y[r] = mul_sat(gelu(g), u)
+  int32_t softcap = 0;
+  // prologue
+  int32_t pro = kProNone;
+  const int32_t* a = nullptr;
+  const int32_t* res = nullptr;
+  const int32_t* g1 = nullptr;
+  const int32_t* g2 = nullptr;
+  int64_t eps = 0;
+  int32_t scalar = 0;
+  bool has_scalar = false;
+  int32_t* t_out = nullptr;
+};
+void launch_gemv(const GemvArgs& a, cudaStream_t s);
+
+// ---- prefill linear (Y[S,N] = requantize(X[S,K] W^T)) -------------------------
+void launch_linear(const int32_t* X, int32_t S, const DevMat& w, int32_t* Y, int32_t epi, const int32_t* vec,
+                   cudaStream_t s);
+// geglu pair: Y = mul_sat(gelu(X Wg^T), X Wu^T)
+void launch_linear_geglu(const int32_t* X, int32_t S, const DevMat& wg, const DevMat& wu, int32_t* Y,
+                         cudaStream_t s);
+
+// ---- row ops -------------------------------------------------------------------
+// y[s] = rmsnorm(x[s], g)   (g == nullptr: weightless value norm)
+void launch_rmsnorm_rows(const int32_t* x, int32_t S, int32_t n, const int32_t* g, int64_t eps, int32_t* y,
+                         cudaStream_t s);
+// out[s] = scale?(add_sat(res[s], rmsnorm(a[s], g)))
+void launch_norm_residual_rows(const int32_t* a, const int32_t* res, int32_t S, int32_t n, const int32_t* g,
+                               int64_t eps, bool has_scalar, int32_t scalar, int32_t* out, cudaStream_t s);
+
+// ---- attention inputs -------------------------------------------------------------
+struct QkvPostArgs {
+  int32_t S = 1;              // rows (tokens)
+  const int32_t* pos = nullptr;  // device: position of row 0
+  int32_t Hq = 0, Hkv = 0, d = 0, rotary = 0;
+  const int64_t* inv_freq = nullptr;  // [rotary/2] Q32.32 recurrence table
+  const int32_t* q_in = nullptr;      // [S, Hq*d]
+  const int32_t* k_in = nullptr;      // [S, Hkv*d] raw K (nullptr: no own KV)
+  const int32_t* v_in = nullptr;      // [S, Hkv*d] raw V (== k_in for k_eq_v)
+  const int32_t* q_norm = nullptr;
+  const int32_t* k_norm = nullptr;
+  int64_t eps = 0;
+  int32_t* q_out = nullptr;           // [S, Hq*d]
+  int32_t* k_cache = nullptr;         // [Hkv, cap, d]
+  int32_t* v_cache = nullptr;
+  int32_t cap = 0;
+};
+void launch_qkv_post(const QkvPostArgs& a, cudaStream_t s);
+
+// ---- attention -----------------------------------------------------------------
+struct AttnScratch {
+  int32_t* scores = nullptr;  // [Hq, cap]
+  int64_t* exps = nullptr;    // [Hq, cap]
+  int32_t* pmax = nullptr;    // [Hq, nsplit]
+  int32_t* pidx = nullptr;    // [Hq, nsplit]
+  int64_t* psum = nullptr;    // [Hq, nsplit]
+  int64_t* pwsum = nullptr;   // [Hq, nsplit]
+  int64_t* pacc = nullptr;    // [Hq, nsplit, d]
+  int32_t max_splits = 0;
+};
+struct AttnDecodeArgs {
+  const int32_t* pos = nullptr;  // device: position of the current token
+  int32_t Hq = 0, Hkv = 0, d = 0;
+  int32_t window = 0;            // 0 = full attention
+  const int32_t* q = nullptr;    // [Hq, d]
+  const int32_t* k_cache = nullptr;
+  const int32_t* v_cache = nullptr;
+  int32_t cap = 0;
+  int32_t* out = nullptr;        // [Hq, d]
+  AttnScratch sc;
+  int32_t rows_per_split = 64;
+};
+void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s);
+
+struct AttnPrefillArgs {
+  int32_t S = 0;
+  int32_t Hq = 0, Hkv = 0, d = 0;
+  int32_t window = 0;            // 0 = full (causal)
+  const int32_t* q = nullptr;    // [S, Hq*d]
+  const int32_t* k_cache = nullptr;  // [Hkv, cap, d], rows 0..S-1
+  const int32_t* v_cache = nullptr;
+  int32_t cap = 0;
+  int32_t* out = nullptr;        // [S, Hq*d]
+  int32_t* scores = nullptr;     // scratch [Hq, S, S] (or window)
+  int64_t* exps = nullptr;       // scratch same count
+  int64_t scratch_elems = 0;
+};
+void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t s);
+
+// ---- embedding / PLE / logits ------------------------------------------------------
+void launch_embed(const uint32_t* ids, int32_t S, const DevMat& emb, int32_t scale, int32_t* out, int32_t* err,
+                  cudaStream_t s);
+struct PleArgs {
+  int32_t S = 0, L = 0, P = 0;
+  const uint32_t* ids = nullptr;
+  const int32_t* proj = nullptr;   // [S, L*P] = requantize(x0 Wproj^T)
+  DevMat table;                    // [ple_vocab, L*P]
+  const int32_t* norm = nullptr;   // [P]
+  int64_t eps = 0;
+  int32_t emb_scale = 0, proj_scale = 0, in_scale = 0;
+  int32_t* out = nullptr;          // [L, S, P]
+  int32_t* err = nullptr;
+};
+void launch_ple(const PleArgs& a, cudaStream_t s);
+
+// argmax_first over n values; result index written to *idx (u32).  `part`
+// holds at least 2*blocks ints of scratch.
+void launch_argmax(const int32_t* x, int32_t n, int32_t* part, int32_t blocks, uint32_t* idx, cudaStream_t s);
+void launch_softcap(int32_t* x, int32_t n, int32_t cap, cudaStream_t s);
+
+// ---- misc ---------------------------------------------------------------------------
+void launch_add_i32(int32_t* p, int32_t v, cudaStream_t s);  // *p += v
+void launch_copy_rows(const int32_t* src, int32_t* dst, size_t n, cudaStream_t s);
+// synthetic weights (counter-based generator, see detwgt.py)
+void launch_synth(void* dst, int32_t width, int32_t rank, int64_t n, int64_t cols, uint64_t key, cudaStream_t s);
+
+int sm_count();
+
+}  // namespace rdet

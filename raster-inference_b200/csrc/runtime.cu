@@ -1,0 +1,1568 @@
+// rdet runtime: model loading into HBM, per-sequence KV caches, and the
+// prefill / decode / select routines of the reference det path, composed
+// from the sm_100a kernels in kernels.cu.  Implements include/rdet.h.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "det_dev.cuh"
+#include "json.h"
+#include "kernels.h"
+#include "rdet.h"
+#include "sha256.h"
+
+namespace rdet {
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+struct Fail {
+  int code;
+  std::string msg;
+};
+static thread_local std::string g_last_error;
+
+#define CK(x)                                                                                     \
+  do {                                                                                            \
+    cudaError_t e_ = (x);                                                                         \
+    if (e_ != cudaSuccess) throw Fail{RDET_E_CUDA, std::string(#x) + ": " + cudaGetErrorString(e_)}; \
+  } while (0)
+#define REQUIRE(cond, code, msg) \
+  do {                           \
+    if (!(cond)) throw Fail{code, msg}; \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// host-side det conversions for load-time constants
+// (reference det_num/convert.rs:82-189, ops.rs:555-611)
+// ---------------------------------------------------------------------------
+typedef __int128 i128;
+typedef unsigned __int128 u128;
+
+static i128 f32_fixed(float x, int frac, u128 maxpos, u128 maxneg) {
+  uint32_t bits;
+  memcpy(&bits, &x, 4);
+  REQUIRE(((bits >> 23) & 0xff) != 0xff, RDET_E_FORMAT, "det conversion requires a finite f32");
+  bool neg = bits >> 31;
+  int e8 = (bits >> 23) & 0xff;
+  uint32_t frac_bits = bits & 0x7fffff;
+  if (e8 == 0 && frac_bits == 0) return 0;
+  u128 sig = e8 ? ((1u << 23) | frac_bits) : frac_bits;
+  int exp2 = (e8 ? e8 - 150 : -149) + frac;
+  u128 lim = neg ? maxneg : maxpos;
+  u128 mag;
+  if (exp2 >= 0) {
+    mag = (exp2 >= 128 || sig > (lim >> exp2)) ? lim : (sig << exp2);
+  } else {
+    int sh = -exp2;
+    if (sh >= 128) mag = 0;
+    else {
+      u128 q = sig >> sh, rem = sig & (((u128)1 << sh) - 1), half = (u128)1 << (sh - 1);
+      mag = (rem > half || (rem == half && (q & 1))) ? q + 1 : q;
+      if (mag > lim) mag = lim;
+    }
+  }
+  if (neg) return mag >= maxneg ? -(i128)maxneg : -(i128)mag;
+  return (i128)mag;
+}
+static int32_t host_f32_to_act(float x) {
+  i128 v = f32_fixed(x, 16, (u128)INT32_MAX, (u128)1 << 31);
+  return v < (i128)INT32_MIN ? INT32_MIN : (v > (i128)INT32_MAX ? INT32_MAX : (int32_t)v);
+}
+static int64_t host_f32_to_acc(float x) {
+  i128 v = f32_fixed(x, 32, (u128)INT64_MAX, (u128)1 << 63);
+  return v < (i128)INT64_MIN ? INT64_MIN : (v > (i128)INT64_MAX ? INT64_MAX : (int64_t)v);
+}
+static i128 rte_div128(i128 n, i128 d) {
+  i128 q = n / d, r = n % d;
+  if (r == 0) return q;
+  i128 ar = r < 0 ? -r : r, ad = d < 0 ? -d : d;
+  i128 step = ((n < 0) != (d < 0)) ? -1 : 1;
+  if (2 * ar < ad) return q;
+  if (2 * ar > ad) return q + step;
+  return (q & 1) ? q + step : q;
+}
+static int64_t clamp64(i128 v) {
+  return v > (i128)INT64_MAX ? INT64_MAX : (v < (i128)INT64_MIN ? INT64_MIN : (int64_t)v);
+}
+static int64_t host_pow_acc(int64_t b, uint32_t e) {
+  int64_t r = kOneAcc;
+  for (uint32_t i = 0; i < e; ++i) r = acc_mul(r, b);
+  return r;
+}
+// ops.rs:561 nth_root_acc — bisection with ties-to-even rounding
+static int64_t host_nth_root(int64_t v, uint32_t deg) {
+  if (deg == 1 || v == kOneAcc) return v;
+  int64_t lo = 0, hi = v > kOneAcc ? v : kOneAcc;
+  while (lo < hi) {
+    int64_t mid = lo + (hi - lo + 1) / 2;
+    if (host_pow_acc(mid, deg) <= v) lo = mid; else hi = mid - 1;
+  }
+  int64_t up = lo == INT64_MAX ? lo : lo + 1;
+  i128 le = (i128)v - host_pow_acc(lo, deg), ue = (i128)host_pow_acc(up, deg) - v;
+  if (le < 0) le = -le;
+  if (ue < 0) ue = -ue;
+  if (ue < le) return up;
+  if (le < ue) return lo;
+  return (lo & 1) ? up : lo;
+}
+// inverse-frequency recurrence of rope_rotate_pairs_in_place (ops.rs:184-195):
+// inv[0] = 1.0, inv[i+1] = acc_mul(inv[i], step), step = div_acc(1, base^(1/(dim/2)))
+static std::vector<int64_t> rope_inv_freq(int64_t base, int freq_dim, int rotary) {
+  int64_t root = host_nth_root(base, (uint32_t)(freq_dim / 2));
+  REQUIRE(root != 0, RDET_E_FORMAT, "rope base root is zero");
+  int64_t step = clamp64(rte_div128((i128)kOneAcc << 32, (i128)root));
+  std::vector<int64_t> t(rotary / 2);
+  int64_t f = kOneAcc;
+  for (int i = 0; i < rotary / 2; ++i) { t[i] = f; f = acc_mul(f, step); }
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// config (reference GemmaTextConfigFile, io.rs:61-190 and :1896-2045)
+// ---------------------------------------------------------------------------
+struct LayerCfg {
+  bool sliding = false;
+  int head_dim = 0, kv_heads = 0, rotary = 0, window = 0;
+  bool trim = false;  // cache_sliding_window is Some
+  int donor = -1;     // kv_shared_layer_index
+  bool k_eq_v = false;
+  float rope_theta = 0;
+};
+struct ModelCfg {
+  int H = 0, L = 0, Hq = 0, kv = 0, d = 0, dg = 0, V = 0, P = 0, ple_vocab = 0, sliding_window = 0;
+  bool tied = true, has_softcap = false;
+  float softcap = 0, eps = 0;
+  std::vector<LayerCfg> layers;
+};
+
+static const json::Value& text_cfg(const json::Value& root) {
+  const json::Value* t = root.get("text_config");
+  return t ? *t : root;
+}
+static const json::Value* opt_field(const json::Value& t, const char* k) {
+  const json::Value* v = t.get(k);
+  return (v && !v->is_null()) ? v : nullptr;
+}
+static long req_int(const json::Value& t, const char* k) {
+  const json::Value* v = opt_field(t, k);
+  REQUIRE(v && v->kind == json::Value::Num, RDET_E_FORMAT, std::string("config.json: missing field ") + k);
+  return (long)v->num;
+}
+static float num_f32(const json::Value& v) { return strtof(v.str.c_str(), nullptr); }
+
+static ModelCfg parse_config(const std::string& text) {
+  json::Value root;
+  try {
+    root = json::parse(text);
+  } catch (const std::exception& e) {
+    throw Fail{RDET_E_FORMAT, e.what()};
+  }
+  const json::Value& t = text_cfg(root);
+  ModelCfg c;
+  const json::Value* moe = opt_field(t, "enable_moe_block");
+  REQUIRE(moe && moe->kind == json::Value::Bool, RDET_E_FORMAT, "config.json: missing field enable_moe_block");
+  REQUIRE(!moe->b, RDET_E_FORMAT, "only Gemma 4 dense layers are supported, not MoE checkpoints");
+  const json::Value* act = opt_field(t, "hidden_activation");
+  REQUIRE(act && act->kind == json::Value::Str, RDET_E_FORMAT, "config.json: missing field hidden_activation");
+  REQUIRE(act->str == "gelu_pytorch_tanh", RDET_E_FORMAT, "only gelu_pytorch_tanh is supported, got " + act->str);
+  c.H = (int)req_int(t, "hidden_size");
+  c.L = (int)req_int(t, "num_hidden_layers");
+  c.Hq = (int)req_int(t, "num_attention_heads");
+  c.kv = (int)req_int(t, "num_key_value_heads");
+  c.d = (int)req_int(t, "head_dim");
+  c.V = (int)req_int(t, "vocab_size");
+  c.sliding_window = (int)req_int(t, "sliding_window");
+  const json::Value* v;
+  c.dg = (v = opt_field(t, "global_head_dim")) ? (int)v->num : c.d;
+  c.P = (v = opt_field(t, "hidden_size_per_layer_input")) ? (int)v->num : 0;
+  c.ple_vocab = (v = opt_field(t, "vocab_size_per_layer_input")) ? (int)v->num : c.V;
+  int gkv = (v = opt_field(t, "num_global_key_value_heads")) ? (int)v->num : c.kv;
+  bool keqv = (v = opt_field(t, "attention_k_eq_v")) ? v->b : false;
+  c.tied = (v = opt_field(t, "tie_word_embeddings")) ? v->b : true;
+  int nshared = (v = opt_field(t, "num_kv_shared_layers")) ? (int)v->num : 0;
+  bool bidir = (v = opt_field(t, "use_bidirectional_attention")) && v->kind == json::Value::Str && v->str == "all";
+  if ((v = opt_field(t, "final_logit_softcapping"))) { c.has_softcap = true; c.softcap = num_f32(*v); }
+  const json::Value* epsv = opt_field(t, "rms_norm_eps");
+  REQUIRE(epsv, RDET_E_FORMAT, "config.json: missing field rms_norm_eps");
+  c.eps = num_f32(*epsv);
+  // rope parameters (io.rs:123-150)
+  float partial = 0.25f, local_theta = 10000.0f, full_theta = 1000000.0f;
+  const json::Value* rp = opt_field(t, "rope_parameters");
+  if (rp) {
+    const json::Value* fa = opt_field(*rp, "full_attention");
+    const json::Value* sa = opt_field(*rp, "sliding_attention");
+    const json::Value* g = opt_field(*rp, "rope_theta");
+    if (fa && (v = opt_field(*fa, "partial_rotary_factor"))) partial = num_f32(*v);
+    if (sa && (v = opt_field(*sa, "rope_theta"))) local_theta = num_f32(*v);
+    if (fa && (v = opt_field(*fa, "rope_theta"))) full_theta = num_f32(*v);
+    else if (g) full_theta = num_f32(*g);
+  }
+  const json::Value* lt = opt_field(t, "layer_types");
+  REQUIRE(lt && lt->kind == json::Value::Arr, RDET_E_FORMAT, "config.json: missing field layer_types");
+  REQUIRE((int)lt->arr.size() == c.L, RDET_E_FORMAT, "Gemma config layer count mismatch: num_hidden_layers vs layer_types");
+  std::vector<bool> sl(c.L);
+  for (int l = 0; l < c.L; ++l) sl[l] = lt->arr[l].str == "sliding_attention";
+  // KV sharing (io.rs:165-190): the last num_kv_shared_layers layers reuse the
+  // cache of the last earlier layer of the same attention type.
+  int first_shared = nshared > c.L ? 0 : c.L - nshared;
+  std::vector<int> donor(c.L, -1);
+  std::vector<bool> is_donor(c.L, false);
+  if (nshared > 0)
+    for (int l = first_shared; l < c.L; ++l) {
+      int dnr = -1;
+      for (int j = first_shared - 1; j >= 0; --j)
+        if (sl[j] == sl[l]) { dnr = j; break; }
+      REQUIRE(dnr >= 0, RDET_E_FORMAT, "Gemma layer " + std::to_string(l) + " is configured to share KV without a prior donor layer");
+      donor[l] = dnr;
+      is_donor[dnr] = true;
+    }
+  int window = bidir ? c.sliding_window / 2 + 1 : c.sliding_window;
+  for (int l = 0; l < c.L; ++l) {
+    LayerCfg lc;
+    lc.sliding = sl[l];
+    lc.head_dim = lc.sliding ? c.d : c.dg;
+    lc.kv_heads = lc.sliding ? c.kv : (keqv ? gkv : c.kv);
+    lc.rotary = lc.sliding ? lc.head_dim : (int)((float)lc.head_dim * partial);
+    lc.window = lc.sliding ? window : 0;
+    lc.trim = lc.sliding && !is_donor[l];
+    lc.donor = donor[l];
+    lc.k_eq_v = !lc.sliding && keqv;
+    lc.rope_theta = lc.sliding ? local_theta : full_theta;
+    REQUIRE(lc.kv_heads > 0 && c.Hq / lc.kv_heads > 0, RDET_E_FORMAT, "invalid Gemma head configuration");
+    REQUIRE(c.Hq / lc.kv_heads <= 8, RDET_E_FORMAT, "more than 8 query heads per KV head is not supported");
+    REQUIRE(lc.rotary % 2 == 0 && lc.rotary <= lc.head_dim, RDET_E_FORMAT, "rope_rotate_pairs requires an even rotary_dim within head_dim");
+    if (lc.rotary > 0) REQUIRE(lc.head_dim >= 2 && lc.head_dim % 2 == 0, RDET_E_FORMAT, "rope requires an even freq_base_dim");
+    c.layers.push_back(lc);
+  }
+  return c;
+}
+
+// ---------------------------------------------------------------------------
+// tensor sources: a detwgt v2 artifact (fail-closed) or the seeded generator
+// ---------------------------------------------------------------------------
+struct TensorInfo {
+  std::vector<uint64_t> shape;
+  int width = 32;
+  const uint8_t* payload = nullptr;  // host pointer into the mapped artifact
+  uint64_t bytes = 0;
+};
+
+struct MappedFile {
+  void* base = nullptr;
+  size_t size = 0;
+  ~MappedFile() { if (base && base != MAP_FAILED) munmap(base, size); }
+};
+
+// detwgt v2 reader (io.rs:230-395): every check the reference makes, in the
+// same order, failing closed.
+static std::map<std::string, TensorInfo> parse_detwgt(const uint8_t* b, size_t n) {
+  size_t cur = 0;
+  auto take = [&](size_t len) -> const uint8_t* {
+    REQUIRE(len <= n - cur, RDET_E_FORMAT, "artifact ended unexpectedly");
+    const uint8_t* p = b + cur;
+    cur += len;
+    return p;
+  };
+  auto u32 = [&]() { uint32_t v; memcpy(&v, take(4), 4); return v; };
+  auto u64 = [&]() { uint64_t v; memcpy(&v, take(8), 8); return v; };
+  REQUIRE(memcmp(take(8), "DNWGTV0\0", 8) == 0, RDET_E_FORMAT, "unsupported deterministic artifact magic");
+  uint32_t ver = u32();
+  REQUIRE(ver == 2, RDET_E_FORMAT, "unsupported deterministic artifact format version " + std::to_string(ver) + "; expected 2");
+  uint32_t spec = u32();
+  REQUIRE(spec == 1, RDET_E_FORMAT, "unsupported deterministic artifact det_num spec version " + std::to_string(spec));
+  uint64_t count = u64();
+  std::map<std::string, TensorInfo> out;
+  for (uint64_t t = 0; t < count; ++t) {
+    uint32_t nl = u32();
+    std::string name((const char*)take(nl), nl);
+    uint32_t rank = u32();
+    TensorInfo ti;
+    u128 prod = 1;
+    for (uint32_t i = 0; i < rank; ++i) {
+      uint64_t dim = u64();
+      ti.shape.push_back(dim);
+      prod *= dim;
+      REQUIRE(prod <= (u128)UINT64_MAX, RDET_E_FORMAT, "tensor shape overflowed");
+    }
+    uint64_t ec = u64();
+    REQUIRE((u128)ec == prod, RDET_E_FORMAT, "tensor `" + name + "` element count mismatch");
+    uint32_t w = u32();
+    REQUIRE(w == 16 || w == 32, RDET_E_FORMAT, "tensor `" + name + "` has an invalid element width");
+    ti.width = (int)w;
+    uint64_t pl = u64();
+    REQUIRE((u128)pl == (u128)ec * (w / 8), RDET_E_FORMAT, "tensor `" + name + "` payload length mismatch");
+    uint64_t mass = u64();
+    REQUIRE(!(rank >= 2 && mass >= ((uint64_t)1 << 31)), RDET_E_FORMAT,
+            "tensor `" + name + "` max row mass violates the conversion-time overflow bound");
+    size_t pad = (64 - cur % 64) % 64;
+    const uint8_t* pp = take(pad);
+    for (size_t i = 0; i < pad; ++i) REQUIRE(pp[i] == 0, RDET_E_FORMAT, "tensor `" + name + "` has non-zero payload alignment padding");
+    ti.payload = take((size_t)pl);
+    ti.bytes = pl;
+    REQUIRE(out.find(name) == out.end(), RDET_E_FORMAT, "deterministic artifact contains duplicate tensor `" + name + "`");
+    out.emplace(name, ti);
+  }
+  REQUIRE(cur == n, RDET_E_FORMAT, "deterministic artifact has trailing bytes after tensor payloads");
+  return out;
+}
+
+static uint64_t fnv1a64(const std::string& s) {
+  uint64_t h = 0xCBF29CE484222325ull;
+  for (unsigned char ch : s) { h ^= ch; h *= 0x100000001B3ull; }
+  return h;
+}
+
+// Synthetic tensor table: the same names and shapes as detwgt.layer_shapes().
+static std::map<std::string, TensorInfo> synthetic_table(const ModelCfg& c, const json::Value& t, int width, int F) {
+  std::map<std::string, TensorInfo> m;
+  auto add = [&](const std::string& n, std::vector<uint64_t> shape) {
+    TensorInfo ti;
+    ti.shape = shape;
+    ti.width = shape.size() == 1 ? 32 : width;
+    uint64_t cnt = 1;
+    for (auto d : shape) cnt *= d;
+    ti.bytes = cnt * (ti.width / 8);
+    m[n] = ti;
+  };
+  add("model.language_model.embed_tokens.weight", {(uint64_t)c.V, (uint64_t)c.H});
+  const json::Value* lsv = opt_field(t, "_synthetic_layer_scalar");
+  bool with_scalar = lsv ? lsv->b : true;
+  for (int l = 0; l < c.L; ++l) {
+    const LayerCfg& lc = c.layers[l];
+    std::string p = "model.language_model.layers." + std::to_string(l);
+    uint64_t hd = lc.head_dim, nkv = lc.kv_heads;
+    add(p + ".self_attn.q_proj.weight", {(uint64_t)c.Hq * hd, (uint64_t)c.H});
+    add(p + ".self_attn.k_proj.weight", {nkv * hd, (uint64_t)c.H});
+    if (!lc.k_eq_v) add(p + ".self_attn.v_proj.weight", {nkv * hd, (uint64_t)c.H});
+    add(p + ".self_attn.o_proj.weight", {(uint64_t)c.H, (uint64_t)c.Hq * hd});
+    add(p + ".self_attn.q_norm.weight", {hd});
+    add(p + ".self_attn.k_norm.weight", {hd});
+    for (const char* nn : {"input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm", "post_feedforward_layernorm"})
+      add(p + "." + nn + ".weight", {(uint64_t)c.H});
+    add(p + ".mlp.gate_proj.weight", {(uint64_t)F, (uint64_t)c.H});
+    add(p + ".mlp.up_proj.weight", {(uint64_t)F, (uint64_t)c.H});
+    add(p + ".mlp.down_proj.weight", {(uint64_t)c.H, (uint64_t)F});
+    if (c.P > 0) {
+      add(p + ".per_layer_input_gate.weight", {(uint64_t)c.P, (uint64_t)c.H});
+      add(p + ".per_layer_projection.weight", {(uint64_t)c.H, (uint64_t)c.P});
+      add(p + ".post_per_layer_input_norm.weight", {(uint64_t)c.H});
+    }
+    if (with_scalar) add(p + ".layer_scalar", {1});
+  }
+  if (c.P > 0) {
+    add("model.language_model.embed_tokens_per_layer.weight", {(uint64_t)c.ple_vocab, (uint64_t)c.L * c.P});
+    add("model.language_model.per_layer_model_projection.weight", {(uint64_t)c.L * c.P, (uint64_t)c.H});
+    add("model.language_model.per_layer_projection_norm.weight", {(uint64_t)c.P});
+  }
+  add("model.language_model.norm.weight", {(uint64_t)c.H});
+  const json::Value* tie = opt_field(t, "tie_word_embeddings");
+  if (tie && !tie->b) add("model.language_model.lm_head.weight", {(uint64_t)c.V, (uint64_t)c.H});
+  return m;
+}
+
+// ---------------------------------------------------------------------------
+// device model
+// ---------------------------------------------------------------------------
+struct LayerDev {
+  LayerCfg cfg;
+  int F = 0;
+  DevMat q, k, v, o, gate, up, down, ple_gate, ple_proj;
+  const int32_t *q_norm = nullptr, *k_norm = nullptr, *in_ln = nullptr, *post_attn_ln = nullptr,
+                *pre_ff_ln = nullptr, *post_ff_ln = nullptr, *ple_norm = nullptr;
+  bool has_scalar = false;
+  int32_t scalar = 0;
+  const int64_t* inv_freq = nullptr;
+};
+
+struct PrefillWs {
+  int S = 0;
+  int32_t *x0 = nullptr, *xa = nullptr, *xb = nullptr, *nrm = nullptr, *q = nullptr, *kraw = nullptr,
+          *vraw = nullptr, *qo = nullptr, *comb = nullptr, *attn = nullptr, *hbuf = nullptr, *ple_proj = nullptr,
+          *ple_all = nullptr, *g = nullptr, *pr = nullptr, *scores = nullptr;
+  int64_t* exps = nullptr;
+  int64_t scratch_elems = 0;
+  uint32_t* ids = nullptr;
+};
+struct DecodeWs {
+  int32_t *x0 = nullptr, *t1 = nullptr, *t2 = nullptr, *q = nullptr, *kraw = nullptr, *vraw = nullptr,
+          *qo = nullptr, *comb = nullptr, *attn = nullptr, *hbuf = nullptr, *ple_proj = nullptr, *ple_all = nullptr,
+          *g = nullptr, *pr = nullptr, *argpart = nullptr;
+};
+
+struct Seq;
+
+struct Ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  ModelCfg cfg;
+  int F = 0, dmax = 0, kvmax = 0;
+  int64_t eps = 0;
+  int32_t softcap = 0, emb_scale = 0, ple_emb_scale = 0, ple_proj_scale = 0, ple_in_scale = 0;
+  DevMat emb, lm_head, ple_table, ple_model_proj;
+  const int32_t *final_norm = nullptr, *ple_proj_norm = nullptr;
+  std::vector<LayerDev> layers;
+  std::vector<void*> allocs;
+  uint64_t weight_bytes = 0;
+  uint32_t max_prefill = 4096, flags = 0;
+  PrefillWs pw;
+  DecodeWs dw;
+  int32_t* d_err = nullptr;
+  int argblocks = 0;
+  Seq* prefill_owner = nullptr;  // sequence whose routine-granular prefill is in flight
+  Seq* decode_owner = nullptr;
+  std::vector<void*> live_seqs;  // rdet_seq handles still open on this context
+
+  void* dalloc(size_t bytes) {
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes ? bytes : 16);
+    if (e != cudaSuccess) throw Fail{RDET_E_OOM, std::string("cudaMalloc failed: ") + cudaGetErrorString(e)};
+    allocs.push_back(p);
+    return p;
+  }
+  template <typename T>
+  T* dalloc_n(size_t n) { return static_cast<T*>(dalloc(n * sizeof(T))); }
+  ~Ctx() {
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    for (void* p : allocs) cudaFree(p);
+    if (stream) cudaStreamDestroy(stream);
+  }
+};
+
+struct Seq {
+  Ctx* ctx = nullptr;
+  int cap = 0;
+  std::vector<int32_t*> kc, vc;  // per layer [Hkv, cap, d]; nullptr for KV-sharing layers
+  int32_t* d_pos = nullptr;      // device copy of `pos`
+  int pos = 0;                   // tokens in the cache (position of the next token)
+  bool prefilled = false;
+  int32_t* logits = nullptr;     // [V]
+  uint32_t* d_token = nullptr;
+  uint32_t* d_hist = nullptr;    // generated tokens (graph path)
+  int32_t* d_step = nullptr;
+  int hist_cap = 0;
+  AttnScratch asc;
+  int32_t* dec_out = nullptr;    // [L, H] per-layer outputs of the last decode
+  int32_t* hid = nullptr;        // [S, H] final hidden of the last prefill
+  int32_t* embd = nullptr;       // [S, H] embedding of the last prefill
+  int hid_rows = 0, last_S = 0;
+  bool last_was_prefill = true;
+  std::vector<std::string> layer_hashes;  // per-layer prefill commitments (flag)
+  // routine state
+  int prefill_next = -1, prefill_S = 0;
+  int32_t* prefill_cur = nullptr;
+  int decode_next = -1;
+  int32_t* decode_cur = nullptr;
+  cudaGraphExec_t graph = nullptr;
+  std::vector<void*> allocs;
+  void* dalloc(size_t bytes) {
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes ? bytes : 16);
+    if (e != cudaSuccess) throw Fail{RDET_E_OOM, std::string("cudaMalloc failed: ") + cudaGetErrorString(e)};
+    allocs.push_back(p);
+    return p;
+  }
+  int device = 0;
+  ~Seq() {
+    cudaSetDevice(device);
+    cudaDeviceSynchronize();
+    if (graph) cudaGraphExecDestroy(graph);
+    for (void* p : allocs) cudaFree(p);
+  }
+};
+
+// ---------------------------------------------------------------------------
+// loading
+// ---------------------------------------------------------------------------
+struct Loader {
+  Ctx& c;
+  std::map<std::string, TensorInfo>& tab;
+  bool synthetic;
+  uint64_t seed;
+  bool dry;  // validate names and shapes only (no device work)
+  const TensorInfo* find(const std::string& n) {
+    auto it = tab.find(n);
+    return it == tab.end() ? nullptr : &it->second;
+  }
+  const TensorInfo& need(const std::string& n, size_t rank) {
+    const TensorInfo* t = find(n);
+    REQUIRE(t, RDET_E_FORMAT, "failed to load tensor `" + n + "` from deterministic artifact");
+    REQUIRE(t->shape.size() == rank, RDET_E_FORMAT,
+            "tensor `" + n + "` has rank " + std::to_string(t->shape.size()) + ", expected " + std::to_string(rank));
+    return *t;
+  }
+  void* upload_raw(const std::string& n, const TensorInfo& t) {
+    if (dry) return nullptr;
+    void* p = c.dalloc(t.bytes);
+    c.weight_bytes += t.bytes;
+    if (synthetic) {
+      uint64_t cnt = 1;
+      for (auto d : t.shape) cnt *= d;
+      launch_synth(p, t.width, (int)t.shape.size(), (int64_t)cnt, (int64_t)t.shape.back(), fnv1a64(n) ^ seed, c.stream);
+      CK(cudaGetLastError());
+    } else {
+      CK(cudaMemcpyAsync(p, t.payload, t.bytes, cudaMemcpyHostToDevice, c.stream));
+      CK(cudaStreamSynchronize(c.stream));
+    }
+    return p;
+  }
+  DevMat mat(const std::string& n, int rows = -1, int cols = -1) {
+    const TensorInfo& t = need(n, 2);
+    if (rows >= 0) REQUIRE((int)t.shape[0] == rows, RDET_E_FORMAT, "tensor `" + n + "` has unexpected row count");
+    if (cols >= 0) REQUIRE((int)t.shape[1] == cols, RDET_E_FORMAT, "tensor `" + n + "` has unexpected column count");
+    DevMat m;
+    m.p = upload_raw(n, t);
+    m.width = t.width;
+    m.rows = (int)t.shape[0];
+    m.cols = (int)t.shape[1];
+    return m;
+  }
+  // rank-1 gains widened to i32 on the device
+  const int32_t* vec(const std::string& n, int len) {
+    const TensorInfo& t = need(n, 1);
+    REQUIRE((int)t.shape[0] == len, RDET_E_FORMAT, "rms norm width mismatch for `" + n + "`");
+    if (dry) return nullptr;
+    if (t.width == 32 || synthetic) return static_cast<const int32_t*>(upload_raw(n, t));
+    std::vector<int32_t> w(len);
+    const int16_t* src = reinterpret_cast<const int16_t*>(t.payload);
+    for (int i = 0; i < len; ++i) { int16_t v; memcpy(&v, src + i, 2); w[i] = v; }
+    int32_t* p = c.dalloc_n<int32_t>(len);
+    c.weight_bytes += (uint64_t)len * 4;
+    CK(cudaMemcpy(p, w.data(), (size_t)len * 4, cudaMemcpyHostToDevice));
+    return p;
+  }
+  bool scalar(const std::string& n, int32_t* out) {
+    const TensorInfo* t = find(n);
+    if (!t) return false;
+    REQUIRE(t->shape.size() == 1 && t->shape[0] == 1, RDET_E_FORMAT, "tensor `" + n + "` expected shape [1] for a scalar");
+    if (dry) {
+      *out = 0;
+    } else if (synthetic) {
+      void* p = upload_raw(n, *t);
+      CK(cudaMemcpy(out, p, 4, cudaMemcpyDeviceToHost));
+    } else if (t->width == 16) {
+      int16_t v;
+      memcpy(&v, t->payload, 2);
+      *out = v;
+    } else {
+      memcpy(out, t->payload, 4);
+    }
+    return true;
+  }
+};
+
+static void build_model(Ctx& c, std::map<std::string, TensorInfo>& tab, bool synthetic, uint64_t seed,
+                        bool dry = false) {
+  ModelCfg& m = c.cfg;
+  Loader ld{c, tab, synthetic, seed, dry};
+  const char* emb_names[] = {"model.language_model.embed_tokens.weight", "language_model.embed_tokens.weight", "embed_tokens.weight"};
+  std::string emb_name;
+  for (const char* n : emb_names)
+    if (ld.find(n)) { emb_name = n; break; }
+  REQUIRE(!emb_name.empty(), RDET_E_FORMAT, "failed to find any supported embedding tensor");
+  c.emb = ld.mat(emb_name);
+  REQUIRE(c.emb.cols == m.H, RDET_E_FORMAT, "embedding tensor width mismatch");
+  c.emb_scale = host_f32_to_act(std::sqrt((float)c.emb.cols));  // io.rs:2123
+  c.eps = host_f32_to_acc(m.eps);
+  c.softcap = m.has_softcap ? host_f32_to_act(m.softcap) : 0;
+  if (m.has_softcap) REQUIRE(c.softcap > 0, RDET_E_FORMAT, "softcap_act requires a strictly positive softcap");
+  std::map<std::pair<int64_t, int>, const int64_t*> rope_tabs;
+  for (int l = 0; l < m.L; ++l) {
+    const LayerCfg& lc = m.layers[l];
+    LayerDev L;
+    L.cfg = lc;
+    std::string p = "model.language_model.layers." + std::to_string(l);
+    int hd = lc.head_dim;
+    L.q = ld.mat(p + ".self_attn.q_proj.weight", m.Hq * hd, m.H);
+    L.k = ld.mat(p + ".self_attn.k_proj.weight", lc.kv_heads * hd, m.H);
+    if (lc.k_eq_v) {
+      if (ld.find(p + ".self_attn.v_proj.weight")) L.v = ld.mat(p + ".self_attn.v_proj.weight", lc.kv_heads * hd, m.H);
+    } else {
+      L.v = ld.mat(p + ".self_attn.v_proj.weight", lc.kv_heads * hd, m.H);
+    }
+    L.o = ld.mat(p + ".self_attn.o_proj.weight", m.H, m.Hq * hd);
+    L.gate = ld.mat(p + ".mlp.gate_proj.weight", -1, m.H);
+    L.F = L.gate.rows;
+    L.up = ld.mat(p + ".mlp.up_proj.weight", L.F, m.H);
+    L.down = ld.mat(p + ".mlp.down_proj.weight", m.H, L.F);
+    L.q_norm = ld.vec(p + ".self_attn.q_norm.weight", hd);
+    L.k_norm = ld.vec(p + ".self_attn.k_norm.weight", hd);
+    L.in_ln = ld.vec(p + ".input_layernorm.weight", m.H);
+    L.post_attn_ln = ld.vec(p + ".post_attention_layernorm.weight", m.H);
+    L.pre_ff_ln = ld.vec(p + ".pre_feedforward_layernorm.weight", m.H);
+    L.post_ff_ln = ld.vec(p + ".post_feedforward_layernorm.weight", m.H);
+    if (m.P > 0) {
+      L.ple_gate = ld.mat(p + ".per_layer_input_gate.weight", m.P, m.H);
+      L.ple_proj = ld.mat(p + ".per_layer_projection.weight", m.H, m.P);
+      L.ple_norm = ld.vec(p + ".post_per_layer_input_norm.weight", m.H);
+    }
+    L.has_scalar = ld.scalar(p + ".layer_scalar", &L.scalar);
+    if (lc.rotary > 0 && !dry) {
+      int64_t base = host_f32_to_acc(lc.rope_theta);
+      REQUIRE(base > 0, RDET_E_FORMAT, "rope_rotate_pairs requires a positive base");
+      auto key = std::make_pair(base, hd * 65536 + lc.rotary);
+      auto it = rope_tabs.find(key);
+      if (it == rope_tabs.end()) {
+        std::vector<int64_t> t = rope_inv_freq(base, hd, lc.rotary);
+        int64_t* dp = c.dalloc_n<int64_t>(t.size());
+        CK(cudaMemcpy(dp, t.data(), t.size() * 8, cudaMemcpyHostToDevice));
+        it = rope_tabs.emplace(key, dp).first;
+      }
+      L.inv_freq = it->second;
+    }
+    c.F = std::max(c.F, L.F);
+    c.dmax = std::max(c.dmax, hd);
+    c.kvmax = std::max(c.kvmax, lc.kv_heads);
+    c.layers.push_back(L);
+  }
+  c.final_norm = ld.vec("model.language_model.norm.weight", m.H);
+  c.lm_head = m.tied ? c.emb : ld.mat("model.language_model.lm_head.weight", -1, m.H);
+  if (m.P > 0) {
+    c.ple_table = ld.mat("model.language_model.embed_tokens_per_layer.weight");
+    REQUIRE(c.ple_table.rows >= m.ple_vocab && c.ple_table.cols >= m.L * m.P, RDET_E_FORMAT, "PLE token embedding slice is out of bounds");
+    c.ple_table.rows = m.ple_vocab;  // rows beyond vocab_size_per_layer_input are not addressable
+    c.ple_model_proj = ld.mat("model.language_model.per_layer_model_projection.weight");
+    REQUIRE(c.ple_model_proj.rows >= m.L * m.P && c.ple_model_proj.cols == m.H, RDET_E_FORMAT, "PLE model projection slice is out of bounds");
+    c.ple_model_proj.rows = m.L * m.P;
+    c.ple_proj_norm = ld.vec("model.language_model.per_layer_projection_norm.weight", m.P);
+    c.ple_emb_scale = host_f32_to_act(std::sqrt((float)m.P));              // io.rs:1226-1227
+    c.ple_proj_scale = host_f32_to_act(std::pow((float)m.H, -0.5f));      // io.rs:1228-1229
+    c.ple_in_scale = host_f32_to_act(std::pow(2.0f, -0.5f));              // io.rs:1230-1231
+  }
+  if (!dry) CK(cudaStreamSynchronize(c.stream));
+}
+
+static void alloc_workspaces(Ctx& c) {
+  const ModelCfg& m = c.cfg;
+  size_t S = c.max_prefill;
+  PrefillWs& w = c.pw;
+  w.S = (int)S;
+  size_t HqD = (size_t)m.Hq * c.dmax, KvD = (size_t)c.kvmax * c.dmax, LP = (size_t)m.L * std::max(m.P, 1);
+  w.x0 = c.dalloc_n<int32_t>(S * m.H);
+  w.xa = c.dalloc_n<int32_t>(S * m.H);
+  w.xb = c.dalloc_n<int32_t>(S * m.H);
+  w.nrm = c.dalloc_n<int32_t>(S * m.H);
+  w.q = c.dalloc_n<int32_t>(S * HqD);
+  w.kraw = c.dalloc_n<int32_t>(S * KvD);
+  w.vraw = c.dalloc_n<int32_t>(S * KvD);
+  w.qo = c.dalloc_n<int32_t>(S * HqD);
+  w.comb = c.dalloc_n<int32_t>(S * HqD);
+  w.attn = c.dalloc_n<int32_t>(S * m.H);
+  w.hbuf = c.dalloc_n<int32_t>(S * c.F);
+  w.ple_proj = c.dalloc_n<int32_t>(S * LP);
+  w.ple_all = c.dalloc_n<int32_t>(S * LP);
+  w.g = c.dalloc_n<int32_t>(S * std::max(m.P, 1));
+  w.pr = c.dalloc_n<int32_t>(S * m.H);
+  w.ids = c.dalloc_n<uint32_t>(S);
+  w.scratch_elems = (int64_t)m.Hq * S * S;
+  w.scores = c.dalloc_n<int32_t>(w.scratch_elems);
+  w.exps = c.dalloc_n<int64_t>(w.scratch_elems);
+  DecodeWs& d = c.dw;
+  d.x0 = c.dalloc_n<int32_t>(m.H);
+  d.t1 = c.dalloc_n<int32_t>(m.H);
+  d.t2 = c.dalloc_n<int32_t>(m.H);
+  d.q = c.dalloc_n<int32_t>(HqD);
+  d.kraw = c.dalloc_n<int32_t>(KvD);
+  d.vraw = c.dalloc_n<int32_t>(KvD);
+  d.qo = c.dalloc_n<int32_t>(HqD);
+  d.comb = c.dalloc_n<int32_t>(HqD);
+  d.attn = c.dalloc_n<int32_t>(m.H);
+  d.hbuf = c.dalloc_n<int32_t>(c.F);
+  d.ple_proj = c.dalloc_n<int32_t>(LP);
+  d.ple_all = c.dalloc_n<int32_t>(LP);
+  d.g = c.dalloc_n<int32_t>(std::max(m.P, 1));
+  d.pr = c.dalloc_n<int32_t>(m.H);
+  c.argblocks = std::min(sm_count() * 2, (m.V + 255) / 256);
+  if (c.argblocks < 1) c.argblocks = 1;
+  d.argpart = c.dalloc_n<int32_t>(2 * c.argblocks);
+  c.d_err = c.dalloc_n<int32_t>(1);
+  CK(cudaMemset(c.d_err, 0, 4));
+}
+
+static void check_err_flag(Ctx& c, const char* what) {
+  int32_t e = 0;
+  CK(cudaMemcpyAsync(&e, c.d_err, 4, cudaMemcpyDeviceToHost, c.stream));
+  CK(cudaStreamSynchronize(c.stream));
+  if (e) {
+    CK(cudaMemset(c.d_err, 0, 4));
+    throw Fail{RDET_E_RANGE, std::string(what) + ": token id is out of bounds for the embedding tensor"};
+  }
+}
+
+// ---------------------------------------------------------------------------
+// prefill (deterministic_tiles.rs:69-199; det_kernels.rs:678-821)
+// ---------------------------------------------------------------------------
+static void prefill_begin(Ctx& c, Seq& q, const uint32_t* ids, size_t n) {
+  const ModelCfg& m = c.cfg;
+  REQUIRE(n > 0, RDET_E_INVALID, "transformer embedding requires at least one token id");
+  REQUIRE(n <= c.max_prefill, RDET_E_RANGE, "prompt longer than the context's max_prefill");
+  REQUIRE((int)n <= q.cap, RDET_E_RANGE, "prompt longer than the sequence capacity");
+  for (size_t i = 0; i < n; ++i)
+    REQUIRE(ids[i] < (uint32_t)c.emb.rows, RDET_E_RANGE, "token id " + std::to_string(ids[i]) + " is out of bounds for embedding tensor");
+  if (m.P > 0)
+    for (size_t i = 0; i < n; ++i) REQUIRE(ids[i] < (uint32_t)m.ple_vocab, RDET_E_RANGE, "token id is out of bounds for the PLE table");
+  PrefillWs& w = c.pw;
+  int S = (int)n;
+  cudaStream_t s = c.stream;
+  CK(cudaMemcpyAsync(w.ids, ids, n * 4, cudaMemcpyHostToDevice, s));
+  CK(cudaMemsetAsync(q.d_pos, 0, 4, s));
+  q.pos = 0;
+  q.prefilled = false;
+  launch_embed(w.ids, S, c.emb, c.emb_scale, w.x0, c.d_err, s);
+  if (m.P > 0) {
+    launch_linear(w.x0, S, c.ple_model_proj, w.ple_proj, kEpiPlain, nullptr, s);
+    PleArgs pa;
+    pa.S = S; pa.L = m.L; pa.P = m.P; pa.ids = w.ids; pa.proj = w.ple_proj; pa.table = c.ple_table;
+    pa.norm = c.ple_proj_norm; pa.eps = c.eps; pa.emb_scale = c.ple_emb_scale; pa.proj_scale = c.ple_proj_scale;
+    pa.in_scale = c.ple_in_scale; pa.out = w.ple_all; pa.err = c.d_err;
+    launch_ple(pa, s);
+  }
+  CK(cudaGetLastError());
+  if (q.hid_rows < S) {
+    q.hid = static_cast<int32_t*>(q.dalloc((size_t)S * m.H * 4));
+    q.embd = static_cast<int32_t*>(q.dalloc((size_t)S * m.H * 4));
+    q.hid_rows = S;
+  }
+  CK(cudaMemcpyAsync(q.embd, w.x0, (size_t)S * m.H * 4, cudaMemcpyDeviceToDevice, s));
+  CK(cudaMemcpyAsync(w.xa, w.x0, (size_t)S * m.H * 4, cudaMemcpyDeviceToDevice, s));
+  q.prefill_S = S;
+  q.prefill_cur = w.xa;
+  q.prefill_next = 0;
+  q.layer_hashes.assign(m.L, std::string());
+  c.prefill_owner = &q;
+  check_err_flag(c, "prefill");
+}
+
+static std::string act_hash_rows(const int32_t* host, size_t rows, size_t cols) {
+  Sha256 h;
+  h.put("raster-det-num-act-v1", 21);
+  h.put_u64(rows);
+  for (size_t r = 0; r < rows; ++r) { h.put_u64(cols); h.put(host + r * cols, cols * 4); }
+  return h.hex();
+}
+
+static void prefill_layer(Ctx& c, Seq& q, int l) {
+  const ModelCfg& m = c.cfg;
+  const LayerDev& L = c.layers[l];
+  const LayerCfg& lc = L.cfg;
+  PrefillWs& w = c.pw;
+  cudaStream_t s = c.stream;
+  const int S = q.prefill_S, H = m.H, d = lc.head_dim;
+  int32_t* cur = q.prefill_cur;
+  int32_t* other = cur == w.xa ? w.xb : w.xa;
+  launch_rmsnorm_rows(cur, S, H, L.in_ln, c.eps, w.nrm, s);
+  launch_linear(w.nrm, S, L.q, w.q, kEpiPlain, nullptr, s);
+  QkvPostArgs qa;
+  qa.S = S; qa.pos = q.d_pos; qa.Hq = m.Hq; qa.Hkv = lc.kv_heads; qa.d = d; qa.rotary = lc.rotary;
+  qa.inv_freq = L.inv_freq; qa.q_in = w.q; qa.q_norm = L.q_norm; qa.k_norm = L.k_norm; qa.eps = c.eps;
+  qa.q_out = w.qo; qa.cap = q.cap;
+  const int32_t *kcache, *vcache;
+  if (lc.donor < 0) {
+    launch_linear(w.nrm, S, L.k, w.kraw, kEpiPlain, nullptr, s);
+    const int32_t* vsrc = w.kraw;  // k_eq_v: V is the raw K projection (det_kernels.rs:517-518)
+    if (L.v.p) { launch_linear(w.nrm, S, L.v, w.vraw, kEpiPlain, nullptr, s); vsrc = w.vraw; }
+    qa.k_in = w.kraw; qa.v_in = vsrc; qa.k_cache = q.kc[l]; qa.v_cache = q.vc[l];
+    kcache = q.kc[l];
+    vcache = q.vc[l];
+  } else {
+    // KV-sharing layers attend over the donor's cache; their own K/V
+    // projections cannot affect any output and are not computed.
+    kcache = q.kc[lc.donor];
+    vcache = q.vc[lc.donor];
+  }
+  launch_qkv_post(qa, s);
+  AttnPrefillArgs aa;
+  aa.S = S; aa.Hq = m.Hq; aa.Hkv = lc.kv_heads; aa.d = d; aa.window = lc.window; aa.q = w.qo;
+  aa.k_cache = kcache; aa.v_cache = vcache; aa.cap = q.cap; aa.out = w.comb; aa.scores = w.scores; aa.exps = w.exps;
+  aa.scratch_elems = w.scratch_elems;
+  launch_attn_prefill(aa, s);
+  launch_linear(w.comb, S, L.o, w.attn, kEpiPlain, nullptr, s);
+  bool ple = m.P > 0;
+  // t1 = xs + norm(attn)  -> other
+  launch_norm_residual_rows(w.attn, cur, S, H, L.post_attn_ln, c.eps, false, 0, other, s);
+  launch_rmsnorm_rows(other, S, H, L.pre_ff_ln, c.eps, w.nrm, s);
+  launch_linear_geglu(w.nrm, S, L.gate, L.up, w.hbuf, s);
+  launch_linear(w.hbuf, S, L.down, w.attn, kEpiPlain, nullptr, s);
+  // t2 = t1 + norm(ff) -> cur
+  launch_norm_residual_rows(w.attn, other, S, H, L.post_ff_ln, c.eps, !ple && L.has_scalar, L.scalar, cur, s);
+  int32_t* result = cur;
+  if (ple) {
+    launch_linear(cur, S, L.ple_gate, w.g, kEpiGeluMul, w.ple_all + (size_t)l * S * m.P, s);
+    launch_linear(w.g, S, L.ple_proj, w.pr, kEpiPlain, nullptr, s);
+    launch_norm_residual_rows(w.pr, cur, S, H, L.ple_norm, c.eps, L.has_scalar, L.scalar, other, s);
+    result = other;
+  }
+  CK(cudaGetLastError());
+  q.prefill_cur = result;
+  if (c.flags & RDET_FLAG_LAYER_COMMITMENTS) {
+    std::vector<int32_t> host((size_t)S * H);
+    CK(cudaMemcpyAsync(host.data(), result, host.size() * 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    q.layer_hashes[l] = act_hash_rows(host.data(), S, H);
+  }
+}
+
+static void gemv_logits(Ctx& c, const int32_t* hidden_row, int32_t* logits, cudaStream_t s) {
+  GemvArgs g;
+  g.K = c.cfg.H;
+  g.nseg = 1;
+  g.seg[0].w = c.lm_head;
+  g.seg[0].y = logits;
+  g.seg[0].epi = c.cfg.has_softcap ? kEpiSoftcap : kEpiPlain;
+  g.softcap = c.softcap;
+  g.pro = kProNorm;
+  g.a = hidden_row;
+  g.g1 = c.final_norm;
+  g.eps = c.eps;
+  launch_gemv(g, s);
+}
+
+static void prefill_finalize(Ctx& c, Seq& q) {
+  const ModelCfg& m = c.cfg;
+  REQUIRE(q.prefill_next == m.L, RDET_E_STATE, "prefill.finalize requires every layer to have run");
+  cudaStream_t s = c.stream;
+  int S = q.prefill_S;
+  CK(cudaMemcpyAsync(q.hid, q.prefill_cur, (size_t)S * m.H * 4, cudaMemcpyDeviceToDevice, s));
+  gemv_logits(c, q.prefill_cur + (size_t)(S - 1) * m.H, q.logits, s);
+  int32_t pos = S;
+  CK(cudaMemcpyAsync(q.d_pos, &pos, 4, cudaMemcpyHostToDevice, s));
+  CK(cudaStreamSynchronize(s));
+  CK(cudaGetLastError());
+  q.pos = S;
+  q.last_S = S;
+  q.prefilled = true;
+  q.last_was_prefill = true;
+  q.prefill_next = -1;
+  c.prefill_owner = nullptr;
+}
+
+// ---------------------------------------------------------------------------
+// decode (decode_layer_range/native/tiles.rs:133-197; det_kernels.rs:866-1208)
+// ---------------------------------------------------------------------------
+static void decode_embed(Ctx& c, Seq& q, const uint32_t* d_token) {
+  const ModelCfg& m = c.cfg;
+  DecodeWs& w = c.dw;
+  cudaStream_t s = c.stream;
+  launch_embed(d_token, 1, c.emb, c.emb_scale, w.x0, c.d_err, s);
+  if (m.P > 0) {
+    GemvArgs g;
+    g.K = m.H;
+    g.seg[0].w = c.ple_model_proj;
+    g.seg[0].y = w.ple_proj;
+    g.a = w.x0;
+    launch_gemv(g, s);
+    PleArgs pa;
+    pa.S = 1; pa.L = m.L; pa.P = m.P; pa.ids = d_token; pa.proj = w.ple_proj; pa.table = c.ple_table;
+    pa.norm = c.ple_proj_norm; pa.eps = c.eps; pa.emb_scale = c.ple_emb_scale; pa.proj_scale = c.ple_proj_scale;
+    pa.in_scale = c.ple_in_scale; pa.out = w.ple_all; pa.err = c.d_err;
+    launch_ple(pa, s);
+  }
+}
+
+static const int32_t* decode_layer(Ctx& c, Seq& q, int l, const int32_t* cur) {
+  const ModelCfg& m = c.cfg;
+  const LayerDev& L = c.layers[l];
+  const LayerCfg& lc = L.cfg;
+  DecodeWs& w = c.dw;
+  cudaStream_t s = c.stream;
+  const int H = m.H, d = lc.head_dim;
+  // q/k/v projections of rmsnorm(x)
+  GemvArgs g;
+  g.K = H;
+  g.pro = kProNorm;
+  g.a = cur;
+  g.g1 = L.in_ln;
+  g.eps = c.eps;
+  g.nseg = 1;
+  g.seg[0].w = L.q;
+  g.seg[0].y = w.q;
+  const int32_t *kcache, *vcache;
+  QkvPostArgs qa;
+  qa.S = 1; qa.pos = q.d_pos; qa.Hq = m.Hq; qa.Hkv = lc.kv_heads; qa.d = d; qa.rotary = lc.rotary;
+  qa.inv_freq = L.inv_freq; qa.q_in = w.q; qa.q_norm = L.q_norm; qa.k_norm = L.k_norm; qa.eps = c.eps;
+  qa.q_out = w.qo; qa.cap = q.cap;
+  if (lc.donor < 0) {
+    g.seg[1].w = L.k;
+    g.seg[1].y = w.kraw;
+    g.nseg = 2;
+    const int32_t* vsrc = w.kraw;
+    if (L.v.p) { g.seg[2].w = L.v; g.seg[2].y = w.vraw; g.nseg = 3; vsrc = w.vraw; }
+    qa.k_in = w.kraw; qa.v_in = vsrc; qa.k_cache = q.kc[l]; qa.v_cache = q.vc[l];
+    kcache = q.kc[l];
+    vcache = q.vc[l];
+  } else {
+    kcache = q.kc[lc.donor];
+    vcache = q.vc[lc.donor];
+  }
+  launch_gemv(g, s);
+  launch_qkv_post(qa, s);
+  AttnDecodeArgs aa;
+  aa.pos = q.d_pos; aa.Hq = m.Hq; aa.Hkv = lc.kv_heads; aa.d = d; aa.window = lc.window; aa.q = w.qo;
+  aa.k_cache = kcache; aa.v_cache = vcache; aa.cap = q.cap; aa.out = w.comb; aa.sc = q.asc;
+  aa.rows_per_split = 64;
+  launch_attn_decode(aa, s);
+  GemvArgs go;
+  go.K = m.Hq * d;
+  go.seg[0].w = L.o;
+  go.seg[0].y = w.attn;
+  go.a = w.comb;
+  launch_gemv(go, s);
+  // t1 = x + norm(attn); MLP input = norm(t1)
+  GemvArgs gg;
+  gg.K = H;
+  gg.pro = kProResNorm;
+  gg.a = w.attn; gg.res = cur; gg.g1 = L.post_attn_ln; gg.g2 = L.pre_ff_ln; gg.eps = c.eps; gg.t_out = w.t1;
+  gg.pair_geglu = true;
+  gg.nseg = 2;
+  gg.seg[0].w = L.gate; gg.seg[0].y = w.hbuf;
+  gg.seg[1].w = L.up;
+  launch_gemv(gg, s);
+  GemvArgs gd;
+  gd.K = L.F;
+  gd.seg[0].w = L.down;
+  gd.seg[0].y = w.attn;
+  gd.a = w.hbuf;
+  launch_gemv(gd, s);
+  int32_t* out = q.dec_out + (size_t)l * H;
+  if (m.P > 0) {
+    // t2 = t1 + norm(ff) (stored by block 0); gate = gelu(Wg t2) * ple_in
+    GemvArgs gp;
+    gp.K = H;
+    gp.pro = kProResScale;
+    gp.a = w.attn; gp.res = w.t1; gp.g1 = L.post_ff_ln; gp.eps = c.eps; gp.t_out = w.t2;
+    gp.seg[0].w = L.ple_gate; gp.seg[0].y = w.g; gp.seg[0].epi = kEpiGeluMul;
+    gp.seg[0].vec = w.ple_all + (size_t)l * m.P;
+    launch_gemv(gp, s);
+    GemvArgs gq;
+    gq.K = m.P;
+    gq.seg[0].w = L.ple_proj; gq.seg[0].y = w.pr;
+    gq.a = w.g;
+    launch_gemv(gq, s);
+    launch_norm_residual_rows(w.pr, w.t2, 1, H, L.ple_norm, c.eps, L.has_scalar, L.scalar, out, s);
+  } else {
+    launch_norm_residual_rows(w.attn, w.t1, 1, H, L.post_ff_ln, c.eps, L.has_scalar, L.scalar, out, s);
+  }
+  return out;
+}
+
+static void decode_finalize_launch(Ctx& c, Seq& q, const int32_t* cur) {
+  gemv_logits(c, cur, q.logits, c.stream);
+  launch_add_i32(q.d_pos, 1, c.stream);
+}
+
+// full decode step for the token already in q.d_token (graph-capturable)
+static void decode_step_launch(Ctx& c, Seq& q) {
+  decode_embed(c, q, q.d_token);
+  const int32_t* cur = c.dw.x0;
+  for (int l = 0; l < c.cfg.L; ++l) cur = decode_layer(c, q, l, cur);
+  decode_finalize_launch(c, q, cur);
+}
+
+static void select_launch(Ctx& c, Seq& q) {
+  launch_argmax(q.logits, c.cfg.V, c.dw.argpart, c.argblocks, q.d_token, c.stream);
+}
+
+static void check_decode_ready(Ctx& c, Seq& q) {
+  REQUIRE(q.prefilled, RDET_E_STATE, "decode requires a prefilled sequence");
+  REQUIRE(q.pos < q.cap, RDET_E_RANGE, "sequence KV cache is full");
+  REQUIRE(c.prefill_owner == nullptr, RDET_E_STATE, "a routine-granular prefill is in flight on this context");
+}
+
+static void seq_alloc(Ctx& c, Seq& q, int cap) {
+  const ModelCfg& m = c.cfg;
+  q.ctx = &c;
+  q.device = c.device;
+  q.cap = cap;
+  q.kc.assign(m.L, nullptr);
+  q.vc.assign(m.L, nullptr);
+  for (int l = 0; l < m.L; ++l) {
+    const LayerCfg& lc = m.layers[l];
+    if (lc.donor >= 0) continue;
+    size_t n = (size_t)lc.kv_heads * cap * lc.head_dim;
+    q.kc[l] = static_cast<int32_t*>(q.dalloc(n * 4));
+    q.vc[l] = static_cast<int32_t*>(q.dalloc(n * 4));
+  }
+  q.d_pos = static_cast<int32_t*>(q.dalloc(16));
+  CK(cudaMemset(q.d_pos, 0, 16));
+  q.logits = static_cast<int32_t*>(q.dalloc((size_t)m.V * 4));
+  q.d_token = static_cast<uint32_t*>(q.dalloc(16));
+  q.d_step = static_cast<int32_t*>(q.dalloc(16));
+  q.dec_out = static_cast<int32_t*>(q.dalloc((size_t)m.L * m.H * 4));
+  const int rps = 64;
+  int splits = (cap + rps - 1) / rps;
+  q.asc.max_splits = splits;
+  q.asc.scores = static_cast<int32_t*>(q.dalloc((size_t)m.Hq * cap * 4));
+  q.asc.exps = static_cast<int64_t*>(q.dalloc((size_t)m.Hq * cap * 8));
+  q.asc.pmax = static_cast<int32_t*>(q.dalloc((size_t)m.Hq * splits * 4));
+  q.asc.pidx = static_cast<int32_t*>(q.dalloc((size_t)m.Hq * splits * 4));
+  q.asc.psum = static_cast<int64_t*>(q.dalloc((size_t)m.Hq * splits * 8));
+  q.asc.pwsum = static_cast<int64_t*>(q.dalloc((size_t)m.Hq * splits * 8));
+  q.asc.pacc = static_cast<int64_t*>(q.dalloc((size_t)m.Hq * splits * c.dmax * 8));
+}
+
+// ---------------------------------------------------------------------------
+// commitments / reads
+// ---------------------------------------------------------------------------
+static std::vector<int32_t> d2h(Ctx& c, const int32_t* p, size_t n) {
+  std::vector<int32_t> h(n);
+  if (n) CK(cudaMemcpyAsync(h.data(), p, n * 4, cudaMemcpyDeviceToHost, c.stream));
+  CK(cudaStreamSynchronize(c.stream));
+  return h;
+}
+// rows of the logical cache of (layer, head): trimmed sliding layers keep
+// the last `window` rows (det_tensor.rs:308-337).
+static void kv_rows(Ctx& c, Seq& q, int l, int* start, int* rows) {
+  const LayerCfg& lc = c.cfg.layers[l];
+  int len = q.pos;
+  int keep = (lc.trim && len > lc.window) ? lc.window : len;
+  *start = len - keep;
+  *rows = keep;
+}
+static std::vector<int32_t> kv_read(Ctx& c, Seq& q, int l, int head, bool key) {
+  const LayerCfg& lc = c.cfg.layers[l];
+  int st, rows;
+  kv_rows(c, q, l, &st, &rows);
+  const int32_t* base = (key ? q.kc[l] : q.vc[l]) + ((size_t)head * q.cap + st) * lc.head_dim;
+  return d2h(c, base, (size_t)rows * lc.head_dim);
+}
+static bool kv_commitment(Ctx& c, Seq& q, std::string* out) {
+  const ModelCfg& m = c.cfg;
+  for (int l = 0; l < m.L; ++l)
+    if (!q.kc[l]) return false;  // a KV-sharing layer has no det cache of its own
+  Sha256 h;
+  h.put("raster-det-num-kv-cache-v1", 26);
+  h.put_u64((uint64_t)m.L);
+  for (int l = 0; l < m.L; ++l) {
+    const LayerCfg& lc = m.layers[l];
+    h.put_u64((uint64_t)lc.kv_heads);
+    for (int kind = 0; kind < 2; ++kind) {
+      h.put(kind == 0 ? "k" : "v", 1);
+      h.put_u64((uint64_t)lc.kv_heads);
+      for (int hd = 0; hd < lc.kv_heads; ++hd) {
+        std::vector<int32_t> rows = kv_read(c, q, l, hd, kind == 0);
+        size_t nr = rows.size() / lc.head_dim;
+        h.put_u64(nr);
+        for (size_t r = 0; r < nr; ++r) { h.put_u64((uint64_t)lc.head_dim); h.put(rows.data() + r * lc.head_dim, (size_t)lc.head_dim * 4); }
+      }
+    }
+  }
+  *out = h.hex();
+  return true;
+}
+
+}  // namespace rdet
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+using namespace rdet;
+
+struct rdet_ctx { std::unique_ptr<Ctx> c; };
+struct rdet_seq { std::unique_ptr<Seq> s; rdet_ctx* owner; };
+
+template <typename F>
+static int32_t guard(F&& f) {
+  try {
+    f();
+    return RDET_OK;
+  } catch (const Fail& e) {
+    g_last_error = e.msg;
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    g_last_error = "host out of memory";
+    return RDET_E_OOM;
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return RDET_E_INVALID;
+  }
+}
+
+static void open_common(Ctx& c, const rdet_opts* opts) {
+  c.device = opts ? opts->device : 0;
+  c.max_prefill = (opts && opts->max_prefill) ? opts->max_prefill : 4096;
+  c.flags = opts ? opts->flags : 0;
+  int ndev = 0;
+  CK(cudaGetDeviceCount(&ndev));
+  REQUIRE(c.device >= 0 && c.device < ndev, RDET_E_INVALID, "invalid CUDA device ordinal");
+  CK(cudaSetDevice(c.device));
+  CK(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+}
+
+static std::string read_file(const std::string& path) {
+  FILE* f = fopen(path.c_str(), "rb");
+  REQUIRE(f, RDET_E_IO, "failed to open " + path);
+  std::string s;
+  char buf[65536];
+  size_t n;
+  while ((n = fread(buf, 1, sizeof(buf), f)) > 0) s.append(buf, n);
+  fclose(f);
+  return s;
+}
+
+extern "C" {
+
+const char* rdet_version(void) { return "rdet 0.1 (det_num spec 1, detwgt 2, sm_100a)"; }
+
+int32_t rdet_last_error(char* buf, size_t len) {
+  if (buf && len) snprintf(buf, len, "%s", g_last_error.c_str());
+  return (int32_t)g_last_error.size();
+}
+
+int32_t rdet_open(const char* model_dir, const rdet_opts* opts, rdet_ctx** out) {
+  return guard([&] {
+    REQUIRE(model_dir && out, RDET_E_INVALID, "null argument");
+    auto h = std::make_unique<rdet_ctx>();
+    h->c = std::make_unique<Ctx>();
+    Ctx& c = *h->c;
+    // Parse and validate everything on the host before touching the GPU, so
+    // malformed models fail closed with RDET_E_FORMAT on any machine.
+    std::string dir(model_dir);
+    c.cfg = parse_config(read_file(dir + "/config.json"));
+    std::string wpath = dir + "/model.detwgt";
+    int fd = open(wpath.c_str(), O_RDONLY);
+    REQUIRE(fd >= 0, RDET_E_IO, "failed to open deterministic artifact " + wpath);
+    struct stat st;
+    fstat(fd, &st);
+    MappedFile mf;
+    mf.size = (size_t)st.st_size;
+    mf.base = mf.size ? mmap(nullptr, mf.size, PROT_READ, MAP_PRIVATE, fd, 0) : nullptr;
+    close(fd);
+    REQUIRE(mf.size == 0 || mf.base != MAP_FAILED, RDET_E_IO, "failed to mmap deterministic artifact " + wpath);
+    auto tab = parse_detwgt(static_cast<const uint8_t*>(mf.base), mf.size);
+    {
+      Ctx probe;  // dry pass: every tensor the model needs exists with the right shape
+      probe.cfg = c.cfg;
+      build_model(probe, tab, false, 0, true);
+    }
+    open_common(c, opts);
+    build_model(c, tab, false, 0);
+    alloc_workspaces(c);
+    *out = h.release();
+  });
+}
+
+int32_t rdet_open_synthetic(const char* config_json, uint64_t seed, int32_t width, const rdet_opts* opts,
+                            rdet_ctx** out) {
+  return guard([&] {
+    REQUIRE(config_json && out, RDET_E_INVALID, "null argument");
+    REQUIRE(width == 16 || width == 32, RDET_E_INVALID, "width must be 16 or 32");
+    auto h = std::make_unique<rdet_ctx>();
+    h->c = std::make_unique<Ctx>();
+    Ctx& c = *h->c;
+    c.cfg = parse_config(config_json);
+    json::Value root = json::parse(config_json);
+    const json::Value& t = text_cfg(root);
+    int F = (int)req_int(t, "intermediate_size");
+    auto tab = synthetic_table(c.cfg, t, width, F);
+    open_common(c, opts);
+    build_model(c, tab, true, seed);
+    alloc_workspaces(c);
+    *out = h.release();
+  });
+}
+
+int32_t rdet_close(rdet_ctx* ctx) {
+  return guard([&] {
+    if (!ctx) return;
+    // Sequences still open on this context are freed with it; their handles
+    // must not be used afterwards.
+    std::vector<void*> live = ctx->c->live_seqs;
+    for (void* p : live) delete static_cast<rdet_seq*>(p);
+    delete ctx;
+  });
+}
+
+int32_t rdet_get_model_info(rdet_ctx* ctx, rdet_model_info* out) {
+  return guard([&] {
+    REQUIRE(ctx && out, RDET_E_INVALID, "null argument");
+    const Ctx& c = *ctx->c;
+    out->hidden_size = c.cfg.H;
+    out->vocab_size = c.cfg.V;
+    out->num_layers = c.cfg.L;
+    out->num_heads = c.cfg.Hq;
+    out->ple_dim = c.cfg.P;
+    out->intermediate_size = c.F;
+    out->weight_bytes = c.weight_bytes;
+  });
+}
+
+int32_t rdet_seq_new(rdet_ctx* ctx, uint32_t max_ctx, rdet_seq** out) {
+  return guard([&] {
+    REQUIRE(ctx && out, RDET_E_INVALID, "null argument");
+    REQUIRE(max_ctx > 0, RDET_E_INVALID, "max_ctx must be positive");
+    CK(cudaSetDevice(ctx->c->device));
+    auto h = std::make_unique<rdet_seq>();
+    h->s = std::make_unique<Seq>();
+    h->owner = ctx;
+    seq_alloc(*ctx->c, *h->s, (int)max_ctx);
+    ctx->c->live_seqs.push_back(h.get());
+    *out = h.release();
+  });
+}
+
+int32_t rdet_seq_free(rdet_seq* seq) {
+  return guard([&] {
+    if (!seq) return;
+    Ctx& c = *seq->owner->c;
+    if (c.prefill_owner == seq->s.get()) c.prefill_owner = nullptr;
+    if (c.decode_owner == seq->s.get()) c.decode_owner = nullptr;
+    auto it = std::find(c.live_seqs.begin(), c.live_seqs.end(), (void*)seq);
+    REQUIRE(it != c.live_seqs.end(), RDET_E_INVALID, "unknown sequence handle");
+    c.live_seqs.erase(it);
+    delete seq;
+  });
+}
+
+int32_t rdet_seq_position(rdet_seq* seq, uint32_t* position) {
+  return guard([&] {
+    REQUIRE(seq && position, RDET_E_INVALID, "null argument");
+    *position = (uint32_t)seq->s->pos;
+  });
+}
+
+int32_t rdet_embed(rdet_ctx* ctx, const uint32_t* ids, size_t n, int32_t* act_out) {
+  return guard([&] {
+    REQUIRE(ctx && ids && act_out, RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    CK(cudaSetDevice(c.device));
+    REQUIRE(n > 0, RDET_E_INVALID, "transformer embedding requires at least one token id");
+    REQUIRE(n <= c.max_prefill, RDET_E_RANGE, "too many token ids");
+    REQUIRE(c.prefill_owner == nullptr, RDET_E_STATE, "a routine-granular prefill is in flight on this context");
+    for (size_t i = 0; i < n; ++i)
+      REQUIRE(ids[i] < (uint32_t)c.emb.rows, RDET_E_RANGE, "token id " + std::to_string(ids[i]) + " is out of bounds for embedding tensor");
+    CK(cudaMemcpyAsync(c.pw.ids, ids, n * 4, cudaMemcpyHostToDevice, c.stream));
+    launch_embed(c.pw.ids, (int)n, c.emb, c.emb_scale, c.pw.x0, c.d_err, c.stream);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(act_out, c.pw.x0, n * c.cfg.H * 4, cudaMemcpyDeviceToHost, c.stream));
+    check_err_flag(c, "embed");
+  });
+}
+
+int32_t rdet_prefill_begin(rdet_ctx* ctx, rdet_seq* seq, const uint32_t* ids, size_t n) {
+  return guard([&] {
+    REQUIRE(ctx && seq && ids, RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    CK(cudaSetDevice(c.device));
+    REQUIRE(seq->owner == ctx, RDET_E_INVALID, "sequence belongs to another context");
+    REQUIRE(c.prefill_owner == nullptr || c.prefill_owner == seq->s.get(), RDET_E_STATE, "another prefill is in flight on this context");
+    prefill_begin(c, *seq->s, ids, n);
+  });
+}
+
+int32_t rdet_prefill_range(rdet_ctx* ctx, rdet_seq* seq, uint32_t layer_start, uint32_t layer_end) {
+  return guard([&] {
+    REQUIRE(ctx && seq, RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    Seq& q = *seq->s;
+    CK(cudaSetDevice(c.device));
+    REQUIRE(c.prefill_owner == &q, RDET_E_STATE, "prefill.range requires prefill_begin on this sequence");
+    REQUIRE((int)layer_start == q.prefill_next, RDET_E_STATE, "prefill.range must continue at the next layer");
+    REQUIRE(layer_end >= layer_start && (int)layer_end <= c.cfg.L, RDET_E_RANGE, "layer range out of bounds");
+    for (uint32_t l = layer_start; l < layer_end; ++l) {
+      prefill_layer(c, q, (int)l);
+      q.prefill_next = (int)l + 1;
+    }
+    CK(cudaStreamSynchronize(c.stream));
+  });
+}
+
+int32_t rdet_prefill_finalize(rdet_ctx* ctx, rdet_seq* seq) {
+  return guard([&] {
+    REQUIRE(ctx && seq, RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    CK(cudaSetDevice(c.device));
+    REQUIRE(c.prefill_owner == seq->s.get(), RDET_E_STATE, "prefill.finalize requires prefill_begin on this sequence");
+    prefill_finalize(c, *seq->s);
+  });
+}
+
+int32_t rdet_prefill(rdet_ctx* ctx, rdet_seq* seq, const uint32_t* ids, size_t n) {
+  int32_t rc = rdet_prefill_begin(ctx, seq, ids, n);
+  if (rc != RDET_OK) return rc;
+  rc = rdet_prefill_range(ctx, seq, 0, ctx->c->cfg.L);
+  if (rc != RDET_OK) { ctx->c->prefill_owner = nullptr; return rc; }
+  rc = rdet_prefill_finalize(ctx, seq);
+  if (rc != RDET_OK) ctx->c->prefill_owner = nullptr;
+  return rc;
+}
+
+int32_t rdet_select(rdet_ctx* ctx, rdet_seq* seq, uint32_t* token_out) {
+  return guard([&] {
+    REQUIRE(ctx && seq && token_out, RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    Seq& q = *seq->s;
+    CK(cudaSetDevice(c.device));
+    REQUIRE(q.prefilled, RDET_E_STATE, "select requires logits (run prefill first)");
+    select_launch(c, q);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(token_out, q.d_token, 4, cudaMemcpyDeviceToHost, c.stream));
+    CK(cudaStreamSynchronize(c.stream));
+  });
+}
+
+int32_t rdet_decode_begin(rdet_ctx* ctx, rdet_seq* seq, uint32_t token) {
+  return guard([&] {
+    REQUIRE(ctx && seq, RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    Seq& q = *seq->s;
+    CK(cudaSetDevice(c.device));
+    check_decode_ready(c, q);
+    REQUIRE(c.decode_owner == nullptr || c.decode_owner == &q, RDET_E_STATE, "another decode is in flight on this context");
+    REQUIRE(token < (uint32_t)c.emb.rows, RDET_E_RANGE, "token id " + std::to_string(token) + " is out of bounds for embedding tensor");
+    if (c.cfg.P > 0) REQUIRE(token < (uint32_t)c.cfg.ple_vocab, RDET_E_RANGE, "token id is out of bounds for the PLE table");
+    CK(cudaMemcpyAsync(q.d_token, &token, 4, cudaMemcpyHostToDevice, c.stream));
+    decode_embed(c, q, q.d_token);
+    CK(cudaGetLastError());
+    q.decode_next = 0;
+    q.decode_cur = c.dw.x0;
+    c.decode_owner = &q;
+  });
+}
+
+int32_t rdet_decode_range(rdet_ctx* ctx, rdet_seq* seq, uint32_t layer_start, uint32_t layer_end) {
+  return guard([&] {
+    REQUIRE(ctx && seq, RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    Seq& q = *seq->s;
+    CK(cudaSetDevice(c.device));
+    REQUIRE(c.decode_owner == &q, RDET_E_STATE, "decode.layer_range requires decode_begin on this sequence");
+    REQUIRE((int)layer_start == q.decode_next, RDET_E_STATE, "decode.layer_range must continue at the next layer");
+    REQUIRE(layer_end >= layer_start && (int)layer_end <= c.cfg.L, RDET_E_RANGE, "layer range out of bounds");
+    for (uint32_t l = layer_start; l < layer_end; ++l) {
+      q.decode_cur = const_cast<int32_t*>(decode_layer(c, q, (int)l, q.decode_cur));
+      q.decode_next = (int)l + 1;
+    }
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(c.stream));
+  });
+}
+
+int32_t rdet_decode_finalize(rdet_ctx* ctx, rdet_seq* seq) {
+  return guard([&] {
+    REQUIRE(ctx && seq, RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    Seq& q = *seq->s;
+    CK(cudaSetDevice(c.device));
+    REQUIRE(c.decode_owner == &q && q.decode_next == c.cfg.L, RDET_E_STATE,
+            "decode.transition_finalize requires all layers");
+    decode_finalize_launch(c, q, q.decode_cur);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(c.stream));
+    check_err_flag(c, "decode");
+    q.pos += 1;
+    q.last_was_prefill = false;
+    q.decode_next = -1;
+    c.decode_owner = nullptr;
+  });
+}
+
+int32_t rdet_decode(rdet_ctx* ctx, rdet_seq* const* seqs, const uint32_t* tokens, size_t nseq) {
+  if (!ctx || (nseq && (!seqs || !tokens))) {
+    g_last_error = "null argument";
+    return RDET_E_INVALID;
+  }
+  for (size_t i = 0; i < nseq; ++i) {
+    int32_t rc = rdet_decode_begin(ctx, seqs[i], tokens[i]);
+    if (rc == RDET_OK) rc = rdet_decode_range(ctx, seqs[i], 0, ctx->c->cfg.L);
+    if (rc == RDET_OK) rc = rdet_decode_finalize(ctx, seqs[i]);
+    if (rc != RDET_OK) {
+      ctx->c->decode_owner = nullptr;
+      return rc;
+    }
+  }
+  return RDET_OK;
+}
+
+int32_t rdet_generate(rdet_ctx* ctx, rdet_seq* seq, uint32_t n_tokens, uint32_t* tokens_out) {
+  return guard([&] {
+    REQUIRE(ctx && seq && (tokens_out || n_tokens == 0), RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    Seq& q = *seq->s;
+    CK(cudaSetDevice(c.device));
+    check_decode_ready(c, q);
+    REQUIRE(c.decode_owner == nullptr, RDET_E_STATE, "a routine-granular decode is in flight on this context");
+    REQUIRE(q.pos + (int)n_tokens <= q.cap, RDET_E_RANGE, "generation would overflow the sequence KV cache");
+    if (!q.graph) {
+      cudaGraph_t g;
+      CK(cudaStreamBeginCapture(c.stream, cudaStreamCaptureModeThreadLocal));
+      select_launch(c, q);
+      decode_step_launch(c, q);
+      cudaError_t e = cudaStreamEndCapture(c.stream, &g);
+      if (e != cudaSuccess) throw Fail{RDET_E_CUDA, std::string("graph capture failed: ") + cudaGetErrorString(e)};
+      e = cudaGraphInstantiate(&q.graph, g, 0);
+      cudaGraphDestroy(g);
+      if (e != cudaSuccess) { q.graph = nullptr; throw Fail{RDET_E_CUDA, std::string("graph instantiate failed: ") + cudaGetErrorString(e)}; }
+    }
+    if (q.hist_cap < (int)n_tokens) {
+      q.d_hist = static_cast<uint32_t*>(q.dalloc((size_t)std::max<uint32_t>(n_tokens, 1) * 4));
+      q.hist_cap = (int)n_tokens;
+    }
+    for (uint32_t i = 0; i < n_tokens; ++i) {
+      CK(cudaGraphLaunch(q.graph, c.stream));
+      CK(cudaMemcpyAsync(q.d_hist + i, q.d_token, 4, cudaMemcpyDeviceToDevice, c.stream));
+    }
+    if (n_tokens) CK(cudaMemcpyAsync(tokens_out, q.d_hist, (size_t)n_tokens * 4, cudaMemcpyDeviceToHost, c.stream));
+    CK(cudaStreamSynchronize(c.stream));
+    check_err_flag(c, "generate");
+    q.pos += (int)n_tokens;
+    q.last_was_prefill = false;
+  });
+}
+
+int32_t rdet_read(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t layer, int32_t arg, void* dst, size_t bytes,
+                  size_t* size_out) {
+  return guard([&] {
+    REQUIRE(ctx && seq, RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    Seq& q = *seq->s;
+    CK(cudaSetDevice(c.device));
+    const int H = c.cfg.H;
+    std::vector<int32_t> v;
+    switch (which) {
+      case RDET_BUF_EMBEDDING:
+        REQUIRE(q.embd && q.last_S > 0, RDET_E_STATE, "no prefill embedding available");
+        v = d2h(c, q.embd, (size_t)q.last_S * H);
+        break;
+      case RDET_BUF_HIDDEN:
+        if (q.last_was_prefill) {
+          REQUIRE(q.hid && q.last_S > 0, RDET_E_STATE, "no hidden states available");
+          v = d2h(c, q.hid, (size_t)q.last_S * H);
+        } else {
+          v = d2h(c, q.dec_out + (size_t)(c.cfg.L - 1) * H, H);
+        }
+        break;
+      case RDET_BUF_LOGITS:
+        REQUIRE(q.prefilled, RDET_E_STATE, "no logits available");
+        v = d2h(c, q.logits, c.cfg.V);
+        break;
+      case RDET_BUF_LAYER_OUTPUT:
+        REQUIRE(layer >= 0 && layer < c.cfg.L, RDET_E_RANGE, "layer out of range");
+        REQUIRE(!q.last_was_prefill, RDET_E_STATE, "prefill layer outputs are available as commitments only");
+        v = d2h(c, q.dec_out + (size_t)layer * H, H);
+        break;
+      case RDET_BUF_KV_K:
+      case RDET_BUF_KV_V:
+        REQUIRE(layer >= 0 && layer < c.cfg.L, RDET_E_RANGE, "layer out of range");
+        REQUIRE(q.kc[layer], RDET_E_STATE, "layer shares the KV cache of an earlier layer");
+        REQUIRE(arg >= 0 && arg < c.cfg.layers[layer].kv_heads, RDET_E_RANGE, "kv head out of range");
+        v = kv_read(c, q, layer, arg, which == RDET_BUF_KV_K);
+        break;
+      default:
+        throw Fail{RDET_E_INVALID, "unknown buffer"};
+    }
+    if (size_out) *size_out = v.size() * 4;
+    if (dst) memcpy(dst, v.data(), std::min(bytes, v.size() * 4));
+  });
+}
+
+int32_t rdet_commitment(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t layer, char* hex_out) {
+  int32_t none = 0;
+  int32_t rc = guard([&] {
+    REQUIRE(ctx && seq && hex_out, RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    Seq& q = *seq->s;
+    CK(cudaSetDevice(c.device));
+    const int H = c.cfg.H;
+    std::string hx;
+    switch (which) {
+      case RDET_BUF_EMBEDDING: {
+        REQUIRE(q.embd && q.last_S > 0, RDET_E_STATE, "no prefill embedding available");
+        auto v = d2h(c, q.embd, (size_t)q.last_S * H);
+        hx = act_hash_rows(v.data(), q.last_S, H);
+        break;
+      }
+      case RDET_BUF_HIDDEN: {
+        if (q.last_was_prefill) {
+          REQUIRE(q.hid && q.last_S > 0, RDET_E_STATE, "no hidden states available");
+          auto v = d2h(c, q.hid, (size_t)q.last_S * H);
+          hx = act_hash_rows(v.data(), q.last_S, H);
+        } else {
+          auto v = d2h(c, q.dec_out + (size_t)(c.cfg.L - 1) * H, H);
+          hx = act_hash_rows(v.data(), 1, H);
+        }
+        break;
+      }
+      case RDET_BUF_LOGITS: {
+        REQUIRE(q.prefilled, RDET_E_STATE, "no logits available");
+        auto v = d2h(c, q.logits, c.cfg.V);
+        Sha256 h;
+        h.put("raster-det-num-act-vector-v1", 28);
+        h.put_u64(v.size());
+        h.put(v.data(), v.size() * 4);
+        hx = h.hex();
+        break;
+      }
+      case RDET_BUF_LAYER_OUTPUT: {
+        REQUIRE(layer >= 0 && layer < c.cfg.L, RDET_E_RANGE, "layer out of range");
+        if (q.last_was_prefill) {
+          REQUIRE(!q.layer_hashes.empty() && !q.layer_hashes[layer].empty(), RDET_E_STATE,
+                  "per-layer prefill commitments need RDET_FLAG_LAYER_COMMITMENTS");
+          hx = q.layer_hashes[layer];
+        } else {
+          auto v = d2h(c, q.dec_out + (size_t)layer * H, H);
+          hx = act_hash_rows(v.data(), 1, H);
+        }
+        break;
+      }
+      case RDET_BUF_KV:
+        if (!kv_commitment(c, q, &hx)) { none = 1; return; }
+        break;
+      default:
+        throw Fail{RDET_E_INVALID, "unknown buffer"};
+    }
+    memcpy(hex_out, hx.c_str(), 65);
+  });
+  if (rc == RDET_OK && none) { hex_out[0] = 0; return RDET_NONE; }
+  return rc;
+}
+
+int32_t rdet_det_gemv(const int32_t* x, const void* w, int32_t width, uint32_t rows, uint32_t cols, int32_t* y,
+                      void* stream) {
+  return guard([&] {
+    REQUIRE(x && w && y, RDET_E_INVALID, "null argument");
+    REQUIRE(width == 16 || width == 32, RDET_E_INVALID, "width must be 16 or 32");
+    REQUIRE(rows > 0 && cols > 0 && cols <= 49152, RDET_E_RANGE, "unsupported GEMV shape");
+    REQUIRE(((uintptr_t)w & 15) == 0 && ((uintptr_t)x & 15) == 0, RDET_E_INVALID,
+            "weights and input must be 16-byte aligned");
+    GemvArgs g;
+    g.K = (int)cols;
+    g.seg[0].w.p = w;
+    g.seg[0].w.width = width;
+    g.seg[0].w.rows = (int)rows;
+    g.seg[0].w.cols = (int)cols;
+    g.seg[0].y = y;
+    g.a = x;
+    launch_gemv(g, static_cast<cudaStream_t>(stream));
+    CK(cudaGetLastError());
+  });
+}
+
+int32_t rdet_det_linear(const int32_t* x, uint32_t n_rows_x, const void* w, int32_t width, uint32_t rows,
+                        uint32_t cols, int32_t* y, void* stream) {
+  return guard([&] {
+    REQUIRE(x && w && y, RDET_E_INVALID, "null argument");
+    REQUIRE(width == 16 || width == 32, RDET_E_INVALID, "width must be 16 or 32");
+    REQUIRE(rows > 0 && cols > 0 && n_rows_x > 0, RDET_E_RANGE, "unsupported linear shape");
+    DevMat m;
+    m.p = w;
+    m.width = width;
+    m.rows = (int)rows;
+    m.cols = (int)cols;
+    launch_linear(x, (int)n_rows_x, m, y, kEpiPlain, nullptr, static_cast<cudaStream_t>(stream));
+    CK(cudaGetLastError());
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,74 @@
+"""det GEMV / linear kernels vs the oracle, bit-exact, through the C ABI on
+device buffers (torch is used only to hold device memory)."""
+import numpy as np
+import pytest
+
+import oracle as O
+from helpers import rdet
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+I32_MIN, I32_MAX = -2**31, 2**31 - 1
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def rand_w(rng, rows, cols, width, adversarial=False):
+    if width == 16:
+        w = rng.integers(-32768, 32768, (rows, cols), dtype=np.int64).astype(np.int16)
+        if adversarial:
+            w.flat[::3] = -32768
+            w.flat[1::3] = 32767
+        return w
+    bound = (2**31 - 1) // cols
+    w = rng.integers(-bound, bound + 1, (rows, cols), dtype=np.int64).astype(np.int32)
+    if adversarial:
+        w.flat[::2] = bound
+    return w
+
+
+def rand_x(rng, n, adversarial=False):
+    x = rng.integers(I32_MIN, I32_MAX, n, dtype=np.int64).astype(np.int32) if adversarial else \
+        rng.normal(0, 65536 * 4, n).astype(np.int64).clip(I32_MIN, I32_MAX).astype(np.int32)
+    if adversarial:
+        x[::5] = I32_MIN
+        x[1::5] = I32_MAX
+    return x
+
+
+SHAPES = [(1, 8), (7, 4), (33, 24), (300, 12), (129, 1000), (513, 2560), (2048, 2560), (2560, 10240)]
+
+
+@pytest.mark.parametrize("width", [16, 32])
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("adv", [False, True])
+def test_gemv_bit_exact(width, shape, adv):
+    rng = np.random.default_rng(hash((width, shape, adv)) & 0xFFFF)
+    rows, cols = shape
+    w = rand_w(rng, rows, cols, width, adv)
+    x = rand_x(rng, cols, adv)
+    y = torch.zeros(rows, dtype=torch.int32, device="cuda")
+    wd, xd = dev(w), dev(x)
+    rdet.det_gemv(xd.data_ptr(), wd.data_ptr(), width, rows, cols, y.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(y.cpu().numpy(), O.gemv(x, w))
+
+
+@pytest.mark.parametrize("width", [16, 32])
+@pytest.mark.parametrize("S,rows,cols", [(1, 64, 64), (5, 70, 33), (64, 128, 256), (130, 96, 520), (17, 2560, 512)])
+def test_linear_bit_exact(width, S, rows, cols):
+    rng = np.random.default_rng(S * 1000 + rows + width)
+    w = rand_w(rng, rows, cols, width, True)
+    X = np.stack([rand_x(rng, cols, adversarial=(i % 2 == 0)) for i in range(S)])
+    Y = torch.zeros((S, rows), dtype=torch.int32, device="cuda")
+    rdet.det_linear(dev(X).data_ptr(), S, dev(w).data_ptr(), width, rows, cols, Y.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(Y.cpu().numpy(), O.linear(X, w))
+
+
+def test_gemv_rejects_bad_width():
+    with pytest.raises(rdet.RdetError):
+        rdet.det_gemv(1, 1, 8, 4, 4, 1)
