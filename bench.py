@@ -1,0 +1,349 @@
+#!/usr/bin/env python
+"""Benchmark of the det decode path at the Gemma-4-E4B (stand-in) shape.
+
+One step = one greedy token of the reference's decode loop
+(executors/native.rs:265-450): select_output_token (argmax_first over the
+logits) followed by decode_transition (embedding, PLE input, every layer with
+its KV append and attention over the 4096-token context, final norm,
+lm_head, softcap).  The model is the seeded random-init E4B stand-in
+(raster-inference_b200/configs/e4b_text_standin.json, i16 weights, ~15 GB in
+HBM); the prompt is 4096 seeded uniform-random token ids, prefilled on the GPU
+before timing.  Each step streams every weight once (~9 GB > L2), so no L2
+flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Multi-GPU: the decode of one sequence is not sharded here; each rank runs an
+independent replica (its own sequence), timed on the device and reduced with
+the max over ranks ("scaling": "weak").
+
+Also reported: the det-GEMV roofline (E4B projection shapes, CUDA events on
+the launching stream), prefill tok/s of the 4096-token prompt, the end-to-end
+number through the C ABI with host buffers, and the CPU baseline (the C++
+restatement of the reference det path on the host cores, a bounded sample).
+"""
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+METRIC = "det decode & prefill tok/s (E4B shape, bit-exact); det-GEMV HBM GB/s vs peak"
+CONFIG_PATH = os.path.join(ROOT, "raster-inference_b200", "configs", "e4b_text_standin.json")
+SEED = 20260501
+
+
+def lcg_ids(n, vocab, seed):
+    s, out = seed, []
+    for _ in range(n):
+        s = (s * 6364136223846793005 + 1442695040888963407) & 0xFFFFFFFFFFFFFFFF
+        out.append((s >> 33) % vocab)
+    return out
+
+
+def load_config():
+    with open(CONFIG_PATH) as f:
+        return json.load(f)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.p:
+            self.p.terminate()
+            try:
+                out, _ = self.p.communicate(timeout=10)
+            except Exception:
+                self.p.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU: the oracle (C++ restatement of the reference det path) on host cores
+# ---------------------------------------------------------------------------
+def cpu_decode_rate(cfg, ctx, steps, threads):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O  # CPU baseline only
+    O.set_threads(threads)
+    t0 = time.perf_counter()
+    m = O.Model(None, synthetic=(cfg, SEED, 16))
+    s = m.seq()
+    s.fill_synthetic(ctx, seed=7)
+    setup = time.perf_counter() - t0
+    times = []
+    tok = 1
+    for _ in range(steps):
+        t = time.perf_counter()
+        _, logits, _ = s.decode(tok, want_layer_hashes=False)
+        tok = O.argmax_first(logits)
+        times.append(time.perf_counter() - t)
+    m.close()
+    return times, setup
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return  # the CPU arm runs on rank 0 only
+    cfg = load_config()
+    cores = host_cores()
+    times, _ = cpu_decode_rate(cfg, args.ctx, args.warmup + args.steps, cores)
+    timed = times[args.warmup:]
+    total = sum(timed)
+    value = len(timed) / total
+    sample = (f"{len(timed)} greedy decode steps at context {args.ctx} (seeded synthetic KV cache) on the E4B stand-in, "
+              f"{cores} threads, {cpu_model()}")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(timed),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64",
+            "data": "synthetic (seeded random-init weights of the E4B stand-in shape)",
+            "config": {"workload": "det greedy decode, batch 1, context 4096, E4B stand-in (config 4)",
+                       "model": "gemma-4-e4b-text-standin", "context": args.ctx},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU
+# ---------------------------------------------------------------------------
+def gemv_roofline(torch, rdet, cfg, device, rounds=12):
+    """det-GEMV at the E4B projection shapes, timed per launch with CUDA events
+    on the stream the kernel is launched on; weights are distinct matrices
+    (one layer's worth, ~185 MB > L2), so every launch streams from HBM."""
+    t = cfg["text_config"]
+    H, F, Hq, kv, d, dg, V, P, L = (t["hidden_size"], t["intermediate_size"], t["num_attention_heads"],
+                                    t["num_key_value_heads"], t["head_dim"], t["global_head_dim"],
+                                    t["vocab_size"], t["hidden_size_per_layer_input"], t["num_hidden_layers"])
+    shapes = {"q": (Hq * d, H), "k": (kv * d, H), "v": (kv * d, H), "o": (H, Hq * d), "gate": (F, H),
+              "up": (F, H), "down": (H, F), "q_full": (Hq * dg, H), "o_full": (H, Hq * dg),
+              "ple_model_proj": (L * P, H), "lm_head": (V, H)}
+    g = torch.Generator(device=f"cuda:{device}").manual_seed(3)
+    mats = {k: torch.randint(-32768, 32768, s, dtype=torch.int16, device=f"cuda:{device}", generator=g)
+            for k, s in shapes.items()}
+    xs = {k: torch.randint(-(1 << 20), 1 << 20, (s[1],), dtype=torch.int32, device=f"cuda:{device}", generator=g)
+          for k, s in shapes.items()}
+    ys = {k: torch.empty(s[0], dtype=torch.int32, device=f"cuda:{device}") for k, s in shapes.items()}
+    stream = torch.cuda.Stream(device=device)
+    per = {k: [] for k in shapes}
+    with torch.cuda.stream(stream):
+        for r in range(rounds + 2):
+            for k, (n, kk) in shapes.items():
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                rdet.det_gemv(xs[k].data_ptr(), mats[k].data_ptr(), 16, n, kk, ys[k].data_ptr(), stream.cuda_stream)
+                e1.record(stream)
+                if r >= 2:
+                    per[k].append((e0, e1))
+    stream.synchronize()
+    out, tot_b, tot_t = {}, 0.0, 0.0
+    for k, (n, kk) in shapes.items():
+        ms = statistics.mean(a.elapsed_time(b) for a, b in per[k])
+        b = n * kk * 2 + kk * 4 + n * 4
+        out[k] = {"rows": n, "cols": kk, "us": ms * 1000, "gbs": b / (ms * 1e-3) / 1e9}
+        tot_b += b
+        tot_t += ms * 1e-3
+    return out, tot_b / tot_t / 1e9, tot_b / len(shapes), tot_t / len(shapes)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    rdet = importlib.import_module("raster-inference_b200")
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device(f"cuda:{local_rank}"))
+    cfg = load_config()
+    t = cfg["text_config"]
+    ctx = args.ctx
+    model = rdet.Model.synthetic(cfg, SEED, width=16, device=local_rank, max_prefill=ctx)
+    stream = torch.cuda.ExternalStream(model.stream, device=f"cuda:{local_rank}")
+    seq = model.new_sequence(ctx + args.warmup + args.steps + 64)
+    ids = lcg_ids(ctx, t["vocab_size"], SEED + rank)
+    # prefill of the 4096-token prompt (timed for the prefill field)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    seq.prefill(ids)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prefill_s = e0.elapsed_time(e1) / 1000
+    # warm-up (captures the decode graph)
+    seq.generate(args.warmup)
+    kernels_per_step = seq.kernels_per_step() + 2  # + the two argmax kernels of select
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        toks = seq.generate(args.steps)
+        b.record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    sec = a.elapsed_time(b) / 1000
+    if dist:
+        tt = torch.tensor([sec, prefill_s], dtype=torch.float64, device=f"cuda:{local_rank}")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        sec, prefill_s = float(tt[0]), float(tt[1])
+    value = world * args.steps / sec
+    # end to end through the C ABI with host buffers: decode_transition(token
+    # from host) + select_output_token (token back to host), every step
+    n_e2e = min(args.steps, 32)
+    tok = toks[-1]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        seq.decode(tok)
+        tok = seq.select()
+    e2e_sec = time.perf_counter() - t0
+    if dist:
+        tt = torch.tensor([e2e_sec], dtype=torch.float64, device=f"cuda:{local_rank}")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_sec = float(tt[0])
+    e2e = {"value": world * n_e2e / e2e_sec, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+           "steps": n_e2e}
+    # roofline of the dominant kernel (det GEMV)
+    per, gbs, bytes_per_launch, sec_per_launch = gemv_roofline(torch, rdet, cfg, local_rank)
+    peak, peak_kind = peaks()
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "gemv_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch_e4b_mix")
+    weight_bytes = model.weight_bytes
+    if dist:
+        dist.barrier()
+    if rank != 0:
+        seq.free()
+        model.close()
+        if dist:
+            dist.destroy_process_group()
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * sec / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int64",
+        "data": "synthetic (seeded random-init i16 weights of the E4B stand-in shape; seeded uniform prompt ids)",
+        "config": {"workload": "det greedy decode, batch 1, context 4096, E4B stand-in (config 4)",
+                   "model": "gemma-4-e4b-text-standin", "context": ctx, "global_batch": world,
+                   "parallelism": f"replicas{world}", "l2": "inputs larger than L2 (all weights streamed every step)",
+                   "weight_bytes_hbm": weight_bytes},
+        "prefill": {"tokens": ctx, "tok_s": ctx / prefill_s, "seconds": prefill_s},
+        "e2e": e2e,
+        "gpu_launches": kernels_per_step * args.steps,
+        "roofline": {"bound": "hbm", "kernel": "rdet::gemv_kernel", "achieved": gbs, "peak": peak,
+                     "unit": "GB/s", "frac": gbs / peak, "peak_kind": peak_kind,
+                     "traffic": traffic, "algorithmic_bytes_per_launch": bytes_per_launch,
+                     "us_per_launch": sec_per_launch * 1e6,
+                     "per_shape_gbs": {k: round(v["gbs"], 1) for k, v in per.items()}},
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        cores = host_cores()
+        times, _ = cpu_decode_rate(cfg, ctx, 2, cores)
+        line["cpu_baseline"] = {"value": 1.0 / times[-1], "unit": "tok/s", "cores": cores, "kind": "port",
+                                "sample": f"1 greedy decode step (after 1 warm-up) at context {ctx}, seeded synthetic "
+                                          f"KV cache, E4B stand-in, {cores} threads, {cpu_model()}"}
+    print(json.dumps(line), flush=True)
+    seq.free()
+    model.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args, rank)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

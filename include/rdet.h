@@ -108,8 +108,9 @@ int32_t rdet_decode_range(rdet_ctx* ctx, rdet_seq* seq, uint32_t layer_start, ui
 int32_t rdet_decode_finalize(rdet_ctx* ctx, rdet_seq* seq);
 
 /* Greedy generation on the device (native.rs:265-450 loop: select ->
- * decode_transition), replayed as one CUDA graph per token.  Writes
- * n_tokens selected ids; the last selected token is not decoded. */
+ * decode_transition, n_tokens times), each decode_transition replayed as the
+ * sequence's CUDA graph.  Writes the n_tokens selected ids; logits of the
+ * last decode stay resident. */
 int32_t rdet_generate(rdet_ctx* ctx, rdet_seq* seq, uint32_t n_tokens, uint32_t* tokens_out);
 
 /* ---- canonical bytes and commitments ----------------------------------------
@@ -134,6 +135,13 @@ int32_t rdet_det_gemv(const int32_t* x, const void* w, int32_t width, uint32_t r
                       void* stream);
 int32_t rdet_det_linear(const int32_t* x, uint32_t n_rows_x, const void* w, int32_t width, uint32_t rows,
                         uint32_t cols, int32_t* y, void* stream);
+
+/* The CUDA stream (cudaStream_t) on which the context launches all of its
+ * work, for callers that order their own work or CUDA events against it. */
+int32_t rdet_get_stream(rdet_ctx* ctx, void** stream);
+/* Number of kernels in one captured decode_transition (the sequence's decode
+ * CUDA graph; captured on the first rdet_decode / rdet_generate). */
+int32_t rdet_seq_kernels_per_step(rdet_seq* seq, uint32_t* kernels);
 
 int32_t rdet_last_error(char* buf, size_t len);
 const char* rdet_version(void);

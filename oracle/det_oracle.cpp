@@ -26,6 +26,8 @@
 // drivers, det_kernels.rs:156-178), so results are thread-count independent.
 #include <algorithm>
 #include <atomic>
+#include <condition_variable>
+#include <mutex>
 #include <cmath>
 #include <cstdio>
 #include <functional>
@@ -42,23 +44,83 @@
 using namespace dor;
 
 // ---------------------------------------------------------------------------
-// threading
+// threading: a persistent pool (like the reference's global rayon pool);
+// parallel_for splits [0, n) into contiguous chunks, one per worker.
 // ---------------------------------------------------------------------------
 static int g_threads = 1;
 
-static void parallel_for(size_t n, const std::function<void(size_t, size_t)>& fn) {
-  int t = g_threads;
-  if (t <= 1 || n < 2) { fn(0, n); return; }
-  if ((size_t)t > n) t = (int)n;
-  std::vector<std::thread> ths;
-  size_t chunk = (n + t - 1) / t;
-  for (int i = 0; i < t; ++i) {
-    size_t lo = i * chunk, hi = std::min(n, lo + chunk);
-    if (lo >= hi) break;
-    ths.emplace_back([&fn, lo, hi] { fn(lo, hi); });
+class Pool {
+ public:
+  void resize(int n) {
+    stop();
+    n_ = n;
+    // resize() and run() are called from one host thread, so no job is
+    // published while workers start; each worker begins at the current
+    // generation and takes every job published afterwards.
+    uint64_t g = gen_;
+    for (int i = 1; i < n; ++i) workers_.emplace_back([this, i, g] { loop(i, g); });
   }
-  for (auto& th : ths) th.join();
-}
+  void run(size_t n, const std::function<void(size_t, size_t)>& fn) {
+    int t = n_ < 1 ? 1 : n_;
+    if (t <= 1 || n < 2) { fn(0, n); return; }
+    {
+      std::unique_lock<std::mutex> lk(mu_);
+      fn_ = &fn;
+      n_items_ = n;
+      pending_ = t - 1;
+      ++gen_;
+    }
+    cv_.notify_all();
+    chunk(0, t, n, fn);
+    std::unique_lock<std::mutex> lk(mu_);
+    done_.wait(lk, [this] { return pending_ == 0; });
+  }
+  ~Pool() { stop(); }
+
+ private:
+  static void chunk(int i, int t, size_t n, const std::function<void(size_t, size_t)>& fn) {
+    size_t c = (n + t - 1) / t, lo = i * c, hi = std::min(n, lo + c);
+    if (lo < hi) fn(lo, hi);
+  }
+  void loop(int i, uint64_t seen) {
+    for (;;) {
+      const std::function<void(size_t, size_t)>* fn;
+      size_t n;
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return quit_ || gen_ != seen; });
+        if (quit_) return;
+        seen = gen_;
+        fn = fn_;
+        n = n_items_;
+      }
+      chunk(i, n_, n, *fn);
+      std::unique_lock<std::mutex> lk(mu_);
+      if (--pending_ == 0) done_.notify_one();
+    }
+  }
+  void stop() {
+    {
+      std::unique_lock<std::mutex> lk(mu_);
+      quit_ = true;
+    }
+    cv_.notify_all();
+    for (auto& w : workers_) w.join();
+    workers_.clear();
+    quit_ = false;
+  }
+  std::vector<std::thread> workers_;
+  std::mutex mu_;
+  std::condition_variable cv_, done_;
+  const std::function<void(size_t, size_t)>* fn_ = nullptr;
+  size_t n_items_ = 0;
+  int pending_ = 0, n_ = 1;
+  uint64_t gen_ = 0;
+  bool quit_ = false;
+};
+static Pool g_pool;
+
+static void parallel_for(size_t n, const std::function<void(size_t, size_t)>& fn) { g_pool.run(n, fn); }
 
 struct Fail : std::runtime_error {
   explicit Fail(const std::string& m) : std::runtime_error(m) {}
@@ -698,7 +760,10 @@ extern "C" {
 struct dor_model { std::unique_ptr<Model> m; };
 struct dor_seq { Seq s; };
 
-void dor_set_threads(int n) { g_threads = n < 1 ? 1 : n; }
+void dor_set_threads(int n) {
+  int t = n < 1 ? 1 : n;
+  if (t != g_threads) { g_threads = t; g_pool.resize(t); }
+}
 int dor_get_threads(void) { return g_threads; }
 
 dor_model* dor_model_open(const char* path, const dor_config* cfg, char* err, size_t errlen) {
@@ -732,6 +797,95 @@ long dor_detwgt_validate(const uint8_t* bytes, size_t n, char* err, size_t errle
     return -1;
   }
 }
+// Seeded synthetic model: the counter-based generator of
+// raster-inference_b200/detwgt.py (the same tensor names, shapes and values as
+// detwgt.write_synthetic_model), filled on all oracle threads.
+static uint64_t fnv1a64(const std::string& s) {
+  uint64_t h = 0xCBF29CE484222325ull;
+  for (unsigned char c : s) { h ^= c; h *= 0x100000001B3ull; }
+  return h;
+}
+static uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+static Tensor synth_tensor(const std::string& name, std::vector<size_t> shape, uint64_t seed, int width) {
+  Tensor t;
+  t.shape = shape;
+  size_t n = 1;
+  for (size_t d : shape) n *= d;
+  t.width = shape.size() == 1 ? 32 : width;
+  if (t.width == 16) t.w16.resize(n); else t.w32.resize(n);
+  uint64_t key = fnv1a64(name) ^ seed;
+  int64_t bound = (int64_t)(0x7fffffffLL / (int64_t)shape.back());
+  bool rank1 = shape.size() == 1;
+  parallel_for((n + 4095) / 4096, [&](size_t lo, size_t hi) {
+    for (size_t b = lo; b < hi; ++b)
+      for (size_t i = b * 4096; i < std::min(n, (b + 1) * 4096); ++i) {
+        uint64_t z = mix64(key + (uint64_t)(i + 1) * 0x9E3779B97F4A7C15ull);
+        int32_t v;
+        if (rank1) v = 32768 + (int32_t)(z >> 48);
+        else if (width == 16) v = (int32_t)(z >> 48) - 32768;
+        else v = (int32_t)((int64_t)(z % (uint64_t)(2 * bound + 1)) - bound);
+        if (t.width == 16) t.w16[i] = (int16_t)v; else t.w32[i] = v;
+      }
+  });
+  return t;
+}
+
+dor_model* dor_model_open_synthetic(const dor_config* c, uint64_t seed, int width, int intermediate_size,
+                                    int with_scalar, char* err, size_t errlen) {
+  try {
+    std::map<std::string, Tensor> t;
+    size_t H = c->hidden_size, V = c->vocab_size, L = c->num_hidden_layers, Hq = c->num_attention_heads;
+    size_t F = intermediate_size, P = c->hidden_size_per_layer_input > 0 ? c->hidden_size_per_layer_input : 0;
+    size_t dg = c->global_head_dim > 0 ? c->global_head_dim : c->head_dim;
+    bool keqv = c->attention_k_eq_v == 1;
+    size_t gkv = c->num_global_key_value_heads > 0 ? c->num_global_key_value_heads : c->num_key_value_heads;
+    size_t pv = c->vocab_size_per_layer_input >= 0 ? c->vocab_size_per_layer_input : V;
+    auto add = [&](const std::string& n, std::vector<size_t> sh) { t.emplace(n, synth_tensor(n, sh, seed, width)); };
+    add("model.language_model.embed_tokens.weight", {V, H});
+    for (size_t l = 0; l < L; ++l) {
+      bool sl = c->layer_is_sliding[l] != 0;
+      size_t hd = sl ? (size_t)c->head_dim : dg;
+      size_t nkv = sl ? (size_t)c->num_key_value_heads : (keqv ? gkv : (size_t)c->num_key_value_heads);
+      std::string p = "model.language_model.layers." + std::to_string(l);
+      add(p + ".self_attn.q_proj.weight", {Hq * hd, H});
+      add(p + ".self_attn.k_proj.weight", {nkv * hd, H});
+      if (sl || !keqv) add(p + ".self_attn.v_proj.weight", {nkv * hd, H});
+      add(p + ".self_attn.o_proj.weight", {H, Hq * hd});
+      add(p + ".self_attn.q_norm.weight", {hd});
+      add(p + ".self_attn.k_norm.weight", {hd});
+      for (const char* nn : {"input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
+                             "post_feedforward_layernorm"})
+        add(p + "." + nn + ".weight", {H});
+      add(p + ".mlp.gate_proj.weight", {F, H});
+      add(p + ".mlp.up_proj.weight", {F, H});
+      add(p + ".mlp.down_proj.weight", {H, F});
+      if (P > 0) {
+        add(p + ".per_layer_input_gate.weight", {P, H});
+        add(p + ".per_layer_projection.weight", {H, P});
+        add(p + ".post_per_layer_input_norm.weight", {H});
+      }
+      if (with_scalar) add(p + ".layer_scalar", {1});
+    }
+    if (P > 0) {
+      add("model.language_model.embed_tokens_per_layer.weight", {pv, L * P});
+      add("model.language_model.per_layer_model_projection.weight", {L * P, H});
+      add("model.language_model.per_layer_projection_norm.weight", {P});
+    }
+    add("model.language_model.norm.weight", {H});
+    if (c->tie_word_embeddings == 0) add("model.language_model.lm_head.weight", {V, H});
+    auto* h = new dor_model;
+    h->m = build_model(std::move(t), *c);
+    return h;
+  } catch (const std::exception& e) {
+    set_err(err, errlen, e.what());
+    return nullptr;
+  }
+}
+
 void dor_model_close(dor_model* h) { delete h; }
 // info: H, V, L, Hq, P, then per layer: head_dim, kv_heads, rotary, sliding, window, cache_trim, donor, k_eq_v
 int dor_model_info(const dor_model* h, int64_t* out, size_t cap) {

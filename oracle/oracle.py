@@ -68,6 +68,7 @@ def lib():
             "dor_model_open": (p, [C.c_char_p, C.POINTER(Config), C.c_char_p, sz]),
             "dor_detwgt_validate": (C.c_long, [p, sz, C.c_char_p, sz]),
             "dor_model_close": (None, [p]),
+            "dor_model_open_synthetic": (p, [C.POINTER(Config), C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_char_p, sz]),
             "dor_model_info": (C.c_int, [p, p, sz]),
             "dor_seq_new": (p, [p]),
             "dor_seq_free": (None, [p]),
@@ -179,15 +180,26 @@ class OracleError(RuntimeError):
 class Model:
     """A det model loaded by the oracle from ``model_dir`` (config.json + model.detwgt)."""
 
-    def __init__(self, model_dir: str, threads: int | None = None):
-        with open(os.path.join(model_dir, "config.json")) as f:
-            self.config = json.load(f)
-        self._cfg = config_from_dict(self.config)
+    def __init__(self, model_dir: str | None, threads: int | None = None, synthetic: tuple | None = None):
+        """Load ``model_dir`` (config.json + model.detwgt), or with
+        ``synthetic=(config_dict, seed, width)`` generate the seeded synthetic
+        model of raster-inference_b200/detwgt.py in host memory."""
         L = lib()
         if threads is not None:
             L.dor_set_threads(threads)
         err = C.create_string_buffer(1024)
-        h = L.dor_model_open(os.path.join(model_dir, "model.detwgt").encode(), C.byref(self._cfg), err, 1024)
+        if synthetic is not None:
+            cfg, seed, width = synthetic
+            self.config = cfg
+            self._cfg = config_from_dict(cfg)
+            t = cfg.get("text_config", cfg)
+            h = L.dor_model_open_synthetic(C.byref(self._cfg), seed, width, t["intermediate_size"],
+                                           int(t.get("_synthetic_layer_scalar", True)), err, 1024)
+        else:
+            with open(os.path.join(model_dir, "config.json")) as f:
+                self.config = json.load(f)
+            self._cfg = config_from_dict(self.config)
+            h = L.dor_model_open(os.path.join(model_dir, "model.detwgt").encode(), C.byref(self._cfg), err, 1024)
         if not h:
             raise OracleError(err.value.decode())
         self._h = h

@@ -36,7 +36,7 @@ SYMBOLS = [
     "rdet_seq_position", "rdet_embed", "rdet_prefill", "rdet_prefill_begin", "rdet_prefill_range",
     "rdet_prefill_finalize", "rdet_select", "rdet_decode", "rdet_decode_begin", "rdet_decode_range",
     "rdet_decode_finalize", "rdet_generate", "rdet_read", "rdet_commitment", "rdet_det_gemv", "rdet_det_linear",
-    "rdet_last_error", "rdet_version",
+    "rdet_get_stream", "rdet_seq_kernels_per_step", "rdet_last_error", "rdet_version",
 ]
 
 
@@ -92,6 +92,8 @@ def lib() -> C.CDLL:
         "rdet_commitment": [p, p, i32, i32, C.c_char_p],
         "rdet_det_gemv": [p, p, i32, u32, u32, p, p],
         "rdet_det_linear": [p, u32, p, i32, u32, u32, p, p],
+        "rdet_get_stream": [p, p],
+        "rdet_seq_kernels_per_step": [p, p],
         "rdet_last_error": [C.c_char_p, sz],
     }
     for name, args in sig.items():
@@ -155,6 +157,13 @@ class Model:
             self.close()
         except Exception:
             pass
+
+    @property
+    def stream(self) -> int:
+        """cudaStream_t (as an int) on which this model launches its work."""
+        v = C.c_void_p()
+        _check(lib().rdet_get_stream(self._h, C.byref(v)))
+        return v.value or 0
 
     def new_sequence(self, max_ctx: int) -> "Sequence":
         h = C.c_void_p()
@@ -231,6 +240,11 @@ class Sequence:
         out = np.zeros(max(n, 1), dtype=np.uint32)
         _check(lib().rdet_generate(self.model._h, self._h, n, _ptr(out)))
         return [int(v) for v in out[:n]]
+
+    def kernels_per_step(self) -> int:
+        v = C.c_uint32()
+        _check(lib().rdet_seq_kernels_per_step(self._h, C.byref(v)))
+        return v.value
 
     # -- canonical bytes / commitments -------------------------------------------
     def read(self, which: int, layer: int = 0, arg: int = 0) -> np.ndarray:

@@ -684,8 +684,189 @@ __global__ void attn_prefill_kernel(const AttnPrefillArgs a, int rowlen) {
     a.out[((size_t)i * a.Hq + h) * d + t] = requantize(acc);
   }
 }
+// Tiled prefill attention: one CTA per (KV head, block of QB queries) covering
+// all G query heads of the group (R = QB*G <= 64 query rows), with K and V
+// streamed through shared memory in tiles of 32 keys.  Phase A writes exact
+// scores to scratch and tracks the first max per row; phase B turns each row
+// into exact softmax weights (exp, saturating-free sum, ties-to-even division,
+// residual to the first max); phase C accumulates the weighted V sum in i64.
+constexpr int AP_R = 64, AP_TK = 32, AP_CH = 128;
+
+__global__ void __launch_bounds__(256) attn_prefill_tiled(const AttnPrefillArgs a, int rowlen, int QB) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int d = a.d, dp = d + 4, G = a.Hq / a.Hkv, R = QB * G;
+  int32_t* Qs = reinterpret_cast<int32_t*>(smem_raw);   // [AP_R][dp]
+  int32_t* Ks = Qs + AP_R * dp;                          // [AP_TK][dp] (V tiles use [AP_TK][AP_CH+4])
+  int32_t* Ws = Ks + AP_TK * dp;                         // [AP_R][AP_TK]
+  __shared__ int32_t rmax[AP_R], ridx[AP_R];
+  const int kvh = blockIdx.x, i0 = blockIdx.y * QB;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto row_query = [&](int r) { return i0 + (r % QB); };
+  auto row_head = [&](int r) { return kvh * G + r / QB; };
+  auto win_start = [&](int i) { return (a.window > 0 && i + 1 > a.window) ? i + 1 - a.window : 0; };
+  const int klo = win_start(i0);
+  const int khi = min(a.S, i0 + QB);
+  // Q rows -> smem
+  for (int e = threadIdx.x; e < AP_R * (d / 4); e += blockDim.x) {
+    int r = e / (d / 4), c = e % (d / 4);
+    int4 v = make_int4(0, 0, 0, 0);
+    if (r < R && row_query(r) < a.S)
+      v = reinterpret_cast<const int4*>(a.q + ((size_t)row_query(r) * a.Hq + row_head(r)) * d)[c];
+    reinterpret_cast<int4*>(Qs + r * dp)[c] = v;
+  }
+  // ---- phase A: scores + first max
+  int32_t bm[8], bi[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) { bm[t] = INT32_MIN; bi[t] = INT32_MAX; }
+  const int rbase = warp * 8;
+  for (int kt = klo; kt < khi; kt += AP_TK) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < AP_TK * (d / 4); e += blockDim.x) {
+      int jj = e / (d / 4), c = e % (d / 4), j = kt + jj;
+      int4 v = make_int4(0, 0, 0, 0);
+      if (j < khi) v = reinterpret_cast<const int4*>(a.k_cache + ((size_t)kvh * a.cap + j) * d)[c];
+      reinterpret_cast<int4*>(Ks + jj * dp)[c] = v;
+    }
+    __syncthreads();
+    int64_t acc[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) acc[t] = 0;
+    const int4* kr = reinterpret_cast<const int4*>(Ks + lane * dp);
+    for (int c = 0; c < d / 4; ++c) {
+      int4 kv = kr[c];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        int4 qv = reinterpret_cast<const int4*>(Qs + (rbase + t) * dp)[c];
+        acc[t] += (int64_t)kv.x * qv.x + (int64_t)kv.y * qv.y + (int64_t)kv.z * qv.z + (int64_t)kv.w * qv.w;
+      }
+    }
+    const int j = kt + lane;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      int r = rbase + t;
+      if (r >= R) continue;
+      int i = row_query(r);
+      if (i >= a.S) continue;
+      int st = win_start(i);
+      if (j < st || j > i) continue;
+      int32_t sc = requantize(acc[t]);
+      a.scores[((size_t)row_head(r) * a.S + i) * rowlen + (j - st)] = sc;
+      if (sc > bm[t]) { bm[t] = sc; bi[t] = j; }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    int32_t v = bm[t], ix = bi[t];
+    for (int o = 16; o > 0; o >>= 1) {
+      int32_t v2 = __shfl_xor_sync(0xffffffffu, v, o), i2 = __shfl_xor_sync(0xffffffffu, ix, o);
+      if (v2 > v || (v2 == v && i2 < ix)) { v = v2; ix = i2; }
+    }
+    if (lane == 0) { rmax[rbase + t] = v; ridx[rbase + t] = ix; }
+  }
+  __syncthreads();
+  // ---- phase B: exact softmax weights per row (written over the scores)
+  for (int t = 0; t < 8; ++t) {
+    int r = rbase + t;
+    if (r >= R) break;
+    int i = row_query(r);
+    if (i >= a.S) continue;
+    int st = win_start(i), n = i + 1 - st;
+    int32_t* sc = a.scores + ((size_t)row_head(r) * a.S + i) * rowlen;
+    int32_t mx = rmax[r];
+    uint64_t sum = 0;
+    for (int j = lane; j < n; j += 32) sum += (uint64_t)exp_term(sc[j], mx);
+    sum = (uint64_t)warp_sum64((int64_t)sum);
+    int64_t wsum = 0;
+    for (int j = lane; j < n; j += 32) {
+      int32_t w = softmax_weight(exp_term(sc[j], mx), (int64_t)sum);
+      sc[j] = w;
+      wsum += w;
+    }
+    wsum = warp_sum64(wsum);
+    __syncwarp();
+    if (lane == 0) {
+      int32_t res = sub_sat(kOneAct, wsum > INT32_MAX ? INT32_MAX : (int32_t)wsum);
+      int m = ridx[r] - st;
+      sc[m] = add_sat(sc[m], res);
+    }
+  }
+  __syncthreads();
+  // ---- phase C: out = requantize(sum_j w_j v_j), 128 output dims at a time
+  const int rg = warp, dg = lane;
+  const int cw = d < AP_CH ? d : AP_CH, cwp = cw + 4;
+  for (int c0 = 0; c0 < d; c0 += AP_CH) {
+    int64_t acc[8][4];
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[t][u] = 0;
+    for (int kt = klo; kt < khi; kt += AP_TK) {
+      __syncthreads();
+      for (int e = threadIdx.x; e < AP_TK * (cw / 4); e += blockDim.x) {
+        int jj = e / (cw / 4), c = e % (cw / 4), j = kt + jj;
+        int4 v = make_int4(0, 0, 0, 0);
+        if (j < khi) v = reinterpret_cast<const int4*>(a.v_cache + ((size_t)kvh * a.cap + j) * d + c0)[c];
+        reinterpret_cast<int4*>(Ks + jj * cwp)[c] = v;
+      }
+      for (int e = threadIdx.x; e < AP_R * AP_TK; e += blockDim.x) {
+        int r = e / AP_TK, jj = e % AP_TK, j = kt + jj;
+        int32_t w = 0;
+        if (r < R) {
+          int i = row_query(r);
+          if (i < a.S) {
+            int st = win_start(i);
+            if (j >= st && j <= i) w = a.scores[((size_t)row_head(r) * a.S + i) * rowlen + (j - st)];
+          }
+        }
+        Ws[r * AP_TK + jj] = w;
+      }
+      __syncthreads();
+      if (dg * 4 < cw) {
+        for (int jj = 0; jj < AP_TK; ++jj) {
+          int4 v = reinterpret_cast<const int4*>(Ks + jj * cwp)[dg];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            int64_t w = Ws[(rg * 8 + t) * AP_TK + jj];
+            acc[t][0] += w * v.x;
+            acc[t][1] += w * v.y;
+            acc[t][2] += w * v.z;
+            acc[t][3] += w * v.w;
+          }
+        }
+      }
+    }
+    if (dg * 4 < cw) {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        int r = rg * 8 + t;
+        if (r >= R) continue;
+        int i = row_query(r);
+        if (i >= a.S) continue;
+        int32_t* o = a.out + ((size_t)i * a.Hq + row_head(r)) * d + c0 + dg * 4;
+        o[0] = requantize(acc[t][0]);
+        o[1] = requantize(acc[t][1]);
+        o[2] = requantize(acc[t][2]);
+        o[3] = requantize(acc[t][3]);
+      }
+    }
+  }
+}
+
 void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t s) {
   int rowlen = a.window > 0 ? (a.window < a.S ? a.window : a.S) : a.S;
+  const int G = a.Hq / a.Hkv;
+  size_t smem = ((size_t)AP_R * (a.d + 4) + (size_t)AP_TK * (a.d + 4) + (size_t)AP_R * AP_TK) * 4;
+  if (a.d % 4 == 0 && a.d <= 512 && G <= AP_R && (a.d <= AP_CH || a.d % AP_CH == 0) && smem <= 220 * 1024) {
+    int QB = AP_R / G;
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+      cudaFuncSetAttribute(attn_prefill_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+      configured = 220 * 1024;
+    }
+    dim3 grid(a.Hkv, (a.S + QB - 1) / QB);
+    attn_prefill_tiled<<<grid, 256, smem, s>>>(a, rowlen, QB);
+    return;
+  }
   dim3 grid(a.Hq, a.S);
   attn_prefill_kernel<<<grid, 256, (size_t)a.d * 4, s>>>(a, rowlen);
 }

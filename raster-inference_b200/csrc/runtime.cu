@@ -465,7 +465,8 @@ struct Seq {
   int32_t* prefill_cur = nullptr;
   int decode_next = -1;
   int32_t* decode_cur = nullptr;
-  cudaGraphExec_t graph = nullptr;
+  cudaGraphExec_t graph = nullptr;  // one decode_transition for the token in d_token
+  int graph_kernels = 0;
   std::vector<void*> allocs;
   void* dalloc(size_t bytes) {
     void* p = nullptr;
@@ -550,7 +551,8 @@ struct Loader {
     if (dry) {
       *out = 0;
     } else if (synthetic) {
-      void* p = upload_raw(n, *t);
+      void* p = upload_raw(n, *t);  // generated on the device, read back once
+      c.weight_bytes -= t->bytes;   // held on the host like an artifact scalar
       CK(cudaMemcpy(out, p, 4, cudaMemcpyDeviceToHost));
     } else if (t->width == 16) {
       int16_t v;
@@ -1062,6 +1064,35 @@ static bool kv_commitment(Ctx& c, Seq& q, std::string* out) {
   return true;
 }
 
+// Captures (once per sequence) the whole decode_transition of the token in
+// d_token as one CUDA graph.
+static void ensure_decode_graph(Ctx& c, Seq& q) {
+  if (q.graph) return;
+  cudaGraph_t g;
+  CK(cudaStreamBeginCapture(c.stream, cudaStreamCaptureModeThreadLocal));
+  decode_step_launch(c, q);
+  cudaError_t e = cudaStreamEndCapture(c.stream, &g);
+  if (e != cudaSuccess) throw Fail{RDET_E_CUDA, std::string("graph capture failed: ") + cudaGetErrorString(e)};
+  size_t n = 0;
+  cudaGraphGetNodes(g, nullptr, &n);
+  std::vector<cudaGraphNode_t> nodes(n);
+  cudaGraphGetNodes(g, nodes.data(), &n);
+  int kernels = 0;
+  for (auto nd : nodes) {
+    cudaGraphNodeType ty;
+    if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++kernels;
+  }
+  q.graph_kernels = kernels;
+  e = cudaGraphInstantiate(&q.graph, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) { q.graph = nullptr; throw Fail{RDET_E_CUDA, std::string("graph instantiate failed: ") + cudaGetErrorString(e)}; }
+}
+
+static void check_token(Ctx& c, uint32_t token) {
+  REQUIRE(token < (uint32_t)c.emb.rows, RDET_E_RANGE, "token id " + std::to_string(token) + " is out of bounds for embedding tensor");
+  if (c.cfg.P > 0) REQUIRE(token < (uint32_t)c.cfg.ple_vocab, RDET_E_RANGE, "token id is out of bounds for the PLE table");
+}
+
 }  // namespace rdet
 
 // ===========================================================================
@@ -1320,8 +1351,7 @@ int32_t rdet_decode_begin(rdet_ctx* ctx, rdet_seq* seq, uint32_t token) {
     CK(cudaSetDevice(c.device));
     check_decode_ready(c, q);
     REQUIRE(c.decode_owner == nullptr || c.decode_owner == &q, RDET_E_STATE, "another decode is in flight on this context");
-    REQUIRE(token < (uint32_t)c.emb.rows, RDET_E_RANGE, "token id " + std::to_string(token) + " is out of bounds for embedding tensor");
-    if (c.cfg.P > 0) REQUIRE(token < (uint32_t)c.cfg.ple_vocab, RDET_E_RANGE, "token id is out of bounds for the PLE table");
+    check_token(c, token);
     CK(cudaMemcpyAsync(q.d_token, &token, 4, cudaMemcpyHostToDevice, c.stream));
     decode_embed(c, q, q.d_token);
     CK(cudaGetLastError());
@@ -1369,20 +1399,27 @@ int32_t rdet_decode_finalize(rdet_ctx* ctx, rdet_seq* seq) {
 }
 
 int32_t rdet_decode(rdet_ctx* ctx, rdet_seq* const* seqs, const uint32_t* tokens, size_t nseq) {
-  if (!ctx || (nseq && (!seqs || !tokens))) {
-    g_last_error = "null argument";
-    return RDET_E_INVALID;
-  }
-  for (size_t i = 0; i < nseq; ++i) {
-    int32_t rc = rdet_decode_begin(ctx, seqs[i], tokens[i]);
-    if (rc == RDET_OK) rc = rdet_decode_range(ctx, seqs[i], 0, ctx->c->cfg.L);
-    if (rc == RDET_OK) rc = rdet_decode_finalize(ctx, seqs[i]);
-    if (rc != RDET_OK) {
-      ctx->c->decode_owner = nullptr;
-      return rc;
+  return guard([&] {
+    REQUIRE(ctx && (nseq == 0 || (seqs && tokens)), RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    CK(cudaSetDevice(c.device));
+    REQUIRE(c.decode_owner == nullptr, RDET_E_STATE, "a routine-granular decode is in flight on this context");
+    for (size_t i = 0; i < nseq; ++i) {
+      REQUIRE(seqs[i] && seqs[i]->owner == ctx, RDET_E_INVALID, "sequence belongs to another context");
+      check_decode_ready(c, *seqs[i]->s);
+      check_token(c, tokens[i]);
     }
-  }
-  return RDET_OK;
+    for (size_t i = 0; i < nseq; ++i) {
+      Seq& q = *seqs[i]->s;
+      ensure_decode_graph(c, q);
+      CK(cudaMemcpyAsync(q.d_token, tokens + i, 4, cudaMemcpyHostToDevice, c.stream));
+      CK(cudaGraphLaunch(q.graph, c.stream));
+      q.pos += 1;
+      q.last_was_prefill = false;
+    }
+    CK(cudaStreamSynchronize(c.stream));
+    check_err_flag(c, "decode");
+  });
 }
 
 int32_t rdet_generate(rdet_ctx* ctx, rdet_seq* seq, uint32_t n_tokens, uint32_t* tokens_out) {
@@ -1394,30 +1431,37 @@ int32_t rdet_generate(rdet_ctx* ctx, rdet_seq* seq, uint32_t n_tokens, uint32_t*
     check_decode_ready(c, q);
     REQUIRE(c.decode_owner == nullptr, RDET_E_STATE, "a routine-granular decode is in flight on this context");
     REQUIRE(q.pos + (int)n_tokens <= q.cap, RDET_E_RANGE, "generation would overflow the sequence KV cache");
-    if (!q.graph) {
-      cudaGraph_t g;
-      CK(cudaStreamBeginCapture(c.stream, cudaStreamCaptureModeThreadLocal));
-      select_launch(c, q);
-      decode_step_launch(c, q);
-      cudaError_t e = cudaStreamEndCapture(c.stream, &g);
-      if (e != cudaSuccess) throw Fail{RDET_E_CUDA, std::string("graph capture failed: ") + cudaGetErrorString(e)};
-      e = cudaGraphInstantiate(&q.graph, g, 0);
-      cudaGraphDestroy(g);
-      if (e != cudaSuccess) { q.graph = nullptr; throw Fail{RDET_E_CUDA, std::string("graph instantiate failed: ") + cudaGetErrorString(e)}; }
-    }
+    ensure_decode_graph(c, q);
     if (q.hist_cap < (int)n_tokens) {
       q.d_hist = static_cast<uint32_t*>(q.dalloc((size_t)std::max<uint32_t>(n_tokens, 1) * 4));
       q.hist_cap = (int)n_tokens;
     }
     for (uint32_t i = 0; i < n_tokens; ++i) {
-      CK(cudaGraphLaunch(q.graph, c.stream));
+      select_launch(c, q);
       CK(cudaMemcpyAsync(q.d_hist + i, q.d_token, 4, cudaMemcpyDeviceToDevice, c.stream));
+      CK(cudaGraphLaunch(q.graph, c.stream));
     }
     if (n_tokens) CK(cudaMemcpyAsync(tokens_out, q.d_hist, (size_t)n_tokens * 4, cudaMemcpyDeviceToHost, c.stream));
     CK(cudaStreamSynchronize(c.stream));
     check_err_flag(c, "generate");
     q.pos += (int)n_tokens;
     q.last_was_prefill = false;
+  });
+}
+
+int32_t rdet_get_stream(rdet_ctx* ctx, void** stream) {
+  return guard([&] {
+    REQUIRE(ctx && stream, RDET_E_INVALID, "null argument");
+    *stream = ctx->c->stream;
+  });
+}
+
+int32_t rdet_seq_kernels_per_step(rdet_seq* seq, uint32_t* kernels) {
+  return guard([&] {
+    REQUIRE(seq && kernels, RDET_E_INVALID, "null argument");
+    Seq& q = *seq->s;
+    REQUIRE(q.graph, RDET_E_STATE, "no decode graph captured yet");
+    *kernels = (uint32_t)q.graph_kernels;
   });
 }
 

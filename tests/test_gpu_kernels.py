@@ -64,7 +64,8 @@ def test_linear_bit_exact(width, S, rows, cols):
     w = rand_w(rng, rows, cols, width, True)
     X = np.stack([rand_x(rng, cols, adversarial=(i % 2 == 0)) for i in range(S)])
     Y = torch.zeros((S, rows), dtype=torch.int32, device="cuda")
-    rdet.det_linear(dev(X).data_ptr(), S, dev(w).data_ptr(), width, rows, cols, Y.data_ptr())
+    Xd, wd = dev(X), dev(w)  # keep the device buffers alive across the launch
+    rdet.det_linear(Xd.data_ptr(), S, wd.data_ptr(), width, rows, cols, Y.data_ptr())
     torch.cuda.synchronize()
     assert np.array_equal(Y.cpu().numpy(), O.linear(X, w))
 

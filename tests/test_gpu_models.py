@@ -146,3 +146,14 @@ def test_errors_are_reported():
     s.prefill([1, 2, 3, 4, 5, 6, 7, 8])
     with pytest.raises(rdet.RdetError):
         s.decode(1)  # KV cache full
+
+
+def test_e4b_head_dims_long_prompt():
+    # E4B head geometry (d=256 sliding, d_g=512 full, 8 query / 2 KV heads,
+    # window 512) on a narrow model, with a prompt longer than the window
+    cfg = mini_config(hidden_size=256, intermediate_size=512, num_attention_heads=8, num_key_value_heads=2,
+                      head_dim=256, global_head_dim=512, sliding_window=512, hidden_size_per_layer_input=32,
+                      num_hidden_layers=4, num_kv_shared_layers=1, vocab_size=300,
+                      layer_types=["sliding_attention", "full_attention", "sliding_attention", "sliding_attention"])
+    d = write_model(cfg, seed=8)
+    run_both(d, lcg_ids(600, 300, 2), 4)

@@ -81,3 +81,17 @@ def test_tiny_gemma_dev_config1_runs():
     for _ in range(8):
         s.decode(O.argmax_first(logits))
     assert s.position == 24
+
+
+def test_synthetic_generator_matches_artifact():
+    # the oracle's in-memory synthetic model equals the detwgt artifact that
+    # raster-inference_b200/detwgt.py writes for the same (config, seed, width)
+    from helpers import mini_config, write_model
+    for width, cfg in ((16, mini_config()), (32, mini_config(num_kv_shared_layers=0, tie_word_embeddings=False))):
+        d = write_model(cfg, seed=99, width=width)
+        a = O.Model(d)
+        b = O.Model(None, synthetic=(cfg, 99, width))
+        ids = [3, 1, 4, 1, 5, 9, 2, 6]
+        _, la, ha = a.seq().prefill(ids)
+        _, lb, hb = b.seq().prefill(ids)
+        assert (la == lb).all() and ha == hb
