@@ -136,6 +136,19 @@ int32_t rdet_det_gemv(const int32_t* x, const void* w, int32_t width, uint32_t r
 int32_t rdet_det_linear(const int32_t* x, uint32_t n_rows_x, const void* w, int32_t width, uint32_t rows,
                         uint32_t cols, int32_t* y, void* stream);
 
+/* det decode attention of one token for every query head
+ * (attention_output_into, det_kernels.rs:340-367, as driven by
+ * det_layer_decode :1000-1053): q [num_heads, head_dim] holds the normed,
+ * rotated queries; k_cache / v_cache [num_kv_heads, cap, head_dim] hold the
+ * cache rows by position; rows [max(0, position + 1 - window), position] are
+ * attended (window 0 = full attention); out [num_heads, head_dim].  Query head
+ * h reads KV head h / (num_heads / num_kv_heads).  Scratch memory is allocated
+ * by the library on first use per device and reused.  stream: cudaStream_t or
+ * NULL. */
+int32_t rdet_det_attention_decode(const int32_t* q, const int32_t* k_cache, const int32_t* v_cache, uint32_t cap,
+                                  uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim, uint32_t position,
+                                  uint32_t window, int32_t* out, void* stream);
+
 /* The CUDA stream (cudaStream_t) on which the context launches all of its
  * work, for callers that order their own work or CUDA events against it. */
 int32_t rdet_get_stream(rdet_ctx* ctx, void** stream);

@@ -1012,6 +1012,17 @@ long dor_kv_read(const dor_seq* sq, int layer, int head, int kind, int32_t* out,
   return (long)b.len;
 }
 
+// attention_output_into (det_kernels.rs:340-367) for one query over `rows`
+// key/value rows of width d.
+void dor_attention_one(const int32_t* q, const int32_t* keys, const int32_t* values, size_t rows, size_t d,
+                       int32_t* out) {
+  HeadBuf kb, vb;
+  for (size_t j = 0; j < rows; ++j) { kb.push(keys + j * d, d); vb.push(values + j * d, d); }
+  std::vector<int32_t> lg, w;
+  std::vector<int64_t> ex;
+  attend(q, kb, vb, 0, rows, d, out, lg, ex, w);
+}
+
 uint32_t dor_argmax_first(const int32_t* x, size_t n) { return (uint32_t)argmax_first(x, n); }
 void dor_act_commitment(const int32_t* x, size_t rows, size_t cols, char* out) { put_hash(out, act_commitment(x, rows, cols)); }
 void dor_vec_commitment(const int32_t* x, size_t n, char* out) { put_hash(out, vec_commitment(x, n)); }

@@ -80,6 +80,7 @@ def lib():
             "dor_kv_commitment": (C.c_int, [p, C.c_char_p]),
             "dor_kv_read": (C.c_long, [p, C.c_int, C.c_int, C.c_int, p, sz]),
             "dor_argmax_first": (u32, [p, sz]),
+            "dor_attention_one": (None, [p, p, p, sz, sz, p]),
             "dor_act_commitment": (None, [p, sz, sz, C.c_char_p]),
             "dor_vec_commitment": (None, [p, sz, C.c_char_p]),
             "dor_sha256_hex": (None, [p, sz, C.c_char_p]),
@@ -352,3 +353,13 @@ def validate_detwgt(b: bytes):
     if n < 0:
         raise OracleError(err.value.decode())
     return int(n)
+
+
+def attention_one(q, keys, values) -> np.ndarray:
+    """attention_output_into for one query row over explicit key/value rows."""
+    q = np.ascontiguousarray(q, dtype=np.int32)
+    keys = np.ascontiguousarray(keys, dtype=np.int32)
+    values = np.ascontiguousarray(values, dtype=np.int32)
+    out = np.zeros(q.size, dtype=np.int32)
+    lib().dor_attention_one(_ptr(q), _ptr(keys), _ptr(values), keys.shape[0], q.size, _ptr(out))
+    return out

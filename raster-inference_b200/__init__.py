@@ -36,7 +36,8 @@ SYMBOLS = [
     "rdet_seq_position", "rdet_embed", "rdet_prefill", "rdet_prefill_begin", "rdet_prefill_range",
     "rdet_prefill_finalize", "rdet_select", "rdet_decode", "rdet_decode_begin", "rdet_decode_range",
     "rdet_decode_finalize", "rdet_generate", "rdet_read", "rdet_commitment", "rdet_det_gemv", "rdet_det_linear",
-    "rdet_get_stream", "rdet_seq_kernels_per_step", "rdet_last_error", "rdet_version",
+    "rdet_det_attention_decode", "rdet_get_stream", "rdet_seq_kernels_per_step", "rdet_last_error",
+    "rdet_version",
 ]
 
 
@@ -92,6 +93,7 @@ def lib() -> C.CDLL:
         "rdet_commitment": [p, p, i32, i32, C.c_char_p],
         "rdet_det_gemv": [p, p, i32, u32, u32, p, p],
         "rdet_det_linear": [p, u32, p, i32, u32, u32, p, p],
+        "rdet_det_attention_decode": [p, p, p, u32, u32, u32, u32, u32, u32, p, p],
         "rdet_get_stream": [p, p],
         "rdet_seq_kernels_per_step": [p, p],
         "rdet_last_error": [C.c_char_p, sz],
@@ -307,3 +309,11 @@ def det_gemv(x_ptr: int, w_ptr: int, width: int, rows: int, cols: int, y_ptr: in
 def det_linear(x_ptr: int, s: int, w_ptr: int, width: int, rows: int, cols: int, y_ptr: int, stream: int = 0):
     _check(lib().rdet_det_linear(C.c_void_p(x_ptr), s, C.c_void_p(w_ptr), width, rows, cols, C.c_void_p(y_ptr),
                                  C.c_void_p(stream) if stream else None))
+
+
+def det_attention_decode(q_ptr: int, k_ptr: int, v_ptr: int, cap: int, num_heads: int, num_kv_heads: int,
+                         head_dim: int, position: int, window: int, out_ptr: int, stream: int = 0):
+    """Decode attention of one token on caller-owned device memory (rdet_det_attention_decode)."""
+    _check(lib().rdet_det_attention_decode(C.c_void_p(q_ptr), C.c_void_p(k_ptr), C.c_void_p(v_ptr), cap, num_heads,
+                                           num_kv_heads, head_dim, position, window, C.c_void_p(out_ptr),
+                                           C.c_void_p(stream) if stream else None))

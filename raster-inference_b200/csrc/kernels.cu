@@ -417,7 +417,7 @@ void launch_qkv_post(const QkvPostArgs& a, cudaStream_t s) {
 // key window (attention_output_into, det_kernels.rs:340-367).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void decode_window(const AttnDecodeArgs& a, int* start, int* n) {
-  int len = *a.pos + 1;
+  int len = (a.pos ? *a.pos : a.pos_value) + 1;
   int st = (a.window > 0 && len > a.window) ? len - a.window : 0;
   *start = st;
   *n = len - st;
@@ -450,7 +450,7 @@ __global__ void attn_dec_scores(const AttnDecodeArgs a) {
     }
     for (int g = 0; g < G; ++g) {
       int32_t sc = requantize(warp_sum64(acc[g]));
-      if (lane == 0) a.sc.scores[(size_t)(kvh * G + g) * a.cap + j] = sc;
+      if (lane == 0) a.sc.scores[(size_t)(kvh * G + g) * a.sc.stride + j] = sc;
       if (sc > bm[g]) { bm[g] = sc; bi[g] = j; }  // j increases: first max kept
     }
   }
@@ -504,8 +504,8 @@ __global__ void attn_dec_exp(const AttnDecodeArgs a) {
     int h = kvh * G + g;
     uint64_t s = 0;
     for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) {
-      int64_t e = exp_term(a.sc.scores[(size_t)h * a.cap + j], gmax[g]);
-      a.sc.exps[(size_t)h * a.cap + j] = e;
+      int64_t e = exp_term(a.sc.scores[(size_t)h * a.sc.stride + j], gmax[g]);
+      a.sc.exps[(size_t)h * a.sc.stride + j] = e;
       s += (uint64_t)e;
     }
     s = (uint64_t)warp_sum64((int64_t)s);
@@ -543,7 +543,7 @@ __global__ void attn_dec_wsum(const AttnDecodeArgs a) {
     int64_t wsum = 0;
     for (int j = lo + threadIdx.x; j < lo + R; j += blockDim.x) {
       int32_t w = 0;
-      if (j < hi) w = softmax_weight(a.sc.exps[(size_t)h * a.cap + j], tsum[g]);
+      if (j < hi) w = softmax_weight(a.sc.exps[(size_t)h * a.sc.stride + j], tsum[g]);
       ws[g * R + (j - lo)] = w;
       wsum += w;
     }

@@ -99,9 +99,11 @@ struct AttnScratch {
   int64_t* pwsum = nullptr;   // [Hq, nsplit]
   int64_t* pacc = nullptr;    // [Hq, nsplit, d]
   int32_t max_splits = 0;
+  int32_t stride = 0;         // row stride of scores / exps (>= attended rows)
 };
 struct AttnDecodeArgs {
   const int32_t* pos = nullptr;  // device: position of the current token
+  int32_t pos_value = 0;         // used when pos == nullptr
   int32_t Hq = 0, Hkv = 0, d = 0;
   int32_t window = 0;            // 0 = full attention
   const int32_t* q = nullptr;    // [Hq, d]

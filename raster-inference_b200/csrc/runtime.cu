@@ -1005,6 +1005,7 @@ static void seq_alloc(Ctx& c, Seq& q, int cap) {
   const int rps = 64;
   int splits = (cap + rps - 1) / rps;
   q.asc.max_splits = splits;
+  q.asc.stride = cap;
   q.asc.scores = static_cast<int32_t*>(q.dalloc((size_t)m.Hq * cap * 4));
   q.asc.exps = static_cast<int64_t*>(q.dalloc((size_t)m.Hq * cap * 8));
   q.asc.pmax = static_cast<int32_t*>(q.dalloc((size_t)m.Hq * splits * 4));
@@ -1091,6 +1092,41 @@ static void ensure_decode_graph(Ctx& c, Seq& q) {
 static void check_token(Ctx& c, uint32_t token) {
   REQUIRE(token < (uint32_t)c.emb.rows, RDET_E_RANGE, "token id " + std::to_string(token) + " is out of bounds for embedding tensor");
   if (c.cfg.P > 0) REQUIRE(token < (uint32_t)c.cfg.ple_vocab, RDET_E_RANGE, "token id is out of bounds for the PLE table");
+}
+
+// Decode-attention scratch of the kernel-level entry point: allocated on first
+// use per device and grown on demand.
+struct AttnScratchOwned {
+  AttnScratch sc;
+  int heads = 0, rows = 0, splits = 0, dim = 0;
+  std::vector<void*> ptrs;
+};
+static std::map<int, AttnScratchOwned> g_attn_scratch;
+
+static void attn_entry_args(AttnDecodeArgs& a, const int32_t* q, const int32_t* k_cache, const int32_t* v_cache,
+                            uint32_t cap, uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
+                            uint32_t position, uint32_t window, int32_t* out) {
+  REQUIRE(q && k_cache && v_cache && out, RDET_E_INVALID, "null argument");
+  REQUIRE(num_kv_heads > 0 && num_heads % num_kv_heads == 0 && num_heads / num_kv_heads <= 8, RDET_E_INVALID,
+          "num_heads must be a multiple of num_kv_heads with at most 8 query heads per KV head");
+  REQUIRE(head_dim > 0 && head_dim <= 1024, RDET_E_RANGE, "head_dim out of range");
+  REQUIRE(position < cap, RDET_E_RANGE, "position must be below the cache capacity");
+  a.pos = nullptr;
+  a.pos_value = (int32_t)position;
+  a.Hq = (int)num_heads;
+  a.Hkv = (int)num_kv_heads;
+  a.d = (int)head_dim;
+  a.window = (int)window;
+  a.q = q;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.cap = (int)cap;
+  a.out = out;
+  a.rows_per_split = 64;
+}
+static int attn_rows(uint32_t position, uint32_t window) {
+  int len = (int)position + 1;
+  return (window > 0 && len > (int)window) ? (int)window : len;
 }
 
 }  // namespace rdet
@@ -1589,6 +1625,46 @@ int32_t rdet_det_gemv(const int32_t* x, const void* w, int32_t width, uint32_t r
     g.seg[0].y = y;
     g.a = x;
     launch_gemv(g, static_cast<cudaStream_t>(stream));
+    CK(cudaGetLastError());
+  });
+}
+
+int32_t rdet_det_attention_decode(const int32_t* q, const int32_t* k_cache, const int32_t* v_cache,
+                                             uint32_t cap, uint32_t num_heads, uint32_t num_kv_heads,
+                                             uint32_t head_dim, uint32_t position, uint32_t window, int32_t* out,
+                                             void* stream) {
+  return guard([&] {
+    AttnDecodeArgs a;
+    attn_entry_args(a, q, k_cache, v_cache, cap, num_heads, num_kv_heads, head_dim, position, window, out);
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    int rows = attn_rows(position, window);
+    AttnScratchOwned& o = g_attn_scratch[dev];
+    if (o.heads < (int)num_heads || o.rows < rows || o.dim < (int)head_dim) {
+      for (void* p : o.ptrs) cudaFree(p);
+      o = AttnScratchOwned();
+      o.heads = std::max<int>(num_heads, 8);
+      o.rows = std::max(rows, 1024);
+      o.dim = std::max<int>(head_dim, 256);
+      o.splits = (o.rows + a.rows_per_split - 1) / a.rows_per_split;
+      auto al = [&](size_t bytes) {
+        void* p = nullptr;
+        CK(cudaMalloc(&p, bytes));
+        o.ptrs.push_back(p);
+        return p;
+      };
+      o.sc.scores = static_cast<int32_t*>(al((size_t)o.heads * o.rows * 4));
+      o.sc.exps = static_cast<int64_t*>(al((size_t)o.heads * o.rows * 8));
+      o.sc.pmax = static_cast<int32_t*>(al((size_t)o.heads * o.splits * 4));
+      o.sc.pidx = static_cast<int32_t*>(al((size_t)o.heads * o.splits * 4));
+      o.sc.psum = static_cast<int64_t*>(al((size_t)o.heads * o.splits * 8));
+      o.sc.pwsum = static_cast<int64_t*>(al((size_t)o.heads * o.splits * 8));
+      o.sc.pacc = static_cast<int64_t*>(al((size_t)o.heads * o.splits * o.dim * 8));
+      o.sc.max_splits = o.splits;
+      o.sc.stride = o.rows;
+    }
+    a.sc = o.sc;
+    launch_attn_decode(a, static_cast<cudaStream_t>(stream));
     CK(cudaGetLastError());
   });
 }

@@ -73,3 +73,44 @@ def test_linear_bit_exact(width, S, rows, cols):
 def test_gemv_rejects_bad_width():
     with pytest.raises(rdet.RdetError):
         rdet.det_gemv(1, 1, 8, 4, 4, 1)
+
+
+def attention_case(rng, heads, kv_heads, d, cap, position, window, scale=1 << 17):
+    q = rng.integers(-scale, scale, (heads, d), dtype=np.int64).astype(np.int32)
+    k = rng.integers(-scale, scale, (kv_heads, cap, d), dtype=np.int64).astype(np.int32)
+    v = rng.integers(-scale * 8, scale * 8, (kv_heads, cap, d), dtype=np.int64).astype(np.int32)
+    start = max(0, position + 1 - window) if window else 0
+    g = heads // kv_heads
+    ref = np.stack([O.attention_one(q[h], k[h // g, start:position + 1], v[h // g, start:position + 1])
+                    for h in range(heads)])
+    return q, k, v, ref
+
+
+@pytest.mark.parametrize("heads,kv_heads,d,cap,position,window", [
+    (2, 1, 2, 16, 0, 0), (4, 2, 16, 100, 57, 8), (8, 2, 256, 600, 599, 512), (8, 2, 512, 4400, 4351, 0),
+    (8, 1, 64, 300, 130, 0), (3, 3, 48, 70, 69, 1)])
+def test_attention_decode_bit_exact(heads, kv_heads, d, cap, position, window):
+    rng = np.random.default_rng(position + d)
+    q, k, v, ref = attention_case(rng, heads, kv_heads, d, cap, position, window)
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    out = torch.zeros((heads, d), dtype=torch.int32, device="cuda")
+    rdet.det_attention_decode(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), cap, heads, kv_heads, d, position, window,
+                              out.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), ref)
+
+
+def test_attention_decode_ties_keep_first_max():
+    # equal scores everywhere: softmax residual goes to the first row of the window
+    heads, kv_heads, d, cap, position, window = 2, 1, 8, 300, 260, 200
+    q = np.zeros((heads, d), dtype=np.int32)
+    k = np.ones((kv_heads, cap, d), dtype=np.int32)
+    v = np.arange(kv_heads * cap * d, dtype=np.int32).reshape(kv_heads, cap, d)
+    start = position + 1 - window
+    ref = np.stack([O.attention_one(q[h], k[0, start:position + 1], v[0, start:position + 1]) for h in range(heads)])
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    out = torch.zeros((heads, d), dtype=torch.int32, device="cuda")
+    rdet.det_attention_decode(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), cap, heads, kv_heads, d, position, window,
+                              out.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), ref)
