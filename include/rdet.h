@@ -149,6 +149,25 @@ int32_t rdet_det_attention_decode(const int32_t* q, const int32_t* k_cache, cons
                                   uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim, uint32_t position,
                                   uint32_t window, int32_t* out, void* stream);
 
+/* Decode attention that allocates nothing.  Same arguments and the same
+ * bit-exact result as rdet_det_attention_decode, for callers that cannot
+ * allocate device memory while they run: a serving process that hands all of
+ * HBM to weights and KV caches at start-up has none left to give, and an
+ * executor that keeps its device footprint fixed across decode steps must not
+ * allocate inside the step.  Its scratch is a fixed 4.8 MiB array inside the
+ * library, which every GPU that loads the library holds until the process
+ * exits.  Limits: num_heads <= 16, head_dim <= 512, and at most 4096 attended
+ * rows (min(position + 1, window)); larger requests fail with RDET_E_RANGE.
+ * The first call on a device looks up the array's address on that device
+ * (with that device current) and should come before any stream capture.  All
+ * calls share the one array, which keeps the previous call's contents: calls
+ * that overlap on the GPU (other streams, other host threads) race.  This
+ * entry point has no counterpart in the reference. */
+int32_t rdet_det_attention_decode_noalloc(const int32_t* q, const int32_t* k_cache, const int32_t* v_cache,
+                                          uint32_t cap, uint32_t num_heads, uint32_t num_kv_heads,
+                                          uint32_t head_dim, uint32_t position, uint32_t window, int32_t* out,
+                                          void* stream);
+
 /* The CUDA stream (cudaStream_t) on which the context launches all of its
  * work, for callers that order their own work or CUDA events against it. */
 int32_t rdet_get_stream(rdet_ctx* ctx, void** stream);

@@ -36,7 +36,7 @@ SYMBOLS = [
     "rdet_seq_position", "rdet_embed", "rdet_prefill", "rdet_prefill_begin", "rdet_prefill_range",
     "rdet_prefill_finalize", "rdet_select", "rdet_decode", "rdet_decode_begin", "rdet_decode_range",
     "rdet_decode_finalize", "rdet_generate", "rdet_read", "rdet_commitment", "rdet_det_gemv", "rdet_det_linear",
-    "rdet_det_attention_decode", "rdet_get_stream", "rdet_seq_kernels_per_step", "rdet_last_error",
+    "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_get_stream", "rdet_seq_kernels_per_step", "rdet_last_error",
     "rdet_version",
 ]
 
@@ -94,6 +94,7 @@ def lib() -> C.CDLL:
         "rdet_det_gemv": [p, p, i32, u32, u32, p, p],
         "rdet_det_linear": [p, u32, p, i32, u32, u32, p, p],
         "rdet_det_attention_decode": [p, p, p, u32, u32, u32, u32, u32, u32, p, p],
+        "rdet_det_attention_decode_noalloc": [p, p, p, u32, u32, u32, u32, u32, u32, p, p],
         "rdet_get_stream": [p, p],
         "rdet_seq_kernels_per_step": [p, p],
         "rdet_last_error": [C.c_char_p, sz],
@@ -317,3 +318,15 @@ def det_attention_decode(q_ptr: int, k_ptr: int, v_ptr: int, cap: int, num_heads
     _check(lib().rdet_det_attention_decode(C.c_void_p(q_ptr), C.c_void_p(k_ptr), C.c_void_p(v_ptr), cap, num_heads,
                                            num_kv_heads, head_dim, position, window, C.c_void_p(out_ptr),
                                            C.c_void_p(stream) if stream else None))
+
+
+def det_attention_decode_noalloc(q_ptr: int, k_ptr: int, v_ptr: int, cap: int, num_heads: int, num_kv_heads: int,
+                                 head_dim: int, position: int, window: int, out_ptr: int, stream: int = 0):
+    """rdet_det_attention_decode without any device allocation, for callers
+    that cannot allocate device memory while they run (all of HBM handed to
+    weights and KV caches up front, or a fixed per-step footprint).  Scratch
+    is the library's fixed 4.8 MiB array; limits: 16 heads, head_dim 512,
+    4096 attended rows.  Calls that overlap on the GPU race on that array."""
+    _check(lib().rdet_det_attention_decode_noalloc(C.c_void_p(q_ptr), C.c_void_p(k_ptr), C.c_void_p(v_ptr), cap,
+                                                   num_heads, num_kv_heads, head_dim, position, window,
+                                                   C.c_void_p(out_ptr), C.c_void_p(stream) if stream else None))

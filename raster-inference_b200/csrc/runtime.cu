@@ -12,6 +12,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -1129,6 +1130,46 @@ static int attn_rows(uint32_t position, uint32_t window) {
   return (window > 0 && len > (int)window) ? (int)window : len;
 }
 
+// ---------------------------------------------------------------------------
+// Decode attention without allocation: its scratch is a fixed array compiled
+// into this library (every GPU that loads the library holds it until the
+// process exits).  Host code never uses the array's name as an address: the
+// device address comes from cudaGetSymbolAddress, looked up once per device
+// with that device current.
+// ---------------------------------------------------------------------------
+constexpr int kNoAllocMaxHeads = 16, kNoAllocMaxRows = 4096, kNoAllocMaxHeadDim = 512;
+constexpr int kNoAllocRowsPerSplit = 64, kNoAllocMaxSplits = kNoAllocMaxRows / kNoAllocRowsPerSplit;
+constexpr size_t kNaScores = 0;
+constexpr size_t kNaExps = kNaScores + (size_t)kNoAllocMaxHeads * kNoAllocMaxRows * 4;
+constexpr size_t kNaPmax = kNaExps + (size_t)kNoAllocMaxHeads * kNoAllocMaxRows * 8;
+constexpr size_t kNaPidx = kNaPmax + (size_t)kNoAllocMaxHeads * kNoAllocMaxSplits * 4;
+constexpr size_t kNaPsum = kNaPidx + (size_t)kNoAllocMaxHeads * kNoAllocMaxSplits * 4;
+constexpr size_t kNaPwsum = kNaPsum + (size_t)kNoAllocMaxHeads * kNoAllocMaxSplits * 8;
+constexpr size_t kNaPacc = kNaPwsum + (size_t)kNoAllocMaxHeads * kNoAllocMaxSplits * 8;
+constexpr size_t kNaBytes = kNaPacc + (size_t)kNoAllocMaxHeads * kNoAllocMaxSplits * kNoAllocMaxHeadDim * 8;
+static_assert(kNaExps % 256 == 0 && kNaPmax % 256 == 0 && kNaPidx % 256 == 0 && kNaPsum % 256 == 0 &&
+                  kNaPwsum % 256 == 0 && kNaPacc % 256 == 0,
+              "scratch sections stay 256-byte aligned");
+
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kNaBytes];
+
+static std::mutex g_noalloc_mu;
+static std::map<int, unsigned char*> g_noalloc_addr;  // device ordinal -> device address of the array
+
+static unsigned char* noalloc_scratch_current_device() {
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  auto it = g_noalloc_addr.find(dev);
+  if (it != g_noalloc_addr.end()) return it->second;
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+  REQUIRE(e == cudaSuccess && p, RDET_E_CUDA,
+          std::string("cudaGetSymbolAddress of the attention scratch failed: ") + cudaGetErrorString(e));
+  g_noalloc_addr[dev] = static_cast<unsigned char*>(p);
+  return static_cast<unsigned char*>(p);
+}
+
 }  // namespace rdet
 
 // ===========================================================================
@@ -1664,6 +1705,39 @@ int32_t rdet_det_attention_decode(const int32_t* q, const int32_t* k_cache, cons
       o.sc.stride = o.rows;
     }
     a.sc = o.sc;
+    launch_attn_decode(a, static_cast<cudaStream_t>(stream));
+    CK(cudaGetLastError());
+  });
+}
+
+// Same computation as rdet_det_attention_decode with no device allocation:
+// the scratch is the library's fixed array (see noalloc_scratch_current_device).
+// Every scratch value is written before it is read, so nothing is cleared.
+int32_t rdet_det_attention_decode_noalloc(const int32_t* q, const int32_t* k_cache, const int32_t* v_cache,
+                                          uint32_t cap, uint32_t num_heads, uint32_t num_kv_heads,
+                                          uint32_t head_dim, uint32_t position, uint32_t window, int32_t* out,
+                                          void* stream) {
+  return guard([&] {
+    AttnDecodeArgs a;
+    attn_entry_args(a, q, k_cache, v_cache, cap, num_heads, num_kv_heads, head_dim, position, window, out);
+    const int rows = attn_rows(position, window);
+    REQUIRE(num_heads <= (uint32_t)kNoAllocMaxHeads, RDET_E_RANGE,
+            "rdet_det_attention_decode_noalloc supports at most 16 query heads");
+    REQUIRE(head_dim <= (uint32_t)kNoAllocMaxHeadDim, RDET_E_RANGE,
+            "rdet_det_attention_decode_noalloc supports head_dim <= 512");
+    REQUIRE(rows <= kNoAllocMaxRows, RDET_E_RANGE,
+            "rdet_det_attention_decode_noalloc attends at most 4096 rows (min(position + 1, window))");
+    unsigned char* base = noalloc_scratch_current_device();
+    a.rows_per_split = kNoAllocRowsPerSplit;
+    a.sc.scores = reinterpret_cast<int32_t*>(base + kNaScores);
+    a.sc.exps = reinterpret_cast<int64_t*>(base + kNaExps);
+    a.sc.pmax = reinterpret_cast<int32_t*>(base + kNaPmax);
+    a.sc.pidx = reinterpret_cast<int32_t*>(base + kNaPidx);
+    a.sc.psum = reinterpret_cast<int64_t*>(base + kNaPsum);
+    a.sc.pwsum = reinterpret_cast<int64_t*>(base + kNaPwsum);
+    a.sc.pacc = reinterpret_cast<int64_t*>(base + kNaPacc);
+    a.sc.max_splits = (rows + kNoAllocRowsPerSplit - 1) / kNoAllocRowsPerSplit;
+    a.sc.stride = kNoAllocMaxRows;
     launch_attn_decode(a, static_cast<cudaStream_t>(stream));
     CK(cudaGetLastError());
   });
