@@ -214,7 +214,317 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// decode GEMV v2: weights streamed with bulk async copies (cp.async.bulk) into
+// an mbarrier-pipelined ring of shared-memory stages.  One persistent CTA per
+// SM owns a balanced slice of rows of every matrix in the launch; a producer
+// warp streams whole rows (contiguous in HBM) while 8 consumer warps do the
+// exact i64 MACs from shared memory.  Per-row partial sums are combined in
+// shared memory with wrapping 64-bit adds (order-free), then requantized once.
+// Every pipeline wait is bounded: on timeout the kernel records the failure
+// in g_stream_err and returns instead of hanging.
+// ---------------------------------------------------------------------------
+__device__ int g_stream_err = 0;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait on an mbarrier phase
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+  for (uint32_t i = 0; i < (1u << 26); ++i)
+    if (mbar_test(b, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+constexpr int kStreamConsumerWarps = 8;
+constexpr int kStreamThreads = 32 * (kStreamConsumerWarps + 1);
+constexpr int kStreamMaxStages = 8;
+
+struct StreamCfg {
+  int ns;              // pipeline stages
+  int stage_bytes;     // bytes per stage buffer
+  int rs[3];           // rows per stage, per job
+  int acc_off[3];      // accumulator offset (rows) per job
+  int rpc[3];          // max rows per CTA per job
+  int njobs;
+  int x_bytes;         // bytes of the x buffer (K*4, rounded up to 128)
+};
+
+// rms scale over the 256 consumer threads (x in permuted layout; the sum is order-free)
+__device__ int32_t consumer_norm_scale(const int32_t* xs, int n, int64_t eps, uint64_t* red) {
+  uint64_t s = 0;
+  for (int i = threadIdx.x; i < n; i += 256) {
+    int64_t v = xs[i];
+    s = sat_add_u(s, (uint64_t)(v * v));
+  }
+  s = warp_satsum(s);
+  consumers_sync();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  consumers_sync();
+  if (threadIdx.x == 0) {
+    uint64_t t = 0;
+    for (int i = 0; i < 8; ++i) t = sat_add_u(t, red[i]);
+    red[32] = (uint64_t)(uint32_t)inv_sqrt_acc(acc_add_sat(div_acc_by_u32((int64_t)t, (uint32_t)n), eps));
+  }
+  consumers_sync();
+  return (int32_t)(uint32_t)red[32];
+}
+
+template <int WB>  // weight bytes: 2 (i16) or 4 (i32)
+__global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(const GemvArgs a, const StreamCfg cfg) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ __align__(8) uint64_t full[kStreamMaxStages], empty[kStreamMaxStages];
+  __shared__ uint64_t red[33];
+  const int K = a.K;
+  int32_t* xs = reinterpret_cast<int32_t*>(smem_raw);                      // x in chunk-plane layout
+  unsigned char* stages = smem_raw + cfg.x_bytes;
+  int64_t* acc = reinterpret_cast<int64_t*>(stages + (size_t)cfg.ns * cfg.stage_bytes);
+  const int G = gridDim.x, cta = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rowbytes = K * WB;
+  const int KC = rowbytes / 16;  // 16-byte chunks per row
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < cfg.ns; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kStreamConsumerWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == kStreamConsumerWarps) {
+    // ---------------- producer: stream this CTA's rows of every job
+    if (lane == 0) {
+      int t = 0;
+      bool ok = true;
+      for (int j = 0; j < cfg.njobs && ok; ++j) {
+        const int N = a.seg[j].w.rows;
+        const int lo = (int)((int64_t)N * cta / G), hi = (int)((int64_t)N * (cta + 1) / G);
+        const unsigned char* W = static_cast<const unsigned char*>(a.seg[j].w.p);
+        for (int r = lo; r < hi; r += cfg.rs[j], ++t) {
+          const int s = t % cfg.ns, k = t / cfg.ns;
+          if (t >= cfg.ns && !mbar_wait(&empty[s], (k - 1) & 1)) { ok = false; break; }
+          const int nr = min(cfg.rs[j], hi - r);
+          const uint32_t bytes = (uint32_t)nr * rowbytes;
+          mbar_arrive_tx(&full[s], bytes);
+          bulk_g2s(stages + (size_t)s * cfg.stage_bytes, W + (size_t)r * rowbytes, bytes, &full[s]);
+        }
+      }
+      if (!ok) {
+        atomicExch(&g_stream_err, 1);
+        // let the copies already issued land before the CTA's shared memory goes away
+        for (int i = 0; i < cfg.ns; ++i) {
+          int tt = t - 1 - i;
+          if (tt < 0) break;
+          mbar_wait(&full[tt % cfg.ns], (tt / cfg.ns) & 1);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers: prologue builds x (permuted chunk layout for i16)
+  // storage index p <-> element e: for i16, chunk c = e/8 has its low half at
+  // plane 0 [c*4 ..] and high half at plane 1 [K/2 + c*4 ..] (conflict-free LDS.128)
+  auto elem = [&](int p) -> int {
+    if (WB == 4) return p;
+    int h = p >= (K >> 1);
+    int q = p - h * (K >> 1);
+    return (q >> 2) * 8 + h * 4 + (q & 3);
+  };
+  for (int p = threadIdx.x; p < K; p += 256) xs[p] = a.a[elem(p)];
+  for (int j = 0; j < cfg.njobs; ++j)
+    for (int i = threadIdx.x; i < cfg.rpc[j]; i += 256) acc[cfg.acc_off[j] + i] = 0;
+  consumers_sync();
+  if (a.pro != kProNone) {
+    int32_t sc = consumer_norm_scale(xs, K, a.eps, red);
+    if (a.pro == kProNorm) {
+      for (int p = threadIdx.x; p < K; p += 256) xs[p] = mul_sat(mul_sat(xs[p], sc), a.g1[elem(p)]);
+    } else {
+      for (int p = threadIdx.x; p < K; p += 256) {
+        int e = elem(p);
+        int32_t t = add_sat(a.res[e], mul_sat(mul_sat(xs[p], sc), a.g1[e]));
+        if (a.has_scalar) t = mul_sat(t, a.scalar);
+        xs[p] = t;
+        if (cta == 0 && a.t_out) a.t_out[e] = t;
+      }
+      consumers_sync();
+      if (a.pro == kProResNorm || a.pro == kProResScaleNorm) {
+        int32_t sc2 = consumer_norm_scale(xs, K, a.eps, red);
+        for (int p = threadIdx.x; p < K; p += 256) xs[p] = mul_sat(mul_sat(xs[p], sc2), a.g2[elem(p)]);
+      }
+    }
+  }
+  consumers_sync();
+
+  // ---------------- consumers: stages
+  bool ok = true;
+  int t = 0;
+  for (int j = 0; j < cfg.njobs && ok; ++j) {
+    const int N = a.seg[j].w.rows;
+    const int lo = (int)((int64_t)N * cta / G), hi = (int)((int64_t)N * (cta + 1) / G);
+    int64_t* accj = acc + cfg.acc_off[j];
+    for (int r = lo; r < hi; r += cfg.rs[j], ++t) {
+      const int s = t % cfg.ns, k = t / cfg.ns;
+      if (!mbar_wait(&full[s], k & 1)) { ok = false; break; }
+      const int nr = min(cfg.rs[j], hi - r);
+      const int C = nr * KC;
+      const int c0 = (int)((int64_t)C * warp / kStreamConsumerWarps);
+      const int c1 = (int)((int64_t)C * (warp + 1) / kStreamConsumerWarps);
+      const uint4* sp = reinterpret_cast<const uint4*>(stages + (size_t)s * cfg.stage_bytes);
+      int c = c0 + lane;
+      int row = c / KC, col = c - row * KC;
+      int cur_row = -1;
+      int64_t cur = 0;
+      for (; c < c1; c += 32) {
+        uint4 w = sp[c];
+        int64_t p;
+        if (WB == 2) {
+          int4 xa = reinterpret_cast<const int4*>(xs)[col];
+          int4 xb = reinterpret_cast<const int4*>(xs + (K >> 1))[col];
+          p = (int64_t)xa.x * lo16(w.x) + (int64_t)xa.y * hi16(w.x) + (int64_t)xa.z * lo16(w.y) +
+              (int64_t)xa.w * hi16(w.y) + (int64_t)xb.x * lo16(w.z) + (int64_t)xb.y * hi16(w.z) +
+              (int64_t)xb.z * lo16(w.w) + (int64_t)xb.w * hi16(w.w);
+        } else {
+          int4 xa = reinterpret_cast<const int4*>(xs)[col];
+          p = (int64_t)xa.x * (int32_t)w.x + (int64_t)xa.y * (int32_t)w.y + (int64_t)xa.z * (int32_t)w.z +
+              (int64_t)xa.w * (int32_t)w.w;
+        }
+        if (row != cur_row) {
+          if (cur_row >= 0) atomicAdd(reinterpret_cast<unsigned long long*>(&accj[r - lo + cur_row]), (unsigned long long)cur);
+          cur_row = row;
+          cur = p;
+        } else {
+          cur += p;
+        }
+        col += 32;
+        while (col >= KC) { col -= KC; ++row; }
+      }
+      const int r0 = __shfl_sync(0xffffffffu, cur_row, 0);
+      if (__all_sync(0xffffffffu, cur_row == r0)) {
+        int64_t tot = warp_sum64(cur);
+        if (lane == 0 && r0 >= 0) atomicAdd(reinterpret_cast<unsigned long long*>(&accj[r - lo + r0]), (unsigned long long)tot);
+      } else if (cur_row >= 0) {
+        atomicAdd(reinterpret_cast<unsigned long long*>(&accj[r - lo + cur_row]), (unsigned long long)cur);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  }
+  if (!ok) {
+    atomicExch(&g_stream_err, 1);
+    return;
+  }
+  consumers_sync();
+  // ---------------- epilogue
+  if (a.pair_geglu) {
+    const int N = a.seg[0].w.rows;
+    const int lo = (int)((int64_t)N * cta / G), hi = (int)((int64_t)N * (cta + 1) / G);
+    for (int r = lo + threadIdx.x; r < hi; r += 256)
+      a.seg[0].y[r] = mul_sat(gelu_act(requantize(acc[cfg.acc_off[0] + r - lo])), requantize(acc[cfg.acc_off[1] + r - lo]));
+    return;
+  }
+  for (int j = 0; j < cfg.njobs; ++j) {
+    const GemvSeg& sg = a.seg[j];
+    const int N = sg.w.rows;
+    const int lo = (int)((int64_t)N * cta / G), hi = (int)((int64_t)N * (cta + 1) / G);
+    for (int r = lo + threadIdx.x; r < hi; r += 256) {
+      int32_t v = requantize(acc[cfg.acc_off[j] + r - lo]);
+      if (sg.epi == kEpiSoftcap) v = softcap_act(v, a.softcap);
+      else if (sg.epi == kEpiGeluMul) v = mul_sat(gelu_act(v), sg.vec[r]);
+      sg.y[r] = v;
+    }
+  }
+}
+
+static int g_stream_attr_dev = -1;
+static void stream_set_attrs() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (g_stream_attr_dev == dev) return;
+  cudaFuncSetAttribute(gemv_stream_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  cudaFuncSetAttribute(gemv_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  g_stream_attr_dev = dev;
+}
+void kernels_init() { stream_set_attrs(); }
+
+int stream_error_flag(bool reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_stream_err, sizeof(int));
+  if (reset && v) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_stream_err, &z, sizeof(int));
+  }
+  return v;
+}
+
+// Plans and launches the streamed GEMV; returns false when the launch does not
+// qualify (mixed widths, unaligned rows, oversize rows), so v1 runs instead.
+static bool launch_gemv_stream(const GemvArgs& a, cudaStream_t s) {
+  const int njobs = a.pair_geglu ? 2 : a.nseg;
+  const int width = a.seg[0].w.width;
+  for (int j = 0; j < njobs; ++j) {
+    if (a.seg[j].w.width != width || a.seg[j].w.cols != a.K) return false;
+    if ((reinterpret_cast<uintptr_t>(a.seg[j].w.p) & 15) != 0) return false;
+  }
+  const int WB = width / 8;
+  const long rowbytes = (long)a.K * WB;
+  if (rowbytes % 16 != 0 || rowbytes > 48 * 1024) return false;
+  if (WB == 2 && (a.K % 16) != 0) return false;  // chunk planes need K/2 divisible by 8
+  const int G = sm_count();
+  StreamCfg cfg{};
+  cfg.njobs = njobs;
+  cfg.x_bytes = (int)(((long)a.K * 4 + 127) / 128 * 128);
+  int acc_rows = 0;
+  for (int j = 0; j < njobs; ++j) {
+    const int N = a.seg[j].w.rows;
+    cfg.rpc[j] = (N + G - 1) / G + 1;
+    cfg.acc_off[j] = acc_rows;
+    acc_rows += cfg.rpc[j];
+  }
+  const long acc_bytes = (long)acc_rows * 8;
+  const long budget = 216L * 1024 - cfg.x_bytes - acc_bytes;
+  const long target = 24 * 1024;
+  long stage = rowbytes >= target ? rowbytes : (target / rowbytes) * rowbytes;
+  int ns = (int)(budget / stage);
+  if (ns > kStreamMaxStages) ns = kStreamMaxStages;
+  if (ns < 2) return false;
+  cfg.ns = ns;
+  cfg.stage_bytes = (int)((stage + 127) / 128 * 128);
+  for (int j = 0; j < njobs; ++j) cfg.rs[j] = (int)(stage / rowbytes);
+  const size_t smem = (size_t)cfg.x_bytes + (size_t)cfg.ns * cfg.stage_bytes + (size_t)acc_bytes;
+  if (smem > 220 * 1024) return false;
+  stream_set_attrs();
+  if (WB == 2) gemv_stream_kernel<2><<<G, kStreamThreads, smem, s>>>(a, cfg);
+  else gemv_stream_kernel<4><<<G, kStreamThreads, smem, s>>>(a, cfg);
+  return true;
+}
+
 void launch_gemv(const GemvArgs& a, cudaStream_t s) {
+  if (launch_gemv_stream(a, s)) return;
   int rows = 0;
   if (a.pair_geglu) rows = a.seg[0].w.rows;
   else for (int i = 0; i < a.nseg; ++i) rows += a.seg[i].w.rows;

@@ -159,5 +159,9 @@ void launch_copy_rows(const int32_t* src, int32_t* dst, size_t n, cudaStream_t s
 void launch_synth(void* dst, int32_t width, int32_t rank, int64_t n, int64_t cols, uint64_t key, cudaStream_t s);
 
 int sm_count();
+// per-device one-time kernel attributes (call with the device current, outside stream capture)
+void kernels_init();
+// nonzero when a bounded pipeline wait in a streamed kernel gave up (reset: clear it)
+int stream_error_flag(bool reset);
 
 }  // namespace rdet

@@ -702,6 +702,8 @@ static void check_err_flag(Ctx& c, const char* what) {
     CK(cudaMemset(c.d_err, 0, 4));
     throw Fail{RDET_E_RANGE, std::string(what) + ": token id is out of bounds for the embedding tensor"};
   }
+  if (stream_error_flag(true))
+    throw Fail{RDET_E_CUDA, std::string(what) + ": a weight-streaming pipeline wait timed out"};
 }
 
 // ---------------------------------------------------------------------------
@@ -1206,6 +1208,7 @@ static void open_common(Ctx& c, const rdet_opts* opts) {
   REQUIRE(c.device >= 0 && c.device < ndev, RDET_E_INVALID, "invalid CUDA device ordinal");
   CK(cudaSetDevice(c.device));
   CK(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+  kernels_init();
 }
 
 static std::string read_file(const std::string& path) {
