@@ -257,11 +257,26 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-constexpr int kStreamConsumerWarps = 8;
+
+// Shape of the streamed GEMV (compile-time tunables).
+#ifndef RDET_STREAM_CONSUMER_WARPS
+#define RDET_STREAM_CONSUMER_WARPS 8
+#endif
+#ifndef RDET_STREAM_STAGE_BYTES
+#define RDET_STREAM_STAGE_BYTES (24 * 1024)
+#endif
+#ifndef RDET_STREAM_CTAS_PER_SM
+#define RDET_STREAM_CTAS_PER_SM 1
+#endif
+#ifndef RDET_STREAM_MAX_STAGES
+#define RDET_STREAM_MAX_STAGES 8
+#endif
+constexpr int kStreamConsumerWarps = RDET_STREAM_CONSUMER_WARPS;
+constexpr int kStreamConsumerThreads = 32 * kStreamConsumerWarps;
 constexpr int kStreamThreads = 32 * (kStreamConsumerWarps + 1);
-constexpr int kStreamMaxStages = 8;
+constexpr int kStreamMaxStages = RDET_STREAM_MAX_STAGES;
+constexpr int kStreamCtasPerSm = RDET_STREAM_CTAS_PER_SM;
 
 struct StreamCfg {
   int ns;              // pipeline stages
@@ -273,10 +288,14 @@ struct StreamCfg {
   int x_bytes;         // bytes of the x buffer (K*4, rounded up to 128)
 };
 
-// rms scale over the 256 consumer threads (x in permuted layout; the sum is order-free)
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync 1, %0;" ::"r"(kStreamConsumerThreads) : "memory");
+}
+
+// rms scale over the consumer threads (x in permuted layout; the sum is order-free)
 __device__ int32_t consumer_norm_scale(const int32_t* xs, int n, int64_t eps, uint64_t* red) {
   uint64_t s = 0;
-  for (int i = threadIdx.x; i < n; i += 256) {
+  for (int i = threadIdx.x; i < n; i += kStreamConsumerThreads) {
     int64_t v = xs[i];
     s = sat_add_u(s, (uint64_t)(v * v));
   }
@@ -286,7 +305,7 @@ __device__ int32_t consumer_norm_scale(const int32_t* xs, int n, int64_t eps, ui
   consumers_sync();
   if (threadIdx.x == 0) {
     uint64_t t = 0;
-    for (int i = 0; i < 8; ++i) t = sat_add_u(t, red[i]);
+    for (int i = 0; i < kStreamConsumerWarps; ++i) t = sat_add_u(t, red[i]);
     red[32] = (uint64_t)(uint32_t)inv_sqrt_acc(acc_add_sat(div_acc_by_u32((int64_t)t, (uint32_t)n), eps));
   }
   consumers_sync();
@@ -294,7 +313,8 @@ __device__ int32_t consumer_norm_scale(const int32_t* xs, int n, int64_t eps, ui
 }
 
 template <int WB>  // weight bytes: 2 (i16) or 4 (i32)
-__global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(const GemvArgs a, const StreamCfg cfg) {
+__global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) gemv_stream_kernel(const GemvArgs a,
+                                                                                       const StreamCfg cfg) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t full[kStreamMaxStages], empty[kStreamMaxStages];
   __shared__ uint64_t red[33];
@@ -355,16 +375,16 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(const Ge
     int q = p - h * (K >> 1);
     return (q >> 2) * 8 + h * 4 + (q & 3);
   };
-  for (int p = threadIdx.x; p < K; p += 256) xs[p] = a.a[elem(p)];
+  for (int p = threadIdx.x; p < K; p += kStreamConsumerThreads) xs[p] = a.a[elem(p)];
   for (int j = 0; j < cfg.njobs; ++j)
-    for (int i = threadIdx.x; i < cfg.rpc[j]; i += 256) acc[cfg.acc_off[j] + i] = 0;
+    for (int i = threadIdx.x; i < cfg.rpc[j]; i += kStreamConsumerThreads) acc[cfg.acc_off[j] + i] = 0;
   consumers_sync();
   if (a.pro != kProNone) {
     int32_t sc = consumer_norm_scale(xs, K, a.eps, red);
     if (a.pro == kProNorm) {
-      for (int p = threadIdx.x; p < K; p += 256) xs[p] = mul_sat(mul_sat(xs[p], sc), a.g1[elem(p)]);
+      for (int p = threadIdx.x; p < K; p += kStreamConsumerThreads) xs[p] = mul_sat(mul_sat(xs[p], sc), a.g1[elem(p)]);
     } else {
-      for (int p = threadIdx.x; p < K; p += 256) {
+      for (int p = threadIdx.x; p < K; p += kStreamConsumerThreads) {
         int e = elem(p);
         int32_t t = add_sat(a.res[e], mul_sat(mul_sat(xs[p], sc), a.g1[e]));
         if (a.has_scalar) t = mul_sat(t, a.scalar);
@@ -374,7 +394,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(const Ge
       consumers_sync();
       if (a.pro == kProResNorm || a.pro == kProResScaleNorm) {
         int32_t sc2 = consumer_norm_scale(xs, K, a.eps, red);
-        for (int p = threadIdx.x; p < K; p += 256) xs[p] = mul_sat(mul_sat(xs[p], sc2), a.g2[elem(p)]);
+        for (int p = threadIdx.x; p < K; p += kStreamConsumerThreads) xs[p] = mul_sat(mul_sat(xs[p], sc2), a.g2[elem(p)]);
       }
     }
   }
@@ -443,7 +463,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(const Ge
   if (a.pair_geglu) {
     const int N = a.seg[0].w.rows;
     const int lo = (int)((int64_t)N * cta / G), hi = (int)((int64_t)N * (cta + 1) / G);
-    for (int r = lo + threadIdx.x; r < hi; r += 256)
+    for (int r = lo + threadIdx.x; r < hi; r += kStreamConsumerThreads)
       a.seg[0].y[r] = mul_sat(gelu_act(requantize(acc[cfg.acc_off[0] + r - lo])), requantize(acc[cfg.acc_off[1] + r - lo]));
     return;
   }
@@ -451,7 +471,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(const Ge
     const GemvSeg& sg = a.seg[j];
     const int N = sg.w.rows;
     const int lo = (int)((int64_t)N * cta / G), hi = (int)((int64_t)N * (cta + 1) / G);
-    for (int r = lo + threadIdx.x; r < hi; r += 256) {
+    for (int r = lo + threadIdx.x; r < hi; r += kStreamConsumerThreads) {
       int32_t v = requantize(acc[cfg.acc_off[j] + r - lo]);
       if (sg.epi == kEpiSoftcap) v = softcap_act(v, a.softcap);
       else if (sg.epi == kEpiGeluMul) v = mul_sat(gelu_act(v), sg.vec[r]);
@@ -483,7 +503,7 @@ int stream_error_flag(bool reset) {
 
 // Plans and launches the streamed GEMV; returns false when the launch does not
 // qualify (mixed widths, unaligned rows, oversize rows), so v1 runs instead.
-static bool launch_gemv_stream(const GemvArgs& a, cudaStream_t s) {
+[[maybe_unused]] static bool launch_gemv_stream(const GemvArgs& a, cudaStream_t s) {
   const int njobs = a.pair_geglu ? 2 : a.nseg;
   const int width = a.seg[0].w.width;
   for (int j = 0; j < njobs; ++j) {
@@ -494,7 +514,7 @@ static bool launch_gemv_stream(const GemvArgs& a, cudaStream_t s) {
   const long rowbytes = (long)a.K * WB;
   if (rowbytes % 16 != 0 || rowbytes > 48 * 1024) return false;
   if (WB == 2 && (a.K % 16) != 0) return false;  // chunk planes need K/2 divisible by 8
-  const int G = sm_count();
+  const int G = sm_count() * kStreamCtasPerSm;
   StreamCfg cfg{};
   cfg.njobs = njobs;
   cfg.x_bytes = (int)(((long)a.K * 4 + 127) / 128 * 128);
@@ -506,8 +526,8 @@ static bool launch_gemv_stream(const GemvArgs& a, cudaStream_t s) {
     acc_rows += cfg.rpc[j];
   }
   const long acc_bytes = (long)acc_rows * 8;
-  const long budget = 216L * 1024 - cfg.x_bytes - acc_bytes;
-  const long target = 24 * 1024;
+  const long budget = 216L * 1024 / kStreamCtasPerSm - cfg.x_bytes - acc_bytes;
+  const long target = RDET_STREAM_STAGE_BYTES;
   long stage = rowbytes >= target ? rowbytes : (target / rowbytes) * rowbytes;
   int ns = (int)(budget / stage);
   if (ns > kStreamMaxStages) ns = kStreamMaxStages;
@@ -516,15 +536,182 @@ static bool launch_gemv_stream(const GemvArgs& a, cudaStream_t s) {
   cfg.stage_bytes = (int)((stage + 127) / 128 * 128);
   for (int j = 0; j < njobs; ++j) cfg.rs[j] = (int)(stage / rowbytes);
   const size_t smem = (size_t)cfg.x_bytes + (size_t)cfg.ns * cfg.stage_bytes + (size_t)acc_bytes;
-  if (smem > 220 * 1024) return false;
+  if (smem > 220 * 1024 / kStreamCtasPerSm) return false;
   stream_set_attrs();
   if (WB == 2) gemv_stream_kernel<2><<<G, kStreamThreads, smem, s>>>(a, cfg);
   else gemv_stream_kernel<4><<<G, kStreamThreads, smem, s>>>(a, cfg);
   return true;
 }
 
+// ---------------------------------------------------------------------------
+// decode GEMV v3: each warp computes two rows at once (for gate/up, the gate
+// row and the up row of the same output), all loads of a row piece issued
+// before any math, and four independent i64 accumulator chains.
+// ---------------------------------------------------------------------------
+#ifndef RDET_GEMV3_NCH
+#define RDET_GEMV3_NCH 10
+#endif
+#ifndef RDET_GEMV3_CTAS_PER_SM
+#define RDET_GEMV3_CTAS_PER_SM 2
+#endif
+#ifndef RDET_GEMV3_NCH_W32
+#define RDET_GEMV3_NCH_W32 6
+#endif
+
+template <int WB>
+__device__ __forceinline__ void dot_chunk(const uint4& w, const int32_t* xs, int c, int64_t& a0, int64_t& a1) {
+  if (WB == 2) {
+    const int4* xp = reinterpret_cast<const int4*>(xs + 8 * c);
+    int4 x0 = xp[0], x1 = xp[1];
+    a0 += (int64_t)x0.x * lo16(w.x);
+    a1 += (int64_t)x0.y * hi16(w.x);
+    a0 += (int64_t)x0.z * lo16(w.y);
+    a1 += (int64_t)x0.w * hi16(w.y);
+    a0 += (int64_t)x1.x * lo16(w.z);
+    a1 += (int64_t)x1.y * hi16(w.z);
+    a0 += (int64_t)x1.z * lo16(w.w);
+    a1 += (int64_t)x1.w * hi16(w.w);
+  } else {
+    int4 x0 = reinterpret_cast<const int4*>(xs)[c];
+    a0 += (int64_t)x0.x * (int32_t)w.x;
+    a1 += (int64_t)x0.y * (int32_t)w.y;
+    a0 += (int64_t)x0.z * (int32_t)w.z;
+    a1 += (int64_t)x0.w * (int32_t)w.w;
+  }
+}
+
+// dots of rows ra (matrix A) and rb (matrix B, may be absent) with xs
+template <int WB>
+__device__ __forceinline__ void dot_rows2(const unsigned char* A, int ra, const unsigned char* B, int rb, bool has_b,
+                                          const int32_t* xs, int K, int lane, int64_t& outa, int64_t& outb) {
+  const int nc = K * WB / 16;
+  const uint4* pa = reinterpret_cast<const uint4*>(A + (size_t)ra * K * WB);
+  const uint4* pb = reinterpret_cast<const uint4*>(has_b ? B + (size_t)rb * K * WB : A);
+  constexpr int kG3Nch = WB == 2 ? RDET_GEMV3_NCH : RDET_GEMV3_NCH_W32;
+  int64_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+  for (int c0 = lane; c0 < nc; c0 += 32 * kG3Nch) {
+    uint4 wa[kG3Nch], wb[kG3Nch];
+#pragma unroll
+    for (int u = 0; u < kG3Nch; ++u) {
+      int c = c0 + 32 * u;
+      wa[u] = c < nc ? ldg_stream(pa + c) : make_uint4(0, 0, 0, 0);
+      wb[u] = (has_b && c < nc) ? ldg_stream(pb + c) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kG3Nch; ++u) {
+      int c = c0 + 32 * u;
+      if (c < nc) {
+        dot_chunk<WB>(wa[u], xs, c, a0, a1);
+        if (has_b) dot_chunk<WB>(wb[u], xs, c, b0, b1);
+      }
+    }
+  }
+  outa = warp_sum64(a0 + a1);
+  outb = warp_sum64(b0 + b1);
+}
+
+template <int WB>
+__global__ void __launch_bounds__(kGemvThreads, RDET_GEMV3_CTAS_PER_SM) gemv3_kernel(const GemvArgs a, int per_item) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int32_t* xs = reinterpret_cast<int32_t*>(smem_raw);
+  __shared__ uint64_t red[33];
+  const int K = a.K;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = a.a[i];
+  __syncthreads();
+  if (a.pro != kProNone) {
+    int32_t sc = block_norm_scale(xs, K, a.eps, red);
+    if (a.pro == kProNorm) {
+      for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = mul_sat(mul_sat(xs[i], sc), a.g1[i]);
+    } else {
+      for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        int32_t t = add_sat(a.res[i], mul_sat(mul_sat(xs[i], sc), a.g1[i]));
+        if (a.has_scalar) t = mul_sat(t, a.scalar);
+        xs[i] = t;
+        if (blockIdx.x == 0 && a.t_out) a.t_out[i] = t;
+      }
+      __syncthreads();
+      if (a.pro == kProResNorm || a.pro == kProResScaleNorm) {
+        int32_t sc2 = block_norm_scale(xs, K, a.eps, red);
+        for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = mul_sat(mul_sat(xs[i], sc2), a.g2[i]);
+      }
+    }
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  if (a.pair_geglu) {
+    const int R = a.seg[0].w.rows;
+    const unsigned char* G = static_cast<const unsigned char*>(a.seg[0].w.p);
+    const unsigned char* U = static_cast<const unsigned char*>(a.seg[1].w.p);
+    for (int r = gw; r < R; r += nw) {
+      int64_t g, u;
+      dot_rows2<WB>(G, r, U, r, true, xs, K, lane, g, u);
+      if (lane == 0) a.seg[0].y[r] = mul_sat(gelu_act(requantize(g)), requantize(u));
+    }
+    return;
+  }
+  // work items: `per_item` (1 or 2) consecutive rows within one segment
+  int pairs[3], total = 0;
+  for (int sgi = 0; sgi < a.nseg; ++sgi) {
+    pairs[sgi] = (a.seg[sgi].w.rows + per_item - 1) / per_item;
+    total += pairs[sgi];
+  }
+  for (int gp = gw; gp < total; gp += nw) {
+    int sgi = 0, p = gp;
+    while (p >= pairs[sgi]) { p -= pairs[sgi]; ++sgi; }
+    const GemvSeg& sg = a.seg[sgi];
+    const unsigned char* Wm = static_cast<const unsigned char*>(sg.w.p);
+    const int r0 = per_item * p, r1 = r0 + 1;
+    const bool two = per_item == 2 && r1 < sg.w.rows;
+    int64_t d0, d1;
+    dot_rows2<WB>(Wm, r0, Wm, r1, two, xs, K, lane, d0, d1);
+    if (lane < 2 && (lane == 0 || two)) {
+      const int r = lane == 0 ? r0 : r1;
+      int32_t v = requantize(lane == 0 ? d0 : d1);
+      if (sg.epi == kEpiSoftcap) v = softcap_act(v, a.softcap);
+      else if (sg.epi == kEpiGeluMul) v = mul_sat(gelu_act(v), sg.vec[r]);
+      sg.y[r] = v;
+    }
+  }
+}
+
+static bool launch_gemv3(const GemvArgs& a, cudaStream_t s) {
+  const int njobs = a.pair_geglu ? 2 : a.nseg;
+  const int width = a.seg[0].w.width;
+  for (int j = 0; j < njobs; ++j) {
+    if (a.seg[j].w.width != width || a.seg[j].w.cols != a.K) return false;
+    if ((reinterpret_cast<uintptr_t>(a.seg[j].w.p) & 15) != 0) return false;
+  }
+  const int WB = width / 8;
+  if (((long)a.K * WB) % 16 != 0) return false;
+  // two rows per warp item unless that would leave most warp slots idle
+  const int warps = kGemvThreads / 32;
+  const int cap = sm_count() * RDET_GEMV3_CTAS_PER_SM;
+  int rows = 0;
+  for (int j = 0; j < a.nseg; ++j) rows += a.seg[j].w.rows;
+  const int per_item = (!a.pair_geglu && rows < cap * warps) ? 1 : 2;
+  int items = 0;
+  if (a.pair_geglu) items = a.seg[0].w.rows;
+  else for (int j = 0; j < a.nseg; ++j) items += (a.seg[j].w.rows + per_item - 1) / per_item;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  const size_t smem = (size_t)a.K * 4;
+  if (smem > 48 * 1024) {
+    cudaFuncSetAttribute(gemv3_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gemv3_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  }
+  if (WB == 2) gemv3_kernel<2><<<blocks, kGemvThreads, smem, s>>>(a, per_item);
+  else gemv3_kernel<4><<<blocks, kGemvThreads, smem, s>>>(a, per_item);
+  return true;
+}
+
 void launch_gemv(const GemvArgs& a, cudaStream_t s) {
+#ifdef RDET_GEMV_STREAMED
   if (launch_gemv_stream(a, s)) return;
+#else
+  if (launch_gemv3(a, s)) return;
+#endif
   int rows = 0;
   if (a.pair_geglu) rows = a.seg[0].w.rows;
   else for (int i = 0; i < a.nseg; ++i) rows += a.seg[i].w.rows;
