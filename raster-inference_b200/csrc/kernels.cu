@@ -694,6 +694,7 @@ static bool launch_gemv3(const GemvArgs& a, cudaStream_t s) {
   int items = 0;
   if (a.pair_geglu) items = a.seg[0].w.rows;
   else for (int j = 0; j < a.nseg; ++j) items += (a.seg[j].w.rows + per_item - 1) / per_item;
+  int blocks = (items + warps - 1) / warps;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   const size_t smem = (size_t)a.K * 4;
