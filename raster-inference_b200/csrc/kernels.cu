@@ -5,6 +5,8 @@
 // associative (reference docs/plans/DET_NUM_SPEC.md, "Parallelism legality").
 #include <cstdio>
 
+#include <cooperative_groups.h>
+
 #include "det_dev.cuh"
 #include "kernels.h"
 
@@ -489,7 +491,11 @@ static void stream_set_attrs() {
   cudaFuncSetAttribute(gemv_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   g_stream_attr_dev = dev;
 }
-void kernels_init() { stream_set_attrs(); }
+static void attn_cluster_init();
+void kernels_init() {
+  stream_set_attrs();
+  attn_cluster_init();
+}
 
 int stream_error_flag(bool reset) {
   int v = 0;
@@ -1098,6 +1104,238 @@ void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
   attn_dec_exp<<<grid, 256, 0, s>>>(a);
   attn_dec_wsum<<<grid, 256, (size_t)G * a.rows_per_split * 4, s>>>(a);
   attn_dec_final<<<a.Hq, 256, 0, s>>>(a);
+}
+
+// ---------------------------------------------------------------------------
+// decode attention, cluster version.  Cluster = the CL CTAs of one KV head;
+// CTA r takes rows [n*r/CL, n*(r+1)/CL) of the window.  Exactly the arithmetic
+// of attention_output_into for each of the G query heads of the KV head.
+// ---------------------------------------------------------------------------
+namespace cg = cooperative_groups;
+constexpr int kAcThreads = 512;
+
+template <int G>
+__global__ void __launch_bounds__(kAcThreads) attn_dec_cluster_kernel(const AttnDecodeArgs a, int rmax) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  cg::cluster_group cl = cg::this_cluster();
+  const int CL = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+  const int kvh = blockIdx.y, d = a.d;
+  int32_t* qs = reinterpret_cast<int32_t*>(smem_raw);             // [G][d]
+  int32_t* sc = qs + G * d;                                        // [G][rmax] scores, then weights
+  int64_t* ex = reinterpret_cast<int64_t*>(sc + G * rmax + (G * rmax & 1));  // [G][rmax]
+  int64_t* pacc = ex + G * rmax;                                   // [G][d] partial weighted sums
+  __shared__ int32_t s_max[G], s_idx[G];
+  __shared__ int64_t s_sum[G], s_wsum[G];
+  __shared__ int32_t g_max[G], g_idx[G], g_res[G];
+  __shared__ int64_t g_sum[G];
+  __shared__ int32_t wm[kAcThreads / 32][G], wi[kAcThreads / 32][G];
+  __shared__ int64_t ws[kAcThreads / 32][G];
+  int start, n;
+  decode_window(a, &start, &n);
+  const int lo = (int)((int64_t)n * rank / CL), hi = (int)((int64_t)n * (rank + 1) / CL);
+  const int rows = hi - lo;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = kAcThreads / 32;
+  for (int i = threadIdx.x; i < G * d; i += kAcThreads) qs[i] = a.q[(size_t)kvh * G * d + i];
+  __syncthreads();
+  // ---- phase 1: scores (warp per row; 16-byte loads when d % 128 == 0)
+  int32_t bm[G], bi[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) { bm[g] = INT32_MIN; bi[g] = INT32_MAX; }
+  for (int j = warp; j < rows; j += nwarp) {
+    const int32_t* kr = a.k_cache + ((size_t)kvh * a.cap + start + lo + j) * d;
+    int64_t acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = 0;
+    if ((d & 127) == 0) {
+      for (int c = lane; c < d / 4; c += 32) {
+        int4 kv = reinterpret_cast<const int4*>(kr)[c];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          int4 qv = reinterpret_cast<const int4*>(qs + g * d)[c];
+          acc[g] += (int64_t)kv.x * qv.x + (int64_t)kv.y * qv.y + (int64_t)kv.z * qv.z + (int64_t)kv.w * qv.w;
+        }
+      }
+    } else {
+      for (int t = lane; t < d; t += 32) {
+        int64_t kv = kr[t];
+#pragma unroll
+        for (int g = 0; g < G; ++g) acc[g] += kv * qs[g * d + t];
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      int32_t v = requantize(warp_sum64(acc[g]));
+      if (lane == 0) sc[g * rmax + j] = v;
+      if (v > bm[g]) { bm[g] = v; bi[g] = lo + j; }  // rows ascend: the first max is kept
+    }
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) { wm[warp][g] = bm[g]; wi[warp][g] = bi[g]; }
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    int32_t m = INT32_MIN, mi = INT32_MAX;
+    for (int w = 0; w < nwarp; ++w) {
+      if (wi[w][g] == INT32_MAX) continue;
+      if (wm[w][g] > m || (wm[w][g] == m && wi[w][g] < mi)) { m = wm[w][g]; mi = wi[w][g]; }
+    }
+    s_max[g] = m;
+    s_idx[g] = mi;
+  }
+  cl.sync();
+  // ---- global first max (every CTA computes the same value from all ranks)
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    int32_t m = INT32_MIN, mi = INT32_MAX;
+    for (int r = 0; r < CL; ++r) {
+      int32_t v = *cl.map_shared_rank(&s_max[g], r), ix = *cl.map_shared_rank(&s_idx[g], r);
+      if (ix == INT32_MAX) continue;
+      if (v > m || (v == m && ix < mi)) { m = v; mi = ix; }
+    }
+    g_max[g] = m;
+    g_idx[g] = mi;
+  }
+  __syncthreads();
+  // ---- phase 2: exp terms, local sums
+  for (int g = 0; g < G; ++g) {
+    uint64_t sum = 0;
+    for (int j = threadIdx.x; j < rows; j += kAcThreads) {
+      int64_t e = exp_term(sc[g * rmax + j], g_max[g]);
+      ex[g * rmax + j] = e;
+      sum += (uint64_t)e;
+    }
+    sum = (uint64_t)warp_sum64((int64_t)sum);
+    if (lane == 0) ws[warp][g] = (int64_t)sum;
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    int64_t t = 0;
+    for (int w = 0; w < nwarp; ++w) t += ws[w][threadIdx.x];
+    s_sum[threadIdx.x] = t;
+  }
+  cl.sync();
+  if (threadIdx.x < G) {
+    int64_t t = 0;
+    for (int r = 0; r < CL; ++r) t += *cl.map_shared_rank(&s_sum[threadIdx.x], r);
+    g_sum[threadIdx.x] = t;
+  }
+  __syncthreads();
+  // ---- phase 3: weights, local weight sums and partial weighted V sums
+  for (int g = 0; g < G; ++g) {
+    int64_t wsum = 0;
+    for (int j = threadIdx.x; j < rows; j += kAcThreads) {
+      int32_t w = softmax_weight(ex[g * rmax + j], g_sum[g]);
+      sc[g * rmax + j] = w;
+      wsum += w;
+    }
+    wsum = warp_sum64(wsum);
+    if (lane == 0) ws[warp][g] = wsum;
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    int64_t t = 0;
+    for (int w = 0; w < nwarp; ++w) t += ws[w][threadIdx.x];
+    s_wsum[threadIdx.x] = t;
+  }
+  for (int dim = threadIdx.x; dim < d; dim += kAcThreads) {
+    int64_t acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = 0;
+    const int32_t* vb = a.v_cache + ((size_t)kvh * a.cap + start + lo) * d + dim;
+    for (int j = 0; j < rows; ++j) {
+      int64_t v = vb[(size_t)j * d];
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] += v * sc[g * rmax + j];
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) pacc[g * d + dim] = acc[g];
+  }
+  cl.sync();
+  // ---- combine: this CTA finalizes output dims [d*rank/CL, d*(rank+1)/CL)
+  if (threadIdx.x < G) {
+    int64_t t = 0;
+    for (int r = 0; r < CL; ++r) t += *cl.map_shared_rank(&s_wsum[threadIdx.x], r);
+    g_res[threadIdx.x] = sub_sat(kOneAct, t > INT32_MAX ? INT32_MAX : (int32_t)t);
+  }
+  __syncthreads();
+  const int d0 = (int)((int64_t)d * rank / CL), d1 = (int)((int64_t)d * (rank + 1) / CL);
+  for (int e = threadIdx.x; e < G * (d1 - d0); e += kAcThreads) {
+    const int g = e / (d1 - d0), dim = d0 + e % (d1 - d0);
+    int64_t acc = 0;
+    for (int r = 0; r < CL; ++r) acc += *cl.map_shared_rank(&pacc[g * d + dim], r);
+    acc += (int64_t)a.v_cache[((size_t)kvh * a.cap + start + g_idx[g]) * d + dim] * g_res[g];
+    a.out[((size_t)kvh * G + g) * d + dim] = requantize(acc);
+  }
+  cl.sync();  // keep this CTA's shared memory alive until every rank has read it
+}
+
+static int g_attn_cluster = 0;  // cluster size chosen for this device
+
+template <int G>
+static cudaError_t launch_ac(const AttnDecodeArgs& a, int CL, cudaStream_t s) {
+  const int rmax = (a.cap + CL - 1) / CL + 1;
+  const size_t smem = (size_t)G * a.d * 4 + (size_t)G * rmax * 4 + 4 + (size_t)G * rmax * 8 + (size_t)G * a.d * 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CL, a.Hkv, 1);
+  cfg.blockDim = dim3(kAcThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attn_dec_cluster_kernel<G>, a, rmax);
+}
+
+template <int G>
+static void ac_prepare(int CL) {
+  cudaFuncSetAttribute(attn_dec_cluster_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (CL > 8) cudaFuncSetAttribute(attn_dec_cluster_kernel<G>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+}
+
+static void attn_cluster_init() {
+  if (g_attn_cluster) return;
+  int CL = 16;
+  ac_prepare<1>(CL);
+  ac_prepare<2>(CL);
+  ac_prepare<4>(CL);
+  ac_prepare<8>(CL);
+  // use 16-CTA clusters when the device can schedule them, else the portable 8
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(16, 1, 1);
+  cfg.blockDim = dim3(kAcThreads, 1, 1);
+  cfg.dynamicSmemBytes = 64 * 1024;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 16;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int nclusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&nclusters, attn_dec_cluster_kernel<4>, &cfg) != cudaSuccess || nclusters < 1) {
+    cudaGetLastError();
+    CL = 8;
+  }
+  g_attn_cluster = CL;
+}
+
+void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s) {
+  const int G = a.Hq / a.Hkv;
+  const int CL = g_attn_cluster ? g_attn_cluster : 8;
+  // launch errors surface through cudaGetLastError in the caller
+  switch (G) {
+    case 1: launch_ac<1>(a, CL, s); break;
+    case 2: launch_ac<2>(a, CL, s); break;
+    case 4: launch_ac<4>(a, CL, s); break;
+    case 8: launch_ac<8>(a, CL, s); break;
+    default: launch_attn_decode(a, s); break;
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -115,6 +115,10 @@ struct AttnDecodeArgs {
   int32_t rows_per_split = 64;
 };
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s);
+// Same computation in one kernel: one thread-block cluster per KV head splits
+// the window across its CTAs and combines the exact softmax statistics through
+// distributed shared memory (no global scratch; a.sc is not used).
+void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s);
 
 struct AttnPrefillArgs {
   int32_t S = 0;

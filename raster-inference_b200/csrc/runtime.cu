@@ -917,7 +917,7 @@ static const int32_t* decode_layer(Ctx& c, Seq& q, int l, const int32_t* cur) {
   aa.pos = q.d_pos; aa.Hq = m.Hq; aa.Hkv = lc.kv_heads; aa.d = d; aa.window = lc.window; aa.q = w.qo;
   aa.k_cache = kcache; aa.v_cache = vcache; aa.cap = q.cap; aa.out = w.comb; aa.sc = q.asc;
   aa.rows_per_split = 64;
-  launch_attn_decode(aa, s);
+  launch_attn_decode_cluster(aa, s);
   GemvArgs go;
   go.K = m.Hq * d;
   go.seg[0].w = L.o;
