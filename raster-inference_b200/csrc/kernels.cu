@@ -24,6 +24,34 @@ int sm_count() {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch: every kernel is launched with programmatic
+// stream serialization, waits for the grids it depends on to complete (and
+// their writes to be visible) before touching their outputs, and lets its own
+// dependents start launching right away, so launch latency overlaps the tail
+// of the previous kernel.  Launched without the attribute, both are no-ops.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_entry() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+static inline void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                            Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// ---------------------------------------------------------------------------
 // block reductions
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int64_t warp_sum64(int64_t v) {
@@ -160,6 +188,7 @@ __device__ __forceinline__ int64_t mat_row_dot(const DevMat& m, int r, const int
 constexpr int kGemvThreads = 256;
 
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
+  pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int32_t* xs = reinterpret_cast<int32_t*>(smem_raw);
   __shared__ uint64_t red[33];
@@ -317,6 +346,7 @@ __device__ int32_t consumer_norm_scale(const int32_t* xs, int n, int64_t eps, ui
 template <int WB>  // weight bytes: 2 (i16) or 4 (i32)
 __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) gemv_stream_kernel(const GemvArgs a,
                                                                                        const StreamCfg cfg) {
+  pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t full[kStreamMaxStages], empty[kStreamMaxStages];
   __shared__ uint64_t red[33];
@@ -544,8 +574,8 @@ int stream_error_flag(bool reset) {
   const size_t smem = (size_t)cfg.x_bytes + (size_t)cfg.ns * cfg.stage_bytes + (size_t)acc_bytes;
   if (smem > 220 * 1024 / kStreamCtasPerSm) return false;
   stream_set_attrs();
-  if (WB == 2) gemv_stream_kernel<2><<<G, kStreamThreads, smem, s>>>(a, cfg);
-  else gemv_stream_kernel<4><<<G, kStreamThreads, smem, s>>>(a, cfg);
+  if (WB == 2) launch_k(gemv_stream_kernel<2>, dim3(G), dim3(kStreamThreads), smem, s, a, cfg);
+  else launch_k(gemv_stream_kernel<4>, dim3(G), dim3(kStreamThreads), smem, s, a, cfg);
   return true;
 }
 
@@ -618,6 +648,7 @@ __device__ __forceinline__ void dot_rows2(const unsigned char* A, int ra, const 
 
 template <int WB>
 __global__ void __launch_bounds__(kGemvThreads, RDET_GEMV3_CTAS_PER_SM) gemv3_kernel(const GemvArgs a, int per_item) {
+  pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int32_t* xs = reinterpret_cast<int32_t*>(smem_raw);
   __shared__ uint64_t red[33];
@@ -708,8 +739,8 @@ static bool launch_gemv3(const GemvArgs& a, cudaStream_t s) {
     cudaFuncSetAttribute(gemv3_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(gemv3_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   }
-  if (WB == 2) gemv3_kernel<2><<<blocks, kGemvThreads, smem, s>>>(a, per_item);
-  else gemv3_kernel<4><<<blocks, kGemvThreads, smem, s>>>(a, per_item);
+  if (WB == 2) launch_k(gemv3_kernel<2>, dim3(blocks), dim3(kGemvThreads), smem, s, a, per_item);
+  else launch_k(gemv3_kernel<4>, dim3(blocks), dim3(kGemvThreads), smem, s, a, per_item);
   return true;
 }
 
@@ -729,7 +760,7 @@ void launch_gemv(const GemvArgs& a, cudaStream_t s) {
   if (blocks < 1) blocks = 1;
   size_t smem = (size_t)a.K * 4;
   if (smem > 48 * 1024) cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  gemv_kernel<<<blocks, kGemvThreads, smem, s>>>(a);
+  launch_k(gemv_kernel, dim3(blocks), dim3(kGemvThreads), smem, s, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -741,6 +772,7 @@ constexpr int LT_BM = 64, LT_BN = 64, LT_BK = 32;
 template <bool PAIR>
 __global__ void __launch_bounds__(256) linear_kernel(const int32_t* __restrict__ X, int S, DevMat w, DevMat wu,
                                                      int32_t* __restrict__ Y, int epi, const int32_t* __restrict__ vec) {
+  pdl_entry();
   __shared__ int32_t xs[LT_BK][LT_BM + 1];
   __shared__ int32_t ws[LT_BK][LT_BN + 1];
   __shared__ int32_t us[PAIR ? LT_BK : 1][PAIR ? LT_BN + 1 : 1];
@@ -801,18 +833,19 @@ __global__ void __launch_bounds__(256) linear_kernel(const int32_t* __restrict__
 void launch_linear(const int32_t* X, int32_t S, const DevMat& w, int32_t* Y, int32_t epi, const int32_t* vec,
                    cudaStream_t s) {
   dim3 grid((w.rows + LT_BN - 1) / LT_BN, (S + LT_BM - 1) / LT_BM);
-  linear_kernel<false><<<grid, 256, 0, s>>>(X, S, w, w, Y, epi, vec);
+  launch_k(linear_kernel<false>, dim3(grid), dim3(256), 0, s, X, S, w, w, Y, epi, vec);
 }
 void launch_linear_geglu(const int32_t* X, int32_t S, const DevMat& wg, const DevMat& wu, int32_t* Y,
                          cudaStream_t s) {
   dim3 grid((wg.rows + LT_BN - 1) / LT_BN, (S + LT_BM - 1) / LT_BM);
-  linear_kernel<true><<<grid, 256, 0, s>>>(X, S, wg, wu, Y, kEpiPlain, nullptr);
+  launch_k(linear_kernel<true>, dim3(grid), dim3(256), 0, s, X, S, wg, wu, Y, kEpiPlain, nullptr);
 }
 
 // ---------------------------------------------------------------------------
 // row norms
 // ---------------------------------------------------------------------------
 __global__ void rmsnorm_rows_kernel(const int32_t* x, int n, const int32_t* g, int64_t eps, int32_t* y) {
+  pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int32_t* xs = reinterpret_cast<int32_t*>(smem_raw);
   __shared__ uint64_t red[33];
@@ -830,11 +863,12 @@ void launch_rmsnorm_rows(const int32_t* x, int32_t S, int32_t n, const int32_t* 
                          cudaStream_t s) {
   size_t smem = (size_t)n * 4;
   if (smem > 48 * 1024) cudaFuncSetAttribute(rmsnorm_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  rmsnorm_rows_kernel<<<S, 256, smem, s>>>(x, n, g, eps, y);
+  launch_k(rmsnorm_rows_kernel, dim3(S), dim3(256), smem, s, x, n, g, eps, y);
 }
 
 __global__ void norm_residual_kernel(const int32_t* a, const int32_t* res, int n, const int32_t* g, int64_t eps,
                                      bool has_scalar, int32_t scalar, int32_t* out) {
+  pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int32_t* xs = reinterpret_cast<int32_t*>(smem_raw);
   __shared__ uint64_t red[33];
@@ -852,7 +886,7 @@ void launch_norm_residual_rows(const int32_t* a, const int32_t* res, int32_t S, 
                                int64_t eps, bool has_scalar, int32_t scalar, int32_t* out, cudaStream_t s) {
   size_t smem = (size_t)n * 4;
   if (smem > 48 * 1024) cudaFuncSetAttribute(norm_residual_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  norm_residual_kernel<<<S, 256, smem, s>>>(a, res, n, g, eps, has_scalar, scalar, out);
+  launch_k(norm_residual_kernel, dim3(S), dim3(256), smem, s, a, res, n, g, eps, has_scalar, scalar, out);
 }
 
 // ---------------------------------------------------------------------------
@@ -871,6 +905,7 @@ __device__ void rope_inplace(int32_t* v, int rotary, const int64_t* inv_freq, ui
 }
 
 __global__ void qkv_post_kernel(const QkvPostArgs a) {
+  pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int32_t* vs = reinterpret_cast<int32_t*>(smem_raw);
   __shared__ uint64_t red[33];
@@ -913,7 +948,7 @@ __global__ void qkv_post_kernel(const QkvPostArgs a) {
 }
 void launch_qkv_post(const QkvPostArgs& a, cudaStream_t s) {
   dim3 grid(a.S, a.Hq + (a.k_in ? a.Hkv : 0));
-  qkv_post_kernel<<<grid, 128, (size_t)a.d * 4, s>>>(a);
+  launch_k(qkv_post_kernel, dim3(grid), dim3(128), (size_t)a.d * 4, s, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -929,6 +964,7 @@ __device__ __forceinline__ void decode_window(const AttnDecodeArgs& a, int* star
 
 // phase 1: scores for the G query heads of one KV head over one split.
 __global__ void attn_dec_scores(const AttnDecodeArgs a) {
+  pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int32_t* qs = reinterpret_cast<int32_t*>(smem_raw);  // [G, d]
   __shared__ int32_t wmax[8][8];
@@ -989,6 +1025,7 @@ __device__ __forceinline__ void global_max(const AttnDecodeArgs& a, int h, int n
 
 // phase 2: exp terms and partial sums
 __global__ void attn_dec_exp(const AttnDecodeArgs a) {
+  pdl_entry();
   __shared__ int32_t gmax[8];
   __shared__ uint64_t red[8][8];
   const int kvh = blockIdx.x, split = blockIdx.y;
@@ -1025,6 +1062,7 @@ __global__ void attn_dec_exp(const AttnDecodeArgs a) {
 
 // phase 3: weights and partial weighted sums over V
 __global__ void attn_dec_wsum(const AttnDecodeArgs a) {
+  pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int32_t* ws = reinterpret_cast<int32_t*>(smem_raw);  // [G, rows_per_split]
   __shared__ int64_t tsum[8];
@@ -1074,6 +1112,7 @@ __global__ void attn_dec_wsum(const AttnDecodeArgs a) {
 
 // phase 4: combine splits, residual to the first max, requantize.
 __global__ void attn_dec_final(const AttnDecodeArgs a) {
+  pdl_entry();
   const int h = blockIdx.x, d = a.d, G = a.Hq / a.Hkv, kvh = h / G;
   int start, n;
   decode_window(a, &start, &n);
@@ -1100,10 +1139,10 @@ __global__ void attn_dec_final(const AttnDecodeArgs a) {
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
   const int G = a.Hq / a.Hkv;
   dim3 grid(a.Hkv, a.sc.max_splits);
-  attn_dec_scores<<<grid, 256, (size_t)G * a.d * 4, s>>>(a);
-  attn_dec_exp<<<grid, 256, 0, s>>>(a);
-  attn_dec_wsum<<<grid, 256, (size_t)G * a.rows_per_split * 4, s>>>(a);
-  attn_dec_final<<<a.Hq, 256, 0, s>>>(a);
+  launch_k(attn_dec_scores, dim3(grid), dim3(256), (size_t)G * a.d * 4, s, a);
+  launch_k(attn_dec_exp, dim3(grid), dim3(256), 0, s, a);
+  launch_k(attn_dec_wsum, dim3(grid), dim3(256), (size_t)G * a.rows_per_split * 4, s, a);
+  launch_k(attn_dec_final, dim3(a.Hq), dim3(256), 0, s, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -1116,6 +1155,7 @@ constexpr int kAcThreads = 512;
 
 template <int G>
 __global__ void __launch_bounds__(kAcThreads) attn_dec_cluster_kernel(const AttnDecodeArgs a, int rmax) {
+  pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   cg::cluster_group cl = cg::this_cluster();
   const int CL = (int)cl.num_blocks(), rank = (int)cl.block_rank();
@@ -1282,13 +1322,15 @@ static cudaError_t launch_ac(const AttnDecodeArgs& a, int CL, cudaStream_t s) {
   cfg.blockDim = dim3(kAcThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = CL;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, attn_dec_cluster_kernel<G>, a, rmax);
 }
 
@@ -1343,6 +1385,7 @@ void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s) {
 // (head, query).  Scores live in global scratch rows of length `rowlen`.
 // ---------------------------------------------------------------------------
 __global__ void attn_prefill_kernel(const AttnPrefillArgs a, int rowlen) {
+  pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int32_t* qs = reinterpret_cast<int32_t*>(smem_raw);
   __shared__ int32_t wm[32], wi[32];
@@ -1429,6 +1472,7 @@ __global__ void attn_prefill_kernel(const AttnPrefillArgs a, int rowlen) {
 constexpr int AP_R = 64, AP_TK = 32, AP_CH = 128;
 
 __global__ void __launch_bounds__(256) attn_prefill_tiled(const AttnPrefillArgs a, int rowlen, int QB) {
+  pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int d = a.d, dp = d + 4, G = a.Hq / a.Hkv, R = QB * G;
   int32_t* Qs = reinterpret_cast<int32_t*>(smem_raw);   // [AP_R][dp]
@@ -1600,17 +1644,18 @@ void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t s) {
       configured = 220 * 1024;
     }
     dim3 grid(a.Hkv, (a.S + QB - 1) / QB);
-    attn_prefill_tiled<<<grid, 256, smem, s>>>(a, rowlen, QB);
+    launch_k(attn_prefill_tiled, dim3(grid), dim3(256), smem, s, a, rowlen, QB);
     return;
   }
   dim3 grid(a.Hq, a.S);
-  attn_prefill_kernel<<<grid, 256, (size_t)a.d * 4, s>>>(a, rowlen);
+  launch_k(attn_prefill_kernel, dim3(grid), dim3(256), (size_t)a.d * 4, s, a, rowlen);
 }
 
 // ---------------------------------------------------------------------------
 // embedding gather (io.rs:2446-2518), PLE inputs (prefill_prepare_aux)
 // ---------------------------------------------------------------------------
 __global__ void embed_kernel(const uint32_t* ids, DevMat emb, int32_t scale, int32_t* out, int32_t* err) {
+  pdl_entry();
   const int s = blockIdx.x, H = emb.cols;
   uint32_t id = ids[s];
   if (id >= (uint32_t)emb.rows) {
@@ -1625,10 +1670,11 @@ __global__ void embed_kernel(const uint32_t* ids, DevMat emb, int32_t scale, int
 }
 void launch_embed(const uint32_t* ids, int32_t S, const DevMat& emb, int32_t scale, int32_t* out, int32_t* err,
                   cudaStream_t s) {
-  embed_kernel<<<S, 256, 0, s>>>(ids, emb, scale, out, err);
+  launch_k(embed_kernel, dim3(S), dim3(256), 0, s, ids, emb, scale, out, err);
 }
 
 __global__ void ple_kernel(const PleArgs a) {
+  pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int32_t* vs = reinterpret_cast<int32_t*>(smem_raw);
   __shared__ uint64_t red[33];
@@ -1653,7 +1699,7 @@ __global__ void ple_kernel(const PleArgs a) {
 }
 void launch_ple(const PleArgs& a, cudaStream_t s) {
   dim3 grid(a.S, a.L);
-  ple_kernel<<<grid, 128, (size_t)a.P * 4, s>>>(a);
+  launch_k(ple_kernel, dim3(grid), dim3(128), (size_t)a.P * 4, s, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -1663,6 +1709,7 @@ __device__ __forceinline__ void better(int32_t& v, int32_t& i, int32_t v2, int32
   if (v2 > v || (v2 == v && i2 < i)) { v = v2; i = i2; }
 }
 __global__ void argmax_part_kernel(const int32_t* x, int n, int32_t* part) {
+  pdl_entry();
   __shared__ int32_t sv[32], si[32];
   int32_t bv = INT32_MIN, bi = INT32_MAX;
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) better(bv, bi, x[j], j);
@@ -1679,26 +1726,29 @@ __global__ void argmax_part_kernel(const int32_t* x, int n, int32_t* part) {
   }
 }
 __global__ void argmax_final_kernel(const int32_t* part, int blocks, uint32_t* idx) {
+  pdl_entry();
   int32_t bv = INT32_MIN, bi = INT32_MAX;
   for (int b = 0; b < blocks; ++b) better(bv, bi, part[2 * b], part[2 * b + 1]);
   *idx = (uint32_t)bi;
 }
 void launch_argmax(const int32_t* x, int32_t n, int32_t* part, int32_t blocks, uint32_t* idx, cudaStream_t s) {
-  argmax_part_kernel<<<blocks, 256, 0, s>>>(x, n, part);
-  argmax_final_kernel<<<1, 1, 0, s>>>(part, blocks, idx);
+  launch_k(argmax_part_kernel, dim3(blocks), dim3(256), 0, s, x, n, part);
+  launch_k(argmax_final_kernel, dim3(1), dim3(1), 0, s, part, blocks, idx);
 }
 __global__ void softcap_kernel(int32_t* x, int n, int32_t cap) {
+  pdl_entry();
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) x[j] = softcap_act(x[j], cap);
 }
 void launch_softcap(int32_t* x, int32_t n, int32_t cap, cudaStream_t s) {
-  softcap_kernel<<<(n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024, 256, 0, s>>>(x, n, cap);
+  launch_k(softcap_kernel, dim3((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024), dim3(256), 0, s, x, n, cap);
 }
 
 // ---------------------------------------------------------------------------
 // misc
 // ---------------------------------------------------------------------------
-__global__ void add_i32_kernel(int32_t* p, int32_t v) { *p += v; }
-void launch_add_i32(int32_t* p, int32_t v, cudaStream_t s) { add_i32_kernel<<<1, 1, 0, s>>>(p, v); }
+__global__ void add_i32_kernel(int32_t* p, int32_t v) {
+  pdl_entry(); *p += v; }
+void launch_add_i32(int32_t* p, int32_t v, cudaStream_t s) { launch_k(add_i32_kernel, dim3(1), dim3(1), 0, s, p, v); }
 void launch_copy_rows(const int32_t* src, int32_t* dst, size_t n, cudaStream_t s) {
   cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToDevice, s);
 }
@@ -1709,6 +1759,7 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
   return z ^ (z >> 31);
 }
 __global__ void synth_kernel(void* dst, int width, int rank, int64_t n, int64_t cols, uint64_t key) {
+  pdl_entry();
   const uint64_t GOLD = 0x9E3779B97F4A7C15ull;
   int64_t bound = cols > 0 ? (int64_t)(0x7fffffffLL / cols) : 0;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -1725,7 +1776,7 @@ void launch_synth(void* dst, int32_t width, int32_t rank, int64_t n, int64_t col
   int64_t blocks = (n + 255) / 256;
   if (blocks > 65536) blocks = 65536;
   if (blocks < 1) blocks = 1;
-  synth_kernel<<<(unsigned)blocks, 256, 0, s>>>(dst, width, rank, n, cols, key);
+  launch_k(synth_kernel, dim3((unsigned)blocks), dim3(256), 0, s, dst, width, rank, n, cols, key);
 }
 
 }  // namespace rdet
