@@ -616,43 +616,93 @@ __device__ __forceinline__ void dot_chunk(const uint4& w, const int32_t* xs, int
   }
 }
 
-// dots of rows ra (matrix A) and rb (matrix B, may be absent) with xs
+// Row-pair pieces: a piece is the next kG3Nch 16-byte chunks per lane of two
+// rows.  Loads of a piece are issued together, then consumed.
 template <int WB>
-__device__ __forceinline__ void dot_rows2(const unsigned char* A, int ra, const unsigned char* B, int rb, bool has_b,
-                                          const int32_t* xs, int K, int lane, int64_t& outa, int64_t& outb) {
-  const int nc = K * WB / 16;
-  const uint4* pa = reinterpret_cast<const uint4*>(A + (size_t)ra * K * WB);
-  const uint4* pb = reinterpret_cast<const uint4*>(has_b ? B + (size_t)rb * K * WB : A);
-  constexpr int kG3Nch = WB == 2 ? RDET_GEMV3_NCH : RDET_GEMV3_NCH_W32;
-  int64_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
-  for (int c0 = lane; c0 < nc; c0 += 32 * kG3Nch) {
-    uint4 wa[kG3Nch], wb[kG3Nch];
+struct G3Piece {
+  static constexpr int N = WB == 2 ? RDET_GEMV3_NCH : RDET_GEMV3_NCH_W32;
+  uint4 wa[N], wb[N];
+};
+template <int WB>
+__device__ __forceinline__ void g3_load(G3Piece<WB>& p, const uint4* pa, const uint4* pb, bool has_b, int c0, int nc) {
 #pragma unroll
-    for (int u = 0; u < kG3Nch; ++u) {
-      int c = c0 + 32 * u;
-      wa[u] = c < nc ? ldg_stream(pa + c) : make_uint4(0, 0, 0, 0);
-      wb[u] = (has_b && c < nc) ? ldg_stream(pb + c) : make_uint4(0, 0, 0, 0);
-    }
+  for (int u = 0; u < G3Piece<WB>::N; ++u) {
+    int c = c0 + 32 * u;
+    p.wa[u] = c < nc ? ldg_stream(pa + c) : make_uint4(0, 0, 0, 0);
+    p.wb[u] = (has_b && c < nc) ? ldg_stream(pb + c) : make_uint4(0, 0, 0, 0);
+  }
+}
+template <int WB>
+__device__ __forceinline__ void g3_consume(const G3Piece<WB>& p, const int32_t* xs, bool has_b, int c0, int nc,
+                                           int64_t& a0, int64_t& a1, int64_t& b0, int64_t& b1) {
 #pragma unroll
-    for (int u = 0; u < kG3Nch; ++u) {
-      int c = c0 + 32 * u;
-      if (c < nc) {
-        dot_chunk<WB>(wa[u], xs, c, a0, a1);
-        if (has_b) dot_chunk<WB>(wb[u], xs, c, b0, b1);
-      }
+  for (int u = 0; u < G3Piece<WB>::N; ++u) {
+    int c = c0 + 32 * u;
+    if (c < nc) {
+      dot_chunk<WB>(p.wa[u], xs, c, a0, a1);
+      if (has_b) dot_chunk<WB>(p.wb[u], xs, c, b0, b1);
     }
   }
-  outa = warp_sum64(a0 + a1);
-  outb = warp_sum64(b0 + b1);
+}
+
+// Work item `gp` -> (matrix A row ra, matrix B row rb, has_b, segment)
+struct G3Item {
+  const unsigned char* A;
+  const unsigned char* B;
+  int ra, rb, seg;
+  bool has_b;
+};
+__device__ __forceinline__ G3Item g3_item(const GemvArgs& a, int gp, int per_item) {
+  G3Item it;
+  if (a.pair_geglu) {
+    it.A = static_cast<const unsigned char*>(a.seg[0].w.p);
+    it.B = static_cast<const unsigned char*>(a.seg[1].w.p);
+    it.ra = it.rb = gp;
+    it.seg = 0;
+    it.has_b = true;
+    return it;
+  }
+  int sgi = 0, p = gp;
+  for (;;) {
+    int pr = (a.seg[sgi].w.rows + per_item - 1) / per_item;
+    if (p < pr) break;
+    p -= pr;
+    ++sgi;
+  }
+  it.A = it.B = static_cast<const unsigned char*>(a.seg[sgi].w.p);
+  it.ra = per_item * p;
+  it.rb = it.ra + 1;
+  it.has_b = per_item == 2 && it.rb < a.seg[sgi].w.rows;
+  it.seg = sgi;
+  return it;
 }
 
 template <int WB>
 __global__ void __launch_bounds__(kGemvThreads, RDET_GEMV3_CTAS_PER_SM) gemv3_kernel(const GemvArgs a, int per_item) {
-  pdl_entry();
+  // Weights never depend on earlier kernels: the first piece of this warp's
+  // first item is requested before waiting on the preceding grid.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int32_t* xs = reinterpret_cast<int32_t*>(smem_raw);
   __shared__ uint64_t red[33];
   const int K = a.K;
+  const int nc = K * WB / 16;
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  int total = 0;
+  if (a.pair_geglu) total = a.seg[0].w.rows;
+  else for (int j = 0; j < a.nseg; ++j) total += (a.seg[j].w.rows + per_item - 1) / per_item;
+  G3Piece<WB> pc;
+  G3Item it;
+  const uint4 *pa = nullptr, *pb = nullptr;
+  if (gw < total) {
+    it = g3_item(a, gw, per_item);
+    pa = reinterpret_cast<const uint4*>(it.A + (size_t)it.ra * K * WB);
+    pb = reinterpret_cast<const uint4*>(it.B + (size_t)(it.has_b ? it.rb : it.ra) * K * WB);
+    g3_load<WB>(pc, pa, pb, it.has_b, lane, nc);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = a.a[i];
   __syncthreads();
   if (a.pro != kProNone) {
@@ -674,38 +724,29 @@ __global__ void __launch_bounds__(kGemvThreads, RDET_GEMV3_CTAS_PER_SM) gemv3_ke
     }
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int nw = gridDim.x * (blockDim.x >> 5);
-  if (a.pair_geglu) {
-    const int R = a.seg[0].w.rows;
-    const unsigned char* G = static_cast<const unsigned char*>(a.seg[0].w.p);
-    const unsigned char* U = static_cast<const unsigned char*>(a.seg[1].w.p);
-    for (int r = gw; r < R; r += nw) {
-      int64_t g, u;
-      dot_rows2<WB>(G, r, U, r, true, xs, K, lane, g, u);
-      if (lane == 0) a.seg[0].y[r] = mul_sat(gelu_act(requantize(g)), requantize(u));
-    }
-    return;
-  }
-  // work items: `per_item` (1 or 2) consecutive rows within one segment
-  int pairs[3], total = 0;
-  for (int sgi = 0; sgi < a.nseg; ++sgi) {
-    pairs[sgi] = (a.seg[sgi].w.rows + per_item - 1) / per_item;
-    total += pairs[sgi];
-  }
+  bool first = true;
   for (int gp = gw; gp < total; gp += nw) {
-    int sgi = 0, p = gp;
-    while (p >= pairs[sgi]) { p -= pairs[sgi]; ++sgi; }
-    const GemvSeg& sg = a.seg[sgi];
-    const unsigned char* Wm = static_cast<const unsigned char*>(sg.w.p);
-    const int r0 = per_item * p, r1 = r0 + 1;
-    const bool two = per_item == 2 && r1 < sg.w.rows;
-    int64_t d0, d1;
-    dot_rows2<WB>(Wm, r0, Wm, r1, two, xs, K, lane, d0, d1);
-    if (lane < 2 && (lane == 0 || two)) {
-      const int r = lane == 0 ? r0 : r1;
-      int32_t v = requantize(lane == 0 ? d0 : d1);
+    if (!first) {
+      it = g3_item(a, gp, per_item);
+      pa = reinterpret_cast<const uint4*>(it.A + (size_t)it.ra * K * WB);
+      pb = reinterpret_cast<const uint4*>(it.B + (size_t)(it.has_b ? it.rb : it.ra) * K * WB);
+    }
+    int64_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+    for (int c0 = lane; c0 < nc; c0 += 32 * G3Piece<WB>::N) {
+      if (!first) g3_load<WB>(pc, pa, pb, it.has_b, c0, nc);
+      first = false;
+      g3_consume<WB>(pc, xs, it.has_b, c0, nc, a0, a1, b0, b1);
+    }
+    first = false;
+    const int64_t da = warp_sum64(a0 + a1), db = warp_sum64(b0 + b1);
+    if (a.pair_geglu) {
+      if (lane == 0) a.seg[0].y[it.ra] = mul_sat(gelu_act(requantize(da)), requantize(db));
+      continue;
+    }
+    const GemvSeg& sg = a.seg[it.seg];
+    if (lane < 2 && (lane == 0 || it.has_b)) {
+      const int r = lane == 0 ? it.ra : it.rb;
+      int32_t v = requantize(lane == 0 ? da : db);
       if (sg.epi == kEpiSoftcap) v = softcap_act(v, a.softcap);
       else if (sg.epi == kEpiGeluMul) v = mul_sat(gelu_act(v), sg.vec[r]);
       sg.y[r] = v;
@@ -1153,6 +1194,12 @@ void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
 namespace cg = cooperative_groups;
 constexpr int kAcThreads = 512;
 
+// The k/v row scratch of the fused prologue lives in the partial-sum buffer
+// (G*d i64 >= 2*d i32), which phase 3 overwrites only after the row is stored.
+__device__ __forceinline__ int32_t* pacc_ptr_guard(int64_t* ex, int G, int rmax, int d) {
+  return reinterpret_cast<int32_t*>(ex + G * rmax);
+}
+
 template <int G>
 __global__ void __launch_bounds__(kAcThreads) attn_dec_cluster_kernel(const AttnDecodeArgs a, int rmax) {
   pdl_entry();
@@ -1175,8 +1222,71 @@ __global__ void __launch_bounds__(kAcThreads) attn_dec_cluster_kernel(const Attn
   const int lo = (int)((int64_t)n * rank / CL), hi = (int)((int64_t)n * (rank + 1) / CL);
   const int rows = hi - lo;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = kAcThreads / 32;
-  for (int i = threadIdx.x; i < G * d; i += kAcThreads) qs[i] = a.q[(size_t)kvh * G * d + i];
-  __syncthreads();
+  const AttnFuse& f = a.fuse;
+  if (!f.q_in) {
+    for (int i = threadIdx.x; i < G * d; i += kAcThreads) qs[i] = a.q[(size_t)kvh * G * d + i];
+    __syncthreads();
+  } else {
+    // fused qkv_post: q heads of this KV head (every rank), and on rank 0 the
+    // new K/V row of the cache.  kv[0] = normed+rotated k, kv[1] = normed v.
+    __shared__ int32_t sc_q[G], sc_kv[2];
+    __shared__ int32_t cs_tab[256], sn_tab[256];
+    int32_t* kvrow = pacc_ptr_guard(ex, G, rmax, d);  // scratch for the k/v row (reuses pacc space)
+    const uint32_t pos = (uint32_t)(a.pos ? *a.pos : a.pos_value);
+    const bool own = f.k_in != nullptr && rank == 0;
+    for (int i = threadIdx.x; i < G * d; i += kAcThreads) qs[i] = f.q_in[(size_t)kvh * G * d + i];
+    if (own)
+      for (int i = threadIdx.x; i < d; i += kAcThreads) {
+        kvrow[i] = f.k_in[(size_t)kvh * d + i];
+        kvrow[d + i] = f.v_in[(size_t)kvh * d + i];
+      }
+    const int half = f.rotary >> 1;
+    for (int i = threadIdx.x; i < half; i += kAcThreads) {
+      int32_t cv, sv;
+      sin_cos_acc(pos_angle(pos, f.inv_freq[i]), &cv, &sv);
+      cs_tab[i] = cv;
+      sn_tab[i] = sv;
+    }
+    __syncthreads();
+    if (warp < G) {
+      int32_t scv = warp_norm_scale(qs + warp * d, d, f.eps);
+      if (lane == 0) sc_q[warp] = scv;
+    } else if (own && warp == G) {
+      int32_t scv = warp_norm_scale(kvrow, d, f.eps);
+      if (lane == 0) sc_kv[0] = scv;
+    } else if (own && warp == G + 1) {
+      int32_t scv = warp_norm_scale(kvrow + d, d, f.eps);
+      if (lane == 0) sc_kv[1] = scv;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * d; i += kAcThreads) {
+      int g = i / d, t = i - g * d;
+      qs[i] = mul_sat(mul_sat(qs[i], sc_q[g]), f.q_norm[t]);
+    }
+    if (own)
+      for (int i = threadIdx.x; i < d; i += kAcThreads) {
+        kvrow[i] = mul_sat(mul_sat(kvrow[i], sc_kv[0]), f.k_norm[i]);
+        kvrow[d + i] = mul_sat(kvrow[d + i], sc_kv[1]);
+      }
+    __syncthreads();
+    if (pos != 0 && half > 0) {  // rope_rotate_pairs_in_place leaves position 0 unchanged
+      for (int e = threadIdx.x; e < (G + (own ? 1 : 0)) * half; e += kAcThreads) {
+        int h = e / half, i = e - h * half;
+        int32_t* v = h < G ? qs + h * d : kvrow;
+        int32_t l = v[i], r = v[i + half];
+        v[i] = sub_sat(mul_sat(l, cs_tab[i]), mul_sat(r, sn_tab[i]));
+        v[i + half] = add_sat(mul_sat(r, cs_tab[i]), mul_sat(l, sn_tab[i]));
+      }
+      __syncthreads();
+    }
+    if (own) {
+      for (int i = threadIdx.x; i < d; i += kAcThreads) {
+        f.k_out[((size_t)kvh * a.cap + pos) * d + i] = kvrow[i];
+        f.v_out[((size_t)kvh * a.cap + pos) * d + i] = kvrow[d + i];
+      }
+    }
+    cl.sync();  // the appended row is visible to every rank before scoring
+  }
   // ---- phase 1: scores (warp per row; 16-byte loads when d % 128 == 0)
   int32_t bm[G], bi[G];
 #pragma unroll

@@ -101,6 +101,21 @@ struct AttnScratch {
   int32_t max_splits = 0;
   int32_t stride = 0;         // row stride of scores / exps (>= attended rows)
 };
+// Optional prologue of the cluster decode attention: q/k head RMSNorm, RoPE,
+// value RMSNorm and the KV-cache append of the current token (the work of
+// qkv_post), done inside the attention kernel.
+struct AttnFuse {
+  const int32_t* q_in = nullptr;   // raw q [Hq*d]; nullptr: a.q is already normed/rotated
+  const int32_t* k_in = nullptr;   // raw k [Hkv*d]; nullptr: no own cache (KV-sharing layer)
+  const int32_t* v_in = nullptr;   // raw v [Hkv*d] (== k_in for k_eq_v)
+  const int32_t* q_norm = nullptr;
+  const int32_t* k_norm = nullptr;
+  int64_t eps = 0;
+  int32_t rotary = 0;
+  const int64_t* inv_freq = nullptr;
+  int32_t* k_out = nullptr;        // own cache [Hkv, cap, d] written at row pos
+  int32_t* v_out = nullptr;
+};
 struct AttnDecodeArgs {
   const int32_t* pos = nullptr;  // device: position of the current token
   int32_t pos_value = 0;         // used when pos == nullptr
@@ -113,6 +128,7 @@ struct AttnDecodeArgs {
   int32_t* out = nullptr;        // [Hq, d]
   AttnScratch sc;
   int32_t rows_per_split = 64;
+  AttnFuse fuse;                 // used by the cluster kernel only
 };
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s);
 // Same computation in one kernel: one thread-block cluster per KV head splits

@@ -876,7 +876,39 @@ static void decode_embed(Ctx& c, Seq& q, const uint32_t* d_token) {
   }
 }
 
-static const int32_t* decode_layer(Ctx& c, Seq& q, int l, const int32_t* cur) {
+// The tail of a decode layer (final RMSNorm + residual + layer scalar) left
+// for the next kernel's prologue when the decode step is fused.
+struct PendingTail {
+  bool set = false;
+  const int32_t* a = nullptr;    // branch output to normalize
+  const int32_t* res = nullptr;  // residual input
+  const int32_t* g = nullptr;    // norm gain
+  bool has_scalar = false;
+  int32_t scalar = 0;
+  int32_t* out = nullptr;        // where the layer output row is stored
+};
+
+// Fills the prologue of a GEMV over the layer input: plain RMSNorm of `cur`,
+// or (fused step) the previous layer's pending tail followed by the norm.
+static void input_prologue(Ctx& c, GemvArgs& g, const int32_t* cur, const int32_t* gain, const PendingTail* pend) {
+  g.eps = c.eps;
+  if (pend && pend->set) {
+    g.pro = kProResScaleNorm;
+    g.a = pend->a;
+    g.res = pend->res;
+    g.g1 = pend->g;
+    g.has_scalar = pend->has_scalar;
+    g.scalar = pend->scalar;
+    g.g2 = gain;
+    g.t_out = pend->out;
+  } else {
+    g.pro = kProNorm;
+    g.a = cur;
+    g.g1 = gain;
+  }
+}
+
+static const int32_t* decode_layer(Ctx& c, Seq& q, int l, const int32_t* cur, PendingTail* pend = nullptr) {
   const ModelCfg& m = c.cfg;
   const LayerDev& L = c.layers[l];
   const LayerCfg& lc = L.cfg;
@@ -886,10 +918,7 @@ static const int32_t* decode_layer(Ctx& c, Seq& q, int l, const int32_t* cur) {
   // q/k/v projections of rmsnorm(x)
   GemvArgs g;
   g.K = H;
-  g.pro = kProNorm;
-  g.a = cur;
-  g.g1 = L.in_ln;
-  g.eps = c.eps;
+  input_prologue(c, g, cur, L.in_ln, pend);
   g.nseg = 1;
   g.seg[0].w = L.q;
   g.seg[0].y = w.q;
@@ -912,11 +941,27 @@ static const int32_t* decode_layer(Ctx& c, Seq& q, int l, const int32_t* cur) {
     vcache = q.vc[lc.donor];
   }
   launch_gemv(g, s);
-  launch_qkv_post(qa, s);
   AttnDecodeArgs aa;
   aa.pos = q.d_pos; aa.Hq = m.Hq; aa.Hkv = lc.kv_heads; aa.d = d; aa.window = lc.window; aa.q = w.qo;
   aa.k_cache = kcache; aa.v_cache = vcache; aa.cap = q.cap; aa.out = w.comb; aa.sc = q.asc;
   aa.rows_per_split = 64;
+  // The fused step normalizes, rotates and appends inside the attention
+  // kernel; the routine-granular path keeps the separate qkv_post kernel.
+  const bool fuse_qkv = pend != nullptr && lc.rotary <= 512;
+  if (fuse_qkv) {
+    aa.fuse.q_in = w.q;
+    aa.fuse.k_in = qa.k_in;
+    aa.fuse.v_in = qa.v_in;
+    aa.fuse.q_norm = L.q_norm;
+    aa.fuse.k_norm = L.k_norm;
+    aa.fuse.eps = c.eps;
+    aa.fuse.rotary = lc.rotary;
+    aa.fuse.inv_freq = L.inv_freq;
+    aa.fuse.k_out = qa.k_cache;
+    aa.fuse.v_out = qa.v_cache;
+  } else {
+    launch_qkv_post(qa, s);
+  }
   launch_attn_decode_cluster(aa, s);
   GemvArgs go;
   go.K = m.Hq * d;
@@ -955,24 +1000,49 @@ static const int32_t* decode_layer(Ctx& c, Seq& q, int l, const int32_t* cur) {
     gq.seg[0].w = L.ple_proj; gq.seg[0].y = w.pr;
     gq.a = w.g;
     launch_gemv(gq, s);
-    launch_norm_residual_rows(w.pr, w.t2, 1, H, L.ple_norm, c.eps, L.has_scalar, L.scalar, out, s);
+  }
+  const int32_t* ta = m.P > 0 ? w.pr : w.attn;
+  const int32_t* tres = m.P > 0 ? w.t2 : w.t1;
+  const int32_t* tg = m.P > 0 ? L.ple_norm : L.post_ff_ln;
+  if (pend) {
+    pend->set = true;
+    pend->a = ta;
+    pend->res = tres;
+    pend->g = tg;
+    pend->has_scalar = L.has_scalar;
+    pend->scalar = L.scalar;
+    pend->out = out;
   } else {
-    launch_norm_residual_rows(w.attn, w.t1, 1, H, L.post_ff_ln, c.eps, L.has_scalar, L.scalar, out, s);
+    launch_norm_residual_rows(ta, tres, 1, H, tg, c.eps, L.has_scalar, L.scalar, out, s);
   }
   return out;
 }
 
-static void decode_finalize_launch(Ctx& c, Seq& q, const int32_t* cur) {
-  gemv_logits(c, cur, q.logits, c.stream);
+static void decode_finalize_launch(Ctx& c, Seq& q, const int32_t* cur, const PendingTail* pend = nullptr) {
+  if (pend && pend->set) {
+    GemvArgs g;
+    g.K = c.cfg.H;
+    g.nseg = 1;
+    g.seg[0].w = c.lm_head;
+    g.seg[0].y = q.logits;
+    g.seg[0].epi = c.cfg.has_softcap ? kEpiSoftcap : kEpiPlain;
+    g.softcap = c.softcap;
+    input_prologue(c, g, cur, c.final_norm, pend);
+    launch_gemv(g, c.stream);
+  } else {
+    gemv_logits(c, cur, q.logits, c.stream);
+  }
   launch_add_i32(q.d_pos, 1, c.stream);
 }
 
-// full decode step for the token already in q.d_token (graph-capturable)
+// Full decode step for the token already in q.d_token (graph-capturable).
+// Each layer's final norm + residual runs as the prologue of the next GEMV.
 static void decode_step_launch(Ctx& c, Seq& q) {
   decode_embed(c, q, q.d_token);
   const int32_t* cur = c.dw.x0;
-  for (int l = 0; l < c.cfg.L; ++l) cur = decode_layer(c, q, l, cur);
-  decode_finalize_launch(c, q, cur);
+  PendingTail pend;
+  for (int l = 0; l < c.cfg.L; ++l) cur = decode_layer(c, q, l, cur, &pend);
+  decode_finalize_launch(c, q, cur, &pend);
 }
 
 static void select_launch(Ctx& c, Seq& q) {
