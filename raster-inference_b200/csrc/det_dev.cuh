@@ -15,6 +15,7 @@
 //  * the softmax division div_acc(e, sum) (e <= 2^32 <= sum) is computed from
 //    a double estimate corrected with an exact 128-bit remainder.
 #pragma once
+#include <cmath>
 #include <cstdint>
 
 #ifndef RDET_HD
@@ -112,16 +113,19 @@ RDET_HD bool isq_le(uint32_t c, uint64_t x) {
 RDET_HD unsigned __int128 isq_prod(uint32_t c, uint64_t x) {
   return (unsigned __int128)((uint64_t)c * c) * x;
 }
+// The reference bisects on r; isq_le(r, x) is monotone in r, so the same r is
+// found by starting from the double estimate 2^32/sqrt(x) (relative error
+// below 2^-50, i.e. off by at most one for r < 2^31) and stepping with the
+// exact predicate until it flips.
 RDET_HD int32_t inv_sqrt_acc(int64_t xs) {
   if (xs <= 0) return INT32_MAX;  // x == 0 (negative inputs cannot occur)
   uint64_t x = (uint64_t)xs;
   const uint32_t maxb = 0x7fffffffu;
   if (isq_le(maxb, x)) return INT32_MAX;
-  uint32_t lo = 0, hi = maxb;
-  while (lo < hi) {
-    uint32_t mid = lo + ((hi - lo + 1) >> 1);
-    if (isq_le(mid, x)) lo = mid; else hi = mid - 1;
-  }
+  const double est = 4294967296.0 / sqrt((double)x);
+  uint32_t lo = est >= (double)(maxb - 1) ? maxb - 1 : (uint32_t)est;
+  while (lo > 0 && !isq_le(lo, x)) --lo;
+  while (lo + 1 < maxb && isq_le(lo + 1, x)) ++lo;
   uint32_t up = lo + 1 > maxb ? maxb : lo + 1;
   const unsigned __int128 target = (unsigned __int128)1 << 64;
   unsigned __int128 le = target - isq_prod(lo, x);

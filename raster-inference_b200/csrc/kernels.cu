@@ -4,6 +4,8 @@
 // split across lanes/warps/CTAs freely because wrapping i64 addition is
 // associative (reference docs/plans/DET_NUM_SPEC.md, "Parallelism legality").
 #include <cstdio>
+#include <mutex>
+#include <vector>
 
 #include <cooperative_groups.h>
 
@@ -111,6 +113,24 @@ __device__ int32_t warp_norm_scale(const int32_t* xs, int n, int64_t eps) {
 __device__ __forceinline__ int32_t lo16(uint32_t w) { return (int32_t)(int16_t)(w & 0xffffu); }
 __device__ __forceinline__ int32_t hi16(uint32_t w) { return ((int32_t)w) >> 16; }
 
+// Weight streams are read once per token: with an L2 evict-first policy they
+// do not push out what is reused within the step (activations, KV rows,
+// norm gains, kernel code).
+#ifndef RDET_WEIGHTS_EVICT_FIRST
+#define RDET_WEIGHTS_EVICT_FIRST 0
+#endif
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint4 ldg_stream_pol(const uint4* p, uint64_t pol) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p), "l"(pol));
+  return r;
+}
 __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
   uint4 r;
   asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -276,9 +296,10 @@ __device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// bounded wait on an mbarrier phase
+// bounded wait on an mbarrier phase (each try_wait may suspend the thread
+// for a hardware-defined interval, so the bound is a few seconds at most)
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
-  for (uint32_t i = 0; i < (1u << 26); ++i)
+  for (uint32_t i = 0; i < (1u << 22); ++i)
     if (mbar_test(b, parity)) return true;
   return false;
 }
@@ -512,19 +533,23 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) gemv_stream_
   }
 }
 
-static int g_stream_attr_dev = -1;
 static void stream_set_attrs() {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (g_stream_attr_dev == dev) return;
   cudaFuncSetAttribute(gemv_stream_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   cudaFuncSetAttribute(gemv_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-  g_stream_attr_dev = dev;
 }
 static void attn_cluster_init();
+// Function attributes are per device: set them once for each device.
 void kernels_init() {
+  static std::mutex mu;
+  static std::vector<char> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if ((size_t)dev < done.size() && done[dev]) return;
   stream_set_attrs();
   attn_cluster_init();
+  if ((size_t)dev >= done.size()) done.resize(dev + 1, 0);
+  done[dev] = 1;
 }
 
 int stream_error_flag(bool reset) {
@@ -624,12 +649,18 @@ struct G3Piece {
   uint4 wa[N], wb[N];
 };
 template <int WB>
-__device__ __forceinline__ void g3_load(G3Piece<WB>& p, const uint4* pa, const uint4* pb, bool has_b, int c0, int nc) {
+__device__ __forceinline__ void g3_load(G3Piece<WB>& p, const uint4* pa, const uint4* pb, bool has_b, int c0, int nc,
+                                        uint64_t pol) {
 #pragma unroll
   for (int u = 0; u < G3Piece<WB>::N; ++u) {
     int c = c0 + 32 * u;
+#if RDET_WEIGHTS_EVICT_FIRST
+    p.wa[u] = c < nc ? ldg_stream_pol(pa + c, pol) : make_uint4(0, 0, 0, 0);
+    p.wb[u] = (has_b && c < nc) ? ldg_stream_pol(pb + c, pol) : make_uint4(0, 0, 0, 0);
+#else
     p.wa[u] = c < nc ? ldg_stream(pa + c) : make_uint4(0, 0, 0, 0);
     p.wb[u] = (has_b && c < nc) ? ldg_stream(pb + c) : make_uint4(0, 0, 0, 0);
+#endif
   }
 }
 template <int WB>
@@ -677,19 +708,60 @@ __device__ __forceinline__ G3Item g3_item(const GemvArgs& a, int gp, int per_ite
   return it;
 }
 
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sa), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Shared-memory vectors of the GEMV prologue, each K ints: x, then (when the
+// prologue uses them) res, g1, g2.
+__host__ __device__ inline int gemv_pro_vectors(int pro) {
+  switch (pro) {
+    case kProNorm: return 2;
+    case kProResScale: return 3;
+    case kProResNorm:
+    case kProResScaleNorm: return 4;
+    default: return 1;
+  }
+}
+
+template <int WB>
+__device__ __forceinline__ void g3_epilogue(const GemvArgs& a, const G3Item& it, int lane, int64_t da, int64_t db) {
+  if (a.pair_geglu) {
+    if (lane == 0) a.seg[0].y[it.ra] = mul_sat(gelu_act(requantize(da)), requantize(db));
+    return;
+  }
+  const GemvSeg& sg = a.seg[it.seg];
+  if (lane < 2 && (lane == 0 || it.has_b)) {
+    const int r = lane == 0 ? it.ra : it.rb;
+    int32_t v = requantize(lane == 0 ? da : db);
+    if (sg.epi == kEpiSoftcap) v = softcap_act(v, a.softcap);
+    else if (sg.epi == kEpiGeluMul) v = mul_sat(gelu_act(v), sg.vec[r]);
+    sg.y[r] = v;
+  }
+}
+
 template <int WB>
 __global__ void __launch_bounds__(kGemvThreads, RDET_GEMV3_CTAS_PER_SM) gemv3_kernel(const GemvArgs a, int per_item) {
-  // Weights never depend on earlier kernels: the first piece of this warp's
-  // first item is requested before waiting on the preceding grid.
+  // Weights and norm gains never depend on earlier kernels: the first piece
+  // of this warp's first item and the gains are requested before waiting on
+  // the preceding grid.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  int32_t* xs = reinterpret_cast<int32_t*>(smem_raw);
-  __shared__ uint64_t red[33];
+  const uint64_t pol = l2_evict_first_policy();
   const int K = a.K;
+  int32_t* xs = reinterpret_cast<int32_t*>(smem_raw);
+  int32_t* rs = xs + K;
+  int32_t* g1s = a.pro == kProNorm ? xs + K : rs + K;
+  int32_t* g2s = g1s + K;
+  __shared__ uint64_t red[33];
   const int nc = K * WB / 16;
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nw = gridDim.x * (blockDim.x >> 5);
+  const bool has_res = a.pro == kProResNorm || a.pro == kProResScale || a.pro == kProResScaleNorm;
+  const bool norm2 = a.pro == kProResNorm || a.pro == kProResScaleNorm;
   int total = 0;
   if (a.pair_geglu) total = a.seg[0].w.rows;
   else for (int j = 0; j < a.nseg; ++j) total += (a.seg[j].w.rows + per_item - 1) / per_item;
@@ -700,57 +772,56 @@ __global__ void __launch_bounds__(kGemvThreads, RDET_GEMV3_CTAS_PER_SM) gemv3_ke
     it = g3_item(a, gw, per_item);
     pa = reinterpret_cast<const uint4*>(it.A + (size_t)it.ra * K * WB);
     pb = reinterpret_cast<const uint4*>(it.B + (size_t)(it.has_b ? it.rb : it.ra) * K * WB);
-    g3_load<WB>(pc, pa, pb, it.has_b, lane, nc);
+    g3_load<WB>(pc, pa, pb, it.has_b, lane, nc, pol);
   }
+  if (a.pro != kProNone)
+    for (int i = threadIdx.x; i < K; i += blockDim.x) cp_async4(g1s + i, a.g1 + i);
+  if (norm2)
+    for (int i = threadIdx.x; i < K; i += blockDim.x) cp_async4(g2s + i, a.g2 + i);
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = a.a[i];
+  for (int i = threadIdx.x; i < K; i += blockDim.x) cp_async4(xs + i, a.a + i);
+  if (has_res)
+    for (int i = threadIdx.x; i < K; i += blockDim.x) cp_async4(rs + i, a.res + i);
+  cp_async_wait_all();
   __syncthreads();
   if (a.pro != kProNone) {
     int32_t sc = block_norm_scale(xs, K, a.eps, red);
     if (a.pro == kProNorm) {
-      for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = mul_sat(mul_sat(xs[i], sc), a.g1[i]);
+      for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = mul_sat(mul_sat(xs[i], sc), g1s[i]);
     } else {
       for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        int32_t t = add_sat(a.res[i], mul_sat(mul_sat(xs[i], sc), a.g1[i]));
+        int32_t t = add_sat(rs[i], mul_sat(mul_sat(xs[i], sc), g1s[i]));
         if (a.has_scalar) t = mul_sat(t, a.scalar);
         xs[i] = t;
         if (blockIdx.x == 0 && a.t_out) a.t_out[i] = t;
       }
       __syncthreads();
-      if (a.pro == kProResNorm || a.pro == kProResScaleNorm) {
+      if (norm2) {
         int32_t sc2 = block_norm_scale(xs, K, a.eps, red);
-        for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = mul_sat(mul_sat(xs[i], sc2), a.g2[i]);
+        for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = mul_sat(mul_sat(xs[i], sc2), g2s[i]);
       }
     }
   }
   __syncthreads();
-  bool first = true;
-  for (int gp = gw; gp < total; gp += nw) {
-    if (!first) {
-      it = g3_item(a, gp, per_item);
-      pa = reinterpret_cast<const uint4*>(it.A + (size_t)it.ra * K * WB);
-      pb = reinterpret_cast<const uint4*>(it.B + (size_t)(it.has_b ? it.rb : it.ra) * K * WB);
-    }
+  // The first piece of every item is already in flight when the item starts:
+  // the next item's is issued before this item's epilogue.
+  for (int gp = gw; gp < total;) {
     int64_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
     for (int c0 = lane; c0 < nc; c0 += 32 * G3Piece<WB>::N) {
-      if (!first) g3_load<WB>(pc, pa, pb, it.has_b, c0, nc);
-      first = false;
+      if (c0 != lane) g3_load<WB>(pc, pa, pb, it.has_b, c0, nc, pol);
       g3_consume<WB>(pc, xs, it.has_b, c0, nc, a0, a1, b0, b1);
     }
-    first = false;
     const int64_t da = warp_sum64(a0 + a1), db = warp_sum64(b0 + b1);
-    if (a.pair_geglu) {
-      if (lane == 0) a.seg[0].y[it.ra] = mul_sat(gelu_act(requantize(da)), requantize(db));
-      continue;
+    const G3Item cur = it;
+    const int gn = gp + nw;
+    if (gn < total) {
+      it = g3_item(a, gn, per_item);
+      pa = reinterpret_cast<const uint4*>(it.A + (size_t)it.ra * K * WB);
+      pb = reinterpret_cast<const uint4*>(it.B + (size_t)(it.has_b ? it.rb : it.ra) * K * WB);
+      g3_load<WB>(pc, pa, pb, it.has_b, lane, nc, pol);
     }
-    const GemvSeg& sg = a.seg[it.seg];
-    if (lane < 2 && (lane == 0 || it.has_b)) {
-      const int r = lane == 0 ? it.ra : it.rb;
-      int32_t v = requantize(lane == 0 ? da : db);
-      if (sg.epi == kEpiSoftcap) v = softcap_act(v, a.softcap);
-      else if (sg.epi == kEpiGeluMul) v = mul_sat(gelu_act(v), sg.vec[r]);
-      sg.y[r] = v;
-    }
+    g3_epilogue<WB>(a, cur, lane, da, db);
+    gp = gn;
   }
 }
 
@@ -775,7 +846,8 @@ static bool launch_gemv3(const GemvArgs& a, cudaStream_t s) {
   int blocks = (items + warps - 1) / warps;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  const size_t smem = (size_t)a.K * 4;
+  const size_t smem = (size_t)a.K * 4 * gemv_pro_vectors(a.pro);
+  if (smem > 200 * 1024) return false;
   if (smem > 48 * 1024) {
     cudaFuncSetAttribute(gemv3_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(gemv3_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -1187,172 +1259,328 @@ void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
 }
 
 // ---------------------------------------------------------------------------
-// decode attention, cluster version.  Cluster = the CL CTAs of one KV head;
-// CTA r takes rows [n*r/CL, n*(r+1)/CL) of the window.  Exactly the arithmetic
-// of attention_output_into for each of the G query heads of the KV head.
+// decode attention, cluster version.  One thread-block cluster per group of
+// GC query heads of one KV head; CTA r of the cluster takes rows
+// [n*r/CL, n*(r+1)/CL) of the window.  GC is the smallest group that lets all
+// clusters be resident at once (a 16-CTA cluster needs 16 SMs of one GPC).
+// Exactly the arithmetic of attention_output_into: the first max, exp terms,
+// sum and weights are cluster-wide values combined through distributed shared
+// memory, and the weighted V sums (wrapping i64) are added across CTAs.
+//
+// Data path: model constants (norm gains, RoPE inverse frequencies) are
+// requested before the grid-dependency wait; right after it thread 0 starts
+// bulk copies (TMA, no multicast) of the CTA's K rows and then V rows -- one
+// contiguous span each -- into a ring of 32 KB shared-memory slots, each
+// with an mbarrier that counts the bytes.  Waits are bounded: a wait that
+// gives up sets the library's pipeline error flag (the host raises an error)
+// instead of hanging.  With the fused prologue every CTA builds the current
+// token's K/V row itself and reads it from shared memory, so clusters of one
+// KV head never wait on each other; one CTA per KV head appends the row to
+// the cache.  Cluster-wide reductions read one rank per lane and finish with
+// warp shuffles.
 // ---------------------------------------------------------------------------
 namespace cg = cooperative_groups;
-constexpr int kAcThreads = 512;
+constexpr int kAcThreads = 256;
+constexpr int kAcWarps = kAcThreads / 32;
+constexpr int kAcTileBytes = 32 * 1024;
+constexpr int kAcStages = 4;
 
-// The k/v row scratch of the fused prologue lives in the partial-sum buffer
-// (G*d i64 >= 2*d i32), which phase 3 overwrites only after the row is stored.
-__device__ __forceinline__ int32_t* pacc_ptr_guard(int64_t* ex, int G, int rmax, int d) {
-  return reinterpret_cast<int32_t*>(ex + G * rmax);
+__device__ __forceinline__ int64_t dot4(const int4& k, const int4& q) {
+  return (int64_t)k.x * q.x + (int64_t)k.y * q.y + (int64_t)k.z * q.z + (int64_t)k.w * q.w;
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(sa), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
 
-template <int G>
-__global__ void __launch_bounds__(kAcThreads) attn_dec_cluster_kernel(const AttnDecodeArgs a, int rmax) {
-  pdl_entry();
+struct AcLayout {  // offsets in 4-byte words of the dynamic shared memory
+  int ring, qs, kvrow, qn, kn, ifq, sc, ex, pacc, total;
+};
+__host__ __device__ inline AcLayout ac_layout(int gc, int d, int rmax) {
+  AcLayout L;
+  int o = 0;
+  L.ring = o; o += kAcStages * kAcTileBytes / 4;  // 16-byte aligned slots first
+  L.qs = o; o += gc * d;
+  L.kvrow = o; o += 2 * d;
+  L.qn = o; o += d;
+  L.kn = o; o += d;
+  o = (o + 1) & ~1;
+  L.ifq = o; o += 2 * 256;
+  L.ex = o; o += 2 * gc * rmax;
+  L.pacc = o; o += 2 * gc * d;
+  L.sc = o; o += gc * rmax;
+  L.total = o;
+  return L;
+}
+
+// Sums each of the S per-lane values over the warp (S a power of two <= 32):
+// transposed butterfly -- at each of the first log2(S) steps a lane keeps half
+// of its values and trades the other half -- then plain xor steps.  Lane l
+// returns the total of value l / (32 / S).  Wrapping i64 sums are order-free,
+// so the result equals warp_sum64 of each value.
+template <int S>
+__device__ __forceinline__ int64_t warp_multi_sum(int64_t (&v)[S], int lane) {
+#pragma unroll
+  for (int cnt = S, o = 16; cnt > 1; cnt >>= 1, o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < cnt / 2; ++i) {
+      const int64_t send = up ? v[i] : v[i + cnt / 2];
+      const int64_t keep = up ? v[i + cnt / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  int64_t t = v[0];
+#pragma unroll
+  for (int o = 16 / S; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  return t;
+}
+
+// (value, index) of the first maximum; index INT32_MAX marks "no rows"
+__device__ __forceinline__ void first_max_merge(int32_t& v, int32_t& ix, int32_t ov, int32_t oi) {
+  if (oi != INT32_MAX && (ix == INT32_MAX || ov > v || (ov == v && oi < ix))) { v = ov; ix = oi; }
+}
+
+// Head dims up to 128*NCH with d % 4 == 0; lane l owns 16-byte chunks
+// l + 32u (u < NCH) of every row.
+template <int GC, int NCH>
+__global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const AttnDecodeArgs a, int rmax) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
+  int32_t* sm = reinterpret_cast<int32_t*>(smem_raw);
   cg::cluster_group cl = cg::this_cluster();
   const int CL = (int)cl.num_blocks(), rank = (int)cl.block_rank();
-  const int kvh = blockIdx.y, d = a.d;
-  int32_t* qs = reinterpret_cast<int32_t*>(smem_raw);             // [G][d]
-  int32_t* sc = qs + G * d;                                        // [G][rmax] scores, then weights
-  int64_t* ex = reinterpret_cast<int64_t*>(sc + G * rmax + (G * rmax & 1));  // [G][rmax]
-  int64_t* pacc = ex + G * rmax;                                   // [G][d] partial weighted sums
-  __shared__ int32_t s_max[G], s_idx[G];
-  __shared__ int64_t s_sum[G], s_wsum[G];
-  __shared__ int32_t g_max[G], g_idx[G], g_res[G];
-  __shared__ int64_t g_sum[G];
-  __shared__ int32_t wm[kAcThreads / 32][G], wi[kAcThreads / 32][G];
-  __shared__ int64_t ws[kAcThreads / 32][G];
+  const int d = a.d, nch = d >> 2;
+  const int G = a.Hq / a.Hkv;
+  const int qh0 = blockIdx.y * GC;  // first query head of this cluster
+  const int kvh = qh0 / G;
+  const AcLayout Ly = ac_layout(GC, d, rmax);
+  unsigned char* ring = smem_raw + (size_t)Ly.ring * 4;
+  int32_t* qs = sm + Ly.qs;        // [GC][d]
+  int32_t* kvrow = sm + Ly.kvrow;  // current token's k, v
+  int32_t* qn = sm + Ly.qn;
+  int32_t* kn = sm + Ly.kn;
+  int64_t* ifq = reinterpret_cast<int64_t*>(sm + Ly.ifq);
+  int32_t* sc = sm + Ly.sc;                                  // [GC][rmax] scores, then weights
+  int64_t* ex = reinterpret_cast<int64_t*>(sm + Ly.ex);      // [GC][rmax]
+  int64_t* pacc = reinterpret_cast<int64_t*>(sm + Ly.pacc);  // [GC][d]
+  __shared__ __align__(8) uint64_t full[kAcStages];
+  __shared__ int32_t s_max[GC], s_idx[GC], g_max[GC], g_idx[GC], g_res[GC], sc_q[GC], sc_kv[2];
+  __shared__ int64_t s_sum[GC], s_wsum[GC], g_sum[GC];
+  __shared__ int32_t wm[kAcWarps][GC], wi[kAcWarps][GC];
+  __shared__ int64_t ws[kAcWarps][GC];
+  __shared__ int32_t cs_tab[256], sn_tab[256];
+  __shared__ int s_fail;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const AttnFuse& f = a.fuse;
+  const bool fused = f.q_in != nullptr;
+  const bool new_row = fused && f.k_in != nullptr;  // this layer appends the current token
+  const int half = fused ? (f.rotary >> 1) : 0;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // model constants, requested before the grid-dependency wait
+  if (fused) {
+    for (int i = tid; i < d; i += kAcThreads) {
+      cp_async4(qn + i, f.q_norm + i);
+      if (new_row) cp_async4(kn + i, f.k_norm + i);
+    }
+    for (int i = tid; i < half; i += kAcThreads) cp_async8(ifq + i, f.inv_freq + i);
+  }
+  if (tid == 0) {
+    for (int i = 0; i < kAcStages; ++i) mbar_init(&full[i], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_fail = 0;
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int pos = a.pos ? *a.pos : a.pos_value;
   int start, n;
   decode_window(a, &start, &n);
   const int lo = (int)((int64_t)n * rank / CL), hi = (int)((int64_t)n * (rank + 1) / CL);
   const int rows = hi - lo;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = kAcThreads / 32;
-  const AttnFuse& f = a.fuse;
-  if (!f.q_in) {
-    for (int i = threadIdx.x; i < G * d; i += kAcThreads) qs[i] = a.q[(size_t)kvh * G * d + i];
-    __syncthreads();
+  const int TR = kAcTileBytes / (d * 4);  // rows per tile
+  const int tiles = (rows + TR - 1) / TR;
+  const int total_tiles = 2 * tiles;  // K tiles, then V tiles
+  const size_t head_base = (size_t)kvh * a.cap;
+  // the current token's row (when built here) is the CTA's last row and is
+  // not copied from the cache
+  const int copy_rows = rows - ((new_row && rows > 0 && start + hi - 1 == pos) ? 1 : 0);
+  // unified tile u: K tile u (u < tiles) or V tile u - tiles, in slot u % S
+  auto issue = [&](int u) {  // thread 0 only
+    const int slot = u % kAcStages;
+    const int t = u < tiles ? u : u - tiles;
+    const int32_t* cache = u < tiles ? a.k_cache : a.v_cache;
+    const int r0 = t * TR;
+    const int nr = min(TR, copy_rows - r0);
+    if (nr > 0) {
+      const uint32_t bytes = (uint32_t)nr * d * 4;
+      mbar_arrive_tx(&full[slot], bytes);
+      bulk_g2s(ring + (size_t)slot * kAcTileBytes, cache + (head_base + start + lo + r0) * d, bytes, &full[slot]);
+    } else {
+      mbar_arrive(&full[slot]);
+    }
+  };
+  auto wait_tile = [&](int u) {  // every thread
+    if (!mbar_wait(&full[u % kAcStages], (u / kAcStages) & 1)) s_fail = 1;
+  };
+  if (tid == 0)
+    for (int u = 0; u < kAcStages && u < total_tiles; ++u) issue(u);
+  for (int i = tid; i < GC * d; i += kAcThreads) pacc[i] = 0;
+  if (!fused) {
+    for (int i = tid; i < GC * d; i += kAcThreads) qs[i] = a.q[(size_t)qh0 * d + i];
   } else {
-    // fused qkv_post: q heads of this KV head (every rank), and on rank 0 the
-    // new K/V row of the cache.  kv[0] = normed+rotated k, kv[1] = normed v.
-    __shared__ int32_t sc_q[G], sc_kv[2];
-    __shared__ int32_t cs_tab[256], sn_tab[256];
-    int32_t* kvrow = pacc_ptr_guard(ex, G, rmax, d);  // scratch for the k/v row (reuses pacc space)
-    const uint32_t pos = (uint32_t)(a.pos ? *a.pos : a.pos_value);
-    const bool own = f.k_in != nullptr && rank == 0;
-    for (int i = threadIdx.x; i < G * d; i += kAcThreads) qs[i] = f.q_in[(size_t)kvh * G * d + i];
-    if (own)
-      for (int i = threadIdx.x; i < d; i += kAcThreads) {
+    for (int i = tid; i < GC * d; i += kAcThreads) qs[i] = f.q_in[(size_t)qh0 * d + i];
+    if (new_row)
+      for (int i = tid; i < d; i += kAcThreads) {
         kvrow[i] = f.k_in[(size_t)kvh * d + i];
         kvrow[d + i] = f.v_in[(size_t)kvh * d + i];
       }
-    const int half = f.rotary >> 1;
-    for (int i = threadIdx.x; i < half; i += kAcThreads) {
+    cp_async_commit_wait_all();  // the constants have landed
+    __syncthreads();
+    for (int i = tid; i < half; i += kAcThreads) {
       int32_t cv, sv;
-      sin_cos_acc(pos_angle(pos, f.inv_freq[i]), &cv, &sv);
+      sin_cos_acc(pos_angle((uint32_t)pos, ifq[i]), &cv, &sv);
       cs_tab[i] = cv;
       sn_tab[i] = sv;
     }
-    __syncthreads();
-    if (warp < G) {
-      int32_t scv = warp_norm_scale(qs + warp * d, d, f.eps);
-      if (lane == 0) sc_q[warp] = scv;
-    } else if (own && warp == G) {
+    if (warp >= kAcWarps - GC) {
+      const int g = warp - (kAcWarps - GC);
+      int32_t scv = warp_norm_scale(qs + g * d, d, f.eps);
+      if (lane == 0) sc_q[g] = scv;
+    } else if (new_row && warp == kAcWarps - GC - 1) {
       int32_t scv = warp_norm_scale(kvrow, d, f.eps);
       if (lane == 0) sc_kv[0] = scv;
-    } else if (own && warp == G + 1) {
+    } else if (new_row && warp == kAcWarps - GC - 2) {
       int32_t scv = warp_norm_scale(kvrow + d, d, f.eps);
       if (lane == 0) sc_kv[1] = scv;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < G * d; i += kAcThreads) {
-      int g = i / d, t = i - g * d;
-      qs[i] = mul_sat(mul_sat(qs[i], sc_q[g]), f.q_norm[t]);
+    for (int i = tid; i < GC * d; i += kAcThreads) {
+      const int g = i / d, t = i - g * d;
+      qs[i] = mul_sat(mul_sat(qs[i], sc_q[g]), qn[t]);
     }
-    if (own)
-      for (int i = threadIdx.x; i < d; i += kAcThreads) {
-        kvrow[i] = mul_sat(mul_sat(kvrow[i], sc_kv[0]), f.k_norm[i]);
+    if (new_row)
+      for (int i = tid; i < d; i += kAcThreads) {
+        kvrow[i] = mul_sat(mul_sat(kvrow[i], sc_kv[0]), kn[i]);
         kvrow[d + i] = mul_sat(kvrow[d + i], sc_kv[1]);
       }
     __syncthreads();
     if (pos != 0 && half > 0) {  // rope_rotate_pairs_in_place leaves position 0 unchanged
-      for (int e = threadIdx.x; e < (G + (own ? 1 : 0)) * half; e += kAcThreads) {
-        int h = e / half, i = e - h * half;
-        int32_t* v = h < G ? qs + h * d : kvrow;
-        int32_t l = v[i], r = v[i + half];
+      const int nv = GC + (new_row ? 1 : 0);
+      for (int e = tid; e < nv * half; e += kAcThreads) {
+        const int h = e / half, i = e - h * half;
+        int32_t* v = h < GC ? qs + h * d : kvrow;
+        const int32_t l = v[i], r = v[i + half];
         v[i] = sub_sat(mul_sat(l, cs_tab[i]), mul_sat(r, sn_tab[i]));
         v[i + half] = add_sat(mul_sat(r, cs_tab[i]), mul_sat(l, sn_tab[i]));
       }
+    }
+    if (new_row && rank == 0 && qh0 % G == 0) {
       __syncthreads();
-    }
-    if (own) {
-      for (int i = threadIdx.x; i < d; i += kAcThreads) {
-        f.k_out[((size_t)kvh * a.cap + pos) * d + i] = kvrow[i];
-        f.v_out[((size_t)kvh * a.cap + pos) * d + i] = kvrow[d + i];
+      for (int i = tid; i < d; i += kAcThreads) {
+        f.k_out[(head_base + pos) * d + i] = kvrow[i];
+        f.v_out[(head_base + pos) * d + i] = kvrow[d + i];
       }
     }
-    cl.sync();  // the appended row is visible to every rank before scoring
-  }
-  // ---- phase 1: scores (warp per row; 16-byte loads when d % 128 == 0)
-  int32_t bm[G], bi[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) { bm[g] = INT32_MIN; bi[g] = INT32_MAX; }
-  for (int j = warp; j < rows; j += nwarp) {
-    const int32_t* kr = a.k_cache + ((size_t)kvh * a.cap + start + lo + j) * d;
-    int64_t acc[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = 0;
-    if ((d & 127) == 0) {
-      for (int c = lane; c < d / 4; c += 32) {
-        int4 kv = reinterpret_cast<const int4*>(kr)[c];
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          int4 qv = reinterpret_cast<const int4*>(qs + g * d)[c];
-          acc[g] += (int64_t)kv.x * qv.x + (int64_t)kv.y * qv.y + (int64_t)kv.z * qv.z + (int64_t)kv.w * qv.w;
-        }
-      }
-    } else {
-      for (int t = lane; t < d; t += 32) {
-        int64_t kv = kr[t];
-#pragma unroll
-        for (int g = 0; g < G; ++g) acc[g] += kv * qs[g * d + t];
-      }
-    }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      int32_t v = requantize(warp_sum64(acc[g]));
-      if (lane == 0) sc[g * rmax + j] = v;
-      if (v > bm[g]) { bm[g] = v; bi[g] = lo + j; }  // rows ascend: the first max is kept
-    }
-  }
-  if (lane == 0) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) { wm[warp][g] = bm[g]; wi[warp][g] = bi[g]; }
   }
   __syncthreads();
-  if (threadIdx.x < G) {
-    const int g = threadIdx.x;
-    int32_t m = INT32_MIN, mi = INT32_MAX;
-    for (int w = 0; w < nwarp; ++w) {
-      if (wi[w][g] == INT32_MAX) continue;
-      if (wm[w][g] > m || (wm[w][g] == m && wi[w][g] < mi)) { m = wm[w][g]; mi = wi[w][g]; }
+  // ---- phase 1: scores, tile by tile from shared memory.  A warp takes RB
+  // rows at a time; the RB*GC dot products of a step are reduced together and
+  // lane l owns value l / (32/S) (row l/(32/S)/GC of the step, head % GC).
+  constexpr int RB = NCH >= 4 ? 2 : (NCH == 2 ? 4 : 8);
+  constexpr int S = RB * GC;
+  int4 qv[GC][NCH];
+#pragma unroll
+  for (int g = 0; g < GC; ++g)
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) {
+      const int c = lane + 32 * u;
+      qv[g][u] = c < nch ? reinterpret_cast<const int4*>(qs + g * d)[c] : make_int4(0, 0, 0, 0);
     }
+  const int own = lane / (32 / S);  // value index this lane finalizes
+  const int own_r = own / GC, own_g = own % GC;
+  const bool owner = lane % (32 / S) == 0;
+  int32_t bm = INT32_MIN, bi = INT32_MAX;  // this lane's candidate for head own_g
+  for (int t = 0; t < tiles; ++t) {
+    wait_tile(t);
+    const int r0 = t * TR, nr = min(TR, rows - r0);
+    const int32_t* tile = reinterpret_cast<const int32_t*>(ring + (size_t)(t % kAcStages) * kAcTileBytes);
+    for (int base = warp * RB; base < nr; base += kAcWarps * RB) {
+      int64_t acc[S];
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        const int i = base + r;
+        int4 kv[NCH];
+        const int4* kr = reinterpret_cast<const int4*>(
+            (new_row && start + lo + r0 + i == pos) ? kvrow : tile + (size_t)(i < nr ? i : 0) * d);
+#pragma unroll
+        for (int u = 0; u < NCH; ++u) {
+          const int c = lane + 32 * u;
+          kv[u] = (i < nr && c < nch) ? kr[c] : make_int4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int g = 0; g < GC; ++g) {
+          int64_t x = 0;
+#pragma unroll
+          for (int u = 0; u < NCH; ++u) x += dot4(kv[u], qv[g][u]);
+          acc[r * GC + g] = x;
+        }
+      }
+      const int64_t tot = warp_multi_sum<S>(acc, lane);
+      const int i = base + own_r;
+      if (owner && i < nr) {
+        const int j = r0 + i;
+        const int32_t v = requantize(tot);
+        sc[own_g * rmax + j] = v;
+        if (v > bm) { bm = v; bi = lo + j; }  // a lane's rows ascend: the first max is kept
+      }
+    }
+    __syncthreads();
+    if (tid == 0 && t + kAcStages < total_tiles) issue(t + kAcStages);
+  }
+  // per-head first max over the lanes that own the head, then over warps
+#pragma unroll
+  for (int g = 0; g < GC; ++g) {
+    int32_t m = own_g == g ? bm : INT32_MIN, mi = own_g == g ? bi : INT32_MAX;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const int32_t om = __shfl_xor_sync(0xffffffffu, m, o), oi = __shfl_xor_sync(0xffffffffu, mi, o);
+      first_max_merge(m, mi, om, oi);
+    }
+    if (lane == 0) { wm[warp][g] = m; wi[warp][g] = mi; }
+  }
+  __syncthreads();
+  if (tid < GC) {
+    const int g = tid;
+    int32_t m = INT32_MIN, mi = INT32_MAX;
+    for (int w = 0; w < kAcWarps; ++w) first_max_merge(m, mi, wm[w][g], wi[w][g]);
     s_max[g] = m;
     s_idx[g] = mi;
   }
   cl.sync();
-  // ---- global first max (every CTA computes the same value from all ranks)
-  if (threadIdx.x < G) {
-    const int g = threadIdx.x;
+  // ---- global first max: warp g reads rank `lane` and reduces by shuffles
+  if (warp < GC) {
+    const int g = warp;
     int32_t m = INT32_MIN, mi = INT32_MAX;
-    for (int r = 0; r < CL; ++r) {
-      int32_t v = *cl.map_shared_rank(&s_max[g], r), ix = *cl.map_shared_rank(&s_idx[g], r);
-      if (ix == INT32_MAX) continue;
-      if (v > m || (v == m && ix < mi)) { m = v; mi = ix; }
+    if (lane < CL) {
+      m = *cl.map_shared_rank(&s_max[g], lane);
+      mi = *cl.map_shared_rank(&s_idx[g], lane);
     }
-    g_max[g] = m;
-    g_idx[g] = mi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const int32_t om = __shfl_xor_sync(0xffffffffu, m, o), oi = __shfl_xor_sync(0xffffffffu, mi, o);
+      first_max_merge(m, mi, om, oi);
+    }
+    if (lane == 0) { g_max[g] = m; g_idx[g] = mi; }
   }
   __syncthreads();
   // ---- phase 2: exp terms, local sums
-  for (int g = 0; g < G; ++g) {
+#pragma unroll
+  for (int g = 0; g < GC; ++g) {
     uint64_t sum = 0;
-    for (int j = threadIdx.x; j < rows; j += kAcThreads) {
-      int64_t e = exp_term(sc[g * rmax + j], g_max[g]);
+    for (int j = tid; j < rows; j += kAcThreads) {
+      const int64_t e = exp_term(sc[g * rmax + j], g_max[g]);
       ex[g * rmax + j] = e;
       sum += (uint64_t)e;
     }
@@ -1360,23 +1588,24 @@ __global__ void __launch_bounds__(kAcThreads) attn_dec_cluster_kernel(const Attn
     if (lane == 0) ws[warp][g] = (int64_t)sum;
   }
   __syncthreads();
-  if (threadIdx.x < G) {
+  if (tid < GC) {
     int64_t t = 0;
-    for (int w = 0; w < nwarp; ++w) t += ws[w][threadIdx.x];
-    s_sum[threadIdx.x] = t;
+    for (int w = 0; w < kAcWarps; ++w) t += ws[w][tid];
+    s_sum[tid] = t;
   }
   cl.sync();
-  if (threadIdx.x < G) {
-    int64_t t = 0;
-    for (int r = 0; r < CL; ++r) t += *cl.map_shared_rank(&s_sum[threadIdx.x], r);
-    g_sum[threadIdx.x] = t;
+  if (warp < GC) {
+    const int64_t v = lane < CL ? *cl.map_shared_rank(&s_sum[warp], lane) : 0;
+    const int64_t t = warp_sum64(v);
+    if (lane == 0) g_sum[warp] = t;
   }
   __syncthreads();
-  // ---- phase 3: weights, local weight sums and partial weighted V sums
-  for (int g = 0; g < G; ++g) {
+  // ---- phase 3: weights, local weight sums, partial weighted V sums
+#pragma unroll
+  for (int g = 0; g < GC; ++g) {
     int64_t wsum = 0;
-    for (int j = threadIdx.x; j < rows; j += kAcThreads) {
-      int32_t w = softmax_weight(ex[g * rmax + j], g_sum[g]);
+    for (int j = tid; j < rows; j += kAcThreads) {
+      const int32_t w = softmax_weight(ex[g * rmax + j], g_sum[g]);
       sc[g * rmax + j] = w;
       wsum += w;
     }
@@ -1384,53 +1613,105 @@ __global__ void __launch_bounds__(kAcThreads) attn_dec_cluster_kernel(const Attn
     if (lane == 0) ws[warp][g] = wsum;
   }
   __syncthreads();
-  if (threadIdx.x < G) {
+  if (tid < GC) {
     int64_t t = 0;
-    for (int w = 0; w < nwarp; ++w) t += ws[w][threadIdx.x];
-    s_wsum[threadIdx.x] = t;
+    for (int w = 0; w < kAcWarps; ++w) t += ws[w][tid];
+    s_wsum[tid] = t;
   }
-  for (int dim = threadIdx.x; dim < d; dim += kAcThreads) {
-    int64_t acc[G];
+  int64_t acc[GC][NCH][4];
 #pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = 0;
-    const int32_t* vb = a.v_cache + ((size_t)kvh * a.cap + start + lo) * d + dim;
-    for (int j = 0; j < rows; ++j) {
-      int64_t v = vb[(size_t)j * d];
+  for (int g = 0; g < GC; ++g)
 #pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] += v * sc[g * rmax + j];
+    for (int u = 0; u < NCH; ++u)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[g][u][e] = 0;
+  for (int t = 0; t < tiles; ++t) {
+    const int uu = tiles + t;
+    wait_tile(uu);
+    const int r0 = t * TR, nr = min(TR, rows - r0);
+    const int32_t* tile = reinterpret_cast<const int32_t*>(ring + (size_t)(uu % kAcStages) * kAcTileBytes);
+    for (int i = warp; i < nr; i += kAcWarps) {
+      const int j = r0 + i;
+      const int4* vr = reinterpret_cast<const int4*>(
+          (new_row && start + lo + j == pos) ? kvrow + d : tile + (size_t)i * d);
+#pragma unroll
+      for (int u = 0; u < NCH; ++u) {
+        const int c = lane + 32 * u;
+        if (c < nch) {
+          const int4 v = vr[c];
+#pragma unroll
+          for (int g = 0; g < GC; ++g) {
+            const int32_t w = sc[g * rmax + j];
+            acc[g][u][0] += (int64_t)v.x * w;
+            acc[g][u][1] += (int64_t)v.y * w;
+            acc[g][u][2] += (int64_t)v.z * w;
+            acc[g][u][3] += (int64_t)v.w * w;
+          }
+        }
+      }
     }
-#pragma unroll
-    for (int g = 0; g < G; ++g) pacc[g * d + dim] = acc[g];
+    __syncthreads();
+    if (tid == 0 && uu + kAcStages < total_tiles) issue(uu + kAcStages);
   }
+#pragma unroll
+  for (int g = 0; g < GC; ++g)
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) {
+      const int c = lane + 32 * u;
+      if (c < nch)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          atomicAdd(reinterpret_cast<unsigned long long*>(&pacc[g * d + 4 * c + e]), (unsigned long long)acc[g][u][e]);
+    }
   cl.sync();
-  // ---- combine: this CTA finalizes output dims [d*rank/CL, d*(rank+1)/CL)
-  if (threadIdx.x < G) {
-    int64_t t = 0;
-    for (int r = 0; r < CL; ++r) t += *cl.map_shared_rank(&s_wsum[threadIdx.x], r);
-    g_res[threadIdx.x] = sub_sat(kOneAct, t > INT32_MAX ? INT32_MAX : (int32_t)t);
+  // ---- combine: this CTA finalizes output dims [d*rank/CL, d*(rank+1)/CL);
+  // CL consecutive lanes read one element's partial sums from the CL ranks
+  if (warp < GC) {
+    const int64_t v = lane < CL ? *cl.map_shared_rank(&s_wsum[warp], lane) : 0;
+    const int64_t t = warp_sum64(v);
+    if (lane == 0) g_res[warp] = sub_sat(kOneAct, t > INT32_MAX ? INT32_MAX : (int32_t)t);
   }
   __syncthreads();
   const int d0 = (int)((int64_t)d * rank / CL), d1 = (int)((int64_t)d * (rank + 1) / CL);
-  for (int e = threadIdx.x; e < G * (d1 - d0); e += kAcThreads) {
-    const int g = e / (d1 - d0), dim = d0 + e % (d1 - d0);
-    int64_t acc = 0;
-    for (int r = 0; r < CL; ++r) acc += *cl.map_shared_rank(&pacc[g * d + dim], r);
-    acc += (int64_t)a.v_cache[((size_t)kvh * a.cap + start + g_idx[g]) * d + dim] * g_res[g];
-    a.out[((size_t)kvh * G + g) * d + dim] = requantize(acc);
+  const int per = d1 - d0, nel = GC * per, epw = kAcThreads / CL;
+  for (int base = 0; base < nel; base += epw) {
+    const int e = base + tid / CL, r = tid % CL;
+    int64_t v = 0;
+    int g = 0, dim = 0;
+    if (e < nel) {
+      g = e / per;
+      dim = d0 + e % per;
+      v = *cl.map_shared_rank(&pacc[g * d + dim], r);
+    }
+    for (int o = CL >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (r == 0 && e < nel) {
+      const int32_t* vmax =
+          (new_row && start + g_idx[g] == pos) ? kvrow + d : a.v_cache + (head_base + start + g_idx[g]) * d;
+      v += (int64_t)vmax[dim] * g_res[g];
+      a.out[(size_t)(qh0 + g) * d + dim] = requantize(v);
+    }
+  }
+  if (s_fail && tid == 0) {
+    atomicExch(&g_stream_err, 1);
+    // every issued copy has a consumer wait; give stragglers one more bounded
+    // wait before the CTA's shared memory is released
+    for (int u = max(0, total_tiles - kAcStages); u < total_tiles; ++u)
+      mbar_wait(&full[u % kAcStages], (u / kAcStages) & 1);
   }
   cl.sync();  // keep this CTA's shared memory alive until every rank has read it
 }
 
-static int g_attn_cluster = 0;  // cluster size chosen for this device
+static int g_attn_cluster = 0;   // cluster size chosen for this device
+static int g_attn_max_clusters = 0;  // 16- or 8-CTA clusters resident at once
 
-template <int G>
-static cudaError_t launch_ac(const AttnDecodeArgs& a, int CL, cudaStream_t s) {
-  const int rmax = (a.cap + CL - 1) / CL + 1;
-  const size_t smem = (size_t)G * a.d * 4 + (size_t)G * rmax * 4 + 4 + (size_t)G * rmax * 8 + (size_t)G * a.d * 8;
+static size_t ac_smem(int gc, int d, int rmax) { return (size_t)ac_layout(gc, d, rmax).total * 4; }
+
+template <int GC, int NCH>
+static cudaError_t launch_ac(const AttnDecodeArgs& a, int CL, int rmax, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(CL, a.Hkv, 1);
+  cfg.gridDim = dim3(CL, a.Hq / GC, 1);
   cfg.blockDim = dim3(kAcThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = ac_smem(GC, a.d, rmax);
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1441,52 +1722,104 @@ static cudaError_t launch_ac(const AttnDecodeArgs& a, int CL, cudaStream_t s) {
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, attn_dec_cluster_kernel<G>, a, rmax);
+  return cudaLaunchKernelEx(&cfg, attn_dec_cluster_kernel<GC, NCH>, a, rmax);
 }
 
-template <int G>
+constexpr size_t kAcMaxSmem = 200 * 1024;
+
+template <int GC, int NCH>
+static void ac_prepare1(int CL) {
+  cudaFuncSetAttribute(attn_dec_cluster_kernel<GC, NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAcMaxSmem);
+  if (CL > 8)
+    cudaFuncSetAttribute(attn_dec_cluster_kernel<GC, NCH>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+}
+template <int NCH>
 static void ac_prepare(int CL) {
-  cudaFuncSetAttribute(attn_dec_cluster_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  if (CL > 8) cudaFuncSetAttribute(attn_dec_cluster_kernel<G>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  ac_prepare1<1, NCH>(CL);
+  ac_prepare1<2, NCH>(CL);
+  if (NCH <= 2) ac_prepare1<4, NCH>(CL);
 }
 
-static void attn_cluster_init() {
-  if (g_attn_cluster) return;
-  int CL = 16;
-  ac_prepare<1>(CL);
-  ac_prepare<2>(CL);
-  ac_prepare<4>(CL);
-  ac_prepare<8>(CL);
-  // use 16-CTA clusters when the device can schedule them, else the portable 8
+static int ac_max_clusters(int CL) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(16, 1, 1);
+  cfg.gridDim = dim3(CL, 1, 1);
   cfg.blockDim = dim3(kAcThreads, 1, 1);
-  cfg.dynamicSmemBytes = 64 * 1024;
+  cfg.dynamicSmemBytes = ac_smem(1, 512, 300);  // one CTA per SM
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 16;
+  attr[0].val.clusterDim.x = CL;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  int nclusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&nclusters, attn_dec_cluster_kernel<4>, &cfg) != cudaSuccess || nclusters < 1) {
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, attn_dec_cluster_kernel<1, 4>, &cfg) != cudaSuccess) {
     cudaGetLastError();
-    CL = 8;
+    n = 0;
   }
-  g_attn_cluster = CL;
+  return n;
+}
+
+static void attn_cluster_init() {
+  ac_prepare<1>(16);
+  ac_prepare<2>(16);
+  ac_prepare<4>(16);
+  if (g_attn_cluster) return;
+  // 16-CTA clusters when the device can schedule them, else the portable 8
+  int n = ac_max_clusters(16);
+  if (n >= 1) {
+    g_attn_cluster = 16;
+  } else {
+    g_attn_cluster = 8;
+    n = ac_max_clusters(8);
+  }
+  g_attn_max_clusters = n > 0 ? n : 1;
+}
+
+static int ac_rmax(int window, int cap, int CL) {
+  const int span = window > 0 && window < cap ? window : cap;
+  return (span + CL - 1) / CL + 1;
+}
+
+// Query heads per cluster: the smallest power of two dividing the group size
+// G that keeps Hq/GC clusters resident together (capped by register budget).
+static int ac_group(int Hq, int Hkv, int d) {
+  const int G = Hq / Hkv;
+  const int cap = d <= 256 ? 4 : 2;
+  const int maxc = g_attn_max_clusters > 0 ? g_attn_max_clusters : 1;
+  int gc = 1;
+  while (Hq / gc > maxc && gc * 2 <= cap && G % (gc * 2) == 0) gc *= 2;
+  return gc;
+}
+
+bool attn_decode_cluster_fits(int Hq, int Hkv, int d, int window, int cap, int rotary) {
+  const int CL = g_attn_cluster ? g_attn_cluster : 8;
+  if (!(Hkv > 0 && Hq % Hkv == 0 && d > 0 && d % 4 == 0 && d <= 512 && (rotary >> 1) <= 256)) return false;
+  const int gc = ac_group(Hq, Hkv, d);
+  return gc <= 8 - 2 && ac_smem(gc, d, ac_rmax(window, cap, CL)) <= kAcMaxSmem;
 }
 
 void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s) {
-  const int G = a.Hq / a.Hkv;
   const int CL = g_attn_cluster ? g_attn_cluster : 8;
+  const int rmax = ac_rmax(a.window, a.cap, CL);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(a.k_cache) | reinterpret_cast<uintptr_t>(a.v_cache)) & 15) == 0;
+  if (!aligned || !attn_decode_cluster_fits(a.Hq, a.Hkv, a.d, a.window, a.cap, a.fuse.q_in ? a.fuse.rotary : 0)) {
+    launch_attn_decode(a, s);  // callers only fuse when the cluster kernel fits
+    return;
+  }
+  const int gc = ac_group(a.Hq, a.Hkv, a.d);
   // launch errors surface through cudaGetLastError in the caller
-  switch (G) {
-    case 1: launch_ac<1>(a, CL, s); break;
-    case 2: launch_ac<2>(a, CL, s); break;
-    case 4: launch_ac<4>(a, CL, s); break;
-    case 8: launch_ac<8>(a, CL, s); break;
-    default: launch_attn_decode(a, s); break;
+  if (a.d <= 128) {
+    if (gc == 1) launch_ac<1, 1>(a, CL, rmax, s);
+    else if (gc == 2) launch_ac<2, 1>(a, CL, rmax, s);
+    else launch_ac<4, 1>(a, CL, rmax, s);
+  } else if (a.d <= 256) {
+    if (gc == 1) launch_ac<1, 2>(a, CL, rmax, s);
+    else if (gc == 2) launch_ac<2, 2>(a, CL, rmax, s);
+    else launch_ac<4, 2>(a, CL, rmax, s);
+  } else {
+    if (gc == 1) launch_ac<1, 4>(a, CL, rmax, s);
+    else launch_ac<2, 4>(a, CL, rmax, s);
   }
 }
 

@@ -42,7 +42,9 @@ struct GemvArgs {
   GemvSeg seg[3];
   bool pair_geglu = false;  // seg[0]=gate, seg[1]=up: seg[0].y[r] = mul_sat(gelu(g), u)
   int32_t softcap = 0;
-  // prologue
+  // prologue.  g1/g2 are model constants: the kernel reads them before
+  // waiting on the preceding grid, so no earlier kernel in the stream may
+  // write them.
   int32_t pro = kProNone;
   const int32_t* a = nullptr;
   const int32_t* res = nullptr;
@@ -131,10 +133,15 @@ struct AttnDecodeArgs {
   AttnFuse fuse;                 // used by the cluster kernel only
 };
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s);
-// Same computation in one kernel: one thread-block cluster per KV head splits
-// the window across its CTAs and combines the exact softmax statistics through
-// distributed shared memory (no global scratch; a.sc is not used).
+// Same computation in one kernel: one thread-block cluster per query head
+// splits the window across its CTAs and combines the exact softmax statistics
+// through distributed shared memory (no global scratch).
 void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s);
+// Whether launch_attn_decode_cluster runs the cluster kernel for this shape
+// (rotary: the fused prologue's rotary width, 0 when not fused).  When it
+// does not, it falls back to launch_attn_decode, which needs a.sc and does
+// not fuse the prologue.
+bool attn_decode_cluster_fits(int Hq, int Hkv, int d, int window, int cap, int rotary);
 
 struct AttnPrefillArgs {
   int32_t S = 0;
@@ -179,7 +186,8 @@ void launch_copy_rows(const int32_t* src, int32_t* dst, size_t n, cudaStream_t s
 void launch_synth(void* dst, int32_t width, int32_t rank, int64_t n, int64_t cols, uint64_t key, cudaStream_t s);
 
 int sm_count();
-// per-device one-time kernel attributes (call with the device current, outside stream capture)
+// one-time kernel attributes of the current device (idempotent; call outside
+// stream capture before the first launch on a device)
 void kernels_init();
 // nonzero when a bounded pipeline wait in a streamed kernel gave up (reset: clear it)
 int stream_error_flag(bool reset);

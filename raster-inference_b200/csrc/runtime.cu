@@ -947,7 +947,8 @@ static const int32_t* decode_layer(Ctx& c, Seq& q, int l, const int32_t* cur, Pe
   aa.rows_per_split = 64;
   // The fused step normalizes, rotates and appends inside the attention
   // kernel; the routine-granular path keeps the separate qkv_post kernel.
-  const bool fuse_qkv = pend != nullptr && lc.rotary <= 512;
+  const bool fuse_qkv =
+      pend != nullptr && attn_decode_cluster_fits(m.Hq, lc.kv_heads, d, lc.window, q.cap, lc.rotary);
   if (fuse_qkv) {
     aa.fuse.q_in = w.q;
     aa.fuse.k_in = qa.k_in;
@@ -1725,6 +1726,7 @@ int32_t rdet_commitment(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t lay
 int32_t rdet_det_gemv(const int32_t* x, const void* w, int32_t width, uint32_t rows, uint32_t cols, int32_t* y,
                       void* stream) {
   return guard([&] {
+    kernels_init();
     REQUIRE(x && w && y, RDET_E_INVALID, "null argument");
     REQUIRE(width == 16 || width == 32, RDET_E_INVALID, "width must be 16 or 32");
     REQUIRE(rows > 0 && cols > 0 && cols <= 49152, RDET_E_RANGE, "unsupported GEMV shape");
@@ -1748,6 +1750,7 @@ int32_t rdet_det_attention_decode(const int32_t* q, const int32_t* k_cache, cons
                                              uint32_t head_dim, uint32_t position, uint32_t window, int32_t* out,
                                              void* stream) {
   return guard([&] {
+    kernels_init();
     AttnDecodeArgs a;
     attn_entry_args(a, q, k_cache, v_cache, cap, num_heads, num_kv_heads, head_dim, position, window, out);
     int dev = 0;
@@ -1778,7 +1781,7 @@ int32_t rdet_det_attention_decode(const int32_t* q, const int32_t* k_cache, cons
       o.sc.stride = o.rows;
     }
     a.sc = o.sc;
-    launch_attn_decode(a, static_cast<cudaStream_t>(stream));
+    launch_attn_decode_cluster(a, static_cast<cudaStream_t>(stream));
     CK(cudaGetLastError());
   });
 }
@@ -1791,6 +1794,7 @@ int32_t rdet_det_attention_decode_noalloc(const int32_t* q, const int32_t* k_cac
                                           uint32_t head_dim, uint32_t position, uint32_t window, int32_t* out,
                                           void* stream) {
   return guard([&] {
+    kernels_init();
     AttnDecodeArgs a;
     attn_entry_args(a, q, k_cache, v_cache, cap, num_heads, num_kv_heads, head_dim, position, window, out);
     const int rows = attn_rows(position, window);
@@ -1819,6 +1823,7 @@ int32_t rdet_det_attention_decode_noalloc(const int32_t* q, const int32_t* k_cac
 int32_t rdet_det_linear(const int32_t* x, uint32_t n_rows_x, const void* w, int32_t width, uint32_t rows,
                         uint32_t cols, int32_t* y, void* stream) {
   return guard([&] {
+    kernels_init();
     REQUIRE(x && w && y, RDET_E_INVALID, "null argument");
     REQUIRE(width == 16 || width == 32, RDET_E_INVALID, "width must be 16 or 32");
     REQUIRE(rows > 0 && cols > 0 && n_rows_x > 0, RDET_E_RANGE, "unsupported linear shape");

@@ -88,7 +88,11 @@ def attention_case(rng, heads, kv_heads, d, cap, position, window, scale=1 << 17
 
 @pytest.mark.parametrize("heads,kv_heads,d,cap,position,window", [
     (2, 1, 2, 16, 0, 0), (4, 2, 16, 100, 57, 8), (8, 2, 256, 600, 599, 512), (8, 2, 512, 4400, 4351, 0),
-    (8, 1, 64, 300, 130, 0), (3, 3, 48, 70, 69, 1)])
+    (8, 1, 64, 300, 130, 0), (3, 3, 48, 70, 69, 1),
+    # fewer window rows than cluster CTAs; a head dim below the 16-byte chunk
+    # grid; many query heads (several waves of clusters); the first tiles of a
+    # sliding window
+    (8, 2, 512, 64, 5, 0), (4, 4, 192, 2000, 1999, 0), (16, 4, 128, 3100, 3099, 0), (8, 2, 256, 40, 20, 512)])
 def test_attention_decode_bit_exact(heads, kv_heads, d, cap, position, window):
     rng = np.random.default_rng(position + d)
     q, k, v, ref = attention_case(rng, heads, kv_heads, d, cap, position, window)
@@ -114,3 +118,34 @@ def test_attention_decode_ties_keep_first_max():
                               out.data_ptr())
     torch.cuda.synchronize()
     assert np.array_equal(out.cpu().numpy(), ref)
+
+
+FRESH_PROCESS_SCRIPT = r"""
+import os, sys, numpy as np, torch
+root = sys.argv[2]
+sys.path[:0] = [sys.argv[1], os.path.join(root, "tests", "golden"), os.path.join(root, "oracle"), root]
+from helpers import rdet
+import oracle as O
+from test_gpu_kernels import attention_case, dev
+rng = np.random.default_rng(5)
+for heads, kv, d, cap, pos, win in [(8, 2, 256, 700, 650, 512), (8, 2, 512, 300, 299, 0)]:
+    q, k, v, ref = attention_case(rng, heads, kv, d, cap, pos, win)
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    out = torch.zeros((heads, d), dtype=torch.int32, device="cuda")
+    rdet.det_attention_decode(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), cap, heads, kv, d, pos, win, out.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), ref), (heads, kv, d, pos, win)
+print("FRESH-OK")
+"""
+
+
+def test_kernel_entries_in_a_fresh_process():
+    # the kernel-level entry points set up their device on first use: no
+    # model needs to have been opened in the process
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    r = subprocess.run([sys.executable, "-c", FRESH_PROCESS_SCRIPT, here, os.path.dirname(here)],
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "FRESH-OK" in r.stdout, r.stdout + r.stderr
