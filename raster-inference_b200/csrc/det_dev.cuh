@@ -27,14 +27,18 @@ namespace rdet {
 constexpr int32_t kOneAct = 1 << 16;
 constexpr int64_t kOneAcc = (int64_t)1 << 32;
 
-// ops.rs:770 + :445 — floor shift by 16 then ties-to-even on the low half.
+// ops.rs:770 + :445 — floor shift by 16 then ties-to-even on the low half,
+// on the two 32-bit words of a: q = low word of a >> 16; the quotient fits
+// in i32 iff bits 47..63 of a all equal q's sign bit; the dropped half r
+// rounds up iff r + 0x7fff + (q & 1) carries into bit 16.
 RDET_HD int32_t requantize(int64_t a) {
-  int64_t q = a >> 16;
-  uint32_t r = (uint32_t)a & 0xffffu;
-  q += (r > 0x8000u) | ((r == 0x8000u) & (uint32_t)q & 1u);
-  q = q < (int64_t)INT32_MIN ? (int64_t)INT32_MIN : q;
-  q = q > (int64_t)INT32_MAX ? (int64_t)INT32_MAX : q;
-  return (int32_t)q;
+  const uint32_t lo = (uint32_t)a;
+  const int32_t hi = (int32_t)(a >> 32);
+  const int32_t q = (int32_t)(((uint32_t)hi << 16) | (lo >> 16));
+  const uint32_t inc = ((lo & 0xffffu) + 0x7fffu + ((uint32_t)q & 1u)) >> 16;
+  if ((hi >> 15) != (q >> 31)) return hi < 0 ? INT32_MIN : INT32_MAX;
+  if (q == INT32_MAX && inc) return INT32_MAX;
+  return q + (int32_t)inc;
 }
 
 // ops.rs:770 for an arbitrary shift in [1, 63]

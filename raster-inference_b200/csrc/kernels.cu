@@ -612,9 +612,11 @@ int stream_error_flag(bool reset) {
 #ifndef RDET_GEMV3_NCH
 #define RDET_GEMV3_NCH 10
 #endif
-#ifndef RDET_GEMV3_CTAS_PER_SM
-#define RDET_GEMV3_CTAS_PER_SM 2
-#endif
+// Two shapes of the same kernel: 256 threads x 2 CTAs per SM, and 512 x 1.
+// Every CTA builds the input vector itself; the 512-thread shape halves that
+// redundant prologue work per SM and measured fastest over a whole decode
+// step, so the launcher uses it throughout.
+constexpr int kG3ThreadsPerSm = 512;
 #ifndef RDET_GEMV3_NCH_W32
 #define RDET_GEMV3_NCH_W32 6
 #endif
@@ -742,8 +744,8 @@ __device__ __forceinline__ void g3_epilogue(const GemvArgs& a, const G3Item& it,
   }
 }
 
-template <int WB>
-__global__ void __launch_bounds__(kGemvThreads, RDET_GEMV3_CTAS_PER_SM) gemv3_kernel(const GemvArgs a, int per_item) {
+template <int WB, int THREADS>
+__global__ void __launch_bounds__(THREADS, kG3ThreadsPerSm / THREADS) gemv3_kernel(const GemvArgs a, int per_item) {
   // Weights and norm gains never depend on earlier kernels: the first piece
   // of this warp's first item and the gains are requested before waiting on
   // the preceding grid.
@@ -834,11 +836,12 @@ static bool launch_gemv3(const GemvArgs& a, cudaStream_t s) {
   }
   const int WB = width / 8;
   if (((long)a.K * WB) % 16 != 0) return false;
-  // two rows per warp item unless that would leave most warp slots idle
-  const int warps = kGemvThreads / 32;
-  const int cap = sm_count() * RDET_GEMV3_CTAS_PER_SM;
   int rows = 0;
   for (int j = 0; j < a.nseg; ++j) rows += a.seg[j].w.rows;
+  const int threads = 512;
+  // two rows per warp item unless that would leave most warp slots idle
+  const int warps = threads / 32;
+  const int cap = sm_count() * (kG3ThreadsPerSm / threads);
   const int per_item = (!a.pair_geglu && rows < cap * warps) ? 1 : 2;
   int items = 0;
   if (a.pair_geglu) items = a.seg[0].w.rows;
@@ -849,11 +852,19 @@ static bool launch_gemv3(const GemvArgs& a, cudaStream_t s) {
   const size_t smem = (size_t)a.K * 4 * gemv_pro_vectors(a.pro);
   if (smem > 200 * 1024) return false;
   if (smem > 48 * 1024) {
-    cudaFuncSetAttribute(gemv3_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(gemv3_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gemv3_kernel<2, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gemv3_kernel<4, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gemv3_kernel<2, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gemv3_kernel<4, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   }
-  if (WB == 2) launch_k(gemv3_kernel<2>, dim3(blocks), dim3(kGemvThreads), smem, s, a, per_item);
-  else launch_k(gemv3_kernel<4>, dim3(blocks), dim3(kGemvThreads), smem, s, a, per_item);
+  const dim3 grid(blocks), block(threads);
+  if (WB == 2) {
+    if (threads == 512) launch_k(gemv3_kernel<2, 512>, grid, block, smem, s, a, per_item);
+    else launch_k(gemv3_kernel<2, 256>, grid, block, smem, s, a, per_item);
+  } else {
+    if (threads == 512) launch_k(gemv3_kernel<4, 512>, grid, block, smem, s, a, per_item);
+    else launch_k(gemv3_kernel<4, 256>, grid, block, smem, s, a, per_item);
+  }
   return true;
 }
 
@@ -1372,6 +1383,7 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
   __shared__ int32_t wm[kAcWarps][GC], wi[kAcWarps][GC];
   __shared__ int64_t ws[kAcWarps][GC];
   __shared__ int32_t cs_tab[256], sn_tab[256];
+  __shared__ int32_t vmx[GC][128];  // first-max V row, this CTA's output dims
   __shared__ int s_fail;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const AttnFuse& f = a.fuse;
@@ -1575,17 +1587,30 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
     if (lane == 0) { g_max[g] = m; g_idx[g] = mi; }
   }
   __syncthreads();
-  // ---- phase 2: exp terms, local sums
+  // the combine's residual row v[first max], this CTA's dims, fetched early
+  const int d0 = (int)((int64_t)d * rank / CL), d1 = (int)((int64_t)d * (rank + 1) / CL);
+  const int per = d1 - d0;
+  for (int e = tid; e < GC * per; e += kAcThreads) {
+    const int g = e / per, dim = d0 + e % per;
+    const int r = start + g_idx[g];
+    if (new_row && r == pos) vmx[g][e % per] = kvrow[d + dim];
+    else cp_async4(&vmx[g][e % per], a.v_cache + (head_base + r) * d + dim);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  // ---- phase 2: exp terms and local sums, (head, row) pairs in parallel
+  {
+    int64_t sum[GC];
 #pragma unroll
-  for (int g = 0; g < GC; ++g) {
-    uint64_t sum = 0;
-    for (int j = tid; j < rows; j += kAcThreads) {
-      const int64_t e = exp_term(sc[g * rmax + j], g_max[g]);
-      ex[g * rmax + j] = e;
-      sum += (uint64_t)e;
+    for (int g = 0; g < GC; ++g) sum[g] = 0;
+    for (int e = tid; e < GC * rows; e += kAcThreads) {
+      const int g = e / rows, j = e - g * rows;
+      const int64_t x = exp_term(sc[g * rmax + j], g_max[g]);
+      ex[g * rmax + j] = x;
+#pragma unroll
+      for (int h = 0; h < GC; ++h) sum[h] += h == g ? x : 0;
     }
-    sum = (uint64_t)warp_sum64((int64_t)sum);
-    if (lane == 0) ws[warp][g] = (int64_t)sum;
+    const int64_t t = warp_multi_sum<GC>(sum, lane);
+    if (lane % (32 / GC) == 0) ws[warp][lane / (32 / GC)] = t;
   }
   __syncthreads();
   if (tid < GC) {
@@ -1601,16 +1626,19 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
   }
   __syncthreads();
   // ---- phase 3: weights, local weight sums, partial weighted V sums
+  {
+    int64_t wsum[GC];
 #pragma unroll
-  for (int g = 0; g < GC; ++g) {
-    int64_t wsum = 0;
-    for (int j = tid; j < rows; j += kAcThreads) {
+    for (int g = 0; g < GC; ++g) wsum[g] = 0;
+    for (int e = tid; e < GC * rows; e += kAcThreads) {
+      const int g = e / rows, j = e - g * rows;
       const int32_t w = softmax_weight(ex[g * rmax + j], g_sum[g]);
       sc[g * rmax + j] = w;
-      wsum += w;
+#pragma unroll
+      for (int h = 0; h < GC; ++h) wsum[h] += h == g ? w : 0;
     }
-    wsum = warp_sum64(wsum);
-    if (lane == 0) ws[warp][g] = wsum;
+    const int64_t t = warp_multi_sum<GC>(wsum, lane);
+    if (lane % (32 / GC) == 0) ws[warp][lane / (32 / GC)] = t;
   }
   __syncthreads();
   if (tid < GC) {
@@ -1671,9 +1699,9 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
     const int64_t t = warp_sum64(v);
     if (lane == 0) g_res[warp] = sub_sat(kOneAct, t > INT32_MAX ? INT32_MAX : (int32_t)t);
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
-  const int d0 = (int)((int64_t)d * rank / CL), d1 = (int)((int64_t)d * (rank + 1) / CL);
-  const int per = d1 - d0, nel = GC * per, epw = kAcThreads / CL;
+  const int nel = GC * per, epw = kAcThreads / CL;
   for (int base = 0; base < nel; base += epw) {
     const int e = base + tid / CL, r = tid % CL;
     int64_t v = 0;
@@ -1685,9 +1713,7 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
     }
     for (int o = CL >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     if (r == 0 && e < nel) {
-      const int32_t* vmax =
-          (new_row && start + g_idx[g] == pos) ? kvrow + d : a.v_cache + (head_base + start + g_idx[g]) * d;
-      v += (int64_t)vmax[dim] * g_res[g];
+      v += (int64_t)vmx[g][dim - d0] * g_res[g];
       a.out[(size_t)(qh0 + g) * d + dim] = requantize(v);
     }
   }

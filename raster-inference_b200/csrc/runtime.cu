@@ -969,6 +969,7 @@ static const int32_t* decode_layer(Ctx& c, Seq& q, int l, const int32_t* cur, Pe
   go.seg[0].w = L.o;
   go.seg[0].y = w.attn;
   go.a = w.comb;
+
   launch_gemv(go, s);
   // t1 = x + norm(attn); MLP input = norm(t1)
   GemvArgs gg;
@@ -995,6 +996,7 @@ static const int32_t* decode_layer(Ctx& c, Seq& q, int l, const int32_t* cur, Pe
     gp.a = w.attn; gp.res = w.t1; gp.g1 = L.post_ff_ln; gp.eps = c.eps; gp.t_out = w.t2;
     gp.seg[0].w = L.ple_gate; gp.seg[0].y = w.g; gp.seg[0].epi = kEpiGeluMul;
     gp.seg[0].vec = w.ple_all + (size_t)l * m.P;
+
     launch_gemv(gp, s);
     GemvArgs gq;
     gq.K = m.P;

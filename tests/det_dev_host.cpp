@@ -70,6 +70,18 @@ extern "C" int64_t rdet_host_check(const char* fn, uint64_t seed, int64_t n) {
       int64_t a = g.wide(64, true);
       bad += rdet::requantize(a) != dor::requantize(a);
     }
+  } else if (!strcmp(fn, "requantize_edges")) {
+    // every value within 2^17 of the saturation and sign boundaries, and of
+    // the ties around them
+    const int64_t centers[] = {0, (int64_t)1 << 47, -((int64_t)1 << 47), ((int64_t)INT32_MAX << 16),
+                               ((int64_t)INT32_MIN << 16), INT64_MAX - (1 << 17), INT64_MIN + (1 << 17),
+                               (int64_t)1 << 32, -((int64_t)1 << 32)};
+    for (int64_t c : centers)
+      for (int64_t o = -(1 << 17); o <= (1 << 17); ++o) {
+        const int64_t a = c + o;
+        bad += rdet::requantize(a) != dor::requantize(a);
+      }
+    (void)n;
   } else if (!strcmp(fn, "rshift_rte")) {
     for (int64_t i = 0; i < n; ++i) {
       int64_t a = g.wide(64, true);

@@ -35,6 +35,7 @@ CASES = [
     ("inv_sqrt_acc", 2_000_000),
     ("rms_norm_scale", 200_000),
     ("requantize", 2_000_000),
+    ("requantize_edges", 1),
     ("rshift_rte", 2_000_000),
     ("div_act", 1_000_000),
     ("div_acc_by_u32", 1_000_000),
