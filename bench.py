@@ -177,43 +177,90 @@ def run_reference(args, rank):
 # ---------------------------------------------------------------------------
 # GPU
 # ---------------------------------------------------------------------------
-def gemv_roofline(torch, rdet, cfg, device, rounds=12):
-    """det-GEMV at the E4B projection shapes, timed per launch with CUDA events
-    on the stream the kernel is launched on; weights are distinct matrices
-    (one layer's worth, ~185 MB > L2), so every launch streams from HBM."""
+def e4b_gemv_shapes(cfg):
     t = cfg["text_config"]
     H, F, Hq, kv, d, dg, V, P, L = (t["hidden_size"], t["intermediate_size"], t["num_attention_heads"],
                                     t["num_key_value_heads"], t["head_dim"], t["global_head_dim"],
                                     t["vocab_size"], t["hidden_size_per_layer_input"], t["num_hidden_layers"])
-    shapes = {"q": (Hq * d, H), "k": (kv * d, H), "v": (kv * d, H), "o": (H, Hq * d), "gate": (F, H),
-              "up": (F, H), "down": (H, F), "q_full": (Hq * dg, H), "o_full": (H, Hq * dg),
-              "ple_model_proj": (L * P, H), "lm_head": (V, H)}
+    return {"q": (Hq * d, H), "k": (kv * d, H), "v": (kv * d, H), "o": (H, Hq * d), "gate": (F, H),
+            "up": (F, H), "down": (H, F), "q_full": (Hq * dg, H), "o_full": (H, Hq * dg),
+            "ple_model_proj": (L * P, H), "lm_head": (V, H)}
+
+
+def gemv_roofline(torch, rdet, cfg, device, copies=8, rounds=3):
+    """det-GEMV (gemv3_kernel) at the E4B projection shapes.  For each shape,
+    `copies` launches over distinct weight copies run back to back on one
+    stream (as inside the decode step) between two CUDA events on that
+    stream; the mean per launch is the launch duration.  Between two uses of
+    one copy every other shape streams (> L2), so each launch reads HBM."""
+    shapes = e4b_gemv_shapes(cfg)
     g = torch.Generator(device=f"cuda:{device}").manual_seed(3)
-    mats = {k: torch.randint(-32768, 32768, s, dtype=torch.int16, device=f"cuda:{device}", generator=g)
-            for k, s in shapes.items()}
-    xs = {k: torch.randint(-(1 << 20), 1 << 20, (s[1],), dtype=torch.int32, device=f"cuda:{device}", generator=g)
+    dev = f"cuda:{device}"
+    mats = {k: [torch.randint(-32768, 32768, s, dtype=torch.int16, device=dev, generator=g)
+                for _ in range(copies if k != "lm_head" else 2)] for k, s in shapes.items()}
+    xs = {k: torch.randint(-(1 << 20), 1 << 20, (s[1],), dtype=torch.int32, device=dev, generator=g)
           for k, s in shapes.items()}
-    ys = {k: torch.empty(s[0], dtype=torch.int32, device=f"cuda:{device}") for k, s in shapes.items()}
+    ys = {k: torch.empty(s[0], dtype=torch.int32, device=dev) for k, s in shapes.items()}
     stream = torch.cuda.Stream(device=device)
     per = {k: [] for k in shapes}
     with torch.cuda.stream(stream):
-        for r in range(rounds + 2):
+        for r in range(rounds + 1):
             for k, (n, kk) in shapes.items():
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-                rdet.det_gemv(xs[k].data_ptr(), mats[k].data_ptr(), 16, n, kk, ys[k].data_ptr(), stream.cuda_stream)
+                for m in mats[k]:
+                    rdet.det_gemv(xs[k].data_ptr(), m.data_ptr(), 16, n, kk, ys[k].data_ptr(), stream.cuda_stream)
                 e1.record(stream)
-                if r >= 2:
-                    per[k].append((e0, e1))
+                if r >= 1:
+                    per[k].append((e0, e1, len(mats[k])))
     stream.synchronize()
     out, tot_b, tot_t = {}, 0.0, 0.0
     for k, (n, kk) in shapes.items():
-        ms = statistics.mean(a.elapsed_time(b) for a, b in per[k])
+        ms = statistics.mean(a.elapsed_time(b) / c for a, b, c in per[k])
         b = n * kk * 2 + kk * 4 + n * 4
         out[k] = {"rows": n, "cols": kk, "us": ms * 1000, "gbs": b / (ms * 1e-3) / 1e9}
         tot_b += b
         tot_t += ms * 1e-3
     return out, tot_b / tot_t / 1e9, tot_b / len(shapes), tot_t / len(shapes)
+
+
+def run_kernel_case(args):
+    """A few launches of one kernel at E4B shapes, sized for an ncu capture
+    (a few GB on the device): --kernel-case gemv runs gemv3 on the q, down and
+    lm_head shapes; --kernel-case attn runs the cluster decode attention of a
+    sliding and a full layer at context --ctx."""
+    import torch
+    rdet = importlib.import_module("raster-inference_b200")
+    cfg = load_config()
+    t = cfg["text_config"]
+    dev = "cuda:0"
+    g = torch.Generator(device=dev).manual_seed(5)
+    if args.kernel_case == "gemv":
+        shapes = e4b_gemv_shapes(cfg)
+        for k in ("q", "down", "lm_head"):
+            n, kk = shapes[k]
+            w = torch.randint(-32768, 32768, (n, kk), dtype=torch.int16, device=dev, generator=g)
+            x = torch.randint(-(1 << 20), 1 << 20, (kk,), dtype=torch.int32, device=dev, generator=g)
+            y = torch.empty(n, dtype=torch.int32, device=dev)
+            rdet.det_gemv(x.data_ptr(), w.data_ptr(), 16, n, kk, y.data_ptr())
+            torch.cuda.synchronize()
+            print(f"gemv {k}: rows {n} cols {kk} bytes {n * kk * 2 + kk * 4 + n * 4}")
+    else:
+        Hq, kv, d, dg, win = (t["num_attention_heads"], t["num_key_value_heads"], t["head_dim"],
+                              t["global_head_dim"], t["sliding_window"])
+        ctx = args.ctx
+        for name, hd, w in (("sliding", d, win), ("full", dg, 0)):
+            cap = ctx + 64
+            q = torch.randint(-(1 << 17), 1 << 17, (Hq, hd), dtype=torch.int32, device=dev, generator=g)
+            kc = torch.randint(-(1 << 17), 1 << 17, (kv, cap, hd), dtype=torch.int32, device=dev, generator=g)
+            vc = torch.randint(-(1 << 20), 1 << 20, (kv, cap, hd), dtype=torch.int32, device=dev, generator=g)
+            out = torch.empty((Hq, hd), dtype=torch.int32, device=dev)
+            pos = ctx - 1
+            rdet.det_attention_decode(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), cap, Hq, kv, hd, pos, w,
+                                      out.data_ptr())
+            torch.cuda.synchronize()
+            rows = min(pos + 1, w) if w else pos + 1
+            print(f"attn {name}: heads {Hq}/{kv} head_dim {hd} rows {rows} kv_bytes {2 * kv * rows * hd * 4}")
 
 
 def run_ours(args, rank, world, local_rank):
@@ -283,7 +330,9 @@ def run_ours(args, rank, world, local_rank):
     tpath = os.path.join(ROOT, "profiles", "gemv_traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
-            traffic = json.load(f).get("dram_bytes_per_launch_e4b_mix")
+            ratio = json.load(f).get("dram_to_algorithmic_bytes")
+        if ratio:
+            traffic = ratio * bytes_per_launch
     weight_bytes = model.weight_bytes
     if dist:
         dist.barrier()
@@ -305,7 +354,7 @@ def run_ours(args, rank, world, local_rank):
         "prefill": {"tokens": ctx, "tok_s": ctx / prefill_s, "seconds": prefill_s},
         "e2e": e2e,
         "gpu_launches": kernels_per_step * args.steps,
-        "roofline": {"bound": "hbm", "kernel": "rdet::gemv_kernel", "achieved": gbs, "peak": peak,
+        "roofline": {"bound": "hbm", "kernel": "rdet::gemv3_kernel", "achieved": gbs, "peak": peak,
                      "unit": "GB/s", "frac": gbs / peak, "peak_kind": peak_kind,
                      "traffic": traffic, "algorithmic_bytes_per_launch": bytes_per_launch,
                      "us_per_launch": sec_per_launch * 1e6,
@@ -333,7 +382,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-case", choices=["gemv", "attn"],
+                    help="run a few launches of one kernel at E4B shapes for an ncu capture, then exit")
     args = ap.parse_args()
+    if args.kernel_case:
+        run_kernel_case(args)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
