@@ -41,6 +41,8 @@ typedef struct rdet_opts {
   uint32_t flags;        /* RDET_FLAG_* */
 } rdet_opts;
 #define RDET_FLAG_LAYER_COMMITMENTS 1u /* keep per-layer prefill commitments */
+#define RDET_FLAG_NO_TENSOR_CORES 2u   /* prefill on CUDA cores only: no weight byte planes
+                                          (saves one extra copy of the projection weights) */
 
 typedef struct rdet_model_info {
   uint32_t hidden_size, vocab_size, num_layers, num_heads, ple_dim, intermediate_size;
@@ -130,7 +132,13 @@ int32_t rdet_commitment(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t lay
  * det GEMV / linear: y[s, r] = requantize(sum_k x[s, k] * w[r, k]) with exact
  * wrapping i64 accumulation (det_kernels.rs:108-203 det_linear_rows_into /
  * det_linear_slab).  w is row-major [rows, cols], i16 (width 16) or i32
- * (width 32).  stream: a cudaStream_t or NULL. */
+ * (width 32).  stream: a cudaStream_t or NULL.
+ * rdet_det_linear with at least 32 rows of x, an i16 w whose cols are a
+ * multiple of 16 (at most 32768) and 16-byte aligned x and w runs on the
+ * tensor cores (exact byte-limb decomposition, same result); the byte planes
+ * live in a per-device scratch that the library allocates on first use and
+ * grows as needed, shared by all such calls on the device (calls that overlap
+ * on the GPU race on it). */
 int32_t rdet_det_gemv(const int32_t* x, const void* w, int32_t width, uint32_t rows, uint32_t cols, int32_t* y,
                       void* stream);
 int32_t rdet_det_linear(const int32_t* x, uint32_t n_rows_x, const void* w, int32_t width, uint32_t rows,
@@ -170,6 +178,11 @@ int32_t rdet_det_attention_decode_noalloc(const int32_t* q, const int32_t* k_cac
 
 /* The CUDA stream (cudaStream_t) on which the context launches all of its
  * work, for callers that order their own work or CUDA events against it. */
+/* 1 when this context's prefill linears run on the tcgen05 tensor cores (an
+ * sm_100 device, the context opened without RDET_FLAG_NO_TENSOR_CORES and at
+ * least one eligible weight), else 0.  Prompts shorter than 32 tokens use the
+ * CUDA-core linear either way.  No counterpart in the reference. */
+int32_t rdet_tensor_core_prefill(rdet_ctx* ctx);
 int32_t rdet_get_stream(rdet_ctx* ctx, void** stream);
 /* Number of kernels in one captured decode_transition (the sequence's decode
  * CUDA graph; captured on the first rdet_decode / rdet_generate). */

@@ -29,6 +29,7 @@ LIB_PATH = os.path.join(_HERE, "librdet.so")
 RDET_OK, RDET_NONE = 0, 1
 BUF_EMBEDDING, BUF_HIDDEN, BUF_LOGITS, BUF_LAYER_OUTPUT, BUF_KV, BUF_KV_K, BUF_KV_V = range(7)
 FLAG_LAYER_COMMITMENTS = 1
+FLAG_NO_TENSOR_CORES = 2
 
 # Exported symbols, in the order include/rdet.h declares them.
 SYMBOLS = [
@@ -36,7 +37,7 @@ SYMBOLS = [
     "rdet_seq_position", "rdet_embed", "rdet_prefill", "rdet_prefill_begin", "rdet_prefill_range",
     "rdet_prefill_finalize", "rdet_select", "rdet_decode", "rdet_decode_begin", "rdet_decode_range",
     "rdet_decode_finalize", "rdet_generate", "rdet_read", "rdet_commitment", "rdet_det_gemv", "rdet_det_linear",
-    "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_get_stream", "rdet_seq_kernels_per_step", "rdet_last_error",
+    "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_get_stream", "rdet_tensor_core_prefill", "rdet_seq_kernels_per_step", "rdet_last_error",
     "rdet_version",
 ]
 
@@ -96,6 +97,7 @@ def lib() -> C.CDLL:
         "rdet_det_attention_decode": [p, p, p, u32, u32, u32, u32, u32, u32, p, p],
         "rdet_det_attention_decode_noalloc": [p, p, p, u32, u32, u32, u32, u32, u32, p, p],
         "rdet_get_stream": [p, p],
+        "rdet_tensor_core_prefill": [p],
         "rdet_seq_kernels_per_step": [p, p],
         "rdet_last_error": [C.c_char_p, sz],
     }
@@ -134,8 +136,10 @@ class Model:
         self.weight_bytes = info.weight_bytes
 
     @classmethod
-    def open(cls, model_dir: str, device: int = 0, max_prefill: int = 0, layer_commitments: bool = False):
-        opts = Opts(device, max_prefill, FLAG_LAYER_COMMITMENTS if layer_commitments else 0)
+    def open(cls, model_dir: str, device: int = 0, max_prefill: int = 0, layer_commitments: bool = False,
+             tensor_cores: bool = True):
+        flags = (FLAG_LAYER_COMMITMENTS if layer_commitments else 0) | (0 if tensor_cores else FLAG_NO_TENSOR_CORES)
+        opts = Opts(device, max_prefill, flags)
         h = C.c_void_p()
         _check(lib().rdet_open(model_dir.encode(), C.byref(opts), C.byref(h)))
         with open(os.path.join(model_dir, "config.json")) as f:
@@ -144,8 +148,9 @@ class Model:
 
     @classmethod
     def synthetic(cls, config: dict, seed: int, width: int = 16, device: int = 0, max_prefill: int = 0,
-                  layer_commitments: bool = False):
-        opts = Opts(device, max_prefill, FLAG_LAYER_COMMITMENTS if layer_commitments else 0)
+                  layer_commitments: bool = False, tensor_cores: bool = True):
+        flags = (FLAG_LAYER_COMMITMENTS if layer_commitments else 0) | (0 if tensor_cores else FLAG_NO_TENSOR_CORES)
+        opts = Opts(device, max_prefill, flags)
         h = C.c_void_p()
         _check(lib().rdet_open_synthetic(json.dumps(config).encode(), seed, width, C.byref(opts), C.byref(h)))
         return cls(h, config)
@@ -160,6 +165,11 @@ class Model:
             self.close()
         except Exception:
             pass
+
+    @property
+    def tensor_core_prefill(self) -> bool:
+        """Whether prefill linears of >= 32 tokens run on the tcgen05 tensor cores."""
+        return bool(lib().rdet_tensor_core_prefill(self._h))
 
     @property
     def stream(self) -> int:

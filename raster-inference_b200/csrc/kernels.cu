@@ -548,6 +548,7 @@ void kernels_init() {
   if ((size_t)dev < done.size() && done[dev]) return;
   stream_set_attrs();
   attn_cluster_init();
+  tc_init();
   if ((size_t)dev >= done.size()) done.resize(dev + 1, 0);
   done[dev] = 1;
 }
@@ -559,7 +560,7 @@ int stream_error_flag(bool reset) {
     int z = 0;
     cudaMemcpyToSymbol(g_stream_err, &z, sizeof(int));
   }
-  return v;
+  return v | tc_error_flag(reset);
 }
 
 // Plans and launches the streamed GEMV; returns false when the launch does not

@@ -64,6 +64,40 @@ void launch_linear(const int32_t* X, int32_t S, const DevMat& w, int32_t* Y, int
 void launch_linear_geglu(const int32_t* X, int32_t S, const DevMat& wg, const DevMat& wu, int32_t* Y,
                          cudaStream_t s);
 
+// ---- prefill linear on tcgen05 int8 tensor cores (tc_gemm.cu) ------------------
+// Exact: X + 2^31 and W + 2^15 split into unsigned byte planes, byte products
+// on the tensor cores, recombined with row-sum corrections in wrapping i64.
+// Bit-exact with launch_linear / launch_linear_geglu for i16 weights with
+// K a multiple of 16 and K <= kTcMaxK.
+constexpr int kTcMaxK = 32768;
+struct TcWeight {           // byte planes of one weight matrix (or a gate/up pair)
+  alignas(64) unsigned char map[128];  // TMA tensor map of the planes
+  uint8_t* planes = nullptr;           // [2][nrows][K]
+  uint64_t* rowsum = nullptr;          // [nrows] sum over k of W + 2^15
+  int32_t N = 0, K = 0, nrows = 0;
+  bool pair = false;                   // rows interleave gate and up in blocks of 48
+};
+struct TcAct {              // byte planes of one activation matrix
+  alignas(64) unsigned char map[128];
+  uint8_t* planes = nullptr;           // [4][S][K]
+  uint64_t* rowsum = nullptr;          // [S] sum over k of X + 2^31
+  int32_t S = 0, K = 0;
+};
+bool tc_supported();                         // current device is sm_100
+bool tc_weight_eligible(const DevMat& w);
+size_t tc_weight_bytes(int rows, int K, bool pair);
+// Builds the planes of g (and u, for the gate/up pair) into `mem`
+// (tc_weight_bytes); returns false if the tensor map cannot be encoded.
+bool tc_prepare_weight(TcWeight& t, const DevMat& g, const DevMat* u, void* mem, cudaStream_t s);
+size_t tc_act_bytes(int S, int K);
+// X [S, K] (16-byte aligned, K % 16 == 0) -> planes in `mem` (tc_act_bytes)
+bool tc_prepare_act(TcAct& a, const int32_t* X, int S, int K, void* mem, cudaStream_t s);
+// Y [S, N] = epilogue(requantize(X W^T)); a pair writes mul_sat(gelu(gate), up)
+void launch_tc_linear(const TcAct& a, const TcWeight& w, int32_t* Y, int32_t epi, const int32_t* vec,
+                      cudaStream_t s);
+void tc_init();  // per-device kernel attributes (called by kernels_init)
+int tc_error_flag(bool reset);  // nonzero when a tensor-core pipeline wait gave up
+
 // ---- row ops -------------------------------------------------------------------
 // y[s] = rmsnorm(x[s], g)   (g == nullptr: weightless value norm)
 void launch_rmsnorm_rows(const int32_t* x, int32_t S, int32_t n, const int32_t* g, int64_t eps, int32_t* y,

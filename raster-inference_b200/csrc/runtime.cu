@@ -385,6 +385,8 @@ struct LayerDev {
   bool has_scalar = false;
   int32_t scalar = 0;
   const int64_t* inv_freq = nullptr;
+  // tensor-core prefill operands (byte planes), built when eligible
+  TcWeight tq, tk, tv, to, tgu, tdown, tpg, tpp;
 };
 
 struct PrefillWs {
@@ -424,6 +426,10 @@ struct Ctx {
   Seq* prefill_owner = nullptr;  // sequence whose routine-granular prefill is in flight
   Seq* decode_owner = nullptr;
   std::vector<void*> live_seqs;  // rdet_seq handles still open on this context
+  bool tc = false;               // prefill linears run on the tensor cores
+  TcWeight t_ple_model;
+  void* tc_act = nullptr;        // activation byte planes of the current linear
+  int tc_act_k = 0;              // largest K the activation planes hold
 
   void* dalloc(size_t bytes) {
     void* p = nullptr;
@@ -694,6 +700,80 @@ static void alloc_workspaces(Ctx& c) {
   CK(cudaMemset(c.d_err, 0, 4));
 }
 
+// Byte planes of every prefill weight the tensor-core linear can take (i16,
+// K a multiple of 16): one more copy of those weights in HBM.
+static void prepare_tensor_cores(Ctx& c) {
+  if ((c.flags & RDET_FLAG_NO_TENSOR_CORES) || !tc_supported()) return;
+  const ModelCfg& m = c.cfg;
+  int kmax = 0;
+  auto prep = [&](TcWeight& t, const DevMat& w, const DevMat* u = nullptr) {
+    if (!w.p || !tc_weight_eligible(w) || (u && (!u->p || !tc_weight_eligible(*u) || u->rows != w.rows ||
+                                                 u->cols != w.cols)))
+      return;
+    void* mem = c.dalloc(tc_weight_bytes(w.rows, w.cols, u != nullptr));
+    REQUIRE(tc_prepare_weight(t, w, u, mem, c.stream), RDET_E_CUDA, "tensor map encoding failed");
+    kmax = std::max(kmax, w.cols);
+  };
+  for (LayerDev& L : c.layers) {
+    prep(L.tq, L.q);
+    if (L.cfg.donor < 0) {
+      prep(L.tk, L.k);
+      if (L.v.p) prep(L.tv, L.v);
+    }
+    prep(L.to, L.o);
+    prep(L.tgu, L.gate, &L.up);
+    prep(L.tdown, L.down);
+    if (m.P > 0) {
+      prep(L.tpg, L.ple_gate);
+      prep(L.tpp, L.ple_proj);
+    }
+  }
+  if (m.P > 0) prep(c.t_ple_model, c.ple_model_proj);
+  if (kmax > 0) {
+    c.tc_act = c.dalloc(tc_act_bytes((int)c.max_prefill, kmax));
+    c.tc_act_k = kmax;
+  }
+  CK(cudaStreamSynchronize(c.stream));
+  CK(cudaGetLastError());
+  c.tc = kmax > 0;
+}
+
+// Prefill linear: tensor cores when the weight has byte planes and the
+// prompt is long enough to fill them, else the CUDA-core kernel.  Both are
+// bit-exact.  `act` carries the activation planes of X between calls that
+// share X (pass the same TcAct with prepared = true).
+constexpr int kTcMinRows = 32;
+struct ActPlanes {
+  TcAct a;
+  bool ready = false;
+};
+static void prefill_linear(Ctx& c, const int32_t* X, int S, const DevMat& w, const TcWeight& t, int32_t* Y,
+                           int32_t epi, const int32_t* vec, ActPlanes* shared = nullptr) {
+  cudaStream_t s = c.stream;
+  if (c.tc && t.planes && S >= kTcMinRows && w.cols <= c.tc_act_k) {
+    ActPlanes local;
+    ActPlanes& ap = shared ? *shared : local;
+    if (!ap.ready) {
+      REQUIRE(tc_prepare_act(ap.a, X, S, w.cols, c.tc_act, s), RDET_E_CUDA, "tensor map encoding failed");
+      ap.ready = true;
+    }
+    launch_tc_linear(ap.a, t, Y, epi, vec, s);
+    return;
+  }
+  launch_linear(X, S, w, Y, epi, vec, s);
+}
+// MLP gate/up pair: Y = mul_sat(gelu(X Wg^T), X Wu^T)
+static void prefill_geglu(Ctx& c, const int32_t* X, int S, const LayerDev& L, int32_t* Y) {
+  cudaStream_t s = c.stream;
+  if (c.tc && L.tgu.planes && S >= kTcMinRows && L.gate.cols <= c.tc_act_k) {
+    TcAct a;
+    REQUIRE(tc_prepare_act(a, X, S, L.gate.cols, c.tc_act, s), RDET_E_CUDA, "tensor map encoding failed");
+    launch_tc_linear(a, L.tgu, Y, kEpiPlain, nullptr, s);
+    return;
+  }
+  launch_linear_geglu(X, S, L.gate, L.up, Y, s);
+}
+
 static void check_err_flag(Ctx& c, const char* what) {
   int32_t e = 0;
   CK(cudaMemcpyAsync(&e, c.d_err, 4, cudaMemcpyDeviceToHost, c.stream));
@@ -727,7 +807,7 @@ static void prefill_begin(Ctx& c, Seq& q, const uint32_t* ids, size_t n) {
   q.prefilled = false;
   launch_embed(w.ids, S, c.emb, c.emb_scale, w.x0, c.d_err, s);
   if (m.P > 0) {
-    launch_linear(w.x0, S, c.ple_model_proj, w.ple_proj, kEpiPlain, nullptr, s);
+    prefill_linear(c, w.x0, S, c.ple_model_proj, c.t_ple_model, w.ple_proj, kEpiPlain, nullptr);
     PleArgs pa;
     pa.S = S; pa.L = m.L; pa.P = m.P; pa.ids = w.ids; pa.proj = w.ple_proj; pa.table = c.ple_table;
     pa.norm = c.ple_proj_norm; pa.eps = c.eps; pa.emb_scale = c.ple_emb_scale; pa.proj_scale = c.ple_proj_scale;
@@ -768,16 +848,17 @@ static void prefill_layer(Ctx& c, Seq& q, int l) {
   int32_t* cur = q.prefill_cur;
   int32_t* other = cur == w.xa ? w.xb : w.xa;
   launch_rmsnorm_rows(cur, S, H, L.in_ln, c.eps, w.nrm, s);
-  launch_linear(w.nrm, S, L.q, w.q, kEpiPlain, nullptr, s);
+  ActPlanes nrm_planes;  // q, k and v read the same normed input
+  prefill_linear(c, w.nrm, S, L.q, L.tq, w.q, kEpiPlain, nullptr, &nrm_planes);
   QkvPostArgs qa;
   qa.S = S; qa.pos = q.d_pos; qa.Hq = m.Hq; qa.Hkv = lc.kv_heads; qa.d = d; qa.rotary = lc.rotary;
   qa.inv_freq = L.inv_freq; qa.q_in = w.q; qa.q_norm = L.q_norm; qa.k_norm = L.k_norm; qa.eps = c.eps;
   qa.q_out = w.qo; qa.cap = q.cap;
   const int32_t *kcache, *vcache;
   if (lc.donor < 0) {
-    launch_linear(w.nrm, S, L.k, w.kraw, kEpiPlain, nullptr, s);
+    prefill_linear(c, w.nrm, S, L.k, L.tk, w.kraw, kEpiPlain, nullptr, &nrm_planes);
     const int32_t* vsrc = w.kraw;  // k_eq_v: V is the raw K projection (det_kernels.rs:517-518)
-    if (L.v.p) { launch_linear(w.nrm, S, L.v, w.vraw, kEpiPlain, nullptr, s); vsrc = w.vraw; }
+    if (L.v.p) { prefill_linear(c, w.nrm, S, L.v, L.tv, w.vraw, kEpiPlain, nullptr, &nrm_planes); vsrc = w.vraw; }
     qa.k_in = w.kraw; qa.v_in = vsrc; qa.k_cache = q.kc[l]; qa.v_cache = q.vc[l];
     kcache = q.kc[l];
     vcache = q.vc[l];
@@ -793,19 +874,19 @@ static void prefill_layer(Ctx& c, Seq& q, int l) {
   aa.k_cache = kcache; aa.v_cache = vcache; aa.cap = q.cap; aa.out = w.comb; aa.scores = w.scores; aa.exps = w.exps;
   aa.scratch_elems = w.scratch_elems;
   launch_attn_prefill(aa, s);
-  launch_linear(w.comb, S, L.o, w.attn, kEpiPlain, nullptr, s);
+  prefill_linear(c, w.comb, S, L.o, L.to, w.attn, kEpiPlain, nullptr);
   bool ple = m.P > 0;
   // t1 = xs + norm(attn)  -> other
   launch_norm_residual_rows(w.attn, cur, S, H, L.post_attn_ln, c.eps, false, 0, other, s);
   launch_rmsnorm_rows(other, S, H, L.pre_ff_ln, c.eps, w.nrm, s);
-  launch_linear_geglu(w.nrm, S, L.gate, L.up, w.hbuf, s);
-  launch_linear(w.hbuf, S, L.down, w.attn, kEpiPlain, nullptr, s);
+  prefill_geglu(c, w.nrm, S, L, w.hbuf);
+  prefill_linear(c, w.hbuf, S, L.down, L.tdown, w.attn, kEpiPlain, nullptr);
   // t2 = t1 + norm(ff) -> cur
   launch_norm_residual_rows(w.attn, other, S, H, L.post_ff_ln, c.eps, !ple && L.has_scalar, L.scalar, cur, s);
   int32_t* result = cur;
   if (ple) {
-    launch_linear(cur, S, L.ple_gate, w.g, kEpiGeluMul, w.ple_all + (size_t)l * S * m.P, s);
-    launch_linear(w.g, S, L.ple_proj, w.pr, kEpiPlain, nullptr, s);
+    prefill_linear(c, cur, S, L.ple_gate, L.tpg, w.g, kEpiGeluMul, w.ple_all + (size_t)l * S * m.P);
+    prefill_linear(c, w.g, S, L.ple_proj, L.tpp, w.pr, kEpiPlain, nullptr);
     launch_norm_residual_rows(w.pr, cur, S, H, L.ple_norm, c.eps, L.has_scalar, L.scalar, other, s);
     result = other;
   }
@@ -1178,6 +1259,13 @@ struct AttnScratchOwned {
   std::vector<void*> ptrs;
 };
 static std::map<int, AttnScratchOwned> g_attn_scratch;
+// byte-plane scratch of the kernel-level tensor-core linear, per device
+struct LinScratch {
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+static std::map<int, LinScratch> g_lin_scratch;
+static std::mutex g_lin_scratch_mu;
 
 static void attn_entry_args(AttnDecodeArgs& a, const int32_t* q, const int32_t* k_cache, const int32_t* v_cache,
                             uint32_t cap, uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
@@ -1333,6 +1421,7 @@ int32_t rdet_open(const char* model_dir, const rdet_opts* opts, rdet_ctx** out) 
     open_common(c, opts);
     build_model(c, tab, false, 0);
     alloc_workspaces(c);
+    prepare_tensor_cores(c);
     *out = h.release();
   });
 }
@@ -1353,6 +1442,7 @@ int32_t rdet_open_synthetic(const char* config_json, uint64_t seed, int32_t widt
     open_common(c, opts);
     build_model(c, tab, true, seed);
     alloc_workspaces(c);
+    prepare_tensor_cores(c);
     *out = h.release();
   });
 }
@@ -1725,6 +1815,11 @@ int32_t rdet_commitment(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t lay
   return rc;
 }
 
+int32_t rdet_tensor_core_prefill(rdet_ctx* ctx) {
+  if (!ctx || !ctx->c) return 0;
+  return ctx->c->tc ? 1 : 0;
+}
+
 int32_t rdet_det_gemv(const int32_t* x, const void* w, int32_t width, uint32_t rows, uint32_t cols, int32_t* y,
                       void* stream) {
   return guard([&] {
@@ -1834,7 +1929,36 @@ int32_t rdet_det_linear(const int32_t* x, uint32_t n_rows_x, const void* w, int3
     m.width = width;
     m.rows = (int)rows;
     m.cols = (int)cols;
-    launch_linear(x, (int)n_rows_x, m, y, kEpiPlain, nullptr, static_cast<cudaStream_t>(stream));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if ((int)n_rows_x >= kTcMinRows && tc_weight_eligible(m) && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+        tc_supported()) {
+      // byte planes of w and x in the per-device scratch, then the tensor-core GEMM
+      int dev = 0;
+      CK(cudaGetDevice(&dev));
+      const size_t wb = (tc_weight_bytes((int)rows, (int)cols, false) + 255) & ~(size_t)255;
+      const size_t need = wb + tc_act_bytes((int)n_rows_x, (int)cols);
+      std::lock_guard<std::mutex> lk(g_lin_scratch_mu);
+      LinScratch& sc = g_lin_scratch[dev];
+      if (sc.bytes < need) {
+        if (sc.p) {
+          CK(cudaDeviceSynchronize());
+          CK(cudaFree(sc.p));
+          sc.p = nullptr;
+          sc.bytes = 0;
+        }
+        CK(cudaMalloc(&sc.p, need));
+        sc.bytes = need;
+      }
+      TcWeight tw;
+      TcAct ta;
+      unsigned char* base = static_cast<unsigned char*>(sc.p);
+      REQUIRE(tc_prepare_weight(tw, m, nullptr, base, s), RDET_E_CUDA, "tensor map encoding failed");
+      REQUIRE(tc_prepare_act(ta, x, (int)n_rows_x, (int)cols, base + wb, s), RDET_E_CUDA,
+              "tensor map encoding failed");
+      launch_tc_linear(ta, tw, y, kEpiPlain, nullptr, s);
+    } else {
+      launch_linear(x, (int)n_rows_x, m, y, kEpiPlain, nullptr, s);
+    }
     CK(cudaGetLastError());
   });
 }

@@ -1,0 +1,482 @@
+// Prefill det linear on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// Y[s, n] = requantize(sum_k X[s, k] * W[n, k])   (wrapping i64 sum; the
+// arithmetic of linear_into / matmul_det in the reference's det path)
+//
+// Exact integer decomposition.  With X_u = X + 2^31 (u32) and W_u = W + 2^15
+// (u16), both non-negative,
+//   sum_k X W = sum_k X_u W_u - 2^15 sum_k X_u - 2^31 sum_k W_u + 2^46 K
+// holds exactly in wrapping i64.  X_u splits into four byte limbs x_a and W_u
+// into two byte limbs w_b (all u8), and
+//   sum_k X_u W_u = sum_{a,b} 2^(8(a+b)) P_ab,   P_ab = sum_k x_a w_b.
+// Each P_ab is an unsigned int8 tensor-core product accumulated in 32 bits.
+//
+// One MMA per activation limb: the B operand stacks the low-byte plane rows
+// of an N tile (96 weight rows) above the high-byte plane rows (N = 192), so
+// MMA a writes [P_a0 | P_a1] into TMEM columns [96a, 96a + 192).  The four
+// regions overlap by 96 columns: column block g = [96g, 96g + 96) accumulates
+// exactly the products with shift 8g (P_g0 + P_(g-1)1), 480 columns in all.
+// A block holds at most two non-negative products of at most 255*255*K each,
+// so its 32-bit accumulator is exact (read as u32) for K < 33025.  The
+// epilogue recombines the five blocks and the two row-sum corrections in
+// wrapping i64 and requantizes: bit-exact with the CUDA-core linear.
+//
+// Pipeline per CTA (one 128 x 96 output tile): warp 4 streams activation limb
+// tiles (4 x 128 x 64 B) and the stacked weight tile (192 x 64 B) with TMA
+// (tiled, 64-byte swizzle, no multicast) into a 4-stage ring; warp 5 issues
+// the MMAs (M=128, N=192, K=32, kind::i8, u8 x u8 -> s32) and frees stages
+// with tcgen05.commit; warps 0-3 zero the accumulator before the first MMA
+// and drain it through tcgen05.ld afterwards.  Every mbarrier wait is bounded
+// and reports a timeout through the library's pipeline error flag.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "det_dev.cuh"
+#include "kernels.h"
+
+namespace rdet {
+
+// set when a bounded pipeline wait gives up (read by tc_error_flag)
+__device__ int g_tc_err = 0;
+
+namespace {
+
+constexpr int kTcM = 128;         // output rows (tokens) per tile
+constexpr int kTcN = 96;          // output columns (weight rows) per tile
+constexpr int kTcNB = 2 * kTcN;   // stacked B rows (low and high byte planes)
+constexpr int kTcKB = 64;         // K bytes per stage (one 64-byte swizzle row)
+constexpr int kTcStages = 4;
+constexpr int kTcATile = kTcM * kTcKB;         // 8 KB per activation limb
+constexpr int kTcBTile = kTcNB * kTcKB;        // 12 KB
+constexpr int kTcStage = 4 * kTcATile + kTcBTile;  // 44 KB
+constexpr int kTcSmem = kTcStages * kTcStage + 1024;  // + alignment slack
+constexpr int kTcThreads = 192;
+constexpr uint32_t kTcCols = 512;  // TMEM columns allocated (480 used)
+
+__device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void tc_mbar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void tc_mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool tc_mbar_wait(uint64_t* b, uint32_t parity) {
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(su32(bar))
+      : "memory");
+}
+
+// K-major operand in the 64-byte swizzle layout: rows of 64 bytes, 8-row
+// swizzle atoms 512 bytes apart (stride byte offset), descriptor version 1.
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)(512 >> 4) << 32) | (1ull << 46) | (4ull << 61);
+}
+// kind::i8 instruction descriptor: s32 accumulator, u8 A and B, both
+// K-major, N = 192, M = 128.
+constexpr uint32_t kTcIdesc = (2u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kTcNB >> 3) << 17) |
+                              ((uint32_t)(kTcM >> 4) << 24);
+
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(d),
+      "l"(a), "l"(b), "r"(kTcIdesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st_zero32(uint32_t taddr) {
+  const uint32_t z = 0;
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+      "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
+      "r"(z)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// operand preparation
+// ---------------------------------------------------------------------------
+
+// Activation rows -> four byte planes of X + 2^31 and the row sums of X + 2^31.
+__global__ void tc_act_prep_kernel(const int32_t* __restrict__ X, int S, int K, uint8_t* __restrict__ planes,
+                                   uint64_t* __restrict__ rowsum) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int s = blockIdx.x;
+  const int4* xr = reinterpret_cast<const int4*>(X + (size_t)s * K);
+  const size_t plane = (size_t)S * K;
+  uint64_t sum = 0;
+  for (int c = threadIdx.x; c < K / 4; c += blockDim.x) {
+    const int4 v = xr[c];
+    const uint32_t u[4] = {(uint32_t)v.x + 0x80000000u, (uint32_t)v.y + 0x80000000u, (uint32_t)v.z + 0x80000000u,
+                           (uint32_t)v.w + 0x80000000u};
+    sum += (uint64_t)u[0] + u[1] + u[2] + u[3];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const uint32_t packed = ((u[0] >> (8 * a)) & 0xffu) | (((u[1] >> (8 * a)) & 0xffu) << 8) |
+                              (((u[2] >> (8 * a)) & 0xffu) << 16) | (((u[3] >> (8 * a)) & 0xffu) << 24);
+      *reinterpret_cast<uint32_t*>(planes + a * plane + (size_t)s * K + 4 * c) = packed;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  __shared__ uint64_t part[32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t t = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
+    rowsum[s] = t;
+  }
+}
+
+// Weight rows (i16) -> low/high byte planes of W + 2^15 and their row sums.
+// Plane row R maps to source row R, or for a gate/up pair to gate row
+// 48*(R/96) + R%96 (R%96 < 48) or up row 48*(R/96) + R%96 - 48.
+__global__ void tc_weight_prep_kernel(const int16_t* __restrict__ W, const int16_t* __restrict__ U, int rows,
+                                      int K, int nrows, uint8_t* __restrict__ planes, uint64_t* __restrict__ rowsum) {
+  const int R = blockIdx.x;
+  const int16_t* src = nullptr;
+  if (U == nullptr) {
+    if (R < rows) src = W + (size_t)R * K;
+  } else {
+    const int b = R / kTcN, j = R % kTcN, h = kTcN / 2;
+    const int r = b * h + (j < h ? j : j - h);
+    if (r < rows) src = (j < h ? W : U) + (size_t)r * K;
+  }
+  const size_t plane = (size_t)nrows * K;
+  uint64_t sum = 0;
+  for (int c = threadIdx.x; c < K / 8; c += blockDim.x) {
+    uint16_t u[8];
+    if (src) {
+      const int4 v = reinterpret_cast<const int4*>(src)[c];
+      const int16_t* e = reinterpret_cast<const int16_t*>(&v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) u[i] = (uint16_t)((int32_t)e[i] + 32768);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) u[i] = 0;
+    }
+    uint64_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      sum += u[i];
+      lo |= (uint64_t)(u[i] & 0xffu) << (8 * i);
+      hi |= (uint64_t)(u[i] >> 8) << (8 * i);
+    }
+    *reinterpret_cast<uint64_t*>(planes + (size_t)R * K + 8 * c) = lo;
+    *reinterpret_cast<uint64_t*>(planes + plane + (size_t)R * K + 8 * c) = hi;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  __shared__ uint64_t part[32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t t = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
+    rowsum[R] = t;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// the GEMM
+// ---------------------------------------------------------------------------
+// EPI: 0 plain, 1 gelu(y) * vec[s, n], 2 gate/up pair (gelu(gate) * up)
+template <int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_linear_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
+                     const uint64_t* __restrict__ arow, const uint64_t* __restrict__ brow, int S, int N, int K,
+                     int32_t* __restrict__ Y, const int32_t* __restrict__ vec) {
+  extern __shared__ __align__(16) unsigned char tc_smem_raw[];
+  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf;
+  __shared__ uint32_t tmem_holder;
+  __shared__ int fail;
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * kTcM, nt = blockIdx.x, r0 = nt * kTcN;
+  const int nkb = (K + kTcKB - 1) / kTcKB;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTcStages; ++i) {
+      tc_mbar_init(&full[i], 1);
+      tc_mbar_init(&empty[i], 1);
+    }
+    tc_mbar_init(&accf, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    fail = 0;
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_holder)),
+                 "r"(kTcCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_holder;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (warp < 4) {
+    // zero the 480 accumulator columns of this warp's 32 lanes
+    const uint32_t base = tmem + ((uint32_t)(32 * warp) << 16);
+    for (int c = 0; c < 5 * kTcN; c += 32) tmem_st_zero32(base + c);
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 4) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int st = kb % kTcStages;
+        if (kb >= kTcStages && !tc_mbar_wait(&empty[st], ((kb / kTcStages) - 1) & 1)) fail = 1;
+        unsigned char* sbuf = smem + (size_t)st * kTcStage;
+        tc_mbar_expect_tx(&full[st], kTcStage);
+        for (int a = 0; a < 4; ++a) tma_load_3d(sbuf + a * kTcATile, &amap, kb * kTcKB, m0, a, &full[st]);
+        tma_load_3d(sbuf + 4 * kTcATile, &bmap, kb * kTcKB, r0, 0, &full[st]);
+        tma_load_3d(sbuf + 4 * kTcATile + kTcN * kTcKB, &bmap, kb * kTcKB, r0, 1, &full[st]);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int st = kb % kTcStages;
+        if (!tc_mbar_wait(&full[st], (kb / kTcStages) & 1)) fail = 1;
+        tc_fence_after();
+        const unsigned char* sbuf = smem + (size_t)st * kTcStage;
+        const uint32_t baddr = su32(sbuf + 4 * kTcATile);
+#pragma unroll
+        for (int j = 0; j < kTcKB / 32; ++j) {
+          const uint64_t bdesc = smem_desc_sw64(baddr + 32 * j);
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            const uint64_t adesc = smem_desc_sw64(su32(sbuf + a * kTcATile) + 32 * j);
+            tc_mma(tmem + (uint32_t)(kTcN * a), adesc, bdesc, 1u);
+          }
+        }
+        // free the stage once these MMAs have read it (the last stages are
+        // never reloaded, so nothing waits for them)
+        if (kb + kTcStages < nkb) tc_commit(&empty[st]);
+      }
+      tc_commit(&accf);
+    }
+  } else {
+    // epilogue: thread = token row m0 + 32*warp + lane (TMEM lane)
+    if (!tc_mbar_wait(&accf, 0)) fail = 1;
+    tc_fence_after();
+    const int m = m0 + 32 * warp + lane;
+    const bool mrow = m < S;
+    const uint64_t corr = (mrow ? (arow[m] << 15) : 0) - ((uint64_t)K << 46);
+    const uint32_t tbase = tmem + ((uint32_t)(32 * warp) << 16);
+    constexpr int kOut = EPI == 2 ? kTcN / 2 : kTcN;  // outputs per tile row
+    for (int c0 = 0; c0 < kOut; c0 += 8) {
+      uint32_t g[5][8], h[5][8];
+#pragma unroll
+      for (int gg = 0; gg < 5; ++gg) tmem_ld8(tbase + kTcN * gg + c0, g[gg]);
+      if (EPI == 2) {
+#pragma unroll
+        for (int gg = 0; gg < 5; ++gg) tmem_ld8(tbase + kTcN * gg + kTcN / 2 + c0, h[gg]);
+      }
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int j = c0 + i;
+        // plane rows of a pair cover whole tiles; a plain matrix has N rows
+        const int n = EPI == 2 ? nt * (kTcN / 2) + j : r0 + j;
+        if (!mrow || n >= N) continue;
+        uint64_t acc = (uint64_t)g[0][i] + ((uint64_t)g[1][i] << 8) + ((uint64_t)g[2][i] << 16) +
+                       ((uint64_t)g[3][i] << 24) + ((uint64_t)g[4][i] << 32);
+        acc -= corr + (brow[r0 + j] << 31);
+        int32_t y = requantize((int64_t)acc);
+        if (EPI == 2) {
+          uint64_t accu = (uint64_t)h[0][i] + ((uint64_t)h[1][i] << 8) + ((uint64_t)h[2][i] << 16) +
+                          ((uint64_t)h[3][i] << 24) + ((uint64_t)h[4][i] << 32);
+          accu -= corr + (brow[r0 + kTcN / 2 + j] << 31);
+          y = mul_sat(gelu_act(y), requantize((int64_t)accu));
+        } else if (EPI == 1) {
+          y = mul_sat(gelu_act(y), vec[(size_t)m * N + n]);
+        }
+        Y[(size_t)m * N + n] = y;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (fail && threadIdx.x == 0) atomicExch(&g_tc_err, 1);
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+// u8 planes [planes][rows][K] -> 3D map (K, rows, planes), box (64, box_rows, 1)
+bool encode_planes(void* out, const uint8_t* base, int nplanes, int rows, int K, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  CUtensorMap* map = reinterpret_cast<CUtensorMap*>(out);
+  const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)nplanes};
+  const cuuint64_t strides[2] = {(cuuint64_t)K, (cuuint64_t)rows * (cuuint64_t)K};
+  const cuuint32_t box[3] = {(cuuint32_t)kTcKB, (cuuint32_t)box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename... KArgs, typename... Args>
+void tc_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+}  // namespace
+
+static_assert(sizeof(CUtensorMap) <= sizeof(TcAct::map), "tensor map storage");
+
+int tc_error_flag(bool reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_tc_err, sizeof(int));
+  if (reset && v) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_tc_err, &z, sizeof(int));
+  }
+  return v;
+}
+
+void tc_init() {
+  cudaFuncSetAttribute(tc_linear_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+  cudaFuncSetAttribute(tc_linear_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+  cudaFuncSetAttribute(tc_linear_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+}
+
+bool tc_supported() {
+  static int ok = -1;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  if (ok < 0) {
+    int dev = 0, major = 0, minor = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    ok = (major == 10 && minor == 0 && encode_fn() != nullptr) ? 1 : 0;
+  }
+  return ok == 1;
+}
+
+bool tc_weight_eligible(const DevMat& w) {
+  return w.width == 16 && w.cols > 0 && w.cols % 16 == 0 && w.cols <= kTcMaxK && w.rows > 0 &&
+         (reinterpret_cast<uintptr_t>(w.p) & 15) == 0;
+}
+
+int tc_plane_rows(int rows, bool pair) { return pair ? kTcN * ((rows + kTcN / 2 - 1) / (kTcN / 2)) : rows; }
+
+size_t tc_weight_bytes(int rows, int K, bool pair) {
+  const size_t nr = (size_t)tc_plane_rows(rows, pair);
+  return 2 * nr * K + nr * 8;
+}
+
+bool tc_prepare_weight(TcWeight& t, const DevMat& g, const DevMat* u, void* mem, cudaStream_t s) {
+  const bool pair = u != nullptr;
+  t.N = g.rows;
+  t.K = g.cols;
+  t.pair = pair;
+  t.nrows = tc_plane_rows(g.rows, pair);
+  t.planes = static_cast<uint8_t*>(mem);
+  t.rowsum = reinterpret_cast<uint64_t*>(t.planes + 2 * (size_t)t.nrows * t.K);
+  tc_weight_prep_kernel<<<t.nrows, 128, 0, s>>>(static_cast<const int16_t*>(g.p),
+                                                pair ? static_cast<const int16_t*>(u->p) : nullptr, g.rows, g.cols,
+                                                t.nrows, t.planes, t.rowsum);
+  return encode_planes(t.map, t.planes, 2, t.nrows, t.K, kTcN);
+}
+
+size_t tc_act_bytes(int S, int K) { return 4 * (size_t)S * K + (size_t)S * 8; }
+
+bool tc_prepare_act(TcAct& a, const int32_t* X, int S, int K, void* mem, cudaStream_t s) {
+  a.S = S;
+  a.K = K;
+  a.planes = static_cast<uint8_t*>(mem);
+  a.rowsum = reinterpret_cast<uint64_t*>(a.planes + 4 * (size_t)S * K);
+  tc_launch(tc_act_prep_kernel, dim3(S), dim3(256), 0, s, X, S, K, a.planes, a.rowsum);
+  return encode_planes(a.map, a.planes, 4, S, K, kTcM);
+}
+
+void launch_tc_linear(const TcAct& a, const TcWeight& w, int32_t* Y, int32_t epi, const int32_t* vec,
+                      cudaStream_t s) {
+  const int ntiles = (w.nrows + kTcN - 1) / kTcN;
+  const dim3 grid(ntiles, (a.S + kTcM - 1) / kTcM);
+  const CUtensorMap& am = *reinterpret_cast<const CUtensorMap*>(a.map);
+  const CUtensorMap& bm = *reinterpret_cast<const CUtensorMap*>(w.map);
+  if (w.pair)
+    tc_launch(tc_linear_kernel<2>, grid, dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N, a.K,
+              Y, vec);
+  else if (epi == kEpiGeluMul)
+    tc_launch(tc_linear_kernel<1>, grid, dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N, a.K,
+              Y, vec);
+  else
+    tc_launch(tc_linear_kernel<0>, grid, dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N, a.K,
+              Y, vec);
+}
+
+}  // namespace rdet

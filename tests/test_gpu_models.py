@@ -157,3 +157,23 @@ def test_e4b_head_dims_long_prompt():
                       layer_types=["sliding_attention", "full_attention", "sliding_attention", "sliding_attention"])
     d = write_model(cfg, seed=8)
     run_both(d, lcg_ids(600, 300, 2), 4)
+
+
+@pytest.mark.parametrize("variant", ["default", "k_eq_v_global_kv", "gqa8", "bidirectional_window"])
+def test_tensor_core_prefill_long_prompt(variant):
+    # prompts of >= 32 tokens take the tcgen05 prefill linear (several M tiles,
+    # a partial last tile); the no-tensor-core context must agree with it
+    cfg, width = VARIANTS[variant]
+    cfg = {"text_config": {k: v for k, v in cfg["text_config"].items() if v is not None}}
+    d = write_model(cfg, seed=21, width=width)
+    ids = lcg_ids(300, cfg["text_config"]["vocab_size"], 9)
+    run_both(d, ids, 3)
+    cuda = rdet.Model.open(d, max_prefill=len(ids), tensor_cores=False)
+    s = cuda.new_sequence(len(ids) + 4)
+    s.prefill(ids)
+    tc = rdet.Model.open(d, max_prefill=len(ids))
+    assert tc.tensor_core_prefill and not cuda.tensor_core_prefill
+    t = tc.new_sequence(len(ids) + 4)
+    t.prefill(ids)
+    assert s.commitment(rdet.BUF_HIDDEN) == t.commitment(rdet.BUF_HIDDEN)
+    assert np.array_equal(s.read(rdet.BUF_LOGITS), t.read(rdet.BUF_LOGITS))
