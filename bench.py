@@ -235,6 +235,20 @@ def run_kernel_case(args):
     t = cfg["text_config"]
     dev = "cuda:0"
     g = torch.Generator(device=dev).manual_seed(5)
+    if args.kernel_case == "tc":
+        # prefill linear on the tensor cores (rdet_det_linear, >= 32 rows): byte-plane
+        # prep kernels then tc_linear_kernel, at 2048 prompt tokens
+        shapes = e4b_gemv_shapes(cfg)
+        S = 2048
+        for k in ("gate", "down", "q"):
+            n, kk = shapes[k]
+            w = torch.randint(-32768, 32768, (n, kk), dtype=torch.int16, device=dev, generator=g)
+            x = torch.randint(-(1 << 20), 1 << 20, (S, kk), dtype=torch.int32, device=dev, generator=g)
+            y = torch.empty((S, n), dtype=torch.int32, device=dev)
+            rdet.det_linear(x.data_ptr(), S, w.data_ptr(), 16, n, kk, y.data_ptr())
+            torch.cuda.synchronize()
+            print(f"tc linear {k}: S {S} rows {n} cols {kk} int8 limb MACs {8 * S * n * kk}")
+        return
     if args.kernel_case == "gemv":
         shapes = e4b_gemv_shapes(cfg)
         for k in ("q", "down", "lm_head"):
@@ -382,7 +396,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-case", choices=["gemv", "attn"],
+    ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc"],
                     help="run a few launches of one kernel at E4B shapes for an ncu capture, then exit")
     args = ap.parse_args()
     if args.kernel_case:

@@ -292,14 +292,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_commit(&accf);
     }
   } else {
-    // epilogue: thread = token row m0 + 32*warp + lane (TMEM lane)
+    // epilogue: thread = token row m0 + 32*warp + lane (TMEM lane).  Results
+    // are staged in shared memory (the ring is idle once every MMA is done),
+    // then written out row by row so that a warp's stores are contiguous.
     if (!tc_mbar_wait(&accf, 0)) fail = 1;
     tc_fence_after();
-    const int m = m0 + 32 * warp + lane;
+    constexpr int kOut = EPI == 2 ? kTcN / 2 : kTcN;  // outputs per tile row
+    constexpr int kStride = kOut + 1;                  // odd: conflict-free row-wise staging
+    int32_t* stage = reinterpret_cast<int32_t*>(smem);
+    const int rl = 32 * warp + lane;
+    const int m = m0 + rl;
     const bool mrow = m < S;
+    const int nbase = EPI == 2 ? nt * (kTcN / 2) : r0;
     const uint64_t corr = (mrow ? (arow[m] << 15) : 0) - ((uint64_t)K << 46);
     const uint32_t tbase = tmem + ((uint32_t)(32 * warp) << 16);
-    constexpr int kOut = EPI == 2 ? kTcN / 2 : kTcN;  // outputs per tile row
     for (int c0 = 0; c0 < kOut; c0 += 8) {
       uint32_t g[5][8], h[5][8];
 #pragma unroll
@@ -313,21 +319,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int i = 0; i < 8; ++i) {
         const int j = c0 + i;
         // plane rows of a pair cover whole tiles; a plain matrix has N rows
-        const int n = EPI == 2 ? nt * (kTcN / 2) + j : r0 + j;
-        if (!mrow || n >= N) continue;
-        uint64_t acc = (uint64_t)g[0][i] + ((uint64_t)g[1][i] << 8) + ((uint64_t)g[2][i] << 16) +
-                       ((uint64_t)g[3][i] << 24) + ((uint64_t)g[4][i] << 32);
-        acc -= corr + (brow[r0 + j] << 31);
-        int32_t y = requantize((int64_t)acc);
-        if (EPI == 2) {
-          uint64_t accu = (uint64_t)h[0][i] + ((uint64_t)h[1][i] << 8) + ((uint64_t)h[2][i] << 16) +
-                          ((uint64_t)h[3][i] << 24) + ((uint64_t)h[4][i] << 32);
-          accu -= corr + (brow[r0 + kTcN / 2 + j] << 31);
-          y = mul_sat(gelu_act(y), requantize((int64_t)accu));
-        } else if (EPI == 1) {
-          y = mul_sat(gelu_act(y), vec[(size_t)m * N + n]);
+        const int n = nbase + j;
+        int32_t y = 0;
+        if (mrow && n < N) {
+          uint64_t acc = (uint64_t)g[0][i] + ((uint64_t)g[1][i] << 8) + ((uint64_t)g[2][i] << 16) +
+                         ((uint64_t)g[3][i] << 24) + ((uint64_t)g[4][i] << 32);
+          acc -= corr + (brow[r0 + j] << 31);
+          y = requantize((int64_t)acc);
+          if (EPI == 2) {
+            uint64_t accu = (uint64_t)h[0][i] + ((uint64_t)h[1][i] << 8) + ((uint64_t)h[2][i] << 16) +
+                            ((uint64_t)h[3][i] << 24) + ((uint64_t)h[4][i] << 32);
+            accu -= corr + (brow[r0 + kTcN / 2 + j] << 31);
+            y = mul_sat(gelu_act(y), requantize((int64_t)accu));
+          } else if (EPI == 1) {
+            y = mul_sat(gelu_act(y), vec[(size_t)m * N + n]);
+          }
         }
-        Y[(size_t)m * N + n] = y;
+        stage[rl * kStride + j] = y;
+      }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+    for (int r = warp; r < kTcM; r += 4) {
+      const int mm = m0 + r;
+      if (mm >= S) break;
+      for (int c = lane; c < kOut; c += 32) {
+        const int n = nbase + c;
+        if (n < N) Y[(size_t)mm * N + n] = stage[r * kStride + c];
       }
     }
   }
