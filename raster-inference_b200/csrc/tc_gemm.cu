@@ -53,8 +53,11 @@ constexpr int kTcStages = 4;
 constexpr int kTcATile = kTcM * kTcKB;         // 8 KB per activation limb
 constexpr int kTcBTile = kTcNB * kTcKB;        // 12 KB
 constexpr int kTcStage = 4 * kTcATile + kTcBTile;  // 44 KB
-constexpr int kTcSmem = kTcStages * kTcStage + 1024;  // + alignment slack
-constexpr int kTcThreads = 192;
+constexpr int kTcOutStride = kTcN + 1;                 // staged output row (odd: conflict-free)
+constexpr int kTcStageOut = kTcM * kTcOutStride * 4;   // 49.7 KB output staging
+constexpr int kTcSmem = kTcStages * kTcStage + kTcStageOut + 1024;  // + alignment slack
+constexpr int kTcEpiWarps = 8;  // two per TMEM lane quarter, each half of the columns
+constexpr int kTcThreads = 32 * (kTcEpiWarps + 2);
 constexpr uint32_t kTcCols = 512;  // TMEM columns allocated (480 used)
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -92,13 +95,16 @@ __device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr) {
 }
 // kind::i8 instruction descriptor: s32 accumulator, u8 A and B, both
 // K-major, N = 192, M = 128.
-constexpr uint32_t kTcIdesc = (2u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kTcNB >> 3) << 17) |
-                              ((uint32_t)(kTcM >> 4) << 24);
+constexpr uint32_t tc_idesc(int n) {
+  return (2u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
+}
+constexpr uint32_t kTcIdesc = tc_idesc(kTcNB);    // both byte planes
+constexpr uint32_t kTcIdescHalf = tc_idesc(kTcN); // one byte plane
 
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(d),
-      "l"(a), "l"(b), "r"(kTcIdesc), "r"(acc)
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
@@ -113,15 +119,6 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_st_zero32(uint32_t taddr) {
-  const uint32_t z = 0;
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-      "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
-      "r"(z)
-      : "memory");
-}
-
 // ---------------------------------------------------------------------------
 // operand preparation
 // ---------------------------------------------------------------------------
@@ -212,20 +209,30 @@ __global__ void tc_weight_prep_kernel(const int16_t* __restrict__ W, const int16
 // the GEMM
 // ---------------------------------------------------------------------------
 // EPI: 0 plain, 1 gelu(y) * vec[s, n], 2 gate/up pair (gelu(gate) * up)
+//
+// Persistent: CTA b takes tiles b, b + grid, ... (N tile fastest).  The
+// producer streams stages across tile boundaries, so the next tile's first
+// stages load while the epilogue drains the previous accumulator; the MMA
+// warp starts a tile once the epilogue has moved the accumulator out of TMEM
+// (tmem_empty).  No zeroing: the first K step of a tile writes every TMEM
+// column once with accumulate off before anything accumulates into it
+// (limbs 0 and 2 fresh, limb 1 onto them, limb 3 split into its low-plane
+// half that accumulates and its high-plane half that is fresh).
 template <int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
                      const uint64_t* __restrict__ arow, const uint64_t* __restrict__ brow, int S, int N, int K,
-                     int32_t* __restrict__ Y, const int32_t* __restrict__ vec) {
+                     int ntiles_n, int ntiles, int32_t* __restrict__ Y, const int32_t* __restrict__ vec) {
   extern __shared__ __align__(16) unsigned char tc_smem_raw[];
-  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf;
+  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf, tmem_empty;
   __shared__ uint32_t tmem_holder;
   __shared__ int fail;
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+  int32_t* stage_out = reinterpret_cast<int32_t*>(smem + (size_t)kTcStages * kTcStage);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * kTcM, nt = blockIdx.x, r0 = nt * kTcN;
   const int nkb = (K + kTcKB - 1) / kTcKB;
+  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (threadIdx.x == 0) {
     for (int i = 0; i < kTcStages; ++i) {
@@ -233,6 +240,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_mbar_init(&empty[i], 1);
     }
     tc_mbar_init(&accf, 1);
+    tc_mbar_init(&tmem_empty, kTcEpiWarps);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fail = 0;
   }
@@ -247,105 +255,124 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_holder;
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (warp < 4) {
-    // zero the 480 accumulator columns of this warp's 32 lanes
-    const uint32_t base = tmem + ((uint32_t)(32 * warp) << 16);
-    for (int c = 0; c < 5 * kTcN; c += 32) tmem_st_zero32(base + c);
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 4) {
+  if (warp == kTcEpiWarps) {
+    // ---- producer: every stage of every tile of this CTA, through the ring
     if (lane == 0) {
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int st = kb % kTcStages;
-        if (kb >= kTcStages && !tc_mbar_wait(&empty[st], ((kb / kTcStages) - 1) & 1)) fail = 1;
-        unsigned char* sbuf = smem + (size_t)st * kTcStage;
-        tc_mbar_expect_tx(&full[st], kTcStage);
-        for (int a = 0; a < 4; ++a) tma_load_3d(sbuf + a * kTcATile, &amap, kb * kTcKB, m0, a, &full[st]);
-        tma_load_3d(sbuf + 4 * kTcATile, &bmap, kb * kTcKB, r0, 0, &full[st]);
-        tma_load_3d(sbuf + 4 * kTcATile + kTcN * kTcKB, &bmap, kb * kTcKB, r0, 1, &full[st]);
+      int q = 0;
+      for (int it = 0; it < my_tiles; ++it) {
+        const int t = blockIdx.x + it * gridDim.x;
+        const int m0 = (t / ntiles_n) * kTcM, r0 = (t % ntiles_n) * kTcN;
+        for (int kb = 0; kb < nkb; ++kb, ++q) {
+          const int st = q % kTcStages;
+          if (q >= kTcStages && !tc_mbar_wait(&empty[st], ((q / kTcStages) - 1) & 1)) fail = 1;
+          unsigned char* sbuf = smem + (size_t)st * kTcStage;
+          tc_mbar_expect_tx(&full[st], kTcStage);
+          for (int a = 0; a < 4; ++a) tma_load_3d(sbuf + a * kTcATile, &amap, kb * kTcKB, m0, a, &full[st]);
+          tma_load_3d(sbuf + 4 * kTcATile, &bmap, kb * kTcKB, r0, 0, &full[st]);
+          tma_load_3d(sbuf + 4 * kTcATile + kTcN * kTcKB, &bmap, kb * kTcKB, r0, 1, &full[st]);
+        }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kTcEpiWarps + 1) {
+    // ---- MMA issue
     if (lane == 0) {
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int st = kb % kTcStages;
-        if (!tc_mbar_wait(&full[st], (kb / kTcStages) & 1)) fail = 1;
+      int q = 0;
+      const int qlast = my_tiles * nkb;
+      for (int it = 0; it < my_tiles; ++it) {
+        if (it > 0 && !tc_mbar_wait(&tmem_empty, (it - 1) & 1)) fail = 1;
         tc_fence_after();
-        const unsigned char* sbuf = smem + (size_t)st * kTcStage;
-        const uint32_t baddr = su32(sbuf + 4 * kTcATile);
+        for (int kb = 0; kb < nkb; ++kb, ++q) {
+          const int st = q % kTcStages;
+          if (!tc_mbar_wait(&full[st], (q / kTcStages) & 1)) fail = 1;
+          tc_fence_after();
+          const unsigned char* sbuf = smem + (size_t)st * kTcStage;
+          const uint32_t baddr = su32(sbuf + 4 * kTcATile);
 #pragma unroll
-        for (int j = 0; j < kTcKB / 32; ++j) {
-          const uint64_t bdesc = smem_desc_sw64(baddr + 32 * j);
+          for (int j = 0; j < kTcKB / 32; ++j) {
+            const uint64_t bdesc = smem_desc_sw64(baddr + 32 * j);
+            const uint64_t ad[4] = {smem_desc_sw64(su32(sbuf) + 32 * j), smem_desc_sw64(su32(sbuf + kTcATile) + 32 * j),
+                                    smem_desc_sw64(su32(sbuf + 2 * kTcATile) + 32 * j),
+                                    smem_desc_sw64(su32(sbuf + 3 * kTcATile) + 32 * j)};
+            if (kb == 0 && j == 0) {
+              tc_mma(tmem + 0 * kTcN, ad[0], bdesc, kTcIdesc, 0u);
+              tc_mma(tmem + 2 * kTcN, ad[2], bdesc, kTcIdesc, 0u);
+              tc_mma(tmem + 1 * kTcN, ad[1], bdesc, kTcIdesc, 1u);
+              tc_mma(tmem + 3 * kTcN, ad[3], bdesc, kTcIdescHalf, 1u);
+              tc_mma(tmem + 4 * kTcN, ad[3], smem_desc_sw64(baddr + kTcN * kTcKB), kTcIdescHalf, 0u);
+            } else {
 #pragma unroll
-          for (int a = 0; a < 4; ++a) {
-            const uint64_t adesc = smem_desc_sw64(su32(sbuf + a * kTcATile) + 32 * j);
-            tc_mma(tmem + (uint32_t)(kTcN * a), adesc, bdesc, 1u);
+              for (int a = 0; a < 4; ++a) tc_mma(tmem + (uint32_t)(kTcN * a), ad[a], bdesc, kTcIdesc, 1u);
+            }
           }
+          // free the stage once these MMAs have read it (the CTA's last stages
+          // are never reloaded, so nothing waits for them)
+          if (q + kTcStages < qlast) tc_commit(&empty[st]);
         }
-        // free the stage once these MMAs have read it (the last stages are
-        // never reloaded, so nothing waits for them)
-        if (kb + kTcStages < nkb) tc_commit(&empty[st]);
+        tc_commit(&accf);
       }
-      tc_commit(&accf);
     }
   } else {
-    // epilogue: thread = token row m0 + 32*warp + lane (TMEM lane).  Results
-    // are staged in shared memory (the ring is idle once every MMA is done),
-    // then written out row by row so that a warp's stores are contiguous.
-    if (!tc_mbar_wait(&accf, 0)) fail = 1;
-    tc_fence_after();
+    // ---- epilogue: warp w reads TMEM lanes 32*(w%4).. and column half w/4
     constexpr int kOut = EPI == 2 ? kTcN / 2 : kTcN;  // outputs per tile row
-    constexpr int kStride = kOut + 1;                  // odd: conflict-free row-wise staging
-    int32_t* stage = reinterpret_cast<int32_t*>(smem);
-    const int rl = 32 * warp + lane;
-    const int m = m0 + rl;
-    const bool mrow = m < S;
-    const int nbase = EPI == 2 ? nt * (kTcN / 2) : r0;
-    const uint64_t corr = (mrow ? (arow[m] << 15) : 0) - ((uint64_t)K << 46);
-    const uint32_t tbase = tmem + ((uint32_t)(32 * warp) << 16);
-    for (int c0 = 0; c0 < kOut; c0 += 8) {
-      uint32_t g[5][8], h[5][8];
+    constexpr int kHalf = kOut / 2;
+    const int quarter = warp & 3, half = warp >> 2;
+    const int rl = 32 * quarter + lane;
+    const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16);
+    for (int it = 0; it < my_tiles; ++it) {
+      const int t = blockIdx.x + it * gridDim.x;
+      const int m0 = (t / ntiles_n) * kTcM, nt = t % ntiles_n, r0 = nt * kTcN;
+      const int nbase = EPI == 2 ? nt * (kTcN / 2) : r0;
+      const int m = m0 + rl;
+      const bool mrow = m < S;
+      const uint64_t corr = (mrow ? (arow[m] << 15) : 0) - ((uint64_t)K << 46);
+      if (!tc_mbar_wait(&accf, it & 1)) fail = 1;
+      tc_fence_after();
+      for (int c0 = half * kHalf; c0 < (half + 1) * kHalf; c0 += 8) {
+        uint32_t g[5][8], h[5][8];
 #pragma unroll
-      for (int gg = 0; gg < 5; ++gg) tmem_ld8(tbase + kTcN * gg + c0, g[gg]);
-      if (EPI == 2) {
+        for (int gg = 0; gg < 5; ++gg) tmem_ld8(tbase + kTcN * gg + c0, g[gg]);
+        if (EPI == 2) {
 #pragma unroll
-        for (int gg = 0; gg < 5; ++gg) tmem_ld8(tbase + kTcN * gg + kTcN / 2 + c0, h[gg]);
-      }
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int j = c0 + i;
-        // plane rows of a pair cover whole tiles; a plain matrix has N rows
-        const int n = nbase + j;
-        int32_t y = 0;
-        if (mrow && n < N) {
-          uint64_t acc = (uint64_t)g[0][i] + ((uint64_t)g[1][i] << 8) + ((uint64_t)g[2][i] << 16) +
-                         ((uint64_t)g[3][i] << 24) + ((uint64_t)g[4][i] << 32);
-          acc -= corr + (brow[r0 + j] << 31);
-          y = requantize((int64_t)acc);
-          if (EPI == 2) {
-            uint64_t accu = (uint64_t)h[0][i] + ((uint64_t)h[1][i] << 8) + ((uint64_t)h[2][i] << 16) +
-                            ((uint64_t)h[3][i] << 24) + ((uint64_t)h[4][i] << 32);
-            accu -= corr + (brow[r0 + kTcN / 2 + j] << 31);
-            y = mul_sat(gelu_act(y), requantize((int64_t)accu));
-          } else if (EPI == 1) {
-            y = mul_sat(gelu_act(y), vec[(size_t)m * N + n]);
-          }
+          for (int gg = 0; gg < 5; ++gg) tmem_ld8(tbase + kTcN * gg + kTcN / 2 + c0, h[gg]);
         }
-        stage[rl * kStride + j] = y;
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int j = c0 + i;
+          // plane rows of a pair cover whole tiles; a plain matrix has N rows
+          const int n = nbase + j;
+          int32_t y = 0;
+          if (mrow && n < N) {
+            uint64_t acc = (uint64_t)g[0][i] + ((uint64_t)g[1][i] << 8) + ((uint64_t)g[2][i] << 16) +
+                           ((uint64_t)g[3][i] << 24) + ((uint64_t)g[4][i] << 32);
+            acc -= corr + (brow[r0 + j] << 31);
+            y = requantize((int64_t)acc);
+            if (EPI == 2) {
+              uint64_t accu = (uint64_t)h[0][i] + ((uint64_t)h[1][i] << 8) + ((uint64_t)h[2][i] << 16) +
+                              ((uint64_t)h[3][i] << 24) + ((uint64_t)h[4][i] << 32);
+              accu -= corr + (brow[r0 + kTcN / 2 + j] << 31);
+              y = mul_sat(gelu_act(y), requantize((int64_t)accu));
+            } else if (EPI == 1) {
+              y = mul_sat(gelu_act(y), vec[(size_t)m * N + n]);
+            }
+          }
+          stage_out[rl * kTcOutStride + j] = y;
+        }
       }
-    }
-    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
-    for (int r = warp; r < kTcM; r += 4) {
-      const int mm = m0 + r;
-      if (mm >= S) break;
-      for (int c = lane; c < kOut; c += 32) {
-        const int n = nbase + c;
-        if (n < N) Y[(size_t)mm * N + n] = stage[r * kStride + c];
+      // the accumulator is in registers/shared memory: TMEM is free for the next tile
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&tmem_empty)) : "memory");
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kTcEpiWarps) : "memory");  // staging complete
+      for (int r = warp; r < kTcM; r += kTcEpiWarps) {
+        const int mm = m0 + r;
+        if (mm >= S) break;
+        for (int c = lane; c < kOut; c += 32) {
+          const int n = nbase + c;
+          if (n < N) Y[(size_t)mm * N + n] = stage_out[r * kTcOutStride + c];
+        }
       }
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kTcEpiWarps) : "memory");  // staging free again
     }
   }
   tc_fence_before();
@@ -481,19 +508,20 @@ bool tc_prepare_act(TcAct& a, const int32_t* X, int S, int K, void* mem, cudaStr
 
 void launch_tc_linear(const TcAct& a, const TcWeight& w, int32_t* Y, int32_t epi, const int32_t* vec,
                       cudaStream_t s) {
-  const int ntiles = (w.nrows + kTcN - 1) / kTcN;
-  const dim3 grid(ntiles, (a.S + kTcM - 1) / kTcM);
+  const int ntiles_n = (w.nrows + kTcN - 1) / kTcN;
+  const int ntiles = ntiles_n * ((a.S + kTcM - 1) / kTcM);
+  const int grid = ntiles < sm_count() ? ntiles : sm_count();
   const CUtensorMap& am = *reinterpret_cast<const CUtensorMap*>(a.map);
   const CUtensorMap& bm = *reinterpret_cast<const CUtensorMap*>(w.map);
   if (w.pair)
-    tc_launch(tc_linear_kernel<2>, grid, dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N, a.K,
-              Y, vec);
+    tc_launch(tc_linear_kernel<2>, dim3(grid), dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N,
+              a.K, ntiles_n, ntiles, Y, vec);
   else if (epi == kEpiGeluMul)
-    tc_launch(tc_linear_kernel<1>, grid, dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N, a.K,
-              Y, vec);
+    tc_launch(tc_linear_kernel<1>, dim3(grid), dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N,
+              a.K, ntiles_n, ntiles, Y, vec);
   else
-    tc_launch(tc_linear_kernel<0>, grid, dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N, a.K,
-              Y, vec);
+    tc_launch(tc_linear_kernel<0>, dim3(grid), dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N,
+              a.K, ntiles_n, ntiles, Y, vec);
 }
 
 }  // namespace rdet
