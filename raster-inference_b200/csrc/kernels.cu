@@ -1035,7 +1035,8 @@ __global__ void qkv_post_kernel(const QkvPostArgs a) {
   int32_t* vs = reinterpret_cast<int32_t*>(smem_raw);
   __shared__ uint64_t red[33];
   const int s = blockIdx.x, head = blockIdx.y, d = a.d;
-  const uint32_t pos = (uint32_t)(*a.pos + s);
+  const bool rows = a.pos_rows != nullptr;
+  const uint32_t pos = rows ? (uint32_t)*a.pos_rows[s] : (uint32_t)(*a.pos + s);
   if (head < a.Hq) {
     const int32_t* src = a.q_in + ((size_t)s * a.Hq + head) * d;
     for (int i = threadIdx.x; i < d; i += blockDim.x) vs[i] = src[i];
@@ -1050,6 +1051,10 @@ __global__ void qkv_post_kernel(const QkvPostArgs a) {
     return;
   }
   if (!a.k_in) return;
+  // this layer appends K/V: the cache tables are set (a KV-sharing layer has none)
+  int32_t* const kcache = rows ? a.kc_rows[s] : a.k_cache;
+  int32_t* const vcache = rows ? a.vc_rows[s] : a.v_cache;
+  const int cap = rows ? a.cap_rows[s] : a.cap;
   const int h = head - a.Hq;
   // K: head norm + RoPE
   const int32_t* ks = a.k_in + ((size_t)s * a.Hkv + h) * d;
@@ -1060,7 +1065,7 @@ __global__ void qkv_post_kernel(const QkvPostArgs a) {
   __syncthreads();
   rope_inplace(vs, a.rotary, a.inv_freq, pos);
   __syncthreads();
-  int32_t* kd = a.k_cache + ((size_t)h * a.cap + pos) * d;
+  int32_t* kd = kcache + ((size_t)h * cap + pos) * d;
   for (int i = threadIdx.x; i < d; i += blockDim.x) kd[i] = vs[i];
   __syncthreads();
   // V: weightless value norm of the raw projection
@@ -1068,7 +1073,7 @@ __global__ void qkv_post_kernel(const QkvPostArgs a) {
   for (int i = threadIdx.x; i < d; i += blockDim.x) vs[i] = vsrc[i];
   __syncthreads();
   int32_t sv = block_norm_scale(vs, d, a.eps, red);
-  int32_t* vd = a.v_cache + ((size_t)h * a.cap + pos) * d;
+  int32_t* vd = vcache + ((size_t)h * cap + pos) * d;
   for (int i = threadIdx.x; i < d; i += blockDim.x) vd[i] = mul_sat(vs[i], sv);
 }
 void launch_qkv_post(const QkvPostArgs& a, cudaStream_t s) {
@@ -1081,7 +1086,7 @@ void launch_qkv_post(const QkvPostArgs& a, cudaStream_t s) {
 // key window (attention_output_into, det_kernels.rs:340-367).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void decode_window(const AttnDecodeArgs& a, int* start, int* n) {
-  int len = (a.pos ? *a.pos : a.pos_value) + 1;
+  int len = (a.pos_rows ? *a.pos_rows[blockIdx.z] : (a.pos ? *a.pos : a.pos_value)) + 1;
   int st = (a.window > 0 && len > a.window) ? len - a.window : 0;
   *start = st;
   *n = len - st;
@@ -1407,7 +1412,15 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
   }
   __syncthreads();
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int pos = a.pos ? *a.pos : a.pos_value;
+  // batched decode: cluster row blockIdx.z is its own sequence
+  const int brow = blockIdx.z;
+  const bool batched = a.pos_rows != nullptr;
+  const int32_t* const kc = batched ? a.kc_rows[brow] : a.k_cache;
+  const int32_t* const vc = batched ? a.vc_rows[brow] : a.v_cache;
+  const int capr = batched ? a.cap_rows[brow] : a.cap;
+  const int32_t* const qrow = a.q + (size_t)brow * a.Hq * d;
+  int32_t* const orow = a.out + (size_t)brow * a.Hq * d;
+  const int pos = batched ? *a.pos_rows[brow] : (a.pos ? *a.pos : a.pos_value);
   int start, n;
   decode_window(a, &start, &n);
   const int lo = (int)((int64_t)n * rank / CL), hi = (int)((int64_t)n * (rank + 1) / CL);
@@ -1415,7 +1428,7 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
   const int TR = kAcTileBytes / (d * 4);  // rows per tile
   const int tiles = (rows + TR - 1) / TR;
   const int total_tiles = 2 * tiles;  // K tiles, then V tiles
-  const size_t head_base = (size_t)kvh * a.cap;
+  const size_t head_base = (size_t)kvh * capr;
   // the current token's row (when built here) is the CTA's last row and is
   // not copied from the cache
   const int copy_rows = rows - ((new_row && rows > 0 && start + hi - 1 == pos) ? 1 : 0);
@@ -1423,7 +1436,7 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
   auto issue = [&](int u) {  // thread 0 only
     const int slot = u % kAcStages;
     const int t = u < tiles ? u : u - tiles;
-    const int32_t* cache = u < tiles ? a.k_cache : a.v_cache;
+    const int32_t* cache = u < tiles ? kc : vc;
     const int r0 = t * TR;
     const int nr = min(TR, copy_rows - r0);
     if (nr > 0) {
@@ -1441,7 +1454,7 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
     for (int u = 0; u < kAcStages && u < total_tiles; ++u) issue(u);
   for (int i = tid; i < GC * d; i += kAcThreads) pacc[i] = 0;
   if (!fused) {
-    for (int i = tid; i < GC * d; i += kAcThreads) qs[i] = a.q[(size_t)qh0 * d + i];
+    for (int i = tid; i < GC * d; i += kAcThreads) qs[i] = qrow[(size_t)qh0 * d + i];
   } else {
     for (int i = tid; i < GC * d; i += kAcThreads) qs[i] = f.q_in[(size_t)qh0 * d + i];
     if (new_row)
@@ -1595,7 +1608,7 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
     const int g = e / per, dim = d0 + e % per;
     const int r = start + g_idx[g];
     if (new_row && r == pos) vmx[g][e % per] = kvrow[d + dim];
-    else cp_async4(&vmx[g][e % per], a.v_cache + (head_base + r) * d + dim);
+    else cp_async4(&vmx[g][e % per], vc + (head_base + r) * d + dim);
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   // ---- phase 2: exp terms and local sums, (head, row) pairs in parallel
@@ -1715,7 +1728,7 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
     for (int o = CL >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     if (r == 0 && e < nel) {
       v += (int64_t)vmx[g][dim - d0] * g_res[g];
-      a.out[(size_t)(qh0 + g) * d + dim] = requantize(v);
+      orow[(size_t)(qh0 + g) * d + dim] = requantize(v);
     }
   }
   if (s_fail && tid == 0) {
@@ -1736,7 +1749,7 @@ static size_t ac_smem(int gc, int d, int rmax) { return (size_t)ac_layout(gc, d,
 template <int GC, int NCH>
 static cudaError_t launch_ac(const AttnDecodeArgs& a, int CL, int rmax, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(CL, a.Hq / GC, 1);
+  cfg.gridDim = dim3(CL, a.Hq / GC, a.batch > 0 ? a.batch : 1);
   cfg.blockDim = dim3(kAcThreads, 1, 1);
   cfg.dynamicSmemBytes = ac_smem(GC, a.d, rmax);
   cfg.stream = s;
@@ -1829,12 +1842,17 @@ bool attn_decode_cluster_fits(int Hq, int Hkv, int d, int window, int cap, int r
 void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s) {
   const int CL = g_attn_cluster ? g_attn_cluster : 8;
   const int rmax = ac_rmax(a.window, a.cap, CL);
+  // (batched rows use the library's own 16-byte aligned cache allocations)
   const bool aligned = ((reinterpret_cast<uintptr_t>(a.k_cache) | reinterpret_cast<uintptr_t>(a.v_cache)) & 15) == 0;
   if (!aligned || !attn_decode_cluster_fits(a.Hq, a.Hkv, a.d, a.window, a.cap, a.fuse.q_in ? a.fuse.rotary : 0)) {
     launch_attn_decode(a, s);  // callers only fuse when the cluster kernel fits
     return;
   }
-  const int gc = ac_group(a.Hq, a.Hkv, a.d);
+  int gc = ac_group(a.Hq, a.Hkv, a.d);
+  if (a.batch > 1) {  // many clusters already: share K/V reads between query heads
+    const int G = a.Hq / a.Hkv, cap = a.d <= 256 ? 4 : 2;
+    while (gc * 2 <= cap && G % (gc * 2) == 0 && ac_smem(gc * 2, a.d, rmax) <= kAcMaxSmem) gc *= 2;
+  }
   // launch errors surface through cudaGetLastError in the caller
   if (a.d <= 128) {
     if (gc == 1) launch_ac<1, 1>(a, CL, rmax, s);
@@ -2216,6 +2234,25 @@ void launch_softcap(int32_t* x, int32_t n, int32_t cap, cudaStream_t s) {
 // ---------------------------------------------------------------------------
 // misc
 // ---------------------------------------------------------------------------
+__global__ void add_i32_rows_kernel(int32_t* const* p, int32_t n, int32_t v) {
+  pdl_entry();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) *p[i] += v;
+}
+void launch_add_i32_rows(int32_t* const* p, int32_t n, int32_t v, cudaStream_t s) {
+  launch_k(add_i32_rows_kernel, dim3(1), dim3(256), 0, s, p, n, v);
+}
+__global__ void scatter_rows_kernel(const int32_t* src, int32_t n, int32_t* const* dst, size_t off) {
+  pdl_entry();
+  const int r = blockIdx.x;
+  const int32_t* sr = src + (size_t)r * n;
+  int32_t* dr = dst[r] + off;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) dr[i] = sr[i];
+}
+void launch_scatter_rows(const int32_t* src, int32_t rows, int32_t n, int32_t* const* dst, size_t off,
+                         cudaStream_t s) {
+  launch_k(scatter_rows_kernel, dim3(rows), dim3(256), 0, s, src, n, dst, off);
+}
+
 __global__ void add_i32_kernel(int32_t* p, int32_t v) {
   pdl_entry(); *p += v; }
 void launch_add_i32(int32_t* p, int32_t v, cudaStream_t s) { launch_k(add_i32_kernel, dim3(1), dim3(1), 0, s, p, v); }

@@ -122,6 +122,13 @@ struct QkvPostArgs {
   int32_t* k_cache = nullptr;         // [Hkv, cap, d]
   int32_t* v_cache = nullptr;
   int32_t cap = 0;
+  // batched decode: row s is its own sequence (position *pos_rows[s], caches
+  // kc_rows[s] / vc_rows[s] of capacity cap_rows[s]); pos, k_cache, v_cache and
+  // cap are then unused
+  const int32_t* const* pos_rows = nullptr;
+  int32_t* const* kc_rows = nullptr;
+  int32_t* const* vc_rows = nullptr;
+  const int32_t* cap_rows = nullptr;
 };
 void launch_qkv_post(const QkvPostArgs& a, cudaStream_t s);
 
@@ -165,6 +172,14 @@ struct AttnDecodeArgs {
   AttnScratch sc;
   int32_t rows_per_split = 64;
   AttnFuse fuse;                 // used by the cluster kernel only
+  // batched decode (cluster kernel, not fused): `batch` query rows, row b
+  // attends with position *pos_rows[b] over kc_rows[b] / vc_rows[b] (capacity
+  // cap_rows[b]); q and out hold [batch, Hq, d]; cap is the largest capacity
+  int32_t batch = 1;
+  const int32_t* const* pos_rows = nullptr;
+  const int32_t* const* kc_rows = nullptr;
+  const int32_t* const* vc_rows = nullptr;
+  const int32_t* cap_rows = nullptr;
 };
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s);
 // Same computation in one kernel: one thread-block cluster per query head
@@ -215,6 +230,10 @@ void launch_softcap(int32_t* x, int32_t n, int32_t cap, cudaStream_t s);
 
 // ---- misc ---------------------------------------------------------------------------
 void launch_add_i32(int32_t* p, int32_t v, cudaStream_t s);  // *p += v
+void launch_add_i32_rows(int32_t* const* p, int32_t n, int32_t v, cudaStream_t s);  // *p[i] += v
+// dst[r] + off <- src row r (n ints), for r < rows
+void launch_scatter_rows(const int32_t* src, int32_t rows, int32_t n, int32_t* const* dst, size_t off,
+                         cudaStream_t s);
 void launch_copy_rows(const int32_t* src, int32_t* dst, size_t n, cudaStream_t s);
 // synthetic weights (counter-based generator, see detwgt.py)
 void launch_synth(void* dst, int32_t width, int32_t rank, int64_t n, int64_t cols, uint64_t key, cudaStream_t s);

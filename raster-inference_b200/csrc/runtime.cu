@@ -427,9 +427,22 @@ struct Ctx {
   Seq* decode_owner = nullptr;
   std::vector<void*> live_seqs;  // rdet_seq handles still open on this context
   bool tc = false;               // prefill linears run on the tensor cores
-  TcWeight t_ple_model;
+  TcWeight t_ple_model, t_lm_head;
   void* tc_act = nullptr;        // activation byte planes of the current linear
   int tc_act_k = 0;              // largest K the activation planes hold
+  // batched decode: per-row tables (device) and the batch logits
+  struct {
+    int rows = 0;                  // rows the tables hold
+    void* mem = nullptr;           // one allocation for every table below
+    uint32_t* ids = nullptr;
+    int32_t** pos = nullptr;       // [rows] each sequence's device position
+    int32_t* caps = nullptr;       // [rows]
+    int32_t** kc = nullptr;        // [L][rows] (a KV-sharing layer lists its donor's cache)
+    int32_t** vc = nullptr;
+    int32_t** dec_out = nullptr;   // [rows] each sequence's per-layer outputs
+    int32_t** logits_dst = nullptr;
+    int32_t* logits = nullptr;     // [rows, V]
+  } bw;
 
   void* dalloc(size_t bytes) {
     void* p = nullptr;
@@ -729,6 +742,7 @@ static void prepare_tensor_cores(Ctx& c) {
     }
   }
   if (m.P > 0) prep(c.t_ple_model, c.ple_model_proj);
+  prep(c.t_lm_head, c.lm_head);  // logits of batched decode
   if (kmax > 0) {
     c.tc_act = c.dalloc(tc_act_bytes((int)c.max_prefill, kmax));
     c.tc_act_k = kmax;
@@ -1224,6 +1238,146 @@ static bool kv_commitment(Ctx& c, Seq& q, std::string* out) {
 
 // Captures (once per sequence) the whole decode_transition of the token in
 // d_token as one CUDA graph.
+// ---------------------------------------------------------------------------
+// Batched decode: every sequence of the batch advances by one token in one
+// pass.  The projections run once over the batch rows (row GEMMs: tensor
+// cores from 32 rows); q/k norm, RoPE, the KV append and the attention use
+// each row's own position, caches and window.  Each row computes exactly
+// what decode_layer computes for that sequence alone.
+// ---------------------------------------------------------------------------
+static void batch_tables(Ctx& c, Seq* const* seqs, int B) {
+  const ModelCfg& m = c.cfg;
+  auto& bw = c.bw;
+  if (bw.rows < B) {
+    const int rows = std::max(B, 8);
+    const size_t ptrs = (size_t)rows * (3 + 2 * (size_t)m.L);
+    const size_t bytes = ptrs * 8 + (size_t)rows * 8 + (size_t)rows * m.V * 4 + 256;
+    bw.mem = c.dalloc(bytes);
+    auto* base = static_cast<unsigned char*>(bw.mem);
+    bw.pos = reinterpret_cast<int32_t**>(base);
+    bw.dec_out = bw.pos + rows;
+    bw.logits_dst = bw.dec_out + rows;
+    bw.kc = bw.logits_dst + rows;
+    bw.vc = bw.kc + (size_t)m.L * rows;
+    bw.ids = reinterpret_cast<uint32_t*>(bw.vc + (size_t)m.L * rows);
+    bw.caps = reinterpret_cast<int32_t*>(bw.ids + rows);
+    bw.logits = reinterpret_cast<int32_t*>((reinterpret_cast<uintptr_t>(bw.caps + rows) + 255) & ~(uintptr_t)255);
+    bw.rows = rows;
+  }
+  const int rows = bw.rows;
+  std::vector<int32_t*> host((size_t)rows * (3 + 2 * (size_t)m.L), nullptr);
+  std::vector<int32_t> caps(rows, 0);
+  for (int b = 0; b < B; ++b) {
+    Seq& q = *seqs[b];
+    host[b] = q.d_pos;
+    host[rows + b] = q.dec_out;
+    host[2 * (size_t)rows + b] = q.logits;
+    for (int l = 0; l < m.L; ++l) {
+      const int own = m.layers[l].donor < 0 ? l : m.layers[l].donor;
+      host[(3 + (size_t)l) * rows + b] = q.kc[own];
+      host[(3 + (size_t)m.L + l) * rows + b] = q.vc[own];
+    }
+    caps[b] = q.cap;
+  }
+  CK(cudaMemcpyAsync(bw.pos, host.data(), host.size() * 8, cudaMemcpyHostToDevice, c.stream));
+  CK(cudaMemcpyAsync(bw.caps, caps.data(), (size_t)rows * 4, cudaMemcpyHostToDevice, c.stream));
+}
+
+static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32_t* cur) {
+  const ModelCfg& m = c.cfg;
+  const LayerDev& L = c.layers[l];
+  const LayerCfg& lc = L.cfg;
+  PrefillWs& w = c.pw;
+  auto& bw = c.bw;
+  cudaStream_t s = c.stream;
+  const int H = m.H, d = lc.head_dim;
+  int32_t* other = cur == w.xa ? w.xb : w.xa;
+  launch_rmsnorm_rows(cur, B, H, L.in_ln, c.eps, w.nrm, s);
+  ActPlanes nrm_planes;
+  prefill_linear(c, w.nrm, B, L.q, L.tq, w.q, kEpiPlain, nullptr, &nrm_planes);
+  QkvPostArgs qa;
+  qa.S = B; qa.Hq = m.Hq; qa.Hkv = lc.kv_heads; qa.d = d; qa.rotary = lc.rotary; qa.inv_freq = L.inv_freq;
+  qa.q_in = w.q; qa.q_norm = L.q_norm; qa.k_norm = L.k_norm; qa.eps = c.eps; qa.q_out = w.qo;
+  qa.pos_rows = bw.pos; qa.cap_rows = bw.caps;
+  if (lc.donor < 0) {
+    prefill_linear(c, w.nrm, B, L.k, L.tk, w.kraw, kEpiPlain, nullptr, &nrm_planes);
+    const int32_t* vsrc = w.kraw;  // k_eq_v: V is the raw K projection
+    if (L.v.p) { prefill_linear(c, w.nrm, B, L.v, L.tv, w.vraw, kEpiPlain, nullptr, &nrm_planes); vsrc = w.vraw; }
+    qa.k_in = w.kraw; qa.v_in = vsrc;
+    qa.kc_rows = bw.kc + (size_t)l * bw.rows;
+    qa.vc_rows = bw.vc + (size_t)l * bw.rows;
+  }
+  launch_qkv_post(qa, s);
+  AttnDecodeArgs aa;
+  aa.Hq = m.Hq; aa.Hkv = lc.kv_heads; aa.d = d; aa.window = lc.window; aa.q = w.qo; aa.out = w.comb;
+  aa.cap = maxcap; aa.batch = B; aa.pos_rows = bw.pos; aa.cap_rows = bw.caps;
+  aa.kc_rows = bw.kc + (size_t)l * bw.rows;
+  aa.vc_rows = bw.vc + (size_t)l * bw.rows;
+  launch_attn_decode_cluster(aa, s);
+  prefill_linear(c, w.comb, B, L.o, L.to, w.attn, kEpiPlain, nullptr);
+  const bool ple = m.P > 0;
+  launch_norm_residual_rows(w.attn, cur, B, H, L.post_attn_ln, c.eps, false, 0, other, s);
+  launch_rmsnorm_rows(other, B, H, L.pre_ff_ln, c.eps, w.nrm, s);
+  prefill_geglu(c, w.nrm, B, L, w.hbuf);
+  prefill_linear(c, w.hbuf, B, L.down, L.tdown, w.attn, kEpiPlain, nullptr);
+  launch_norm_residual_rows(w.attn, other, B, H, L.post_ff_ln, c.eps, !ple && L.has_scalar, L.scalar, cur, s);
+  int32_t* result = cur;
+  if (ple) {
+    prefill_linear(c, cur, B, L.ple_gate, L.tpg, w.g, kEpiGeluMul, w.ple_all + (size_t)l * B * m.P);
+    prefill_linear(c, w.g, B, L.ple_proj, L.tpp, w.pr, kEpiPlain, nullptr);
+    launch_norm_residual_rows(w.pr, cur, B, H, L.ple_norm, c.eps, L.has_scalar, L.scalar, other, s);
+    result = other;
+  }
+  launch_scatter_rows(result, B, H, bw.dec_out, (size_t)l * H, s);
+  return result;
+}
+
+// Whether the batched path can run these sequences (distinct, and the
+// batched cluster attention fits every layer's window).
+static bool batch_supported(Ctx& c, Seq* const* seqs, int B) {
+  if (B < 2) return false;
+  for (int i = 0; i < B; ++i)
+    for (int j = 0; j < i; ++j)
+      if (seqs[i] == seqs[j]) return false;
+  int maxcap = 0;
+  for (int i = 0; i < B; ++i) maxcap = std::max(maxcap, seqs[i]->cap);
+  for (const LayerDev& L : c.layers)
+    if (!attn_decode_cluster_fits(c.cfg.Hq, L.cfg.kv_heads, L.cfg.head_dim, L.cfg.window, maxcap, 0)) return false;
+  return true;
+}
+
+static void decode_batch(Ctx& c, Seq* const* seqs, const uint32_t* tokens, int B) {
+  const ModelCfg& m = c.cfg;
+  PrefillWs& w = c.pw;
+  cudaStream_t s = c.stream;
+  batch_tables(c, seqs, B);
+  auto& bw = c.bw;
+  int maxcap = 0;
+  for (int i = 0; i < B; ++i) maxcap = std::max(maxcap, seqs[i]->cap);
+  CK(cudaMemcpyAsync(bw.ids, tokens, (size_t)B * 4, cudaMemcpyHostToDevice, s));
+  launch_embed(bw.ids, B, c.emb, c.emb_scale, w.xa, c.d_err, s);
+  if (m.P > 0) {
+    prefill_linear(c, w.xa, B, c.ple_model_proj, c.t_ple_model, w.ple_proj, kEpiPlain, nullptr);
+    PleArgs pa;
+    pa.S = B; pa.L = m.L; pa.P = m.P; pa.ids = bw.ids; pa.proj = w.ple_proj; pa.table = c.ple_table;
+    pa.norm = c.ple_proj_norm; pa.eps = c.eps; pa.emb_scale = c.ple_emb_scale; pa.proj_scale = c.ple_proj_scale;
+    pa.in_scale = c.ple_in_scale; pa.out = w.ple_all; pa.err = c.d_err;
+    launch_ple(pa, s);
+  }
+  int32_t* cur = w.xa;
+  for (int l = 0; l < m.L; ++l) cur = const_cast<int32_t*>(decode_batch_layer(c, B, maxcap, l, cur));
+  launch_rmsnorm_rows(cur, B, m.H, c.final_norm, c.eps, w.nrm, s);
+  prefill_linear(c, w.nrm, B, c.lm_head, c.t_lm_head, bw.logits, kEpiPlain, nullptr);
+  if (m.has_softcap) launch_softcap(bw.logits, B * m.V, c.softcap, s);
+  launch_scatter_rows(bw.logits, B, m.V, bw.logits_dst, 0, s);
+  launch_add_i32_rows(bw.pos, B, 1, s);
+  CK(cudaGetLastError());
+  for (int i = 0; i < B; ++i) {
+    seqs[i]->pos += 1;
+    seqs[i]->last_was_prefill = false;
+  }
+}
+
 static void ensure_decode_graph(Ctx& c, Seq& q) {
   if (q.graph) return;
   cudaGraph_t g;
@@ -1652,13 +1806,32 @@ int32_t rdet_decode(rdet_ctx* ctx, rdet_seq* const* seqs, const uint32_t* tokens
       check_decode_ready(c, *seqs[i]->s);
       check_token(c, tokens[i]);
     }
-    for (size_t i = 0; i < nseq; ++i) {
-      Seq& q = *seqs[i]->s;
-      ensure_decode_graph(c, q);
-      CK(cudaMemcpyAsync(q.d_token, tokens + i, 4, cudaMemcpyHostToDevice, c.stream));
-      CK(cudaGraphLaunch(q.graph, c.stream));
-      q.pos += 1;
-      q.last_was_prefill = false;
+    std::vector<Seq*> batch(nseq);
+    for (size_t i = 0; i < nseq; ++i) batch[i] = seqs[i]->s.get();
+    if (batch_supported(c, batch.data(), (int)nseq)) {
+      // chunks of at most max_prefill rows (the row workspaces' size)
+      for (size_t i0 = 0; i0 < nseq; i0 += c.max_prefill) {
+        const int B = (int)std::min<size_t>(c.max_prefill, nseq - i0);
+        if (B >= 2) {
+          decode_batch(c, batch.data() + i0, tokens + i0, B);
+          continue;
+        }
+        Seq& q = *batch[i0];
+        ensure_decode_graph(c, q);
+        CK(cudaMemcpyAsync(q.d_token, tokens + i0, 4, cudaMemcpyHostToDevice, c.stream));
+        CK(cudaGraphLaunch(q.graph, c.stream));
+        q.pos += 1;
+        q.last_was_prefill = false;
+      }
+    } else {
+      for (size_t i = 0; i < nseq; ++i) {
+        Seq& q = *batch[i];
+        ensure_decode_graph(c, q);
+        CK(cudaMemcpyAsync(q.d_token, tokens + i, 4, cudaMemcpyHostToDevice, c.stream));
+        CK(cudaGraphLaunch(q.graph, c.stream));
+        q.pos += 1;
+        q.last_was_prefill = false;
+      }
     }
     CK(cudaStreamSynchronize(c.stream));
     check_err_flag(c, "decode");

@@ -177,3 +177,48 @@ def test_tensor_core_prefill_long_prompt(variant):
     t.prefill(ids)
     assert s.commitment(rdet.BUF_HIDDEN) == t.commitment(rdet.BUF_HIDDEN)
     assert np.array_equal(s.read(rdet.BUF_LOGITS), t.read(rdet.BUF_LOGITS))
+
+
+def check_batched_equals_solo(cfg, width, lens, steps, seed):
+    cfg = {"text_config": {k: v for k, v in cfg["text_config"].items() if v is not None}}
+    V = cfg["text_config"]["vocab_size"]
+    d = write_model(cfg, seed=seed, width=width)
+    m = rdet.Model.open(d, max_prefill=max(max(lens), len(lens)))
+    batch = [m.new_sequence(n + steps + 4) for n in lens]
+    solo = [m.new_sequence(n + steps + 4) for n in lens]
+    for i, n in enumerate(lens):
+        ids = lcg_ids(n, V, 100 + i)
+        batch[i].prefill(ids)
+        solo[i].prefill(ids)
+    L = m.L
+    for step in range(steps):
+        toks = [s.select() for s in batch]
+        assert toks == [s.select() for s in solo], step
+        rdet.decode_batch(m, batch, toks)
+        for s, t in zip(solo, toks):
+            s.decode(t)
+        for i, (a, b) in enumerate(zip(batch, solo)):
+            assert np.array_equal(a.read(rdet.BUF_LOGITS), b.read(rdet.BUF_LOGITS)), (step, i)
+            assert a.commitment(rdet.BUF_HIDDEN) == b.commitment(rdet.BUF_HIDDEN), (step, i)
+            assert a.commitment(rdet.BUF_LAYER_OUTPUT, L // 2) == b.commitment(rdet.BUF_LAYER_OUTPUT, L // 2)
+            assert a.commitment(rdet.BUF_KV) == b.commitment(rdet.BUF_KV), (step, i)
+            assert a.position == b.position
+
+
+@pytest.mark.parametrize("variant,B", [("default", 5), ("default", 40), ("k_eq_v_global_kv", 40),
+                                       ("gqa8", 33), ("no_share_untied_i32", 34), ("bidirectional_window", 6)])
+def test_batched_ragged_decode_equals_solo(variant, B):
+    # ragged batch: each sequence has its own length (some past the window);
+    # >= 32 rows take the tensor-core GEMMs, fewer the CUDA-core linear
+    cfg, width = VARIANTS[variant]
+    lens = [1 + (7 * i * i + 3 * i) % 37 for i in range(B)]
+    check_batched_equals_solo(cfg, width, lens, 4, seed=30 + B)
+
+
+def test_batched_ragged_decode_e4b_head_dims():
+    cfg = mini_config(hidden_size=256, intermediate_size=512, num_attention_heads=8, num_key_value_heads=2,
+                      head_dim=256, global_head_dim=512, sliding_window=512, hidden_size_per_layer_input=32,
+                      num_hidden_layers=4, num_kv_shared_layers=1, vocab_size=300,
+                      layer_types=["sliding_attention", "full_attention", "sliding_attention", "sliding_attention"])
+    lens = [5 + (97 * i) % 640 for i in range(36)]
+    check_batched_equals_solo(cfg, 16, lens, 3, seed=44)
