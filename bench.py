@@ -337,6 +337,40 @@ def run_ours(args, rank, world, local_rank):
         e2e_sec = float(tt[0])
     e2e = {"value": world * n_e2e / e2e_sec, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
            "steps": n_e2e}
+    # batched ragged decode (BASELINE config 5 shape): 64 sequences, prompt
+    # lengths 128 + draw % 3969 (seeded), one batched decode_transition per step
+    batched = None
+    if args.batch > 0:
+        bm, bstream = model, stream  # max_prefill (the context) >= the batch rows
+        lens = [128 + (x % 3969) for x in lcg_ids(args.batch, 1 << 30, SEED + 7 + rank)]
+        seqs = [bm.new_sequence(n + args.batch_steps + 8) for n in lens]
+        for i, (sq, n) in enumerate(zip(seqs, lens)):
+            sq.prefill(lcg_ids(n, t["vocab_size"], SEED + 100 + i))
+        toks = [sq.select() for sq in seqs]
+        for _ in range(2):  # warm-up
+            rdet.decode_batch(bm, seqs, toks)
+            toks = [sq.select() for sq in seqs]
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record(bstream)
+        for _ in range(args.batch_steps):
+            rdet.decode_batch(bm, seqs, toks)
+        b1.record(bstream)
+        torch.cuda.synchronize()
+        bsec = b0.elapsed_time(b1) / 1000
+        if dist:
+            tt = torch.tensor([bsec], dtype=torch.float64, device=f"cuda:{local_rank}")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            bsec = float(tt[0])
+        batched = {"sequences": args.batch, "context": f"128 + draw mod 3969 (seeded), mean {sum(lens) // len(lens)}",
+                   "steps": args.batch_steps, "tok_s": world * args.batch * args.batch_steps / bsec,
+                   "ms_per_step": 1000 * bsec / args.batch_steps,
+                   "note": "device-timed batched decode_transition (same token fed back: decode cost does not depend "
+                           "on token values)"}
+        for sq in seqs:
+            sq.free()
     # roofline of the dominant kernel (det GEMV)
     per, gbs, bytes_per_launch, sec_per_launch = gemv_roofline(torch, rdet, cfg, local_rank)
     peak, peak_kind = peaks()
@@ -367,6 +401,7 @@ def run_ours(args, rank, world, local_rank):
                    "weight_bytes_hbm": weight_bytes},
         "prefill": {"tokens": ctx, "tok_s": ctx / prefill_s, "seconds": prefill_s},
         "e2e": e2e,
+        "batched_decode": batched,
         "gpu_launches": kernels_per_step * args.steps,
         "roofline": {"bound": "hbm", "kernel": "rdet::gemv3_kernel", "achieved": gbs, "peak": peak,
                      "unit": "GB/s", "frac": gbs / peak, "peak_kind": peak_kind,
@@ -396,6 +431,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=64, help="sequences of the batched ragged decode line (0: skip)")
+    ap.add_argument("--batch-steps", type=int, default=8)
     ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc"],
                     help="run a few launches of one kernel at E4B shapes for an ncu capture, then exit")
     args = ap.parse_args()
