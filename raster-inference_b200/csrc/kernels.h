@@ -92,9 +92,22 @@ bool tc_prepare_weight(TcWeight& t, const DevMat& g, const DevMat* u, void* mem,
 size_t tc_act_bytes(int S, int K);
 // X [S, K] (16-byte aligned, K % 16 == 0) -> planes in `mem` (tc_act_bytes)
 bool tc_prepare_act(TcAct& a, const int32_t* X, int S, int K, void* mem, cudaStream_t s);
-// Y [S, N] = epilogue(requantize(X W^T)); a pair writes mul_sat(gelu(gate), up)
-void launch_tc_linear(const TcAct& a, const TcWeight& w, int32_t* Y, int32_t epi, const int32_t* vec,
-                      cudaStream_t s);
+// Output of the tensor-core linear.  y: Y [S, N] = epilogue(requantize(X W^T))
+// (a pair writes mul_sat(gelu(gate), up); kEpiGeluMul multiplies by
+// vec[s * ldv + n]).  y64 instead: the exact wrapping i64 sums before
+// requantize (needs scratch).  With scratch the K loop may be split across
+// CTAs when the output tiles alone would leave SMs idle.
+struct TcOut {
+  int32_t* y = nullptr;
+  int64_t* y64 = nullptr;
+  int32_t epi = 0;
+  const int32_t* vec = nullptr;
+  int32_t ldv = 0;              // 0: N
+  void* scratch = nullptr;      // split-K partials, [splits][S][rows] u64
+  size_t scratch_bytes = 0;
+};
+// false when y64 is asked for and the scratch cannot hold the partial sums
+bool launch_tc_linear(const TcAct& a, const TcWeight& w, const TcOut& o, cudaStream_t s);
 void tc_init();  // per-device kernel attributes (called by kernels_init)
 int tc_error_flag(bool reset);  // nonzero when a tensor-core pipeline wait gave up
 

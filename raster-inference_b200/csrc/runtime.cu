@@ -430,6 +430,8 @@ struct Ctx {
   TcWeight t_ple_model, t_lm_head;
   void* tc_act = nullptr;        // activation byte planes of the current linear
   int tc_act_k = 0;              // largest K the activation planes hold
+  void* tc_split = nullptr;      // split-K partial sums of the tensor-core linear
+  size_t tc_split_bytes = 0;
   // batched decode: per-row tables (device) and the batch logits
   struct {
     int rows = 0;                  // rows the tables hold
@@ -713,6 +715,8 @@ static void alloc_workspaces(Ctx& c) {
   CK(cudaMemset(c.d_err, 0, 4));
 }
 
+constexpr size_t kTcSplitScratch = 64ull << 20;  // split-K partials for short row counts
+
 // Byte planes of every prefill weight the tensor-core linear can take (i16,
 // K a multiple of 16): one more copy of those weights in HBM.
 static void prepare_tensor_cores(Ctx& c) {
@@ -746,6 +750,8 @@ static void prepare_tensor_cores(Ctx& c) {
   if (kmax > 0) {
     c.tc_act = c.dalloc(tc_act_bytes((int)c.max_prefill, kmax));
     c.tc_act_k = kmax;
+    c.tc_split_bytes = kTcSplitScratch;
+    c.tc_split = c.dalloc(c.tc_split_bytes);
   }
   CK(cudaStreamSynchronize(c.stream));
   CK(cudaGetLastError());
@@ -771,7 +777,13 @@ static void prefill_linear(Ctx& c, const int32_t* X, int S, const DevMat& w, con
       REQUIRE(tc_prepare_act(ap.a, X, S, w.cols, c.tc_act, s), RDET_E_CUDA, "tensor map encoding failed");
       ap.ready = true;
     }
-    launch_tc_linear(ap.a, t, Y, epi, vec, s);
+    TcOut o;
+    o.y = Y;
+    o.epi = epi;
+    o.vec = vec;
+    o.scratch = c.tc_split;
+    o.scratch_bytes = c.tc_split_bytes;
+    launch_tc_linear(ap.a, t, o, s);
     return;
   }
   launch_linear(X, S, w, Y, epi, vec, s);
@@ -782,7 +794,11 @@ static void prefill_geglu(Ctx& c, const int32_t* X, int S, const LayerDev& L, in
   if (c.tc && L.tgu.planes && S >= kTcMinRows && L.gate.cols <= c.tc_act_k) {
     TcAct a;
     REQUIRE(tc_prepare_act(a, X, S, L.gate.cols, c.tc_act, s), RDET_E_CUDA, "tensor map encoding failed");
-    launch_tc_linear(a, L.tgu, Y, kEpiPlain, nullptr, s);
+    TcOut o;
+    o.y = Y;
+    o.scratch = c.tc_split;
+    o.scratch_bytes = c.tc_split_bytes;
+    launch_tc_linear(a, L.tgu, o, s);
     return;
   }
   launch_linear_geglu(X, S, L.gate, L.up, Y, s);
@@ -2109,7 +2125,8 @@ int32_t rdet_det_linear(const int32_t* x, uint32_t n_rows_x, const void* w, int3
       int dev = 0;
       CK(cudaGetDevice(&dev));
       const size_t wb = (tc_weight_bytes((int)rows, (int)cols, false) + 255) & ~(size_t)255;
-      const size_t need = wb + tc_act_bytes((int)n_rows_x, (int)cols);
+      const size_t ab = (tc_act_bytes((int)n_rows_x, (int)cols) + 255) & ~(size_t)255;
+      const size_t need = wb + ab + kTcSplitScratch;
       std::lock_guard<std::mutex> lk(g_lin_scratch_mu);
       LinScratch& sc = g_lin_scratch[dev];
       if (sc.bytes < need) {
@@ -2128,7 +2145,11 @@ int32_t rdet_det_linear(const int32_t* x, uint32_t n_rows_x, const void* w, int3
       REQUIRE(tc_prepare_weight(tw, m, nullptr, base, s), RDET_E_CUDA, "tensor map encoding failed");
       REQUIRE(tc_prepare_act(ta, x, (int)n_rows_x, (int)cols, base + wb, s), RDET_E_CUDA,
               "tensor map encoding failed");
-      launch_tc_linear(ta, tw, y, kEpiPlain, nullptr, s);
+      TcOut o;
+      o.y = y;
+      o.scratch = base + wb + ab;
+      o.scratch_bytes = kTcSplitScratch;
+      launch_tc_linear(ta, tw, o, s);
     } else {
       launch_linear(x, (int)n_rows_x, m, y, kEpiPlain, nullptr, s);
     }

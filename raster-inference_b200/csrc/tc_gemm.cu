@@ -31,6 +31,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -218,11 +219,16 @@ __global__ void tc_weight_prep_kernel(const int16_t* __restrict__ W, const int16
 // column once with accumulate off before anything accumulates into it
 // (limbs 0 and 2 fresh, limb 1 onto them, limb 3 split into its low-plane
 // half that accumulates and its high-plane half that is fresh).
+// EPI 3 (split K): work item i is tile i / ks, K range i % ks of ks equal
+// parts; the epilogue writes the raw sum of the range, sum_g 2^(8g) G_g (no
+// corrections, not requantized), to part[(i % ks)][S][nrows] and
+// tc_splitk_reduce finishes the output.
 template <int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_linear_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
                      const uint64_t* __restrict__ arow, const uint64_t* __restrict__ brow, int S, int N, int K,
-                     int ntiles_n, int ntiles, int32_t* __restrict__ Y, const int32_t* __restrict__ vec) {
+                     int ntiles_n, int ntiles, int ks, int nrows, int32_t* __restrict__ Y,
+                     const int32_t* __restrict__ vec, int ldv, uint64_t* __restrict__ part) {
   extern __shared__ __align__(16) unsigned char tc_smem_raw[];
   __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf, tmem_empty;
   __shared__ uint32_t tmem_holder;
@@ -232,7 +238,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   int32_t* stage_out = reinterpret_cast<int32_t*>(smem + (size_t)kTcStages * kTcStage);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = (K + kTcKB - 1) / kTcKB;
-  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int nitems = ntiles * ks;  // ks == 1 except in split-K mode
+  const int my_tiles = blockIdx.x < nitems ? (nitems - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (threadIdx.x == 0) {
     for (int i = 0; i < kTcStages; ++i) {
@@ -260,9 +267,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       int q = 0;
       for (int it = 0; it < my_tiles; ++it) {
-        const int t = blockIdx.x + it * gridDim.x;
+        const int item = blockIdx.x + it * gridDim.x, t = item / ks, sp = item % ks;
         const int m0 = (t / ntiles_n) * kTcM, r0 = (t % ntiles_n) * kTcN;
-        for (int kb = 0; kb < nkb; ++kb, ++q) {
+        const int kb0 = (int)((int64_t)nkb * sp / ks), kb1 = (int)((int64_t)nkb * (sp + 1) / ks);
+        for (int kb = kb0; kb < kb1; ++kb, ++q) {
           const int st = q % kTcStages;
           if (q >= kTcStages && !tc_mbar_wait(&empty[st], ((q / kTcStages) - 1) & 1)) fail = 1;
           unsigned char* sbuf = smem + (size_t)st * kTcStage;
@@ -276,12 +284,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == kTcEpiWarps + 1) {
     // ---- MMA issue
     if (lane == 0) {
-      int q = 0;
-      const int qlast = my_tiles * nkb;
+      int q = 0, qlast = 0;
       for (int it = 0; it < my_tiles; ++it) {
+        const int sp = (blockIdx.x + it * gridDim.x) % ks;
+        qlast += (int)((int64_t)nkb * (sp + 1) / ks) - (int)((int64_t)nkb * sp / ks);
+      }
+      for (int it = 0; it < my_tiles; ++it) {
+        const int sp = (blockIdx.x + it * gridDim.x) % ks;
+        const int kb0 = (int)((int64_t)nkb * sp / ks), kb1 = (int)((int64_t)nkb * (sp + 1) / ks);
         if (it > 0 && !tc_mbar_wait(&tmem_empty, (it - 1) & 1)) fail = 1;
         tc_fence_after();
-        for (int kb = 0; kb < nkb; ++kb, ++q) {
+        for (int kb = kb0; kb < kb1; ++kb, ++q) {
           const int st = q % kTcStages;
           if (!tc_mbar_wait(&full[st], (q / kTcStages) & 1)) fail = 1;
           tc_fence_after();
@@ -293,7 +306,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint64_t ad[4] = {smem_desc_sw64(su32(sbuf) + 32 * j), smem_desc_sw64(su32(sbuf + kTcATile) + 32 * j),
                                     smem_desc_sw64(su32(sbuf + 2 * kTcATile) + 32 * j),
                                     smem_desc_sw64(su32(sbuf + 3 * kTcATile) + 32 * j)};
-            if (kb == 0 && j == 0) {
+            if (kb == kb0 && j == 0) {
               tc_mma(tmem + 0 * kTcN, ad[0], bdesc, kTcIdesc, 0u);
               tc_mma(tmem + 2 * kTcN, ad[2], bdesc, kTcIdesc, 0u);
               tc_mma(tmem + 1 * kTcN, ad[1], bdesc, kTcIdesc, 1u);
@@ -319,7 +332,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int rl = 32 * quarter + lane;
     const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16);
     for (int it = 0; it < my_tiles; ++it) {
-      const int t = blockIdx.x + it * gridDim.x;
+      const int item = blockIdx.x + it * gridDim.x, t = item / ks, sp = item % ks;
       const int m0 = (t / ntiles_n) * kTcM, nt = t % ntiles_n, r0 = nt * kTcN;
       const int nbase = EPI == 2 ? nt * (kTcN / 2) : r0;
       const int m = m0 + rl;
@@ -327,6 +340,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint64_t corr = (mrow ? (arow[m] << 15) : 0) - ((uint64_t)K << 46);
       if (!tc_mbar_wait(&accf, it & 1)) fail = 1;
       tc_fence_after();
+      if (EPI == 3) {
+        // raw partial of this K range for all 96 plane rows, straight from registers
+        for (int c0 = half * (kTcN / 2); c0 < (half + 1) * (kTcN / 2); c0 += 8) {
+          uint32_t g[5][8];
+#pragma unroll
+          for (int gg = 0; gg < 5; ++gg) tmem_ld8(tbase + kTcN * gg + c0, g[gg]);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if (mrow) {
+            uint64_t* dst = part + ((size_t)sp * S + m) * nrows + r0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int j = c0 + i;
+              if (r0 + j < nrows)
+                dst[j] = (uint64_t)g[0][i] + ((uint64_t)g[1][i] << 8) + ((uint64_t)g[2][i] << 16) +
+                         ((uint64_t)g[3][i] << 24) + ((uint64_t)g[4][i] << 32);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&tmem_empty)) : "memory");
+        continue;
+      }
+      if constexpr (EPI != 3) {
       for (int c0 = half * kHalf; c0 < (half + 1) * kHalf; c0 += 8) {
         uint32_t g[5][8], h[5][8];
 #pragma unroll
@@ -353,7 +390,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               accu -= corr + (brow[r0 + kTcN / 2 + j] << 31);
               y = mul_sat(gelu_act(y), requantize((int64_t)accu));
             } else if (EPI == 1) {
-              y = mul_sat(gelu_act(y), vec[(size_t)m * N + n]);
+              y = mul_sat(gelu_act(y), vec[(size_t)m * ldv + n]);
             }
           }
           stage_out[rl * kTcOutStride + j] = y;
@@ -373,6 +410,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       asm volatile("bar.sync 1, %0;" ::"n"(32 * kTcEpiWarps) : "memory");  // staging free again
+      }
     }
   }
   tc_fence_before();
@@ -381,6 +419,43 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcCols) : "memory");
+  }
+}
+
+// Split-K finish: y = sum over splits of the raw partials, minus the row-sum
+// corrections over the full K, then the epilogue.  MODE 0 plain, 1
+// gelu(y) * vec[s, n] (row stride ldv), 2 gate/up pair, 3 the exact i64 sum
+// before requantize (a tensor-parallel partial).
+template <int MODE>
+__global__ void tc_splitk_reduce_kernel(const uint64_t* __restrict__ part, int ks, int S, int nrows, int N, int K,
+                                        const uint64_t* __restrict__ arow, const uint64_t* __restrict__ brow,
+                                        int32_t* __restrict__ Y, int64_t* __restrict__ Y64,
+                                        const int32_t* __restrict__ vec, int ldv) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const size_t total = (size_t)S * N;
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const int m = (int)(e / N), n = (int)(e % N);
+    const int r = MODE == 2 ? kTcN * (n / (kTcN / 2)) + n % (kTcN / 2) : n;
+    const uint64_t corr = (arow[m] << 15) - ((uint64_t)K << 46);
+    uint64_t acc = 0;
+    for (int sp = 0; sp < ks; ++sp) acc += part[((size_t)sp * S + m) * nrows + r];
+    acc -= corr + (brow[r] << 31);
+    if (MODE == 3) {
+      Y64[e] = (int64_t)acc;
+      continue;
+    }
+    int32_t y = requantize((int64_t)acc);
+    if (MODE == 2) {
+      const int ru = r + kTcN / 2;
+      uint64_t accu = 0;
+      for (int sp = 0; sp < ks; ++sp) accu += part[((size_t)sp * S + m) * nrows + ru];
+      accu -= corr + (brow[ru] << 31);
+      y = mul_sat(gelu_act(y), requantize((int64_t)accu));
+    } else if (MODE == 1) {
+      y = mul_sat(gelu_act(y), vec[(size_t)m * ldv + n]);
+    }
+    Y[e] = y;
   }
 }
 
@@ -453,6 +528,7 @@ void tc_init() {
   cudaFuncSetAttribute(tc_linear_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
   cudaFuncSetAttribute(tc_linear_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
   cudaFuncSetAttribute(tc_linear_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+  cudaFuncSetAttribute(tc_linear_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
 }
 
 bool tc_supported() {
@@ -506,22 +582,57 @@ bool tc_prepare_act(TcAct& a, const int32_t* X, int S, int K, void* mem, cudaStr
   return encode_planes(a.map, a.planes, 4, S, K, kTcM);
 }
 
-void launch_tc_linear(const TcAct& a, const TcWeight& w, int32_t* Y, int32_t epi, const int32_t* vec,
-                      cudaStream_t s) {
+bool launch_tc_linear(const TcAct& a, const TcWeight& w, const TcOut& o, cudaStream_t s) {
   const int ntiles_n = (w.nrows + kTcN - 1) / kTcN;
   const int ntiles = ntiles_n * ((a.S + kTcM - 1) / kTcM);
-  const int grid = ntiles < sm_count() ? ntiles : sm_count();
+  const int nkb = (a.K + kTcKB - 1) / kTcKB;
+  const int sms = sm_count();
   const CUtensorMap& am = *reinterpret_cast<const CUtensorMap*>(a.map);
   const CUtensorMap& bm = *reinterpret_cast<const CUtensorMap*>(w.map);
-  if (w.pair)
-    tc_launch(tc_linear_kernel<2>, dim3(grid), dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N,
-              a.K, ntiles_n, ntiles, Y, vec);
-  else if (epi == kEpiGeluMul)
-    tc_launch(tc_linear_kernel<1>, dim3(grid), dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N,
-              a.K, ntiles_n, ntiles, Y, vec);
+  const int ldv = o.ldv > 0 ? o.ldv : w.N;
+  // split K when the tiles alone would leave most SMs idle (few rows), or
+  // when the caller wants the i64 sum; at least 4 stages per split
+  int ks = 1;
+  if (o.scratch && (ntiles * 2 <= sms || o.y64)) {
+    const size_t per_split = (size_t)a.S * w.nrows * 8;
+    ks = std::max(1, std::min(sms / ntiles, nkb / 4));
+    ks = (int)std::min<size_t>((size_t)ks, o.scratch_bytes / per_split);
+    if (ks < 1) ks = 1;
+  }
+  const bool split = o.scratch && (ks > 1 || o.y64) && (size_t)ks * a.S * w.nrows * 8 <= o.scratch_bytes;
+  if (o.y64 && !split) return false;  // the i64 sums need the split-K scratch
+  if (!split) {
+    const int grid = std::min(ntiles, sms);
+    if (w.pair)
+      tc_launch(tc_linear_kernel<2>, dim3(grid), dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N,
+                a.K, ntiles_n, ntiles, 1, w.nrows, o.y, o.vec, ldv, (uint64_t*)nullptr);
+    else if (o.epi == kEpiGeluMul)
+      tc_launch(tc_linear_kernel<1>, dim3(grid), dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N,
+                a.K, ntiles_n, ntiles, 1, w.nrows, o.y, o.vec, ldv, (uint64_t*)nullptr);
+    else
+      tc_launch(tc_linear_kernel<0>, dim3(grid), dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N,
+                a.K, ntiles_n, ntiles, 1, w.nrows, o.y, o.vec, ldv, (uint64_t*)nullptr);
+    return true;
+  }
+  uint64_t* part = static_cast<uint64_t*>(o.scratch);
+  const int grid = std::min(ntiles * ks, sms);
+  tc_launch(tc_linear_kernel<3>, dim3(grid), dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N, a.K,
+            ntiles_n, ntiles, ks, w.nrows, (int32_t*)nullptr, (const int32_t*)nullptr, ldv, part);
+  const size_t total = (size_t)a.S * w.N;
+  const int rblocks = (int)std::min<size_t>((total + 255) / 256, (size_t)sms * 8);
+  if (o.y64)
+    tc_launch(tc_splitk_reduce_kernel<3>, dim3(rblocks), dim3(256), 0, s, (const uint64_t*)part, ks, a.S, w.nrows,
+              w.N, a.K, a.rowsum, w.rowsum, (int32_t*)nullptr, o.y64, o.vec, ldv);
+  else if (w.pair)
+    tc_launch(tc_splitk_reduce_kernel<2>, dim3(rblocks), dim3(256), 0, s, (const uint64_t*)part, ks, a.S, w.nrows,
+              w.N, a.K, a.rowsum, w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv);
+  else if (o.epi == kEpiGeluMul)
+    tc_launch(tc_splitk_reduce_kernel<1>, dim3(rblocks), dim3(256), 0, s, (const uint64_t*)part, ks, a.S, w.nrows,
+              w.N, a.K, a.rowsum, w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv);
   else
-    tc_launch(tc_linear_kernel<0>, dim3(grid), dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N,
-              a.K, ntiles_n, ntiles, Y, vec);
+    tc_launch(tc_splitk_reduce_kernel<0>, dim3(rblocks), dim3(256), 0, s, (const uint64_t*)part, ks, a.S, w.nrows,
+              w.N, a.K, a.rowsum, w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv);
+  return true;
 }
 
 }  // namespace rdet
