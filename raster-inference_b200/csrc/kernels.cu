@@ -1836,11 +1836,24 @@ bool attn_decode_cluster_fits(int Hq, int Hkv, int d, int window, int cap, int r
   const int CL = g_attn_cluster ? g_attn_cluster : 8;
   if (!(Hkv > 0 && Hq % Hkv == 0 && d > 0 && d % 4 == 0 && d <= 512 && (rotary >> 1) <= 256)) return false;
   const int gc = ac_group(Hq, Hkv, d);
-  return gc <= 8 - 2 && ac_smem(gc, d, ac_rmax(window, cap, CL)) <= kAcMaxSmem;
+  return gc <= 8 - 2 && d <= 128 * CL && ac_smem(gc, d, ac_rmax(window, cap, CL)) <= kAcMaxSmem;
 }
 
+// Cluster size of batched launches: the batch rows already fill the GPU, so
+// each sequence gets a small cluster (fewer fixed per-CTA phase latencies).
+#ifndef RDET_AC_BATCH_CL
+#define RDET_AC_BATCH_CL 2
+#endif
+
 void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s) {
-  const int CL = g_attn_cluster ? g_attn_cluster : 8;
+  int CL = g_attn_cluster ? g_attn_cluster : 8;
+  if (a.batch > 1) {
+    // a CTA finalises d / CL output dims (at most 128: the first-max V row
+    // is staged in a [GC][128] shared array)
+    int cl = RDET_AC_BATCH_CL;
+    while (cl < CL && (a.d > 128 * cl || ac_smem(1, a.d, ac_rmax(a.window, a.cap, cl)) > kAcMaxSmem)) cl *= 2;
+    CL = cl < CL ? cl : CL;
+  }
   const int rmax = ac_rmax(a.window, a.cap, CL);
   // (batched rows use the library's own 16-byte aligned cache allocations)
   const bool aligned = ((reinterpret_cast<uintptr_t>(a.k_cache) | reinterpret_cast<uintptr_t>(a.v_cache)) & 15) == 0;
