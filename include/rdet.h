@@ -178,6 +178,23 @@ int32_t rdet_det_attention_decode_noalloc(const int32_t* q, const int32_t* k_cac
 
 /* The CUDA stream (cudaStream_t) on which the context launches all of its
  * work, for callers that order their own work or CUDA events against it. */
+/* Tensor-parallel batched decode (no counterpart in the reference, which runs
+ * one process on the CPU).  Every rank
+ * opens the same model on its own GPU; rank 0 creates an id with
+ * rdet_nccl_unique_id (128 bytes), the caller hands it to every rank, and each
+ * calls rdet_tp_init with its rank.  Afterwards rdet_decode on two or more
+ * sequences shards query heads, the MLP intermediate rows, the per-layer-input
+ * rows and the vocabulary across the ranks: column-slice projections give exact
+ * i64 partial sums that an NCCL int64 all-reduce completes before requantize,
+ * and logits are all-gathered, so each rank's results are identical to an
+ * unsharded decode.  All ranks must call rdet_decode with the same sequences
+ * and tokens.  Prefill, single-sequence decode and commitments are unchanged
+ * (every rank keeps the whole model and complete KV caches).  Needs the
+ * tensor-core path (sm_100, i16 weights) and libnccl.so.2 at run time. */
+int32_t rdet_nccl_unique_id(void* id_out, size_t len);
+int32_t rdet_tp_init(rdet_ctx* ctx, int32_t rank, int32_t world, const void* id, size_t len);
+int32_t rdet_tp_world(rdet_ctx* ctx); /* 1 when not sharded */
+
 /* 1 when this context's prefill linears run on the tcgen05 tensor cores (an
  * sm_100 device, the context opened without RDET_FLAG_NO_TENSOR_CORES and at
  * least one eligible weight), else 0.  Prompts shorter than 32 tokens use the

@@ -37,7 +37,7 @@ SYMBOLS = [
     "rdet_seq_position", "rdet_embed", "rdet_prefill", "rdet_prefill_begin", "rdet_prefill_range",
     "rdet_prefill_finalize", "rdet_select", "rdet_decode", "rdet_decode_begin", "rdet_decode_range",
     "rdet_decode_finalize", "rdet_generate", "rdet_read", "rdet_commitment", "rdet_det_gemv", "rdet_det_linear",
-    "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_get_stream", "rdet_tensor_core_prefill", "rdet_seq_kernels_per_step", "rdet_last_error",
+    "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_get_stream", "rdet_tensor_core_prefill", "rdet_nccl_unique_id", "rdet_tp_init", "rdet_tp_world", "rdet_seq_kernels_per_step", "rdet_last_error",
     "rdet_version",
 ]
 
@@ -98,6 +98,9 @@ def lib() -> C.CDLL:
         "rdet_det_attention_decode_noalloc": [p, p, p, u32, u32, u32, u32, u32, u32, p, p],
         "rdet_get_stream": [p, p],
         "rdet_tensor_core_prefill": [p],
+        "rdet_nccl_unique_id": [p, sz],
+        "rdet_tp_init": [p, i32, i32, p, sz],
+        "rdet_tp_world": [p],
         "rdet_seq_kernels_per_step": [p, p],
         "rdet_last_error": [C.c_char_p, sz],
     }
@@ -165,6 +168,16 @@ class Model:
             self.close()
         except Exception:
             pass
+
+    def tp_init(self, rank: int, world: int, uid: bytes):
+        """Shard the batched decode over `world` ranks (rdet_tp_init); every rank
+        opened the same model and passes the same id from nccl_unique_id()."""
+        buf = C.create_string_buffer(bytes(uid), len(uid))
+        _check(lib().rdet_tp_init(self._h, rank, world, buf, len(uid)))
+
+    @property
+    def tp_world(self) -> int:
+        return int(lib().rdet_tp_world(self._h))
 
     @property
     def tensor_core_prefill(self) -> bool:
@@ -274,6 +287,13 @@ class Sequence:
 
     def logits(self) -> np.ndarray:
         return self.read(BUF_LOGITS)
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL id (128 bytes) for Model.tp_init on every rank."""
+    buf = C.create_string_buffer(128)
+    _check(lib().rdet_nccl_unique_id(buf, 128))
+    return buf.raw
 
 
 def decode_batch(model: Model, seqs, tokens):

@@ -3,6 +3,7 @@
 // det_num v1 arithmetic exactly (see det_dev.cuh); integer MAC reductions are
 // split across lanes/warps/CTAs freely because wrapping i64 addition is
 // associative (reference docs/plans/DET_NUM_SPEC.md, "Parallelism legality").
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 #include <vector>
@@ -1286,7 +1287,7 @@ void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s) {
 //
 // Data path: model constants (norm gains, RoPE inverse frequencies) are
 // requested before the grid-dependency wait; right after it thread 0 starts
-// bulk copies (TMA, no multicast) of the CTA's K rows and then V rows -- one
+// bulk copies (TMA, into this CTA's own shared memory) of its K rows and then V rows -- one
 // contiguous span each -- into a ring of 32 KB shared-memory slots, each
 // with an mbarrier that counts the bytes.  Waits are bounded: a wait that
 // gives up sets the library's pipeline error flag (the host raises an error)
@@ -1370,9 +1371,9 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
   cg::cluster_group cl = cg::this_cluster();
   const int CL = (int)cl.num_blocks(), rank = (int)cl.block_rank();
   const int d = a.d, nch = d >> 2;
-  const int G = a.Hq / a.Hkv;
-  const int qh0 = blockIdx.y * GC;  // first query head of this cluster
-  const int kvh = qh0 / G;
+  const int G = a.group ? a.group : a.Hq / a.Hkv;
+  const int qh0 = blockIdx.y * GC;  // first (local) query head of this cluster
+  const int kvh = (a.head0 + qh0) / G;
   const AcLayout Ly = ac_layout(GC, d, rmax);
   unsigned char* ring = smem_raw + (size_t)Ly.ring * 4;
   int32_t* qs = sm + Ly.qs;        // [GC][d]
@@ -1502,7 +1503,7 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
         v[i + half] = add_sat(mul_sat(r, cs_tab[i]), mul_sat(l, sn_tab[i]));
       }
     }
-    if (new_row && rank == 0 && qh0 % G == 0) {
+    if (new_row && rank == 0 && (a.head0 + qh0) % G == 0) {
       __syncthreads();
       for (int i = tid; i < d; i += kAcThreads) {
         f.k_out[(head_base + pos) * d + i] = kvrow[i];
@@ -1832,10 +1833,16 @@ static int ac_group(int Hq, int Hkv, int d) {
   return gc;
 }
 
-bool attn_decode_cluster_fits(int Hq, int Hkv, int d, int window, int cap, int rotary) {
+bool attn_decode_cluster_fits(int Hq, int Hkv, int d, int window, int cap, int rotary, int group) {
   const int CL = g_attn_cluster ? g_attn_cluster : 8;
-  if (!(Hkv > 0 && Hq % Hkv == 0 && d > 0 && d % 4 == 0 && d <= 512 && (rotary >> 1) <= 256)) return false;
-  const int gc = ac_group(Hq, Hkv, d);
+  if (group == 0) {
+    if (!(Hkv > 0 && Hq % Hkv == 0)) return false;
+    group = Hq / Hkv;
+  }
+  if (!(d > 0 && d % 4 == 0 && d <= 512 && (rotary >> 1) <= 256)) return false;
+  const int gl = std::max(1, std::min(group, Hq));
+  if (Hq % gl != 0) return false;
+  const int gc = ac_group(Hq, Hq / gl, d);
   return gc <= 8 - 2 && d <= 128 * CL && ac_smem(gc, d, ac_rmax(window, cap, CL)) <= kAcMaxSmem;
 }
 
@@ -1857,14 +1864,19 @@ void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s) {
   const int rmax = ac_rmax(a.window, a.cap, CL);
   // (batched rows use the library's own 16-byte aligned cache allocations)
   const bool aligned = ((reinterpret_cast<uintptr_t>(a.k_cache) | reinterpret_cast<uintptr_t>(a.v_cache)) & 15) == 0;
-  if (!aligned || !attn_decode_cluster_fits(a.Hq, a.Hkv, a.d, a.window, a.cap, a.fuse.q_in ? a.fuse.rotary : 0)) {
+  if (!aligned ||
+      !attn_decode_cluster_fits(a.Hq, a.Hkv, a.d, a.window, a.cap, a.fuse.q_in ? a.fuse.rotary : 0, a.group)) {
     launch_attn_decode(a, s);  // callers only fuse when the cluster kernel fits
     return;
   }
-  int gc = ac_group(a.Hq, a.Hkv, a.d);
+  // a cluster's GC query heads share one KV head: GC divides the model's group
+  // size and the local head count
+  const int G = a.group ? a.group : a.Hq / a.Hkv;
+  const int Gl = std::min(G, a.Hq);
+  int gc = ac_group(a.Hq, a.Hq / Gl, a.d);
   if (a.batch > 1) {  // many clusters already: share K/V reads between query heads
-    const int G = a.Hq / a.Hkv, cap = a.d <= 256 ? 4 : 2;
-    while (gc * 2 <= cap && G % (gc * 2) == 0 && ac_smem(gc * 2, a.d, rmax) <= kAcMaxSmem) gc *= 2;
+    const int cap = a.d <= 256 ? 4 : 2;
+    while (gc * 2 <= cap && Gl % (gc * 2) == 0 && ac_smem(gc * 2, a.d, rmax) <= kAcMaxSmem) gc *= 2;
   }
   // launch errors surface through cudaGetLastError in the caller
   if (a.d <= 128) {
@@ -2264,6 +2276,30 @@ __global__ void scatter_rows_kernel(const int32_t* src, int32_t n, int32_t* cons
 void launch_scatter_rows(const int32_t* src, int32_t rows, int32_t n, int32_t* const* dst, size_t off,
                          cudaStream_t s) {
   launch_k(scatter_rows_kernel, dim3(rows), dim3(256), 0, s, src, n, dst, off);
+}
+
+__global__ void requantize_rows_kernel(const int64_t* x, size_t n, int32_t* y) {
+  pdl_entry();
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    y[i] = requantize(x[i]);
+}
+void launch_requantize_rows(const int64_t* x, size_t n, int32_t* y, cudaStream_t s) {
+  const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)sm_count() * 4);
+  launch_k(requantize_rows_kernel, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, s, x, n, y);
+}
+__global__ void gather_vocab_kernel(const int32_t* src, int32_t world, int32_t rows, int32_t vl, int32_t* const* dst) {
+  pdl_entry();
+  const int r = blockIdx.y;
+  int32_t* d = dst[r];
+  const size_t n = (size_t)world * vl;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t w = i / vl, j = i % vl;
+    d[i] = src[(w * rows + r) * vl + j];
+  }
+}
+void launch_gather_vocab(const int32_t* src, int32_t world, int32_t rows, int32_t vl, int32_t* const* dst,
+                         cudaStream_t s) {
+  launch_k(gather_vocab_kernel, dim3(64, rows), dim3(256), 0, s, src, world, rows, vl, dst);
 }
 
 __global__ void add_i32_kernel(int32_t* p, int32_t v) {

@@ -89,6 +89,11 @@ size_t tc_weight_bytes(int rows, int K, bool pair);
 // Builds the planes of g (and u, for the gate/up pair) into `mem`
 // (tc_weight_bytes); returns false if the tensor map cannot be encoded.
 bool tc_prepare_weight(TcWeight& t, const DevMat& g, const DevMat* u, void* mem, cudaStream_t s);
+// Same for the block rows [row0, row0 + rows) x columns [col0, col0 + cols) of
+// g (and u); row0/rows select gate/up rows of a pair.  col0 and cols are
+// multiples of 16.  Memory: tc_weight_bytes(rows, cols, pair).
+bool tc_prepare_weight_slice(TcWeight& t, const DevMat& g, const DevMat* u, int row0, int rows, int col0, int cols,
+                             void* mem, cudaStream_t s);
 size_t tc_act_bytes(int S, int K);
 // X [S, K] (16-byte aligned, K % 16 == 0) -> planes in `mem` (tc_act_bytes)
 bool tc_prepare_act(TcAct& a, const int32_t* X, int S, int K, void* mem, cudaStream_t s);
@@ -189,6 +194,10 @@ struct AttnDecodeArgs {
   // attends with position *pos_rows[b] over kc_rows[b] / vc_rows[b] (capacity
   // cap_rows[b]); q and out hold [batch, Hq, d]; cap is the largest capacity
   int32_t batch = 1;
+  // tensor-parallel shard: q / out hold Hq local heads, global index head0 + h;
+  // group = query heads per KV head of the model (0: Hq / Hkv), caches keep
+  // all Hkv KV heads
+  int32_t head0 = 0, group = 0;
   const int32_t* const* pos_rows = nullptr;
   const int32_t* const* kc_rows = nullptr;
   const int32_t* const* vc_rows = nullptr;
@@ -203,7 +212,7 @@ void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s);
 // (rotary: the fused prologue's rotary width, 0 when not fused).  When it
 // does not, it falls back to launch_attn_decode, which needs a.sc and does
 // not fuse the prologue.
-bool attn_decode_cluster_fits(int Hq, int Hkv, int d, int window, int cap, int rotary);
+bool attn_decode_cluster_fits(int Hq, int Hkv, int d, int window, int cap, int rotary, int group = 0);
 
 struct AttnPrefillArgs {
   int32_t S = 0;
@@ -244,6 +253,10 @@ void launch_softcap(int32_t* x, int32_t n, int32_t cap, cudaStream_t s);
 // ---- misc ---------------------------------------------------------------------------
 void launch_add_i32(int32_t* p, int32_t v, cudaStream_t s);  // *p += v
 void launch_add_i32_rows(int32_t* const* p, int32_t n, int32_t v, cudaStream_t s);  // *p[i] += v
+void launch_requantize_rows(const int64_t* x, size_t n, int32_t* y, cudaStream_t s);  // y = requantize(x)
+// vocab-sharded logits: src [world][rows][vl] -> dst[r][w * vl + j]
+void launch_gather_vocab(const int32_t* src, int32_t world, int32_t rows, int32_t vl, int32_t* const* dst,
+                         cudaStream_t s);
 // dst[r] + off <- src row r (n ints), for r < rows
 void launch_scatter_rows(const int32_t* src, int32_t rows, int32_t n, int32_t* const* dst, size_t off,
                          cudaStream_t s);

@@ -1,6 +1,7 @@
 // rdet runtime: model loading into HBM, per-sequence KV caches, and the
 // prefill / decode / select routines of the reference det path, composed
 // from the sm_100a kernels in kernels.cu.  Implements include/rdet.h.
+#include <dlfcn.h>
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
@@ -16,6 +17,8 @@
 #include <stdexcept>
 #include <string>
 #include <vector>
+
+#include <nccl.h>  // types only: libnccl is loaded at run time
 
 #include "det_dev.cuh"
 #include "json.h"
@@ -404,6 +407,59 @@ struct DecodeWs {
           *g = nullptr, *pr = nullptr, *argpart = nullptr;
 };
 
+// ---------------------------------------------------------------------------
+// NCCL, loaded when tensor-parallel decode is first set up (the library has no
+// link-time dependency on it; a process that already loaded libnccl.so.2, as
+// torch does, shares that copy)
+// ---------------------------------------------------------------------------
+struct NcclApi {
+  bool ok = false;
+  decltype(&ncclGetUniqueId) getUniqueId = nullptr;
+  decltype(&ncclCommInitRank) commInitRank = nullptr;
+  decltype(&ncclAllReduce) allReduce = nullptr;
+  decltype(&ncclAllGather) allGather = nullptr;
+  decltype(&ncclCommDestroy) commDestroy = nullptr;
+  decltype(&ncclGetErrorString) errorString = nullptr;
+};
+static NcclApi& nccl_api() {
+  static NcclApi n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    n.getUniqueId = reinterpret_cast<decltype(&ncclGetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+    n.commInitRank = reinterpret_cast<decltype(&ncclCommInitRank)>(dlsym(h, "ncclCommInitRank"));
+    n.allReduce = reinterpret_cast<decltype(&ncclAllReduce)>(dlsym(h, "ncclAllReduce"));
+    n.allGather = reinterpret_cast<decltype(&ncclAllGather)>(dlsym(h, "ncclAllGather"));
+    n.commDestroy = reinterpret_cast<decltype(&ncclCommDestroy)>(dlsym(h, "ncclCommDestroy"));
+    n.errorString = reinterpret_cast<decltype(&ncclGetErrorString)>(dlsym(h, "ncclGetErrorString"));
+    n.ok = n.getUniqueId && n.commInitRank && n.allReduce && n.allGather && n.commDestroy && n.errorString;
+  });
+  return n;
+}
+#define NCK(x)                                                                                    \
+  do {                                                                                            \
+    ncclResult_t r_ = (x);                                                                        \
+    if (r_ != ncclSuccess) throw Fail{RDET_E_CUDA, std::string(#x) + ": " + nccl_api().errorString(r_)}; \
+  } while (0)
+
+// Tensor-parallel shard of the batched decode (every rank holds the whole
+// model; these are the byte planes of this rank's slices)
+struct TpLayer {
+  TcWeight q, o, gu, down, pg, pp;
+};
+struct TpState {
+  int rank = 0, world = 1;
+  ncclComm_t comm = nullptr;
+  int Hql = 0, head0 = 0, Fl = 0, Pl = 0, Vl = 0;
+  std::vector<TpLayer> layers;
+  TcWeight lm;
+  int rows = 0;                // rows of the buffers below
+  int64_t* part = nullptr;     // [rows, H] partial sums before requantize
+  int32_t* lgl = nullptr;      // [rows, Vl] this rank's logits
+  int32_t* lga = nullptr;      // [world, rows, Vl] gathered logits
+};
+
 struct Seq;
 
 struct Ctx {
@@ -445,6 +501,7 @@ struct Ctx {
     int32_t** logits_dst = nullptr;
     int32_t* logits = nullptr;     // [rows, V]
   } bw;
+  TpState tp;
 
   void* dalloc(size_t bytes) {
     void* p = nullptr;
@@ -458,6 +515,7 @@ struct Ctx {
   ~Ctx() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
+    if (tp.comm) nccl_api().commDestroy(tp.comm);
     for (void* p : allocs) cudaFree(p);
     if (stream) cudaStreamDestroy(stream);
   }
@@ -1348,6 +1406,196 @@ static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32
   return result;
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-parallel batched decode.  Rank r of `world` computes query heads
+// [head0, head0 + Hql) (q projection rows, attention), the gate/up rows
+// [r*Fl, (r+1)*Fl), per-layer-input gate rows [r*Pl, (r+1)*Pl) and vocab
+// rows [r*Vl, (r+1)*Vl).  The o, down and per-layer-input projections take
+// the matching column slices and produce exact i64 partial sums that one
+// NCCL all-reduce (int64 sum: wrapping addition is order-free) completes
+// before requantize; logits are all-gathered.  K/V projections and appends
+// run in full on every rank, so every rank's caches stay complete and every
+// other path of the context stays valid.
+// ---------------------------------------------------------------------------
+static void tp_linear(Ctx& c, const int32_t* X, int S, int K, const TcWeight& w, const TcOut& o) {
+  TcAct a;
+  REQUIRE(tc_prepare_act(a, X, S, K, c.tc_act, c.stream), RDET_E_CUDA, "tensor map encoding failed");
+  TcOut oo = o;
+  oo.scratch = c.tc_split;
+  oo.scratch_bytes = c.tc_split_bytes;
+  REQUIRE(launch_tc_linear(a, w, oo, c.stream), RDET_E_RANGE, "batch too large for the split-K scratch");
+}
+
+// partial sums [S, H] of a column slice -> all-reduce -> requantize into y
+static void tp_linear_reduce(Ctx& c, const int32_t* X, int S, int K, const TcWeight& w, int32_t* y) {
+  TcOut o;
+  o.y64 = c.tp.part;
+  tp_linear(c, X, S, K, w, o);
+  const size_t n = (size_t)S * w.N;
+  NCK(nccl_api().allReduce(c.tp.part, c.tp.part, n, ncclInt64, ncclSum, c.tp.comm, c.stream));
+  launch_requantize_rows(c.tp.part, n, y, c.stream);
+}
+
+static const int32_t* decode_batch_layer_tp(Ctx& c, int B, int maxcap, int l, int32_t* cur) {
+  const ModelCfg& m = c.cfg;
+  const LayerDev& L = c.layers[l];
+  const LayerCfg& lc = L.cfg;
+  const TpLayer& T = c.tp.layers[l];
+  PrefillWs& w = c.pw;
+  auto& bw = c.bw;
+  cudaStream_t s = c.stream;
+  const int H = m.H, d = lc.head_dim, Hql = c.tp.Hql;
+  int32_t* other = cur == w.xa ? w.xb : w.xa;
+  launch_rmsnorm_rows(cur, B, H, L.in_ln, c.eps, w.nrm, s);
+  TcOut oq;
+  oq.y = w.q;
+  tp_linear(c, w.nrm, B, H, T.q, oq);
+  QkvPostArgs qa;
+  qa.S = B; qa.Hq = Hql; qa.Hkv = lc.kv_heads; qa.d = d; qa.rotary = lc.rotary; qa.inv_freq = L.inv_freq;
+  qa.q_in = w.q; qa.q_norm = L.q_norm; qa.k_norm = L.k_norm; qa.eps = c.eps; qa.q_out = w.qo;
+  qa.pos_rows = bw.pos; qa.cap_rows = bw.caps;
+  if (lc.donor < 0) {
+    ActPlanes nrm_planes;
+    prefill_linear(c, w.nrm, B, L.k, L.tk, w.kraw, kEpiPlain, nullptr, &nrm_planes);
+    const int32_t* vsrc = w.kraw;  // k_eq_v: V is the raw K projection
+    if (L.v.p) { prefill_linear(c, w.nrm, B, L.v, L.tv, w.vraw, kEpiPlain, nullptr, &nrm_planes); vsrc = w.vraw; }
+    qa.k_in = w.kraw; qa.v_in = vsrc;
+    qa.kc_rows = bw.kc + (size_t)l * bw.rows;
+    qa.vc_rows = bw.vc + (size_t)l * bw.rows;
+  }
+  launch_qkv_post(qa, s);
+  AttnDecodeArgs aa;
+  aa.Hq = Hql; aa.Hkv = lc.kv_heads; aa.group = m.Hq / lc.kv_heads; aa.head0 = c.tp.head0;
+  aa.d = d; aa.window = lc.window; aa.q = w.qo; aa.out = w.comb;
+  aa.cap = maxcap; aa.batch = B; aa.pos_rows = bw.pos; aa.cap_rows = bw.caps;
+  aa.kc_rows = bw.kc + (size_t)l * bw.rows;
+  aa.vc_rows = bw.vc + (size_t)l * bw.rows;
+  launch_attn_decode_cluster(aa, s);
+  tp_linear_reduce(c, w.comb, B, Hql * d, T.o, w.attn);
+  const bool ple = m.P > 0;
+  launch_norm_residual_rows(w.attn, cur, B, H, L.post_attn_ln, c.eps, false, 0, other, s);
+  launch_rmsnorm_rows(other, B, H, L.pre_ff_ln, c.eps, w.nrm, s);
+  TcOut og;
+  og.y = w.hbuf;
+  tp_linear(c, w.nrm, B, H, T.gu, og);
+  tp_linear_reduce(c, w.hbuf, B, c.tp.Fl, T.down, w.attn);
+  launch_norm_residual_rows(w.attn, other, B, H, L.post_ff_ln, c.eps, !ple && L.has_scalar, L.scalar, cur, s);
+  int32_t* result = cur;
+  if (ple) {
+    TcOut op;
+    op.y = w.g;
+    op.epi = kEpiGeluMul;
+    op.vec = w.ple_all + (size_t)l * B * m.P + (size_t)c.tp.rank * c.tp.Pl;
+    op.ldv = m.P;
+    tp_linear(c, cur, B, H, T.pg, op);
+    tp_linear_reduce(c, w.g, B, c.tp.Pl, T.pp, w.pr);
+    launch_norm_residual_rows(w.pr, cur, B, H, L.ple_norm, c.eps, L.has_scalar, L.scalar, other, s);
+    result = other;
+  }
+  launch_scatter_rows(result, B, H, bw.dec_out, (size_t)l * H, s);
+  return result;
+}
+
+static void tp_buffers(Ctx& c, int B) {
+  TpState& t = c.tp;
+  if (t.rows >= B) return;
+  const int rows = std::max(B, 8);
+  t.part = c.dalloc_n<int64_t>((size_t)rows * c.cfg.H);
+  t.lgl = c.dalloc_n<int32_t>((size_t)rows * t.Vl);
+  t.lga = c.dalloc_n<int32_t>((size_t)t.world * rows * t.Vl);
+  t.rows = rows;
+}
+
+static void tp_init(Ctx& c, int rank, int world, const ncclUniqueId& id) {
+  const ModelCfg& m = c.cfg;
+  TpState& t = c.tp;
+  REQUIRE(t.comm == nullptr, RDET_E_STATE, "tensor-parallel decode is already set up on this context");
+  REQUIRE(world >= 1 && rank >= 0 && rank < world, RDET_E_INVALID, "invalid tensor-parallel rank or world size");
+  REQUIRE(c.tc, RDET_E_STATE, "tensor-parallel decode runs on the tensor-core linear (sm_100, i16 weights)");
+  REQUIRE(nccl_api().ok, RDET_E_STATE, "libnccl.so.2 could not be loaded");
+  REQUIRE(m.Hq % world == 0, RDET_E_INVALID, "num_attention_heads must be a multiple of the world size");
+  const int Hql = m.Hq / world;
+  for (const LayerDev& L : c.layers) {
+    const int G = m.Hq / L.cfg.kv_heads;
+    REQUIRE(Hql % G == 0 || G % Hql == 0, RDET_E_INVALID, "each rank's query heads must cover whole KV groups");
+    REQUIRE((Hql * L.cfg.head_dim) % 16 == 0, RDET_E_INVALID, "head slice width must be a multiple of 16");
+    REQUIRE(L.F % world == 0 && (L.F / world) % 16 == 0, RDET_E_INVALID,
+            "intermediate_size / world must be a multiple of 16");
+    REQUIRE(L.tq.planes && L.to.planes && L.tgu.planes && L.tdown.planes, RDET_E_STATE,
+            "tensor-parallel decode needs i16 projection weights");
+  }
+  if (m.P > 0)
+    REQUIRE(m.P % world == 0 && (m.P / world) % 16 == 0, RDET_E_INVALID,
+            "hidden_size_per_layer_input / world must be a multiple of 16");
+  REQUIRE(m.V % world == 0 && c.t_lm_head.planes, RDET_E_INVALID, "vocab_size must be a multiple of the world size");
+  t.rank = rank;
+  t.world = world;
+  t.Hql = Hql;
+  t.head0 = rank * Hql;
+  t.Fl = c.F / world;
+  t.Pl = m.P > 0 ? m.P / world : 0;
+  t.Vl = m.V / world;
+  t.layers.assign(m.L, TpLayer());
+  auto slice = [&](TcWeight& tw, const DevMat& g, const DevMat* u, int row0, int rows, int col0, int cols) {
+    void* mem = c.dalloc(tc_weight_bytes(rows, cols, u != nullptr));
+    REQUIRE(tc_prepare_weight_slice(tw, g, u, row0, rows, col0, cols, mem, c.stream), RDET_E_CUDA,
+            "tensor map encoding failed");
+  };
+  for (int l = 0; l < m.L; ++l) {
+    const LayerDev& L = c.layers[l];
+    TpLayer& T = t.layers[l];
+    const int d = L.cfg.head_dim, Fl = L.F / world;
+    slice(T.q, L.q, nullptr, t.head0 * d, Hql * d, 0, m.H);
+    slice(T.o, L.o, nullptr, 0, m.H, t.head0 * d, Hql * d);
+    slice(T.gu, L.gate, &L.up, rank * Fl, Fl, 0, m.H);
+    slice(T.down, L.down, nullptr, 0, m.H, rank * Fl, Fl);
+    if (m.P > 0) {
+      slice(T.pg, L.ple_gate, nullptr, rank * t.Pl, t.Pl, 0, m.H);
+      slice(T.pp, L.ple_proj, nullptr, 0, m.H, rank * t.Pl, t.Pl);
+    }
+  }
+  slice(t.lm, c.lm_head, nullptr, rank * t.Vl, t.Vl, 0, m.H);
+  CK(cudaStreamSynchronize(c.stream));
+  CK(cudaGetLastError());
+  NCK(nccl_api().commInitRank(&t.comm, world, id, rank));
+}
+
+static void decode_batch_tp(Ctx& c, Seq* const* seqs, const uint32_t* tokens, int B) {
+  const ModelCfg& m = c.cfg;
+  PrefillWs& w = c.pw;
+  cudaStream_t s = c.stream;
+  batch_tables(c, seqs, B);
+  tp_buffers(c, B);
+  auto& bw = c.bw;
+  int maxcap = 0;
+  for (int i = 0; i < B; ++i) maxcap = std::max(maxcap, seqs[i]->cap);
+  CK(cudaMemcpyAsync(bw.ids, tokens, (size_t)B * 4, cudaMemcpyHostToDevice, s));
+  launch_embed(bw.ids, B, c.emb, c.emb_scale, w.xa, c.d_err, s);
+  if (m.P > 0) {
+    prefill_linear(c, w.xa, B, c.ple_model_proj, c.t_ple_model, w.ple_proj, kEpiPlain, nullptr);
+    PleArgs pa;
+    pa.S = B; pa.L = m.L; pa.P = m.P; pa.ids = bw.ids; pa.proj = w.ple_proj; pa.table = c.ple_table;
+    pa.norm = c.ple_proj_norm; pa.eps = c.eps; pa.emb_scale = c.ple_emb_scale; pa.proj_scale = c.ple_proj_scale;
+    pa.in_scale = c.ple_in_scale; pa.out = w.ple_all; pa.err = c.d_err;
+    launch_ple(pa, s);
+  }
+  int32_t* cur = w.xa;
+  for (int l = 0; l < m.L; ++l) cur = const_cast<int32_t*>(decode_batch_layer_tp(c, B, maxcap, l, cur));
+  launch_rmsnorm_rows(cur, B, m.H, c.final_norm, c.eps, w.nrm, s);
+  TcOut ol;
+  ol.y = c.tp.lgl;
+  tp_linear(c, w.nrm, B, m.H, c.tp.lm, ol);
+  if (m.has_softcap) launch_softcap(c.tp.lgl, B * c.tp.Vl, c.softcap, s);
+  NCK(nccl_api().allGather(c.tp.lgl, c.tp.lga, (size_t)B * c.tp.Vl, ncclInt32, c.tp.comm, s));
+  launch_gather_vocab(c.tp.lga, c.tp.world, B, c.tp.Vl, bw.logits_dst, s);
+  launch_add_i32_rows(bw.pos, B, 1, s);
+  CK(cudaGetLastError());
+  for (int i = 0; i < B; ++i) {
+    seqs[i]->pos += 1;
+    seqs[i]->last_was_prefill = false;
+  }
+}
+
 // Whether the batched path can run these sequences (distinct, and the
 // batched cluster attention fits every layer's window).
 static bool batch_supported(Ctx& c, Seq* const* seqs, int B) {
@@ -1357,8 +1605,11 @@ static bool batch_supported(Ctx& c, Seq* const* seqs, int B) {
       if (seqs[i] == seqs[j]) return false;
   int maxcap = 0;
   for (int i = 0; i < B; ++i) maxcap = std::max(maxcap, seqs[i]->cap);
-  for (const LayerDev& L : c.layers)
-    if (!attn_decode_cluster_fits(c.cfg.Hq, L.cfg.kv_heads, L.cfg.head_dim, L.cfg.window, maxcap, 0)) return false;
+  const bool tp = c.tp.comm != nullptr;
+  for (const LayerDev& L : c.layers) {
+    const int hq = tp ? c.tp.Hql : c.cfg.Hq, group = tp ? c.cfg.Hq / L.cfg.kv_heads : 0;
+    if (!attn_decode_cluster_fits(hq, L.cfg.kv_heads, L.cfg.head_dim, L.cfg.window, maxcap, 0, group)) return false;
+  }
   return true;
 }
 
@@ -1829,7 +2080,8 @@ int32_t rdet_decode(rdet_ctx* ctx, rdet_seq* const* seqs, const uint32_t* tokens
       for (size_t i0 = 0; i0 < nseq; i0 += c.max_prefill) {
         const int B = (int)std::min<size_t>(c.max_prefill, nseq - i0);
         if (B >= 2) {
-          decode_batch(c, batch.data() + i0, tokens + i0, B);
+          if (c.tp.comm) decode_batch_tp(c, batch.data() + i0, tokens + i0, B);
+          else decode_batch(c, batch.data() + i0, tokens + i0, B);
           continue;
         }
         Seq& q = *batch[i0];
@@ -2002,6 +2254,32 @@ int32_t rdet_commitment(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t lay
   });
   if (rc == RDET_OK && none) { hex_out[0] = 0; return RDET_NONE; }
   return rc;
+}
+
+int32_t rdet_nccl_unique_id(void* id_out, size_t len) {
+  return guard([&] {
+    REQUIRE(id_out && len >= sizeof(ncclUniqueId), RDET_E_INVALID, "the id buffer needs 128 bytes");
+    REQUIRE(nccl_api().ok, RDET_E_STATE, "libnccl.so.2 could not be loaded");
+    ncclUniqueId id;
+    NCK(nccl_api().getUniqueId(&id));
+    memcpy(id_out, &id, sizeof(id));
+  });
+}
+
+int32_t rdet_tp_init(rdet_ctx* ctx, int32_t rank, int32_t world, const void* id, size_t len) {
+  return guard([&] {
+    REQUIRE(ctx && id && len >= sizeof(ncclUniqueId), RDET_E_INVALID, "null argument or short id");
+    Ctx& c = *ctx->c;
+    CK(cudaSetDevice(c.device));
+    ncclUniqueId uid;
+    memcpy(&uid, id, sizeof(uid));
+    tp_init(c, rank, world, uid);
+  });
+}
+
+int32_t rdet_tp_world(rdet_ctx* ctx) {
+  if (!ctx || !ctx->c) return 0;
+  return ctx->c->tp.comm ? ctx->c->tp.world : 1;
 }
 
 int32_t rdet_tensor_core_prefill(rdet_ctx* ctx) {

@@ -23,7 +23,7 @@
 //
 // Pipeline per CTA (one 128 x 96 output tile): warp 4 streams activation limb
 // tiles (4 x 128 x 64 B) and the stacked weight tile (192 x 64 B) with TMA
-// (tiled, 64-byte swizzle, no multicast) into a 4-stage ring; warp 5 issues
+// (tiled, 64-byte swizzle, each CTA loading its own tiles) into a 4-stage ring; warp 5 issues
 // the MMAs (M=128, N=192, K=32, kind::i8, u8 x u8 -> s32) and frees stages
 // with tcgen05.commit; warps 0-3 zero the accumulator before the first MMA
 // and drain it through tcgen05.ld afterwards.  Every mbarrier wait is bounded
@@ -160,16 +160,19 @@ __global__ void tc_act_prep_kernel(const int32_t* __restrict__ X, int S, int K, 
 // Weight rows (i16) -> low/high byte planes of W + 2^15 and their row sums.
 // Plane row R maps to source row R, or for a gate/up pair to gate row
 // 48*(R/96) + R%96 (R%96 < 48) or up row 48*(R/96) + R%96 - 48.
+// A slice takes source rows [row0, row0 + rows) and columns [col0, col0 + K)
+// of a matrix with row stride ld.
 __global__ void tc_weight_prep_kernel(const int16_t* __restrict__ W, const int16_t* __restrict__ U, int rows,
-                                      int K, int nrows, uint8_t* __restrict__ planes, uint64_t* __restrict__ rowsum) {
+                                      int K, int nrows, uint8_t* __restrict__ planes, uint64_t* __restrict__ rowsum,
+                                      int row0, int col0, int ld) {
   const int R = blockIdx.x;
   const int16_t* src = nullptr;
   if (U == nullptr) {
-    if (R < rows) src = W + (size_t)R * K;
+    if (R < rows) src = W + (size_t)(row0 + R) * ld + col0;
   } else {
     const int b = R / kTcN, j = R % kTcN, h = kTcN / 2;
     const int r = b * h + (j < h ? j : j - h);
-    if (r < rows) src = (j < h ? W : U) + (size_t)r * K;
+    if (r < rows) src = (j < h ? W : U) + (size_t)(row0 + r) * ld + col0;
   }
   const size_t plane = (size_t)nrows * K;
   uint64_t sum = 0;
@@ -558,16 +561,21 @@ size_t tc_weight_bytes(int rows, int K, bool pair) {
 }
 
 bool tc_prepare_weight(TcWeight& t, const DevMat& g, const DevMat* u, void* mem, cudaStream_t s) {
+  return tc_prepare_weight_slice(t, g, u, 0, g.rows, 0, g.cols, mem, s);
+}
+
+bool tc_prepare_weight_slice(TcWeight& t, const DevMat& g, const DevMat* u, int row0, int rows, int col0, int cols,
+                             void* mem, cudaStream_t s) {
   const bool pair = u != nullptr;
-  t.N = g.rows;
-  t.K = g.cols;
+  t.N = rows;
+  t.K = cols;
   t.pair = pair;
-  t.nrows = tc_plane_rows(g.rows, pair);
+  t.nrows = tc_plane_rows(rows, pair);
   t.planes = static_cast<uint8_t*>(mem);
   t.rowsum = reinterpret_cast<uint64_t*>(t.planes + 2 * (size_t)t.nrows * t.K);
   tc_weight_prep_kernel<<<t.nrows, 128, 0, s>>>(static_cast<const int16_t*>(g.p),
-                                                pair ? static_cast<const int16_t*>(u->p) : nullptr, g.rows, g.cols,
-                                                t.nrows, t.planes, t.rowsum);
+                                                pair ? static_cast<const int16_t*>(u->p) : nullptr, rows, cols,
+                                                t.nrows, t.planes, t.rowsum, row0, col0, g.cols);
   return encode_planes(t.map, t.planes, 2, t.nrows, t.K, kTcN);
 }
 
