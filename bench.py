@@ -342,7 +342,14 @@ def run_ours(args, rank, world, local_rank):
     batched = None
     if args.batch > 0:
         bm, bstream = model, stream  # max_prefill (the context) >= the batch rows
-        lens = [128 + (x % 3969) for x in lcg_ids(args.batch, 1 << 30, SEED + 7 + rank)]
+        # N > 1: the batch is sharded across the ranks (tensor-parallel, same
+        # sequences on every rank): strong scaling of this line
+        tp = world > 1
+        if tp:
+            uid = [rdet.nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(uid, src=0)
+            bm.tp_init(rank, world, uid[0])
+        lens = [128 + (x % 3969) for x in lcg_ids(args.batch, 1 << 30, SEED + 7)]
         seqs = [bm.new_sequence(n + args.batch_steps + 8) for n in lens]
         for i, (sq, n) in enumerate(zip(seqs, lens)):
             sq.prefill(lcg_ids(n, t["vocab_size"], SEED + 100 + i))
@@ -365,7 +372,8 @@ def run_ours(args, rank, world, local_rank):
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             bsec = float(tt[0])
         batched = {"sequences": args.batch, "context": f"128 + draw mod 3969 (seeded), mean {sum(lens) // len(lens)}",
-                   "steps": args.batch_steps, "tok_s": world * args.batch * args.batch_steps / bsec,
+                   "parallelism": f"tp{world}" if tp else "single", "scaling": "strong" if tp else None,
+                   "steps": args.batch_steps, "tok_s": args.batch * args.batch_steps / bsec,
                    "ms_per_step": 1000 * bsec / args.batch_steps,
                    "note": "device-timed batched decode_transition (same token fed back: decode cost does not depend "
                            "on token values)"}
