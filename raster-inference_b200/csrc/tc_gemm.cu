@@ -21,13 +21,15 @@
 // epilogue recombines the five blocks and the two row-sum corrections in
 // wrapping i64 and requantizes: bit-exact with the CUDA-core linear.
 //
-// Pipeline per CTA (one 128 x 96 output tile): warp 4 streams activation limb
-// tiles (4 x 128 x 64 B) and the stacked weight tile (192 x 64 B) with TMA
-// (tiled, 64-byte swizzle, each CTA loading its own tiles) into a 4-stage ring; warp 5 issues
-// the MMAs (M=128, N=192, K=32, kind::i8, u8 x u8 -> s32) and frees stages
-// with tcgen05.commit; warps 0-3 zero the accumulator before the first MMA
-// and drain it through tcgen05.ld afterwards.  Every mbarrier wait is bounded
-// and reports a timeout through the library's pipeline error flag.
+// Pipeline (persistent CTAs, output tiles of 128 tokens x 96 weight rows):
+// warp 8 streams activation limb tiles (4 x 128 x 64 B) and the stacked
+// weight tile (192 x 64 B) with TMA (tiled, 64-byte swizzle, each CTA loading
+// its own tiles) into a 4-stage ring that runs across tile boundaries; warp 9
+// issues the MMAs (M=128, N=192, K=32, kind::i8, u8 x u8 -> s32) and frees
+// stages with tcgen05.commit; warps 0-7 drain the accumulator through
+// tcgen05.ld into a shared-memory tile, release TMEM, then finish the
+// epilogue and store while the next tile's MMAs run.  Every mbarrier wait is
+// bounded and reports a timeout through the library's pipeline error flag.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -367,42 +369,50 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         continue;
       }
       if constexpr (EPI != 3) {
-      for (int c0 = half * kHalf; c0 < (half + 1) * kHalf; c0 += 8) {
-        uint32_t g[5][8], h[5][8];
+      // phase 1, TMEM held: recombine, correct and requantize 16 plane rows
+      // per TMEM wait into this thread's staging row (a gate/up pair stages
+      // gate at column j and up at column kTcN / 2 + j)
+      constexpr int kStep = EPI == 2 ? 8 : 16;
+      for (int c0 = half * kHalf; c0 < (half + 1) * kHalf; c0 += kStep) {
+        uint32_t g[5][2][8];
 #pragma unroll
-        for (int gg = 0; gg < 5; ++gg) tmem_ld8(tbase + kTcN * gg + c0, g[gg]);
-        if (EPI == 2) {
-#pragma unroll
-          for (int gg = 0; gg < 5; ++gg) tmem_ld8(tbase + kTcN * gg + kTcN / 2 + c0, h[gg]);
+        for (int gg = 0; gg < 5; ++gg) {
+          tmem_ld8(tbase + kTcN * gg + c0, g[gg][0]);
+          tmem_ld8(tbase + kTcN * gg + (EPI == 2 ? kTcN / 2 : 8) + c0, g[gg][1]);
         }
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int j = c0 + i;
-          // plane rows of a pair cover whole tiles; a plain matrix has N rows
-          const int n = nbase + j;
+        for (int i = 0; i < 16; ++i) {
+          const int pr = c0 + (EPI == 2 ? (i >> 3) * (kTcN / 2) + (i & 7) : i);  // plane row in the tile
+          const int n = nbase + c0 + (EPI == 2 ? (i & 7) : i);
           int32_t y = 0;
+          // plane rows of a pair cover whole tiles; a plain matrix has N rows
           if (mrow && n < N) {
-            uint64_t acc = (uint64_t)g[0][i] + ((uint64_t)g[1][i] << 8) + ((uint64_t)g[2][i] << 16) +
-                           ((uint64_t)g[3][i] << 24) + ((uint64_t)g[4][i] << 32);
-            acc -= corr + (brow[r0 + j] << 31);
+            uint64_t acc = (uint64_t)g[0][i >> 3][i & 7] + ((uint64_t)g[1][i >> 3][i & 7] << 8) +
+                           ((uint64_t)g[2][i >> 3][i & 7] << 16) + ((uint64_t)g[3][i >> 3][i & 7] << 24) +
+                           ((uint64_t)g[4][i >> 3][i & 7] << 32);
+            acc -= corr + (brow[r0 + pr] << 31);
             y = requantize((int64_t)acc);
-            if (EPI == 2) {
-              uint64_t accu = (uint64_t)h[0][i] + ((uint64_t)h[1][i] << 8) + ((uint64_t)h[2][i] << 16) +
-                              ((uint64_t)h[3][i] << 24) + ((uint64_t)h[4][i] << 32);
-              accu -= corr + (brow[r0 + kTcN / 2 + j] << 31);
-              y = mul_sat(gelu_act(y), requantize((int64_t)accu));
-            } else if (EPI == 1) {
-              y = mul_sat(gelu_act(y), vec[(size_t)m * ldv + n]);
-            }
           }
-          stage_out[rl * kTcOutStride + j] = y;
+          stage_out[rl * kTcOutStride + pr] = y;
         }
       }
-      // the accumulator is in registers/shared memory: TMEM is free for the next tile
+      // the accumulator is in shared memory: TMEM is free for the next tile
       tc_fence_before();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&tmem_empty)) : "memory");
+      // phase 2, overlapping the next tile's MMAs: the GELU epilogues on this
+      // thread's own staged values
+      if constexpr (EPI == 1 || EPI == 2) {
+        if (mrow) {
+          for (int j = half * kHalf; j < (half + 1) * kHalf; ++j) {
+            const int n = nbase + j;
+            if (n >= N) break;
+            int32_t* sp_ = &stage_out[rl * kTcOutStride + j];
+            *sp_ = mul_sat(gelu_act(*sp_), EPI == 2 ? sp_[kTcN / 2] : vec[(size_t)m * ldv + n]);
+          }
+        }
+      }
       asm volatile("bar.sync 1, %0;" ::"n"(32 * kTcEpiWarps) : "memory");  // staging complete
       for (int r = warp; r < kTcM; r += kTcEpiWarps) {
         const int mm = m0 + r;
