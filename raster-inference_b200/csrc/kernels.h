@@ -71,14 +71,16 @@ void launch_linear_geglu(const int32_t* X, int32_t S, const DevMat& wg, const De
 // K a multiple of 16 and K <= kTcMaxK.
 constexpr int kTcMaxK = 32768;
 struct TcWeight {           // byte planes of one weight matrix (or a gate/up pair)
-  alignas(64) unsigned char map[128];  // TMA tensor map of the planes
+  alignas(64) unsigned char map[128];  // TMA tensor map of the planes (96-row boxes)
+  alignas(64) unsigned char map_m[128];  // the same planes in 128-row boxes (short-row-count kernel)
   uint8_t* planes = nullptr;           // [2][nrows][K]
   uint64_t* rowsum = nullptr;          // [nrows] sum over k of W + 2^15
   int32_t N = 0, K = 0, nrows = 0;
   bool pair = false;                   // rows interleave gate and up in blocks of 48
 };
 struct TcAct {              // byte planes of one activation matrix
-  alignas(64) unsigned char map[128];
+  alignas(64) unsigned char map[128];    // 128-row boxes
+  alignas(64) unsigned char map_t[128];  // 64-row boxes (S <= 64: short-row-count kernel)
   uint8_t* planes = nullptr;           // [4][S][K]
   uint64_t* rowsum = nullptr;          // [S] sum over k of X + 2^31
   int32_t S = 0, K = 0;

@@ -97,7 +97,7 @@ __device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr) {
   return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)(512 >> 4) << 32) | (1ull << 46) | (4ull << 61);
 }
 // kind::i8 instruction descriptor: s32 accumulator, u8 A and B, both
-// K-major, N = 192, M = 128.
+// K-major, M = 128, N = n.
 constexpr uint32_t tc_idesc(int n) {
   return (2u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
 }
@@ -435,6 +435,172 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Short row counts (a batched decode step: S <= 64 tokens).  The operands
+// swap roles: the A operand is one byte plane of 128 weight rows (M = 128)
+// and the B operand stacks the four activation limbs of 64 tokens (N = 256,
+// B row a*64 + t).  MMA p (weight plane p) writes [P_0p | P_1p | P_2p | P_3p]
+// into TMEM columns [64p, 64p + 256), so column block g = [64g, 64g + 64)
+// accumulates exactly the products with shift 8g (P_g0 + P_(g-1)1): 320
+// columns, each block at most two products <= 255*255*K (exact as u32 for
+// K < 33025).  No MMA work is spent on padding token rows, and each stage
+// moves 16 KB of weights for 128 rows instead of 12 KB for 96 rows next to
+// 32 KB of mostly-padding activation limbs.
+// The first K step of a tile writes every column once with accumulate off:
+// plane 0 fresh over [0, 256), plane 1's limbs 0-2 onto [64, 256), plane 1's
+// limb 3 fresh over [256, 320).
+// EPI 0 (one K range): corrections and requantize, Y[s][n] for n < N.
+// EPI 3: the raw sum of K range sp, part[sp][s][plane row], finished by
+// tc_splitk_reduce_kernel (any epilogue, the gate/up pair included).
+// ---------------------------------------------------------------------------
+constexpr int kTsM = 128;                              // weight plane rows per tile
+constexpr int kTsT = 64;                               // tokens per tile
+constexpr int kTsATile = kTsM * kTcKB;                 // 8 KB per weight plane
+constexpr int kTsBTile = kTsT * kTcKB;                 // 4 KB per activation limb
+constexpr int kTsStage = 2 * kTsATile + 4 * kTsBTile;  // 32 KB
+constexpr int kTsStages = 6;
+constexpr int kTsSmem = kTsStages * kTsStage + 1024;  // + alignment slack
+constexpr uint32_t kTsIdesc = tc_idesc(4 * kTsT);      // N = 256
+constexpr uint32_t kTsIdesc3 = tc_idesc(3 * kTsT);     // limbs 0-2
+constexpr uint32_t kTsIdesc1 = tc_idesc(kTsT);         // limb 3
+
+template <int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_linear_t_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
+                       const uint64_t* __restrict__ arow, const uint64_t* __restrict__ brow, int S, int N, int K,
+                       int tiles_n, int ntiles, int ks, int nrows, int32_t* __restrict__ Y,
+                       uint64_t* __restrict__ part) {
+  extern __shared__ __align__(16) unsigned char tc_smem_raw[];
+  __shared__ __align__(8) uint64_t full[kTsStages], empty[kTsStages], accf, tmem_empty;
+  __shared__ uint32_t tmem_holder;
+  __shared__ int fail;
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = (K + kTcKB - 1) / kTcKB;
+  const int nitems = ntiles * ks;
+  const int my_tiles = blockIdx.x < nitems ? (nitems - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTsStages; ++i) {
+      tc_mbar_init(&full[i], 1);
+      tc_mbar_init(&empty[i], 1);
+    }
+    tc_mbar_init(&accf, 1);
+    tc_mbar_init(&tmem_empty, kTcEpiWarps);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    fail = 0;
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_holder)),
+                 "r"(kTcCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_holder;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (warp == kTcEpiWarps) {
+    // ---- producer: weight planes (128 rows) and activation limbs (64 tokens)
+    if (lane == 0) {
+      int q = 0;
+      for (int it = 0; it < my_tiles; ++it) {
+        const int item = blockIdx.x + it * gridDim.x, t = item / ks, sp = item % ks;
+        const int r0 = (t % tiles_n) * kTsM, t0 = (t / tiles_n) * kTsT;
+        const int kb0 = (int)((int64_t)nkb * sp / ks), kb1 = (int)((int64_t)nkb * (sp + 1) / ks);
+        for (int kb = kb0; kb < kb1; ++kb, ++q) {
+          const int st = q % kTsStages;
+          if (q >= kTsStages && !tc_mbar_wait(&empty[st], ((q / kTsStages) - 1) & 1)) fail = 1;
+          unsigned char* sbuf = smem + (size_t)st * kTsStage;
+          tc_mbar_expect_tx(&full[st], kTsStage);
+          tma_load_3d(sbuf, &wmap, kb * kTcKB, r0, 0, &full[st]);
+          tma_load_3d(sbuf + kTsATile, &wmap, kb * kTcKB, r0, 1, &full[st]);
+          for (int a = 0; a < 4; ++a)
+            tma_load_3d(sbuf + 2 * kTsATile + a * kTsBTile, &amap, kb * kTcKB, t0, a, &full[st]);
+        }
+      }
+    }
+  } else if (warp == kTcEpiWarps + 1) {
+    // ---- MMA issue
+    if (lane == 0) {
+      int q = 0, qlast = 0;
+      for (int it = 0; it < my_tiles; ++it) {
+        const int sp = (blockIdx.x + it * gridDim.x) % ks;
+        qlast += (int)((int64_t)nkb * (sp + 1) / ks) - (int)((int64_t)nkb * sp / ks);
+      }
+      for (int it = 0; it < my_tiles; ++it) {
+        const int sp = (blockIdx.x + it * gridDim.x) % ks;
+        const int kb0 = (int)((int64_t)nkb * sp / ks), kb1 = (int)((int64_t)nkb * (sp + 1) / ks);
+        if (it > 0 && !tc_mbar_wait(&tmem_empty, (it - 1) & 1)) fail = 1;
+        tc_fence_after();
+        for (int kb = kb0; kb < kb1; ++kb, ++q) {
+          const int st = q % kTsStages;
+          if (!tc_mbar_wait(&full[st], (q / kTsStages) & 1)) fail = 1;
+          tc_fence_after();
+          const uint32_t sb = su32(smem + (size_t)st * kTsStage);
+#pragma unroll
+          for (int j = 0; j < kTcKB / 32; ++j) {
+            const uint64_t w0 = smem_desc_sw64(sb + 32 * j), w1 = smem_desc_sw64(sb + kTsATile + 32 * j);
+            const uint64_t xb = smem_desc_sw64(sb + 2 * kTsATile + 32 * j);
+            if (kb == kb0 && j == 0) {
+              tc_mma(tmem, w0, xb, kTsIdesc, 0u);
+              tc_mma(tmem + kTsT, w1, xb, kTsIdesc3, 1u);
+              tc_mma(tmem + 4 * kTsT, w1, smem_desc_sw64(sb + 2 * kTsATile + 3 * kTsBTile + 32 * j), kTsIdesc1, 0u);
+            } else {
+              tc_mma(tmem, w0, xb, kTsIdesc, 1u);
+              tc_mma(tmem + kTsT, w1, xb, kTsIdesc, 1u);
+            }
+          }
+          if (q + kTsStages < qlast) tc_commit(&empty[st]);
+        }
+        tc_commit(&accf);
+      }
+    }
+  } else {
+    // ---- epilogue: warp w reads TMEM lanes 32*(w%4).. (weight rows) and
+    // tokens [32*(w/4), 32*(w/4) + 32) of the tile
+    const int quarter = warp & 3, half = warp >> 2;
+    const int rl = 32 * quarter + lane;
+    const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16);
+    for (int it = 0; it < my_tiles; ++it) {
+      const int item = blockIdx.x + it * gridDim.x, t = item / ks, sp = item % ks;
+      const int r = (t % tiles_n) * kTsM + rl, t0 = (t / tiles_n) * kTsT;
+      const bool rok = EPI == 3 ? r < nrows : r < N;
+      const uint64_t bcorr = (EPI == 0 && rok) ? (brow[r] << 31) - ((uint64_t)K << 46) : 0;
+      if (!tc_mbar_wait(&accf, it & 1)) fail = 1;
+      tc_fence_after();
+      for (int c0 = 32 * half; c0 < 32 * half + 32; c0 += 8) {
+        uint32_t g[5][8];
+#pragma unroll
+        for (int gg = 0; gg < 5; ++gg) tmem_ld8(tbase + kTsT * gg + c0, g[gg]);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int tok = t0 + c0 + i;
+          if (rok && tok < S) {
+            const uint64_t raw = (uint64_t)g[0][i] + ((uint64_t)g[1][i] << 8) + ((uint64_t)g[2][i] << 16) +
+                                 ((uint64_t)g[3][i] << 24) + ((uint64_t)g[4][i] << 32);
+            if (EPI == 3) part[((size_t)sp * S + tok) * nrows + r] = raw;
+            else Y[(size_t)tok * N + r] = requantize((int64_t)(raw - (arow[tok] << 15) - bcorr));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&tmem_empty)) : "memory");
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (fail && threadIdx.x == 0) atomicExch(&g_tc_err, 1);
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcCols) : "memory");
+  }
+}
+
 // Split-K finish: y = sum over splits of the raw partials, minus the row-sum
 // corrections over the full K, then the epilogue.  MODE 0 plain, 1
 // gelu(y) * vec[s, n] (row stride ldv), 2 gate/up pair, 3 the exact i64 sum
@@ -538,6 +704,8 @@ int tc_error_flag(bool reset) {
 }
 
 void tc_init() {
+  cudaFuncSetAttribute(tc_linear_t_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTsSmem);
+  cudaFuncSetAttribute(tc_linear_t_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTsSmem);
   cudaFuncSetAttribute(tc_linear_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
   cudaFuncSetAttribute(tc_linear_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
   cudaFuncSetAttribute(tc_linear_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
@@ -586,7 +754,8 @@ bool tc_prepare_weight_slice(TcWeight& t, const DevMat& g, const DevMat* u, int 
   tc_weight_prep_kernel<<<t.nrows, 128, 0, s>>>(static_cast<const int16_t*>(g.p),
                                                 pair ? static_cast<const int16_t*>(u->p) : nullptr, rows, cols,
                                                 t.nrows, t.planes, t.rowsum, row0, col0, g.cols);
-  return encode_planes(t.map, t.planes, 2, t.nrows, t.K, kTcN);
+  return encode_planes(t.map, t.planes, 2, t.nrows, t.K, kTcN) &&
+         encode_planes(t.map_m, t.planes, 2, t.nrows, t.K, kTsM);
 }
 
 size_t tc_act_bytes(int S, int K) { return 4 * (size_t)S * K + (size_t)S * 8; }
@@ -597,10 +766,79 @@ bool tc_prepare_act(TcAct& a, const int32_t* X, int S, int K, void* mem, cudaStr
   a.planes = static_cast<uint8_t*>(mem);
   a.rowsum = reinterpret_cast<uint64_t*>(a.planes + 4 * (size_t)S * K);
   tc_launch(tc_act_prep_kernel, dim3(S), dim3(256), 0, s, X, S, K, a.planes, a.rowsum);
-  return encode_planes(a.map, a.planes, 4, S, K, kTcM);
+  return encode_planes(a.map, a.planes, 4, S, K, kTcM) && encode_planes(a.map_t, a.planes, 4, S, K, kTsT);
 }
 
+namespace {
+
+// The split-K finish for partial sums part[ks][S][nrows]: corrections and
+// the epilogue the output asks for.
+void launch_splitk_reduce(const TcAct& a, const TcWeight& w, const TcOut& o, int ks, const uint64_t* part, int ldv,
+                          cudaStream_t s) {
+  const int sms = sm_count();
+  const size_t total = (size_t)a.S * w.N;
+  const int rblocks = (int)std::min<size_t>((total + 255) / 256, (size_t)sms * 8);
+  if (o.y64)
+    tc_launch(tc_splitk_reduce_kernel<3>, dim3(rblocks), dim3(256), 0, s, part, ks, a.S, w.nrows, w.N, a.K, a.rowsum,
+              w.rowsum, (int32_t*)nullptr, o.y64, o.vec, ldv);
+  else if (w.pair)
+    tc_launch(tc_splitk_reduce_kernel<2>, dim3(rblocks), dim3(256), 0, s, part, ks, a.S, w.nrows, w.N, a.K, a.rowsum,
+              w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv);
+  else if (o.epi == kEpiGeluMul)
+    tc_launch(tc_splitk_reduce_kernel<1>, dim3(rblocks), dim3(256), 0, s, part, ks, a.S, w.nrows, w.N, a.K, a.rowsum,
+              w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv);
+  else
+    tc_launch(tc_splitk_reduce_kernel<0>, dim3(rblocks), dim3(256), 0, s, part, ks, a.S, w.nrows, w.N, a.K, a.rowsum,
+              w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv);
+}
+
+// S <= 64: the swapped-operand kernel.  K splits are chosen by a small time
+// model: a stage streams 16 KB of weights, about 0.4 us when every SM
+// streams; partial sums cost 16 bytes per value and split (written, then
+// read) at about 6 TB/s.  A plain output with one split needs no partials.
+// Returns false (nothing launched) when partial sums are needed and the
+// scratch cannot hold them.
+bool launch_tc_linear_t(const TcAct& a, const TcWeight& w, const TcOut& o, int ldv, cudaStream_t s) {
+  const int tiles_n = (w.nrows + kTsM - 1) / kTsM, tiles_t = (a.S + kTsT - 1) / kTsT;
+  const int ntiles = tiles_n * tiles_t;
+  const int nkb = (a.K + kTcKB - 1) / kTcKB;
+  const int sms = sm_count();
+  const bool direct_ok = !w.pair && o.epi == kEpiPlain && !o.y64;
+  const size_t per_split = (size_t)a.S * w.nrows * 8;
+  const double t_stage = 0.4e-6, bw = 6e12;
+  int ks = 0;
+  double best = 1e30;
+  const int kmax = std::max(1, std::min(nkb / 2, 32));
+  for (int k = 1; k <= kmax; ++k) {
+    const bool partial = k > 1 || !direct_ok;
+    if (partial && (!o.scratch || (size_t)k * per_split > o.scratch_bytes)) continue;
+    const double waves = (double)((ntiles * k + sms - 1) / sms);
+    const double t = waves * ((nkb + k - 1) / k) * t_stage + (partial ? 2.0 * k * per_split / bw : 0.0);
+    if (t < best) {
+      best = t;
+      ks = k;
+    }
+  }
+  if (ks == 0) return false;
+  const CUtensorMap& am = *reinterpret_cast<const CUtensorMap*>(a.map_t);
+  const CUtensorMap& wm = *reinterpret_cast<const CUtensorMap*>(w.map_m);
+  const int grid = std::min(ntiles * ks, sms);
+  if (ks == 1 && direct_ok) {
+    tc_launch(tc_linear_t_kernel<0>, dim3(grid), dim3(kTcThreads), kTsSmem, s, am, wm, a.rowsum, w.rowsum, a.S, w.N,
+              a.K, tiles_n, ntiles, 1, w.nrows, o.y, (uint64_t*)nullptr);
+    return true;
+  }
+  uint64_t* part = static_cast<uint64_t*>(o.scratch);
+  tc_launch(tc_linear_t_kernel<3>, dim3(grid), dim3(kTcThreads), kTsSmem, s, am, wm, a.rowsum, w.rowsum, a.S, w.N,
+            a.K, tiles_n, ntiles, ks, w.nrows, (int32_t*)nullptr, part);
+  launch_splitk_reduce(a, w, o, ks, part, ldv, s);
+  return true;
+}
+
+}  // namespace
+
 bool launch_tc_linear(const TcAct& a, const TcWeight& w, const TcOut& o, cudaStream_t s) {
+  if (a.S <= kTsT && launch_tc_linear_t(a, w, o, o.ldv > 0 ? o.ldv : w.N, s)) return true;
   const int ntiles_n = (w.nrows + kTcN - 1) / kTcN;
   const int ntiles = ntiles_n * ((a.S + kTcM - 1) / kTcM);
   const int nkb = (a.K + kTcKB - 1) / kTcKB;
@@ -636,20 +874,7 @@ bool launch_tc_linear(const TcAct& a, const TcWeight& w, const TcOut& o, cudaStr
   const int grid = std::min(ntiles * ks, sms);
   tc_launch(tc_linear_kernel<3>, dim3(grid), dim3(kTcThreads), kTcSmem, s, am, bm, a.rowsum, w.rowsum, a.S, w.N, a.K,
             ntiles_n, ntiles, ks, w.nrows, (int32_t*)nullptr, (const int32_t*)nullptr, ldv, part);
-  const size_t total = (size_t)a.S * w.N;
-  const int rblocks = (int)std::min<size_t>((total + 255) / 256, (size_t)sms * 8);
-  if (o.y64)
-    tc_launch(tc_splitk_reduce_kernel<3>, dim3(rblocks), dim3(256), 0, s, (const uint64_t*)part, ks, a.S, w.nrows,
-              w.N, a.K, a.rowsum, w.rowsum, (int32_t*)nullptr, o.y64, o.vec, ldv);
-  else if (w.pair)
-    tc_launch(tc_splitk_reduce_kernel<2>, dim3(rblocks), dim3(256), 0, s, (const uint64_t*)part, ks, a.S, w.nrows,
-              w.N, a.K, a.rowsum, w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv);
-  else if (o.epi == kEpiGeluMul)
-    tc_launch(tc_splitk_reduce_kernel<1>, dim3(rblocks), dim3(256), 0, s, (const uint64_t*)part, ks, a.S, w.nrows,
-              w.N, a.K, a.rowsum, w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv);
-  else
-    tc_launch(tc_splitk_reduce_kernel<0>, dim3(rblocks), dim3(256), 0, s, (const uint64_t*)part, ks, a.S, w.nrows,
-              w.N, a.K, a.rowsum, w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv);
+  launch_splitk_reduce(a, w, o, ks, part, ldv, s);
   return true;
 }
 

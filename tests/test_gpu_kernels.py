@@ -62,7 +62,10 @@ def test_gemv_bit_exact(width, shape, adv):
     (1, 64, 64), (5, 70, 33), (64, 128, 256), (130, 96, 520), (17, 2560, 512),
     # tensor-core path (>= 32 rows, i16, cols % 16 == 0): one partial tile, odd
     # row counts, several M and N tiles, K across many stages and the longest K
-    (32, 16, 16), (33, 97, 48), (200, 2560, 512), (257, 300, 2560), (129, 193, 1024), (96, 256, 10240)])
+    (32, 16, 16), (33, 97, 48), (200, 2560, 512), (257, 300, 2560), (129, 193, 1024), (96, 256, 10240),
+    # at most 64 rows: the swapped-operand kernel (weights as the 128-row MMA
+    # operand), with K split across SMs and with one K range
+    (64, 2560, 2560), (48, 1000, 4096), (64, 4096, 256)])
 def test_linear_bit_exact(width, S, rows, cols):
     rng = np.random.default_rng(S * 1000 + rows + width)
     w = rand_w(rng, rows, cols, width, True)
