@@ -69,6 +69,19 @@ RDET_HD int64_t acc_add_sat(int64_t a, int64_t b) {  // ops.rs:433
 }
 RDET_HD int32_t mul_sat(int32_t a, int32_t b) { return requantize((int64_t)a * (int64_t)b); }  // ops.rs:38
 
+// c + a * b for i32 a, b and an i64 accumulator, wrapping (the MAC step of
+// every det dot product).  On the device one widening multiply-add: written
+// as (int64_t)a * b + c the compiler emits a slower sequence.
+RDET_HD int64_t mac_wide(int64_t c, int32_t a, int32_t b) {
+#ifdef __CUDA_ARCH__
+  int64_t d;
+  asm("mad.wide.s32 %0, %1, %2, %3;" : "=l"(d) : "r"(a), "r"(b), "l"(c));
+  return d;
+#else
+  return (int64_t)((uint64_t)c + (uint64_t)((int64_t)a * (int64_t)b));
+#endif
+}
+
 // ops.rs:688 specialised to an i64 dividend and a positive i64 divisor.
 RDET_HD int64_t rte_div_i64(int64_t n, int64_t d) {
   int64_t q = n / d, r = n % d;

@@ -161,15 +161,15 @@ __device__ __forceinline__ int64_t row_dot16(const int16_t* row, const int32_t* 
         if (c < nc) {
           const int4* xp = reinterpret_cast<const int4*>(xs + 8 * c);
           int4 a = xp[0], b = xp[1];
-          acc += (int64_t)a.x * lo16(w[u].x) + (int64_t)a.y * hi16(w[u].x);
-          acc += (int64_t)a.z * lo16(w[u].y) + (int64_t)a.w * hi16(w[u].y);
-          acc += (int64_t)b.x * lo16(w[u].z) + (int64_t)b.y * hi16(w[u].z);
-          acc += (int64_t)b.z * lo16(w[u].w) + (int64_t)b.w * hi16(w[u].w);
+          acc = mac_wide(mac_wide(acc, a.x, lo16(w[u].x)), a.y, hi16(w[u].x));
+          acc = mac_wide(mac_wide(acc, a.z, lo16(w[u].y)), a.w, hi16(w[u].y));
+          acc = mac_wide(mac_wide(acc, b.x, lo16(w[u].z)), b.y, hi16(w[u].z));
+          acc = mac_wide(mac_wide(acc, b.z, lo16(w[u].w)), b.w, hi16(w[u].w));
         }
       }
     }
   } else {
-    for (int k = lane; k < K; k += 32) acc += (int64_t)xs[k] * (int64_t)row[k];
+    for (int k = lane; k < K; k += 32) acc = mac_wide(acc, xs[k], (int32_t)row[k]);
   }
   return warp_sum64(acc);
 }
@@ -191,13 +191,13 @@ __device__ __forceinline__ int64_t row_dot32(const int32_t* row, const int32_t* 
         int c = c0 + 32 * u;
         if (c < nc) {
           int4 a = reinterpret_cast<const int4*>(xs)[c];
-          acc += (int64_t)a.x * (int32_t)w[u].x + (int64_t)a.y * (int32_t)w[u].y;
-          acc += (int64_t)a.z * (int32_t)w[u].z + (int64_t)a.w * (int32_t)w[u].w;
+          acc = mac_wide(mac_wide(acc, a.x, (int32_t)w[u].x), a.y, (int32_t)w[u].y);
+          acc = mac_wide(mac_wide(acc, a.z, (int32_t)w[u].z), a.w, (int32_t)w[u].w);
         }
       }
     }
   } else {
-    for (int k = lane; k < K; k += 32) acc += (int64_t)xs[k] * (int64_t)row[k];
+    for (int k = lane; k < K; k += 32) acc = mac_wide(acc, xs[k], (int32_t)row[k]);
   }
   return warp_sum64(acc);
 }
@@ -623,6 +623,9 @@ constexpr int kG3ThreadsPerSm = 512;
 #define RDET_GEMV3_NCH_W32 6
 #endif
 
+// (The product form (int64_t)x * w is kept here: the streaming GEMV is
+// bound by HBM, and mac_wide chains raised its register use past the
+// 512-thread budget.)
 template <int WB>
 __device__ __forceinline__ void dot_chunk(const uint4& w, const int32_t* xs, int c, int64_t& a0, int64_t& a1) {
   if (WB == 2) {
@@ -936,8 +939,8 @@ __global__ void __launch_bounds__(256) linear_kernel(const int32_t* __restrict__
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          acc[i][j] += (int64_t)xv[i] * wv[j];
-          if (PAIR) accu[i][j] += (int64_t)xv[i] * uv[j];
+          acc[i][j] = mac_wide(acc[i][j], xv[i], wv[j]);
+          if (PAIR) accu[i][j] = mac_wide(accu[i][j], xv[i], uv[j]);
         }
     }
     __syncthreads();
@@ -1303,8 +1306,9 @@ constexpr int kAcWarps = kAcThreads / 32;
 constexpr int kAcTileBytes = 32 * 1024;
 constexpr int kAcStages = 4;
 
-__device__ __forceinline__ int64_t dot4(const int4& k, const int4& q) {
-  return (int64_t)k.x * q.x + (int64_t)k.y * q.y + (int64_t)k.z * q.z + (int64_t)k.w * q.w;
+// acc + k . q over one 16-byte chunk (wrapping)
+__device__ __forceinline__ int64_t dot4_acc(int64_t acc, const int4& k, const int4& q) {
+  return mac_wide(mac_wide(mac_wide(mac_wide(acc, k.x, q.x), k.y, q.y), k.z, q.z), k.w, q.w);
 }
 __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
   const unsigned sa = (unsigned)__cvta_generic_to_shared(dst);
@@ -1550,7 +1554,7 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
         for (int g = 0; g < GC; ++g) {
           int64_t x = 0;
 #pragma unroll
-          for (int u = 0; u < NCH; ++u) x += dot4(kv[u], qv[g][u]);
+          for (int u = 0; u < NCH; ++u) x = dot4_acc(x, kv[u], qv[g][u]);
           acc[r * GC + g] = x;
         }
       }
@@ -1685,10 +1689,10 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
 #pragma unroll
           for (int g = 0; g < GC; ++g) {
             const int32_t w = sc[g * rmax + j];
-            acc[g][u][0] += (int64_t)v.x * w;
-            acc[g][u][1] += (int64_t)v.y * w;
-            acc[g][u][2] += (int64_t)v.z * w;
-            acc[g][u][3] += (int64_t)v.w * w;
+            acc[g][u][0] = mac_wide(acc[g][u][0], v.x, w);
+            acc[g][u][1] = mac_wide(acc[g][u][1], v.y, w);
+            acc[g][u][2] = mac_wide(acc[g][u][2], v.z, w);
+            acc[g][u][3] = mac_wide(acc[g][u][3], v.w, w);
           }
         }
       }
@@ -1919,7 +1923,7 @@ __global__ void attn_prefill_kernel(const AttnPrefillArgs a, int rowlen) {
   for (int j = warp; j < n; j += nwarp) {
     const int32_t* kr = a.k_cache + ((size_t)kvh * a.cap + start + j) * d;
     int64_t acc = 0;
-    for (int t = lane; t < d; t += 32) acc += (int64_t)kr[t] * qs[t];
+    for (int t = lane; t < d; t += 32) acc = mac_wide(acc, kr[t], qs[t]);
     int32_t v = requantize(warp_sum64(acc));
     if (lane == 0) sc[j] = v;
     if (v > bm) { bm = v; bi = j; }
@@ -1972,7 +1976,7 @@ __global__ void attn_prefill_kernel(const AttnPrefillArgs a, int rowlen) {
   for (int t = threadIdx.x; t < d; t += blockDim.x) {
     int64_t acc = 0;
     const int32_t* vb = a.v_cache + ((size_t)kvh * a.cap + start) * d + t;
-    for (int j = 0; j < n; ++j) acc += (int64_t)vb[(size_t)j * d] * sc[j];
+    for (int j = 0; j < n; ++j) acc = mac_wide(acc, vb[(size_t)j * d], sc[j]);
     a.out[((size_t)i * a.Hq + h) * d + t] = requantize(acc);
   }
 }
@@ -2030,7 +2034,7 @@ __global__ void __launch_bounds__(256) attn_prefill_tiled(const AttnPrefillArgs 
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
         int4 qv = reinterpret_cast<const int4*>(Qs + (rbase + t) * dp)[c];
-        acc[t] += (int64_t)kv.x * qv.x + (int64_t)kv.y * qv.y + (int64_t)kv.z * qv.z + (int64_t)kv.w * qv.w;
+        acc[t] = dot4_acc(acc[t], kv, qv);
       }
     }
     const int j = kt + lane;
@@ -2119,11 +2123,11 @@ __global__ void __launch_bounds__(256) attn_prefill_tiled(const AttnPrefillArgs 
           int4 v = reinterpret_cast<const int4*>(Ks + jj * cwp)[dg];
 #pragma unroll
           for (int t = 0; t < 8; ++t) {
-            int64_t w = Ws[(rg * 8 + t) * AP_TK + jj];
-            acc[t][0] += w * v.x;
-            acc[t][1] += w * v.y;
-            acc[t][2] += w * v.z;
-            acc[t][3] += w * v.w;
+            const int32_t w = Ws[(rg * 8 + t) * AP_TK + jj];
+            acc[t][0] = mac_wide(acc[t][0], w, v.x);
+            acc[t][1] = mac_wide(acc[t][1], w, v.y);
+            acc[t][2] = mac_wide(acc[t][2], w, v.z);
+            acc[t][3] = mac_wide(acc[t][3], w, v.w);
           }
         }
       }
@@ -2266,16 +2270,23 @@ __global__ void add_i32_rows_kernel(int32_t* const* p, int32_t n, int32_t v) {
 void launch_add_i32_rows(int32_t* const* p, int32_t n, int32_t v, cudaStream_t s) {
   launch_k(add_i32_rows_kernel, dim3(1), dim3(256), 0, s, p, n, v);
 }
-__global__ void scatter_rows_kernel(const int32_t* src, int32_t n, int32_t* const* dst, size_t off) {
+// Row r of src -> dst[r] + off; with cap > 0 each value passes through
+// softcap_act on the way (the logit softcap fused into the copy).
+__global__ void scatter_rows_kernel(const int32_t* src, int32_t n, int32_t* const* dst, size_t off, int32_t cap) {
   pdl_entry();
-  const int r = blockIdx.x;
+  const int r = blockIdx.y;
   const int32_t* sr = src + (size_t)r * n;
   int32_t* dr = dst[r] + off;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) dr[i] = sr[i];
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int32_t v = sr[i];
+    dr[i] = cap > 0 ? softcap_act(v, cap) : v;
+  }
 }
 void launch_scatter_rows(const int32_t* src, int32_t rows, int32_t n, int32_t* const* dst, size_t off,
-                         cudaStream_t s) {
-  launch_k(scatter_rows_kernel, dim3(rows), dim3(256), 0, s, src, n, dst, off);
+                         cudaStream_t s, int32_t cap) {
+  // about 8 values per thread, every row spread over several blocks
+  const int bx = std::max(1, std::min(1024, (n + 2047) / 2048));
+  launch_k(scatter_rows_kernel, dim3(bx, rows), dim3(256), 0, s, src, n, dst, off, cap);
 }
 
 __global__ void requantize_rows_kernel(const int64_t* x, size_t n, int32_t* y) {

@@ -259,9 +259,10 @@ void launch_requantize_rows(const int64_t* x, size_t n, int32_t* y, cudaStream_t
 // vocab-sharded logits: src [world][rows][vl] -> dst[r][w * vl + j]
 void launch_gather_vocab(const int32_t* src, int32_t world, int32_t rows, int32_t vl, int32_t* const* dst,
                          cudaStream_t s);
-// dst[r] + off <- src row r (n ints), for r < rows
+// dst[r] + off <- src row r (n ints), for r < rows; cap > 0 applies the
+// logit softcap (softcap_act) to every value copied
 void launch_scatter_rows(const int32_t* src, int32_t rows, int32_t n, int32_t* const* dst, size_t off,
-                         cudaStream_t s);
+                         cudaStream_t s, int32_t cap = 0);
 void launch_copy_rows(const int32_t* src, int32_t* dst, size_t n, cudaStream_t s);
 // synthetic weights (counter-based generator, see detwgt.py)
 void launch_synth(void* dst, int32_t width, int32_t rank, int64_t n, int64_t cols, uint64_t key, cudaStream_t s);

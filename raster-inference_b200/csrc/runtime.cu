@@ -1635,8 +1635,7 @@ static void decode_batch(Ctx& c, Seq* const* seqs, const uint32_t* tokens, int B
   for (int l = 0; l < m.L; ++l) cur = const_cast<int32_t*>(decode_batch_layer(c, B, maxcap, l, cur));
   launch_rmsnorm_rows(cur, B, m.H, c.final_norm, c.eps, w.nrm, s);
   prefill_linear(c, w.nrm, B, c.lm_head, c.t_lm_head, bw.logits, kEpiPlain, nullptr);
-  if (m.has_softcap) launch_softcap(bw.logits, B * m.V, c.softcap, s);
-  launch_scatter_rows(bw.logits, B, m.V, bw.logits_dst, 0, s);
+  launch_scatter_rows(bw.logits, B, m.V, bw.logits_dst, 0, s, m.has_softcap ? c.softcap : 0);
   launch_add_i32_rows(bw.pos, B, 1, s);
   CK(cudaGetLastError());
   for (int i = 0; i < B; ++i) {
