@@ -1677,25 +1677,39 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
     wait_tile(uu);
     const int r0 = t * TR, nr = min(TR, rows - r0);
     const int32_t* tile = reinterpret_cast<const int32_t*>(ring + (size_t)(uu % kAcStages) * kAcTileBytes);
-    for (int i = warp; i < nr; i += kAcWarps) {
-      const int j = r0 + i;
-      const int4* vr = reinterpret_cast<const int4*>(
-          (new_row && start + lo + j == pos) ? kvrow + d : tile + (size_t)i * d);
+    // two rows per warp step: both rows' V chunks and weights are loaded
+    // before any multiply-add (rows past the tile load as zero weight x 0)
+    for (int i0 = warp; i0 < nr; i0 += 2 * kAcWarps) {
+      int4 vv[2][NCH];
+      int32_t ww[2][GC];
 #pragma unroll
-      for (int u = 0; u < NCH; ++u) {
-        const int c = lane + 32 * u;
-        if (c < nch) {
-          const int4 v = vr[c];
+      for (int h = 0; h < 2; ++h) {
+        const int i = i0 + h * kAcWarps;
+        const bool ok = i < nr;
+        const int j = r0 + (ok ? i : 0);
+        const int4* vr = reinterpret_cast<const int4*>(
+            (new_row && start + lo + j == pos) ? kvrow + d : tile + (size_t)(ok ? i : 0) * d);
+#pragma unroll
+        for (int u = 0; u < NCH; ++u) {
+          const int c = lane + 32 * u;
+          vv[h][u] = (ok && c < nch) ? vr[c] : make_int4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int g = 0; g < GC; ++g) ww[h][g] = ok ? sc[g * rmax + j] : 0;
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int u = 0; u < NCH; ++u)
 #pragma unroll
           for (int g = 0; g < GC; ++g) {
-            const int32_t w = sc[g * rmax + j];
+            const int32_t w = ww[h][g];
+            const int4 v = vv[h][u];
             acc[g][u][0] = mac_wide(acc[g][u][0], v.x, w);
             acc[g][u][1] = mac_wide(acc[g][u][1], v.y, w);
             acc[g][u][2] = mac_wide(acc[g][u][2], v.z, w);
             acc[g][u][3] = mac_wide(acc[g][u][3], v.w, w);
           }
-        }
-      }
     }
     __syncthreads();
     if (tid == 0 && uu + kAcStages < total_tiles) issue(uu + kAcStages);
