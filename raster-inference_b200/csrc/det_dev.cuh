@@ -67,7 +67,17 @@ RDET_HD int64_t acc_add_sat(int64_t a, int64_t b) {  // ops.rs:433
   if (((a ^ (int64_t)s) & (b ^ (int64_t)s)) < 0) return a < 0 ? INT64_MIN : INT64_MAX;
   return (int64_t)s;
 }
-RDET_HD int32_t mul_sat(int32_t a, int32_t b) { return requantize((int64_t)a * (int64_t)b); }  // ops.rs:38
+// a * b widened to i64 (one widening multiply on the device)
+RDET_HD int64_t mul_wide(int32_t a, int32_t b) {
+#ifdef __CUDA_ARCH__
+  int64_t d;
+  asm("mul.wide.s32 %0, %1, %2;" : "=l"(d) : "r"(a), "r"(b));
+  return d;
+#else
+  return (int64_t)a * (int64_t)b;
+#endif
+}
+RDET_HD int32_t mul_sat(int32_t a, int32_t b) { return requantize(mul_wide(a, b)); }  // ops.rs:38
 
 // c + a * b for i32 a, b and an i64 accumulator, wrapping (the MAC step of
 // every det dot product).  On the device one widening multiply-add: written

@@ -73,35 +73,36 @@ __device__ __forceinline__ uint64_t warp_satsum(uint64_t v) {
   return v;
 }
 
-// rms_norm_scale (ops.rs:406) of n values in shared memory, computed by the
-// whole block; every thread gets the scale.  `red` is >= 33 u64 of smem.
-__device__ int32_t block_norm_scale(const int32_t* xs, int n, int64_t eps, uint64_t* red) {
-  uint64_t s = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    int64_t v = xs[i];
-    s = sat_add_u(s, (uint64_t)(v * v));
-  }
+// rms_norm_scale (ops.rs:406) from each thread's saturating partial sum of
+// squares, computed by the whole block; every thread gets the scale.  Warp 0
+// combines the per-warp sums (saturating sums are order-free).  `red` is
+// >= 33 u64 of smem.
+__device__ int32_t block_norm_scale_partial(uint64_t s, int n, int64_t eps, uint64_t* red) {
   s = warp_satsum(s);
-  int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
   __syncthreads();
   if (l == 0) red[w] = s;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    uint64_t t = 0;
-    for (int i = 0; i < nw; ++i) t = sat_add_u(t, red[i]);
-    int64_t mean = div_acc_by_u32((int64_t)t, (uint32_t)n);
-    red[32] = (uint64_t)(uint32_t)inv_sqrt_acc(acc_add_sat(mean, eps));
+  if (w == 0) {
+    const uint64_t t = warp_satsum(l < nw ? red[l] : 0);
+    if (l == 0) {
+      const int64_t mean = div_acc_by_u32((int64_t)t, (uint32_t)n);
+      red[32] = (uint64_t)(uint32_t)inv_sqrt_acc(acc_add_sat(mean, eps));
+    }
   }
   __syncthreads();
   return (int32_t)(uint32_t)red[32];
 }
+// the same over n values in shared memory
+__device__ int32_t block_norm_scale(const int32_t* xs, int n, int64_t eps, uint64_t* red) {
+  uint64_t s = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s = sat_add_u(s, (uint64_t)mul_wide(xs[i], xs[i]));
+  return block_norm_scale_partial(s, n, eps, red);
+}
 // same for one warp over n values (lane-strided); returns scale to all lanes
 __device__ int32_t warp_norm_scale(const int32_t* xs, int n, int64_t eps) {
   uint64_t s = 0;
-  for (int i = threadIdx.x & 31; i < n; i += 32) {
-    int64_t v = xs[i];
-    s = sat_add_u(s, (uint64_t)(v * v));
-  }
+  for (int i = threadIdx.x & 31; i < n; i += 32) s = sat_add_u(s, (uint64_t)mul_wide(xs[i], xs[i]));
   s = warp_satsum(s);
   int32_t sc = 0;
   if ((threadIdx.x & 31) == 0) sc = inv_sqrt_acc(acc_add_sat(div_acc_by_u32((int64_t)s, (uint32_t)n), eps));
@@ -721,6 +722,12 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// K ints into shared memory, 4-byte copies through L1 (measured faster here
+// than 16-byte L1-bypassing copies for vectors the previous kernel wrote).
+__device__ __forceinline__ void g3_vec_load(int32_t* dst, const int32_t* src, int K) {
+  for (int i = threadIdx.x; i < K; i += blockDim.x) cp_async4(dst + i, src + i);
+}
+
 // Shared-memory vectors of the GEMV prologue, each K ints: x, then (when the
 // prologue uses them) res, g1, g2.
 __host__ __device__ inline int gemv_pro_vectors(int pro) {
@@ -765,7 +772,9 @@ __global__ void __launch_bounds__(THREADS, kG3ThreadsPerSm / THREADS) gemv3_kern
   __shared__ uint64_t red[33];
   const int nc = K * WB / 16;
   const int lane = threadIdx.x & 31;
-  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  // items go round the CTAs first (item i -> CTA i % grid), so a GEMV with
+  // fewer items than warp slots still streams from every SM
+  const int gw = (threadIdx.x >> 5) * gridDim.x + blockIdx.x;
   const int nw = gridDim.x * (blockDim.x >> 5);
   const bool has_res = a.pro == kProResNorm || a.pro == kProResScale || a.pro == kProResScaleNorm;
   const bool norm2 = a.pro == kProResNorm || a.pro == kProResScaleNorm;
@@ -781,14 +790,11 @@ __global__ void __launch_bounds__(THREADS, kG3ThreadsPerSm / THREADS) gemv3_kern
     pb = reinterpret_cast<const uint4*>(it.B + (size_t)(it.has_b ? it.rb : it.ra) * K * WB);
     g3_load<WB>(pc, pa, pb, it.has_b, lane, nc, pol);
   }
-  if (a.pro != kProNone)
-    for (int i = threadIdx.x; i < K; i += blockDim.x) cp_async4(g1s + i, a.g1 + i);
-  if (norm2)
-    for (int i = threadIdx.x; i < K; i += blockDim.x) cp_async4(g2s + i, a.g2 + i);
+  if (a.pro != kProNone) g3_vec_load(g1s, a.g1, K);
+  if (norm2) g3_vec_load(g2s, a.g2, K);
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  for (int i = threadIdx.x; i < K; i += blockDim.x) cp_async4(xs + i, a.a + i);
-  if (has_res)
-    for (int i = threadIdx.x; i < K; i += blockDim.x) cp_async4(rs + i, a.res + i);
+  g3_vec_load(xs, a.a, K);
+  if (has_res) g3_vec_load(rs, a.res, K);
   cp_async_wait_all();
   __syncthreads();
   if (a.pro != kProNone) {
@@ -796,15 +802,18 @@ __global__ void __launch_bounds__(THREADS, kG3ThreadsPerSm / THREADS) gemv3_kern
     if (a.pro == kProNorm) {
       for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = mul_sat(mul_sat(xs[i], sc), g1s[i]);
     } else {
+      // the residual pass also gathers the squares the second norm needs;
+      // each thread rescales only the elements it wrote
+      uint64_t s2 = 0;
       for (int i = threadIdx.x; i < K; i += blockDim.x) {
         int32_t t = add_sat(rs[i], mul_sat(mul_sat(xs[i], sc), g1s[i]));
         if (a.has_scalar) t = mul_sat(t, a.scalar);
         xs[i] = t;
+        s2 = sat_add_u(s2, (uint64_t)mul_wide(t, t));
         if (blockIdx.x == 0 && a.t_out) a.t_out[i] = t;
       }
-      __syncthreads();
       if (norm2) {
-        int32_t sc2 = block_norm_scale(xs, K, a.eps, red);
+        const int32_t sc2 = block_norm_scale_partial(s2, K, a.eps, red);
         for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = mul_sat(mul_sat(xs[i], sc2), g2s[i]);
       }
     }
@@ -851,7 +860,7 @@ static bool launch_gemv3(const GemvArgs& a, cudaStream_t s) {
   int items = 0;
   if (a.pair_geglu) items = a.seg[0].w.rows;
   else for (int j = 0; j < a.nseg; ++j) items += (a.seg[j].w.rows + per_item - 1) / per_item;
-  int blocks = (items + warps - 1) / warps;
+  int blocks = items;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   const size_t smem = (size_t)a.K * 4 * gemv_pro_vectors(a.pro);
