@@ -337,6 +337,20 @@ def run_ours(args, rank, world, local_rank):
         e2e_sec = float(tt[0])
     e2e = {"value": world * n_e2e / e2e_sec, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
            "steps": n_e2e}
+    # prefill of one seeded uniform prompt of 512 and of
+    # 2048 tokens through all layers (device-timed, kernels already warm)
+    prefill_lengths = {}
+    for plen in (512, 2048):
+        ps = model.new_sequence(plen + 8)
+        pids = lcg_ids(plen, t["vocab_size"], SEED + 11 + plen)
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        ps.prefill(pids)
+        p1.record(stream)
+        torch.cuda.synchronize()
+        psec = p0.elapsed_time(p1) / 1000
+        prefill_lengths[str(plen)] = {"tok_s": plen / psec, "seconds": psec}
+        ps.free()
     # batched ragged decode (BASELINE config 5 shape): 64 sequences, prompt
     # lengths 128 + draw % 3969 (seeded), one batched decode_transition per step
     batched = None
@@ -408,6 +422,7 @@ def run_ours(args, rank, world, local_rank):
                    "parallelism": f"replicas{world}", "l2": "inputs larger than L2 (all weights streamed every step)",
                    "weight_bytes_hbm": weight_bytes},
         "prefill": {"tokens": ctx, "tok_s": ctx / prefill_s, "seconds": prefill_s},
+        "prefill_config3": prefill_lengths,
         "e2e": e2e,
         "batched_decode": batched,
         "gpu_launches": kernels_per_step * args.steps,
