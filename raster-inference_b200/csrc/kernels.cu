@@ -1027,6 +1027,97 @@ void launch_norm_residual_rows(const int32_t* a, const int32_t* res, int32_t S, 
   launch_k(norm_residual_kernel, dim3(S), dim3(256), smem, s, a, res, n, g, eps, has_scalar, scalar, out);
 }
 
+// Fused row norms (RowNormArgs in kernels.h).  One block per row, n % 4 == 0,
+// every pointer 16-byte aligned (the launcher's caller checks).
+__global__ void row_norm_kernel(const RowNormArgs a, int S) {
+  pdl_entry();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int4* xs = reinterpret_cast<int4*>(smem_raw);
+  __shared__ uint64_t red[33];
+  const int r = blockIdx.x, n = a.n, nq = n >> 2;
+  const int4* ar = reinterpret_cast<const int4*>(a.a + (size_t)r * n);
+  uint64_t s = 0;
+  for (int q = threadIdx.x; q < nq; q += blockDim.x) {
+    const int4 v = ar[q];
+    xs[q] = v;
+    s = sat_add_u(s, (uint64_t)mul_wide(v.x, v.x));
+    s = sat_add_u(s, (uint64_t)mul_wide(v.y, v.y));
+    s = sat_add_u(s, (uint64_t)mul_wide(v.z, v.z));
+    s = sat_add_u(s, (uint64_t)mul_wide(v.w, v.w));
+  }
+  const int32_t sc = block_norm_scale_partial(s, n, a.eps, red);
+  const int4* g1 = reinterpret_cast<const int4*>(a.g1);
+  auto nrm = [](int32_t x, int32_t k, int32_t g) { return mul_sat(mul_sat(x, k), g); };
+  // y row out: values, and the byte planes + row sum of y + 2^31
+  uint64_t usum = 0;
+  const size_t plane = (size_t)S * n;
+  auto emit = [&](int q, int4 y) {
+    if (a.y_out) reinterpret_cast<int4*>(a.y_out + (size_t)r * n)[q] = y;
+    if (a.planes) {
+      const uint32_t u[4] = {(uint32_t)y.x + 0x80000000u, (uint32_t)y.y + 0x80000000u, (uint32_t)y.z + 0x80000000u,
+                             (uint32_t)y.w + 0x80000000u};
+      usum += (uint64_t)u[0] + u[1] + u[2] + u[3];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t packed = ((u[0] >> (8 * b)) & 0xffu) | (((u[1] >> (8 * b)) & 0xffu) << 8) |
+                                (((u[2] >> (8 * b)) & 0xffu) << 16) | (((u[3] >> (8 * b)) & 0xffu) << 24);
+        *reinterpret_cast<uint32_t*>(a.planes + b * plane + (size_t)r * n + 4 * q) = packed;
+      }
+    }
+  };
+  if (a.res) {
+    const int4* rr = reinterpret_cast<const int4*>(a.res + (size_t)r * n);
+    uint64_t s2 = 0;
+    for (int q = threadIdx.x; q < nq; q += blockDim.x) {
+      const int4 x = xs[q], rv = rr[q], g = g1[q];
+      int4 t = make_int4(add_sat(rv.x, nrm(x.x, sc, g.x)), add_sat(rv.y, nrm(x.y, sc, g.y)),
+                         add_sat(rv.z, nrm(x.z, sc, g.z)), add_sat(rv.w, nrm(x.w, sc, g.w)));
+      if (a.has_scalar)
+        t = make_int4(mul_sat(t.x, a.scalar), mul_sat(t.y, a.scalar), mul_sat(t.z, a.scalar), mul_sat(t.w, a.scalar));
+      xs[q] = t;
+      if (a.t_out) reinterpret_cast<int4*>(a.t_out + (size_t)r * n)[q] = t;
+      if (a.scatter) reinterpret_cast<int4*>(a.scatter[r] + a.scatter_off)[q] = t;
+      s2 = sat_add_u(s2, (uint64_t)mul_wide(t.x, t.x));
+      s2 = sat_add_u(s2, (uint64_t)mul_wide(t.y, t.y));
+      s2 = sat_add_u(s2, (uint64_t)mul_wide(t.z, t.z));
+      s2 = sat_add_u(s2, (uint64_t)mul_wide(t.w, t.w));
+    }
+    if (a.g2) {
+      const int32_t sc2 = block_norm_scale_partial(s2, n, a.eps, red);
+      const int4* g2 = reinterpret_cast<const int4*>(a.g2);
+      for (int q = threadIdx.x; q < nq; q += blockDim.x) {
+        const int4 t = xs[q], g = g2[q];
+        emit(q, make_int4(nrm(t.x, sc2, g.x), nrm(t.y, sc2, g.y), nrm(t.z, sc2, g.z), nrm(t.w, sc2, g.w)));
+      }
+    } else if (a.planes) {
+      for (int q = threadIdx.x; q < nq; q += blockDim.x) emit(q, xs[q]);
+    }
+  } else {
+    for (int q = threadIdx.x; q < nq; q += blockDim.x) {
+      const int4 x = xs[q], g = g1[q];
+      emit(q, make_int4(nrm(x.x, sc, g.x), nrm(x.y, sc, g.y), nrm(x.z, sc, g.z), nrm(x.w, sc, g.w)));
+    }
+  }
+  if (a.planes) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) usum += __shfl_xor_sync(0xffffffffu, usum, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = usum;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint64_t t = 0;
+      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+      a.rowsum[r] = t;
+    }
+  }
+}
+void launch_row_norm(const RowNormArgs& a, int32_t rows, cudaStream_t s) {
+  const size_t smem = (size_t)a.n * 4;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(row_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_k(row_norm_kernel, dim3(rows), dim3(256), smem, s, a, (int)rows);
+}
+
 // ---------------------------------------------------------------------------
 // q/k head norms, RoPE, value norm, KV-cache write.  One block per (row, head).
 // ---------------------------------------------------------------------------

@@ -99,6 +99,9 @@ bool tc_prepare_weight_slice(TcWeight& t, const DevMat& g, const DevMat* u, int 
 size_t tc_act_bytes(int S, int K);
 // X [S, K] (16-byte aligned, K % 16 == 0) -> planes in `mem` (tc_act_bytes)
 bool tc_prepare_act(TcAct& a, const int32_t* X, int S, int K, void* mem, cudaStream_t s);
+// Attaches planes already written at `mem` (layout of tc_prepare_act: [4][S][K]
+// bytes of X + 2^31, then S u64 row sums) and encodes their tensor maps.
+bool tc_attach_act(TcAct& a, int S, int K, void* mem);
 // Output of the tensor-core linear.  y: Y [S, N] = epilogue(requantize(X W^T))
 // (a pair writes mul_sat(gelu(gate), up); kEpiGeluMul multiplies by
 // vec[s * ldv + n]).  y64 instead: the exact wrapping i64 sums before
@@ -125,6 +128,31 @@ void launch_rmsnorm_rows(const int32_t* x, int32_t S, int32_t n, const int32_t* 
 // out[s] = scale?(add_sat(res[s], rmsnorm(a[s], g)))
 void launch_norm_residual_rows(const int32_t* a, const int32_t* res, int32_t S, int32_t n, const int32_t* g,
                                int64_t eps, bool has_scalar, int32_t scalar, int32_t* out, cudaStream_t s);
+// Fused per-row norms (one block per row, n % 4 == 0), covering the row
+// kernels between batched-decode GEMMs:
+//   with res: t = res + norm(a) * g1 (then * scalar), stored to t_out (and
+//             copied to scatter[r] + scatter_off when scatter is set);
+//   without:  t = a;
+//   with g2:  y = norm(t) * g2 stored to y_out (without res: y = norm(a) * g1);
+//   planes:   y's tensor-core activation planes ([4][S][n] bytes of y + 2^31)
+//             and row sums, the layout of tc_prepare_act.
+struct RowNormArgs {
+  const int32_t* a = nullptr;
+  const int32_t* res = nullptr;
+  const int32_t* g1 = nullptr;
+  const int32_t* g2 = nullptr;
+  int32_t n = 0;
+  int64_t eps = 0;
+  bool has_scalar = false;
+  int32_t scalar = 0;
+  int32_t* t_out = nullptr;
+  int32_t* y_out = nullptr;
+  int32_t* const* scatter = nullptr;
+  size_t scatter_off = 0;
+  uint8_t* planes = nullptr;
+  uint64_t* rowsum = nullptr;
+};
+void launch_row_norm(const RowNormArgs& a, int32_t rows, cudaStream_t s);
 
 // ---- attention inputs -------------------------------------------------------------
 struct QkvPostArgs {

@@ -847,11 +847,17 @@ static void prefill_linear(Ctx& c, const int32_t* X, int S, const DevMat& w, con
   launch_linear(X, S, w, Y, epi, vec, s);
 }
 // MLP gate/up pair: Y = mul_sat(gelu(X Wg^T), X Wu^T)
-static void prefill_geglu(Ctx& c, const int32_t* X, int S, const LayerDev& L, int32_t* Y) {
+static void prefill_geglu(Ctx& c, const int32_t* X, int S, const LayerDev& L, int32_t* Y,
+                          ActPlanes* shared = nullptr) {
   cudaStream_t s = c.stream;
   if (c.tc && L.tgu.planes && S >= kTcMinRows && L.gate.cols <= c.tc_act_k) {
-    TcAct a;
-    REQUIRE(tc_prepare_act(a, X, S, L.gate.cols, c.tc_act, s), RDET_E_CUDA, "tensor map encoding failed");
+    ActPlanes local;
+    ActPlanes& ap = shared ? *shared : local;
+    if (!ap.ready) {
+      REQUIRE(tc_prepare_act(ap.a, X, S, L.gate.cols, c.tc_act, s), RDET_E_CUDA, "tensor map encoding failed");
+      ap.ready = true;
+    }
+    const TcAct& a = ap.a;
     TcOut o;
     o.y = Y;
     o.scratch = c.tc_split;
@@ -860,6 +866,28 @@ static void prefill_geglu(Ctx& c, const int32_t* X, int S, const LayerDev& L, in
     return;
   }
   launch_linear_geglu(X, S, L.gate, L.up, Y, s);
+}
+
+// Fused per-row norm of the batched decode (row_norm_kernel).  With `ap`,
+// the kernel also writes the activation byte planes of y for the next
+// tensor-core GEMM and attaches them.  Returns false (nothing launched) when
+// a row pointer or gain is not 16-byte aligned or n % 4 != 0.
+static bool row_norm(Ctx& c, RowNormArgs ra, int B, ActPlanes* ap) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (ra.n % 4 != 0 || !al(ra.a) || !al(ra.res) || !al(ra.g1) || !al(ra.g2) || !al(ra.t_out) || !al(ra.y_out))
+    return false;
+  if (ra.scatter && (ra.scatter_off * 4) % 16 != 0) return false;
+  const bool planes = ap && c.tc && B >= kTcMinRows && ra.n <= c.tc_act_k;
+  if (planes) {
+    ra.planes = static_cast<uint8_t*>(c.tc_act);
+    ra.rowsum = reinterpret_cast<uint64_t*>(ra.planes + 4 * (size_t)B * ra.n);
+  }
+  launch_row_norm(ra, B, c.stream);
+  if (planes) {
+    REQUIRE(tc_attach_act(ap->a, B, ra.n, c.tc_act), RDET_E_CUDA, "tensor map encoding failed");
+    ap->ready = true;
+  }
+  return true;
 }
 
 static void check_err_flag(Ctx& c, const char* what) {
@@ -1366,8 +1394,12 @@ static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32
   cudaStream_t s = c.stream;
   const int H = m.H, d = lc.head_dim;
   int32_t* other = cur == w.xa ? w.xb : w.xa;
-  launch_rmsnorm_rows(cur, B, H, L.in_ln, c.eps, w.nrm, s);
   ActPlanes nrm_planes;
+  {
+    RowNormArgs ra;
+    ra.a = cur; ra.g1 = L.in_ln; ra.n = H; ra.eps = c.eps; ra.y_out = w.nrm;
+    if (!row_norm(c, ra, B, &nrm_planes)) launch_rmsnorm_rows(cur, B, H, L.in_ln, c.eps, w.nrm, s);
+  }
   prefill_linear(c, w.nrm, B, L.q, L.tq, w.q, kEpiPlain, nullptr, &nrm_planes);
   QkvPostArgs qa;
   qa.S = B; qa.Hq = m.Hq; qa.Hkv = lc.kv_heads; qa.d = d; qa.rotary = lc.rotary; qa.inv_freq = L.inv_freq;
@@ -1390,19 +1422,44 @@ static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32
   launch_attn_decode_cluster(aa, s);
   prefill_linear(c, w.comb, B, L.o, L.to, w.attn, kEpiPlain, nullptr);
   const bool ple = m.P > 0;
-  launch_norm_residual_rows(w.attn, cur, B, H, L.post_attn_ln, c.eps, false, 0, other, s);
-  launch_rmsnorm_rows(other, B, H, L.pre_ff_ln, c.eps, w.nrm, s);
-  prefill_geglu(c, w.nrm, B, L, w.hbuf);
+  // post-attention norm + residual, then the MLP input norm (and its planes)
+  ActPlanes ff_planes;
+  {
+    RowNormArgs ra;
+    ra.a = w.attn; ra.res = cur; ra.g1 = L.post_attn_ln; ra.g2 = L.pre_ff_ln; ra.n = H; ra.eps = c.eps;
+    ra.t_out = other; ra.y_out = w.nrm;
+    if (!row_norm(c, ra, B, &ff_planes)) {
+      launch_norm_residual_rows(w.attn, cur, B, H, L.post_attn_ln, c.eps, false, 0, other, s);
+      launch_rmsnorm_rows(other, B, H, L.pre_ff_ln, c.eps, w.nrm, s);
+    }
+  }
+  prefill_geglu(c, w.nrm, B, L, w.hbuf, &ff_planes);
   prefill_linear(c, w.hbuf, B, L.down, L.tdown, w.attn, kEpiPlain, nullptr);
-  launch_norm_residual_rows(w.attn, other, B, H, L.post_ff_ln, c.eps, !ple && L.has_scalar, L.scalar, cur, s);
+  // post-MLP norm + residual: the layer output (no PLE; copied to each
+  // sequence's layer-output row) or the per-layer-input GEMM's input
+  ActPlanes pg_planes;
+  bool scattered = false;
+  {
+    RowNormArgs ra;
+    ra.a = w.attn; ra.res = other; ra.g1 = L.post_ff_ln; ra.n = H; ra.eps = c.eps;
+    ra.has_scalar = !ple && L.has_scalar; ra.scalar = L.scalar; ra.t_out = cur;
+    if (!ple) { ra.scatter = bw.dec_out; ra.scatter_off = (size_t)l * H; }
+    if (row_norm(c, ra, B, ple ? &pg_planes : nullptr)) scattered = !ple;
+    else launch_norm_residual_rows(w.attn, other, B, H, L.post_ff_ln, c.eps, !ple && L.has_scalar, L.scalar, cur, s);
+  }
   int32_t* result = cur;
   if (ple) {
-    prefill_linear(c, cur, B, L.ple_gate, L.tpg, w.g, kEpiGeluMul, w.ple_all + (size_t)l * B * m.P);
+    prefill_linear(c, cur, B, L.ple_gate, L.tpg, w.g, kEpiGeluMul, w.ple_all + (size_t)l * B * m.P, &pg_planes);
     prefill_linear(c, w.g, B, L.ple_proj, L.tpp, w.pr, kEpiPlain, nullptr);
-    launch_norm_residual_rows(w.pr, cur, B, H, L.ple_norm, c.eps, L.has_scalar, L.scalar, other, s);
+    RowNormArgs ra;
+    ra.a = w.pr; ra.res = cur; ra.g1 = L.ple_norm; ra.n = H; ra.eps = c.eps;
+    ra.has_scalar = L.has_scalar; ra.scalar = L.scalar; ra.t_out = other;
+    ra.scatter = bw.dec_out; ra.scatter_off = (size_t)l * H;
+    if (row_norm(c, ra, B, nullptr)) scattered = true;
+    else launch_norm_residual_rows(w.pr, cur, B, H, L.ple_norm, c.eps, L.has_scalar, L.scalar, other, s);
     result = other;
   }
-  launch_scatter_rows(result, B, H, bw.dec_out, (size_t)l * H, s);
+  if (!scattered) launch_scatter_rows(result, B, H, bw.dec_out, (size_t)l * H, s);
   return result;
 }
 

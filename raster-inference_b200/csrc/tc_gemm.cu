@@ -837,6 +837,14 @@ bool launch_tc_linear_t(const TcAct& a, const TcWeight& w, const TcOut& o, int l
 
 }  // namespace
 
+bool tc_attach_act(TcAct& a, int S, int K, void* mem) {
+  a.S = S;
+  a.K = K;
+  a.planes = static_cast<uint8_t*>(mem);
+  a.rowsum = reinterpret_cast<uint64_t*>(a.planes + 4 * (size_t)S * K);
+  return encode_planes(a.map, a.planes, 4, S, K, kTcM) && encode_planes(a.map_t, a.planes, 4, S, K, kTsT);
+}
+
 bool launch_tc_linear(const TcAct& a, const TcWeight& w, const TcOut& o, cudaStream_t s) {
   if (a.S <= kTsT && launch_tc_linear_t(a, w, o, o.ldv > 0 ? o.ldv : w.N, s)) return true;
   const int ntiles_n = (w.nrows + kTcN - 1) / kTcN;
