@@ -122,7 +122,8 @@ int32_t rdet_generate(rdet_ctx* ctx, rdet_seq* seq, uint32_t n_tokens, uint32_t*
  * (transformer_kernels.rs:1395-1482) as 64 lowercase hex chars + NUL:
  *   EMBEDDING, HIDDEN, LAYER_OUTPUT: build_det_activation_commitment (rows)
  *   LOGITS: build_det_vector_commitment
- *   KV: build_det_kv_cache_commitment; returns RDET_NONE when a layer has no
+ *   KV: build_det_kv_cache_commitment over the caches of layers [0, layer)
+ *       (layer 0: all layers); returns RDET_NONE when one of them has no
  *       cache of its own (KV-sharing layers), like the reference's None. */
 int32_t rdet_read(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t layer, int32_t arg, void* dst, size_t bytes,
                   size_t* size_out);

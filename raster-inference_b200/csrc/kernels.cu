@@ -1896,7 +1896,7 @@ template <int NCH>
 static void ac_prepare(int CL) {
   ac_prepare1<1, NCH>(CL);
   ac_prepare1<2, NCH>(CL);
-  if (NCH <= 2) ac_prepare1<4, NCH>(CL);
+  ac_prepare1<4, NCH>(CL);
 }
 
 static int ac_max_clusters(int CL) {
@@ -1972,10 +1972,15 @@ bool attn_decode_cluster_fits(int Hq, int Hkv, int d, int window, int cap, int r
 
 void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s) {
   int CL = g_attn_cluster ? g_attn_cluster : 8;
+  // batched, 512-dim heads: clusters of 8 so that all four query heads of a
+  // KV head fit one cluster (K/V read once); else the smallest cluster
+  const int Gq = a.group ? a.group : a.Hq / a.Hkv;
+  const bool wide4 = a.batch > 1 && a.d > 256 && Gq % 4 == 0 && CL >= 8 &&
+                     ac_smem(4, a.d, ac_rmax(a.window, a.cap, 8)) <= kAcMaxSmem && a.d <= 128 * 8;
   if (a.batch > 1) {
     // a CTA finalises d / CL output dims (at most 128: the first-max V row
     // is staged in a [GC][128] shared array)
-    int cl = RDET_AC_BATCH_CL;
+    int cl = wide4 ? 8 : RDET_AC_BATCH_CL;
     while (cl < CL && (a.d > 128 * cl || ac_smem(1, a.d, ac_rmax(a.window, a.cap, cl)) > kAcMaxSmem)) cl *= 2;
     CL = cl < CL ? cl : CL;
   }
@@ -1993,7 +1998,7 @@ void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s) {
   const int Gl = std::min(G, a.Hq);
   int gc = ac_group(a.Hq, a.Hq / Gl, a.d);
   if (a.batch > 1) {  // many clusters already: share K/V reads between query heads
-    const int cap = a.d <= 256 ? 4 : 2;
+    const int cap = (a.d <= 256 || wide4) ? 4 : 2;
     while (gc * 2 <= cap && Gl % (gc * 2) == 0 && ac_smem(gc * 2, a.d, rmax) <= kAcMaxSmem) gc *= 2;
   }
   // launch errors surface through cudaGetLastError in the caller
@@ -2007,7 +2012,8 @@ void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s) {
     else launch_ac<4, 2>(a, CL, rmax, s);
   } else {
     if (gc == 1) launch_ac<1, 4>(a, CL, rmax, s);
-    else launch_ac<2, 4>(a, CL, rmax, s);
+    else if (gc == 2) launch_ac<2, 4>(a, CL, rmax, s);
+    else launch_ac<4, 4>(a, CL, rmax, s);
   }
 }
 

@@ -1313,14 +1313,16 @@ static std::vector<int32_t> kv_read(Ctx& c, Seq& q, int l, int head, bool key) {
   const int32_t* base = (key ? q.kc[l] : q.vc[l]) + ((size_t)head * q.cap + st) * lc.head_dim;
   return d2h(c, base, (size_t)rows * lc.head_dim);
 }
-static bool kv_commitment(Ctx& c, Seq& q, std::string* out) {
+// Over the caches of layers [0, nl) (the reference commits the caches built
+// so far: after each prefill layer, and the whole list after prefill/decode).
+static bool kv_commitment(Ctx& c, Seq& q, std::string* out, int nl) {
   const ModelCfg& m = c.cfg;
-  for (int l = 0; l < m.L; ++l)
+  for (int l = 0; l < nl; ++l)
     if (!q.kc[l]) return false;  // a KV-sharing layer has no det cache of its own
   Sha256 h;
   h.put("raster-det-num-kv-cache-v1", 26);
-  h.put_u64((uint64_t)m.L);
-  for (int l = 0; l < m.L; ++l) {
+  h.put_u64((uint64_t)nl);
+  for (int l = 0; l < nl; ++l) {
     const LayerCfg& lc = m.layers[l];
     h.put_u64((uint64_t)lc.kv_heads);
     for (int kind = 0; kind < 2; ++kind) {
@@ -2301,7 +2303,8 @@ int32_t rdet_commitment(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t lay
         break;
       }
       case RDET_BUF_KV:
-        if (!kv_commitment(c, q, &hx)) { none = 1; return; }
+        REQUIRE(layer >= 0 && layer <= c.cfg.L, RDET_E_RANGE, "KV layer count out of range");
+        if (!kv_commitment(c, q, &hx, layer > 0 ? layer : c.cfg.L)) { none = 1; return; }
         break;
       default:
         throw Fail{RDET_E_INVALID, "unknown buffer"};
