@@ -823,7 +823,8 @@ static void prepare_tensor_cores(Ctx& c) {
 constexpr int kTcMinRows = 32;
 struct ActPlanes {
   TcAct a;
-  bool ready = false;
+  bool ready = false;   // a holds the planes of the normalized rows
+  bool normed = false;  // the normalized rows are already in the workspace (w.nrm)
 };
 static void prefill_linear(Ctx& c, const int32_t* X, int S, const DevMat& w, const TcWeight& t, int32_t* Y,
                            int32_t epi, const int32_t* vec, ActPlanes* shared = nullptr) {
@@ -1387,7 +1388,13 @@ static void batch_tables(Ctx& c, Seq* const* seqs, int B) {
   CK(cudaMemcpyAsync(bw.caps, caps.data(), (size_t)rows * 4, cudaMemcpyHostToDevice, c.stream));
 }
 
-static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32_t* cur) {
+// in_planes: the layer input's norm already applied into w.nrm (and its
+// tensor-core planes) by the previous layer's last row kernel when ready.
+// next_gain / next_planes: this layer's last row kernel also writes
+// norm(output) * next_gain into w.nrm and its planes (the next layer's input
+// norm, or the final norm before lm_head), setting next_planes->ready.
+static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32_t* cur, ActPlanes* in_planes,
+                                         const int32_t* next_gain, ActPlanes* next_planes) {
   const ModelCfg& m = c.cfg;
   const LayerDev& L = c.layers[l];
   const LayerCfg& lc = L.cfg;
@@ -1397,7 +1404,9 @@ static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32
   const int H = m.H, d = lc.head_dim;
   int32_t* other = cur == w.xa ? w.xb : w.xa;
   ActPlanes nrm_planes;
-  {
+  if (in_planes && in_planes->ready) {
+    nrm_planes = *in_planes;
+  } else if (!in_planes || !in_planes->normed) {
     RowNormArgs ra;
     ra.a = cur; ra.g1 = L.in_ln; ra.n = H; ra.eps = c.eps; ra.y_out = w.nrm;
     if (!row_norm(c, ra, B, &nrm_planes)) launch_rmsnorm_rows(cur, B, H, L.in_ln, c.eps, w.nrm, s);
@@ -1445,9 +1454,16 @@ static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32
     RowNormArgs ra;
     ra.a = w.attn; ra.res = other; ra.g1 = L.post_ff_ln; ra.n = H; ra.eps = c.eps;
     ra.has_scalar = !ple && L.has_scalar; ra.scalar = L.scalar; ra.t_out = cur;
-    if (!ple) { ra.scatter = bw.dec_out; ra.scatter_off = (size_t)l * H; }
-    if (row_norm(c, ra, B, ple ? &pg_planes : nullptr)) scattered = !ple;
-    else launch_norm_residual_rows(w.attn, other, B, H, L.post_ff_ln, c.eps, !ple && L.has_scalar, L.scalar, cur, s);
+    if (!ple) {
+      ra.scatter = bw.dec_out; ra.scatter_off = (size_t)l * H;
+      if (next_gain) { ra.g2 = next_gain; ra.y_out = w.nrm; }
+    }
+    if (row_norm(c, ra, B, ple ? &pg_planes : (next_gain ? next_planes : nullptr))) {
+      scattered = !ple;
+      if (!ple && next_gain) next_planes->normed = true;
+    } else {
+      launch_norm_residual_rows(w.attn, other, B, H, L.post_ff_ln, c.eps, !ple && L.has_scalar, L.scalar, cur, s);
+    }
   }
   int32_t* result = cur;
   if (ple) {
@@ -1457,8 +1473,13 @@ static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32
     ra.a = w.pr; ra.res = cur; ra.g1 = L.ple_norm; ra.n = H; ra.eps = c.eps;
     ra.has_scalar = L.has_scalar; ra.scalar = L.scalar; ra.t_out = other;
     ra.scatter = bw.dec_out; ra.scatter_off = (size_t)l * H;
-    if (row_norm(c, ra, B, nullptr)) scattered = true;
-    else launch_norm_residual_rows(w.pr, cur, B, H, L.ple_norm, c.eps, L.has_scalar, L.scalar, other, s);
+    if (next_gain) { ra.g2 = next_gain; ra.y_out = w.nrm; }
+    if (row_norm(c, ra, B, next_gain ? next_planes : nullptr)) {
+      scattered = true;
+      if (next_gain) next_planes->normed = true;
+    } else {
+      launch_norm_residual_rows(w.pr, cur, B, H, L.ple_norm, c.eps, L.has_scalar, L.scalar, other, s);
+    }
     result = other;
   }
   if (!scattered) launch_scatter_rows(result, B, H, bw.dec_out, (size_t)l * H, s);
@@ -1691,9 +1712,15 @@ static void decode_batch(Ctx& c, Seq* const* seqs, const uint32_t* tokens, int B
     launch_ple(pa, s);
   }
   int32_t* cur = w.xa;
-  for (int l = 0; l < m.L; ++l) cur = const_cast<int32_t*>(decode_batch_layer(c, B, maxcap, l, cur));
-  launch_rmsnorm_rows(cur, B, m.H, c.final_norm, c.eps, w.nrm, s);
-  prefill_linear(c, w.nrm, B, c.lm_head, c.t_lm_head, bw.logits, kEpiPlain, nullptr);
+  ActPlanes carry;  // the next layer's (or lm_head's) normalized input, made by the previous layer
+  for (int l = 0; l < m.L; ++l) {
+    ActPlanes next;
+    const int32_t* gain = l + 1 < m.L ? c.layers[l + 1].in_ln : c.final_norm;
+    cur = const_cast<int32_t*>(decode_batch_layer(c, B, maxcap, l, cur, &carry, gain, &next));
+    carry = next;
+  }
+  if (!carry.normed) launch_rmsnorm_rows(cur, B, m.H, c.final_norm, c.eps, w.nrm, s);
+  prefill_linear(c, w.nrm, B, c.lm_head, c.t_lm_head, bw.logits, kEpiPlain, nullptr, carry.ready ? &carry : nullptr);
   launch_scatter_rows(bw.logits, B, m.V, bw.logits_dst, 0, s, m.has_softcap ? c.softcap : 0);
   launch_add_i32_rows(bw.pos, B, 1, s);
   CK(cudaGetLastError());
