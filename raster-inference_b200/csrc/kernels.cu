@@ -1142,7 +1142,7 @@ __global__ void qkv_post_kernel(const QkvPostArgs a) {
   const bool rows = a.pos_rows != nullptr;
   const uint32_t pos = rows ? (uint32_t)*a.pos_rows[s] : (uint32_t)(*a.pos + s);
   if (head < a.Hq) {
-    const int32_t* src = a.q_in + ((size_t)s * a.Hq + head) * d;
+    const int32_t* src = a.q_in + (size_t)s * (a.ld ? a.ld : a.Hq * d) + (size_t)head * d;
     for (int i = threadIdx.x; i < d; i += blockDim.x) vs[i] = src[i];
     __syncthreads();
     int32_t sc = block_norm_scale(vs, d, a.eps, red);
@@ -1161,7 +1161,7 @@ __global__ void qkv_post_kernel(const QkvPostArgs a) {
   const int cap = rows ? a.cap_rows[s] : a.cap;
   const int h = head - a.Hq;
   // K: head norm + RoPE
-  const int32_t* ks = a.k_in + ((size_t)s * a.Hkv + h) * d;
+  const int32_t* ks = a.k_in + (size_t)s * (a.ld ? a.ld : a.Hkv * d) + (size_t)h * d;
   for (int i = threadIdx.x; i < d; i += blockDim.x) vs[i] = ks[i];
   __syncthreads();
   int32_t sc = block_norm_scale(vs, d, a.eps, red);
@@ -1173,7 +1173,7 @@ __global__ void qkv_post_kernel(const QkvPostArgs a) {
   for (int i = threadIdx.x; i < d; i += blockDim.x) kd[i] = vs[i];
   __syncthreads();
   // V: weightless value norm of the raw projection
-  const int32_t* vsrc = a.v_in + ((size_t)s * a.Hkv + h) * d;
+  const int32_t* vsrc = a.v_in + (size_t)s * (a.ld ? a.ld : a.Hkv * d) + (size_t)h * d;
   for (int i = threadIdx.x; i < d; i += blockDim.x) vs[i] = vsrc[i];
   __syncthreads();
   int32_t sv = block_norm_scale(vs, d, a.eps, red);

@@ -98,6 +98,11 @@ bool tc_prepare_weight_slice(TcWeight& t, const DevMat& g, const DevMat* u, int 
                              void* mem, cudaStream_t s);
 size_t tc_act_bytes(int S, int K);
 // X [S, K] (16-byte aligned, K % 16 == 0) -> planes in `mem` (tc_act_bytes)
+// Byte planes of n matrices with the same column count in one buffer
+// ([2][sum of rows][K], then the row sums): views[i] covers matrix i alone,
+// whole covers all rows in order (one GEMM producing [S][sum of rows]).
+size_t tc_weight_group_bytes(const DevMat* mats, int n);
+bool tc_prepare_weight_group(TcWeight* views, const DevMat* mats, int n, TcWeight& whole, void* mem, cudaStream_t s);
 bool tc_prepare_act(TcAct& a, const int32_t* X, int S, int K, void* mem, cudaStream_t s);
 // Attaches planes already written at `mem` (layout of tc_prepare_act: [4][S][K]
 // bytes of X + 2^31, then S u64 row sums) and encodes their tensor maps.
@@ -163,6 +168,7 @@ struct QkvPostArgs {
   const int32_t* q_in = nullptr;      // [S, Hq*d]
   const int32_t* k_in = nullptr;      // [S, Hkv*d] raw K (nullptr: no own KV)
   const int32_t* v_in = nullptr;      // [S, Hkv*d] raw V (== k_in for k_eq_v)
+  int32_t ld = 0;                     // row stride of q_in / k_in / v_in in ints (0: Hq*d, Hkv*d)
   const int32_t* q_norm = nullptr;
   const int32_t* k_norm = nullptr;
   int64_t eps = 0;

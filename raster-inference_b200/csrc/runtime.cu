@@ -389,7 +389,7 @@ struct LayerDev {
   int32_t scalar = 0;
   const int64_t* inv_freq = nullptr;
   // tensor-core prefill operands (byte planes), built when eligible
-  TcWeight tq, tk, tv, to, tgu, tdown, tpg, tpp;
+  TcWeight tq, tk, tv, to, tgu, tdown, tpg, tpp, tqkv;
 };
 
 struct PrefillWs {
@@ -790,10 +790,32 @@ static void prepare_tensor_cores(Ctx& c) {
     kmax = std::max(kmax, w.cols);
   };
   for (LayerDev& L : c.layers) {
-    prep(L.tq, L.q);
+    // a layer's own q, k (and v) share one plane buffer: separate views for the
+    // prefill GEMMs, the whole for one batched-decode GEMM
+    bool grouped = false;
     if (L.cfg.donor < 0) {
-      prep(L.tk, L.k);
-      if (L.v.p) prep(L.tv, L.v);
+      DevMat mats[3] = {L.q, L.k, L.v};
+      const int n = L.v.p ? 3 : 2;
+      bool ok = true;
+      for (int i = 0; i < n; ++i) ok = ok && mats[i].p && tc_weight_eligible(mats[i]) && mats[i].cols == L.q.cols;
+      if (ok) {
+        TcWeight views[3];
+        void* mem = c.dalloc(tc_weight_group_bytes(mats, n));
+        REQUIRE(tc_prepare_weight_group(views, mats, n, L.tqkv, mem, c.stream), RDET_E_CUDA,
+                "tensor map encoding failed");
+        L.tq = views[0];
+        L.tk = views[1];
+        if (n == 3) L.tv = views[2];
+        kmax = std::max(kmax, L.q.cols);
+        grouped = true;
+      }
+    }
+    if (!grouped) {
+      prep(L.tq, L.q);
+      if (L.cfg.donor < 0) {
+        prep(L.tk, L.k);
+        if (L.v.p) prep(L.tv, L.v);
+      }
     }
     prep(L.to, L.o);
     prep(L.tgu, L.gate, &L.up);
@@ -1411,18 +1433,37 @@ static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32
     ra.a = cur; ra.g1 = L.in_ln; ra.n = H; ra.eps = c.eps; ra.y_out = w.nrm;
     if (!row_norm(c, ra, B, &nrm_planes)) launch_rmsnorm_rows(cur, B, H, L.in_ln, c.eps, w.nrm, s);
   }
-  prefill_linear(c, w.nrm, B, L.q, L.tq, w.q, kEpiPlain, nullptr, &nrm_planes);
   QkvPostArgs qa;
   qa.S = B; qa.Hq = m.Hq; qa.Hkv = lc.kv_heads; qa.d = d; qa.rotary = lc.rotary; qa.inv_freq = L.inv_freq;
-  qa.q_in = w.q; qa.q_norm = L.q_norm; qa.k_norm = L.k_norm; qa.eps = c.eps; qa.q_out = w.qo;
+  qa.q_norm = L.q_norm; qa.k_norm = L.k_norm; qa.eps = c.eps; qa.q_out = w.qo;
   qa.pos_rows = bw.pos; qa.cap_rows = bw.caps;
-  if (lc.donor < 0) {
-    prefill_linear(c, w.nrm, B, L.k, L.tk, w.kraw, kEpiPlain, nullptr, &nrm_planes);
-    const int32_t* vsrc = w.kraw;  // k_eq_v: V is the raw K projection
-    if (L.v.p) { prefill_linear(c, w.nrm, B, L.v, L.tv, w.vraw, kEpiPlain, nullptr, &nrm_planes); vsrc = w.vraw; }
-    qa.k_in = w.kraw; qa.v_in = vsrc;
+  // one tensor-core GEMM for q, k and v when their planes share a buffer
+  // (rows [q | k | v] of w.hbuf, which the MLP overwrites later)
+  const int nqkv = L.tqkv.nrows;
+  if (lc.donor < 0 && nqkv > 0 && nrm_planes.ready && (size_t)nqkv <= (size_t)L.F) {
+    TcOut o;
+    o.y = w.hbuf;
+    o.epi = kEpiPlain;
+    o.scratch = c.tc_split;
+    o.scratch_bytes = c.tc_split_bytes;
+    launch_tc_linear(nrm_planes.a, L.tqkv, o, s);
+    qa.ld = nqkv;
+    qa.q_in = w.hbuf;
+    qa.k_in = w.hbuf + L.q.rows;
+    qa.v_in = L.v.p ? w.hbuf + L.q.rows + L.k.rows : qa.k_in;  // k_eq_v: V is the raw K projection
     qa.kc_rows = bw.kc + (size_t)l * bw.rows;
     qa.vc_rows = bw.vc + (size_t)l * bw.rows;
+  } else {
+    prefill_linear(c, w.nrm, B, L.q, L.tq, w.q, kEpiPlain, nullptr, &nrm_planes);
+    qa.q_in = w.q;
+    if (lc.donor < 0) {
+      prefill_linear(c, w.nrm, B, L.k, L.tk, w.kraw, kEpiPlain, nullptr, &nrm_planes);
+      const int32_t* vsrc = w.kraw;  // k_eq_v: V is the raw K projection
+      if (L.v.p) { prefill_linear(c, w.nrm, B, L.v, L.tv, w.vraw, kEpiPlain, nullptr, &nrm_planes); vsrc = w.vraw; }
+      qa.k_in = w.kraw; qa.v_in = vsrc;
+      qa.kc_rows = bw.kc + (size_t)l * bw.rows;
+      qa.vc_rows = bw.vc + (size_t)l * bw.rows;
+    }
   }
   launch_qkv_post(qa, s);
   AttnDecodeArgs aa;

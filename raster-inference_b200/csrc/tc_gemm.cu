@@ -165,7 +165,7 @@ __global__ void tc_act_prep_kernel(const int32_t* __restrict__ X, int S, int K, 
 // A slice takes source rows [row0, row0 + rows) and columns [col0, col0 + K)
 // of a matrix with row stride ld.
 __global__ void tc_weight_prep_kernel(const int16_t* __restrict__ W, const int16_t* __restrict__ U, int rows,
-                                      int K, int nrows, uint8_t* __restrict__ planes, uint64_t* __restrict__ rowsum,
+                                      int K, size_t plane, uint8_t* __restrict__ planes, uint64_t* __restrict__ rowsum,
                                       int row0, int col0, int ld) {
   const int R = blockIdx.x;
   const int16_t* src = nullptr;
@@ -176,7 +176,6 @@ __global__ void tc_weight_prep_kernel(const int16_t* __restrict__ W, const int16
     const int r = b * h + (j < h ? j : j - h);
     if (r < rows) src = (j < h ? W : U) + (size_t)(row0 + r) * ld + col0;
   }
-  const size_t plane = (size_t)nrows * K;
   uint64_t sum = 0;
   for (int c = threadIdx.x; c < K / 8; c += blockDim.x) {
     uint16_t u[8];
@@ -661,12 +660,14 @@ EncodeTiledFn encode_fn() {
 }
 
 // u8 planes [planes][rows][K] -> 3D map (K, rows, planes), box (64, box_rows, 1)
-bool encode_planes(void* out, const uint8_t* base, int nplanes, int rows, int K, int box_rows) {
+// plane_stride: bytes from one plane to the next (0: rows * K, planes back to back)
+bool encode_planes(void* out, const uint8_t* base, int nplanes, int rows, int K, int box_rows,
+                   size_t plane_stride = 0) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   CUtensorMap* map = reinterpret_cast<CUtensorMap*>(out);
   const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)nplanes};
-  const cuuint64_t strides[2] = {(cuuint64_t)K, (cuuint64_t)rows * (cuuint64_t)K};
+  const cuuint64_t strides[2] = {(cuuint64_t)K, plane_stride ? (cuuint64_t)plane_stride : (cuuint64_t)rows * (cuuint64_t)K};
   const cuuint32_t box[3] = {(cuuint32_t)kTcKB, (cuuint32_t)box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, estr,
@@ -753,9 +754,46 @@ bool tc_prepare_weight_slice(TcWeight& t, const DevMat& g, const DevMat* u, int 
   t.rowsum = reinterpret_cast<uint64_t*>(t.planes + 2 * (size_t)t.nrows * t.K);
   tc_weight_prep_kernel<<<t.nrows, 128, 0, s>>>(static_cast<const int16_t*>(g.p),
                                                 pair ? static_cast<const int16_t*>(u->p) : nullptr, rows, cols,
-                                                t.nrows, t.planes, t.rowsum, row0, col0, g.cols);
+                                                (size_t)t.nrows * cols, t.planes, t.rowsum, row0, col0, g.cols);
   return encode_planes(t.map, t.planes, 2, t.nrows, t.K, kTcN) &&
          encode_planes(t.map_m, t.planes, 2, t.nrows, t.K, kTsM);
+}
+
+size_t tc_weight_group_bytes(const DevMat* mats, int n) {
+  size_t rows = 0;
+  for (int i = 0; i < n; ++i) rows += (size_t)mats[i].rows;
+  return 2 * rows * mats[0].cols + rows * 8;
+}
+
+bool tc_prepare_weight_group(TcWeight* views, const DevMat* mats, int n, TcWeight& whole, void* mem,
+                             cudaStream_t s) {
+  const int K = mats[0].cols;
+  int total = 0;
+  for (int i = 0; i < n; ++i) total += mats[i].rows;
+  uint8_t* base = static_cast<uint8_t*>(mem);
+  uint64_t* rowsum = reinterpret_cast<uint64_t*>(base + 2 * (size_t)total * K);
+  const size_t plane = (size_t)total * K;
+  bool ok = true;
+  int off = 0;
+  for (int i = 0; i < n; ++i) {
+    TcWeight& t = views[i];
+    t.N = t.nrows = mats[i].rows;
+    t.K = K;
+    t.pair = false;
+    t.planes = base + (size_t)off * K;
+    t.rowsum = rowsum + off;
+    tc_weight_prep_kernel<<<t.nrows, 128, 0, s>>>(static_cast<const int16_t*>(mats[i].p), nullptr, t.nrows, K, plane,
+                                                  t.planes, t.rowsum, 0, 0, K);
+    ok = ok && encode_planes(t.map, t.planes, 2, t.nrows, K, kTcN, plane) &&
+         encode_planes(t.map_m, t.planes, 2, t.nrows, K, kTsM, plane);
+    off += mats[i].rows;
+  }
+  whole.N = whole.nrows = total;
+  whole.K = K;
+  whole.pair = false;
+  whole.planes = base;
+  whole.rowsum = rowsum;
+  return ok && encode_planes(whole.map, base, 2, total, K, kTcN) && encode_planes(whole.map_m, base, 2, total, K, kTsM);
 }
 
 size_t tc_act_bytes(int S, int K) { return 4 * (size_t)S * K + (size_t)S * 8; }
