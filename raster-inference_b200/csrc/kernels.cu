@@ -1405,6 +1405,7 @@ constexpr int kAcThreads = 256;
 constexpr int kAcWarps = kAcThreads / 32;
 constexpr int kAcTileBytes = 32 * 1024;
 constexpr int kAcStages = 4;
+constexpr int kAcVmx = 256;  // output dims one CTA finalises at most (first-max V row staging)
 
 // acc + k . q over one 16-byte chunk (wrapping)
 __device__ __forceinline__ int64_t dot4_acc(int64_t acc, const int4& k, const int4& q) {
@@ -1494,7 +1495,7 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
   __shared__ int32_t wm[kAcWarps][GC], wi[kAcWarps][GC];
   __shared__ int64_t ws[kAcWarps][GC];
   __shared__ int32_t cs_tab[256], sn_tab[256];
-  __shared__ int32_t vmx[GC][128];  // first-max V row, this CTA's output dims
+  __shared__ int32_t vmx[GC][kAcVmx];  // first-max V row, this CTA's output dims
   __shared__ int s_fail;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const AttnFuse& f = a.fuse;
@@ -1961,7 +1962,7 @@ bool attn_decode_cluster_fits(int Hq, int Hkv, int d, int window, int cap, int r
   const int gl = std::max(1, std::min(group, Hq));
   if (Hq % gl != 0) return false;
   const int gc = ac_group(Hq, Hq / gl, d);
-  return gc <= 8 - 2 && d <= 128 * CL && ac_smem(gc, d, ac_rmax(window, cap, CL)) <= kAcMaxSmem;
+  return gc <= 8 - 2 && d <= kAcVmx * CL && ac_smem(gc, d, ac_rmax(window, cap, CL)) <= kAcMaxSmem;
 }
 
 // Cluster size of batched launches: the batch rows already fill the GPU, so
@@ -1976,12 +1977,15 @@ void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s) {
   // KV head fit one cluster (K/V read once); else the smallest cluster
   const int Gq = a.group ? a.group : a.Hq / a.Hkv;
   const bool wide4 = a.batch > 1 && a.d > 256 && Gq % 4 == 0 && CL >= 8 &&
-                     ac_smem(4, a.d, ac_rmax(a.window, a.cap, 8)) <= kAcMaxSmem && a.d <= 128 * 8;
+                     ac_smem(4, a.d, ac_rmax(a.window, a.cap, 8)) <= kAcMaxSmem && a.d <= kAcVmx * 8;
   if (a.batch > 1) {
-    // a CTA finalises d / CL output dims (at most 128: the first-max V row
-    // is staged in a [GC][128] shared array)
-    int cl = wide4 ? 8 : RDET_AC_BATCH_CL;
-    while (cl < CL && (a.d > 128 * cl || ac_smem(1, a.d, ac_rmax(a.window, a.cap, cl)) > kAcMaxSmem)) cl *= 2;
+    // a CTA finalises d / CL output dims (at most kAcVmx: the first-max V
+    // row is staged in a [GC][kAcVmx] shared array).  One CTA per
+    // (sequence, query group) when those CTAs fit one wave: a second,
+    // partly filled wave of half-size CTAs costs more than longer CTAs.
+    const int groups = a.Hq / std::max(1, std::min(4, Gq));
+    int cl = wide4 ? 8 : ((long)a.batch * groups <= sm_count() ? 1 : RDET_AC_BATCH_CL);
+    while (cl < CL && (a.d > kAcVmx * cl || ac_smem(1, a.d, ac_rmax(a.window, a.cap, cl)) > kAcMaxSmem)) cl *= 2;
     CL = cl < CL ? cl : CL;
   }
   const int rmax = ac_rmax(a.window, a.cap, CL);
