@@ -1885,7 +1885,9 @@ static cudaError_t launch_ac(const AttnDecodeArgs& a, int CL, int rmax, cudaStre
   return cudaLaunchKernelEx(&cfg, attn_dec_cluster_kernel<GC, NCH>, a, rmax);
 }
 
-constexpr size_t kAcMaxSmem = 200 * 1024;
+// dynamic shared memory cap: 227 KB per block minus the kernel's static
+// shared memory (under 7 KB)
+constexpr size_t kAcMaxSmem = 219 * 1024;
 
 template <int GC, int NCH>
 static void ac_prepare1(int CL) {
@@ -1984,7 +1986,8 @@ void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s) {
     // (sequence, query group) when those CTAs fit one wave: a second,
     // partly filled wave of half-size CTAs costs more than longer CTAs.
     const int groups = a.Hq / std::max(1, std::min(4, Gq));
-    int cl = wide4 ? 8 : ((long)a.batch * groups <= sm_count() ? 1 : RDET_AC_BATCH_CL);
+    int cl = wide4 ? (ac_smem(4, a.d, ac_rmax(a.window, a.cap, 4)) <= kAcMaxSmem ? 4 : 8)
+                   : ((long)a.batch * groups <= sm_count() ? 1 : RDET_AC_BATCH_CL);
     while (cl < CL && (a.d > kAcVmx * cl || ac_smem(1, a.d, ac_rmax(a.window, a.cap, cl)) > kAcMaxSmem)) cl *= 2;
     CL = cl < CL ? cl : CL;
   }
