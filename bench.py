@@ -339,18 +339,22 @@ def run_ours(args, rank, world, local_rank):
            "steps": n_e2e}
     # prefill of one seeded uniform prompt of 512 and of
     # 2048 tokens through all layers (device-timed, kernels already warm)
+    # (median of three prefills of the same prompt, each on a fresh sequence)
     prefill_lengths = {}
     for plen in (512, 2048):
-        ps = model.new_sequence(plen + 8)
         pids = lcg_ids(plen, t["vocab_size"], SEED + 11 + plen)
-        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        p0.record(stream)
-        ps.prefill(pids)
-        p1.record(stream)
-        torch.cuda.synchronize()
-        psec = p0.elapsed_time(p1) / 1000
-        prefill_lengths[str(plen)] = {"tok_s": plen / psec, "seconds": psec}
-        ps.free()
+        runs = []
+        for _ in range(3):
+            ps = model.new_sequence(plen + 8)
+            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            p0.record(stream)
+            ps.prefill(pids)
+            p1.record(stream)
+            torch.cuda.synchronize()
+            runs.append(p0.elapsed_time(p1) / 1000)
+            ps.free()
+        psec = statistics.median(runs)
+        prefill_lengths[str(plen)] = {"tok_s": plen / psec, "seconds": psec, "runs": 3}
     # batched ragged decode (BASELINE config 5 shape): 64 sequences, prompt
     # lengths 128 + draw % 3969 (seeded), one batched decode_transition per step
     batched = None

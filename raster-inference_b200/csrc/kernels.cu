@@ -2218,7 +2218,92 @@ __global__ void __launch_bounds__(256) attn_prefill_tiled(const AttnPrefillArgs 
   // ---- phase C: out = requantize(sum_j w_j v_j), 128 output dims at a time
   const int rg = warp, dg = lane;
   const int cw = d < AP_CH ? d : AP_CH, cwp = cw + 4;
-  for (int c0 = 0; c0 < d; c0 += AP_CH) {
+  // Double-buffered form: the Q tile region is free after phase A, so V and
+  // weight tiles t + 1 load (cp.async, zero-filled outside the key range and
+  // window) while tile t is multiplied.  Used when two buffers fit the
+  // block's shared memory (every head_dim >= 64).
+  const int vbuf = AP_TK * cwp + AP_R * AP_TK;  // ints per buffer: V tile, then weights
+  const bool dbl = 2 * vbuf <= AP_R * dp + AP_TK * dp + AP_R * AP_TK;
+  const int nkt = (khi - klo + AP_TK - 1) / AP_TK;
+  for (int c0 = 0; dbl && c0 < d; c0 += AP_CH) {
+    int64_t acc[8][4];
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[t][u] = 0;
+    auto issue = [&](int t) {
+      int32_t* Vb = Qs + (t & 1) * vbuf;
+      int32_t* Wb = Vb + AP_TK * cwp;
+      const int kt = klo + t * AP_TK;
+      for (int e = threadIdx.x; e < AP_TK * (cw / 4); e += blockDim.x) {
+        const int jj = e / (cw / 4), c = e % (cw / 4), j = kt + jj;
+        const int32_t* src = a.v_cache + ((size_t)kvh * a.cap + (j < khi ? j : klo)) * d + c0 + 4 * c;
+        const unsigned sa = (unsigned)__cvta_generic_to_shared(Vb + jj * cwp + 4 * c);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa), "l"(src), "r"(j < khi ? 16 : 0)
+                     : "memory");
+      }
+      for (int e = threadIdx.x; e < AP_R * AP_TK; e += blockDim.x) {
+        const int r = e / AP_TK, jj = e % AP_TK, j = kt + jj;
+        const int32_t* src = a.scores;
+        int bytes = 0;
+        if (r < R) {
+          const int i = row_query(r);
+          if (i < a.S) {
+            const int st = win_start(i);
+            if (j >= st && j <= i) {
+              src = a.scores + ((size_t)row_head(r) * a.S + i) * rowlen + (j - st);
+              bytes = 4;
+            }
+          }
+        }
+        const unsigned sa = (unsigned)__cvta_generic_to_shared(Wb + r * AP_TK + jj);
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(sa), "l"(src), "r"(bytes) : "memory");
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    __syncthreads();  // the region's previous users (phase A, the last chunk) are done
+    if (nkt > 0) issue(0);
+    for (int t = 0; t < nkt; ++t) {
+      if (t + 1 < nkt) {
+        issue(t + 1);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+      }
+      __syncthreads();
+      const int32_t* Vb = Qs + (t & 1) * vbuf;
+      const int32_t* Wb = Vb + AP_TK * cwp;
+      if (dg * 4 < cw) {
+        for (int jj = 0; jj < AP_TK; ++jj) {
+          const int4 v = reinterpret_cast<const int4*>(Vb + jj * cwp)[dg];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int32_t w = Wb[(rg * 8 + q) * AP_TK + jj];
+            acc[q][0] = mac_wide(acc[q][0], w, v.x);
+            acc[q][1] = mac_wide(acc[q][1], w, v.y);
+            acc[q][2] = mac_wide(acc[q][2], w, v.z);
+            acc[q][3] = mac_wide(acc[q][3], w, v.w);
+          }
+        }
+      }
+      __syncthreads();  // buffer t & 1 is refilled by issue(t + 2)
+    }
+    if (dg * 4 < cw) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int r = rg * 8 + q;
+        if (r >= R) continue;
+        const int i = row_query(r);
+        if (i >= a.S) continue;
+        int32_t* o = a.out + ((size_t)i * a.Hq + row_head(r)) * d + c0 + dg * 4;
+        o[0] = requantize(acc[q][0]);
+        o[1] = requantize(acc[q][1]);
+        o[2] = requantize(acc[q][2]);
+        o[3] = requantize(acc[q][3]);
+      }
+    }
+  }
+  for (int c0 = 0; !dbl && c0 < d; c0 += AP_CH) {
     int64_t acc[8][4];
 #pragma unroll
     for (int t = 0; t < 8; ++t)
