@@ -23,6 +23,7 @@ number through the C ABI with host buffers, and the CPU baseline (the C++
 restatement of the reference det path on the host cores, a bounded sample).
 """
 import argparse
+import hashlib
 import importlib
 import json
 import os
@@ -450,6 +451,67 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def run_trace_case(args):
+    """Cost of a checkpoint-traced run at E4B shape: the det trace of a
+    --ctx-token prompt and 2 greedy tokens (every committed checkpoint from
+    input.embedding to decode.transition_finalize, per-layer prefill
+    commitments and the KV-prefix commitments included), wall-clock through
+    the C ABI, beside the same prefill and decode without commitments."""
+    import torch
+    rdet = importlib.import_module("raster-inference_b200")
+    trace = importlib.import_module("raster-inference_b200.trace")
+    cfg = load_config()
+    t = cfg["text_config"]
+    ctx = args.ctx
+    ids = lcg_ids(ctx, t["vocab_size"], SEED)
+    out = {"case": "checkpoint trace", "prompt_tokens": ctx, "new_tokens": 2}
+    for flag in (False, True):
+        model = rdet.Model.synthetic(cfg, SEED, width=16, device=0, max_prefill=ctx, layer_commitments=flag)
+        for rep in range(2):  # the first pass warms kernels, staging and workers
+            seq = model.new_sequence(ctx + 8)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            if flag:
+                spent = {}
+                backend = trace.SeqBackend(seq)
+
+                def timed(name, fn):
+                    def call(*a):
+                        c0 = time.perf_counter()
+                        r = fn(*a)
+                        spent[name] = spent.get(name, 0.0) + time.perf_counter() - c0
+                        return r
+                    return call
+
+                for name in ("prefill", "select", "decode", "embedding_commitment", "hidden_commitment",
+                             "logits_commitment", "layer_output_commitment", "kv_commitment",
+                             "kv_prefix_commitments"):
+                    setattr(backend, name, timed(name, getattr(backend, name)))
+                tr, gen = trace.run(backend, ids, num_layers=model.L, max_new_tokens=2)
+            else:
+                seq.prefill(ids)
+                gen = seq.generate(2)
+            torch.cuda.synchronize()
+            sec = time.perf_counter() - t0
+            seq.free()
+        key = "traced" if flag else "plain"
+        out[key] = {"seconds": sec, "generated": gen}
+        if flag:
+            out[key]["entries"] = len(tr.entries)
+            out[key]["entries_sha256"] = hashlib.sha256(json.dumps(tr.entries).encode()).hexdigest()
+            out[key]["seconds_by_call"] = {k: round(v, 4) for k, v in spent.items()}
+        model.close()
+    out["overhead_seconds"] = out["traced"]["seconds"] - out["plain"]["seconds"]
+    try:
+        with open("/proc/cpuinfo") as f:
+            sha_ext = " sha_ni" in f.read()
+    except OSError:
+        sha_ext = False
+    out["sha256_impl"] = "x86 SHA extensions" if sha_ext else "scalar"
+    out["host"] = cpu_model()
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -462,7 +524,12 @@ def main():
     ap.add_argument("--batch-steps", type=int, default=8)
     ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc"],
                     help="run a few launches of one kernel at E4B shapes for an ncu capture, then exit")
+    ap.add_argument("--trace-case", action="store_true",
+                    help="time a checkpoint-traced run (commitments on) against a plain one at --ctx, then exit")
     args = ap.parse_args()
+    if args.trace_case:
+        run_trace_case(args)
+        return
     if args.kernel_case:
         run_kernel_case(args)
         return

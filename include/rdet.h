@@ -128,6 +128,13 @@ int32_t rdet_generate(rdet_ctx* ctx, rdet_seq* seq, uint32_t n_tokens, uint32_t*
 int32_t rdet_read(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t layer, int32_t arg, void* dst, size_t bytes,
                   size_t* size_out);
 int32_t rdet_commitment(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t layer, char* hex_out);
+/* The KV commitments of the layer prefixes [0, p) for p = 1..n at once: what
+ * n calls rdet_commitment(RDET_BUF_KV, p) return, i.e. det_layer_caches_sha256
+ * of prefill.range_finalize after each layer (prefill_range_finalize/mod.rs:
+ * 38-72 in the reference).  The caches download once and the n independent
+ * hashes run on host threads.  hex_out holds n * 65 bytes; entry p-1 is the
+ * hex + NUL, or an empty string where that prefix is RDET_NONE.  n <= layers. */
+int32_t rdet_kv_prefix_commitments(rdet_ctx* ctx, rdet_seq* seq, uint32_t n, char* hex_out);
 
 /* ---- kernel-level entry points on caller-owned device memory -----------------
  * det GEMV / linear: y[s, r] = requantize(sum_k x[s, k] * w[r, k]) with exact

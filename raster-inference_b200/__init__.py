@@ -36,7 +36,8 @@ SYMBOLS = [
     "rdet_open", "rdet_open_synthetic", "rdet_close", "rdet_get_model_info", "rdet_seq_new", "rdet_seq_free",
     "rdet_seq_position", "rdet_embed", "rdet_prefill", "rdet_prefill_begin", "rdet_prefill_range",
     "rdet_prefill_finalize", "rdet_select", "rdet_decode", "rdet_decode_begin", "rdet_decode_range",
-    "rdet_decode_finalize", "rdet_generate", "rdet_read", "rdet_commitment", "rdet_det_gemv", "rdet_det_linear",
+    "rdet_decode_finalize", "rdet_generate", "rdet_read", "rdet_commitment", "rdet_kv_prefix_commitments",
+    "rdet_det_gemv", "rdet_det_linear",
     "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_get_stream", "rdet_tensor_core_prefill", "rdet_nccl_unique_id", "rdet_tp_init", "rdet_tp_world", "rdet_seq_kernels_per_step", "rdet_last_error",
     "rdet_version",
 ]
@@ -92,6 +93,7 @@ def lib() -> C.CDLL:
         "rdet_generate": [p, p, u32, p],
         "rdet_read": [p, p, i32, i32, i32, p, sz, p],
         "rdet_commitment": [p, p, i32, i32, C.c_char_p],
+        "rdet_kv_prefix_commitments": [p, p, C.c_uint32, C.c_char_p],
         "rdet_det_gemv": [p, p, i32, u32, u32, p, p],
         "rdet_det_linear": [p, u32, p, i32, u32, u32, p, p],
         "rdet_det_attention_decode": [p, p, p, u32, u32, u32, u32, u32, u32, p, p],
@@ -284,6 +286,17 @@ class Sequence:
         buf = C.create_string_buffer(65)
         rc = _check(lib().rdet_commitment(self.model._h, self._h, which, layer, buf))
         return None if rc == RDET_NONE else buf.value.decode()
+
+    def kv_prefix_commitments(self, n: int) -> list:
+        """commitment(BUF_KV, p) for p = 1..n in one call (None where a
+        prefix holds a KV-sharing layer)."""
+        buf = C.create_string_buffer(65 * max(n, 1))
+        _check(lib().rdet_kv_prefix_commitments(self.model._h, self._h, n, buf))
+        out = []
+        for p in range(n):
+            h = buf.raw[65 * p:65 * p + 64]
+            out.append(None if h[0] == 0 else h.decode())
+        return out
 
     def logits(self) -> np.ndarray:
         return self.read(BUF_LOGITS)

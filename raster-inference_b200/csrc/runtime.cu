@@ -8,14 +8,19 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
+#include <condition_variable>
 #include <cstdio>
 #include <cstring>
+#include <deque>
+#include <functional>
 #include <map>
 #include <memory>
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include <nccl.h>  // types only: libnccl is loaded at run time
@@ -462,6 +467,38 @@ struct TpState {
 
 struct Seq;
 
+// Per-layer prefill commitments off the critical path.  Each layer's output
+// is copied into a device slab on the compute stream (device to device, so
+// the next layers may overwrite their buffers at once), downloaded into a
+// pinned host slab on a copy stream, and hashed by a host worker while the
+// GPU runs the following layers.  A slab is reused only after its hash is
+// done, which also means its download has finished.
+struct CommitPipe {
+  int nslots = 0;
+  size_t slot_elems = 0;
+  int32_t* dslab = nullptr;  // [nslots, slot_elems] (Ctx::dalloc)
+  int32_t* hslab = nullptr;  // pinned, same shape
+  cudaStream_t copy = nullptr;
+  std::vector<cudaEvent_t> staged, copied;
+  std::vector<char> busy;    // slot's hash not finished
+  int next = 0;
+  std::mutex mu;
+  std::condition_variable cv;
+  std::deque<std::function<void()>> jobs;
+  int pending = 0;           // submitted and not finished
+  std::string error;
+  bool stop = false;
+  std::vector<std::thread> workers;
+};
+
+// Reusable pinned staging for the KV-cache commitment (two halves: one being
+// downloaded while the other is hashed).
+struct KvStage {
+  int32_t* host = nullptr;
+  size_t half_elems = 0;
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+};
+
 struct Ctx {
   int device = 0;
   cudaStream_t stream = nullptr;
@@ -502,6 +539,8 @@ struct Ctx {
     int32_t* logits = nullptr;     // [rows, V]
   } bw;
   TpState tp;
+  CommitPipe cp;
+  KvStage kvs;
 
   void* dalloc(size_t bytes) {
     void* p = nullptr;
@@ -515,6 +554,20 @@ struct Ctx {
   ~Ctx() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
+    {
+      std::unique_lock<std::mutex> lk(cp.mu);
+      cp.cv.wait(lk, [&] { return cp.pending == 0; });
+      cp.stop = true;
+    }
+    cp.cv.notify_all();
+    for (auto& t : cp.workers) t.join();
+    for (cudaEvent_t e : cp.staged) cudaEventDestroy(e);
+    for (cudaEvent_t e : cp.copied) cudaEventDestroy(e);
+    if (cp.copy) cudaStreamDestroy(cp.copy);
+    if (cp.hslab) cudaFreeHost(cp.hslab);
+    for (cudaEvent_t e : kvs.ev)
+      if (e) cudaEventDestroy(e);
+    if (kvs.host) cudaFreeHost(kvs.host);
     if (tp.comm) nccl_api().commDestroy(tp.comm);
     for (void* p : allocs) cudaFree(p);
     if (stream) cudaStreamDestroy(stream);
@@ -977,6 +1030,107 @@ static std::string act_hash_rows(const int32_t* host, size_t rows, size_t cols) 
   return h.hex();
 }
 
+static void commit_pipe_start(Ctx& c) {
+  CommitPipe& p = c.cp;
+  if (p.nslots) return;
+  const unsigned hw = std::thread::hardware_concurrency();
+  const int workers = std::max(1, std::min(6, (int)(hw > 2 ? hw - 2 : 1)));
+  const int nslots = workers + 2;
+  p.slot_elems = (size_t)c.max_prefill * c.cfg.H;
+  p.dslab = c.dalloc_n<int32_t>(p.slot_elems * nslots);
+  void* h = nullptr;
+  if (cudaHostAlloc(&h, p.slot_elems * nslots * 4, cudaHostAllocDefault) != cudaSuccess)
+    throw Fail{RDET_E_OOM, "pinned staging for the layer commitments could not be allocated"};
+  p.hslab = static_cast<int32_t*>(h);
+  CK(cudaStreamCreateWithFlags(&p.copy, cudaStreamNonBlocking));
+  p.staged.assign(nslots, nullptr);
+  p.copied.assign(nslots, nullptr);
+  for (int k = 0; k < nslots; ++k) {
+    CK(cudaEventCreateWithFlags(&p.staged[k], cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&p.copied[k], cudaEventDisableTiming));
+  }
+  p.busy.assign(nslots, 0);
+  p.nslots = nslots;
+  const int dev = c.device;
+  for (int i = 0; i < workers; ++i)
+    p.workers.emplace_back([&p, dev] {
+      cudaSetDevice(dev);
+      for (;;) {
+        std::function<void()> job;
+        {
+          std::unique_lock<std::mutex> lk(p.mu);
+          p.cv.wait(lk, [&] { return p.stop || !p.jobs.empty(); });
+          if (p.jobs.empty()) return;
+          job = std::move(p.jobs.front());
+          p.jobs.pop_front();
+        }
+        job();
+      }
+    });
+}
+
+// Stages layer output `src` ([rows, H]) and queues its hash into *dst.
+static void commit_layer_async(Ctx& c, const int32_t* src, int rows, std::string* dst) {
+  commit_pipe_start(c);
+  CommitPipe& p = c.cp;
+  const int k = p.next;
+  p.next = (k + 1) % p.nslots;
+  {
+    std::unique_lock<std::mutex> lk(p.mu);
+    p.cv.wait(lk, [&] { return !p.busy[k]; });
+    p.busy[k] = 1;
+    ++p.pending;
+  }
+  const size_t cols = c.cfg.H, n = (size_t)rows * cols;
+  int32_t* ds = p.dslab + k * p.slot_elems;
+  int32_t* hs = p.hslab + k * p.slot_elems;
+  try {
+    CK(cudaMemcpyAsync(ds, src, n * 4, cudaMemcpyDeviceToDevice, c.stream));
+    CK(cudaEventRecord(p.staged[k], c.stream));
+    CK(cudaStreamWaitEvent(p.copy, p.staged[k], 0));
+    CK(cudaMemcpyAsync(hs, ds, n * 4, cudaMemcpyDeviceToHost, p.copy));
+    CK(cudaEventRecord(p.copied[k], p.copy));
+  } catch (...) {
+    {
+      std::lock_guard<std::mutex> lk(p.mu);
+      p.busy[k] = 0;
+      --p.pending;
+    }
+    p.cv.notify_all();
+    throw;
+  }
+  cudaEvent_t ev = p.copied[k];
+  {
+    std::lock_guard<std::mutex> lk(p.mu);
+    p.jobs.emplace_back([&p, k, ev, hs, rows, cols, dst] {
+      cudaError_t e = cudaEventSynchronize(ev);
+      std::string hx;
+      if (e == cudaSuccess) hx = act_hash_rows(hs, rows, cols);
+      {
+        std::lock_guard<std::mutex> lk2(p.mu);
+        if (e == cudaSuccess) *dst = hx;
+        else if (p.error.empty()) p.error = std::string("layer commitment download: ") + cudaGetErrorString(e);
+        p.busy[k] = 0;
+        --p.pending;
+      }
+      p.cv.notify_all();
+    });
+  }
+  p.cv.notify_all();
+}
+
+// Waits for every queued layer hash; reports the first failure when `report`.
+static void commit_join(Ctx& c, bool report) {
+  CommitPipe& p = c.cp;
+  std::string err;
+  {
+    std::unique_lock<std::mutex> lk(p.mu);
+    p.cv.wait(lk, [&] { return p.pending == 0; });
+    err.swap(p.error);
+  }
+  if (report && !err.empty()) throw Fail{RDET_E_CUDA, err};
+}
+
 static void prefill_layer(Ctx& c, Seq& q, int l) {
   const ModelCfg& m = c.cfg;
   const LayerDev& L = c.layers[l];
@@ -1031,12 +1185,7 @@ static void prefill_layer(Ctx& c, Seq& q, int l) {
   }
   CK(cudaGetLastError());
   q.prefill_cur = result;
-  if (c.flags & RDET_FLAG_LAYER_COMMITMENTS) {
-    std::vector<int32_t> host((size_t)S * H);
-    CK(cudaMemcpyAsync(host.data(), result, host.size() * 4, cudaMemcpyDeviceToHost, s));
-    CK(cudaStreamSynchronize(s));
-    q.layer_hashes[l] = act_hash_rows(host.data(), S, H);
-  }
+  if (c.flags & RDET_FLAG_LAYER_COMMITMENTS) commit_layer_async(c, result, S, &q.layer_hashes[l]);
 }
 
 static void gemv_logits(Ctx& c, const int32_t* hidden_row, int32_t* logits, cudaStream_t s) {
@@ -1338,29 +1487,144 @@ static std::vector<int32_t> kv_read(Ctx& c, Seq& q, int l, int head, bool key) {
 }
 // Over the caches of layers [0, nl) (the reference commits the caches built
 // so far: after each prefill layer, and the whole list after prefill/decode).
+// Hashes layer l's K then V cache in the commitment's byte order from host
+// memory holding, per kind, every head's live rows back to back ([Hkv, rows,
+// d], what kv_download writes).
+static void kv_hash_layer(Sha256& h, const LayerCfg& lc, int rows, const int32_t* k, const int32_t* v) {
+  h.put_u64((uint64_t)lc.kv_heads);
+  for (int kind = 0; kind < 2; ++kind) {
+    h.put(kind == 0 ? "k" : "v", 1);
+    h.put_u64((uint64_t)lc.kv_heads);
+    const int32_t* base = kind == 0 ? k : v;
+    for (int hd = 0; hd < lc.kv_heads; ++hd) {
+      h.put_u64((uint64_t)rows);
+      const int32_t* hr = base + (size_t)hd * rows * lc.head_dim;
+      for (int r = 0; r < rows; ++r) { h.put_u64((uint64_t)lc.head_dim); h.put(hr + (size_t)r * lc.head_dim, (size_t)lc.head_dim * 4); }
+    }
+  }
+}
+
+// Queues on c.stream one strided download of every head's live rows of
+// layer l's K (kind 0) or V cache into dst.
+static void kv_download(Ctx& c, Seq& q, int l, int kind, int32_t* dst) {
+  const LayerCfg& lc = c.cfg.layers[l];
+  int st, rows;
+  kv_rows(c, q, l, &st, &rows);
+  const size_t width = (size_t)rows * lc.head_dim * 4;
+  const int32_t* src = (kind == 0 ? q.kc[l] : q.vc[l]) + (size_t)st * lc.head_dim;
+  if (width)
+    CK(cudaMemcpy2DAsync(dst, width, src, (size_t)q.cap * lc.head_dim * 4, width, lc.kv_heads,
+                         cudaMemcpyDeviceToHost, c.stream));
+}
+
+static int32_t* pinned_alloc(size_t bytes, const char* what) {
+  void* h = nullptr;
+  if (cudaHostAlloc(&h, bytes ? bytes : 16, cudaHostAllocDefault) != cudaSuccess)
+    throw Fail{RDET_E_OOM, std::string("pinned staging for the ") + what + " could not be allocated"};
+  return static_cast<int32_t*>(h);
+}
+
+// Over the caches of layers [0, nl) (the reference commits the caches built
+// so far: after each prefill layer, and the whole list after prefill/decode).
 static bool kv_commitment(Ctx& c, Seq& q, std::string* out, int nl) {
   const ModelCfg& m = c.cfg;
   for (int l = 0; l < nl; ++l)
     if (!q.kc[l]) return false;  // a KV-sharing layer has no det cache of its own
+  // both kinds of layer l+1 download into one half of the pinned stage while
+  // layer l is hashed from the other
+  size_t most = 0;
+  for (int l = 0; l < nl; ++l) {
+    int st, rows;
+    kv_rows(c, q, l, &st, &rows);
+    most = std::max(most, (size_t)2 * m.layers[l].kv_heads * rows * m.layers[l].head_dim);
+  }
+  KvStage& ks = c.kvs;
+  if (!ks.ev[0]) {
+    CK(cudaEventCreateWithFlags(&ks.ev[0], cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&ks.ev[1], cudaEventDisableTiming));
+  }
+  if (ks.half_elems < most) {
+    if (ks.host) CK(cudaFreeHost(ks.host));
+    ks.host = nullptr;
+    ks.half_elems = 0;
+    ks.host = pinned_alloc(2 * most * 4, "KV commitment");
+    ks.half_elems = most;
+  }
+  auto half = [&](int l) { return ks.host + (l & 1) * ks.half_elems; };
+  auto enqueue = [&](int l) {
+    const LayerCfg& lc = m.layers[l];
+    int st, rows;
+    kv_rows(c, q, l, &st, &rows);
+    kv_download(c, q, l, 0, half(l));
+    kv_download(c, q, l, 1, half(l) + (size_t)lc.kv_heads * rows * lc.head_dim);
+    CK(cudaEventRecord(ks.ev[l & 1], c.stream));
+  };
   Sha256 h;
   h.put("raster-det-num-kv-cache-v1", 26);
   h.put_u64((uint64_t)nl);
+  if (nl) enqueue(0);
   for (int l = 0; l < nl; ++l) {
+    if (l + 1 < nl) enqueue(l + 1);
+    CK(cudaEventSynchronize(ks.ev[l & 1]));
     const LayerCfg& lc = m.layers[l];
-    h.put_u64((uint64_t)lc.kv_heads);
-    for (int kind = 0; kind < 2; ++kind) {
-      h.put(kind == 0 ? "k" : "v", 1);
-      h.put_u64((uint64_t)lc.kv_heads);
-      for (int hd = 0; hd < lc.kv_heads; ++hd) {
-        std::vector<int32_t> rows = kv_read(c, q, l, hd, kind == 0);
-        size_t nr = rows.size() / lc.head_dim;
-        h.put_u64(nr);
-        for (size_t r = 0; r < nr; ++r) { h.put_u64((uint64_t)lc.head_dim); h.put(rows.data() + r * lc.head_dim, (size_t)lc.head_dim * 4); }
-      }
-    }
+    int st, rows;
+    kv_rows(c, q, l, &st, &rows);
+    kv_hash_layer(h, lc, rows, half(l), half(l) + (size_t)lc.kv_heads * rows * lc.head_dim);
   }
   *out = h.hex();
   return true;
+}
+
+// The commitments of the prefixes [0, p) for p = 1..n together: one download
+// of the caches the longest prefix covers, then the prefixes' independent
+// SHA-256 streams spread over host threads (longest first).  out[p-1] is
+// empty where that prefix includes a KV-sharing layer.
+static void kv_prefix_commitments(Ctx& c, Seq& q, int n, std::vector<std::string>* out) {
+  const ModelCfg& m = c.cfg;
+  out->assign(n, std::string());
+  int own = 0;
+  while (own < n && q.kc[own]) ++own;
+  if (!own) return;
+  std::vector<size_t> off(own + 1, 0);
+  std::vector<int> rows(own);
+  for (int l = 0; l < own; ++l) {
+    int st;
+    kv_rows(c, q, l, &st, &rows[l]);
+    off[l + 1] = off[l] + (size_t)2 * m.layers[l].kv_heads * rows[l] * m.layers[l].head_dim;
+  }
+  std::unique_ptr<int32_t, cudaError_t (*)(void*)> host(pinned_alloc(off[own] * 4, "KV prefix commitments"),
+                                                         cudaFreeHost);
+  try {
+    for (int l = 0; l < own; ++l) {
+      const size_t kv = (size_t)m.layers[l].kv_heads * rows[l] * m.layers[l].head_dim;
+      kv_download(c, q, l, 0, host.get() + off[l]);
+      kv_download(c, q, l, 1, host.get() + off[l] + kv);
+    }
+    CK(cudaStreamSynchronize(c.stream));
+  } catch (...) {
+    cudaStreamSynchronize(c.stream);  // no download may still target the staging when it is freed
+    throw;
+  }
+  std::atomic<int> next{0};
+  auto work = [&] {
+    for (int i; (i = next.fetch_add(1)) < own;) {
+      const int p = own - i;  // longest prefix first
+      Sha256 h;
+      h.put("raster-det-num-kv-cache-v1", 26);
+      h.put_u64((uint64_t)p);
+      for (int l = 0; l < p; ++l) {
+        const int32_t* k = host.get() + off[l];
+        kv_hash_layer(h, m.layers[l], rows[l], k, k + (size_t)m.layers[l].kv_heads * rows[l] * m.layers[l].head_dim);
+      }
+      (*out)[p - 1] = h.hex();
+    }
+  };
+  const unsigned hw = std::thread::hardware_concurrency();
+  const int nt = std::max(1, std::min(own, std::min(8, (int)(hw > 1 ? hw - 1 : 1))));
+  std::vector<std::thread> ts;
+  for (int t = 1; t < nt; ++t) ts.emplace_back(work);
+  work();
+  for (auto& t : ts) t.join();
 }
 
 // Captures (once per sequence) the whole decode_transition of the token in
@@ -2091,11 +2355,16 @@ int32_t rdet_prefill_range(rdet_ctx* ctx, rdet_seq* seq, uint32_t layer_start, u
     REQUIRE(c.prefill_owner == &q, RDET_E_STATE, "prefill.range requires prefill_begin on this sequence");
     REQUIRE((int)layer_start == q.prefill_next, RDET_E_STATE, "prefill.range must continue at the next layer");
     REQUIRE(layer_end >= layer_start && (int)layer_end <= c.cfg.L, RDET_E_RANGE, "layer range out of bounds");
+    struct JoinAtExit {  // no layer hash outlives the call, whatever happens
+      Ctx& c;
+      ~JoinAtExit() { commit_join(c, false); }
+    } join{c};
     for (uint32_t l = layer_start; l < layer_end; ++l) {
       prefill_layer(c, q, (int)l);
       q.prefill_next = (int)l + 1;
     }
     CK(cudaStreamSynchronize(c.stream));
+    commit_join(c, true);
   });
 }
 
@@ -2381,6 +2650,22 @@ int32_t rdet_commitment(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t lay
   });
   if (rc == RDET_OK && none) { hex_out[0] = 0; return RDET_NONE; }
   return rc;
+}
+
+int32_t rdet_kv_prefix_commitments(rdet_ctx* ctx, rdet_seq* seq, uint32_t n, char* hex_out) {
+  return guard([&] {
+    REQUIRE(ctx && seq && (hex_out || n == 0), RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    Seq& q = *seq->s;
+    CK(cudaSetDevice(c.device));
+    REQUIRE(n <= (uint32_t)c.cfg.L, RDET_E_RANGE, "more prefixes than layers");
+    std::vector<std::string> hx;
+    kv_prefix_commitments(c, q, (int)n, &hx);
+    for (uint32_t p = 0; p < n; ++p) {
+      if (hx[p].empty()) hex_out[65 * (size_t)p] = 0;
+      else memcpy(hex_out + 65 * (size_t)p, hx[p].c_str(), 65);
+    }
+  });
 }
 
 int32_t rdet_nccl_unique_id(void* id_out, size_t len) {

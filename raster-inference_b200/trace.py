@@ -117,6 +117,9 @@ def run(backend: Backend, prompt_token_ids: Sequence[int], num_layers: int, max_
     if add("prefill.prepare_aux", {"det_embedded_prompt_activations_sha256": emb, "prompt_token_ids": ids,
                                    "prompt_token_ids_sha256": ids_sha}):
         return tr, []
+    # a backend that computes every layer prefix's KV commitment at once
+    # (one download, parallel hashes) supplies kv_prefix_commitments
+    prefix_kv = backend.kv_prefix_commitments(L) if hasattr(backend, "kv_prefix_commitments") else None
     done: list = []
     for layer in range(L):
         out = backend.layer_output_commitment(layer)
@@ -126,7 +129,8 @@ def run(backend: Backend, prompt_token_ids: Sequence[int], num_layers: int, max_
         done.append(out)
         if add("prefill.range_finalize", {"completed_layer_output_det_sha256s": list(done),
                                           "det_current_activations_sha256": out,
-                                          "det_layer_caches_sha256": backend.kv_commitment(layer + 1),
+                                          "det_layer_caches_sha256": prefix_kv[layer] if prefix_kv is not None
+                                          else backend.kv_commitment(layer + 1),
                                           "execution_mode": DET, "next_layer_idx": layer + 1}):
             return tr, []
     if add("prefill.finalize", {"decode_position": S, "decode_token_count": S,
@@ -200,3 +204,6 @@ class SeqBackend:
 
     def kv_commitment(self, layers):
         return self.seq.commitment(self._b[4], layers)
+
+    def kv_prefix_commitments(self, n):
+        return self.seq.kv_prefix_commitments(n)

@@ -39,3 +39,24 @@ def test_cuda_path_reproduces_native_det_full():
 def test_cuda_path_reproduces_native_det_terminal():
     tr, _ = run_trace(terminal=GOLD["terminal"])
     assert [list(e) for e in tr.entries] == GOLD["native-det-terminal"]
+
+
+@pytest.mark.parametrize("donor", [False, True], ids=["no_donor", "donor"])
+def test_kv_prefix_commitments_match_single_calls(donor):
+    # rdet_kv_prefix_commitments against n calls of rdet_commitment(KV, p):
+    # after prefill and after decode steps that trim the sliding caches
+    # (window 4 < 6 prompt + 5 generated rows); a KV-sharing model gives None
+    # from its first shared layer on
+    import det_goldens_fixture as fx
+    d = tempfile.mkdtemp()
+    fx.write_fixture(d, donor=donor)
+    m = rdet.Model.open(d, max_prefill=16)
+    s = m.new_sequence(64)
+    s.prefill(fx.PROMPT_IDS)
+    for steps in (0, 5):
+        s.generate(steps)
+        want = [s.commitment(rdet.BUF_KV, p) for p in range(1, m.L + 1)]
+        assert s.kv_prefix_commitments(m.L) == want
+        assert s.kv_prefix_commitments(2) == want[:2]
+        assert (want[-1] is None) == donor and want[0] is not None
+    m.close()
