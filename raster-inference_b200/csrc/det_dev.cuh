@@ -104,18 +104,54 @@ RDET_HD int64_t rte_div_i64(int64_t n, int64_t d) {
   return (q & 1) ? q + step : q;
 }
 
-// ops.rs:50 div_act: ties-even (n << 16) / d, clamped to i32 (fits i64).
+// floor(a / d) and its remainder for a <= 2^63 and 0 < d < 2^32, for a
+// divisor known only at run time (a 64-bit integer division is a long
+// software sequence on the GPU).  The double quotient is off by at most
+// 2^11 / d + 1 (a rounds to 53 bits, the quotient once more); the exact
+// remainder of that estimate lies within 2^11 + 2d, so a second estimate from
+// it (when still large) leaves the quotient within one, and whole-d steps on
+// the exact remainder finish it.
+RDET_HD uint64_t udiv_u64_u32(uint64_t a, uint32_t d, uint64_t* rem) {
+  const double dd = (double)d;
+  uint64_t q = (uint64_t)((double)a / dd);
+  int64_t r = (int64_t)(a - q * (uint64_t)d);
+  if (r < -4 * (int64_t)d || r >= 5 * (int64_t)d) {
+    q += (uint64_t)(int64_t)((double)r / dd);
+    r = (int64_t)(a - q * (uint64_t)d);
+  }
+  while (r < 0) { --q; r += d; }
+  while (r >= (int64_t)d) { ++q; r -= d; }
+  *rem = (uint64_t)r;
+  return q;
+}
+
+// ops.rs:688 on magnitudes: |n| / |d| rounded half to even, then the sign
+// (`neg`) applied.  The reference truncates toward zero and rounds the
+// remainder's magnitude, ties to the even truncated quotient: the same value.
+RDET_HD int64_t rte_div_mag(uint64_t a, uint32_t d, bool neg) {
+  uint64_t r;
+  uint64_t q = udiv_u64_u32(a, d, &r);
+  const uint64_t twice = 2 * r;  // r < 2^32
+  if (twice > d || (twice == d && (q & 1))) q += 1;
+  return neg ? (int64_t)(0 - q) : (int64_t)q;
+}
+
+// ops.rs:50 div_act: ties-even (n << 16) / d, clamped to i32 (d != 0).
 RDET_HD int32_t div_act(int32_t n, int32_t d) {
-  int64_t dividend = (int64_t)n * 65536;
-  int64_t dd = d;
-  int64_t q;
-  if (dd < 0) q = rte_div_i64(-dividend, -dd);  // same quotient and tie rule
-  else q = rte_div_i64(dividend, dd);
+  const int64_t dividend = (int64_t)n * 65536;  // |dividend| <= 2^47
+  const uint64_t a = dividend < 0 ? (uint64_t)(-dividend) : (uint64_t)dividend;
+  const uint32_t m = d < 0 ? 0u - (uint32_t)d : (uint32_t)d;
+  const int64_t q = rte_div_mag(a, m, (dividend < 0) != (d < 0));
   return q > INT32_MAX ? INT32_MAX : (q < INT32_MIN ? INT32_MIN : (int32_t)q);
 }
 
-// ops.rs:78 div_acc_by_u32
-RDET_HD int64_t div_acc_by_u32(int64_t v, uint32_t d) { return rte_div_i64(v, (int64_t)d); }
+// ops.rs:78 div_acc_by_u32 (d > 0).  Constant divisors (the series of
+// exp_term and sin_cos_acc) call rte_div_i64, which the compiler turns into
+// a multiply by a reciprocal.
+RDET_HD int64_t div_acc_by_u32(int64_t v, uint32_t d) {
+  const uint64_t a = v < 0 ? 0 - (uint64_t)v : (uint64_t)v;
+  return rte_div_mag(a, d, v < 0);
+}
 
 // ops.rs:682 acc_mul: (l*r) / 2^32, ties to even, clamped to i64.
 RDET_HD int64_t acc_mul(int64_t l, int64_t r) {
@@ -143,13 +179,18 @@ RDET_HD unsigned __int128 isq_prod(uint32_t c, uint64_t x) {
 // The reference bisects on r; isq_le(r, x) is monotone in r, so the same r is
 // found by starting from the double estimate 2^32/sqrt(x) (relative error
 // below 2^-50, i.e. off by at most one for r < 2^31) and stepping with the
-// exact predicate until it flips.
+// exact predicate until it flips (the steps make any estimate exact; the
+// device takes the estimate from the double reciprocal square root).
 RDET_HD int32_t inv_sqrt_acc(int64_t xs) {
   if (xs <= 0) return INT32_MAX;  // x == 0 (negative inputs cannot occur)
   uint64_t x = (uint64_t)xs;
   const uint32_t maxb = 0x7fffffffu;
   if (isq_le(maxb, x)) return INT32_MAX;
+#ifdef __CUDA_ARCH__
+  const double est = 4294967296.0 * rsqrt((double)x);
+#else
   const double est = 4294967296.0 / sqrt((double)x);
+#endif
   uint32_t lo = est >= (double)(maxb - 1) ? maxb - 1 : (uint32_t)est;
   while (lo > 0 && !isq_le(lo, x)) --lo;
   while (lo + 1 < maxb && isq_le(lo + 1, x)) ++lo;
@@ -173,9 +214,9 @@ RDET_HD int64_t softmax_exp_term(int64_t delta) {
   int64_t shift = pos / LN2;
   int64_t r = pos - shift * LN2;
   int64_t r2 = acc_mul(r, r), r3 = acc_mul(r2, r), r4 = acc_mul(r3, r), r5 = acc_mul(r4, r);
-  int64_t inner = acc_add_sat(div_acc_by_u32(r4, 24), neg_sat64(div_acc_by_u32(r5, 120)));
-  inner = acc_add_sat(neg_sat64(div_acc_by_u32(r3, 6)), inner);
-  inner = acc_add_sat(div_acc_by_u32(r2, 2), inner);
+  int64_t inner = acc_add_sat(rte_div_i64(r4, 24), neg_sat64(rte_div_i64(r5, 120)));
+  inner = acc_add_sat(neg_sat64(rte_div_i64(r3, 6)), inner);
+  inner = acc_add_sat(rte_div_i64(r2, 2), inner);
   int64_t approx = acc_add_sat(acc_add_sat(kOneAcc, neg_sat64(r)), inner);
   if (approx <= 0) return 0;
   if (shift >= 64) return 0;
@@ -234,11 +275,11 @@ RDET_HD void sin_cos_acc(int64_t angle, int32_t* c_out, int32_t* s_out) {
   else { a = TWO_PI - red; sneg = true; cneg = false; }
   int64_t a2 = acc_mul(a, a);
   int64_t a3 = acc_mul(a2, a), a5 = acc_mul(a3, a2), a7 = acc_mul(a5, a2);
-  int64_t sp = acc_add_sat(acc_add_sat(a, neg_sat64(div_acc_by_u32(a3, 6))),
-                           acc_add_sat(div_acc_by_u32(a5, 120), neg_sat64(div_acc_by_u32(a7, 5040))));
+  int64_t sp = acc_add_sat(acc_add_sat(a, neg_sat64(rte_div_i64(a3, 6))),
+                           acc_add_sat(rte_div_i64(a5, 120), neg_sat64(rte_div_i64(a7, 5040))));
   int64_t a4 = acc_mul(a2, a2), a6 = acc_mul(a4, a2);
-  int64_t cp = acc_add_sat(acc_add_sat(kOneAcc, neg_sat64(div_acc_by_u32(a2, 2))),
-                           acc_add_sat(div_acc_by_u32(a4, 24), neg_sat64(div_acc_by_u32(a6, 720))));
+  int64_t cp = acc_add_sat(acc_add_sat(kOneAcc, neg_sat64(rte_div_i64(a2, 2))),
+                           acc_add_sat(rte_div_i64(a4, 24), neg_sat64(rte_div_i64(a6, 720))));
   int32_t s = requantize(sp), c = requantize(cp);
   *s_out = sneg ? neg_sat(s) : s;
   *c_out = cneg ? neg_sat(c) : c;

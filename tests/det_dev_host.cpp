@@ -101,6 +101,44 @@ extern "C" int64_t rdet_host_check(const char* fn, uint64_t seed, int64_t n) {
       uint32_t d = 1 + (uint32_t)(g.next() % 0xfffffffeull);
       bad += rdet::div_acc_by_u32(a, d) != dor::div_acc_by_u32(a, d);
     }
+  } else if (!strcmp(fn, "div_edges")) {
+    // the run-time-divisor division at its edges: every divisor class (small,
+    // the model dims, around 2^31 and 2^32), dividends at the i64 limits,
+    // exact multiples, ties and their neighbours, and divisors of 1..12 bits
+    // with full-range dividends (the largest first estimates)
+    const uint32_t ds[] = {1, 2, 3, 5, 6, 7, 24, 120, 255, 256, 257, 512, 2560, 5040, 10240, 65535, 65536,
+                           0x7fffffffu, 0x80000000u, 0x80000001u, 0xfffffffeu, 0xffffffffu};
+    const int64_t as[] = {INT64_MIN, INT64_MIN + 1, INT64_MAX, INT64_MAX - 1, -1, 0, 1,
+                          (int64_t)1 << 62, -((int64_t)1 << 62), (int64_t)1 << 53, ((int64_t)1 << 53) + 1};
+    for (uint32_t d : ds) {
+      for (int64_t a : as) bad += rdet::div_acc_by_u32(a, d) != dor::div_acc_by_u32(a, d);
+      for (int k = 0; k < 64; ++k) {
+        const int64_t base = (int64_t)(g.next() >> 2) / (int64_t)d * (int64_t)d;  // a multiple of d
+        for (int64_t off = -2; off <= 2; ++off)
+          for (int64_t sgn = -1; sgn <= 1; sgn += 2) {
+            const int64_t m = sgn * base;
+            int64_t a = m + off;
+            bad += rdet::div_acc_by_u32(a, d) != dor::div_acc_by_u32(a, d);
+            a = m + (int64_t)(d / 2) + off;  // around the tie
+            bad += rdet::div_acc_by_u32(a, d) != dor::div_acc_by_u32(a, d);
+          }
+      }
+    }
+    for (int64_t i = 0; i < n; ++i) {
+      const int bits = 1 + (int)(g.next() % 12);
+      uint32_t d = (uint32_t)(g.next() & ((1u << bits) - 1));
+      if (d == 0) d = 1;
+      const int64_t a = g.wide(64, true);
+      bad += rdet::div_acc_by_u32(a, d) != dor::div_acc_by_u32(a, d);
+      const int32_t x = g.act();
+      int32_t y = (int32_t)(g.next() & ((1u << bits) - 1)) * ((g.next() & 1) ? 1 : -1);
+      if (y == 0) y = -1;
+      bad += rdet::div_act(x, y) != dor::div_act(x, y);
+    }
+    const int32_t acts[] = {INT32_MIN, INT32_MIN + 1, INT32_MAX, -1, 0, 1, 32768, -32768};
+    for (int32_t x : acts)
+      for (int32_t y : acts)
+        if (y) bad += rdet::div_act(x, y) != dor::div_act(x, y);
   } else if (!strcmp(fn, "acc_mul")) {
     for (int64_t i = 0; i < n; ++i) {
       int64_t a = g.wide(64, true), b = g.wide(64, true);

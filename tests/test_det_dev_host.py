@@ -39,6 +39,7 @@ CASES = [
     ("rshift_rte", 2_000_000),
     ("div_act", 1_000_000),
     ("div_acc_by_u32", 1_000_000),
+    ("div_edges", 1_000_000),
     ("acc_mul", 1_000_000),
     ("exp_term", 1_000_000),
     ("softmax_weight", 1_000_000),
