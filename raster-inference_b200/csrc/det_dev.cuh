@@ -222,8 +222,40 @@ RDET_HD int64_t softmax_exp_term(int64_t delta) {
   if (shift >= 64) return 0;
   return rshift_rte(approx, (uint32_t)shift);
 }
-RDET_HD int64_t exp_term(int32_t logit, int32_t max_logit) {  // ops.rs:261
-  return softmax_exp_term((int64_t)sub_sat(logit, max_logit) * 65536);
+// acc_mul (ops.rs:682) of two values in [0, 2^32): the product fits 64 bits.
+RDET_HD uint32_t acc_mul_u32(uint32_t a, uint32_t b) {
+  const uint64_t p = (uint64_t)a * b;
+  uint32_t q = (uint32_t)(p >> 32);  // <= 2^32 - 2, so the rounding step cannot wrap
+  const uint32_t low = (uint32_t)p;
+  if (low > 0x80000000u || (low == 0x80000000u && (q & 1))) q += 1;
+  return q;
+}
+// rte_div_i64 of a value in [0, 2^32) by a small constant
+RDET_HD uint32_t rte_div_u32(uint32_t v, uint32_t d) {
+  const uint32_t q = v / d, r = v - q * d;
+  return (2 * r > d || (2 * r == d && (q & 1))) ? q + 1 : q;
+}
+
+// ops.rs:261 + :505 for logit <= max_logit (the row maximum): the same
+// value as softmax_exp_term in 32-bit pieces.  With delta = -pos in
+// (-16, 0], the reduced argument r = pos mod ln2 lies in [0, 2^32), so every
+// power r^k is an acc_mul of values below 2^32 and every series term a
+// division of such a value by a constant; no term reaches 2^33, so the
+// reference's saturating adds add exactly.
+RDET_HD int64_t exp_term(int32_t logit, int32_t max_logit) {
+  const int32_t d = sub_sat(logit, max_logit);
+  if (d > 0) return softmax_exp_term((int64_t)d * 65536);  // a logit above the max: the general form
+  if (d <= -(16 << 16)) return 0;                            // delta <= -16
+  const uint64_t LN2 = 2977044472ull;
+  const uint64_t pos = (uint64_t)(-(int64_t)d) << 16;       // [0, 2^36)
+  const uint32_t shift = (uint32_t)(pos / LN2);              // <= 23
+  const uint32_t r = (uint32_t)(pos - shift * LN2);
+  const uint32_t r2 = acc_mul_u32(r, r), r3 = acc_mul_u32(r2, r), r4 = acc_mul_u32(r3, r),
+                 r5 = acc_mul_u32(r4, r);
+  const int64_t approx = kOneAcc - (int64_t)r + rte_div_u32(r2, 2) - (int64_t)rte_div_u32(r3, 6) +
+                         rte_div_u32(r4, 24) - (int64_t)rte_div_u32(r5, 120);
+  if (approx <= 0) return 0;
+  return rshift_rte(approx, shift);
 }
 
 // ops.rs:64 + :266: requantize(div_acc(e, sum)) for 0 <= e <= sum, sum > 0.

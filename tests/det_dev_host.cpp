@@ -8,6 +8,7 @@
 #include "../raster-inference_b200/csrc/det_dev.cuh"
 #include "../oracle/det_num.hpp"
 
+#include <algorithm>
 #include <cstring>
 
 namespace {
@@ -139,6 +140,21 @@ extern "C" int64_t rdet_host_check(const char* fn, uint64_t seed, int64_t n) {
     for (int32_t x : acts)
       for (int32_t y : acts)
         if (y) bad += rdet::div_act(x, y) != dor::div_act(x, y);
+  } else if (!strcmp(fn, "exp_term_all")) {
+    // every logit - max difference the series sees (beyond -16 the term is
+    // 0), with the max at 0, at the i32 extremes and at random values
+    const int32_t maxes[] = {0, INT32_MAX, INT32_MIN + (16 << 16) + 8, 123456789};
+    for (int32_t m : maxes)
+      for (int64_t dd = -(16 << 16) - 64; dd <= 0; ++dd) {
+        if ((int64_t)m + dd < INT32_MIN) continue;
+        const int32_t l = (int32_t)((int64_t)m + dd);
+        bad += rdet::exp_term(l, m) != dor::attention_softmax_exp_term(l, m);
+      }
+    for (int64_t i = 0; i < n; ++i) {
+      const int32_t m = g.act();
+      const int32_t l = (int32_t)std::max<int64_t>(INT32_MIN, (int64_t)m - (int64_t)(g.next() % (17u << 16)));
+      bad += rdet::exp_term(l, m) != dor::attention_softmax_exp_term(l, m);
+    }
   } else if (!strcmp(fn, "acc_mul")) {
     for (int64_t i = 0; i < n; ++i) {
       int64_t a = g.wide(64, true), b = g.wide(64, true);

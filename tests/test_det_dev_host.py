@@ -42,6 +42,7 @@ CASES = [
     ("div_edges", 1_000_000),
     ("acc_mul", 1_000_000),
     ("exp_term", 1_000_000),
+    ("exp_term_all", 1_000_000),
     ("softmax_weight", 1_000_000),
     ("tanh_act", 1_000_000),
     ("softcap_act", 500_000),
