@@ -175,6 +175,21 @@ extern "C" int64_t rdet_host_check(const char* fn, uint64_t seed, int64_t n) {
       if (g.next() % 8 == 0) e = (int64_t)1 << 32;
       bad += rdet::softmax_weight(e, sum) != dor::requantize(dor::div_acc(e, sum));
     }
+    // sums of a few exp terms (the windows' range) with e at and around the
+    // ties of both roundings, and sums at the 2^61 switch
+    for (int64_t i = 0; i < n; ++i) {
+      const int64_t sum = ((int64_t)1 << 32) + (int64_t)(g.next() % ((uint64_t)1 << (33 + i % 17)));
+      const int64_t q = (int64_t)(g.next() % (((uint64_t)1 << 32) + 1));  // a target quotient
+      const int64_t e0 = (int64_t)(((unsigned __int128)q * (uint64_t)sum) >> 32);
+      for (int64_t off = -1; off <= 1; ++off) {
+        const int64_t e = std::min<int64_t>(std::max<int64_t>(e0 + off, 1), std::min<int64_t>(sum, (int64_t)1 << 32));
+        bad += rdet::softmax_weight(e, sum) != dor::requantize(dor::div_acc(e, sum));
+      }
+    }
+    const int64_t sums[] = {((int64_t)1 << 61) - 1, (int64_t)1 << 61, ((int64_t)1 << 61) + 1, INT64_MAX};
+    for (int64_t sum : sums)
+      for (int64_t e : {(int64_t)1, (int64_t)2, ((int64_t)1 << 32) - 1, (int64_t)1 << 32})
+        bad += rdet::softmax_weight(e, sum) != dor::requantize(dor::div_acc(e, sum));
   } else if (!strcmp(fn, "tanh_act")) {
     for (int64_t i = 0; i < n; ++i) {
       int32_t x = edge(i) ? kActEdges[i] : g.act(20);
