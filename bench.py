@@ -236,6 +236,25 @@ def run_kernel_case(args):
     t = cfg["text_config"]
     dev = "cuda:0"
     g = torch.Generator(device=dev).manual_seed(5)
+    if args.kernel_case == "prefill":
+        # one prefill of the --ctx-token prompt at E4B shape inside the NVTX
+        # range "prefill" (after an unrecorded prefill that does first-use
+        # setup), for a launch list filtered with --nvtx-include "prefill/"
+        model = rdet.Model.synthetic(cfg, SEED, width=16, device=0, max_prefill=args.ctx)
+        ids = lcg_ids(args.ctx, t["vocab_size"], SEED)
+        for rep in range(2):
+            seq = model.new_sequence(args.ctx + 8)
+            torch.cuda.synchronize()
+            if rep:
+                torch.cuda.nvtx.range_push("prefill")
+            seq.prefill(ids)
+            torch.cuda.synchronize()
+            if rep:
+                torch.cuda.nvtx.range_pop()
+            seq.free()
+        model.close()
+        print(f"prefill: {args.ctx} tokens")
+        return
     if args.kernel_case == "tc":
         # prefill linear on the tensor cores (rdet_det_linear, >= 32 rows): byte-plane
         # prep kernels then tc_linear_kernel, at 2048 prompt tokens
@@ -522,7 +541,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched ragged decode line (0: skip)")
     ap.add_argument("--batch-steps", type=int, default=8)
-    ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc"],
+    ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc", "prefill"],
                     help="run a few launches of one kernel at E4B shapes for an ncu capture, then exit")
     ap.add_argument("--trace-case", action="store_true",
                     help="time a checkpoint-traced run (commitments on) against a plain one at --ctx, then exit")

@@ -2115,7 +2115,9 @@ __global__ void attn_prefill_kernel(const AttnPrefillArgs a, int rowlen) {
 // residual to the first max); phase C accumulates the weighted V sum in i64.
 constexpr int AP_R = 64, AP_TK = 32, AP_CH = 128;
 
-__global__ void __launch_bounds__(256) attn_prefill_tiled(const AttnPrefillArgs a, int rowlen, int QB) {
+// Two CTAs per SM where shared memory allows (head_dim 256: ~106 KB each), so
+// one CTA's tile loads and barriers overlap the other's multiply-adds.
+__global__ void __launch_bounds__(256, 2) attn_prefill_tiled(const AttnPrefillArgs a, int rowlen, int QB) {
   pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int d = a.d, dp = d + 4, G = a.Hq / a.Hkv, R = QB * G;
@@ -2123,7 +2125,9 @@ __global__ void __launch_bounds__(256) attn_prefill_tiled(const AttnPrefillArgs 
   int32_t* Ks = Qs + AP_R * dp;                          // [AP_TK][dp] (V tiles use [AP_TK][AP_CH+4])
   int32_t* Ws = Ks + AP_TK * dp;                         // [AP_R][AP_TK]
   __shared__ int32_t rmax[AP_R], ridx[AP_R];
-  const int kvh = blockIdx.x, i0 = blockIdx.y * QB;
+  // query blocks in descending order: under a causal mask the last blocks
+  // read the most keys, and starting them first keeps the final wave short
+  const int kvh = blockIdx.x, i0 = (gridDim.y - 1 - blockIdx.y) * QB;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   auto row_query = [&](int r) { return i0 + (r % QB); };
   auto row_head = [&](int r) { return kvh * G + r / QB; };
@@ -2370,6 +2374,8 @@ void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t s) {
     static size_t configured = 0;
     if (smem > 48 * 1024 && smem > configured) {
       cudaFuncSetAttribute(attn_prefill_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+      cudaFuncSetAttribute(attn_prefill_tiled, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared);
       configured = 220 * 1024;
     }
     dim3 grid(a.Hkv, (a.S + QB - 1) / QB);
