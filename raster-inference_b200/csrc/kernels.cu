@@ -2114,10 +2114,13 @@ __global__ void attn_prefill_kernel(const AttnPrefillArgs a, int rowlen) {
 // into exact softmax weights (exp, saturating-free sum, ties-to-even division,
 // residual to the first max); phase C accumulates the weighted V sum in i64.
 constexpr int AP_R = 64, AP_TK = 32, AP_CH = 128;
+// RPW rows per warp: 8 warps of 8 rows when two CTAs share an SM (head_dim
+// 256, ~106 KB each), 16 warps of 4 rows when one 206 KB CTA (head_dim 512)
+// holds the SM, so that either way enough independent multiply-add chains
+// are in flight.
 
-// Two CTAs per SM where shared memory allows (head_dim 256: ~106 KB each), so
-// one CTA's tile loads and barriers overlap the other's multiply-adds.
-__global__ void __launch_bounds__(256, 2) attn_prefill_tiled(const AttnPrefillArgs a, int rowlen, int QB) {
+template <int RPW>
+__global__ void __launch_bounds__(32 * AP_R / RPW, RPW == 8 ? 2 : 1) attn_prefill_tiled(const AttnPrefillArgs a, int rowlen, int QB) {
   pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int d = a.d, dp = d + 4, G = a.Hq / a.Hkv, R = QB * G;
@@ -2143,10 +2146,10 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_tiled(const AttnPrefillAr
     reinterpret_cast<int4*>(Qs + r * dp)[c] = v;
   }
   // ---- phase A: scores + first max
-  int32_t bm[8], bi[8];
+  int32_t bm[RPW], bi[RPW];
 #pragma unroll
-  for (int t = 0; t < 8; ++t) { bm[t] = INT32_MIN; bi[t] = INT32_MAX; }
-  const int rbase = warp * 8;
+  for (int t = 0; t < RPW; ++t) { bm[t] = INT32_MIN; bi[t] = INT32_MAX; }
+  const int rbase = warp * RPW;
   for (int kt = klo; kt < khi; kt += AP_TK) {
     __syncthreads();
     for (int e = threadIdx.x; e < AP_TK * (d / 4); e += blockDim.x) {
@@ -2156,21 +2159,21 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_tiled(const AttnPrefillAr
       reinterpret_cast<int4*>(Ks + jj * dp)[c] = v;
     }
     __syncthreads();
-    int64_t acc[8];
+    int64_t acc[RPW];
 #pragma unroll
-    for (int t = 0; t < 8; ++t) acc[t] = 0;
+    for (int t = 0; t < RPW; ++t) acc[t] = 0;
     const int4* kr = reinterpret_cast<const int4*>(Ks + lane * dp);
     for (int c = 0; c < d / 4; ++c) {
       int4 kv = kr[c];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) {
+      for (int t = 0; t < RPW; ++t) {
         int4 qv = reinterpret_cast<const int4*>(Qs + (rbase + t) * dp)[c];
         acc[t] = dot4_acc(acc[t], kv, qv);
       }
     }
     const int j = kt + lane;
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
+    for (int t = 0; t < RPW; ++t) {
       int r = rbase + t;
       if (r >= R) continue;
       int i = row_query(r);
@@ -2183,7 +2186,7 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_tiled(const AttnPrefillAr
     }
   }
 #pragma unroll
-  for (int t = 0; t < 8; ++t) {
+  for (int t = 0; t < RPW; ++t) {
     int32_t v = bm[t], ix = bi[t];
     for (int o = 16; o > 0; o >>= 1) {
       int32_t v2 = __shfl_xor_sync(0xffffffffu, v, o), i2 = __shfl_xor_sync(0xffffffffu, ix, o);
@@ -2193,7 +2196,7 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_tiled(const AttnPrefillAr
   }
   __syncthreads();
   // ---- phase B: exact softmax weights per row (written over the scores)
-  for (int t = 0; t < 8; ++t) {
+  for (int t = 0; t < RPW; ++t) {
     int r = rbase + t;
     if (r >= R) break;
     int i = row_query(r);
@@ -2230,9 +2233,9 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_tiled(const AttnPrefillAr
   const bool dbl = 2 * vbuf <= AP_R * dp + AP_TK * dp + AP_R * AP_TK;
   const int nkt = (khi - klo + AP_TK - 1) / AP_TK;
   for (int c0 = 0; dbl && c0 < d; c0 += AP_CH) {
-    int64_t acc[8][4];
+    int64_t acc[RPW][4];
 #pragma unroll
-    for (int t = 0; t < 8; ++t)
+    for (int t = 0; t < RPW; ++t)
 #pragma unroll
       for (int u = 0; u < 4; ++u) acc[t][u] = 0;
     auto issue = [&](int t) {
@@ -2281,8 +2284,8 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_tiled(const AttnPrefillAr
         for (int jj = 0; jj < AP_TK; ++jj) {
           const int4 v = reinterpret_cast<const int4*>(Vb + jj * cwp)[dg];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const int32_t w = Wb[(rg * 8 + q) * AP_TK + jj];
+          for (int q = 0; q < RPW; ++q) {
+            const int32_t w = Wb[(rg * RPW + q) * AP_TK + jj];
             acc[q][0] = mac_wide(acc[q][0], w, v.x);
             acc[q][1] = mac_wide(acc[q][1], w, v.y);
             acc[q][2] = mac_wide(acc[q][2], w, v.z);
@@ -2294,8 +2297,8 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_tiled(const AttnPrefillAr
     }
     if (dg * 4 < cw) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int r = rg * 8 + q;
+      for (int q = 0; q < RPW; ++q) {
+        const int r = rg * RPW + q;
         if (r >= R) continue;
         const int i = row_query(r);
         if (i >= a.S) continue;
@@ -2308,9 +2311,9 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_tiled(const AttnPrefillAr
     }
   }
   for (int c0 = 0; !dbl && c0 < d; c0 += AP_CH) {
-    int64_t acc[8][4];
+    int64_t acc[RPW][4];
 #pragma unroll
-    for (int t = 0; t < 8; ++t)
+    for (int t = 0; t < RPW; ++t)
 #pragma unroll
       for (int u = 0; u < 4; ++u) acc[t][u] = 0;
     for (int kt = klo; kt < khi; kt += AP_TK) {
@@ -2338,8 +2341,8 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_tiled(const AttnPrefillAr
         for (int jj = 0; jj < AP_TK; ++jj) {
           int4 v = reinterpret_cast<const int4*>(Ks + jj * cwp)[dg];
 #pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            const int32_t w = Ws[(rg * 8 + t) * AP_TK + jj];
+          for (int t = 0; t < RPW; ++t) {
+            const int32_t w = Ws[(rg * RPW + t) * AP_TK + jj];
             acc[t][0] = mac_wide(acc[t][0], w, v.x);
             acc[t][1] = mac_wide(acc[t][1], w, v.y);
             acc[t][2] = mac_wide(acc[t][2], w, v.z);
@@ -2350,8 +2353,8 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_tiled(const AttnPrefillAr
     }
     if (dg * 4 < cw) {
 #pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        int r = rg * 8 + t;
+      for (int t = 0; t < RPW; ++t) {
+        int r = rg * RPW + t;
         if (r >= R) continue;
         int i = row_query(r);
         if (i >= a.S) continue;
@@ -2371,15 +2374,21 @@ void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t s) {
   size_t smem = ((size_t)AP_R * (a.d + 4) + (size_t)AP_TK * (a.d + 4) + (size_t)AP_R * AP_TK) * 4;
   if (a.d % 4 == 0 && a.d <= 512 && G <= AP_R && (a.d <= AP_CH || a.d % AP_CH == 0) && smem <= 220 * 1024) {
     int QB = AP_R / G;
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-      cudaFuncSetAttribute(attn_prefill_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-      cudaFuncSetAttribute(attn_prefill_tiled, cudaFuncAttributePreferredSharedMemoryCarveout,
+    static bool configured = false;
+    if (!configured) {
+      cudaFuncSetAttribute(attn_prefill_tiled<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+      cudaFuncSetAttribute(attn_prefill_tiled<8>, cudaFuncAttributePreferredSharedMemoryCarveout,
                            cudaSharedmemCarveoutMaxShared);
-      configured = 220 * 1024;
+      cudaFuncSetAttribute(attn_prefill_tiled<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+      cudaFuncSetAttribute(attn_prefill_tiled<4>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared);
+      configured = true;
     }
     dim3 grid(a.Hkv, (a.S + QB - 1) / QB);
-    launch_k(attn_prefill_tiled, dim3(grid), dim3(256), smem, s, a, rowlen, QB);
+    if (2 * (smem + 1024) <= 228 * 1024)  // two CTAs fit an SM's shared memory
+      launch_k(attn_prefill_tiled<8>, dim3(grid), dim3(32 * AP_R / 8), smem, s, a, rowlen, QB);
+    else
+      launch_k(attn_prefill_tiled<4>, dim3(grid), dim3(32 * AP_R / 4), smem, s, a, rowlen, QB);
     return;
   }
   dim3 grid(a.Hq, a.S);
