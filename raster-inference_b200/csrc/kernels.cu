@@ -2115,9 +2115,9 @@ __global__ void attn_prefill_kernel(const AttnPrefillArgs a, int rowlen) {
 // residual to the first max); phase C accumulates the weighted V sum in i64.
 constexpr int AP_R = 64, AP_TK = 32, AP_CH = 128;
 // RPW rows per warp: 8 warps of 8 rows when two CTAs share an SM (head_dim
-// 256, ~106 KB each), 16 warps of 4 rows when one 206 KB CTA (head_dim 512)
-// holds the SM, so that either way enough independent multiply-add chains
-// are in flight.
+// 256, ~106 KB each), 32 warps of 2 rows (64 registers) when one 206 KB CTA
+// (head_dim 512) holds the SM, so that either way enough independent
+// multiply-add chains are in flight.
 
 template <int RPW>
 __global__ void __launch_bounds__(32 * AP_R / RPW, RPW == 8 ? 2 : 1) attn_prefill_tiled(const AttnPrefillArgs a, int rowlen, int QB) {
@@ -2379,8 +2379,8 @@ void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t s) {
       cudaFuncSetAttribute(attn_prefill_tiled<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
       cudaFuncSetAttribute(attn_prefill_tiled<8>, cudaFuncAttributePreferredSharedMemoryCarveout,
                            cudaSharedmemCarveoutMaxShared);
-      cudaFuncSetAttribute(attn_prefill_tiled<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-      cudaFuncSetAttribute(attn_prefill_tiled<4>, cudaFuncAttributePreferredSharedMemoryCarveout,
+      cudaFuncSetAttribute(attn_prefill_tiled<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+      cudaFuncSetAttribute(attn_prefill_tiled<2>, cudaFuncAttributePreferredSharedMemoryCarveout,
                            cudaSharedmemCarveoutMaxShared);
       configured = true;
     }
@@ -2388,7 +2388,7 @@ void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t s) {
     if (2 * (smem + 1024) <= 228 * 1024)  // two CTAs fit an SM's shared memory
       launch_k(attn_prefill_tiled<8>, dim3(grid), dim3(32 * AP_R / 8), smem, s, a, rowlen, QB);
     else
-      launch_k(attn_prefill_tiled<4>, dim3(grid), dim3(32 * AP_R / 4), smem, s, a, rowlen, QB);
+      launch_k(attn_prefill_tiled<2>, dim3(grid), dim3(32 * AP_R / 2), smem, s, a, rowlen, QB);
     return;
   }
   dim3 grid(a.Hq, a.S);
