@@ -2204,14 +2204,31 @@ __global__ void __launch_bounds__(32 * AP_R / RPW, RPW == 8 ? 2 : 1) attn_prefil
     int st = win_start(i), n = i + 1 - st;
     int32_t* sc = a.scores + ((size_t)row_head(r) * a.S + i) * rowlen;
     int32_t mx = rmax[r];
+    // four score loads in flight per lane (the scores sit in L2: one load
+    // at a time left this phase waiting on L2 latency)
+    constexpr int BU = 4;
     uint64_t sum = 0;
-    for (int j = lane; j < n; j += 32) sum += (uint64_t)exp_term(sc[j], mx);
+    for (int j0 = lane; j0 < n; j0 += 32 * BU) {
+      int32_t v[BU];
+#pragma unroll
+      for (int u = 0; u < BU; ++u) v[u] = j0 + 32 * u < n ? sc[j0 + 32 * u] : 0;
+#pragma unroll
+      for (int u = 0; u < BU; ++u)
+        if (j0 + 32 * u < n) sum += (uint64_t)exp_term(v[u], mx);
+    }
     sum = (uint64_t)warp_sum64((int64_t)sum);
     int64_t wsum = 0;
-    for (int j = lane; j < n; j += 32) {
-      int32_t w = softmax_weight(exp_term(sc[j], mx), (int64_t)sum);
-      sc[j] = w;
-      wsum += w;
+    for (int j0 = lane; j0 < n; j0 += 32 * BU) {
+      int32_t v[BU];
+#pragma unroll
+      for (int u = 0; u < BU; ++u) v[u] = j0 + 32 * u < n ? sc[j0 + 32 * u] : 0;
+#pragma unroll
+      for (int u = 0; u < BU; ++u)
+        if (j0 + 32 * u < n) {
+          const int32_t w = softmax_weight(exp_term(v[u], mx), (int64_t)sum);
+          sc[j0 + 32 * u] = w;
+          wsum += w;
+        }
     }
     wsum = warp_sum64(wsum);
     __syncwarp();
