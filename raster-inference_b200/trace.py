@@ -171,6 +171,19 @@ def run(backend: Backend, prompt_token_ids: Sequence[int], num_layers: int, max_
     return tr, gen
 
 
+def run_request(backend: Backend, preparer, prompt, num_layers: int, max_new_tokens: int,
+                temperature: float = 1.0, add_generation_prompt: bool = True, add_special_tokens: bool = True,
+                terminal: Optional[str] = None):
+    """A run from the request's prompt bytes: prompt.prepare through
+    ``preparer`` (a ``prompt.PromptPreparer`` of the bundle), then ``run`` with
+    the prompt text for prompt.prepare and the preparer's detokenize for
+    output.finalize.  Returns (trace, generated ids)."""
+    prep = preparer.prepare(prompt, add_generation_prompt=add_generation_prompt,
+                            add_special_tokens=add_special_tokens)
+    return run(backend, prep.prompt_token_ids, num_layers, max_new_tokens, prompt_text=prep.prompt_text,
+               temperature=temperature, detokenize=preparer.detokenize, terminal=terminal)
+
+
 class SeqBackend:
     """Backend over an rdet sequence (the CUDA path through the C ABI).  The
     model must be opened with layer_commitments=True (per-layer prefill

@@ -10,6 +10,8 @@ chat_template.jinja and tokenizer.json (jinja2 + tokenizers, the same render
 and encode calls as prompt_prepare/native/tiles.rs:48-86), and the text of the
 generated ids from tokenizer.decode(ids, skip_special_tokens=True)
 (output_finalize/native/tiles.rs:5-13); the generated ids come from the oracle.
+The bundle's chat_template.jinja and tokenizer.json are copied beside the
+output (tiny_gemma_dev_text/) for the prompt.prepare tests.
 Run where the reference checkout is available; the output is committed so that
 tests never read the reference at run time.
 
@@ -67,6 +69,13 @@ out = {
     "native-det-full": entries("native-det-full"),
     "native-det-terminal": entries("native-det-terminal"),
 }
+# the bundle's chat template and tokenizer, as text fixtures for the
+# prompt.prepare tests (tests/test_prompt.py)
+text_dir = os.path.join(HERE, "tiny_gemma_dev_text")
+os.makedirs(text_dir, exist_ok=True)
+for name in ("chat_template.jinja", "tokenizer.json"):
+    with open(os.path.join(bundle, name), "rb") as f_in, open(os.path.join(text_dir, name), "wb") as f_out:
+        f_out.write(f_in.read())
 dst = os.path.join(HERE, "det_trace_goldens.json")
 with open(dst, "w") as f:
     json.dump(out, f, indent=1)
