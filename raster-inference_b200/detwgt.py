@@ -75,24 +75,44 @@ def max_row_mass(shape, bits: np.ndarray) -> int:
     return int(a.sum(axis=1).max()) if a.size else 0
 
 
-def encode(tensors, policy: str = "auto") -> bytes:
-    """Encode ``[(name, shape, int32 array)]`` as a detwgt v2 artifact."""
-    out = bytearray()
-    out += MAGIC + struct.pack("<IIQ", FORMAT_VERSION, SPEC_VERSION, len(tensors))
-    for name, shape, bits in tensors:
+def write(f, tensors, count: int, policy: str = "auto") -> int:
+    """Stream ``count`` tensors ``(name, shape, int32 array)`` (any iterable,
+    consumed one at a time; a fourth element, when present, is the tensor's
+    max row mass already computed) to the binary file ``f`` as a detwgt v2
+    artifact; returns the bytes written."""
+    head = MAGIC + struct.pack("<IIQ", FORMAT_VERSION, SPEC_VERSION, count)
+    f.write(head)
+    written, n = len(head), 0
+    for item in tensors:
+        name, shape, bits = item[:3]
         bits = np.ascontiguousarray(bits, dtype=np.int32).ravel()
         if int(np.prod(shape)) != bits.size:
             raise ValueError(f"tensor `{name}` has {bits.size} values but shape product {int(np.prod(shape))}")
         fits16 = bits.size == 0 or (bits.min() >= -32768 and bits.max() <= 32767)
         width = 16 if (policy == "auto" and fits16) else 32
         nb = name.encode()
-        out += struct.pack("<I", len(nb)) + nb + struct.pack("<I", len(shape))
+        rec = bytearray(struct.pack("<I", len(nb)) + nb + struct.pack("<I", len(shape)))
         for d in shape:
-            out += struct.pack("<Q", int(d))
-        out += struct.pack("<QIQQ", bits.size, width, bits.size * width // 8, max_row_mass(shape, bits))
-        out += b"\0" * ((ALIGN - len(out) % ALIGN) % ALIGN)
-        out += (bits.astype("<i2") if width == 16 else bits.astype("<i4")).tobytes()
-    return bytes(out)
+            rec += struct.pack("<Q", int(d))
+        mass = item[3] if len(item) > 3 else max_row_mass(shape, bits)
+        rec += struct.pack("<QIQQ", bits.size, width, bits.size * width // 8, mass)
+        rec += b"\0" * ((ALIGN - (written + len(rec)) % ALIGN) % ALIGN)
+        f.write(rec)
+        payload = (bits.astype("<i2") if width == 16 else bits.astype("<i4")).tobytes()
+        f.write(payload)
+        written += len(rec) + len(payload)
+        n += 1
+    if n != count:
+        raise ValueError(f"{n} tensors written, {count} declared")
+    return written
+
+
+def encode(tensors, policy: str = "auto") -> bytes:
+    """Encode ``[(name, shape, int32 array)]`` as a detwgt v2 artifact."""
+    import io
+    buf = io.BytesIO()
+    write(buf, tensors, len(tensors), policy)
+    return buf.getvalue()
 
 
 def layer_shapes(cfg: dict):
