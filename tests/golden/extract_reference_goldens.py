@@ -11,7 +11,9 @@ import json
 import os
 import sys
 
-src = os.path.join(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", "testdata/det_commitment_goldens.json")
+if len(sys.argv) < 2:
+    sys.exit("usage: extract_reference_goldens.py <raster-inference checkout>")
+src = os.path.join(sys.argv[1], "testdata/det_commitment_goldens.json")
 with open(src) as f:
     g = json.load(f)
 out = {name: {"det": fx["det"]} for name, fx in g.items()}

@@ -28,7 +28,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(HERE, "..", ".."))
 sys.path.insert(0, os.path.join(HERE, ".."))
 
-ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) < 2:
+    sys.exit("usage: extract_trace_goldens.py <raster-inference checkout>")
+ref = sys.argv[1]
 bundle = os.path.join(ref, "assets/tiny-gemma-dev")
 PROMPT = "hello raster prompt"
 MAX_NEW = 2
