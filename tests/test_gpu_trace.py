@@ -36,6 +36,21 @@ def test_cuda_path_reproduces_native_det_full():
     assert [list(e) for e in tr.entries] == GOLD["native-det-full"]
 
 
+def test_cuda_path_from_prompt_text_reproduces_native_det_full():
+    # the request path: prompt bytes -> prompt.prepare (the bundle's chat
+    # template and tokenizer) -> the CUDA path -> output.finalize
+    prompt = importlib.import_module("raster-inference_b200.prompt")
+    d = tiny_gemma_dev.write_bundle(tempfile.mkdtemp(), detwgt.encode)
+    m = rdet.Model.open(d, max_prefill=32, layer_commitments=True)
+    seq = m.new_sequence(64)
+    tr, gen = trace.run_request(trace.SeqBackend(seq), prompt.PromptPreparer(os.path.join(HERE, "golden",
+                                                                                          "tiny_gemma_dev_text")),
+                                GOLD["prompt_text"].encode("utf-8"), num_layers=m.L,
+                                max_new_tokens=GOLD["max_new_tokens"], temperature=GOLD["temperature"])
+    assert gen == GOLD["generated_token_ids"]
+    assert [list(e) for e in tr.entries] == GOLD["native-det-full"]
+
+
 def test_cuda_path_reproduces_native_det_terminal():
     tr, _ = run_trace(terminal=GOLD["terminal"])
     assert [list(e) for e in tr.entries] == GOLD["native-det-terminal"]
