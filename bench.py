@@ -294,7 +294,24 @@ def run_kernel_case(args):
                                       out.data_ptr())
             torch.cuda.synchronize()
             rows = min(pos + 1, w) if w else pos + 1
-            print(f"attn {name}: heads {Hq}/{kv} head_dim {hd} rows {rows} kv_bytes {2 * kv * rows * hd * 4}")
+            line = f"attn {name}: heads {Hq}/{kv} head_dim {hd} rows {rows} kv_bytes {2 * kv * rows * hd * 4}"
+            if args.time_calls:
+                # per-call time of the allocating entry point (cluster kernel)
+                # and of the allocation-free one (split-phase kernels), CUDA
+                # events around back-to-back calls on the default stream
+                us = {}
+                for label, fn in (("alloc", rdet.det_attention_decode),
+                                  ("noalloc", rdet.det_attention_decode_noalloc)):
+                    fn(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), cap, Hq, kv, hd, pos, w, out.data_ptr())
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    for _ in range(args.time_calls):
+                        fn(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), cap, Hq, kv, hd, pos, w, out.data_ptr())
+                    e1.record()
+                    torch.cuda.synchronize()
+                    us[label] = 1000 * e0.elapsed_time(e1) / args.time_calls
+                line += f" us_per_call alloc {us['alloc']:.1f} noalloc {us['noalloc']:.1f}"
+            print(line)
 
 
 def run_ours(args, rank, world, local_rank):
@@ -543,6 +560,9 @@ def main():
     ap.add_argument("--batch-steps", type=int, default=8)
     ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc", "prefill"],
                     help="run a few launches of one kernel at E4B shapes for an ncu capture, then exit")
+    ap.add_argument("--time-calls", type=int, default=0,
+                    help="with --kernel-case attn: time this many back-to-back calls of each decode-attention entry "
+                         "point")
     ap.add_argument("--trace-case", action="store_true",
                     help="time a checkpoint-traced run (commitments on) against a plain one at --ctx, then exit")
     args = ap.parse_args()

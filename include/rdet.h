@@ -3,13 +3,16 @@
  *
  * C ABI of the drop-in CUDA executor for casettek/raster-inference's det
  * path.  A Rust executor `src/runtime/executors/cuda.rs` beside the
- * reference's `native.rs` binds these symbols.  Every
+ * reference's `native.rs` binds these symbols through a thin FFI.  Every
  * call returns an int32 status (RDET_OK or a negative RDET_E_* code); the
  * message of the last failure on the calling thread is available from
  * rdet_last_error().  No exception or panic crosses this boundary.  All
  * results are bit-exact with the reference det path (det_num spec v1).
  *
- * Threading: one host thread drives one context at a time.
+ * Threading: one host thread drives one context at a time.  The
+ * kernel-level entry points (rdet_det_gemv, rdet_det_linear,
+ * rdet_det_attention_decode) may be called from several host threads; their
+ * per-device scratch is handed out under a lock.
  */
 #ifndef RDET_H_
 #define RDET_H_
@@ -177,15 +180,17 @@ int32_t rdet_det_attention_decode(const int32_t* q, const int32_t* k_cache, cons
  * The first call on a device looks up the array's address on that device
  * (with that device current) and should come before any stream capture.  All
  * calls share the one array, which keeps the previous call's contents: calls
- * that overlap on the GPU (other streams, other host threads) race.  This
- * entry point has no counterpart in the reference. */
+ * that overlap on the GPU (other streams, other host threads) race.  The
+ * array's address is looked up once per device ordinal and kept: after
+ * cudaDeviceReset (or a release and re-creation of the device's primary
+ * context) the kept address is stale, so do not call this entry point in a
+ * process that resets the device after its first call.  This entry point has
+ * no counterpart in the reference. */
 int32_t rdet_det_attention_decode_noalloc(const int32_t* q, const int32_t* k_cache, const int32_t* v_cache,
                                           uint32_t cap, uint32_t num_heads, uint32_t num_kv_heads,
                                           uint32_t head_dim, uint32_t position, uint32_t window, int32_t* out,
                                           void* stream);
 
-/* The CUDA stream (cudaStream_t) on which the context launches all of its
- * work, for callers that order their own work or CUDA events against it. */
 /* Tensor-parallel batched decode (no counterpart in the reference, which runs
  * one process on the CPU).  Every rank
  * opens the same model on its own GPU; rank 0 creates an id with
@@ -208,6 +213,8 @@ int32_t rdet_tp_world(rdet_ctx* ctx); /* 1 when not sharded */
  * least one eligible weight), else 0.  Prompts shorter than 32 tokens use the
  * CUDA-core linear either way.  No counterpart in the reference. */
 int32_t rdet_tensor_core_prefill(rdet_ctx* ctx);
+/* The CUDA stream (cudaStream_t) on which the context launches all of its
+ * work, for callers that order their own work or CUDA events against it. */
 int32_t rdet_get_stream(rdet_ctx* ctx, void** stream);
 /* Number of kernels in one captured decode_transition (the sequence's decode
  * CUDA graph; captured on the first rdet_decode / rdet_generate). */

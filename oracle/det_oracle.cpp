@@ -405,17 +405,54 @@ static inline int64_t dot_row(const int32_t* x, const Tensor& w, size_t row_star
   return (int64_t)acc;
 }
 
+// dot_row for four consecutive token rows of X (row stride xs) at once, one
+// weight load per four products.
+static inline void dot_row4(const int32_t* x, size_t xs, const Tensor& w, size_t row_start, size_t col_off, size_t k,
+                            int64_t* out) {
+  uint64_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+  const int32_t *x0 = x, *x1 = x + xs, *x2 = x + 2 * xs, *x3 = x + 3 * xs;
+  if (w.width == 16) {
+    const int16_t* p = w.w16.data() + row_start + col_off;
+    for (size_t i = 0; i < k; ++i) {
+      int64_t v = p[i];
+      a0 += (uint64_t)((int64_t)x0[i] * v); a1 += (uint64_t)((int64_t)x1[i] * v);
+      a2 += (uint64_t)((int64_t)x2[i] * v); a3 += (uint64_t)((int64_t)x3[i] * v);
+    }
+  } else {
+    const int32_t* p = w.w32.data() + row_start + col_off;
+    for (size_t i = 0; i < k; ++i) {
+      int64_t v = p[i];
+      a0 += (uint64_t)((int64_t)x0[i] * v); a1 += (uint64_t)((int64_t)x1[i] * v);
+      a2 += (uint64_t)((int64_t)x2[i] * v); a3 += (uint64_t)((int64_t)x3[i] * v);
+    }
+  }
+  out[0] = (int64_t)a0; out[1] = (int64_t)a1; out[2] = (int64_t)a2; out[3] = (int64_t)a3;
+}
+
 // rows [row_off, row_off+n) and cols [col_off, col_off+k) of w; X is [S,k].
+// Every output is the reference's per-row dot product (det_kernels.rs:180-203
+// runs one det_linear_rows_into per token row); the work is only visited in
+// blocks of 64 weight rows x 16 token rows so that a block's weight rows stay
+// in cache while the block's tokens use them.  Wrapping sums are
+// order-independent, so the visiting order does not change any result.
 static void linear(const int32_t* X, size_t S, const Tensor& w, size_t row_off, size_t n, size_t col_off, size_t k,
                    int32_t* Y) {
   size_t cols = w.cols();
-  const size_t CH = 64;
-  size_t nch = (n + CH - 1) / CH;
-  parallel_for(S * nch, [&](size_t lo, size_t hi) {
+  const size_t RB = 64, SB = 16;
+  size_t nrb = (n + RB - 1) / RB, nsb = (S + SB - 1) / SB;
+  parallel_for(nrb * nsb, [&](size_t lo, size_t hi) {
     for (size_t it = lo; it < hi; ++it) {
-      size_t s = it / nch, c0 = (it % nch) * CH, c1 = std::min(n, c0 + CH);
-      for (size_t r = c0; r < c1; ++r)
-        Y[s * n + r] = requantize(dot_row(X + s * k, w, (row_off + r) * cols, col_off, k));
+      size_t r0 = (it / nsb) * RB, r1 = std::min(n, r0 + RB);
+      size_t s0 = (it % nsb) * SB, s1 = std::min(S, s0 + SB);
+      for (size_t r = r0; r < r1; ++r) {
+        size_t s = s0;
+        for (; s + 4 <= s1; s += 4) {
+          int64_t acc[4];
+          dot_row4(X + s * k, k, w, (row_off + r) * cols, col_off, k, acc);
+          for (int j = 0; j < 4; ++j) Y[(s + j) * n + r] = requantize(acc[j]);
+        }
+        for (; s < s1; ++s) Y[s * n + r] = requantize(dot_row(X + s * k, w, (row_off + r) * cols, col_off, k));
+      }
     }
   });
 }
@@ -726,11 +763,15 @@ static std::string vec_commitment(const int32_t* x, size_t n) {
   h.update_i32s(x, n);
   return h.hex();
 }
-static bool kv_commitment(const Seq& sq, std::string* out) {
+// build_det_kv_cache_commitment (transformer_kernels.rs:1460-1482) over the
+// caches of the first nl layers (all layers when nl is 0)
+static bool kv_commitment(const Seq& sq, std::string* out, size_t nl = 0) {
+  if (nl == 0 || nl > sq.caches.size()) nl = sq.caches.size();
   Sha256 h;
   h.update("raster-det-num-kv-cache-v1", 26);
-  h.update_u64(sq.caches.size());
-  for (const LayerCache& c : sq.caches) {
+  h.update_u64(nl);
+  for (size_t l = 0; l < nl; ++l) {
+    const LayerCache& c = sq.caches[l];
     if (!c.det) return false;
     h.update_u64(c.heads);
     for (int kind = 0; kind < 2; ++kind) {
@@ -998,6 +1039,13 @@ int dor_seq_fill_synthetic(const dor_model* h, dor_seq* sq, size_t ctx, uint64_t
 int dor_kv_commitment(const dor_seq* sq, char* out) {
   std::string hx;
   if (!kv_commitment(sq->s, &hx)) return 1;
+  put_hash(out, hx);
+  return 0;
+}
+// the commitment over the caches of layers [0, layers)
+int dor_kv_commitment_prefix(const dor_seq* sq, size_t layers, char* out) {
+  std::string hx;
+  if (!kv_commitment(sq->s, &hx, layers)) return 1;
   put_hash(out, hx);
   return 0;
 }

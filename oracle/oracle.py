@@ -78,6 +78,7 @@ def lib():
             "dor_decode": (C.c_int, [p, p, u32, p, p, p, C.c_char_p, sz]),
             "dor_seq_fill_synthetic": (C.c_int, [p, p, sz, C.c_uint64]),
             "dor_kv_commitment": (C.c_int, [p, C.c_char_p]),
+            "dor_kv_commitment_prefix": (C.c_int, [p, sz, C.c_char_p]),
             "dor_kv_read": (C.c_long, [p, C.c_int, C.c_int, C.c_int, p, sz]),
             "dor_argmax_first": (u32, [p, sz]),
             "dor_attention_one": (None, [p, p, p, sz, sz, p]),
@@ -279,9 +280,11 @@ class Seq:
     def fill_synthetic(self, ctx: int, seed: int = 1):
         lib().dor_seq_fill_synthetic(self.m._h, self._h, ctx, seed)
 
-    def kv_commitment(self):
+    def kv_commitment(self, layers: int | None = None):
+        """KV commitment over every layer's cache, or over layers [0, layers)."""
         out = C.create_string_buffer(65)
-        rc = lib().dor_kv_commitment(self._h, out)
+        rc = (lib().dor_kv_commitment(self._h, out) if layers is None else
+              lib().dor_kv_commitment_prefix(self._h, layers, out))
         return None if rc != 0 else out.value.decode()
 
     def kv_rows(self, layer: int, head: int, kind: int) -> np.ndarray | None:

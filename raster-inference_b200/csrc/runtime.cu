@@ -2070,6 +2070,10 @@ struct AttnScratchOwned {
   std::vector<void*> ptrs;
 };
 static std::map<int, AttnScratchOwned> g_attn_scratch;
+// held from the lookup (and any regrowth) of a device's scratch until the
+// kernel that uses it is enqueued, so two host threads never grow, free or
+// hand out one device's scratch at the same time
+static std::mutex g_attn_scratch_mu;
 // byte-plane scratch of the kernel-level tensor-core linear, per device
 struct LinScratch {
   void* p = nullptr;
@@ -2732,9 +2736,11 @@ int32_t rdet_det_attention_decode(const int32_t* q, const int32_t* k_cache, cons
     int dev = 0;
     CK(cudaGetDevice(&dev));
     int rows = attn_rows(position, window);
+    std::lock_guard<std::mutex> lk(g_attn_scratch_mu);
     AttnScratchOwned& o = g_attn_scratch[dev];
     if (o.heads < (int)num_heads || o.rows < rows || o.dim < (int)head_dim) {
-      for (void* p : o.ptrs) cudaFree(p);
+      if (!o.ptrs.empty()) CK(cudaDeviceSynchronize());  // earlier launches may still read the old scratch
+      for (void* p : o.ptrs) CK(cudaFree(p));
       o = AttnScratchOwned();
       o.heads = std::max<int>(num_heads, 8);
       o.rows = std::max(rows, 1024);
