@@ -47,6 +47,15 @@ def lcg_ids(n, vocab, seed):
     return out
 
 
+def load_fixtures():
+    """The CPU oracle's E4B-shape results (tests/golden/e4b_fixtures.json), or None."""
+    path = os.path.join(ROOT, "tests", "golden", "e4b_fixtures.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f)
+
+
 def load_config():
     with open(CONFIG_PATH) as f:
         return json.load(f)
@@ -132,7 +141,10 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU: the oracle (C++ restatement of the reference det path) on host cores
 # ---------------------------------------------------------------------------
-def cpu_decode_rate(cfg, ctx, steps, threads):
+def cpu_decode_rate(cfg, ctx, steps, threads, single_thread_steps=0):
+    """Greedy decode steps of the CPU oracle at context ctx (seeded synthetic
+    KV cache) on `threads` host threads, then `single_thread_steps` more on
+    one thread.  Returns (times, single-thread times, setup seconds)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O  # CPU baseline only
     O.set_threads(threads)
@@ -141,15 +153,92 @@ def cpu_decode_rate(cfg, ctx, steps, threads):
     s = m.seq()
     s.fill_synthetic(ctx, seed=7)
     setup = time.perf_counter() - t0
-    times = []
     tok = 1
-    for _ in range(steps):
-        t = time.perf_counter()
-        _, logits, _ = s.decode(tok, want_layer_hashes=False)
-        tok = O.argmax_first(logits)
-        times.append(time.perf_counter() - t)
+
+    def run(n):
+        nonlocal tok
+        out = []
+        for _ in range(n):
+            t = time.perf_counter()
+            _, logits, _ = s.decode(tok, want_layer_hashes=False)
+            tok = O.argmax_first(logits)
+            out.append(time.perf_counter() - t)
+        return out
+
+    times = run(steps)
+    single = []
+    if single_thread_steps:
+        O.set_threads(1)
+        single = run(single_thread_steps)
+        O.set_threads(threads)
     m.close()
-    return times, setup
+    return times, single, setup
+
+
+def config1_routines(rdet):
+    """the reference's tiny-gemma-dev bundle, a 16-token
+    prompt (LCG seed 0 over its 280-token vocabulary), prefill and 8 greedy
+    tokens, wall time per routine through the C ABI (host-synchronous calls)
+    and through the CPU oracle, tokens and commitments compared."""
+    import tempfile
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import tiny_gemma_dev  # fixture writer: regenerates the reference's bundle bytes
+    import oracle as O  # checker and CPU timing only
+    detwgt = importlib.import_module("raster-inference_b200.detwgt")
+    d = tiny_gemma_dev.write_bundle(tempfile.mkdtemp(prefix="rdet-c1-"), detwgt.encode)
+    ids = tiny_gemma_dev.lcg_token_ids(16, 280, 0)
+    out = {"prompt_tokens": 16, "new_tokens": 8}
+    m = rdet.Model.open(d, max_prefill=16)
+    res = {}
+    for rep in range(2):  # the first pass warms up
+        t = {"input.embedding": 0.0, "prefill": 0.0, "select_output_token": 0.0, "decode_transition": 0.0}
+        s = m.new_sequence(32)
+        c0 = time.perf_counter()
+        m.embed(ids)
+        t["input.embedding"] = time.perf_counter() - c0
+        c0 = time.perf_counter()
+        s.prefill(ids)
+        t["prefill"] = time.perf_counter() - c0
+        toks = []
+        for _ in range(8):
+            c0 = time.perf_counter()
+            tok = s.select()
+            t["select_output_token"] += (time.perf_counter() - c0) / 8
+            toks.append(tok)
+            c0 = time.perf_counter()
+            s.decode(tok)
+            t["decode_transition"] += (time.perf_counter() - c0) / 8
+        res = {"ms": {k: round(1000 * v, 4) for k, v in t.items()}, "tokens": toks,
+               "kv": s.commitment(rdet.BUF_KV), "logits": s.commitment(rdet.BUF_LOGITS)}
+        s.free()
+    m.close()
+    om = O.Model(d, threads=1)
+    t = {"input.embedding": 0.0, "prefill": 0.0, "select_output_token": 0.0, "decode_transition": 0.0}
+    os_ = om.seq()
+    c0 = time.perf_counter()
+    om.embed(ids)
+    t["input.embedding"] = time.perf_counter() - c0
+    c0 = time.perf_counter()
+    _, logits, _ = os_.prefill(ids, want_layer_hashes=False)
+    t["prefill"] = time.perf_counter() - c0
+    ctoks = []
+    for _ in range(8):
+        c0 = time.perf_counter()
+        tok = O.argmax_first(logits)
+        t["select_output_token"] += (time.perf_counter() - c0) / 8
+        ctoks.append(tok)
+        c0 = time.perf_counter()
+        _, logits, _ = os_.decode(tok, want_layer_hashes=False)
+        t["decode_transition"] += (time.perf_counter() - c0) / 8
+    out["gpu_ms_per_routine"] = res["ms"]
+    out["cpu_ms_per_routine"] = {k: round(1000 * v, 4) for k, v in t.items()}
+    out["cpu_threads"] = 1
+    out["bit_exact_vs_cpu"] = (res["tokens"] == ctoks and res["kv"] == os_.kv_commitment() and
+                               res["logits"] == O.vec_commitment(logits))
+    out["tokens"] = res["tokens"]
+    om.close()
+    return out
 
 
 def run_reference(args, rank):
@@ -157,7 +246,7 @@ def run_reference(args, rank):
         return  # the CPU arm runs on rank 0 only
     cfg = load_config()
     cores = host_cores()
-    times, _ = cpu_decode_rate(cfg, args.ctx, args.warmup + args.steps, cores)
+    times, _, _ = cpu_decode_rate(cfg, args.ctx, args.warmup + args.steps, cores)
     timed = times[args.warmup:]
     total = sum(timed)
     value = len(timed) / total
@@ -188,7 +277,30 @@ def e4b_gemv_shapes(cfg):
             "ple_model_proj": (L * P, H), "lm_head": (V, H)}
 
 
-def gemv_roofline(torch, rdet, cfg, device, copies=8, rounds=3):
+def decode_step_bytes(cfg, ctx):
+    """Algorithmic HBM bytes of one decode step at context ctx: every weight a
+    decode GEMV streams (i16; the KV-sharing layers' unused k/v projections
+    excluded), the KV rows each layer's attention reads and the rows it
+    appends, the PLE model projection and lm_head."""
+    t = cfg["text_config"]
+    H, F, Hq, kv, d, dg, V, P, L, W = (t["hidden_size"], t["intermediate_size"], t["num_attention_heads"],
+                                       t["num_key_value_heads"], t["head_dim"], t["global_head_dim"],
+                                       t["vocab_size"], t["hidden_size_per_layer_input"], t["num_hidden_layers"],
+                                       t["sliding_window"])
+    shared = t.get("num_kv_shared_layers") or 0
+    total = L * P * H * 2 + V * H * 2
+    for l, lt in enumerate(t["layer_types"]):
+        sliding = lt == "sliding_attention"
+        hd = d if sliding else dg
+        rows = min(ctx, W) if sliding else ctx
+        total += (Hq * hd * H + H * Hq * hd + 3 * F * H + 2 * P * H) * 2
+        total += 2 * kv * hd * rows * 4
+        if l < L - shared:
+            total += 2 * kv * hd * H * 2 + 2 * kv * hd * 4
+    return total
+
+
+def gemv_roofline(torch, rdet, cfg, device, copies=8, rounds=3, check=False):
     """det-GEMV (gemv3_kernel) at the E4B projection shapes.  For each shape,
     `copies` launches over distinct weight copies run back to back on one
     stream (as inside the decode step) between two CUDA events on that
@@ -199,8 +311,9 @@ def gemv_roofline(torch, rdet, cfg, device, copies=8, rounds=3):
     dev = f"cuda:{device}"
     mats = {k: [torch.randint(-32768, 32768, s, dtype=torch.int16, device=dev, generator=g)
                 for _ in range(copies if k != "lm_head" else 2)] for k, s in shapes.items()}
-    xs = {k: torch.randint(-(1 << 20), 1 << 20, (s[1],), dtype=torch.int32, device=dev, generator=g)
-          for k, s in shapes.items()}
+    # activations: N(0, 1) quantized with f32_to_act
+    detwgt = importlib.import_module("raster-inference_b200.detwgt")
+    xs = {k: torch.from_numpy(detwgt.normal_acts(s[1], 1000 + n)).to(dev) for n, (k, s) in enumerate(shapes.items())}
     ys = {k: torch.empty(s[0], dtype=torch.int32, device=dev) for k, s in shapes.items()}
     stream = torch.cuda.Stream(device=device)
     per = {k: [] for k in shapes}
@@ -215,6 +328,20 @@ def gemv_roofline(torch, rdet, cfg, device, copies=8, rounds=3):
                 if r >= 1:
                     per[k].append((e0, e1, len(mats[k])))
     stream.synchronize()
+    # bit check of every output row of the first weight copy against the CPU
+    # det GEMV (outside the timed region)
+    bit_exact = None
+    if check:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O  # checker only
+        bit_exact = True
+        for k, (n, kk) in shapes.items():
+            with torch.cuda.stream(stream):
+                rdet.det_gemv(xs[k].data_ptr(), mats[k][0].data_ptr(), 16, n, kk, ys[k].data_ptr(),
+                              stream.cuda_stream)
+            stream.synchronize()
+            if not (ys[k].cpu().numpy() == O.gemv(xs[k].cpu().numpy(), mats[k][0].cpu().numpy())).all():
+                bit_exact = False
     out, tot_b, tot_t = {}, 0.0, 0.0
     for k, (n, kk) in shapes.items():
         ms = statistics.mean(a.elapsed_time(b) / c for a, b, c in per[k])
@@ -222,7 +349,7 @@ def gemv_roofline(torch, rdet, cfg, device, copies=8, rounds=3):
         out[k] = {"rows": n, "cols": kk, "us": ms * 1000, "gbs": b / (ms * 1e-3) / 1e9}
         tot_b += b
         tot_t += ms * 1e-3
-    return out, tot_b / tot_t / 1e9, tot_b / len(shapes), tot_t / len(shapes)
+    return out, tot_b / tot_t / 1e9, tot_b / len(shapes), tot_t / len(shapes), bit_exact
 
 
 def run_kernel_case(args):
@@ -331,15 +458,23 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.ExternalStream(model.stream, device=f"cuda:{local_rank}")
     seq = model.new_sequence(ctx + args.warmup + args.steps + 64)
     ids = lcg_ids(ctx, t["vocab_size"], SEED + rank)
-    # prefill of the 4096-token prompt (timed for the prefill field)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
+    # prefill of the 4096-token prompt (the prefill field: median of three
+    # prefills on fresh sequences after one untimed prefill)
+    prefill_runs = []
+    for rep in range(4):
+        ps = model.new_sequence(ctx + 8)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ps.prefill(ids)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if rep:
+            prefill_runs.append(e0.elapsed_time(e1) / 1000)
+        ps.free()
+    prefill_s = statistics.median(prefill_runs)
     seq.prefill(ids)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    prefill_s = e0.elapsed_time(e1) / 1000
     # warm-up (captures the decode graph)
-    seq.generate(args.warmup)
+    warm_toks = seq.generate(args.warmup)
     kernels_per_step = seq.kernels_per_step() + 2  # + the two argmax kernels of select
     if dist:
         dist.barrier()
@@ -374,6 +509,30 @@ def run_ours(args, rank, world, local_rank):
         e2e_sec = float(tt[0])
     e2e = {"value": world * n_e2e / e2e_sec, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
            "steps": n_e2e}
+    # BASELINE config 4 as stated: the 4096-token prompt, then 256 greedy
+    # tokens (device-timed generation) checked against the CPU oracle's tokens
+    config4 = None
+    if args.config4_tokens > 0:
+        c4 = model.new_sequence(ctx + args.config4_tokens + 8)
+        c4.prefill(lcg_ids(ctx, t["vocab_size"], SEED))
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        c4_toks = c4.generate(args.config4_tokens)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        c4_sec = g0.elapsed_time(g1) / 1000
+        fx = load_fixtures()
+        exact = None
+        if fx and "config4" in fx and ctx == fx["config4"]["prompt_tokens"]:
+            ref = fx["config4"]["tokens"]
+            n4 = min(len(ref), len(c4_toks))
+            exact = c4_toks[:n4] == ref[:n4] and (warm_toks + toks == ref[:args.warmup + len(toks)]
+                                                  if rank == 0 else True)
+        config4 = {"prompt_tokens": ctx, "tokens": args.config4_tokens, "tok_s": args.config4_tokens / c4_sec,
+                   "ms_per_token": 1000 * c4_sec / args.config4_tokens, "bit_exact_vs_cpu": exact,
+                   "note": "one rdet_generate of all tokens after a fresh prefill; tokens compared with the CPU "
+                           "oracle's (tests/golden/e4b_fixtures.json), as are the timed steps' tokens"}
+        c4.free()
     # prefill of one seeded uniform prompt of 512 and of
     # 2048 tokens through all layers (device-timed, kernels already warm)
     # (median of three prefills of the same prompt, each on a fresh sequence)
@@ -392,8 +551,9 @@ def run_ours(args, rank, world, local_rank):
             ps.free()
         psec = statistics.median(runs)
         prefill_lengths[str(plen)] = {"tok_s": plen / psec, "seconds": psec, "runs": 3}
-    # batched ragged decode (BASELINE config 5 shape): 64 sequences, prompt
-    # lengths 128 + draw % 3969 (seeded), one batched decode_transition per step
+    # batched ragged decode: 64 sequences, prompt lengths
+    # 128 + draw % 3969 (seeded), greedy: one batched decode_transition per
+    # step, then select_output_token for every sequence
     batched = None
     if args.batch > 0:
         bm, bstream = model, stream  # max_prefill (the context) >= the batch rows
@@ -405,37 +565,49 @@ def run_ours(args, rank, world, local_rank):
             dist.broadcast_object_list(uid, src=0)
             bm.tp_init(rank, world, uid[0])
         lens = [128 + (x % 3969) for x in lcg_ids(args.batch, 1 << 30, SEED + 7)]
-        seqs = [bm.new_sequence(n + args.batch_steps + 8) for n in lens]
+        nsteps = args.batch_steps
+        seqs = [bm.new_sequence(n + nsteps + 8) for n in lens]
         for i, (sq, n) in enumerate(zip(seqs, lens)):
             sq.prefill(lcg_ids(n, t["vocab_size"], SEED + 100 + i))
         toks = [sq.select() for sq in seqs]
-        for _ in range(2):  # warm-up
-            rdet.decode_batch(bm, seqs, toks)
-            toks = [sq.select() for sq in seqs]
+        gen = [[] for _ in seqs]
+        step_ms = []
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
-        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        b0.record(bstream)
-        for _ in range(args.batch_steps):
+        for step in range(nsteps):
+            for i, tk in enumerate(toks):
+                gen[i].append(tk)
+            b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            b0.record(bstream)
             rdet.decode_batch(bm, seqs, toks)
-        b1.record(bstream)
-        torch.cuda.synchronize()
-        bsec = b0.elapsed_time(b1) / 1000
+            b1.record(bstream)
+            toks = [sq.select() for sq in seqs]  # synchronizes
+            step_ms.append(b0.elapsed_time(b1))
+        timed = step_ms[3:] if len(step_ms) > 6 else step_ms  # the first steps warm up
+        bsec = sum(timed) / 1000
         if dist:
             tt = torch.tensor([bsec], dtype=torch.float64, device=f"cuda:{local_rank}")
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             bsec = float(tt[0])
+        exact = None
+        fx = load_fixtures()
+        if fx and "config5" in fx and nsteps >= fx["config5"]["tokens_per_sequence"] and args.batch == fx["config5"]["batch"]:
+            n5 = fx["config5"]["tokens_per_sequence"]
+            exact = all(gen[int(k)][:n5] == r["tokens"] for k, r in fx["config5"]["sequences"].items())
         batched = {"sequences": args.batch, "context": f"128 + draw mod 3969 (seeded), mean {sum(lens) // len(lens)}",
                    "parallelism": f"tp{world}" if tp else "single", "scaling": "strong" if tp else None,
-                   "steps": args.batch_steps, "tok_s": args.batch * args.batch_steps / bsec,
-                   "ms_per_step": 1000 * bsec / args.batch_steps,
-                   "note": "device-timed batched decode_transition (same token fed back: decode cost does not depend "
-                           "on token values)"}
+                   "steps": nsteps, "timed_steps": len(timed), "tok_s": args.batch * len(timed) / bsec,
+                   "ms_per_step": 1000 * bsec / len(timed),
+                   "bit_exact_vs_cpu": exact,
+                   "note": "greedy: device-timed batched decode_transition per step, select_output_token per "
+                           "sequence between steps (not timed); the first 3 steps are warm-up; bit_exact_vs_cpu "
+                           "checks the CPU oracle's 4-sequence subset (tests/golden/e4b_fixtures.json)"}
         for sq in seqs:
             sq.free()
     # roofline of the dominant kernel (det GEMV)
-    per, gbs, bytes_per_launch, sec_per_launch = gemv_roofline(torch, rdet, cfg, local_rank)
+    per, gbs, bytes_per_launch, sec_per_launch, gemv_exact = gemv_roofline(torch, rdet, cfg, local_rank,
+                                                                            check=(rank == 0))
     peak, peak_kind = peaks()
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "gemv_traffic.json")
@@ -445,6 +617,9 @@ def run_ours(args, rank, world, local_rank):
         if ratio:
             traffic = ratio * bytes_per_launch
     weight_bytes = model.weight_bytes
+    step_bytes = decode_step_bytes(cfg, ctx)
+    step_frac = {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (sec / args.steps) / 1e9,
+                 "frac": step_bytes / (sec / args.steps) / 1e9 / peaks()[0]}
     if dist:
         dist.barrier()
     if rank != 0:
@@ -464,6 +639,7 @@ def run_ours(args, rank, world, local_rank):
                    "weight_bytes_hbm": weight_bytes},
         "prefill": {"tokens": ctx, "tok_s": ctx / prefill_s, "seconds": prefill_s},
         "prefill_config3": prefill_lengths,
+        "config4": config4,
         "e2e": e2e,
         "batched_decode": batched,
         "gpu_launches": kernels_per_step * args.steps,
@@ -471,15 +647,24 @@ def run_ours(args, rank, world, local_rank):
                      "unit": "GB/s", "frac": gbs / peak, "peak_kind": peak_kind,
                      "traffic": traffic, "algorithmic_bytes_per_launch": bytes_per_launch,
                      "us_per_launch": sec_per_launch * 1e6,
-                     "per_shape_gbs": {k: round(v["gbs"], 1) for k, v in per.items()}},
+                     "per_shape_gbs": {k: round(v["gbs"], 1) for k, v in per.items()},
+                     "per_shape_frac": {k: round(v["gbs"] / peak, 3) for k, v in per.items()},
+                     "step_frac": step_frac,
+                     "activations": "N(0,1) quantized with f32_to_act (config 2)",
+                     "bit_exact_vs_cpu": gemv_exact},
         "clocks": clk.summary(),
     }
+    if world == 1:
+        line["config1"] = config1_routines(rdet)
     if world == 1 and not args.no_cpu_baseline:
         cores = host_cores()
-        times, _ = cpu_decode_rate(cfg, ctx, 2, cores)
-        line["cpu_baseline"] = {"value": 1.0 / times[-1], "unit": "tok/s", "cores": cores, "kind": "port",
-                                "sample": f"1 greedy decode step (after 1 warm-up) at context {ctx}, seeded synthetic "
-                                          f"KV cache, E4B stand-in, {cores} threads, {cpu_model()}"}
+        times, single, _ = cpu_decode_rate(cfg, ctx, 4, cores, single_thread_steps=3)
+        line["cpu_baseline"] = {"value": 3 / sum(times[1:]), "unit": "tok/s", "cores": cores, "kind": "port",
+                                "sample": f"3 greedy decode steps (after 1 warm-up) at context {ctx}, seeded synthetic "
+                                          f"KV cache, E4B stand-in, {cores} threads, {cpu_model()}",
+                                "single_thread": {"value": len(single) / sum(single), "unit": "tok/s", "cores": 1,
+                                                  "sample": f"{len(single)} greedy decode steps on one thread, same "
+                                                            f"model and cache"}}
     print(json.dumps(line), flush=True)
     seq.free()
     model.close()
@@ -556,8 +741,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config4-tokens", type=int, default=256, help="greedy tokens of the config-4 line (0: skip)")
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched ragged decode line (0: skip)")
-    ap.add_argument("--batch-steps", type=int, default=8)
+    ap.add_argument("--batch-steps", type=int, default=128, help="greedy steps of the batched line (config 5: 128)")
     ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc", "prefill"],
                     help="run a few launches of one kernel at E4B shapes for an ncu capture, then exit")
     ap.add_argument("--time-calls", type=int, default=0,

@@ -168,6 +168,21 @@ int32_t rdet_det_attention_decode(const int32_t* q, const int32_t* k_cache, cons
                                   uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim, uint32_t position,
                                   uint32_t window, int32_t* out, void* stream);
 
+/* det prefill attention of n_tokens prompt positions for every query head
+ * (det_attention_prefill, det_kernels.rs:525-671): q [n_tokens, num_heads,
+ * head_dim] holds the normed, rotated queries; k_cache / v_cache [num_kv_heads,
+ * cap, head_dim] hold the prompt's keys and values in rows [0, n_tokens);
+ * query i attends to keys [max(0, i + 1 - window), i] (window 0 = causal over
+ * the whole prompt); out [n_tokens, num_heads, head_dim].  Runs on the tcgen05
+ * tensor cores when head_dim is a multiple of 64 and num_heads / num_kv_heads
+ * divides 128 (flags RDET_FLAG_NO_TENSOR_CORES forces the CUDA-core kernel);
+ * the result is the same either way.  Scratch memory is allocated by the
+ * library on first use per device and grown as needed.  stream: cudaStream_t
+ * or NULL. */
+int32_t rdet_det_attention_prefill(const int32_t* q, const int32_t* k_cache, const int32_t* v_cache, uint32_t cap,
+                                   uint32_t n_tokens, uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
+                                   uint32_t window, uint32_t flags, int32_t* out, void* stream);
+
 /* Decode attention that allocates nothing.  Same arguments and the same
  * bit-exact result as rdet_det_attention_decode, for callers that cannot
  * allocate device memory while they run: a serving process that hands all of

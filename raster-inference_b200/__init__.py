@@ -38,7 +38,7 @@ SYMBOLS = [
     "rdet_prefill_finalize", "rdet_select", "rdet_decode", "rdet_decode_begin", "rdet_decode_range",
     "rdet_decode_finalize", "rdet_generate", "rdet_read", "rdet_commitment", "rdet_kv_prefix_commitments",
     "rdet_det_gemv", "rdet_det_linear",
-    "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_get_stream", "rdet_tensor_core_prefill", "rdet_nccl_unique_id", "rdet_tp_init", "rdet_tp_world", "rdet_seq_kernels_per_step", "rdet_last_error",
+    "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_det_attention_prefill", "rdet_get_stream", "rdet_tensor_core_prefill", "rdet_nccl_unique_id", "rdet_tp_init", "rdet_tp_world", "rdet_seq_kernels_per_step", "rdet_last_error",
     "rdet_version",
 ]
 
@@ -98,6 +98,7 @@ def lib() -> C.CDLL:
         "rdet_det_linear": [p, u32, p, i32, u32, u32, p, p],
         "rdet_det_attention_decode": [p, p, p, u32, u32, u32, u32, u32, u32, p, p],
         "rdet_det_attention_decode_noalloc": [p, p, p, u32, u32, u32, u32, u32, u32, p, p],
+        "rdet_det_attention_prefill": [p, p, p, u32, u32, u32, u32, u32, u32, u32, p, p],
         "rdet_get_stream": [p, p],
         "rdet_tensor_core_prefill": [p],
         "rdet_nccl_unique_id": [p, sz],
@@ -361,6 +362,17 @@ def det_attention_decode(q_ptr: int, k_ptr: int, v_ptr: int, cap: int, num_heads
     _check(lib().rdet_det_attention_decode(C.c_void_p(q_ptr), C.c_void_p(k_ptr), C.c_void_p(v_ptr), cap, num_heads,
                                            num_kv_heads, head_dim, position, window, C.c_void_p(out_ptr),
                                            C.c_void_p(stream) if stream else None))
+
+
+def det_attention_prefill(q_ptr: int, k_ptr: int, v_ptr: int, cap: int, n_tokens: int, num_heads: int,
+                          num_kv_heads: int, head_dim: int, window: int, out_ptr: int, tensor_cores: bool = True,
+                          stream: int = 0):
+    """Prefill attention of a prompt on caller-owned device memory
+    (rdet_det_attention_prefill); tensor_cores=False forces the CUDA-core kernel."""
+    _check(lib().rdet_det_attention_prefill(C.c_void_p(q_ptr), C.c_void_p(k_ptr), C.c_void_p(v_ptr), cap, n_tokens,
+                                            num_heads, num_kv_heads, head_dim, window,
+                                            0 if tensor_cores else FLAG_NO_TENSOR_CORES, C.c_void_p(out_ptr),
+                                            C.c_void_p(stream) if stream else None))
 
 
 def det_attention_decode_noalloc(q_ptr: int, k_ptr: int, v_ptr: int, cap: int, num_heads: int, num_kv_heads: int,

@@ -551,6 +551,7 @@ void kernels_init() {
   stream_set_attrs();
   attn_cluster_init();
   tc_init();
+  tc_attn_init();
   if ((size_t)dev >= done.size()) done.resize(dev + 1, 0);
   done[dev] = 1;
 }
@@ -562,7 +563,7 @@ int stream_error_flag(bool reset) {
     int z = 0;
     cudaMemcpyToSymbol(g_stream_err, &z, sizeof(int));
   }
-  return v | tc_error_flag(reset);
+  return v | tc_error_flag(reset) | tc_attn_error_flag(reset);
 }
 
 // Plans and launches the streamed GEMV; returns false when the launch does not
@@ -1225,7 +1226,9 @@ __global__ void attn_dec_scores(const AttnDecodeArgs a) {
     for (int g = 0; g < G; ++g) {
       int32_t sc = requantize(warp_sum64(acc[g]));
       if (lane == 0) a.sc.scores[(size_t)(kvh * G + g) * a.sc.stride + j] = sc;
-      if (sc > bm[g]) { bm[g] = sc; bi[g] = j; }  // j increases: first max kept
+      // j increases: the first max is kept (a row whose scores all equal
+      // INT32_MIN takes its first row)
+      if (sc > bm[g] || bi[g] == INT32_MAX) { bm[g] = sc; bi[g] = j; }
     }
   }
   if (lane == 0)
@@ -1665,7 +1668,7 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
         const int j = r0 + i;
         const int32_t v = requantize(tot);
         sc[own_g * rmax + j] = v;
-        if (v > bm) { bm = v; bi = lo + j; }  // a lane's rows ascend: the first max is kept
+        if (v > bm || bi == INT32_MAX) { bm = v; bi = lo + j; }  // a lane's rows ascend: the first max is kept
       }
     }
     __syncthreads();
@@ -2053,7 +2056,7 @@ __global__ void attn_prefill_kernel(const AttnPrefillArgs a, int rowlen) {
     for (int t = lane; t < d; t += 32) acc = mac_wide(acc, kr[t], qs[t]);
     int32_t v = requantize(warp_sum64(acc));
     if (lane == 0) sc[j] = v;
-    if (v > bm) { bm = v; bi = j; }
+    if (v > bm || bi == INT32_MAX) { bm = v; bi = j; }
   }
   if (lane == 0) { wm[warp] = bm; wi[warp] = bi; }
   __syncthreads();
@@ -2182,7 +2185,7 @@ __global__ void __launch_bounds__(32 * AP_R / RPW, RPW == 8 ? 2 : 1) attn_prefil
       if (j < st || j > i) continue;
       int32_t sc = requantize(acc[t]);
       a.scores[((size_t)row_head(r) * a.S + i) * rowlen + (j - st)] = sc;
-      if (sc > bm[t]) { bm[t] = sc; bi[t] = j; }
+      if (sc > bm[t] || bi[t] == INT32_MAX) { bm[t] = sc; bi[t] = j; }
     }
   }
 #pragma unroll

@@ -264,6 +264,17 @@ struct AttnPrefillArgs {
   int64_t scratch_elems = 0;
 };
 void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t s);
+// The same attention on the tcgen05 tensor cores (tc_attn.cu): exact byte-limb
+// products for q k^T and for the weighted values, the exact softmax on the CUDA
+// cores between them.  Eligible when head_dim is a multiple of 64, the query
+// heads per KV head divide 128 and S <= 32768.  Workspace: tc_attn_ws_bytes
+// (0 when not eligible).  Returns false, launching nothing, when the shape,
+// alignment or workspace does not qualify.
+size_t tc_attn_ws_bytes(int S, int Hq, int Hkv, int d);
+bool tc_attn_eligible(int S, int Hq, int Hkv, int d);
+bool launch_attn_prefill_tc(const AttnPrefillArgs& a, void* ws, size_t ws_bytes, cudaStream_t s);
+void tc_attn_init();                 // per-device kernel attributes (called by kernels_init)
+int tc_attn_error_flag(bool reset);  // nonzero when one of its pipeline waits gave up
 
 // ---- embedding / PLE / logits ------------------------------------------------------
 void launch_embed(const uint32_t* ids, int32_t S, const DevMat& emb, int32_t scale, int32_t* out, int32_t* err,

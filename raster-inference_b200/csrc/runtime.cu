@@ -525,6 +525,8 @@ struct Ctx {
   int tc_act_k = 0;              // largest K the activation planes hold
   void* tc_split = nullptr;      // split-K partial sums of the tensor-core linear
   size_t tc_split_bytes = 0;
+  void* ta_ws = nullptr;         // workspace of the tensor-core prefill attention
+  size_t ta_ws_bytes = 0;
   // batched decode: per-row tables (device) and the batch logits
   struct {
     int rows = 0;                  // rows the tables hold
@@ -833,6 +835,11 @@ constexpr size_t kTcSplitScratch = 64ull << 20;  // split-K partials for short r
 static void prepare_tensor_cores(Ctx& c) {
   if ((c.flags & RDET_FLAG_NO_TENSOR_CORES) || !tc_supported()) return;
   const ModelCfg& m = c.cfg;
+  // prefill attention on the tensor cores: one workspace sized for the
+  // largest eligible layer shape at max_prefill tokens
+  for (const LayerDev& L : c.layers)
+    c.ta_ws_bytes = std::max(c.ta_ws_bytes, tc_attn_ws_bytes((int)c.max_prefill, m.Hq, L.cfg.kv_heads, L.cfg.head_dim));
+  if (c.ta_ws_bytes) c.ta_ws = c.dalloc(c.ta_ws_bytes);
   int kmax = 0;
   auto prep = [&](TcWeight& t, const DevMat& w, const DevMat* u = nullptr) {
     if (!w.p || !tc_weight_eligible(w) || (u && (!u->p || !tc_weight_eligible(*u) || u->rows != w.rows ||
@@ -1166,7 +1173,7 @@ static void prefill_layer(Ctx& c, Seq& q, int l) {
   aa.S = S; aa.Hq = m.Hq; aa.Hkv = lc.kv_heads; aa.d = d; aa.window = lc.window; aa.q = w.qo;
   aa.k_cache = kcache; aa.v_cache = vcache; aa.cap = q.cap; aa.out = w.comb; aa.scores = w.scores; aa.exps = w.exps;
   aa.scratch_elems = w.scratch_elems;
-  launch_attn_prefill(aa, s);
+  if (!(c.ta_ws && launch_attn_prefill_tc(aa, c.ta_ws, c.ta_ws_bytes, s))) launch_attn_prefill(aa, s);
   prefill_linear(c, w.comb, S, L.o, L.to, w.attn, kEpiPlain, nullptr);
   bool ple = m.P > 0;
   // t1 = xs + norm(attn)  -> other
@@ -2081,6 +2088,9 @@ struct LinScratch {
 };
 static std::map<int, LinScratch> g_lin_scratch;
 static std::mutex g_lin_scratch_mu;
+// scratch of the kernel-level prefill attention, per device (same rules)
+static std::map<int, LinScratch> g_pattn_scratch;
+static std::mutex g_pattn_scratch_mu;
 
 static void attn_entry_args(AttnDecodeArgs& a, const int32_t* q, const int32_t* k_cache, const int32_t* v_cache,
                             uint32_t cap, uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
@@ -2798,6 +2808,62 @@ int32_t rdet_det_attention_decode_noalloc(const int32_t* q, const int32_t* k_cac
     a.sc.max_splits = (rows + kNoAllocRowsPerSplit - 1) / kNoAllocRowsPerSplit;
     a.sc.stride = kNoAllocMaxRows;
     launch_attn_decode(a, static_cast<cudaStream_t>(stream));
+    CK(cudaGetLastError());
+  });
+}
+
+int32_t rdet_det_attention_prefill(const int32_t* q, const int32_t* k_cache, const int32_t* v_cache, uint32_t cap,
+                                   uint32_t n_tokens, uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
+                                   uint32_t window, uint32_t flags, int32_t* out, void* stream) {
+  return guard([&] {
+    kernels_init();
+    REQUIRE(q && k_cache && v_cache && out, RDET_E_INVALID, "null argument");
+    REQUIRE(n_tokens > 0 && n_tokens <= cap, RDET_E_RANGE, "n_tokens must be in [1, cap]");
+    REQUIRE(num_kv_heads > 0 && num_heads % num_kv_heads == 0, RDET_E_INVALID,
+            "num_heads must be a multiple of num_kv_heads");
+    REQUIRE(head_dim > 0 && head_dim <= 512 && head_dim % 4 == 0, RDET_E_RANGE,
+            "head_dim must be a multiple of 4, at most 512");
+    REQUIRE((((uintptr_t)q | (uintptr_t)k_cache | (uintptr_t)v_cache | (uintptr_t)out) & 15) == 0, RDET_E_INVALID,
+            "q, caches and out must be 16-byte aligned");
+    AttnPrefillArgs a;
+    a.S = (int)n_tokens;
+    a.Hq = (int)num_heads;
+    a.Hkv = (int)num_kv_heads;
+    a.d = (int)head_dim;
+    a.window = (int)window;
+    a.q = q;
+    a.k_cache = k_cache;
+    a.v_cache = v_cache;
+    a.cap = (int)cap;
+    a.out = out;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool tc = !(flags & RDET_FLAG_NO_TENSOR_CORES) &&
+                    tc_attn_eligible(a.S, a.Hq, a.Hkv, a.d);
+    const int rowlen = a.window > 0 ? std::min(a.window, a.S) : a.S;
+    const size_t cuda_elems = (size_t)a.Hq * a.S * rowlen;
+    const size_t need = tc ? tc_attn_ws_bytes(a.S, a.Hq, a.Hkv, a.d) : cuda_elems * 12 + 256;
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(g_pattn_scratch_mu);
+    LinScratch& sc = g_pattn_scratch[dev];
+    if (sc.bytes < need) {
+      if (sc.p) {
+        CK(cudaDeviceSynchronize());  // earlier launches may still read the old scratch
+        CK(cudaFree(sc.p));
+        sc.p = nullptr;
+        sc.bytes = 0;
+      }
+      CK(cudaMalloc(&sc.p, need));
+      sc.bytes = need;
+    }
+    if (tc) {
+      REQUIRE(launch_attn_prefill_tc(a, sc.p, sc.bytes, s), RDET_E_CUDA, "tensor-core attention launch failed");
+    } else {
+      a.scores = static_cast<int32_t*>(sc.p);
+      a.exps = reinterpret_cast<int64_t*>(static_cast<unsigned char*>(sc.p) + ((cuda_elems * 4 + 255) & ~(size_t)255));
+      a.scratch_elems = (int64_t)cuda_elems;
+      launch_attn_prefill(a, s);
+    }
     CK(cudaGetLastError());
   });
 }

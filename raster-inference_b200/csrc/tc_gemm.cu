@@ -40,6 +40,7 @@
 
 #include "det_dev.cuh"
 #include "kernels.h"
+#include "tc_ptx.cuh"
 
 namespace rdet {
 
@@ -63,65 +64,12 @@ constexpr int kTcEpiWarps = 8;  // two per TMEM lane quarter, each half of the c
 constexpr int kTcThreads = 32 * (kTcEpiWarps + 2);
 constexpr uint32_t kTcCols = 512;  // TMEM columns allocated (480 used)
 
-__device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+using namespace tcx;
 
-__device__ __forceinline__ void tc_mbar_init(uint64_t* b, uint32_t n) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
-}
-__device__ __forceinline__ void tc_mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool tc_mbar_wait(uint64_t* b, uint32_t parity) {
-  for (uint32_t i = 0; i < (1u << 22); ++i) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(su32(b)), "r"(parity)
-        : "memory");
-    if (ok) return true;
-  }
-  return false;
-}
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];" ::"r"(su32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(su32(bar))
-      : "memory");
-}
+// kind::i8 instruction descriptors of this file's MMAs (M = 128)
+constexpr uint32_t kTcIdesc = idesc_u8(kTcNB);    // both byte planes
+constexpr uint32_t kTcIdescHalf = idesc_u8(kTcN); // one byte plane
 
-// K-major operand in the 64-byte swizzle layout: rows of 64 bytes, 8-row
-// swizzle atoms 512 bytes apart (stride byte offset), descriptor version 1.
-__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr) {
-  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)(512 >> 4) << 32) | (1ull << 46) | (4ull << 61);
-}
-// kind::i8 instruction descriptor: s32 accumulator, u8 A and B, both
-// K-major, M = 128, N = n.
-constexpr uint32_t tc_idesc(int n) {
-  return (2u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
-}
-constexpr uint32_t kTcIdesc = tc_idesc(kTcNB);    // both byte planes
-constexpr uint32_t kTcIdescHalf = tc_idesc(kTcN); // one byte plane
-
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
 // ---------------------------------------------------------------------------
 // operand preparation
 // ---------------------------------------------------------------------------
@@ -247,11 +195,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (threadIdx.x == 0) {
     for (int i = 0; i < kTcStages; ++i) {
-      tc_mbar_init(&full[i], 1);
-      tc_mbar_init(&empty[i], 1);
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
     }
-    tc_mbar_init(&accf, 1);
-    tc_mbar_init(&tmem_empty, kTcEpiWarps);
+    mbar_init(&accf, 1);
+    mbar_init(&tmem_empty, kTcEpiWarps);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fail = 0;
   }
@@ -261,9 +209,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  tc_fence_before();
+  fence_before();
   __syncthreads();
-  tc_fence_after();
+  fence_after();
   const uint32_t tmem = tmem_holder;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (warp == kTcEpiWarps) {
@@ -276,9 +224,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int kb0 = (int)((int64_t)nkb * sp / ks), kb1 = (int)((int64_t)nkb * (sp + 1) / ks);
         for (int kb = kb0; kb < kb1; ++kb, ++q) {
           const int st = q % kTcStages;
-          if (q >= kTcStages && !tc_mbar_wait(&empty[st], ((q / kTcStages) - 1) & 1)) fail = 1;
+          if (q >= kTcStages && !mbar_wait(&empty[st], ((q / kTcStages) - 1) & 1)) fail = 1;
           unsigned char* sbuf = smem + (size_t)st * kTcStage;
-          tc_mbar_expect_tx(&full[st], kTcStage);
+          mbar_expect_tx(&full[st], kTcStage);
           for (int a = 0; a < 4; ++a) tma_load_3d(sbuf + a * kTcATile, &amap, kb * kTcKB, m0, a, &full[st]);
           tma_load_3d(sbuf + 4 * kTcATile, &bmap, kb * kTcKB, r0, 0, &full[st]);
           tma_load_3d(sbuf + 4 * kTcATile + kTcN * kTcKB, &bmap, kb * kTcKB, r0, 1, &full[st]);
@@ -296,12 +244,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int it = 0; it < my_tiles; ++it) {
         const int sp = (blockIdx.x + it * gridDim.x) % ks;
         const int kb0 = (int)((int64_t)nkb * sp / ks), kb1 = (int)((int64_t)nkb * (sp + 1) / ks);
-        if (it > 0 && !tc_mbar_wait(&tmem_empty, (it - 1) & 1)) fail = 1;
-        tc_fence_after();
+        if (it > 0 && !mbar_wait(&tmem_empty, (it - 1) & 1)) fail = 1;
+        fence_after();
         for (int kb = kb0; kb < kb1; ++kb, ++q) {
           const int st = q % kTcStages;
-          if (!tc_mbar_wait(&full[st], (q / kTcStages) & 1)) fail = 1;
-          tc_fence_after();
+          if (!mbar_wait(&full[st], (q / kTcStages) & 1)) fail = 1;
+          fence_after();
           const unsigned char* sbuf = smem + (size_t)st * kTcStage;
           const uint32_t baddr = su32(sbuf + 4 * kTcATile);
 #pragma unroll
@@ -311,21 +259,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                     smem_desc_sw64(su32(sbuf + 2 * kTcATile) + 32 * j),
                                     smem_desc_sw64(su32(sbuf + 3 * kTcATile) + 32 * j)};
             if (kb == kb0 && j == 0) {
-              tc_mma(tmem + 0 * kTcN, ad[0], bdesc, kTcIdesc, 0u);
-              tc_mma(tmem + 2 * kTcN, ad[2], bdesc, kTcIdesc, 0u);
-              tc_mma(tmem + 1 * kTcN, ad[1], bdesc, kTcIdesc, 1u);
-              tc_mma(tmem + 3 * kTcN, ad[3], bdesc, kTcIdescHalf, 1u);
-              tc_mma(tmem + 4 * kTcN, ad[3], smem_desc_sw64(baddr + kTcN * kTcKB), kTcIdescHalf, 0u);
+              mma_i8(tmem + 0 * kTcN, ad[0], bdesc, kTcIdesc, 0u);
+              mma_i8(tmem + 2 * kTcN, ad[2], bdesc, kTcIdesc, 0u);
+              mma_i8(tmem + 1 * kTcN, ad[1], bdesc, kTcIdesc, 1u);
+              mma_i8(tmem + 3 * kTcN, ad[3], bdesc, kTcIdescHalf, 1u);
+              mma_i8(tmem + 4 * kTcN, ad[3], smem_desc_sw64(baddr + kTcN * kTcKB), kTcIdescHalf, 0u);
             } else {
 #pragma unroll
-              for (int a = 0; a < 4; ++a) tc_mma(tmem + (uint32_t)(kTcN * a), ad[a], bdesc, kTcIdesc, 1u);
+              for (int a = 0; a < 4; ++a) mma_i8(tmem + (uint32_t)(kTcN * a), ad[a], bdesc, kTcIdesc, 1u);
             }
           }
           // free the stage once these MMAs have read it (the CTA's last stages
           // are never reloaded, so nothing waits for them)
-          if (q + kTcStages < qlast) tc_commit(&empty[st]);
+          if (q + kTcStages < qlast) mma_commit(&empty[st]);
         }
-        tc_commit(&accf);
+        mma_commit(&accf);
       }
     }
   } else {
@@ -342,8 +290,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int m = m0 + rl;
       const bool mrow = m < S;
       const uint64_t corr = (mrow ? (arow[m] << 15) : 0) - ((uint64_t)K << 46);
-      if (!tc_mbar_wait(&accf, it & 1)) fail = 1;
-      tc_fence_after();
+      if (!mbar_wait(&accf, it & 1)) fail = 1;
+      fence_after();
       if (EPI == 3) {
         // raw partial of this K range for all 96 plane rows, straight from registers
         for (int c0 = half * (kTcN / 2); c0 < (half + 1) * (kTcN / 2); c0 += 8) {
@@ -362,7 +310,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
           }
         }
-        tc_fence_before();
+        fence_before();
         __syncwarp();
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&tmem_empty)) : "memory");
         continue;
@@ -397,7 +345,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       // the accumulator is in shared memory: TMEM is free for the next tile
-      tc_fence_before();
+      fence_before();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&tmem_empty)) : "memory");
       // phase 2, overlapping the next tile's MMAs: the GELU epilogues on this
@@ -425,11 +373,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   }
-  tc_fence_before();
+  fence_before();
   __syncthreads();
   if (fail && threadIdx.x == 0) atomicExch(&g_tc_err, 1);
   if (warp == 0) {
-    tc_fence_after();
+    fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcCols) : "memory");
   }
 }
@@ -459,9 +407,9 @@ constexpr int kTsBTile = kTsT * kTcKB;                 // 4 KB per activation li
 constexpr int kTsStage = 2 * kTsATile + 4 * kTsBTile;  // 32 KB
 constexpr int kTsStages = 6;
 constexpr int kTsSmem = kTsStages * kTsStage + 1024;  // + alignment slack
-constexpr uint32_t kTsIdesc = tc_idesc(4 * kTsT);      // N = 256
-constexpr uint32_t kTsIdesc3 = tc_idesc(3 * kTsT);     // limbs 0-2
-constexpr uint32_t kTsIdesc1 = tc_idesc(kTsT);         // limb 3
+constexpr uint32_t kTsIdesc = idesc_u8(4 * kTsT);      // N = 256
+constexpr uint32_t kTsIdesc3 = idesc_u8(3 * kTsT);     // limbs 0-2
+constexpr uint32_t kTsIdesc1 = idesc_u8(kTsT);         // limb 3
 
 template <int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
@@ -482,11 +430,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (threadIdx.x == 0) {
     for (int i = 0; i < kTsStages; ++i) {
-      tc_mbar_init(&full[i], 1);
-      tc_mbar_init(&empty[i], 1);
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
     }
-    tc_mbar_init(&accf, 1);
-    tc_mbar_init(&tmem_empty, kTcEpiWarps);
+    mbar_init(&accf, 1);
+    mbar_init(&tmem_empty, kTcEpiWarps);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fail = 0;
   }
@@ -496,9 +444,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  tc_fence_before();
+  fence_before();
   __syncthreads();
-  tc_fence_after();
+  fence_after();
   const uint32_t tmem = tmem_holder;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (warp == kTcEpiWarps) {
@@ -511,9 +459,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int kb0 = (int)((int64_t)nkb * sp / ks), kb1 = (int)((int64_t)nkb * (sp + 1) / ks);
         for (int kb = kb0; kb < kb1; ++kb, ++q) {
           const int st = q % kTsStages;
-          if (q >= kTsStages && !tc_mbar_wait(&empty[st], ((q / kTsStages) - 1) & 1)) fail = 1;
+          if (q >= kTsStages && !mbar_wait(&empty[st], ((q / kTsStages) - 1) & 1)) fail = 1;
           unsigned char* sbuf = smem + (size_t)st * kTsStage;
-          tc_mbar_expect_tx(&full[st], kTsStage);
+          mbar_expect_tx(&full[st], kTsStage);
           tma_load_3d(sbuf, &wmap, kb * kTcKB, r0, 0, &full[st]);
           tma_load_3d(sbuf + kTsATile, &wmap, kb * kTcKB, r0, 1, &full[st]);
           for (int a = 0; a < 4; ++a)
@@ -532,29 +480,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int it = 0; it < my_tiles; ++it) {
         const int sp = (blockIdx.x + it * gridDim.x) % ks;
         const int kb0 = (int)((int64_t)nkb * sp / ks), kb1 = (int)((int64_t)nkb * (sp + 1) / ks);
-        if (it > 0 && !tc_mbar_wait(&tmem_empty, (it - 1) & 1)) fail = 1;
-        tc_fence_after();
+        if (it > 0 && !mbar_wait(&tmem_empty, (it - 1) & 1)) fail = 1;
+        fence_after();
         for (int kb = kb0; kb < kb1; ++kb, ++q) {
           const int st = q % kTsStages;
-          if (!tc_mbar_wait(&full[st], (q / kTsStages) & 1)) fail = 1;
-          tc_fence_after();
+          if (!mbar_wait(&full[st], (q / kTsStages) & 1)) fail = 1;
+          fence_after();
           const uint32_t sb = su32(smem + (size_t)st * kTsStage);
 #pragma unroll
           for (int j = 0; j < kTcKB / 32; ++j) {
             const uint64_t w0 = smem_desc_sw64(sb + 32 * j), w1 = smem_desc_sw64(sb + kTsATile + 32 * j);
             const uint64_t xb = smem_desc_sw64(sb + 2 * kTsATile + 32 * j);
             if (kb == kb0 && j == 0) {
-              tc_mma(tmem, w0, xb, kTsIdesc, 0u);
-              tc_mma(tmem + kTsT, w1, xb, kTsIdesc3, 1u);
-              tc_mma(tmem + 4 * kTsT, w1, smem_desc_sw64(sb + 2 * kTsATile + 3 * kTsBTile + 32 * j), kTsIdesc1, 0u);
+              mma_i8(tmem, w0, xb, kTsIdesc, 0u);
+              mma_i8(tmem + kTsT, w1, xb, kTsIdesc3, 1u);
+              mma_i8(tmem + 4 * kTsT, w1, smem_desc_sw64(sb + 2 * kTsATile + 3 * kTsBTile + 32 * j), kTsIdesc1, 0u);
             } else {
-              tc_mma(tmem, w0, xb, kTsIdesc, 1u);
-              tc_mma(tmem + kTsT, w1, xb, kTsIdesc, 1u);
+              mma_i8(tmem, w0, xb, kTsIdesc, 1u);
+              mma_i8(tmem + kTsT, w1, xb, kTsIdesc, 1u);
             }
           }
-          if (q + kTsStages < qlast) tc_commit(&empty[st]);
+          if (q + kTsStages < qlast) mma_commit(&empty[st]);
         }
-        tc_commit(&accf);
+        mma_commit(&accf);
       }
     }
   } else {
@@ -568,8 +516,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int r = (t % tiles_n) * kTsM + rl, t0 = (t / tiles_n) * kTsT;
       const bool rok = EPI == 3 ? r < nrows : r < N;
       const uint64_t bcorr = (EPI == 0 && rok) ? (brow[r] << 31) - ((uint64_t)K << 46) : 0;
-      if (!tc_mbar_wait(&accf, it & 1)) fail = 1;
-      tc_fence_after();
+      if (!mbar_wait(&accf, it & 1)) fail = 1;
+      fence_after();
       for (int c0 = 32 * half; c0 < 32 * half + 32; c0 += 8) {
         uint32_t g[5][8];
 #pragma unroll
@@ -586,16 +534,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       }
-      tc_fence_before();
+      fence_before();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&tmem_empty)) : "memory");
     }
   }
-  tc_fence_before();
+  fence_before();
   __syncthreads();
   if (fail && threadIdx.x == 0) atomicExch(&g_tc_err, 1);
   if (warp == 0) {
-    tc_fence_after();
+    fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcCols) : "memory");
   }
 }
@@ -637,42 +585,10 @@ __global__ void tc_splitk_reduce_kernel(const uint64_t* __restrict__ part, int k
   }
 }
 
-// ---------------------------------------------------------------------------
-// host side
-// ---------------------------------------------------------------------------
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-    else
-      cudaGetLastError();
-  });
-  return fn;
-}
-
 // u8 planes [planes][rows][K] -> 3D map (K, rows, planes), box (64, box_rows, 1)
-// plane_stride: bytes from one plane to the next (0: rows * K, planes back to back)
 bool encode_planes(void* out, const uint8_t* base, int nplanes, int rows, int K, int box_rows,
                    size_t plane_stride = 0) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  CUtensorMap* map = reinterpret_cast<CUtensorMap*>(out);
-  const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)nplanes};
-  const cuuint64_t strides[2] = {(cuuint64_t)K, plane_stride ? (cuuint64_t)plane_stride : (cuuint64_t)rows * (cuuint64_t)K};
-  const cuuint32_t box[3] = {(cuuint32_t)kTcKB, (cuuint32_t)box_rows, 1};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return encode_u8_planes(out, base, nplanes, rows, K, box_rows, 1, plane_stride);
 }
 
 template <typename... KArgs, typename... Args>
@@ -691,6 +607,39 @@ void tc_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaS
 }
 
 }  // namespace
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+bool encode_u8_planes(void* out, const uint8_t* base, int nplanes, int rows, int K, int box_rows, int box_planes,
+                      size_t plane_stride) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  CUtensorMap* map = reinterpret_cast<CUtensorMap*>(out);
+  const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)nplanes};
+  const cuuint64_t strides[2] = {(cuuint64_t)K,
+                                 plane_stride ? (cuuint64_t)plane_stride : (cuuint64_t)rows * (cuuint64_t)K};
+  const cuuint32_t box[3] = {(cuuint32_t)kTcKB, (cuuint32_t)box_rows, (cuuint32_t)box_planes};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 static_assert(sizeof(CUtensorMap) <= sizeof(TcAct::map), "tensor map storage");
 

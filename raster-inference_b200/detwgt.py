@@ -169,3 +169,48 @@ def write_synthetic_model(model_dir: str, cfg: dict, seed: int, width: int = 16,
     with open(os.path.join(model_dir, "model.detwgt"), "wb") as f:
         f.write(encode(tensors, policy))
     return model_dir
+
+
+# ---------------------------------------------------------------------------
+# synthetic inputs of the benchmarks (the seeded token ids and activations that
+# bench.py and the E4B-shape parity tests share)
+# ---------------------------------------------------------------------------
+def lcg_draws(n: int, seed: int) -> list[int]:
+    """The reference fixture's LCG (det_goldens.rs:348-356): s <- s *
+    6364136223846793005 + 1442695040888963407 mod 2^64, draw = s >> 33."""
+    s, out = seed, []
+    for _ in range(n):
+        s = (s * 6364136223846793005 + 1442695040888963407) & 0xFFFFFFFFFFFFFFFF
+        out.append(s >> 33)
+    return out
+
+
+def lcg_token_ids(n: int, vocab: int, seed: int) -> list[int]:
+    return [d % vocab for d in lcg_draws(n, seed)]
+
+
+def normal_f32(n: int, seed: int) -> np.ndarray:
+    """n draws of N(0, 1) as float32: Box-Muller on pairs of LCG draws
+    reduced to 30 bits, u1 in (0, 1], u2 in [0, 1)."""
+    u = np.array([d % (1 << 30) for d in lcg_draws(2 * ((n + 1) // 2), seed)], dtype=np.float64)
+    u1 = (u[0::2] + 1.0) / float(1 << 30)
+    u2 = u[1::2] / float(1 << 30)
+    r = np.sqrt(-2.0 * np.log(u1))
+    z = np.empty(u1.size * 2, dtype=np.float64)
+    z[0::2] = r * np.cos(2.0 * np.pi * u2)
+    z[1::2] = r * np.sin(2.0 * np.pi * u2)
+    return z[:n].astype(np.float32)
+
+
+def f32_to_act(x: np.ndarray) -> np.ndarray:
+    """det_num f32_to_act (convert.rs:52-57, :82-93) for finite float32
+    values: round half to even of x * 2^16, saturated to i32.  x * 2^16 is
+    exact in float64 (an exponent shift of a float32), and rint rounds half
+    to even."""
+    q = np.rint(np.asarray(x, dtype=np.float32).astype(np.float64) * 65536.0)
+    return np.clip(q, -2.0**31, 2.0**31 - 1).astype(np.int32)
+
+
+def normal_acts(n: int, seed: int) -> np.ndarray:
+    """Activations of the GEMV microbenchmark: N(0, 1) quantized with f32_to_act."""
+    return f32_to_act(normal_f32(n, seed))

@@ -93,3 +93,22 @@ def test_product_config_validation():
     with pytest.raises(rdet.RdetError) as e:
         rdet.Model.synthetic(bad, 1)
     assert "layer count mismatch" in e.value.msg
+
+
+def test_benchmark_activations_follow_f32_to_act():
+    """The GEMV microbenchmark's N(0,1) activations are quantized exactly as
+    the oracle's f32_to_act (det_num/convert.rs:52-57) quantizes them."""
+    import oracle as O
+    z = detwgt.normal_f32(3001, 9)
+    x = detwgt.normal_acts(3001, 9)
+    assert x.dtype == np.int32 and x.size == 3001
+    assert abs(float(z.mean())) < 0.1 and 0.9 < float(z.std()) < 1.1
+    assert all(int(x[i]) == O.lib().dor_f32_to_act(float(z[i])) for i in range(x.size))
+    # halfway and saturating inputs
+    edge = np.array([0.5 / 65536, 1.5 / 65536, -2.5 / 65536, 40000.0, -40000.0, 3.0e38], dtype=np.float32)
+    assert [int(v) for v in detwgt.f32_to_act(edge)] == [O.lib().dor_f32_to_act(float(v)) for v in edge]
+
+
+def test_lcg_token_ids_match_fixture_generator():
+    from tiny_gemma_dev import lcg_token_ids
+    assert detwgt.lcg_token_ids(50, 280, 0) == lcg_token_ids(50, 280, 0)

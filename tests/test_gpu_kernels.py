@@ -156,3 +156,24 @@ def test_kernel_entries_in_a_fresh_process():
     r = subprocess.run([sys.executable, "-c", FRESH_PROCESS_SCRIPT, here, os.path.dirname(here)],
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "FRESH-OK" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("heads,kv_heads,d,cap,position,window", [(8, 2, 256, 600, 599, 512), (8, 2, 512, 300, 299, 0),
+                                                                 (2, 1, 64, 50, 40, 0)])
+def test_attention_decode_scores_all_int32_min(heads, kv_heads, d, cap, position, window):
+    # every score saturates at INT32_MIN, so every row ties: argmax_first picks
+    # the first row of the window (det_num/ops.rs:463-478)
+    rng = np.random.default_rng(d + position)
+    q = np.full((heads, d), I32_MAX, dtype=np.int32)
+    k = np.full((kv_heads, cap, d), I32_MIN, dtype=np.int32)
+    v = rng.integers(I32_MIN, I32_MAX, (kv_heads, cap, d), dtype=np.int64).astype(np.int32)
+    start = max(0, position + 1 - window) if window else 0
+    g = heads // kv_heads
+    ref = np.stack([O.attention_one(q[h], k[h // g, start:position + 1], v[h // g, start:position + 1])
+                    for h in range(heads)])
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    out = torch.zeros((heads, d), dtype=torch.int32, device="cuda")
+    rdet.det_attention_decode(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), cap, heads, kv_heads, d, position, window,
+                              out.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), ref)
