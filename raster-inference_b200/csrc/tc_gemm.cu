@@ -35,6 +35,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -46,6 +47,12 @@ namespace rdet {
 
 // set when a bounded pipeline wait gives up (read by tc_error_flag)
 __device__ int g_tc_err = 0;
+// the CTA-pair GEMM for prompts of more than 128 tokens (0: one-CTA tiles;
+// RDET_TC_PAIR=0 in the environment selects them)
+static bool g_tc_pair = [] {
+  const char* e = getenv("RDET_TC_PAIR");
+  return !(e && e[0] == '0');
+}();
 
 namespace {
 
@@ -383,6 +390,277 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// The same GEMM on a CTA pair (tcgen05 cta_group::2, a cluster of two CTAs):
+// an output tile is 256 tokens x 96 weight rows.  CTA r of the pair holds
+// tokens [m0 + 128r, m0 + 128r + 128) of the four activation limbs (the A
+// rows of its half of M = 256) and byte plane r of the tile's 96 weight rows
+// (its half of the B operand's N = 192 rows: plane 0 in CTA 0, plane 1 in
+// CTA 1).  Every MMA therefore reads 4 KB of A and 3 KB of B from each SM's
+// shared memory instead of 4 KB and 6 KB, and a stage moves 38 KB per SM
+// instead of 44 KB.  The MMA's N columns keep the one-CTA order (low plane,
+// then high plane), so the TMEM blocks and the epilogue are those of
+// tc_linear_kernel, each CTA draining its own 128 rows.
+// The leader (rank 0) issues every MMA; both CTAs' TMA loads (cta_group::2,
+// no multicast) signal the leader's stage barrier, which expects both
+// halves' bytes; the leader's commits arrive on both CTAs' barriers; both
+// epilogues release TMEM on the leader's barrier.  Block 4 (shift 32) is
+// zeroed by the epilogue before each tile (a plane cannot be addressed alone
+// when B is split by plane across the pair), so a tile's first K step runs
+// limbs 0 and 2 with accumulate off and limbs 1 and 3 onto them.
+// Tiles go round the pairs in the order that keeps the smaller operand in L2
+// (m_fast: all token tiles of a weight tile before the next weight tile).
+// ---------------------------------------------------------------------------
+constexpr int kT2M = 2 * kTcM;                     // tokens per pair tile
+constexpr int kT2Stages = 4;
+constexpr int kT2BTile = kTcN * kTcKB;             // 6 KB: one weight plane
+constexpr int kT2Stage = 4 * kTcATile + kT2BTile;  // 38 KB
+constexpr int kT2Smem = kT2Stages * kT2Stage + kTcStageOut + 1024;
+// kind::i8 instruction descriptor with M = 256 (cta_group::2), N = 192
+constexpr uint32_t kT2Idesc = (2u << 4) | ((uint32_t)(kTcNB >> 3) << 17) | ((uint32_t)(kT2M >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same location in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// tiled 3D TMA load into this CTA's shared memory whose completion is counted
+// on an mbarrier of either CTA of the pair (no multicast)
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4}], [%5];" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void mma_i8_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// arrive on the barrier at the same offset in both CTAs once the MMAs issued
+// so far have completed
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          su32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+__device__ __forceinline__ void tmem_st8_zero(uint32_t taddr) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr), "r"(0)
+               : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_linear2_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
+                      const uint64_t* __restrict__ arow, const uint64_t* __restrict__ brow, int S, int N, int K,
+                      int ntiles_m, int ntiles_n, int m_fast, int32_t* __restrict__ Y,
+                      const int32_t* __restrict__ vec, int ldv) {
+  extern __shared__ __align__(16) unsigned char tc_smem_raw[];
+  __shared__ __align__(8) uint64_t full[kT2Stages], empty[kT2Stages], accf, tmem_empty;
+  __shared__ uint32_t tmem_holder;
+  __shared__ int fail;
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+  int32_t* stage_out = reinterpret_cast<int32_t*>(smem + (size_t)kT2Stages * kT2Stage);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int nkb = (K + kTcKB - 1) / kTcKB;
+  const int ntiles = ntiles_m * ntiles_n;
+  const int my_tiles = pair < ntiles ? (ntiles - 1 - pair) / npairs + 1 : 0;
+  auto tile_of = [&](int it, int& m0, int& nt) {
+    const int t = pair + it * npairs;
+    const int mt = m_fast ? t % ntiles_m : t / ntiles_n;
+    nt = m_fast ? t / ntiles_m : t % ntiles_n;
+    m0 = mt * kT2M;
+  };
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kT2Stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(&accf, 1);
+    mbar_init(&tmem_empty, 2 * kTcEpiWarps);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    fail = 0;
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_holder)),
+                 "r"(kTcCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
+  fence_after();
+  const uint32_t tmem = tmem_holder;
+  const uint32_t tmem_empty_leader = mapa_rank(su32(&tmem_empty), 0);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (warp == kTcEpiWarps) {
+    // ---- producer (both CTAs): this CTA's A rows and weight plane, counted
+    // on the leader's stage barrier
+    if (lane == 0) {
+      int q = 0;
+      for (int it = 0; it < my_tiles; ++it) {
+        int m0, nt;
+        tile_of(it, m0, nt);
+        for (int kb = 0; kb < nkb; ++kb, ++q) {
+          const int st = q % kT2Stages;
+          if (q >= kT2Stages && !mbar_wait(&empty[st], ((q / kT2Stages) - 1) & 1)) fail = 1;
+          unsigned char* sbuf = smem + (size_t)st * kT2Stage;
+          if (rank == 0) mbar_expect_tx(&full[st], 2 * kT2Stage);
+          const uint32_t bar = mapa_rank(su32(&full[st]), 0);
+          for (int a = 0; a < 4; ++a)
+            tma_load_3d_pair(sbuf + a * kTcATile, &amap, kb * kTcKB, m0 + kTcM * (int)rank, a, bar);
+          tma_load_3d_pair(sbuf + 4 * kTcATile, &bmap, kb * kTcKB, nt * kTcN, (int)rank, bar);
+        }
+      }
+    }
+  } else if (warp == kTcEpiWarps + 1) {
+    // ---- MMA issue (leader only)
+    if (rank == 0 && lane == 0) {
+      const int qlast = my_tiles * nkb;
+      int q = 0;
+      for (int it = 0; it < my_tiles; ++it) {
+        if (!mbar_wait(&tmem_empty, it & 1)) fail = 1;
+        fence_after();
+        for (int kb = 0; kb < nkb; ++kb, ++q) {
+          const int st = q % kT2Stages;
+          if (!mbar_wait(&full[st], (q / kT2Stages) & 1)) fail = 1;
+          fence_after();
+          const unsigned char* sbuf = smem + (size_t)st * kT2Stage;
+          const uint32_t baddr = su32(sbuf + 4 * kTcATile);
+#pragma unroll
+          for (int j = 0; j < kTcKB / 32; ++j) {
+            const uint64_t bdesc = smem_desc_sw64(baddr + 32 * j);
+            const uint64_t ad[4] = {smem_desc_sw64(su32(sbuf) + 32 * j), smem_desc_sw64(su32(sbuf + kTcATile) + 32 * j),
+                                    smem_desc_sw64(su32(sbuf + 2 * kTcATile) + 32 * j),
+                                    smem_desc_sw64(su32(sbuf + 3 * kTcATile) + 32 * j)};
+            if (kb == 0 && j == 0) {
+              mma_i8_pair(tmem + 0 * kTcN, ad[0], bdesc, kT2Idesc, 0u);
+              mma_i8_pair(tmem + 2 * kTcN, ad[2], bdesc, kT2Idesc, 0u);
+              mma_i8_pair(tmem + 1 * kTcN, ad[1], bdesc, kT2Idesc, 1u);
+              mma_i8_pair(tmem + 3 * kTcN, ad[3], bdesc, kT2Idesc, 1u);  // block 4 was zeroed
+            } else {
+#pragma unroll
+              for (int a = 0; a < 4; ++a) mma_i8_pair(tmem + (uint32_t)(kTcN * a), ad[a], bdesc, kT2Idesc, 1u);
+            }
+          }
+          if (q + kT2Stages < qlast) mma_commit_pair(&empty[st]);
+        }
+        mma_commit_pair(&accf);
+      }
+    }
+  } else {
+    // ---- epilogue (both CTAs): warp w reads TMEM lanes 32*(w%4).. and its
+    // column half of this CTA's 128 rows
+    constexpr int kOut = EPI == 2 ? kTcN / 2 : kTcN;
+    constexpr int kHalf = kOut / 2;
+    constexpr int kStep = EPI == 2 ? 8 : 16;
+    const int quarter = warp & 3, half = warp >> 2;
+    const int rl = 32 * quarter + lane;
+    const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16);
+    // block 4 of the columns this warp reads: zero before the first tile
+    for (int c0 = half * kHalf; c0 < (half + 1) * kHalf; c0 += kStep) {
+      tmem_st8_zero(tbase + 4 * kTcN + c0);
+      tmem_st8_zero(tbase + 4 * kTcN + (EPI == 2 ? kTcN / 2 : 8) + c0);
+    }
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(tmem_empty_leader);
+    for (int it = 0; it < my_tiles; ++it) {
+      int m0, nt;
+      tile_of(it, m0, nt);
+      m0 += kTcM * (int)rank;
+      const int r0 = nt * kTcN;
+      const int nbase = EPI == 2 ? nt * (kTcN / 2) : r0;
+      const int m = m0 + rl;
+      const bool mrow = m < S;
+      const uint64_t corr = (mrow ? (arow[m] << 15) : 0) - ((uint64_t)K << 46);
+      if (!mbar_wait(&accf, it & 1)) fail = 1;
+      fence_after();
+      for (int c0 = half * kHalf; c0 < (half + 1) * kHalf; c0 += kStep) {
+        uint32_t g[5][2][8];
+#pragma unroll
+        for (int gg = 0; gg < 5; ++gg) {
+          tmem_ld8(tbase + kTcN * gg + c0, g[gg][0]);
+          tmem_ld8(tbase + kTcN * gg + (EPI == 2 ? kTcN / 2 : 8) + c0, g[gg][1]);
+        }
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        // these block-4 columns are read: zero them for the next tile
+        tmem_st8_zero(tbase + 4 * kTcN + c0);
+        tmem_st8_zero(tbase + 4 * kTcN + (EPI == 2 ? kTcN / 2 : 8) + c0);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int pr = c0 + (EPI == 2 ? (i >> 3) * (kTcN / 2) + (i & 7) : i);
+          const int n = nbase + c0 + (EPI == 2 ? (i & 7) : i);
+          int32_t y = 0;
+          if (mrow && n < N) {
+            uint64_t acc = (uint64_t)g[0][i >> 3][i & 7] + ((uint64_t)g[1][i >> 3][i & 7] << 8) +
+                           ((uint64_t)g[2][i >> 3][i & 7] << 16) + ((uint64_t)g[3][i >> 3][i & 7] << 24) +
+                           ((uint64_t)g[4][i >> 3][i & 7] << 32);
+            acc -= corr + (brow[r0 + pr] << 31);
+            y = requantize((int64_t)acc);
+          }
+          stage_out[rl * kTcOutStride + pr] = y;
+        }
+      }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tmem_empty_leader);
+      if constexpr (EPI == 1 || EPI == 2) {
+        if (mrow) {
+          for (int j = half * kHalf; j < (half + 1) * kHalf; ++j) {
+            const int n = nbase + j;
+            if (n >= N) break;
+            int32_t* sp_ = &stage_out[rl * kTcOutStride + j];
+            *sp_ = mul_sat(gelu_act(*sp_), EPI == 2 ? sp_[kTcN / 2] : vec[(size_t)m * ldv + n]);
+          }
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kTcEpiWarps) : "memory");  // staging complete
+      for (int r = warp; r < kTcM; r += kTcEpiWarps) {
+        const int mm = m0 + r;
+        if (mm >= S) break;
+        for (int c = lane; c < kOut; c += 32) {
+          const int n = nbase + c;
+          if (n < N) Y[(size_t)mm * N + n] = stage_out[r * kTcOutStride + c];
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kTcEpiWarps) : "memory");  // staging free again
+    }
+  }
+  fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the leader's MMAs no longer read this CTA's shared memory
+  if (fail && threadIdx.x == 0) atomicExch(&g_tc_err, 1);
+  if (warp == 0) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Short row counts (a batched decode step: S <= 64 tokens).  The operands
 // swap roles: the A operand is one byte plane of 128 weight rows (M = 128)
 // and the B operand stacks the four activation limbs of 64 tokens (N = 256,
@@ -591,6 +869,27 @@ bool encode_planes(void* out, const uint8_t* base, int nplanes, int rows, int K,
   return encode_u8_planes(out, base, nplanes, rows, K, box_rows, 1, plane_stride);
 }
 
+// launch as clusters of two CTAs (the CTA-pair kernels), with programmatic
+// stream serialization
+template <typename... KArgs, typename... Args>
+void tc_launch_pair(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 template <typename... KArgs, typename... Args>
 void tc_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
   cudaLaunchConfig_t cfg = {};
@@ -660,6 +959,9 @@ void tc_init() {
   cudaFuncSetAttribute(tc_linear_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
   cudaFuncSetAttribute(tc_linear_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
   cudaFuncSetAttribute(tc_linear_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+  cudaFuncSetAttribute(tc_linear2_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kT2Smem);
+  cudaFuncSetAttribute(tc_linear2_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kT2Smem);
+  cudaFuncSetAttribute(tc_linear2_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kT2Smem);
 }
 
 bool tc_supported() {
@@ -852,6 +1154,24 @@ bool launch_tc_linear(const TcAct& a, const TcWeight& w, const TcOut& o, cudaStr
   }
   const bool split = o.scratch && (ks > 1 || o.y64) && (size_t)ks * a.S * w.nrows * 8 <= o.scratch_bytes;
   if (o.y64 && !split) return false;  // the i64 sums need the split-K scratch
+  if (!split && a.S > kTcM && g_tc_pair && sms >= 2) {
+    // CTA pairs: 256-token tiles, B split by plane across the pair
+    const int tm = (a.S + kT2M - 1) / kT2M, tiles = tm * ntiles_n;
+    const int grid = 2 * std::min(tiles, sms / 2);
+    // keep the smaller operand resident in L2: all token tiles of a weight
+    // tile in a row when the activation planes are the smaller
+    const int m_fast = (size_t)4 * a.S * a.K < (size_t)2 * w.nrows * a.K ? 1 : 0;
+    if (w.pair)
+      tc_launch_pair(tc_linear2_kernel<2>, dim3(grid), dim3(kTcThreads), kT2Smem, s, am, bm, a.rowsum, w.rowsum, a.S,
+                     w.N, a.K, tm, ntiles_n, m_fast, o.y, o.vec, ldv);
+    else if (o.epi == kEpiGeluMul)
+      tc_launch_pair(tc_linear2_kernel<1>, dim3(grid), dim3(kTcThreads), kT2Smem, s, am, bm, a.rowsum, w.rowsum, a.S,
+                     w.N, a.K, tm, ntiles_n, m_fast, o.y, o.vec, ldv);
+    else
+      tc_launch_pair(tc_linear2_kernel<0>, dim3(grid), dim3(kTcThreads), kT2Smem, s, am, bm, a.rowsum, w.rowsum, a.S,
+                     w.N, a.K, tm, ntiles_n, m_fast, o.y, o.vec, ldv);
+    return true;
+  }
   if (!split) {
     const int grid = std::min(ntiles, sms);
     if (w.pair)

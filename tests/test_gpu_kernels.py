@@ -65,7 +65,11 @@ def test_gemv_bit_exact(width, shape, adv):
     (32, 16, 16), (33, 97, 48), (200, 2560, 512), (257, 300, 2560), (129, 193, 1024), (96, 256, 10240),
     # at most 64 rows: the swapped-operand kernel (weights as the 128-row MMA
     # operand), with K split across SMs and with one K range
-    (64, 2560, 2560), (48, 1000, 4096), (64, 4096, 256)])
+    (64, 2560, 2560), (48, 1000, 4096), (64, 4096, 256),
+    # more than 128 rows: CTA pairs (256-token tiles, the weight planes split
+    # across the pair), a partial second half-tile, both tile orders (more
+    # activation than weight bytes, and fewer)
+    (1000, 2048, 2560), (777, 96, 4096), (2048, 2560, 10240)])
 def test_linear_bit_exact(width, S, rows, cols):
     rng = np.random.default_rng(S * 1000 + rows + width)
     w = rand_w(rng, rows, cols, width, True)
