@@ -382,6 +382,31 @@ def run_kernel_case(args):
         model.close()
         print(f"prefill: {args.ctx} tokens")
         return
+    if args.kernel_case == "tcattn":
+        # prefill attention on the tensor cores (rdet_det_attention_prefill) for
+        # a full layer (head_dim 512, causal) and a sliding layer (head_dim 256,
+        # window 512) of a --ctx-token prompt at the E4B head counts
+        Hq, kv, d, dg, win = (t["num_attention_heads"], t["num_key_value_heads"], t["head_dim"],
+                              t["global_head_dim"], t["sliding_window"])
+        S = args.ctx
+        for name, hd, w in (("full", dg, 0), ("sliding", d, win)):
+            q = torch.randint(-(1 << 18), 1 << 18, (S, Hq, hd), dtype=torch.int32, device=dev, generator=g)
+            kc = torch.randint(-(1 << 18), 1 << 18, (kv, S, hd), dtype=torch.int32, device=dev, generator=g)
+            vc = torch.randint(-(1 << 20), 1 << 20, (kv, S, hd), dtype=torch.int32, device=dev, generator=g)
+            out = torch.empty((S, Hq, hd), dtype=torch.int32, device=dev)
+            rdet.det_attention_prefill(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), S, S, Hq, kv, hd, w,
+                                       out.data_ptr())
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            rdet.det_attention_prefill(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), S, S, Hq, kv, hd, w,
+                                       out.data_ptr())
+            e1.record()
+            torch.cuda.synchronize()
+            keys = sum(min(i + 1, w) if w else i + 1 for i in range(S))
+            print(f"tc attn {name}: S {S} heads {Hq}/{kv} head_dim {hd} window {w} ms {e0.elapsed_time(e1):.3f} "
+                  f"score MACs {Hq * hd * keys} int8 limb MACs {Hq * hd * keys * 28}")
+        return
     if args.kernel_case == "tc":
         # prefill linear on the tensor cores (rdet_det_linear, >= 32 rows): byte-plane
         # prep kernels then tc_linear_kernel, at 2048 prompt tokens
@@ -744,7 +769,7 @@ def main():
     ap.add_argument("--config4-tokens", type=int, default=256, help="greedy tokens of the config-4 line (0: skip)")
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched ragged decode line (0: skip)")
     ap.add_argument("--batch-steps", type=int, default=128, help="greedy steps of the batched line (config 5: 128)")
-    ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc", "prefill"],
+    ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc", "tcattn", "prefill"],
                     help="run a few launches of one kernel at E4B shapes for an ncu capture, then exit")
     ap.add_argument("--time-calls", type=int, default=0,
                     help="with --kernel-case attn: time this many back-to-back calls of each decode-attention entry "

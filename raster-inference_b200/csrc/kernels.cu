@@ -1134,6 +1134,31 @@ __device__ void rope_inplace(int32_t* v, int rotary, const int64_t* inv_freq, ui
   }
 }
 
+// rope_inplace with the (cos, sin) pairs of this position from a table
+__device__ void rope_inplace_tab(int32_t* v, int rotary, const int32_t* cs, uint32_t pos) {
+  if (rotary == 0 || pos == 0) return;
+  int half = rotary >> 1;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const int2 t = reinterpret_cast<const int2*>(cs)[i];
+    int32_t l = v[i], r = v[i + half];
+    v[i] = sub_sat(mul_sat(l, t.x), mul_sat(r, t.y));
+    v[i + half] = add_sat(mul_sat(r, t.x), mul_sat(l, t.y));
+  }
+}
+
+__global__ void rope_table_kernel(const int64_t* inv_freq, int half, int32_t* cs) {
+  pdl_entry();
+  const uint32_t p = blockIdx.x;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    int32_t c, sn;
+    sin_cos_acc(pos_angle(p, inv_freq[i]), &c, &sn);
+    reinterpret_cast<int2*>(cs)[(size_t)p * half + i] = make_int2(c, sn);
+  }
+}
+void launch_rope_table(const int64_t* inv_freq, int half, int S, int32_t* cs, cudaStream_t s) {
+  launch_k(rope_table_kernel, dim3(S), dim3(half < 128 ? (half + 31) / 32 * 32 : 128), 0, s, inv_freq, half, cs);
+}
+
 __global__ void qkv_post_kernel(const QkvPostArgs a) {
   pdl_entry();
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -1149,7 +1174,8 @@ __global__ void qkv_post_kernel(const QkvPostArgs a) {
     int32_t sc = block_norm_scale(vs, d, a.eps, red);
     for (int i = threadIdx.x; i < d; i += blockDim.x) vs[i] = mul_sat(mul_sat(vs[i], sc), a.q_norm[i]);
     __syncthreads();
-    rope_inplace(vs, a.rotary, a.inv_freq, pos);
+    if (a.rope_cs) rope_inplace_tab(vs, a.rotary, a.rope_cs + (size_t)s * a.rotary, pos);
+    else rope_inplace(vs, a.rotary, a.inv_freq, pos);
     __syncthreads();
     int32_t* dst = a.q_out + ((size_t)s * a.Hq + head) * d;
     for (int i = threadIdx.x; i < d; i += blockDim.x) dst[i] = vs[i];
@@ -1168,7 +1194,8 @@ __global__ void qkv_post_kernel(const QkvPostArgs a) {
   int32_t sc = block_norm_scale(vs, d, a.eps, red);
   for (int i = threadIdx.x; i < d; i += blockDim.x) vs[i] = mul_sat(mul_sat(vs[i], sc), a.k_norm[i]);
   __syncthreads();
-  rope_inplace(vs, a.rotary, a.inv_freq, pos);
+  if (a.rope_cs) rope_inplace_tab(vs, a.rotary, a.rope_cs + (size_t)s * a.rotary, pos);
+  else rope_inplace(vs, a.rotary, a.inv_freq, pos);
   __syncthreads();
   int32_t* kd = kcache + ((size_t)h * cap + pos) * d;
   for (int i = threadIdx.x; i < d; i += blockDim.x) kd[i] = vs[i];

@@ -165,6 +165,9 @@ struct QkvPostArgs {
   const int32_t* pos = nullptr;  // device: position of row 0
   int32_t Hq = 0, Hkv = 0, d = 0, rotary = 0;
   const int64_t* inv_freq = nullptr;  // [rotary/2] Q32.32 recurrence table
+  // prefill: (cos, sin) of row s's position for every rotary pair, [S][rotary/2][2]
+  // (launch_rope_table), or nullptr to compute them from inv_freq
+  const int32_t* rope_cs = nullptr;
   const int32_t* q_in = nullptr;      // [S, Hq*d]
   const int32_t* k_in = nullptr;      // [S, Hkv*d] raw K (nullptr: no own KV)
   const int32_t* v_in = nullptr;      // [S, Hkv*d] raw V (== k_in for k_eq_v)
@@ -185,6 +188,10 @@ struct QkvPostArgs {
   const int32_t* cap_rows = nullptr;
 };
 void launch_qkv_post(const QkvPostArgs& a, cudaStream_t s);
+// cs[p][i] = (cos, sin) of pos_angle(p, inv_freq[i]) for positions p in [0, S)
+// and pairs i in [0, half): the RoPE factors of a prompt, once per distinct
+// inverse-frequency table instead of once per (row, head, layer)
+void launch_rope_table(const int64_t* inv_freq, int half, int S, int32_t* cs, cudaStream_t s);
 
 // ---- attention -----------------------------------------------------------------
 struct AttnScratch {

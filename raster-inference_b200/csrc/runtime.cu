@@ -527,6 +527,11 @@ struct Ctx {
   size_t tc_split_bytes = 0;
   void* ta_ws = nullptr;         // workspace of the tensor-core prefill attention
   size_t ta_ws_bytes = 0;
+  // distinct RoPE inverse-frequency tables (device pointer, rotary / 2) and,
+  // for a prefill, each one's (cos, sin) factors per prompt position
+  std::vector<std::pair<const int64_t*, int>> rope_list;
+  int32_t* rope_cs = nullptr;    // [rope_list.size()][max_prefill][max half][2]
+  int rope_half_max = 0;
   // batched decode: per-row tables (device) and the batch logits
   struct {
     int rows = 0;                  // rows the tables hold
@@ -756,6 +761,7 @@ static void build_model(Ctx& c, std::map<std::string, TensorInfo>& tab, bool syn
         int64_t* dp = c.dalloc_n<int64_t>(t.size());
         CK(cudaMemcpy(dp, t.data(), t.size() * 8, cudaMemcpyHostToDevice));
         it = rope_tabs.emplace(key, dp).first;
+        c.rope_list.emplace_back(dp, lc.rotary / 2);
       }
       L.inv_freq = it->second;
     }
@@ -803,6 +809,9 @@ static void alloc_workspaces(Ctx& c) {
   w.g = c.dalloc_n<int32_t>(S * std::max(m.P, 1));
   w.pr = c.dalloc_n<int32_t>(S * m.H);
   w.ids = c.dalloc_n<uint32_t>(S);
+  for (auto& r : c.rope_list) c.rope_half_max = std::max(c.rope_half_max, r.second);
+  if (!c.rope_list.empty())
+    c.rope_cs = c.dalloc_n<int32_t>(c.rope_list.size() * S * (size_t)c.rope_half_max * 2);
   w.scratch_elems = (int64_t)m.Hq * S * S;
   w.scores = c.dalloc_n<int32_t>(w.scratch_elems);
   w.exps = c.dalloc_n<int64_t>(w.scratch_elems);
@@ -1005,6 +1014,10 @@ static void prefill_begin(Ctx& c, Seq& q, const uint32_t* ids, size_t n) {
   q.pos = 0;
   q.prefilled = false;
   launch_embed(w.ids, S, c.emb, c.emb_scale, w.x0, c.d_err, s);
+  // RoPE factors of positions [0, S), once per distinct frequency table
+  for (size_t t = 0; t < c.rope_list.size(); ++t)
+    launch_rope_table(c.rope_list[t].first, c.rope_list[t].second, S,
+                      c.rope_cs + t * (size_t)c.max_prefill * c.rope_half_max * 2, s);
   if (m.P > 0) {
     prefill_linear(c, w.x0, S, c.ple_model_proj, c.t_ple_model, w.ple_proj, kEpiPlain, nullptr);
     PleArgs pa;
@@ -1154,6 +1167,9 @@ static void prefill_layer(Ctx& c, Seq& q, int l) {
   qa.S = S; qa.pos = q.d_pos; qa.Hq = m.Hq; qa.Hkv = lc.kv_heads; qa.d = d; qa.rotary = lc.rotary;
   qa.inv_freq = L.inv_freq; qa.q_in = w.q; qa.q_norm = L.q_norm; qa.k_norm = L.k_norm; qa.eps = c.eps;
   qa.q_out = w.qo; qa.cap = q.cap;
+  for (size_t t = 0; t < c.rope_list.size(); ++t)
+    if (c.rope_list[t].first == L.inv_freq)
+      qa.rope_cs = c.rope_cs + t * (size_t)c.max_prefill * c.rope_half_max * 2;
   const int32_t *kcache, *vcache;
   if (lc.donor < 0) {
     prefill_linear(c, w.nrm, S, L.k, L.tk, w.kraw, kEpiPlain, nullptr, &nrm_planes);

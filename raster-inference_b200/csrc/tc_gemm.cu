@@ -435,12 +435,20 @@ __device__ __forceinline__ void cluster_sync_all() {
 // tiled 3D TMA load into this CTA's shared memory whose completion is counted
 // on an mbarrier of either CTA of the pair (no multicast)
 __device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, int x, int y, int z,
-                                                 uint32_t bar_cluster) {
+                                                 uint32_t bar_cluster, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
-      "%4}], [%5];" ::"r"(su32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar_cluster)
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+      "[%1, {%2, %3, %4}], [%5], %6;" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar_cluster), "l"(policy)
       : "memory");
+}
+// L2 policies: the operand every tile of a wave re-reads stays (evict_last),
+// the one read once streams through (evict_first)
+__device__ __forceinline__ uint64_t l2_policy(bool keep) {
+  uint64_t p;
+  if (keep) asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  else asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 __device__ __forceinline__ void mma_i8_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
@@ -518,6 +526,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---- producer (both CTAs): this CTA's A rows and weight plane, counted
     // on the leader's stage barrier
     if (lane == 0) {
+      // m_fast: the activation tiles are re-read by every weight tile
+      const uint64_t pol_a = l2_policy(m_fast != 0), pol_b = l2_policy(m_fast == 0);
       int q = 0;
       for (int it = 0; it < my_tiles; ++it) {
         int m0, nt;
@@ -529,8 +539,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (rank == 0) mbar_expect_tx(&full[st], 2 * kT2Stage);
           const uint32_t bar = mapa_rank(su32(&full[st]), 0);
           for (int a = 0; a < 4; ++a)
-            tma_load_3d_pair(sbuf + a * kTcATile, &amap, kb * kTcKB, m0 + kTcM * (int)rank, a, bar);
-          tma_load_3d_pair(sbuf + 4 * kTcATile, &bmap, kb * kTcKB, nt * kTcN, (int)rank, bar);
+            tma_load_3d_pair(sbuf + a * kTcATile, &amap, kb * kTcKB, m0 + kTcM * (int)rank, a, bar, pol_a);
+          tma_load_3d_pair(sbuf + 4 * kTcATile, &bmap, kb * kTcKB, nt * kTcN, (int)rank, bar, pol_b);
         }
       }
     }
