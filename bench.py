@@ -135,7 +135,8 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "window": "from the 4096-token prefills through the timed decode steps"}
 
 
 # ---------------------------------------------------------------------------
@@ -298,6 +299,32 @@ def decode_step_bytes(cfg, ctx):
         if l < L - shared:
             total += 2 * kv * hd * H * 2 + 2 * kv * hd * 4
     return total
+
+
+INT8_PEAK_OPS = 4.5e15  # B200 dense int8 tensor ops/s, nominal (no measured int8 figure on this pool)
+
+
+def prefill_int8_ops(cfg, S):
+    """int8 tensor-core ops (2 per multiply-add) of one S-token prefill:
+    every projection as 8 byte-limb products per det multiply-add (4
+    activation limbs x 2 weight limbs of i16 weights; the KV-sharing layers'
+    unused k/v projections excluded), the PLE model projection, and the
+    attention's 16 (scores) + 12 (weighted values) limb products per (query,
+    key, dim) of each head.  lm_head runs as a GEMV on the last row only."""
+    t = cfg["text_config"]
+    H, F, Hq, kv, d, dg, P, L, W = (t["hidden_size"], t["intermediate_size"], t["num_attention_heads"],
+                                    t["num_key_value_heads"], t["head_dim"], t["global_head_dim"],
+                                    t["hidden_size_per_layer_input"], t["num_hidden_layers"], t["sliding_window"])
+    shared = t.get("num_kv_shared_layers") or 0
+    macs = L * P * H * S * 8
+    for l, lt in enumerate(t["layer_types"]):
+        sliding = lt == "sliding_attention"
+        hd = d if sliding else dg
+        proj = Hq * hd * H + H * Hq * hd + 3 * F * H + 2 * P * H + (2 * kv * hd * H if l < L - shared else 0)
+        macs += proj * S * 8
+        pairs = sum(min(i + 1, W) for i in range(S)) if sliding else S * (S + 1) // 2
+        macs += Hq * hd * pairs * 28
+    return 2 * macs
 
 
 def gemv_roofline(torch, rdet, cfg, device, copies=8, rounds=3, check=False):
@@ -483,6 +510,10 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.ExternalStream(model.stream, device=f"cuda:{local_rank}")
     seq = model.new_sequence(ctx + args.warmup + args.steps + 64)
     ids = lcg_ids(ctx, t["vocab_size"], SEED + rank)
+    # clocks: sampled from the prefills below through the timed decode region
+    # (the decode region alone is shorter than the sampler's 200 ms period)
+    clk = ClockSampler(local_rank)
+    clk.__enter__()
     # prefill of the 4096-token prompt (the prefill field: median of three
     # prefills on fresh sequences after one untimed prefill)
     prefill_runs = []
@@ -504,12 +535,12 @@ def run_ours(args, rank, world, local_rank):
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local_rank) as clk:
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        toks = seq.generate(args.steps)
-        b.record(stream)
-        torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    toks = seq.generate(args.steps)
+    b.record(stream)
+    torch.cuda.synchronize()
+    clk.__exit__(None, None, None)
     if dist:
         dist.barrier()
     sec = a.elapsed_time(b) / 1000
@@ -575,7 +606,11 @@ def run_ours(args, rank, world, local_rank):
             runs.append(p0.elapsed_time(p1) / 1000)
             ps.free()
         psec = statistics.median(runs)
-        prefill_lengths[str(plen)] = {"tok_s": plen / psec, "seconds": psec, "runs": 3}
+        ops = prefill_int8_ops(cfg, plen)
+        prefill_lengths[str(plen)] = {"tok_s": plen / psec, "seconds": psec, "runs": 3,
+                                      "int8_util": ops / psec / INT8_PEAK_OPS,
+                                      "int8_util_note": "whole prefill: the tensor-core GEMMs' and attention's int8 "
+                                                        "ops / prefill time / 4.5 POPS nominal dense int8"}
     # batched ragged decode: 64 sequences, prompt lengths
     # 128 + draw % 3969 (seeded), greedy: one batched decode_transition per
     # step, then select_output_token for every sequence
@@ -662,7 +697,8 @@ def run_ours(args, rank, world, local_rank):
                    "model": "gemma-4-e4b-text-standin", "context": ctx, "global_batch": world,
                    "parallelism": f"replicas{world}", "l2": "inputs larger than L2 (all weights streamed every step)",
                    "weight_bytes_hbm": weight_bytes},
-        "prefill": {"tokens": ctx, "tok_s": ctx / prefill_s, "seconds": prefill_s},
+        "prefill": {"tokens": ctx, "tok_s": ctx / prefill_s, "seconds": prefill_s,
+                    "int8_util": prefill_int8_ops(cfg, ctx) / prefill_s / INT8_PEAK_OPS},
         "prefill_config3": prefill_lengths,
         "config4": config4,
         "e2e": e2e,
