@@ -493,6 +493,73 @@ def run_kernel_case(args):
             print(line)
 
 
+def batched_run(args, torch, rdet, dist, model, stream, t, rank, world, local_rank, mode):
+    """64 sequences, prompt lengths 128 + draw % 3969
+    (seeded), greedy: one batched decode_transition per step, then
+    select_output_token for every sequence.  mode "single": all sequences on
+    this GPU; "split": sequence i on rank i % world, each rank one batched
+    decode of its own sequences per step; "tp": every rank decodes all of them
+    through the tensor-parallel path.  Steps are device-timed per step (the
+    selects between steps are not), max over ranks; the first 3 steps warm
+    up.  The CPU oracle's 4-sequence subset is checked token for token."""
+    lens = [128 + (x % 3969) for x in lcg_ids(args.batch, 1 << 30, SEED + 7)]
+    mine = [i for i in range(args.batch) if mode != "split" or i % world == rank]
+    if mode == "tp":
+        uid = [rdet.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        model.tp_init(rank, world, uid[0])
+    nsteps = args.batch_steps
+    seqs = [model.new_sequence(lens[i] + nsteps + 8) for i in mine]
+    for sq, i in zip(seqs, mine):
+        sq.prefill(lcg_ids(lens[i], t["vocab_size"], SEED + 100 + i))
+    toks = [sq.select() for sq in seqs]
+    gen = {i: [] for i in mine}
+    step_ms = []
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    for step in range(nsteps):
+        for i, tk in zip(mine, toks):
+            gen[i].append(tk)
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record(stream)
+        rdet.decode_batch(model, seqs, toks)
+        b1.record(stream)
+        toks = [sq.select() for sq in seqs]  # synchronizes
+        step_ms.append(b0.elapsed_time(b1))
+    timed = step_ms[3:] if len(step_ms) > 6 else step_ms
+    bsec = sum(timed) / 1000
+    # fixture check: mismatching and checked sequences, summed over the ranks
+    bad = checked = 0
+    fx = load_fixtures()
+    if fx and "config5" in fx and nsteps >= fx["config5"]["tokens_per_sequence"] and args.batch == fx["config5"]["batch"]:
+        n5 = fx["config5"]["tokens_per_sequence"]
+        for k, r in fx["config5"]["sequences"].items():
+            if int(k) in gen:
+                checked += 1
+                bad += gen[int(k)][:n5] != r["tokens"]
+    if dist:
+        tt = torch.tensor([bsec], dtype=torch.float64, device=f"cuda:{local_rank}")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        bsec = float(tt[0])
+        cc = torch.tensor([bad, checked], dtype=torch.int64, device=f"cuda:{local_rank}")
+        dist.all_reduce(cc, op=dist.ReduceOp.SUM)
+        bad, checked = int(cc[0]), int(cc[1])
+        if mode == "tp":  # every rank checked the same sequences
+            bad, checked = bad // world, checked // world
+    for sq in seqs:
+        sq.free()
+    par = {"single": "single", "split": f"sequences split over {world} ranks", "tp": f"tp{world}"}[mode]
+    return {"sequences": args.batch, "context": f"128 + draw mod 3969 (seeded), mean {sum(lens) // len(lens)}",
+            "parallelism": par, "scaling": None if mode == "single" else "strong",
+            "steps": nsteps, "timed_steps": len(timed), "tok_s": args.batch * len(timed) / bsec,
+            "ms_per_step": 1000 * bsec / len(timed),
+            "bit_exact_vs_cpu": (bad == 0) if checked else None, "checked_sequences": checked,
+            "note": "greedy: device-timed batched decode_transition per step (max over ranks), "
+                    "select_output_token per sequence between steps (not timed); the first 3 steps are warm-up; "
+                    "bit_exact_vs_cpu checks the CPU oracle's 4-sequence subset (tests/golden/e4b_fixtures.json)"}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     rdet = importlib.import_module("raster-inference_b200")
@@ -614,57 +681,16 @@ def run_ours(args, rank, world, local_rank):
     # batched ragged decode: 64 sequences, prompt lengths
     # 128 + draw % 3969 (seeded), greedy: one batched decode_transition per
     # step, then select_output_token for every sequence
-    batched = None
+    batched = batched_tp = None
     if args.batch > 0:
-        bm, bstream = model, stream  # max_prefill (the context) >= the batch rows
-        # N > 1: the batch is sharded across the ranks (tensor-parallel, same
-        # sequences on every rank): strong scaling of this line
-        tp = world > 1
-        if tp:
-            uid = [rdet.nccl_unique_id() if rank == 0 else None]
-            dist.broadcast_object_list(uid, src=0)
-            bm.tp_init(rank, world, uid[0])
-        lens = [128 + (x % 3969) for x in lcg_ids(args.batch, 1 << 30, SEED + 7)]
-        nsteps = args.batch_steps
-        seqs = [bm.new_sequence(n + nsteps + 8) for n in lens]
-        for i, (sq, n) in enumerate(zip(seqs, lens)):
-            sq.prefill(lcg_ids(n, t["vocab_size"], SEED + 100 + i))
-        toks = [sq.select() for sq in seqs]
-        gen = [[] for _ in seqs]
-        step_ms = []
-        torch.cuda.synchronize()
-        if dist:
-            dist.barrier()
-        for step in range(nsteps):
-            for i, tk in enumerate(toks):
-                gen[i].append(tk)
-            b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            b0.record(bstream)
-            rdet.decode_batch(bm, seqs, toks)
-            b1.record(bstream)
-            toks = [sq.select() for sq in seqs]  # synchronizes
-            step_ms.append(b0.elapsed_time(b1))
-        timed = step_ms[3:] if len(step_ms) > 6 else step_ms  # the first steps warm up
-        bsec = sum(timed) / 1000
-        if dist:
-            tt = torch.tensor([bsec], dtype=torch.float64, device=f"cuda:{local_rank}")
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            bsec = float(tt[0])
-        exact = None
-        fx = load_fixtures()
-        if fx and "config5" in fx and nsteps >= fx["config5"]["tokens_per_sequence"] and args.batch == fx["config5"]["batch"]:
-            n5 = fx["config5"]["tokens_per_sequence"]
-            exact = all(gen[int(k)][:n5] == r["tokens"] for k, r in fx["config5"]["sequences"].items())
-        batched = {"sequences": args.batch, "context": f"128 + draw mod 3969 (seeded), mean {sum(lens) // len(lens)}",
-                   "parallelism": f"tp{world}" if tp else "single", "scaling": "strong" if tp else None,
-                   "steps": nsteps, "timed_steps": len(timed), "tok_s": args.batch * len(timed) / bsec,
-                   "ms_per_step": 1000 * bsec / len(timed),
-                   "bit_exact_vs_cpu": exact,
-                   "note": "greedy: device-timed batched decode_transition per step, select_output_token per "
-                           "sequence between steps (not timed); the first 3 steps are warm-up; bit_exact_vs_cpu "
-                           "checks the CPU oracle's 4-sequence subset (tests/golden/e4b_fixtures.json)"}
-        for sq in seqs:
-            sq.free()
+        # N > 1: "split" gives each rank its share of the 64 sequences (no
+        # collective: sequences are independent), then "tp" decodes all 64 on
+        # every rank with the tensor-parallel path (rdet_tp_init); both are
+        # strong scaling of the same batch.  N = 1: one unsharded run.
+        batched = batched_run(args, torch, rdet, dist, model, stream, t, rank, world, local_rank,
+                              "split" if world > 1 else "single")
+        if world > 1:
+            batched_tp = batched_run(args, torch, rdet, dist, model, stream, t, rank, world, local_rank, "tp")
     # roofline of the dominant kernel (det GEMV)
     per, gbs, bytes_per_launch, sec_per_launch, gemv_exact = gemv_roofline(torch, rdet, cfg, local_rank,
                                                                             check=(rank == 0))
@@ -703,6 +729,7 @@ def run_ours(args, rank, world, local_rank):
         "config4": config4,
         "e2e": e2e,
         "batched_decode": batched,
+        "batched_decode_tp": batched_tp,
         "gpu_launches": kernels_per_step * args.steps,
         "roofline": {"bound": "hbm", "kernel": "rdet::gemv3_kernel", "achieved": gbs, "peak": peak,
                      "unit": "GB/s", "frac": gbs / peak, "peak_kind": peak_kind,
