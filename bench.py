@@ -409,6 +409,42 @@ def run_kernel_case(args):
         model.close()
         print(f"prefill: {args.ctx} tokens")
         return
+    if args.kernel_case == "convert":
+        # model ingestion: a vocab x hidden bf16 tensor (lm_head-sized) to Q16.16
+        # on the GPU (device time, CUDA events) and through convert.py's GPU
+        # path with the host<->device copies, beside the host form
+        convert = importlib.import_module("raster-inference_b200.convert")
+        import numpy as np
+        rows, cols = t["vocab_size"], t["hidden_size"]
+        rng = np.random.default_rng(3)
+        w = rng.normal(0, 0.02, (rows, cols)).astype(np.float32)
+        raw = (w.view(np.uint32) >> 16).astype("<u2").tobytes()
+        src = torch.from_numpy(np.frombuffer(raw, dtype=np.uint8).copy()).to(dev)
+        out = torch.empty(rows * cols, dtype=torch.int32, device=dev)
+        mass = torch.empty(rows, dtype=torch.int64, device=dev)
+        stats = torch.zeros(2, dtype=torch.int32, device=dev)
+        rdet.convert_to_wgt(src.data_ptr(), "BF16", rows, cols, out.data_ptr(), mass.data_ptr(), stats.data_ptr())
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        rdet.convert_to_wgt(src.data_ptr(), "BF16", rows, cols, out.data_ptr(), mass.data_ptr(), stats.data_ptr())
+        e1.record()
+        torch.cuda.synchronize()
+        dev_s = e0.elapsed_time(e1) / 1000
+        t0 = time.perf_counter()
+        gb, gm = convert.convert_tensor_gpu(memoryview(raw), "BF16", (rows, cols), 0)
+        gpu_s = time.perf_counter() - t0
+        from concurrent.futures import ThreadPoolExecutor
+        with ThreadPoolExecutor(max_workers=host_cores()) as pool:
+            t0 = time.perf_counter()
+            hb, hm = convert.convert_tensor(memoryview(raw), "BF16", (rows, cols), pool)
+            host_s = time.perf_counter() - t0
+        n = rows * cols
+        print(json.dumps({"case": "convert bf16", "values": n, "device_gvalues_s": n / dev_s / 1e9,
+                          "device_gbs": n * 6 / dev_s / 1e9, "gpu_path_gvalues_s": n / gpu_s / 1e9,
+                          "host_gvalues_s": n / host_s / 1e9, "host_cores": host_cores(),
+                          "identical": bool(np.array_equal(gb, hb) and np.array_equal(gm, hm))}))
+        return
     if args.kernel_case == "tcattn":
         # prefill attention on the tensor cores (rdet_det_attention_prefill) for
         # a full layer (head_dim 512, causal) and a sliding layer (head_dim 256,
@@ -832,7 +868,7 @@ def main():
     ap.add_argument("--config4-tokens", type=int, default=256, help="greedy tokens of the config-4 line (0: skip)")
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched ragged decode line (0: skip)")
     ap.add_argument("--batch-steps", type=int, default=128, help="greedy steps of the batched line (config 5: 128)")
-    ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc", "tcattn", "prefill"],
+    ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc", "tcattn", "prefill", "convert"],
                     help="run a few launches of one kernel at E4B shapes for an ncu capture, then exit")
     ap.add_argument("--time-calls", type=int, default=0,
                     help="with --kernel-case attn: time this many back-to-back calls of each decode-attention entry "

@@ -183,6 +183,22 @@ int32_t rdet_det_attention_prefill(const int32_t* q, const int32_t* k_cache, con
                                    uint32_t n_tokens, uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
                                    uint32_t window, uint32_t flags, int32_t* out, void* stream);
 
+/* Model ingestion on the GPU: safetensors values to det Q16.16 weights
+ * (f32_to_wgt, det_num/convert.rs:77-93, as the reference's
+ * gemma-det-num-wgt-converter applies it, tools/gemma-det-num-wgt-converter/
+ * main.rs:218-388).  src holds rows * row_len little-endian values of dtype
+ * RDET_SRC_*; out[i] = round half to even of value * 2^16, saturated to i32
+ * (0 for a non-finite value); row_mass[r] = sum over the row of |out| (the
+ * converter's overflow-bound input); stats[0] = the number of non-finite
+ * values (the reference rejects the tensor when it is not 0), stats[1] = 1
+ * when some value does not fit i16 (the tensor is then stored at width 32).
+ * All pointers are device memory; stats is zeroed by the call. */
+#define RDET_SRC_F32 0
+#define RDET_SRC_BF16 1
+#define RDET_SRC_F16 2
+int32_t rdet_convert_to_wgt(const void* src, int32_t dtype, uint64_t rows, uint64_t row_len, int32_t* out,
+                            uint64_t* row_mass, uint32_t* stats, void* stream);
+
 /* Decode attention that allocates nothing.  Same arguments and the same
  * bit-exact result as rdet_det_attention_decode, for callers that cannot
  * allocate device memory while they run: a serving process that hands all of

@@ -38,7 +38,7 @@ SYMBOLS = [
     "rdet_prefill_finalize", "rdet_select", "rdet_decode", "rdet_decode_begin", "rdet_decode_range",
     "rdet_decode_finalize", "rdet_generate", "rdet_read", "rdet_commitment", "rdet_kv_prefix_commitments",
     "rdet_det_gemv", "rdet_det_linear",
-    "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_det_attention_prefill", "rdet_get_stream", "rdet_tensor_core_prefill", "rdet_nccl_unique_id", "rdet_tp_init", "rdet_tp_world", "rdet_seq_kernels_per_step", "rdet_last_error",
+    "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_det_attention_prefill", "rdet_convert_to_wgt", "rdet_get_stream", "rdet_tensor_core_prefill", "rdet_nccl_unique_id", "rdet_tp_init", "rdet_tp_world", "rdet_seq_kernels_per_step", "rdet_last_error",
     "rdet_version",
 ]
 
@@ -99,6 +99,7 @@ def lib() -> C.CDLL:
         "rdet_det_attention_decode": [p, p, p, u32, u32, u32, u32, u32, u32, p, p],
         "rdet_det_attention_decode_noalloc": [p, p, p, u32, u32, u32, u32, u32, u32, p, p],
         "rdet_det_attention_prefill": [p, p, p, u32, u32, u32, u32, u32, u32, u32, p, p],
+        "rdet_convert_to_wgt": [p, i32, C.c_uint64, C.c_uint64, p, p, p, p],
         "rdet_get_stream": [p, p],
         "rdet_tensor_core_prefill": [p],
         "rdet_nccl_unique_id": [p, sz],
@@ -373,6 +374,19 @@ def det_attention_prefill(q_ptr: int, k_ptr: int, v_ptr: int, cap: int, n_tokens
                                             num_heads, num_kv_heads, head_dim, window,
                                             0 if tensor_cores else FLAG_NO_TENSOR_CORES, C.c_void_p(out_ptr),
                                             C.c_void_p(stream) if stream else None))
+
+
+SRC_DTYPES = {"F32": 0, "BF16": 1, "F16": 2}
+
+
+def convert_to_wgt(src_ptr: int, dtype: str, rows: int, row_len: int, out_ptr: int, row_mass_ptr: int,
+                   stats_ptr: int, stream: int = 0):
+    """safetensors values -> Q16.16 weights on the GPU (rdet_convert_to_wgt):
+    out = f32_to_wgt(value), row_mass = sum |out| per row, stats = [non-finite
+    count, does not fit i16]; all device pointers."""
+    _check(lib().rdet_convert_to_wgt(C.c_void_p(src_ptr), SRC_DTYPES[dtype], rows, row_len, C.c_void_p(out_ptr),
+                                     C.c_void_p(row_mass_ptr), C.c_void_p(stats_ptr),
+                                     C.c_void_p(stream) if stream else None))
 
 
 def det_attention_decode_noalloc(q_ptr: int, k_ptr: int, v_ptr: int, cap: int, num_heads: int, num_kv_heads: int,

@@ -18,12 +18,13 @@ main.rs:218-560`` with ``src/shared/numerics/det_num/convert.rs:77-189``:
   rank-1 tensors record their mass without the check;
 * a tensor whose every value fits i16 is stored at half width.
 
-Conversion is a one-time host step per model: streamed tensor by tensor (memory
-holds one tensor at a time), each tensor's rows converted in chunks on all host
-cores; the GPU loads the output.
+Conversion is a one-time step per model, streamed tensor by tensor (memory
+holds one tensor at a time): each tensor's rows convert in chunks on all host
+cores, or with ``--device N`` on that GPU (``rdet_convert_to_wgt``, the same
+results); the GPU loads the output.
 
     python -m raster-inference_b200.convert --input <model-dir-or-safetensors> \\
-        --output-dir <new-dir> [--config config.json] [--report-bounds] [--report-widths]
+        --output-dir <new-dir> [--config config.json] [--device N] [--report-bounds] [--report-widths]
 """
 from __future__ import annotations
 
@@ -101,6 +102,33 @@ def convert_tensor(raw, dtype: str, shape, pool=None, chunk_values: int = 1 << 2
         for f in [pool.submit(_convert_rows, raw, dtype, row, r0, r1, out, mass) for r0, r1 in spans]:
             f.result()
     return out, mass
+
+
+def convert_tensor_gpu(raw, dtype: str, shape, device: int):
+    """convert_tensor on the GPU (rdet_convert_to_wgt): the raw values go to
+    the device, the Q16.16 bits and row masses come back.  Same results as the
+    host form; fails loudly when the CUDA library or device is missing."""
+    import torch  # device memory only
+
+    from . import convert_to_wgt
+
+    n = int(np.prod(shape)) if len(shape) else 1
+    row = max(int(shape[-1]) if len(shape) else 1, 1)
+    rows = n // row if n else 0
+    if n == 0:
+        return np.empty(0, dtype=np.int32), np.zeros(0, dtype=np.uint64)
+    dev = torch.device("cuda", device)
+    src = torch.from_numpy(np.frombuffer(raw, dtype=np.uint8).copy()).to(dev)
+    out = torch.empty(n, dtype=torch.int32, device=dev)
+    mass = torch.empty(rows, dtype=torch.int64, device=dev)
+    stats = torch.zeros(2, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    convert_to_wgt(src.data_ptr(), dtype, rows, row, out.data_ptr(), mass.data_ptr(), stats.data_ptr(),
+                   stream.cuda_stream)
+    st = stats.cpu().numpy()
+    if st[0]:
+        raise ValueError("f32_to_wgt requires a finite source value")
+    return out.cpu().numpy(), mass.cpu().numpy().view(np.uint64)
 
 
 class SafeTensors:
@@ -202,10 +230,11 @@ def _check_row_mass(name: str, shape, mass: np.ndarray) -> int:
     return int(mass.max())
 
 
-def convert(input_path: str, output_dir: str, config: str | None = None) -> dict:
+def convert(input_path: str, output_dir: str, config: str | None = None, device: int | None = None) -> dict:
     """convert_model_to_det_num_wgt_artifact (main.rs:218-320): returns the
     summary (tensor count, input and output payload bytes, per-tensor width
-    and max row mass)."""
+    and max row mass).  device: a CUDA device ordinal converts the values on
+    that GPU (rdet_convert_to_wgt), None on the host cores."""
     weights, cfg = _resolve(input_path, config)
     _prepare_output(output_dir)
     st = SafeTensors(weights)
@@ -219,7 +248,10 @@ def convert(input_path: str, output_dir: str, config: str | None = None) -> dict
             dtype, shape, raw = st.tensor(name)
             in_bytes += len(raw)
             try:
-                bits, row_mass = convert_tensor(raw, dtype, shape, pool)
+                if device is None:
+                    bits, row_mass = convert_tensor(raw, dtype, shape, pool)
+                else:
+                    bits, row_mass = convert_tensor_gpu(raw, dtype, shape, device)
             except ValueError as e:
                 raise ValueError(f"failed to convert tensor `{name}` to Wgt: {e}") from None
             mass = _check_row_mass(name, shape, row_mass)
@@ -250,8 +282,10 @@ def main(argv=None) -> int:
     ap.add_argument("--config")
     ap.add_argument("--report-bounds", action="store_true")
     ap.add_argument("--report-widths", action="store_true")
+    ap.add_argument("--device", type=int, default=None,
+                    help="convert the values on this CUDA device (default: on the host cores)")
     a = ap.parse_args(argv)
-    s = convert(a.input, a.output_dir, a.config)
+    s = convert(a.input, a.output_dir, a.config, a.device)
     print(f"converted {s['tensor_count']} tensors: {s['input_tensor_bytes']} source bytes -> "
           f"{s['output_tensor_bytes']} payload bytes ({s['output_weights_path']})")
     b = s["tensor_bounds"]

@@ -309,6 +309,14 @@ void launch_add_i32(int32_t* p, int32_t v, cudaStream_t s);  // *p += v
 void launch_add_i32_rows(int32_t* const* p, int32_t n, int32_t v, cudaStream_t s);  // *p[i] += v
 void launch_requantize_rows(const int64_t* x, size_t n, int32_t* y, cudaStream_t s);  // y = requantize(x)
 // vocab-sharded logits: src [world][rows][vl] -> dst[r][w * vl + j]
+// ---- model ingestion: safetensors values -> Q16.16 weights (convert.cu) --------------
+enum SrcDtype : int32_t { kSrcF32 = 0, kSrcBF16 = 1, kSrcF16 = 2 };
+// out[r * row_len + k] = f32_to_wgt(src value), row_mass[r] = sum_k |out|;
+// stats[0] += non-finite values (written as 0), stats[1] |= 1 when a value
+// does not fit i16.  stats must start at zero.
+void launch_convert_wgt(const void* src, int dtype, uint64_t rows, uint64_t row_len, int32_t* out,
+                        uint64_t* row_mass, uint32_t* stats, cudaStream_t s);
+
 void launch_gather_vocab(const int32_t* src, int32_t world, int32_t rows, int32_t vl, int32_t* const* dst,
                          cudaStream_t s);
 // dst[r] + off <- src row r (n ints), for r < rows; cap > 0 applies the

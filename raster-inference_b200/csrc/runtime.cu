@@ -2884,6 +2884,21 @@ int32_t rdet_det_attention_prefill(const int32_t* q, const int32_t* k_cache, con
   });
 }
 
+int32_t rdet_convert_to_wgt(const void* src, int32_t dtype, uint64_t rows, uint64_t row_len, int32_t* out,
+                            uint64_t* row_mass, uint32_t* stats, void* stream) {
+  return guard([&] {
+    kernels_init();
+    REQUIRE(dtype == kSrcF32 || dtype == kSrcBF16 || dtype == kSrcF16, RDET_E_INVALID,
+            "dtype must be RDET_SRC_F32, RDET_SRC_BF16 or RDET_SRC_F16");
+    REQUIRE(rows == 0 || (src && out && row_mass && stats), RDET_E_INVALID, "null argument");
+    REQUIRE(rows == 0 || row_len > 0, RDET_E_RANGE, "row_len must be positive");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (stats) CK(cudaMemsetAsync(stats, 0, 2 * sizeof(uint32_t), s));
+    launch_convert_wgt(src, dtype, rows, row_len, out, row_mass, stats, s);
+    CK(cudaGetLastError());
+  });
+}
+
 int32_t rdet_det_linear(const int32_t* x, uint32_t n_rows_x, const void* w, int32_t width, uint32_t rows,
                         uint32_t cols, int32_t* y, void* stream) {
   return guard([&] {
