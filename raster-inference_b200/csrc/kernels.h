@@ -81,8 +81,9 @@ struct TcWeight {           // byte planes of one weight matrix (or a gate/up pa
 struct TcAct {              // byte planes of one activation matrix
   alignas(64) unsigned char map[128];    // 128-row boxes
   alignas(64) unsigned char map_t[128];  // 64-row boxes (S <= 64: short-row-count kernel)
-  uint8_t* planes = nullptr;           // [4][S][K]
-  uint64_t* rowsum = nullptr;          // [S] sum over k of X + 2^31
+  uint8_t* planes = nullptr;           // [4][S][K] byte limbs of X + 2^e (e per row: 23 or 31)
+  uint64_t* rowsum = nullptr;          // [S] sum over k of X + 2^e; top bit set when e = 23
+  uint32_t* tile4 = nullptr;           // [S / 256] 1 when a 256-row tile has a row with e = 31 (or null)
   int32_t S = 0, K = 0;
 };
 bool tc_supported();                         // current device is sm_100

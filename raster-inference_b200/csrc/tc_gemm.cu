@@ -70,6 +70,24 @@ constexpr int kTcSmem = kTcStages * kTcStage + kTcStageOut + 1024;  // + alignme
 constexpr int kTcEpiWarps = 8;  // two per TMEM lane quarter, each half of the columns
 constexpr int kTcThreads = 32 * (kTcEpiWarps + 2);
 constexpr uint32_t kTcCols = 512;  // TMEM columns allocated (480 used)
+constexpr int kT2Mrows = 256;      // tokens per CTA-pair tile
+constexpr uint64_t kRowOff23 = 1ull << 63;  // row-sum flag: the row's offset is 2^23, not 2^31
+
+// An activation row's corrections.  Its planes hold X + 2^e (e = 23 when the
+// row sum's top bit is set, else 31), so for one output
+//   sum X W = sum X_u W_u - 2^15 sum X_u - 2^e sum W_u + 2^(15 + e) K.
+// row_corr = 2^15 sum X_u - 2^(15 + e) K (wrapping); the weight term is
+// brow << e.
+struct RowCorr {
+  uint64_t corr;
+  uint32_t e;
+};
+__device__ __forceinline__ RowCorr row_corr(uint64_t rw, int K) {
+  RowCorr r;
+  r.e = (rw & kRowOff23) ? 23u : 31u;
+  r.corr = ((rw & ~kRowOff23) << 15) - ((uint64_t)K << (15 + r.e));
+  return r;
+}
 
 using namespace tcx;
 
@@ -81,19 +99,30 @@ constexpr uint32_t kTcIdescHalf = idesc_u8(kTcN); // one byte plane
 // operand preparation
 // ---------------------------------------------------------------------------
 
-// Activation rows -> four byte planes of X + 2^31 and the row sums of X + 2^31.
+// Activation rows -> four byte planes of X + 2^e and the row sums of X + 2^e,
+// e chosen per row: 23 when every value of the row lies in [-2^23, 2^23) (then
+// X + 2^23 < 2^24 and limb 3 is zero), else 31.  The row sum carries the choice
+// in its top bit (set for 23; a sum is below 2^47); tile4[row / 256] is set
+// when a row of that 256-row tile needs the fourth limb (tile4 starts at 0).
 __global__ void tc_act_prep_kernel(const int32_t* __restrict__ X, int S, int K, uint8_t* __restrict__ planes,
-                                   uint64_t* __restrict__ rowsum) {
+                                   uint64_t* __restrict__ rowsum, uint32_t* __restrict__ tile4) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int s = blockIdx.x;
   const int4* xr = reinterpret_cast<const int4*>(X + (size_t)s * K);
   const size_t plane = (size_t)S * K;
+  int wide = 0;
+  for (int c = threadIdx.x; c < K / 4 && !wide; c += blockDim.x) {
+    const int4 v = xr[c];
+    wide |= (v.x < -(1 << 23) || v.x >= (1 << 23) || v.y < -(1 << 23) || v.y >= (1 << 23) || v.z < -(1 << 23) ||
+             v.z >= (1 << 23) || v.w < -(1 << 23) || v.w >= (1 << 23));
+  }
+  const bool four = __syncthreads_or(wide) != 0;
+  const uint32_t off = four ? 0x80000000u : 0x00800000u;
   uint64_t sum = 0;
   for (int c = threadIdx.x; c < K / 4; c += blockDim.x) {
     const int4 v = xr[c];
-    const uint32_t u[4] = {(uint32_t)v.x + 0x80000000u, (uint32_t)v.y + 0x80000000u, (uint32_t)v.z + 0x80000000u,
-                           (uint32_t)v.w + 0x80000000u};
+    const uint32_t u[4] = {(uint32_t)v.x + off, (uint32_t)v.y + off, (uint32_t)v.z + off, (uint32_t)v.w + off};
     sum += (uint64_t)u[0] + u[1] + u[2] + u[3];
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
@@ -110,7 +139,8 @@ __global__ void tc_act_prep_kernel(const int32_t* __restrict__ X, int S, int K, 
   if (threadIdx.x == 0) {
     uint64_t t = 0;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
-    rowsum[s] = t;
+    rowsum[s] = four ? t : (t | kRowOff23);
+    if (four && tile4) atomicOr(&tile4[s / kT2Mrows], 1u);
   }
 }
 
@@ -296,7 +326,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int nbase = EPI == 2 ? nt * (kTcN / 2) : r0;
       const int m = m0 + rl;
       const bool mrow = m < S;
-      const uint64_t corr = (mrow ? (arow[m] << 15) : 0) - ((uint64_t)K << 46);
+      const RowCorr rc = row_corr(mrow ? arow[m] : 0, K);
       if (!mbar_wait(&accf, it & 1)) fail = 1;
       fence_after();
       if (EPI == 3) {
@@ -345,7 +375,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint64_t acc = (uint64_t)g[0][i >> 3][i & 7] + ((uint64_t)g[1][i >> 3][i & 7] << 8) +
                            ((uint64_t)g[2][i >> 3][i & 7] << 16) + ((uint64_t)g[3][i >> 3][i & 7] << 24) +
                            ((uint64_t)g[4][i >> 3][i & 7] << 32);
-            acc -= corr + (brow[r0 + pr] << 31);
+            acc -= rc.corr + (brow[r0 + pr] << rc.e);
             y = requantize((int64_t)acc);
           }
           stage_out[rl * kTcOutStride + pr] = y;
@@ -410,7 +440,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // Tiles go round the pairs in the order that keeps the smaller operand in L2
 // (m_fast: all token tiles of a weight tile before the next weight tile).
 // ---------------------------------------------------------------------------
-constexpr int kT2M = 2 * kTcM;                     // tokens per pair tile
+constexpr int kT2M = kT2Mrows;                     // tokens per pair tile
+static_assert(kT2M == 2 * kTcM, "a pair tile is two one-CTA tiles");
 constexpr int kT2Stages = 4;
 constexpr int kT2BTile = kTcN * kTcKB;             // 6 KB: one weight plane
 constexpr int kT2Stage = 4 * kTcATile + kT2BTile;  // 38 KB
@@ -478,7 +509,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_linear2_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
                       const uint64_t* __restrict__ arow, const uint64_t* __restrict__ brow, int S, int N, int K,
                       int ntiles_m, int ntiles_n, int m_fast, int32_t* __restrict__ Y,
-                      const int32_t* __restrict__ vec, int ldv) {
+                      const int32_t* __restrict__ vec, int ldv, const uint32_t* __restrict__ tile4) {
   extern __shared__ __align__(16) unsigned char tc_smem_raw[];
   __shared__ __align__(8) uint64_t full[kT2Stages], empty[kT2Stages], accf, tmem_empty;
   __shared__ uint32_t tmem_holder;
@@ -532,13 +563,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int it = 0; it < my_tiles; ++it) {
         int m0, nt;
         tile_of(it, m0, nt);
+        // a tile whose rows all fit 24 bits skips activation limb 3 (zero)
+        const int limbs = (tile4 == nullptr || tile4[m0 / kT2M]) ? 4 : 3;
+        const uint32_t tx = 2u * (uint32_t)(limbs * kTcATile + kT2BTile);
         for (int kb = 0; kb < nkb; ++kb, ++q) {
           const int st = q % kT2Stages;
           if (q >= kT2Stages && !mbar_wait(&empty[st], ((q / kT2Stages) - 1) & 1)) fail = 1;
           unsigned char* sbuf = smem + (size_t)st * kT2Stage;
-          if (rank == 0) mbar_expect_tx(&full[st], 2 * kT2Stage);
+          if (rank == 0) mbar_expect_tx(&full[st], tx);
           const uint32_t bar = mapa_rank(su32(&full[st]), 0);
-          for (int a = 0; a < 4; ++a)
+          for (int a = 0; a < limbs; ++a)
             tma_load_3d_pair(sbuf + a * kTcATile, &amap, kb * kTcKB, m0 + kTcM * (int)rank, a, bar, pol_a);
           tma_load_3d_pair(sbuf + 4 * kTcATile, &bmap, kb * kTcKB, nt * kTcN, (int)rank, bar, pol_b);
         }
@@ -550,6 +584,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int qlast = my_tiles * nkb;
       int q = 0;
       for (int it = 0; it < my_tiles; ++it) {
+        int m0, nt;
+        tile_of(it, m0, nt);
+        const bool four = tile4 == nullptr || tile4[m0 / kT2M];
         if (!mbar_wait(&tmem_empty, it & 1)) fail = 1;
         fence_after();
         for (int kb = 0; kb < nkb; ++kb, ++q) {
@@ -568,10 +605,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               mma_i8_pair(tmem + 0 * kTcN, ad[0], bdesc, kT2Idesc, 0u);
               mma_i8_pair(tmem + 2 * kTcN, ad[2], bdesc, kT2Idesc, 0u);
               mma_i8_pair(tmem + 1 * kTcN, ad[1], bdesc, kT2Idesc, 1u);
-              mma_i8_pair(tmem + 3 * kTcN, ad[3], bdesc, kT2Idesc, 1u);  // block 4 was zeroed
+              if (four) mma_i8_pair(tmem + 3 * kTcN, ad[3], bdesc, kT2Idesc, 1u);  // block 4 was zeroed
             } else {
 #pragma unroll
-              for (int a = 0; a < 4; ++a) mma_i8_pair(tmem + (uint32_t)(kTcN * a), ad[a], bdesc, kT2Idesc, 1u);
+              for (int a = 0; a < 3; ++a) mma_i8_pair(tmem + (uint32_t)(kTcN * a), ad[a], bdesc, kT2Idesc, 1u);
+              if (four) mma_i8_pair(tmem + 3 * kTcN, ad[3], bdesc, kT2Idesc, 1u);
             }
           }
           if (q + kT2Stages < qlast) mma_commit_pair(&empty[st]);
@@ -605,7 +643,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int nbase = EPI == 2 ? nt * (kTcN / 2) : r0;
       const int m = m0 + rl;
       const bool mrow = m < S;
-      const uint64_t corr = (mrow ? (arow[m] << 15) : 0) - ((uint64_t)K << 46);
+      const RowCorr rc = row_corr(mrow ? arow[m] : 0, K);
       if (!mbar_wait(&accf, it & 1)) fail = 1;
       fence_after();
       for (int c0 = half * kHalf; c0 < (half + 1) * kHalf; c0 += kStep) {
@@ -628,7 +666,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint64_t acc = (uint64_t)g[0][i >> 3][i & 7] + ((uint64_t)g[1][i >> 3][i & 7] << 8) +
                            ((uint64_t)g[2][i >> 3][i & 7] << 16) + ((uint64_t)g[3][i >> 3][i & 7] << 24) +
                            ((uint64_t)g[4][i >> 3][i & 7] << 32);
-            acc -= corr + (brow[r0 + pr] << 31);
+            acc -= rc.corr + (brow[r0 + pr] << rc.e);
             y = requantize((int64_t)acc);
           }
           stage_out[rl * kTcOutStride + pr] = y;
@@ -803,7 +841,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int item = blockIdx.x + it * gridDim.x, t = item / ks, sp = item % ks;
       const int r = (t % tiles_n) * kTsM + rl, t0 = (t / tiles_n) * kTsT;
       const bool rok = EPI == 3 ? r < nrows : r < N;
-      const uint64_t bcorr = (EPI == 0 && rok) ? (brow[r] << 31) - ((uint64_t)K << 46) : 0;
+      const uint64_t bw = (EPI == 0 && rok) ? brow[r] : 0;
       if (!mbar_wait(&accf, it & 1)) fail = 1;
       fence_after();
       for (int c0 = 32 * half; c0 < 32 * half + 32; c0 += 8) {
@@ -818,7 +856,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint64_t raw = (uint64_t)g[0][i] + ((uint64_t)g[1][i] << 8) + ((uint64_t)g[2][i] << 16) +
                                  ((uint64_t)g[3][i] << 24) + ((uint64_t)g[4][i] << 32);
             if (EPI == 3) part[((size_t)sp * S + tok) * nrows + r] = raw;
-            else Y[(size_t)tok * N + r] = requantize((int64_t)(raw - (arow[tok] << 15) - bcorr));
+            else {
+              const RowCorr rc = row_corr(arow[tok], K);
+              Y[(size_t)tok * N + r] = requantize((int64_t)(raw - rc.corr - (bw << rc.e)));
+            }
           }
         }
       }
@@ -851,10 +892,10 @@ __global__ void tc_splitk_reduce_kernel(const uint64_t* __restrict__ part, int k
   for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
     const int m = (int)(e / N), n = (int)(e % N);
     const int r = MODE == 2 ? kTcN * (n / (kTcN / 2)) + n % (kTcN / 2) : n;
-    const uint64_t corr = (arow[m] << 15) - ((uint64_t)K << 46);
+    const RowCorr rc = row_corr(arow[m], K);
     uint64_t acc = 0;
     for (int sp = 0; sp < ks; ++sp) acc += part[((size_t)sp * S + m) * nrows + r];
-    acc -= corr + (brow[r] << 31);
+    acc -= rc.corr + (brow[r] << rc.e);
     if (MODE == 3) {
       Y64[e] = (int64_t)acc;
       continue;
@@ -864,7 +905,7 @@ __global__ void tc_splitk_reduce_kernel(const uint64_t* __restrict__ part, int k
       const int ru = r + kTcN / 2;
       uint64_t accu = 0;
       for (int sp = 0; sp < ks; ++sp) accu += part[((size_t)sp * S + m) * nrows + ru];
-      accu -= corr + (brow[ru] << 31);
+      accu -= rc.corr + (brow[ru] << rc.e);
       y = mul_sat(gelu_act(y), requantize((int64_t)accu));
     } else if (MODE == 1) {
       y = mul_sat(gelu_act(y), vec[(size_t)m * ldv + n]);
@@ -1057,14 +1098,18 @@ bool tc_prepare_weight_group(TcWeight* views, const DevMat* mats, int n, TcWeigh
   return ok && encode_planes(whole.map, base, 2, total, K, kTcN) && encode_planes(whole.map_m, base, 2, total, K, kTsM);
 }
 
-size_t tc_act_bytes(int S, int K) { return 4 * (size_t)S * K + (size_t)S * 8; }
+size_t tc_act_bytes(int S, int K) {
+  return 4 * (size_t)S * K + (size_t)S * 8 + ((size_t)(S + kT2Mrows - 1) / kT2Mrows) * 4;
+}
 
 bool tc_prepare_act(TcAct& a, const int32_t* X, int S, int K, void* mem, cudaStream_t s) {
   a.S = S;
   a.K = K;
   a.planes = static_cast<uint8_t*>(mem);
   a.rowsum = reinterpret_cast<uint64_t*>(a.planes + 4 * (size_t)S * K);
-  tc_launch(tc_act_prep_kernel, dim3(S), dim3(256), 0, s, X, S, K, a.planes, a.rowsum);
+  a.tile4 = reinterpret_cast<uint32_t*>(a.rowsum + S);
+  if (cudaMemsetAsync(a.tile4, 0, ((size_t)(S + kT2Mrows - 1) / kT2Mrows) * 4, s) != cudaSuccess) return false;
+  tc_launch(tc_act_prep_kernel, dim3(S), dim3(256), 0, s, X, S, K, a.planes, a.rowsum, a.tile4);
   return encode_planes(a.map, a.planes, 4, S, K, kTcM) && encode_planes(a.map_t, a.planes, 4, S, K, kTsT);
 }
 
@@ -1141,6 +1186,7 @@ bool tc_attach_act(TcAct& a, int S, int K, void* mem) {
   a.K = K;
   a.planes = static_cast<uint8_t*>(mem);
   a.rowsum = reinterpret_cast<uint64_t*>(a.planes + 4 * (size_t)S * K);
+  a.tile4 = nullptr;  // planes written elsewhere use 2^31 on every row
   return encode_planes(a.map, a.planes, 4, S, K, kTcM) && encode_planes(a.map_t, a.planes, 4, S, K, kTsT);
 }
 
@@ -1173,13 +1219,13 @@ bool launch_tc_linear(const TcAct& a, const TcWeight& w, const TcOut& o, cudaStr
     const int m_fast = (size_t)4 * a.S * a.K < (size_t)2 * w.nrows * a.K ? 1 : 0;
     if (w.pair)
       tc_launch_pair(tc_linear2_kernel<2>, dim3(grid), dim3(kTcThreads), kT2Smem, s, am, bm, a.rowsum, w.rowsum, a.S,
-                     w.N, a.K, tm, ntiles_n, m_fast, o.y, o.vec, ldv);
+                     w.N, a.K, tm, ntiles_n, m_fast, o.y, o.vec, ldv, (const uint32_t*)a.tile4);
     else if (o.epi == kEpiGeluMul)
       tc_launch_pair(tc_linear2_kernel<1>, dim3(grid), dim3(kTcThreads), kT2Smem, s, am, bm, a.rowsum, w.rowsum, a.S,
-                     w.N, a.K, tm, ntiles_n, m_fast, o.y, o.vec, ldv);
+                     w.N, a.K, tm, ntiles_n, m_fast, o.y, o.vec, ldv, (const uint32_t*)a.tile4);
     else
       tc_launch_pair(tc_linear2_kernel<0>, dim3(grid), dim3(kTcThreads), kT2Smem, s, am, bm, a.rowsum, w.rowsum, a.S,
-                     w.N, a.K, tm, ntiles_n, m_fast, o.y, o.vec, ldv);
+                     w.N, a.K, tm, ntiles_n, m_fast, o.y, o.vec, ldv, (const uint32_t*)a.tile4);
     return true;
   }
   if (!split) {

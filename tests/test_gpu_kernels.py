@@ -181,3 +181,22 @@ def test_attention_decode_scores_all_int32_min(heads, kv_heads, d, cap, position
                               out.data_ptr())
     torch.cuda.synchronize()
     assert np.array_equal(out.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("S,rows,cols,edge_row", [(300, 2560, 2560, None), (1000, 960, 4096, None),
+                                                  (600, 2048, 2560, 437), (257, 96, 10240, 256)])
+def test_linear_activations_within_24_bits_bit_exact(S, rows, cols, edge_row):
+    # rows whose values all lie in [-2^23, 2^23) are offset by 2^23 and the CTA
+    # pair skips activation limb 3 on tiles made only of such rows; one row at
+    # the boundary (2^23 itself) forces the fourth limb on its 256-row tile
+    rng = np.random.default_rng(S + rows + cols)
+    w = rand_w(rng, rows, cols, 16, True)
+    X = rng.integers(-(1 << 23), 1 << 23, (S, cols), dtype=np.int64).astype(np.int32)
+    X[0, :4] = [-(1 << 23), (1 << 23) - 1, 0, -1]
+    if edge_row is not None:
+        X[edge_row, 5] = 1 << 23
+    Y = torch.zeros((S, rows), dtype=torch.int32, device="cuda")
+    Xd, wd = dev(X), dev(w)
+    rdet.det_linear(Xd.data_ptr(), S, wd.data_ptr(), 16, rows, cols, Y.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(Y.cpu().numpy(), O.linear(X, w))
