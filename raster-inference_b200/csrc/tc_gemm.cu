@@ -3,9 +3,11 @@
 // Y[s, n] = requantize(sum_k X[s, k] * W[n, k])   (wrapping i64 sum; the
 // arithmetic of linear_into / matmul_det in the reference's det path)
 //
-// Exact integer decomposition.  With X_u = X + 2^31 (u32) and W_u = W + 2^15
-// (u16), both non-negative,
-//   sum_k X W = sum_k X_u W_u - 2^15 sum_k X_u - 2^31 sum_k W_u + 2^46 K
+// Exact integer decomposition.  With X_u = X + 2^e (u32; e = 31, or e = 23
+// for an activation row whose values all lie in [-2^23, 2^23), so that its
+// X_u < 2^24 and byte limb 3 is zero) and W_u = W + 2^15 (u16), both
+// non-negative,
+//   sum_k X W = sum_k X_u W_u - 2^15 sum_k X_u - 2^e sum_k W_u + 2^(15+e) K
 // holds exactly in wrapping i64.  X_u splits into four byte limbs x_a and W_u
 // into two byte limbs w_b (all u8), and
 //   sum_k X_u W_u = sum_{a,b} 2^(8(a+b)) P_ab,   P_ab = sum_k x_a w_b.
@@ -436,7 +438,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // epilogues release TMEM on the leader's barrier.  Block 4 (shift 32) is
 // zeroed by the epilogue before each tile (a plane cannot be addressed alone
 // when B is split by plane across the pair), so a tile's first K step runs
-// limbs 0 and 2 with accumulate off and limbs 1 and 3 onto them.
+// limbs 0 and 2 with accumulate off and limbs 1 and 3 onto them.  A tile whose
+// 256 rows all have e = 23 loads and multiplies activation limbs 0-2 only (6
+// limb products instead of 8; block 4 stays zero).
 // Tiles go round the pairs in the order that keeps the smaller operand in L2
 // (m_fast: all token tiles of a weight tile before the next weight tile).
 // ---------------------------------------------------------------------------
