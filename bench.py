@@ -409,6 +409,28 @@ def run_kernel_case(args):
         model.close()
         print(f"prefill: {args.ctx} tokens")
         return
+    if args.kernel_case == "batch":
+        # one greedy step of the 64-sequence ragged batch
+        # inside the NVTX range "batch", after two untimed steps, for a launch
+        # list filtered with --nvtx-include "batch/"
+        model = rdet.Model.synthetic(cfg, SEED, width=16, device=0, max_prefill=args.ctx)
+        lens = [128 + (x % 3969) for x in lcg_ids(args.batch, 1 << 30, SEED + 7)]
+        seqs = [model.new_sequence(n + 16) for n in lens]
+        for i, (sq, n) in enumerate(zip(seqs, lens)):
+            sq.prefill(lcg_ids(n, t["vocab_size"], SEED + 100 + i))
+        toks = [sq.select() for sq in seqs]
+        for rep in range(3):
+            torch.cuda.synchronize()
+            if rep == 2:
+                torch.cuda.nvtx.range_push("batch")
+            rdet.decode_batch(model, seqs, toks)
+            torch.cuda.synchronize()
+            if rep == 2:
+                torch.cuda.nvtx.range_pop()
+            toks = [sq.select() for sq in seqs]
+        model.close()
+        print(f"batched decode step: {args.batch} sequences")
+        return
     if args.kernel_case == "convert":
         # model ingestion: a vocab x hidden bf16 tensor (lm_head-sized) to Q16.16
         # on the GPU (device time, CUDA events) and through convert.py's GPU
@@ -868,7 +890,7 @@ def main():
     ap.add_argument("--config4-tokens", type=int, default=256, help="greedy tokens of the config-4 line (0: skip)")
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched ragged decode line (0: skip)")
     ap.add_argument("--batch-steps", type=int, default=128, help="greedy steps of the batched line (config 5: 128)")
-    ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc", "tcattn", "prefill", "convert"],
+    ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc", "tcattn", "prefill", "convert", "batch"],
                     help="run a few launches of one kernel at E4B shapes for an ncu capture, then exit")
     ap.add_argument("--time-calls", type=int, default=0,
                     help="with --kernel-case attn: time this many back-to-back calls of each decode-attention entry "
