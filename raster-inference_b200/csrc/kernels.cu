@@ -1049,22 +1049,16 @@ __global__ void row_norm_kernel(const RowNormArgs a, int S) {
   const int32_t sc = block_norm_scale_partial(s, n, a.eps, red);
   const int4* g1 = reinterpret_cast<const int4*>(a.g1);
   auto nrm = [](int32_t x, int32_t k, int32_t g) { return mul_sat(mul_sat(x, k), g); };
-  // y row out: values, and the byte planes + row sum of y + 2^31
-  uint64_t usum = 0;
-  const size_t plane = (size_t)S * n;
-  auto emit = [&](int q, int4 y) {
+  auto out_of24 = [](int4 y) {
+    return y.x < -(1 << 23) || y.x >= (1 << 23) || y.y < -(1 << 23) || y.y >= (1 << 23) || y.z < -(1 << 23) ||
+           y.z >= (1 << 23) || y.w < -(1 << 23) || y.w >= (1 << 23);
+  };
+  // the output row y is left in xs (and y_out); wide: some value needs 32 bits
+  int wide = 0;
+  auto keep = [&](int q, int4 y) {
+    xs[q] = y;
     if (a.y_out) reinterpret_cast<int4*>(a.y_out + (size_t)r * n)[q] = y;
-    if (a.planes) {
-      const uint32_t u[4] = {(uint32_t)y.x + 0x80000000u, (uint32_t)y.y + 0x80000000u, (uint32_t)y.z + 0x80000000u,
-                             (uint32_t)y.w + 0x80000000u};
-      usum += (uint64_t)u[0] + u[1] + u[2] + u[3];
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const uint32_t packed = ((u[0] >> (8 * b)) & 0xffu) | (((u[1] >> (8 * b)) & 0xffu) << 8) |
-                                (((u[2] >> (8 * b)) & 0xffu) << 16) | (((u[3] >> (8 * b)) & 0xffu) << 24);
-        *reinterpret_cast<uint32_t*>(a.planes + b * plane + (size_t)r * n + 4 * q) = packed;
-      }
-    }
+    wide |= out_of24(y);
   };
   if (a.res) {
     const int4* rr = reinterpret_cast<const int4*>(a.res + (size_t)r * n);
@@ -1082,35 +1076,52 @@ __global__ void row_norm_kernel(const RowNormArgs a, int S) {
       s2 = sat_add_u(s2, (uint64_t)mul_wide(t.y, t.y));
       s2 = sat_add_u(s2, (uint64_t)mul_wide(t.z, t.z));
       s2 = sat_add_u(s2, (uint64_t)mul_wide(t.w, t.w));
+      if (!a.g2) wide |= out_of24(t);
     }
     if (a.g2) {
       const int32_t sc2 = block_norm_scale_partial(s2, n, a.eps, red);
       const int4* g2 = reinterpret_cast<const int4*>(a.g2);
       for (int q = threadIdx.x; q < nq; q += blockDim.x) {
         const int4 t = xs[q], g = g2[q];
-        emit(q, make_int4(nrm(t.x, sc2, g.x), nrm(t.y, sc2, g.y), nrm(t.z, sc2, g.z), nrm(t.w, sc2, g.w)));
+        keep(q, make_int4(nrm(t.x, sc2, g.x), nrm(t.y, sc2, g.y), nrm(t.z, sc2, g.z), nrm(t.w, sc2, g.w)));
       }
-    } else if (a.planes) {
-      for (int q = threadIdx.x; q < nq; q += blockDim.x) emit(q, xs[q]);
     }
   } else {
     for (int q = threadIdx.x; q < nq; q += blockDim.x) {
       const int4 x = xs[q], g = g1[q];
-      emit(q, make_int4(nrm(x.x, sc, g.x), nrm(x.y, sc, g.y), nrm(x.z, sc, g.z), nrm(x.w, sc, g.w)));
+      keep(q, make_int4(nrm(x.x, sc, g.x), nrm(x.y, sc, g.y), nrm(x.z, sc, g.z), nrm(x.w, sc, g.w)));
     }
   }
-  if (a.planes) {
+  if (!a.planes) return;
+  // byte planes and row sum of y + 2^e: e = 23 when the whole row fits 24
+  // bits (the row sum then carries the top-bit flag), else 31 (and the row's
+  // 256-row tile is marked as needing the fourth limb)
+  const bool four = __syncthreads_or(wide) != 0;
+  const uint32_t off = four ? 0x80000000u : 0x00800000u;
+  const size_t plane = (size_t)S * n;
+  uint64_t usum = 0;
+  for (int q = threadIdx.x; q < nq; q += blockDim.x) {
+    const int4 y = xs[q];
+    const uint32_t u[4] = {(uint32_t)y.x + off, (uint32_t)y.y + off, (uint32_t)y.z + off, (uint32_t)y.w + off};
+    usum += (uint64_t)u[0] + u[1] + u[2] + u[3];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) usum += __shfl_xor_sync(0xffffffffu, usum, o);
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    __syncthreads();
-    if (l == 0) red[w] = usum;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      uint64_t t = 0;
-      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
-      a.rowsum[r] = t;
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t packed = ((u[0] >> (8 * b)) & 0xffu) | (((u[1] >> (8 * b)) & 0xffu) << 8) |
+                              (((u[2] >> (8 * b)) & 0xffu) << 16) | (((u[3] >> (8 * b)) & 0xffu) << 24);
+      *reinterpret_cast<uint32_t*>(a.planes + b * plane + (size_t)r * n + 4 * q) = packed;
     }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) usum += __shfl_xor_sync(0xffffffffu, usum, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = usum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t t = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+    a.rowsum[r] = four ? t : (t | (1ull << 63));
+    if (four && a.tile4) atomicOr(&a.tile4[r / 256], 1u);
   }
 }
 void launch_row_norm(const RowNormArgs& a, int32_t rows, cudaStream_t s) {

@@ -106,8 +106,17 @@ size_t tc_weight_group_bytes(const DevMat* mats, int n);
 bool tc_prepare_weight_group(TcWeight* views, const DevMat* mats, int n, TcWeight& whole, void* mem, cudaStream_t s);
 bool tc_prepare_act(TcAct& a, const int32_t* X, int S, int K, void* mem, cudaStream_t s);
 // Attaches planes already written at `mem` (layout of tc_prepare_act: [4][S][K]
-// bytes of X + 2^31, then S u64 row sums) and encodes their tensor maps.
-bool tc_attach_act(TcAct& a, int S, int K, void* mem);
+// bytes of X + 2^e, then S u64 row sums, then the tile flags) and encodes
+// their tensor maps.  with_tile4: the producer zeroed and set the tile flags
+// (tc_act_tile4(mem, S, K)); else every tile multiplies all four limbs.
+bool tc_attach_act(TcAct& a, int S, int K, void* mem, bool with_tile4 = false);
+// The tile flags of the activation layout at `mem`: one u32 per
+// kTcFlagRows rows, nonzero when a row of that tile has offset 2^31.
+uint32_t* tc_act_tile4(void* mem, int S, int K);
+constexpr int kTcFlagRows = 256;
+// Up to this many rows the linear takes its short-row kernel, which
+// multiplies all four limbs and reads no tile flags.
+constexpr int kTcShortRows = 64;
 // Output of the tensor-core linear.  y: Y [S, N] = epilogue(requantize(X W^T))
 // (a pair writes mul_sat(gelu(gate), up); kEpiGeluMul multiplies by
 // vec[s * ldv + n]).  y64 instead: the exact wrapping i64 sums before
@@ -135,13 +144,13 @@ void launch_rmsnorm_rows(const int32_t* x, int32_t S, int32_t n, const int32_t* 
 void launch_norm_residual_rows(const int32_t* a, const int32_t* res, int32_t S, int32_t n, const int32_t* g,
                                int64_t eps, bool has_scalar, int32_t scalar, int32_t* out, cudaStream_t s);
 // Fused per-row norms (one block per row, n % 4 == 0), covering the row
-// kernels between batched-decode GEMMs:
+// kernels between the GEMMs of a batched decode step and of a prefill layer:
 //   with res: t = res + norm(a) * g1 (then * scalar), stored to t_out (and
 //             copied to scatter[r] + scatter_off when scatter is set);
-//   without:  t = a;
-//   with g2:  y = norm(t) * g2 stored to y_out (without res: y = norm(a) * g1);
-//   planes:   y's tensor-core activation planes ([4][S][n] bytes of y + 2^31)
-//             and row sums, the layout of tc_prepare_act.
+//   with g2:  y = norm(t) * g2 stored to y_out;
+//   without res: y = norm(a) * g1 stored to y_out;
+//   planes:   the tensor-core activation planes and row sums (the layout of
+//             tc_prepare_act) of y, or of t when res is set without g2.
 struct RowNormArgs {
   const int32_t* a = nullptr;
   const int32_t* res = nullptr;
@@ -155,8 +164,13 @@ struct RowNormArgs {
   int32_t* y_out = nullptr;
   int32_t* const* scatter = nullptr;
   size_t scatter_off = 0;
+  // tensor-core operand of the output row y: byte planes of y + 2^e (e = 23
+  // when the row fits 24 bits, flagged in the row sum's top bit, else 31;
+  // the tensor-core linear's activation layout) and tile4[row / 256] set for
+  // a row with e = 31 (tile4 zeroed by the caller; may be null)
   uint8_t* planes = nullptr;
   uint64_t* rowsum = nullptr;
+  uint32_t* tile4 = nullptr;
 };
 void launch_row_norm(const RowNormArgs& a, int32_t rows, cudaStream_t s);
 

@@ -917,10 +917,15 @@ struct ActPlanes {
   bool ready = false;   // a holds the planes of the normalized rows
   bool normed = false;  // the normalized rows are already in the workspace (w.nrm)
 };
+// True when a prefill linear of weight planes `t` over S rows of `cols`
+// columns runs on the tensor cores.
+static bool prefill_tc(const Ctx& c, const TcWeight& t, int S, int cols) {
+  return c.tc && t.planes && S >= kTcMinRows && cols <= c.tc_act_k;
+}
 static void prefill_linear(Ctx& c, const int32_t* X, int S, const DevMat& w, const TcWeight& t, int32_t* Y,
                            int32_t epi, const int32_t* vec, ActPlanes* shared = nullptr) {
   cudaStream_t s = c.stream;
-  if (c.tc && t.planes && S >= kTcMinRows && w.cols <= c.tc_act_k) {
+  if (prefill_tc(c, t, S, w.cols)) {
     ActPlanes local;
     ActPlanes& ap = shared ? *shared : local;
     if (!ap.ready) {
@@ -942,7 +947,7 @@ static void prefill_linear(Ctx& c, const int32_t* X, int S, const DevMat& w, con
 static void prefill_geglu(Ctx& c, const int32_t* X, int S, const LayerDev& L, int32_t* Y,
                           ActPlanes* shared = nullptr) {
   cudaStream_t s = c.stream;
-  if (c.tc && L.tgu.planes && S >= kTcMinRows && L.gate.cols <= c.tc_act_k) {
+  if (prefill_tc(c, L.tgu, S, L.gate.cols)) {
     ActPlanes local;
     ActPlanes& ap = shared ? *shared : local;
     if (!ap.ready) {
@@ -970,13 +975,19 @@ static bool row_norm(Ctx& c, RowNormArgs ra, int B, ActPlanes* ap) {
     return false;
   if (ra.scatter && (ra.scatter_off * 4) % 16 != 0) return false;
   const bool planes = ap && c.tc && B >= kTcMinRows && ra.n <= c.tc_act_k;
+  // tile flags only where the linear reads them (past the short-row kernel)
+  const bool flags = planes && B > kTcShortRows;
   if (planes) {
     ra.planes = static_cast<uint8_t*>(c.tc_act);
     ra.rowsum = reinterpret_cast<uint64_t*>(ra.planes + 4 * (size_t)B * ra.n);
   }
+  if (flags) {
+    ra.tile4 = tc_act_tile4(c.tc_act, B, ra.n);
+    CK(cudaMemsetAsync(ra.tile4, 0, (size_t)(B + kTcFlagRows - 1) / kTcFlagRows * 4, c.stream));
+  }
   launch_row_norm(ra, B, c.stream);
   if (planes) {
-    REQUIRE(tc_attach_act(ap->a, B, ra.n, c.tc_act), RDET_E_CUDA, "tensor map encoding failed");
+    REQUIRE(tc_attach_act(ap->a, B, ra.n, c.tc_act, flags), RDET_E_CUDA, "tensor map encoding failed");
     ap->ready = true;
   }
   return true;
@@ -1160,8 +1171,19 @@ static void prefill_layer(Ctx& c, Seq& q, int l) {
   const int S = q.prefill_S, H = m.H, d = lc.head_dim;
   int32_t* cur = q.prefill_cur;
   int32_t* other = cur == w.xa ? w.xb : w.xa;
-  launch_rmsnorm_rows(cur, S, H, L.in_ln, c.eps, w.nrm, s);
+  // The row norms run as row_norm_kernel, which also writes the byte planes
+  // of the next linear's input (the plain norm kernels when a row pointer is
+  // not 16-byte aligned).  A normed row goes to w.nrm only when a linear
+  // reading it runs on the CUDA cores.
   ActPlanes nrm_planes;  // q, k and v read the same normed input
+  {
+    const bool own_kv = lc.donor < 0;
+    const bool all_tc = prefill_tc(c, L.tq, S, H) && (!own_kv || prefill_tc(c, L.tk, S, H)) &&
+                        (!own_kv || !L.v.p || prefill_tc(c, L.tv, S, H));
+    RowNormArgs ra;
+    ra.a = cur; ra.g1 = L.in_ln; ra.n = H; ra.eps = c.eps; ra.y_out = all_tc ? nullptr : w.nrm;
+    if (!row_norm(c, ra, S, &nrm_planes)) launch_rmsnorm_rows(cur, S, H, L.in_ln, c.eps, w.nrm, s);
+  }
   prefill_linear(c, w.nrm, S, L.q, L.tq, w.q, kEpiPlain, nullptr, &nrm_planes);
   QkvPostArgs qa;
   qa.S = S; qa.pos = q.d_pos; qa.Hq = m.Hq; qa.Hkv = lc.kv_heads; qa.d = d; qa.rotary = lc.rotary;
@@ -1192,16 +1214,31 @@ static void prefill_layer(Ctx& c, Seq& q, int l) {
   if (!(c.ta_ws && launch_attn_prefill_tc(aa, c.ta_ws, c.ta_ws_bytes, s))) launch_attn_prefill(aa, s);
   prefill_linear(c, w.comb, S, L.o, L.to, w.attn, kEpiPlain, nullptr);
   bool ple = m.P > 0;
-  // t1 = xs + norm(attn)  -> other
-  launch_norm_residual_rows(w.attn, cur, S, H, L.post_attn_ln, c.eps, false, 0, other, s);
-  launch_rmsnorm_rows(other, S, H, L.pre_ff_ln, c.eps, w.nrm, s);
-  prefill_geglu(c, w.nrm, S, L, w.hbuf);
+  // t1 = xs + norm(attn) -> other, and the MLP input norm(t1) with its planes
+  ActPlanes ff_planes;
+  {
+    RowNormArgs ra;
+    ra.a = w.attn; ra.res = cur; ra.g1 = L.post_attn_ln; ra.g2 = L.pre_ff_ln; ra.n = H; ra.eps = c.eps;
+    ra.t_out = other; ra.y_out = prefill_tc(c, L.tgu, S, H) ? nullptr : w.nrm;
+    if (!row_norm(c, ra, S, &ff_planes)) {
+      launch_norm_residual_rows(w.attn, cur, S, H, L.post_attn_ln, c.eps, false, 0, other, s);
+      launch_rmsnorm_rows(other, S, H, L.pre_ff_ln, c.eps, w.nrm, s);
+    }
+  }
+  prefill_geglu(c, w.nrm, S, L, w.hbuf, &ff_planes);
   prefill_linear(c, w.hbuf, S, L.down, L.tdown, w.attn, kEpiPlain, nullptr);
-  // t2 = t1 + norm(ff) -> cur
-  launch_norm_residual_rows(w.attn, other, S, H, L.post_ff_ln, c.eps, !ple && L.has_scalar, L.scalar, cur, s);
+  // t2 = t1 + norm(ff) -> cur, with the planes of t2 for the per-layer-input gate
+  ActPlanes t2_planes;
+  {
+    RowNormArgs ra;
+    ra.a = w.attn; ra.res = other; ra.g1 = L.post_ff_ln; ra.n = H; ra.eps = c.eps;
+    ra.has_scalar = !ple && L.has_scalar; ra.scalar = L.scalar; ra.t_out = cur;
+    if (!row_norm(c, ra, S, ple ? &t2_planes : nullptr))
+      launch_norm_residual_rows(w.attn, other, S, H, L.post_ff_ln, c.eps, !ple && L.has_scalar, L.scalar, cur, s);
+  }
   int32_t* result = cur;
   if (ple) {
-    prefill_linear(c, cur, S, L.ple_gate, L.tpg, w.g, kEpiGeluMul, w.ple_all + (size_t)l * S * m.P);
+    prefill_linear(c, cur, S, L.ple_gate, L.tpg, w.g, kEpiGeluMul, w.ple_all + (size_t)l * S * m.P, &t2_planes);
     prefill_linear(c, w.g, S, L.ple_proj, L.tpp, w.pr, kEpiPlain, nullptr);
     launch_norm_residual_rows(w.pr, cur, S, H, L.ple_norm, c.eps, L.has_scalar, L.scalar, other, s);
     result = other;

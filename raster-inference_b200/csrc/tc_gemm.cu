@@ -445,6 +445,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // (m_fast: all token tiles of a weight tile before the next weight tile).
 // ---------------------------------------------------------------------------
 constexpr int kT2M = kT2Mrows;                     // tokens per pair tile
+static_assert(kT2M == kTcFlagRows, "one tile flag per pair tile");
 static_assert(kT2M == 2 * kTcM, "a pair tile is two one-CTA tiles");
 constexpr int kT2Stages = 4;
 constexpr int kT2BTile = kTcN * kTcKB;             // 6 KB: one weight plane
@@ -732,6 +733,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // ---------------------------------------------------------------------------
 constexpr int kTsM = 128;                              // weight plane rows per tile
 constexpr int kTsT = 64;                               // tokens per tile
+static_assert(kTsT == kTcShortRows, "the short-row kernel covers up to kTcShortRows rows");
 constexpr int kTsATile = kTsM * kTcKB;                 // 8 KB per weight plane
 constexpr int kTsBTile = kTsT * kTcKB;                 // 4 KB per activation limb
 constexpr int kTsStage = 2 * kTsATile + 4 * kTsBTile;  // 32 KB
@@ -1185,12 +1187,16 @@ bool launch_tc_linear_t(const TcAct& a, const TcWeight& w, const TcOut& o, int l
 
 }  // namespace
 
-bool tc_attach_act(TcAct& a, int S, int K, void* mem) {
+uint32_t* tc_act_tile4(void* mem, int S, int K) {
+  return reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(mem) + 4 * (size_t)S * K + 8 * (size_t)S);
+}
+
+bool tc_attach_act(TcAct& a, int S, int K, void* mem, bool with_tile4) {
   a.S = S;
   a.K = K;
   a.planes = static_cast<uint8_t*>(mem);
   a.rowsum = reinterpret_cast<uint64_t*>(a.planes + 4 * (size_t)S * K);
-  a.tile4 = nullptr;  // planes written elsewhere use 2^31 on every row
+  a.tile4 = with_tile4 ? tc_act_tile4(mem, S, K) : nullptr;
   return encode_planes(a.map, a.planes, 4, S, K, kTcM) && encode_planes(a.map_t, a.planes, 4, S, K, kTsT);
 }
 
