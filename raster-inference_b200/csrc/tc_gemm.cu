@@ -93,6 +93,12 @@ __device__ __forceinline__ RowCorr row_corr(uint64_t rw, int K) {
 
 using namespace tcx;
 
+// sum over g of blk[g] * 2^(8g): the overlapping TMEM column blocks of one
+// output (each block a u32 accumulator)
+__device__ __forceinline__ uint64_t limb_sum(uint32_t g0, uint32_t g1, uint32_t g2, uint32_t g3, uint32_t g4) {
+  return (uint64_t)g0 + ((uint64_t)g1 << 8) + ((uint64_t)g2 << 16) + ((uint64_t)g3 << 24) + ((uint64_t)g4 << 32);
+}
+
 // kind::i8 instruction descriptors of this file's MMAs (M = 128)
 constexpr uint32_t kTcIdesc = idesc_u8(kTcNB);    // both byte planes
 constexpr uint32_t kTcIdescHalf = idesc_u8(kTcN); // one byte plane
@@ -344,8 +350,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int i = 0; i < 8; ++i) {
               const int j = c0 + i;
               if (r0 + j < nrows)
-                dst[j] = (uint64_t)g[0][i] + ((uint64_t)g[1][i] << 8) + ((uint64_t)g[2][i] << 16) +
-                         ((uint64_t)g[3][i] << 24) + ((uint64_t)g[4][i] << 32);
+                dst[j] = limb_sum(g[0][i], g[1][i], g[2][i], g[3][i], g[4][i]);
             }
           }
         }
@@ -374,9 +379,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           int32_t y = 0;
           // plane rows of a pair cover whole tiles; a plain matrix has N rows
           if (mrow && n < N) {
-            uint64_t acc = (uint64_t)g[0][i >> 3][i & 7] + ((uint64_t)g[1][i >> 3][i & 7] << 8) +
-                           ((uint64_t)g[2][i >> 3][i & 7] << 16) + ((uint64_t)g[3][i >> 3][i & 7] << 24) +
-                           ((uint64_t)g[4][i >> 3][i & 7] << 32);
+            uint64_t acc = limb_sum(g[0][i >> 3][i & 7], g[1][i >> 3][i & 7], g[2][i >> 3][i & 7],
+                                    g[3][i >> 3][i & 7], g[4][i >> 3][i & 7]);
             acc -= rc.corr + (brow[r0 + pr] << rc.e);
             y = requantize((int64_t)acc);
           }
@@ -447,9 +451,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 constexpr int kT2M = kT2Mrows;                     // tokens per pair tile
 static_assert(kT2M == kTcFlagRows, "one tile flag per pair tile");
 static_assert(kT2M == 2 * kTcM, "a pair tile is two one-CTA tiles");
+// The TMA ring: four 38 KB stages (four activation limbs and a weight plane),
+// or five 30 KB stages when no tile of the launch needs the fourth limb.  The
+// loads' latency, not L2 bandwidth, bounds the main loop, so the bytes in
+// flight set its speed.
 constexpr int kT2Stages = 4;
+constexpr int kT2Stages3 = 5;
 constexpr int kT2BTile = kTcN * kTcKB;             // 6 KB: one weight plane
 constexpr int kT2Stage = 4 * kTcATile + kT2BTile;  // 38 KB
+constexpr int kT2Stage3 = 3 * kTcATile + kT2BTile; // 30 KB
+static_assert(kT2Stages3 * kT2Stage3 <= kT2Stages * kT2Stage, "both rings fit the same shared memory");
+static_assert(kT2Stage3 % 1024 == 0, "stages keep the swizzle alignment");
 constexpr int kT2Smem = kT2Stages * kT2Stage + kTcStageOut + 1024;
 // kind::i8 instruction descriptor with M = 256 (cta_group::2), N = 192
 constexpr uint32_t kT2Idesc = (2u << 4) | ((uint32_t)(kTcNB >> 3) << 17) | ((uint32_t)(kT2M >> 4) << 24);
@@ -516,9 +528,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                       int ntiles_m, int ntiles_n, int m_fast, int32_t* __restrict__ Y,
                       const int32_t* __restrict__ vec, int ldv, const uint32_t* __restrict__ tile4) {
   extern __shared__ __align__(16) unsigned char tc_smem_raw[];
-  __shared__ __align__(8) uint64_t full[kT2Stages], empty[kT2Stages], accf, tmem_empty;
+  __shared__ __align__(8) uint64_t full[kT2Stages3], empty[kT2Stages3], accf, tmem_empty;
   __shared__ uint32_t tmem_holder;
   __shared__ int fail;
+  // each epilogue warp's copy of the tile's weight row sums, shifted by 23
+  // (first half) and by 31 (second half): the row's e picks one
+  __shared__ uint64_t bsum[kTcEpiWarps][2 * kTcN];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
   int32_t* stage_out = reinterpret_cast<int32_t*>(smem + (size_t)kT2Stages * kT2Stage);
@@ -536,7 +551,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   };
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kT2Stages; ++i) {
+    for (int i = 0; i < kT2Stages3; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
@@ -558,13 +573,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem = tmem_holder;
   const uint32_t tmem_empty_leader = mapa_rank(su32(&tmem_empty), 0);
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // ring shape (every thread derives the same one from the tile flags)
+  bool any4 = tile4 == nullptr;
+  for (int i = 0; i < ntiles_m && !any4; ++i) any4 = tile4[i] != 0;
+  const int nst = any4 ? kT2Stages : kT2Stages3;
+  const int stage_bytes = any4 ? kT2Stage : kT2Stage3;
+  const int boff = (any4 ? 4 : 3) * kTcATile;  // the weight plane's offset in a stage
   if (warp == kTcEpiWarps) {
     // ---- producer (both CTAs): this CTA's A rows and weight plane, counted
     // on the leader's stage barrier
     if (lane == 0) {
       // m_fast: the activation tiles are re-read by every weight tile
       const uint64_t pol_a = l2_policy(m_fast != 0), pol_b = l2_policy(m_fast == 0);
-      int q = 0;
+      int q = 0, st = 0;
+      uint32_t ph = 0;  // parity of the ring round
       for (int it = 0; it < my_tiles; ++it) {
         int m0, nt;
         tile_of(it, m0, nt);
@@ -572,14 +594,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int limbs = (tile4 == nullptr || tile4[m0 / kT2M]) ? 4 : 3;
         const uint32_t tx = 2u * (uint32_t)(limbs * kTcATile + kT2BTile);
         for (int kb = 0; kb < nkb; ++kb, ++q) {
-          const int st = q % kT2Stages;
-          if (q >= kT2Stages && !mbar_wait(&empty[st], ((q / kT2Stages) - 1) & 1)) fail = 1;
-          unsigned char* sbuf = smem + (size_t)st * kT2Stage;
+          if (q >= nst && !mbar_wait(&empty[st], ph ^ 1u)) fail = 1;
+          unsigned char* sbuf = smem + (size_t)st * stage_bytes;
           if (rank == 0) mbar_expect_tx(&full[st], tx);
           const uint32_t bar = mapa_rank(su32(&full[st]), 0);
           for (int a = 0; a < limbs; ++a)
             tma_load_3d_pair(sbuf + a * kTcATile, &amap, kb * kTcKB, m0 + kTcM * (int)rank, a, bar, pol_a);
-          tma_load_3d_pair(sbuf + 4 * kTcATile, &bmap, kb * kTcKB, nt * kTcN, (int)rank, bar, pol_b);
+          tma_load_3d_pair(sbuf + boff, &bmap, kb * kTcKB, nt * kTcN, (int)rank, bar, pol_b);
+          if (++st == nst) { st = 0; ph ^= 1u; }
         }
       }
     }
@@ -587,7 +609,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---- MMA issue (leader only)
     if (rank == 0 && lane == 0) {
       const int qlast = my_tiles * nkb;
-      int q = 0;
+      int q = 0, st = 0;
+      uint32_t ph = 0;  // parity of the ring round
       for (int it = 0; it < my_tiles; ++it) {
         int m0, nt;
         tile_of(it, m0, nt);
@@ -595,11 +618,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (!mbar_wait(&tmem_empty, it & 1)) fail = 1;
         fence_after();
         for (int kb = 0; kb < nkb; ++kb, ++q) {
-          const int st = q % kT2Stages;
-          if (!mbar_wait(&full[st], (q / kT2Stages) & 1)) fail = 1;
+          if (!mbar_wait(&full[st], ph)) fail = 1;
           fence_after();
-          const unsigned char* sbuf = smem + (size_t)st * kT2Stage;
-          const uint32_t baddr = su32(sbuf + 4 * kTcATile);
+          const unsigned char* sbuf = smem + (size_t)st * stage_bytes;
+          const uint32_t baddr = su32(sbuf + boff);
 #pragma unroll
           for (int j = 0; j < kTcKB / 32; ++j) {
             const uint64_t bdesc = smem_desc_sw64(baddr + 32 * j);
@@ -617,7 +639,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               if (four) mma_i8_pair(tmem + 3 * kTcN, ad[3], bdesc, kT2Idesc, 1u);
             }
           }
-          if (q + kT2Stages < qlast) mma_commit_pair(&empty[st]);
+          if (q + nst < qlast) mma_commit_pair(&empty[st]);
+          if (++st == nst) { st = 0; ph ^= 1u; }
         }
         mma_commit_pair(&accf);
       }
@@ -649,6 +672,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int m = m0 + rl;
       const bool mrow = m < S;
       const RowCorr rc = row_corr(mrow ? arow[m] : 0, K);
+      // the tile's weight row sums, fetched before the accumulator is ready
+      uint64_t* bw = bsum[warp];
+      for (int j = lane; j < kTcN; j += 32) {
+        const int nn = EPI == 2 ? nbase + (j % (kTcN / 2)) : r0 + j;
+        const uint64_t b = nn < N ? brow[r0 + j] : 0;
+        bw[j] = b << 23;
+        bw[kTcN + j] = b << 31;
+      }
+      __syncwarp();
+      const uint64_t* bws = bw + (rc.e == 23 ? 0 : kTcN);
       if (!mbar_wait(&accf, it & 1)) fail = 1;
       fence_after();
       for (int c0 = half * kHalf; c0 < (half + 1) * kHalf; c0 += kStep) {
@@ -668,10 +701,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int n = nbase + c0 + (EPI == 2 ? (i & 7) : i);
           int32_t y = 0;
           if (mrow && n < N) {
-            uint64_t acc = (uint64_t)g[0][i >> 3][i & 7] + ((uint64_t)g[1][i >> 3][i & 7] << 8) +
-                           ((uint64_t)g[2][i >> 3][i & 7] << 16) + ((uint64_t)g[3][i >> 3][i & 7] << 24) +
-                           ((uint64_t)g[4][i >> 3][i & 7] << 32);
-            acc -= rc.corr + (brow[r0 + pr] << rc.e);
+            const uint64_t acc = limb_sum(g[0][i >> 3][i & 7], g[1][i >> 3][i & 7], g[2][i >> 3][i & 7],
+                                          g[3][i >> 3][i & 7], g[4][i >> 3][i & 7]) -
+                                 rc.corr - bws[pr];
             y = requantize((int64_t)acc);
           }
           stage_out[rl * kTcOutStride + pr] = y;
@@ -859,8 +891,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int i = 0; i < 8; ++i) {
           const int tok = t0 + c0 + i;
           if (rok && tok < S) {
-            const uint64_t raw = (uint64_t)g[0][i] + ((uint64_t)g[1][i] << 8) + ((uint64_t)g[2][i] << 16) +
-                                 ((uint64_t)g[3][i] << 24) + ((uint64_t)g[4][i] << 32);
+            const uint64_t raw = limb_sum(g[0][i], g[1][i], g[2][i], g[3][i], g[4][i]);
             if (EPI == 3) part[((size_t)sp * S + tok) * nrows + r] = raw;
             else {
               const RowCorr rc = row_corr(arow[tok], K);
