@@ -1037,9 +1037,16 @@ __global__ void row_norm_kernel(const RowNormArgs a, int S) {
   __shared__ uint64_t red[33];
   const int r = blockIdx.x, n = a.n, nq = n >> 2;
   const int4* ar = reinterpret_cast<const int4*>(a.a + (size_t)r * n);
+  const longlong2* ar64 = reinterpret_cast<const longlong2*>(a.a64 + (size_t)r * n);
   uint64_t s = 0;
   for (int q = threadIdx.x; q < nq; q += blockDim.x) {
-    const int4 v = ar[q];
+    int4 v;
+    if (a.a64) {
+      const longlong2 x0 = ar64[2 * q], x1 = ar64[2 * q + 1];
+      v = make_int4(requantize(x0.x), requantize(x0.y), requantize(x1.x), requantize(x1.y));
+    } else {
+      v = ar[q];
+    }
     xs[q] = v;
     s = sat_add_u(s, (uint64_t)mul_wide(v.x, v.x));
     s = sat_add_u(s, (uint64_t)mul_wide(v.y, v.y));
@@ -1228,8 +1235,10 @@ void launch_qkv_post(const QkvPostArgs& a, cudaStream_t s) {
 // decode attention: exact softmax in four grid-wide phases over splits of the
 // key window (attention_output_into, det_kernels.rs:340-367).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void decode_window(const AttnDecodeArgs& a, int* start, int* n) {
-  int len = (a.pos_rows ? *a.pos_rows[blockIdx.z] : (a.pos ? *a.pos : a.pos_value)) + 1;
+// The attended rows [start, start + n) of batch row `row` (its position's
+// window over its own cache).
+__device__ __forceinline__ void decode_window(const AttnDecodeArgs& a, int row, int* start, int* n) {
+  int len = (a.pos_rows ? *a.pos_rows[row] : (a.pos ? *a.pos : a.pos_value)) + 1;
   int st = (a.window > 0 && len > a.window) ? len - a.window : 0;
   *start = st;
   *n = len - st;
@@ -1245,7 +1254,7 @@ __global__ void attn_dec_scores(const AttnDecodeArgs a) {
   const int kvh = blockIdx.x, split = blockIdx.y, d = a.d;
   const int G = a.Hq / a.Hkv;
   int start, n;
-  decode_window(a, &start, &n);
+  decode_window(a, (int)blockIdx.z, &start, &n);
   const int lo = split * a.rows_per_split, hi = min(n, lo + a.rows_per_split);
   for (int i = threadIdx.x; i < G * d; i += blockDim.x) qs[i] = a.q[(size_t)kvh * G * d + i];
   __syncthreads();
@@ -1306,7 +1315,7 @@ __global__ void attn_dec_exp(const AttnDecodeArgs a) {
   const int kvh = blockIdx.x, split = blockIdx.y;
   const int G = a.Hq / a.Hkv;
   int start, n;
-  decode_window(a, &start, &n);
+  decode_window(a, (int)blockIdx.z, &start, &n);
   const int nsplit = (n + a.rows_per_split - 1) / a.rows_per_split;
   const int lo = split * a.rows_per_split, hi = min(n, lo + a.rows_per_split);
   if (threadIdx.x < G) {
@@ -1345,7 +1354,7 @@ __global__ void attn_dec_wsum(const AttnDecodeArgs a) {
   const int kvh = blockIdx.x, split = blockIdx.y, d = a.d;
   const int G = a.Hq / a.Hkv, R = a.rows_per_split;
   int start, n;
-  decode_window(a, &start, &n);
+  decode_window(a, (int)blockIdx.z, &start, &n);
   const int nsplit = (n + R - 1) / R;
   const int lo = split * R, hi = min(n, lo + R);
   if (threadIdx.x < G) {
@@ -1390,7 +1399,7 @@ __global__ void attn_dec_final(const AttnDecodeArgs a) {
   pdl_entry();
   const int h = blockIdx.x, d = a.d, G = a.Hq / a.Hkv, kvh = h / G;
   int start, n;
-  decode_window(a, &start, &n);
+  decode_window(a, (int)blockIdx.z, &start, &n);
   const int nsplit = (n + a.rows_per_split - 1) / a.rows_per_split;
   __shared__ int32_t s_res, s_mi;
   if (threadIdx.x == 0) {
@@ -1560,7 +1569,7 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
   __syncthreads();
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // batched decode: cluster row blockIdx.z is its own sequence
-  const int brow = blockIdx.z;
+  const int brow = a.row_order ? a.row_order[blockIdx.z] : (int)blockIdx.z;
   const bool batched = a.pos_rows != nullptr;
   const int32_t* const kc = batched ? a.kc_rows[brow] : a.k_cache;
   const int32_t* const vc = batched ? a.vc_rows[brow] : a.v_cache;
@@ -1569,7 +1578,7 @@ __global__ void __launch_bounds__(kAcThreads, 1) attn_dec_cluster_kernel(const A
   int32_t* const orow = a.out + (size_t)brow * a.Hq * d;
   const int pos = batched ? *a.pos_rows[brow] : (a.pos ? *a.pos : a.pos_value);
   int start, n;
-  decode_window(a, &start, &n);
+  decode_window(a, brow, &start, &n);
   const int lo = (int)((int64_t)n * rank / CL), hi = (int)((int64_t)n * (rank + 1) / CL);
   const int rows = hi - lo;
   const int TR = kAcTileBytes / (d * 4);  // rows per tile

@@ -153,6 +153,9 @@ void launch_norm_residual_rows(const int32_t* a, const int32_t* res, int32_t S, 
 //             tc_prepare_act) of y, or of t when res is set without g2.
 struct RowNormArgs {
   const int32_t* a = nullptr;
+  // instead of a: exact i64 sums (a tensor-parallel all-reduce's output),
+  // requantized as they are loaded
+  const int64_t* a64 = nullptr;
   const int32_t* res = nullptr;
   const int32_t* g1 = nullptr;
   const int32_t* g2 = nullptr;
@@ -260,6 +263,9 @@ struct AttnDecodeArgs {
   const int32_t* const* kc_rows = nullptr;
   const int32_t* const* vc_rows = nullptr;
   const int32_t* cap_rows = nullptr;
+  // batched: the rows in launch order (longest context first, so that the
+  // longest rows' clusters start in the first wave); null = row order
+  const int32_t* row_order = nullptr;
 };
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s);
 // Same computation in one kernel: one thread-block cluster per query head

@@ -539,6 +539,7 @@ struct Ctx {
     uint32_t* ids = nullptr;
     int32_t** pos = nullptr;       // [rows] each sequence's device position
     int32_t* caps = nullptr;       // [rows]
+    int32_t* order = nullptr;      // [rows] attention launch order, longest context first
     int32_t** kc = nullptr;        // [L][rows] (a KV-sharing layer lists its donor's cache)
     int32_t** vc = nullptr;
     int32_t** dec_out = nullptr;   // [rows] each sequence's per-layer outputs
@@ -971,7 +972,8 @@ static void prefill_geglu(Ctx& c, const int32_t* X, int S, const LayerDev& L, in
 // a row pointer or gain is not 16-byte aligned or n % 4 != 0.
 static bool row_norm(Ctx& c, RowNormArgs ra, int B, ActPlanes* ap) {
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  if (ra.n % 4 != 0 || !al(ra.a) || !al(ra.res) || !al(ra.g1) || !al(ra.g2) || !al(ra.t_out) || !al(ra.y_out))
+  if (ra.n % 4 != 0 || !al(ra.a) || !al(ra.a64) || !al(ra.res) || !al(ra.g1) || !al(ra.g2) || !al(ra.t_out) ||
+      !al(ra.y_out))
     return false;
   if (ra.scatter && (ra.scatter_off * 4) % 16 != 0) return false;
   const bool planes = ap && c.tc && B >= kTcMinRows && ra.n <= c.tc_act_k;
@@ -1702,7 +1704,7 @@ static void batch_tables(Ctx& c, Seq* const* seqs, int B) {
   if (bw.rows < B) {
     const int rows = std::max(B, 8);
     const size_t ptrs = (size_t)rows * (3 + 2 * (size_t)m.L);
-    const size_t bytes = ptrs * 8 + (size_t)rows * 8 + (size_t)rows * m.V * 4 + 256;
+    const size_t bytes = ptrs * 8 + (size_t)rows * 12 + (size_t)rows * m.V * 4 + 256;
     bw.mem = c.dalloc(bytes);
     auto* base = static_cast<unsigned char*>(bw.mem);
     bw.pos = reinterpret_cast<int32_t**>(base);
@@ -1712,12 +1714,13 @@ static void batch_tables(Ctx& c, Seq* const* seqs, int B) {
     bw.vc = bw.kc + (size_t)m.L * rows;
     bw.ids = reinterpret_cast<uint32_t*>(bw.vc + (size_t)m.L * rows);
     bw.caps = reinterpret_cast<int32_t*>(bw.ids + rows);
-    bw.logits = reinterpret_cast<int32_t*>((reinterpret_cast<uintptr_t>(bw.caps + rows) + 255) & ~(uintptr_t)255);
+    bw.order = bw.caps + rows;
+    bw.logits = reinterpret_cast<int32_t*>((reinterpret_cast<uintptr_t>(bw.order + rows) + 255) & ~(uintptr_t)255);
     bw.rows = rows;
   }
   const int rows = bw.rows;
   std::vector<int32_t*> host((size_t)rows * (3 + 2 * (size_t)m.L), nullptr);
-  std::vector<int32_t> caps(rows, 0);
+  std::vector<int32_t> caps(2 * (size_t)rows, 0);  // [caps | row order]
   for (int b = 0; b < B; ++b) {
     Seq& q = *seqs[b];
     host[b] = q.d_pos;
@@ -1730,8 +1733,12 @@ static void batch_tables(Ctx& c, Seq* const* seqs, int B) {
     }
     caps[b] = q.cap;
   }
+  // attention launch order: longest context first (ties by row)
+  int32_t* order = caps.data() + rows;
+  for (int b = 0; b < rows; ++b) order[b] = b;
+  std::stable_sort(order, order + B, [&](int32_t x, int32_t y) { return seqs[x]->pos > seqs[y]->pos; });
   CK(cudaMemcpyAsync(bw.pos, host.data(), host.size() * 8, cudaMemcpyHostToDevice, c.stream));
-  CK(cudaMemcpyAsync(bw.caps, caps.data(), (size_t)rows * 4, cudaMemcpyHostToDevice, c.stream));
+  CK(cudaMemcpyAsync(bw.caps, caps.data(), caps.size() * 4, cudaMemcpyHostToDevice, c.stream));
 }
 
 // in_planes: the layer input's norm already applied into w.nrm (and its
@@ -1795,6 +1802,7 @@ static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32
   aa.cap = maxcap; aa.batch = B; aa.pos_rows = bw.pos; aa.cap_rows = bw.caps;
   aa.kc_rows = bw.kc + (size_t)l * bw.rows;
   aa.vc_rows = bw.vc + (size_t)l * bw.rows;
+  aa.row_order = bw.order;
   launch_attn_decode_cluster(aa, s);
   prefill_linear(c, w.comb, B, L.o, L.to, w.attn, kEpiPlain, nullptr);
   const bool ple = m.P > 0;
@@ -1862,26 +1870,35 @@ static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32
 // run in full on every rank, so every rank's caches stay complete and every
 // other path of the context stays valid.
 // ---------------------------------------------------------------------------
-static void tp_linear(Ctx& c, const int32_t* X, int S, int K, const TcWeight& w, const TcOut& o) {
-  TcAct a;
-  REQUIRE(tc_prepare_act(a, X, S, K, c.tc_act, c.stream), RDET_E_CUDA, "tensor map encoding failed");
+static void tp_linear(Ctx& c, const int32_t* X, int S, int K, const TcWeight& w, const TcOut& o,
+                      ActPlanes* shared = nullptr) {
+  ActPlanes local;
+  ActPlanes& ap = shared ? *shared : local;
+  if (!ap.ready) {
+    REQUIRE(tc_prepare_act(ap.a, X, S, K, c.tc_act, c.stream), RDET_E_CUDA, "tensor map encoding failed");
+    ap.ready = true;
+  }
   TcOut oo = o;
   oo.scratch = c.tc_split;
   oo.scratch_bytes = c.tc_split_bytes;
-  REQUIRE(launch_tc_linear(a, w, oo, c.stream), RDET_E_RANGE, "batch too large for the split-K scratch");
+  REQUIRE(launch_tc_linear(ap.a, w, oo, c.stream), RDET_E_RANGE, "batch too large for the split-K scratch");
 }
 
-// partial sums [S, H] of a column slice -> all-reduce -> requantize into y
-static void tp_linear_reduce(Ctx& c, const int32_t* X, int S, int K, const TcWeight& w, int32_t* y) {
+// partial sums [S, N] of a column slice -> all-reduce, left in c.tp.part (the
+// next row kernel requantizes them as it loads them)
+static void tp_linear_sum(Ctx& c, const int32_t* X, int S, int K, const TcWeight& w) {
   TcOut o;
   o.y64 = c.tp.part;
   tp_linear(c, X, S, K, w, o);
-  const size_t n = (size_t)S * w.N;
-  NCK(nccl_api().allReduce(c.tp.part, c.tp.part, n, ncclInt64, ncclSum, c.tp.comm, c.stream));
-  launch_requantize_rows(c.tp.part, n, y, c.stream);
+  NCK(nccl_api().allReduce(c.tp.part, c.tp.part, (size_t)S * w.N, ncclInt64, ncclSum, c.tp.comm, c.stream));
 }
 
-static const int32_t* decode_batch_layer_tp(Ctx& c, int B, int maxcap, int l, int32_t* cur) {
+// in_planes / next_gain / next_planes as in decode_batch_layer.  The row
+// kernels after each all-reduce requantize the summed partials on load
+// (row_norm_kernel's i64 input), apply the norm and residual, and write the
+// next GEMM's activation planes.
+static const int32_t* decode_batch_layer_tp(Ctx& c, int B, int maxcap, int l, int32_t* cur, ActPlanes* in_planes,
+                                            const int32_t* next_gain, ActPlanes* next_planes) {
   const ModelCfg& m = c.cfg;
   const LayerDev& L = c.layers[l];
   const LayerCfg& lc = L.cfg;
@@ -1891,16 +1908,25 @@ static const int32_t* decode_batch_layer_tp(Ctx& c, int B, int maxcap, int l, in
   cudaStream_t s = c.stream;
   const int H = m.H, d = lc.head_dim, Hql = c.tp.Hql;
   int32_t* other = cur == w.xa ? w.xb : w.xa;
-  launch_rmsnorm_rows(cur, B, H, L.in_ln, c.eps, w.nrm, s);
+  // sums of a column-sliced GEMM -> i32 rows, for the unfused fallbacks
+  auto requantized = [&](int32_t* y) { launch_requantize_rows(c.tp.part, (size_t)B * H, y, s); return y; };
+  ActPlanes nrm_planes;
+  if (in_planes && in_planes->ready) {
+    nrm_planes = *in_planes;
+  } else if (!in_planes || !in_planes->normed) {
+    RowNormArgs ra;
+    ra.a = cur; ra.g1 = L.in_ln; ra.n = H; ra.eps = c.eps; ra.y_out = w.nrm;
+    if (!row_norm(c, ra, B, &nrm_planes)) launch_rmsnorm_rows(cur, B, H, L.in_ln, c.eps, w.nrm, s);
+  }
+  // this rank's query heads and the full K/V projections read the same planes
   TcOut oq;
   oq.y = w.q;
-  tp_linear(c, w.nrm, B, H, T.q, oq);
+  tp_linear(c, w.nrm, B, H, T.q, oq, &nrm_planes);
   QkvPostArgs qa;
   qa.S = B; qa.Hq = Hql; qa.Hkv = lc.kv_heads; qa.d = d; qa.rotary = lc.rotary; qa.inv_freq = L.inv_freq;
   qa.q_in = w.q; qa.q_norm = L.q_norm; qa.k_norm = L.k_norm; qa.eps = c.eps; qa.q_out = w.qo;
   qa.pos_rows = bw.pos; qa.cap_rows = bw.caps;
   if (lc.donor < 0) {
-    ActPlanes nrm_planes;
     prefill_linear(c, w.nrm, B, L.k, L.tk, w.kraw, kEpiPlain, nullptr, &nrm_planes);
     const int32_t* vsrc = w.kraw;  // k_eq_v: V is the raw K projection
     if (L.v.p) { prefill_linear(c, w.nrm, B, L.v, L.tv, w.vraw, kEpiPlain, nullptr, &nrm_planes); vsrc = w.vraw; }
@@ -1915,16 +1941,44 @@ static const int32_t* decode_batch_layer_tp(Ctx& c, int B, int maxcap, int l, in
   aa.cap = maxcap; aa.batch = B; aa.pos_rows = bw.pos; aa.cap_rows = bw.caps;
   aa.kc_rows = bw.kc + (size_t)l * bw.rows;
   aa.vc_rows = bw.vc + (size_t)l * bw.rows;
+  aa.row_order = bw.order;
   launch_attn_decode_cluster(aa, s);
-  tp_linear_reduce(c, w.comb, B, Hql * d, T.o, w.attn);
+  tp_linear_sum(c, w.comb, B, Hql * d, T.o);
   const bool ple = m.P > 0;
-  launch_norm_residual_rows(w.attn, cur, B, H, L.post_attn_ln, c.eps, false, 0, other, s);
-  launch_rmsnorm_rows(other, B, H, L.pre_ff_ln, c.eps, w.nrm, s);
+  // post-attention norm + residual, then the MLP input norm and its planes
+  ActPlanes ff_planes;
+  {
+    RowNormArgs ra;
+    ra.a64 = c.tp.part; ra.res = cur; ra.g1 = L.post_attn_ln; ra.g2 = L.pre_ff_ln; ra.n = H; ra.eps = c.eps;
+    ra.t_out = other; ra.y_out = w.nrm;
+    if (!row_norm(c, ra, B, &ff_planes)) {
+      launch_norm_residual_rows(requantized(w.attn), cur, B, H, L.post_attn_ln, c.eps, false, 0, other, s);
+      launch_rmsnorm_rows(other, B, H, L.pre_ff_ln, c.eps, w.nrm, s);
+    }
+  }
   TcOut og;
   og.y = w.hbuf;
-  tp_linear(c, w.nrm, B, H, T.gu, og);
-  tp_linear_reduce(c, w.hbuf, B, c.tp.Fl, T.down, w.attn);
-  launch_norm_residual_rows(w.attn, other, B, H, L.post_ff_ln, c.eps, !ple && L.has_scalar, L.scalar, cur, s);
+  tp_linear(c, w.nrm, B, H, T.gu, og, &ff_planes);
+  tp_linear_sum(c, w.hbuf, B, c.tp.Fl, T.down);
+  // post-MLP norm + residual: the layer output, or the per-layer-input GEMM's input
+  ActPlanes pg_planes;
+  bool scattered = false;
+  {
+    RowNormArgs ra;
+    ra.a64 = c.tp.part; ra.res = other; ra.g1 = L.post_ff_ln; ra.n = H; ra.eps = c.eps;
+    ra.has_scalar = !ple && L.has_scalar; ra.scalar = L.scalar; ra.t_out = cur;
+    if (!ple) {
+      ra.scatter = bw.dec_out; ra.scatter_off = (size_t)l * H;
+      if (next_gain) { ra.g2 = next_gain; ra.y_out = w.nrm; }
+    }
+    if (row_norm(c, ra, B, ple ? &pg_planes : (next_gain ? next_planes : nullptr))) {
+      scattered = !ple;
+      if (!ple && next_gain) next_planes->normed = true;
+    } else {
+      launch_norm_residual_rows(requantized(w.attn), other, B, H, L.post_ff_ln, c.eps, !ple && L.has_scalar,
+                                L.scalar, cur, s);
+    }
+  }
   int32_t* result = cur;
   if (ple) {
     TcOut op;
@@ -1932,12 +1986,22 @@ static const int32_t* decode_batch_layer_tp(Ctx& c, int B, int maxcap, int l, in
     op.epi = kEpiGeluMul;
     op.vec = w.ple_all + (size_t)l * B * m.P + (size_t)c.tp.rank * c.tp.Pl;
     op.ldv = m.P;
-    tp_linear(c, cur, B, H, T.pg, op);
-    tp_linear_reduce(c, w.g, B, c.tp.Pl, T.pp, w.pr);
-    launch_norm_residual_rows(w.pr, cur, B, H, L.ple_norm, c.eps, L.has_scalar, L.scalar, other, s);
+    tp_linear(c, cur, B, H, T.pg, op, &pg_planes);
+    tp_linear_sum(c, w.g, B, c.tp.Pl, T.pp);
+    RowNormArgs ra;
+    ra.a64 = c.tp.part; ra.res = cur; ra.g1 = L.ple_norm; ra.n = H; ra.eps = c.eps;
+    ra.has_scalar = L.has_scalar; ra.scalar = L.scalar; ra.t_out = other;
+    ra.scatter = bw.dec_out; ra.scatter_off = (size_t)l * H;
+    if (next_gain) { ra.g2 = next_gain; ra.y_out = w.nrm; }
+    if (row_norm(c, ra, B, next_gain ? next_planes : nullptr)) {
+      scattered = true;
+      if (next_gain) next_planes->normed = true;
+    } else {
+      launch_norm_residual_rows(requantized(w.pr), cur, B, H, L.ple_norm, c.eps, L.has_scalar, L.scalar, other, s);
+    }
     result = other;
   }
-  launch_scatter_rows(result, B, H, bw.dec_out, (size_t)l * H, s);
+  if (!scattered) launch_scatter_rows(result, B, H, bw.dec_out, (size_t)l * H, s);
   return result;
 }
 
@@ -2025,11 +2089,17 @@ static void decode_batch_tp(Ctx& c, Seq* const* seqs, const uint32_t* tokens, in
     launch_ple(pa, s);
   }
   int32_t* cur = w.xa;
-  for (int l = 0; l < m.L; ++l) cur = const_cast<int32_t*>(decode_batch_layer_tp(c, B, maxcap, l, cur));
-  launch_rmsnorm_rows(cur, B, m.H, c.final_norm, c.eps, w.nrm, s);
+  ActPlanes carry;  // the next layer's (or lm_head's) normalized input, made by the previous layer
+  for (int l = 0; l < m.L; ++l) {
+    ActPlanes next;
+    const int32_t* gain = l + 1 < m.L ? c.layers[l + 1].in_ln : c.final_norm;
+    cur = const_cast<int32_t*>(decode_batch_layer_tp(c, B, maxcap, l, cur, &carry, gain, &next));
+    carry = next;
+  }
+  if (!carry.normed) launch_rmsnorm_rows(cur, B, m.H, c.final_norm, c.eps, w.nrm, s);
   TcOut ol;
   ol.y = c.tp.lgl;
-  tp_linear(c, w.nrm, B, m.H, c.tp.lm, ol);
+  tp_linear(c, w.nrm, B, m.H, c.tp.lm, ol, carry.ready ? &carry : nullptr);
   if (m.has_softcap) launch_softcap(c.tp.lgl, B * c.tp.Vl, c.softcap, s);
   NCK(nccl_api().allGather(c.tp.lgl, c.tp.lga, (size_t)B * c.tp.Vl, ncclInt32, c.tp.comm, s));
   launch_gather_vocab(c.tp.lga, c.tp.world, B, c.tp.Vl, bw.logits_dst, s);
