@@ -239,6 +239,23 @@ int32_t rdet_nccl_unique_id(void* id_out, size_t len);
 int32_t rdet_tp_init(rdet_ctx* ctx, int32_t rank, int32_t world, const void* id, size_t len);
 int32_t rdet_tp_world(rdet_ctx* ctx); /* 1 when not sharded */
 
+/* NVLink reduction for the tensor-parallel batched decode (no counterpart in
+ * the reference).  After rdet_tp_init, every rank calls rdet_tp_ipc_export,
+ * which allocates its reduction buffers for batches of up to max_batch
+ * sequences and writes an opaque blob (*len = 136 bytes; cap must hold it;
+ * every rank passes the same max_batch);
+ * the caller gathers the blobs of all ranks in rank order (one process per
+ * GPU) and every rank calls rdet_tp_ipc_connect with them.  From then on each
+ * column-slice projection's i64 partial sums are stored by each rank into
+ * every other rank's reduction buffer over NVLink (CUDA IPC peer memory,
+ * plain stores) and summed there once the per-reduction flags are published,
+ * instead of an NCCL all-reduce: same results bit for bit.  The flag waits are bounded; a rank that stops
+ * publishing makes the others' rdet_decode fail with RDET_E_CUDA.  All ranks
+ * must decode in lockstep and close their contexts only after every rank has
+ * finished its last rdet_decode.  At most 8 ranks. */
+int32_t rdet_tp_ipc_export(rdet_ctx* ctx, uint32_t max_batch, void* out, size_t cap, size_t* len);
+int32_t rdet_tp_ipc_connect(rdet_ctx* ctx, const void* blobs, size_t len_each, int32_t world);
+
 /* 1 when this context's prefill linears run on the tcgen05 tensor cores (an
  * sm_100 device, the context opened without RDET_FLAG_NO_TENSOR_CORES and at
  * least one eligible weight), else 0.  Prompts shorter than 32 tokens use the

@@ -38,7 +38,7 @@ SYMBOLS = [
     "rdet_prefill_finalize", "rdet_select", "rdet_decode", "rdet_decode_begin", "rdet_decode_range",
     "rdet_decode_finalize", "rdet_generate", "rdet_read", "rdet_commitment", "rdet_kv_prefix_commitments",
     "rdet_det_gemv", "rdet_det_linear",
-    "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_det_attention_prefill", "rdet_convert_to_wgt", "rdet_get_stream", "rdet_tensor_core_prefill", "rdet_nccl_unique_id", "rdet_tp_init", "rdet_tp_world", "rdet_seq_kernels_per_step", "rdet_last_error",
+    "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_det_attention_prefill", "rdet_convert_to_wgt", "rdet_get_stream", "rdet_tensor_core_prefill", "rdet_nccl_unique_id", "rdet_tp_init", "rdet_tp_world", "rdet_tp_ipc_export", "rdet_tp_ipc_connect", "rdet_seq_kernels_per_step", "rdet_last_error",
     "rdet_version",
 ]
 
@@ -105,6 +105,8 @@ def lib() -> C.CDLL:
         "rdet_nccl_unique_id": [p, sz],
         "rdet_tp_init": [p, i32, i32, p, sz],
         "rdet_tp_world": [p],
+        "rdet_tp_ipc_export": [p, u32, p, sz, p],
+        "rdet_tp_ipc_connect": [p, p, sz, i32],
         "rdet_seq_kernels_per_step": [p, p],
         "rdet_last_error": [C.c_char_p, sz],
     }
@@ -178,6 +180,23 @@ class Model:
         opened the same model and passes the same id from nccl_unique_id()."""
         buf = C.create_string_buffer(bytes(uid), len(uid))
         _check(lib().rdet_tp_init(self._h, rank, world, buf, len(uid)))
+
+    def tp_ipc_export(self, max_batch: int) -> bytes:
+        """This rank's NVLink reduction buffers for batches of up to max_batch
+        sequences (rdet_tp_ipc_export): an opaque blob for every other rank."""
+        buf = C.create_string_buffer(256)
+        n = C.c_size_t(0)
+        _check(lib().rdet_tp_ipc_export(self._h, max_batch, buf, 256, C.byref(n)))
+        return buf.raw[: n.value]
+
+    def tp_ipc_connect(self, blobs) -> None:
+        """Map the other ranks' reduction buffers (all ranks' export blobs in
+        rank order, rdet_tp_ipc_connect): the sharded decode then reduces over
+        NVLink instead of NCCL."""
+        each = len(blobs[0])
+        assert all(len(b) == each for b in blobs)
+        buf = C.create_string_buffer(b"".join(blobs), each * len(blobs))
+        _check(lib().rdet_tp_ipc_connect(self._h, buf, each, len(blobs)))
 
     @property
     def tp_world(self) -> int:

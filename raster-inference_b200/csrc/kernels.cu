@@ -1030,8 +1030,26 @@ void launch_norm_residual_rows(const int32_t* a, const int32_t* res, int32_t S, 
 
 // Fused row norms (RowNormArgs in kernels.h).  One block per row, n % 4 == 0,
 // every pointer 16-byte aligned (the launcher's caller checks).
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __global__ void row_norm_kernel(const RowNormArgs a, int S) {
   pdl_entry();
+  if (a.wait_mask) {
+    // the peers' sums of this reduction have been published
+    if (threadIdx.x == 0) {
+      for (int r = 0; r < 32; ++r) {
+        if (!((a.wait_mask >> r) & 1u)) continue;
+        uint32_t it = 0;
+        while (ld_acquire_sys(a.flags + r) < a.wait_seq && ++it < (1u << 22)) __nanosleep(64);
+        if (it >= (1u << 22)) atomicExch(&g_stream_err, 1);
+      }
+    }
+    __syncthreads();
+  }
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int4* xs = reinterpret_cast<int4*>(smem_raw);
   __shared__ uint64_t red[33];
@@ -1042,7 +1060,15 @@ __global__ void row_norm_kernel(const RowNormArgs a, int S) {
   for (int q = threadIdx.x; q < nq; q += blockDim.x) {
     int4 v;
     if (a.a64) {
-      const longlong2 x0 = ar64[2 * q], x1 = ar64[2 * q + 1];
+      longlong2 x0 = ar64[2 * q], x1 = ar64[2 * q + 1];
+      for (int i = 0; i < a.npeer; ++i) {  // wrapping i64 sums: order-free
+        const longlong2* pr = reinterpret_cast<const longlong2*>(a.a64_peer[i] + (size_t)r * n);
+        const longlong2 y0 = __ldcv(pr + 2 * q), y1 = __ldcv(pr + 2 * q + 1);
+        x0.x = (long long)((unsigned long long)x0.x + (unsigned long long)y0.x);
+        x0.y = (long long)((unsigned long long)x0.y + (unsigned long long)y0.y);
+        x1.x = (long long)((unsigned long long)x1.x + (unsigned long long)y1.x);
+        x1.y = (long long)((unsigned long long)x1.y + (unsigned long long)y1.y);
+      }
       v = make_int4(requantize(x0.x), requantize(x0.y), requantize(x1.x), requantize(x1.y));
     } else {
       v = ar[q];
@@ -2587,6 +2613,18 @@ __global__ void requantize_rows_kernel(const int64_t* x, size_t n, int32_t* y) {
   pdl_entry();
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
     y[i] = requantize(x[i]);
+}
+__global__ void tp_signal_kernel(const TpPeerFlags peers, int world, int rank, uint32_t value) {
+  pdl_entry();
+  const int r = threadIdx.x;
+  if (r < world && r != rank && peers.f[r]) {
+    // the sums the preceding kernels wrote are visible system-wide before the flag
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peers.f[r] + rank), "r"(value) : "memory");
+  }
+}
+void launch_tp_signal(const TpPeerFlags& peers, int32_t world, int32_t rank, uint32_t value, cudaStream_t s) {
+  launch_k(tp_signal_kernel, dim3(1), dim3(32), 0, s, peers, (int)world, (int)rank, value);
 }
 void launch_requantize_rows(const int64_t* x, size_t n, int32_t* y, cudaStream_t s) {
   const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)sm_count() * 4);

@@ -122,9 +122,16 @@ constexpr int kTcShortRows = 64;
 // vec[s * ldv + n]).  y64 instead: the exact wrapping i64 sums before
 // requantize (needs scratch).  With scratch the K loop may be split across
 // CTAs when the output tiles alone would leave SMs idle.
+// Copies of the i64 sums written into other GPUs' memory (peer pointers of
+// the tensor-parallel NVLink reduction), each [S, N] like y64.
+struct TcMirrors {
+  int64_t* p[7] = {};
+  int32_t n = 0;
+};
 struct TcOut {
   int32_t* y = nullptr;
   int64_t* y64 = nullptr;
+  TcMirrors y64_mirror;         // y64 is also stored to these (the split-K finish only)
   int32_t epi = 0;
   const int32_t* vec = nullptr;
   int32_t ldv = 0;              // 0: N
@@ -156,6 +163,14 @@ struct RowNormArgs {
   // instead of a: exact i64 sums (a tensor-parallel all-reduce's output),
   // requantized as they are loaded
   const int64_t* a64 = nullptr;
+  // the tensor-parallel NVLink reduction: a64 plus the same rows of the
+  // peers' sums (peer memory), read once flags[r] >= wait_seq for every rank
+  // r in wait_mask (flags in this GPU's memory, written by the peers; the
+  // wait is bounded and sets the pipeline error flag when it gives up)
+  const int64_t* a64_peer[7] = {};
+  int32_t npeer = 0;
+  const uint32_t* flags = nullptr;
+  uint32_t wait_mask = 0, wait_seq = 0;
   const int32_t* res = nullptr;
   const int32_t* g1 = nullptr;
   const int32_t* g2 = nullptr;
@@ -329,6 +344,13 @@ void launch_softcap(int32_t* x, int32_t n, int32_t cap, cudaStream_t s);
 void launch_add_i32(int32_t* p, int32_t v, cudaStream_t s);  // *p += v
 void launch_add_i32_rows(int32_t* const* p, int32_t n, int32_t v, cudaStream_t s);  // *p[i] += v
 void launch_requantize_rows(const int64_t* x, size_t n, int32_t* y, cudaStream_t s);  // y = requantize(x)
+// Publishes reduction number `value` of rank `rank` to the other ranks:
+// peer_flags[r][rank] = value (system-scope release) for r != rank, after the
+// sums written by the preceding kernels.
+struct TpPeerFlags {
+  uint32_t* f[8] = {};
+};
+void launch_tp_signal(const TpPeerFlags& peers, int32_t world, int32_t rank, uint32_t value, cudaStream_t s);
 // vocab-sharded logits: src [world][rows][vl] -> dst[r][w * vl + j]
 // ---- model ingestion: safetensors values -> Q16.16 weights (convert.cu) --------------
 enum SrcDtype : int32_t { kSrcF32 = 0, kSrcBF16 = 1, kSrcF16 = 2 };

@@ -463,6 +463,22 @@ struct TpState {
   int64_t* part = nullptr;     // [rows, H] partial sums before requantize
   int32_t* lgl = nullptr;      // [rows, Vl] this rank's logits
   int32_t* lga = nullptr;      // [world, rows, Vl] gathered logits
+  // NVLink reduction (rdet_tp_ipc_export / _connect): recv [world][2][p2p_rows][H]
+  // holds every rank's column-slice sums of a reduction (two alternating
+  // slots); each rank's split-K finish stores its sums into its own slot of
+  // every rank's recv (peer stores over NVLink), then publishes the
+  // reduction's number in the peers' flags (one word per source rank); the
+  // next row kernel adds the world slots from local memory.  recv and flags
+  // are mapped into the other ranks through CUDA IPC.
+  bool p2p = false;
+  int p2p_rows = 0;
+  int64_t* recv = nullptr;
+  uint32_t* flags = nullptr;
+  int64_t* peer_recv[8] = {};
+  TpPeerFlags peer_flags;
+  std::vector<void*> ipc_opened;
+  uint32_t seq = 0;            // reductions issued so far
+  const int64_t* last = nullptr;  // the buffer holding the last reduction's local sums
 };
 
 struct Seq;
@@ -576,6 +592,7 @@ struct Ctx {
     for (cudaEvent_t e : kvs.ev)
       if (e) cudaEventDestroy(e);
     if (kvs.host) cudaFreeHost(kvs.host);
+    for (void* p : tp.ipc_opened) cudaIpcCloseMemHandle(p);
     if (tp.comm) nccl_api().commDestroy(tp.comm);
     for (void* p : allocs) cudaFree(p);
     if (stream) cudaStreamDestroy(stream);
@@ -1884,13 +1901,45 @@ static void tp_linear(Ctx& c, const int32_t* X, int S, int K, const TcWeight& w,
   REQUIRE(launch_tc_linear(ap.a, w, oo, c.stream), RDET_E_RANGE, "batch too large for the split-K scratch");
 }
 
-// partial sums [S, N] of a column slice -> all-reduce, left in c.tp.part (the
-// next row kernel requantizes them as it loads them)
+// Sums [S, N] of a column slice, completed over the ranks: with the NVLink
+// reduction, left in this rank's alternating buffer and published to the
+// peers (the next row kernel adds the peers' buffers as it loads); else an
+// NCCL all-reduce in c.tp.part.  Either way the next row kernel requantizes.
 static void tp_linear_sum(Ctx& c, const int32_t* X, int S, int K, const TcWeight& w) {
+  TpState& t = c.tp;
   TcOut o;
-  o.y64 = c.tp.part;
+  if (t.p2p) {
+    REQUIRE(S <= t.p2p_rows, RDET_E_RANGE, "batch larger than the NVLink reduction buffers (rdet_tp_ipc_export)");
+    const size_t slot = ((size_t)t.rank * 2 + (t.seq & 1)) * (size_t)t.p2p_rows * c.cfg.H;
+    o.y64 = t.recv + slot;
+    for (int r = 0; r < t.world; ++r)
+      if (r != t.rank) o.y64_mirror.p[o.y64_mirror.n++] = t.peer_recv[r] + slot;
+    tp_linear(c, X, S, K, w, o);
+    t.last = o.y64;
+    t.seq += 1;
+    launch_tp_signal(t.peer_flags, t.world, t.rank, t.seq, c.stream);
+    return;
+  }
+  o.y64 = t.part;
   tp_linear(c, X, S, K, w, o);
-  NCK(nccl_api().allReduce(c.tp.part, c.tp.part, (size_t)S * w.N, ncclInt64, ncclSum, c.tp.comm, c.stream));
+  NCK(nccl_api().allReduce(t.part, t.part, (size_t)S * w.N, ncclInt64, ncclSum, t.comm, c.stream));
+  t.last = t.part;
+}
+
+// The row kernel's input after tp_linear_sum: the local sums plus, with the
+// NVLink reduction, the peers' buffers of the same reduction and its flag.
+static void tp_sum_input(const Ctx& c, RowNormArgs& ra) {
+  const TpState& t = c.tp;
+  ra.a64 = t.last;
+  if (!t.p2p) return;
+  const size_t slot = (t.seq - 1) & 1;
+  for (int r = 0; r < t.world; ++r) {
+    if (r == t.rank) continue;
+    ra.a64_peer[ra.npeer++] = t.recv + ((size_t)r * 2 + slot) * (size_t)t.p2p_rows * c.cfg.H;
+    ra.wait_mask |= 1u << r;
+  }
+  ra.flags = t.flags;
+  ra.wait_seq = t.seq;
 }
 
 // in_planes / next_gain / next_planes as in decode_batch_layer.  The row
@@ -1909,7 +1958,11 @@ static const int32_t* decode_batch_layer_tp(Ctx& c, int B, int maxcap, int l, in
   const int H = m.H, d = lc.head_dim, Hql = c.tp.Hql;
   int32_t* other = cur == w.xa ? w.xb : w.xa;
   // sums of a column-sliced GEMM -> i32 rows, for the unfused fallbacks
-  auto requantized = [&](int32_t* y) { launch_requantize_rows(c.tp.part, (size_t)B * H, y, s); return y; };
+  auto requantized = [&](int32_t* y) {
+    REQUIRE(!c.tp.p2p, RDET_E_STATE, "the NVLink reduction needs 16-byte aligned rows");
+    launch_requantize_rows(c.tp.part, (size_t)B * H, y, s);
+    return y;
+  };
   ActPlanes nrm_planes;
   if (in_planes && in_planes->ready) {
     nrm_planes = *in_planes;
@@ -1949,7 +2002,7 @@ static const int32_t* decode_batch_layer_tp(Ctx& c, int B, int maxcap, int l, in
   ActPlanes ff_planes;
   {
     RowNormArgs ra;
-    ra.a64 = c.tp.part; ra.res = cur; ra.g1 = L.post_attn_ln; ra.g2 = L.pre_ff_ln; ra.n = H; ra.eps = c.eps;
+    tp_sum_input(c, ra); ra.res = cur; ra.g1 = L.post_attn_ln; ra.g2 = L.pre_ff_ln; ra.n = H; ra.eps = c.eps;
     ra.t_out = other; ra.y_out = w.nrm;
     if (!row_norm(c, ra, B, &ff_planes)) {
       launch_norm_residual_rows(requantized(w.attn), cur, B, H, L.post_attn_ln, c.eps, false, 0, other, s);
@@ -1965,7 +2018,7 @@ static const int32_t* decode_batch_layer_tp(Ctx& c, int B, int maxcap, int l, in
   bool scattered = false;
   {
     RowNormArgs ra;
-    ra.a64 = c.tp.part; ra.res = other; ra.g1 = L.post_ff_ln; ra.n = H; ra.eps = c.eps;
+    tp_sum_input(c, ra); ra.res = other; ra.g1 = L.post_ff_ln; ra.n = H; ra.eps = c.eps;
     ra.has_scalar = !ple && L.has_scalar; ra.scalar = L.scalar; ra.t_out = cur;
     if (!ple) {
       ra.scatter = bw.dec_out; ra.scatter_off = (size_t)l * H;
@@ -1989,7 +2042,7 @@ static const int32_t* decode_batch_layer_tp(Ctx& c, int B, int maxcap, int l, in
     tp_linear(c, cur, B, H, T.pg, op, &pg_planes);
     tp_linear_sum(c, w.g, B, c.tp.Pl, T.pp);
     RowNormArgs ra;
-    ra.a64 = c.tp.part; ra.res = cur; ra.g1 = L.ple_norm; ra.n = H; ra.eps = c.eps;
+    tp_sum_input(c, ra); ra.res = cur; ra.g1 = L.ple_norm; ra.n = H; ra.eps = c.eps;
     ra.has_scalar = L.has_scalar; ra.scalar = L.scalar; ra.t_out = other;
     ra.scatter = bw.dec_out; ra.scatter_off = (size_t)l * H;
     if (next_gain) { ra.g2 = next_gain; ra.y_out = w.nrm; }
@@ -2823,6 +2876,65 @@ int32_t rdet_tp_init(rdet_ctx* ctx, int32_t rank, int32_t world, const void* id,
     ncclUniqueId uid;
     memcpy(&uid, id, sizeof(uid));
     tp_init(c, rank, world, uid);
+  });
+}
+
+// IPC handles of recv and flags, then the row count of recv's slots as a u64.
+constexpr size_t kTpIpcBlob = 2 * sizeof(cudaIpcMemHandle_t) + 8;
+
+int32_t rdet_tp_ipc_export(rdet_ctx* ctx, uint32_t max_batch, void* out, size_t cap, size_t* len) {
+  return guard([&] {
+    REQUIRE(ctx && out && len, RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    TpState& t = c.tp;
+    REQUIRE(t.comm != nullptr, RDET_E_STATE, "rdet_tp_ipc_export needs rdet_tp_init first");
+    REQUIRE(t.recv == nullptr, RDET_E_STATE, "the NVLink reduction buffers are already exported");
+    REQUIRE(max_batch >= 1 && max_batch <= 65536, RDET_E_INVALID, "max_batch must be in [1, 65536]");
+    REQUIRE(t.world <= 8, RDET_E_INVALID, "the NVLink reduction supports at most 8 ranks");
+    REQUIRE(cap >= kTpIpcBlob, RDET_E_INVALID, "the export buffer needs " + std::to_string(kTpIpcBlob) + " bytes");
+    CK(cudaSetDevice(c.device));
+    t.p2p_rows = (int)max_batch;
+    t.recv = c.dalloc_n<int64_t>((size_t)t.world * 2 * t.p2p_rows * c.cfg.H);
+    t.flags = c.dalloc_n<uint32_t>(32);
+    CK(cudaMemset(t.flags, 0, 32 * sizeof(uint32_t)));
+    cudaIpcMemHandle_t h[2];
+    CK(cudaIpcGetMemHandle(&h[0], t.recv));
+    CK(cudaIpcGetMemHandle(&h[1], t.flags));
+    const uint64_t rows = (uint64_t)t.p2p_rows;
+    memcpy(out, h, sizeof(h));
+    memcpy(static_cast<unsigned char*>(out) + sizeof(h), &rows, 8);
+    *len = kTpIpcBlob;
+  });
+}
+
+int32_t rdet_tp_ipc_connect(rdet_ctx* ctx, const void* blobs, size_t len_each, int32_t world) {
+  return guard([&] {
+    REQUIRE(ctx && blobs, RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    TpState& t = c.tp;
+    REQUIRE(t.recv != nullptr, RDET_E_STATE, "rdet_tp_ipc_connect needs rdet_tp_ipc_export first");
+    REQUIRE(!t.p2p, RDET_E_STATE, "the NVLink reduction is already connected");
+    REQUIRE(world == t.world && len_each == kTpIpcBlob, RDET_E_INVALID, "one export blob per rank, in rank order");
+    CK(cudaSetDevice(c.device));
+    // every rank's buffers hold the sums of the same rows: same batch limit
+    CK(cudaDeviceSynchronize());
+    const unsigned char* b = static_cast<const unsigned char*>(blobs);
+    for (int r = 0; r < world; ++r) {
+      if (r == t.rank) continue;
+      cudaIpcMemHandle_t h[2];
+      uint64_t rows = 0;
+      memcpy(h, b + (size_t)r * kTpIpcBlob, sizeof(h));
+      memcpy(&rows, b + (size_t)r * kTpIpcBlob + sizeof(h), 8);
+      REQUIRE(rows == (uint64_t)t.p2p_rows, RDET_E_INVALID, "every rank must export the same max_batch");
+      void* p[2] = {nullptr, nullptr};
+      for (int i = 0; i < 2; ++i) {
+        CK(cudaIpcOpenMemHandle(&p[i], h[i], cudaIpcMemLazyEnablePeerAccess));
+        t.ipc_opened.push_back(p[i]);
+      }
+      t.peer_recv[r] = static_cast<int64_t*>(p[0]);
+      t.peer_flags.f[r] = static_cast<uint32_t*>(p[1]);
+    }
+    t.p2p = true;
   });
 }
 

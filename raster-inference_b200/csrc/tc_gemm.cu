@@ -922,7 +922,7 @@ template <int MODE>
 __global__ void tc_splitk_reduce_kernel(const uint64_t* __restrict__ part, int ks, int S, int nrows, int N, int K,
                                         const uint64_t* __restrict__ arow, const uint64_t* __restrict__ brow,
                                         int32_t* __restrict__ Y, int64_t* __restrict__ Y64,
-                                        const int32_t* __restrict__ vec, int ldv) {
+                                        const int32_t* __restrict__ vec, int ldv, const TcMirrors mirror) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const size_t total = (size_t)S * N;
@@ -935,6 +935,7 @@ __global__ void tc_splitk_reduce_kernel(const uint64_t* __restrict__ part, int k
     acc -= rc.corr + (brow[r] << rc.e);
     if (MODE == 3) {
       Y64[e] = (int64_t)acc;
+      for (int i = 0; i < mirror.n; ++i) mirror.p[i][e] = (int64_t)acc;  // posted stores over NVLink
       continue;
     }
     int32_t y = requantize((int64_t)acc);
@@ -949,6 +950,8 @@ __global__ void tc_splitk_reduce_kernel(const uint64_t* __restrict__ part, int k
     }
     Y[e] = y;
   }
+  // the mirrored sums reach the peers' memory before any later flag store
+  if (MODE == 3 && mirror.n) __threadfence_system();
 }
 
 // u8 planes [planes][rows][K] -> 3D map (K, rows, planes), box (64, box_rows, 1)
@@ -1161,16 +1164,16 @@ void launch_splitk_reduce(const TcAct& a, const TcWeight& w, const TcOut& o, int
   const int rblocks = (int)std::min<size_t>((total + 255) / 256, (size_t)sms * 8);
   if (o.y64)
     tc_launch(tc_splitk_reduce_kernel<3>, dim3(rblocks), dim3(256), 0, s, part, ks, a.S, w.nrows, w.N, a.K, a.rowsum,
-              w.rowsum, (int32_t*)nullptr, o.y64, o.vec, ldv);
+              w.rowsum, (int32_t*)nullptr, o.y64, o.vec, ldv, o.y64_mirror);
   else if (w.pair)
     tc_launch(tc_splitk_reduce_kernel<2>, dim3(rblocks), dim3(256), 0, s, part, ks, a.S, w.nrows, w.N, a.K, a.rowsum,
-              w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv);
+              w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv, o.y64_mirror);
   else if (o.epi == kEpiGeluMul)
     tc_launch(tc_splitk_reduce_kernel<1>, dim3(rblocks), dim3(256), 0, s, part, ks, a.S, w.nrows, w.N, a.K, a.rowsum,
-              w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv);
+              w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv, o.y64_mirror);
   else
     tc_launch(tc_splitk_reduce_kernel<0>, dim3(rblocks), dim3(256), 0, s, part, ks, a.S, w.nrows, w.N, a.K, a.rowsum,
-              w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv);
+              w.rowsum, o.y, (int64_t*)nullptr, o.vec, ldv, o.y64_mirror);
 }
 
 // S <= 64: the swapped-operand kernel.  K splits are chosen by a small time
