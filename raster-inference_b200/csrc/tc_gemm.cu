@@ -1147,8 +1147,10 @@ bool tc_prepare_act(TcAct& a, const int32_t* X, int S, int K, void* mem, cudaStr
   a.K = K;
   a.planes = static_cast<uint8_t*>(mem);
   a.rowsum = reinterpret_cast<uint64_t*>(a.planes + 4 * (size_t)S * K);
-  a.tile4 = reinterpret_cast<uint32_t*>(a.rowsum + S);
-  if (cudaMemsetAsync(a.tile4, 0, ((size_t)(S + kT2Mrows - 1) / kT2Mrows) * 4, s) != cudaSuccess) return false;
+  // the tile flags are read only by the CTA-pair kernel (more than kTcM rows)
+  a.tile4 = S > kTcM ? reinterpret_cast<uint32_t*>(a.rowsum + S) : nullptr;
+  if (a.tile4 && cudaMemsetAsync(a.tile4, 0, ((size_t)(S + kT2Mrows - 1) / kT2Mrows) * 4, s) != cudaSuccess)
+    return false;
   tc_launch(tc_act_prep_kernel, dim3(S), dim3(256), 0, s, X, S, K, a.planes, a.rowsum, a.tile4);
   return encode_planes(a.map, a.planes, 4, S, K, kTcM) && encode_planes(a.map_t, a.planes, 4, S, K, kTsT);
 }
