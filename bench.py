@@ -418,16 +418,16 @@ def run_kernel_case(args):
         seqs = [model.new_sequence(n + 16) for n in lens]
         for i, (sq, n) in enumerate(zip(seqs, lens)):
             sq.prefill(lcg_ids(n, t["vocab_size"], SEED + 100 + i))
-        toks = [sq.select() for sq in seqs]
+        toks = rdet.select_batch(model, seqs)
         for rep in range(3):
             torch.cuda.synchronize()
             if rep == 2:
                 torch.cuda.nvtx.range_push("batch")
             rdet.decode_batch(model, seqs, toks)
+            toks = rdet.select_batch(model, seqs)
             torch.cuda.synchronize()
             if rep == 2:
                 torch.cuda.nvtx.range_pop()
-            toks = [sq.select() for sq in seqs]
         model.close()
         print(f"batched decode step: {args.batch} sequences")
         return
@@ -554,39 +554,48 @@ def run_kernel_case(args):
 def batched_run(args, torch, rdet, dist, model, stream, t, rank, world, local_rank, mode):
     """64 sequences, prompt lengths 128 + draw % 3969
     (seeded), greedy: one batched decode_transition per step, then
-    select_output_token for every sequence.  mode "single": all sequences on
-    this GPU; "split": sequence i on rank i % world, each rank one batched
-    decode of its own sequences per step; "tp": every rank decodes all of them
-    through the tensor-parallel path.  Steps are device-timed per step (the
-    selects between steps are not), max over ranks; the first 3 steps warm
-    up.  The CPU oracle's 4-sequence subset is checked token for token."""
+    select_output_token for every sequence (one batched select).  mode
+    "single": all sequences on this GPU; "split": sequence i on rank i % world,
+    each rank one batched decode of its own sequences per step; "tp": every
+    rank decodes all of them through the tensor-parallel path, selecting by
+    the global argmax over the vocab-sharded logits.  A step is the batched
+    decode_transition plus the batched select with its tokens copied to the
+    host, device-timed per step, max over ranks; the transition alone is
+    reported beside it.  The first 3 steps warm up.  The CPU oracle's
+    4-sequence subset is checked token for token."""
     lens = [128 + (x % 3969) for x in lcg_ids(args.batch, 1 << 30, SEED + 7)]
     mine = [i for i in range(args.batch) if mode != "split" or i % world == rank]
     if mode == "tp":
         uid = [rdet.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         model.tp_init(rank, world, uid[0])
+        model.tp_shard_logits(True)
     nsteps = args.batch_steps
     seqs = [model.new_sequence(lens[i] + nsteps + 8) for i in mine]
     for sq, i in zip(seqs, mine):
         sq.prefill(lcg_ids(lens[i], t["vocab_size"], SEED + 100 + i))
-    toks = [sq.select() for sq in seqs]
+    toks = rdet.select_batch(model, seqs)
     gen = {i: [] for i in mine}
-    step_ms = []
+    step_ms, trans_ms = [], []
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
     for step in range(nsteps):
         for i, tk in zip(mine, toks):
             gen[i].append(tk)
-        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0, bt, b1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         b0.record(stream)
         rdet.decode_batch(model, seqs, toks)
+        bt.record(stream)
+        toks = rdet.select_batch(model, seqs)  # tokens to the host (synchronizes)
         b1.record(stream)
-        toks = [sq.select() for sq in seqs]  # synchronizes
+        b1.synchronize()
         step_ms.append(b0.elapsed_time(b1))
+        trans_ms.append(b0.elapsed_time(bt))
     timed = step_ms[3:] if len(step_ms) > 6 else step_ms
+    ttimed = trans_ms[3:] if len(trans_ms) > 6 else trans_ms
     bsec = sum(timed) / 1000
+    tsec = sum(ttimed) / 1000
     # fixture check: mismatching and checked sequences, summed over the ranks
     bad = checked = 0
     fx = load_fixtures()
@@ -597,9 +606,9 @@ def batched_run(args, torch, rdet, dist, model, stream, t, rank, world, local_ra
                 checked += 1
                 bad += gen[int(k)][:n5] != r["tokens"]
     if dist:
-        tt = torch.tensor([bsec], dtype=torch.float64, device=f"cuda:{local_rank}")
+        tt = torch.tensor([bsec, tsec], dtype=torch.float64, device=f"cuda:{local_rank}")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        bsec = float(tt[0])
+        bsec, tsec = float(tt[0]), float(tt[1])
         cc = torch.tensor([bad, checked], dtype=torch.int64, device=f"cuda:{local_rank}")
         dist.all_reduce(cc, op=dist.ReduceOp.SUM)
         bad, checked = int(cc[0]), int(cc[1])
@@ -611,11 +620,13 @@ def batched_run(args, torch, rdet, dist, model, stream, t, rank, world, local_ra
     return {"sequences": args.batch, "context": f"128 + draw mod 3969 (seeded), mean {sum(lens) // len(lens)}",
             "parallelism": par, "scaling": None if mode == "single" else "strong",
             "steps": nsteps, "timed_steps": len(timed), "tok_s": args.batch * len(timed) / bsec,
-            "ms_per_step": 1000 * bsec / len(timed),
+            "ms_per_step": 1000 * bsec / len(timed), "transition_ms_per_step": 1000 * tsec / len(ttimed),
             "bit_exact_vs_cpu": (bad == 0) if checked else None, "checked_sequences": checked,
-            "note": "greedy: device-timed batched decode_transition per step (max over ranks), "
-                    "select_output_token per sequence between steps (not timed); the first 3 steps are warm-up; "
-                    "bit_exact_vs_cpu checks the CPU oracle's 4-sequence subset (tests/golden/e4b_fixtures.json)"}
+            "note": "greedy: a step is one batched decode_transition plus one batched select_output_token "
+                    "with the tokens read back to the host, device-timed (max over ranks); tensor-parallel "
+                    "ranks select by the global argmax over vocab-sharded logits ((value, index) pairs); "
+                    "the first 3 steps are warm-up; bit_exact_vs_cpu checks the CPU oracle's 4-sequence subset "
+                    "(tests/golden/e4b_fixtures.json)"}
 
 
 def run_ours(args, rank, world, local_rank):

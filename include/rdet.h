@@ -100,6 +100,13 @@ int32_t rdet_prefill_finalize(rdet_ctx* ctx, rdet_seq* seq);
 /* select_output_token: argmax_first over the resident logits, lowest index on
  * ties (decode_select_token/native/tiles.rs:22-38, det_num/ops.rs:463). */
 int32_t rdet_select(rdet_ctx* ctx, rdet_seq* seq, uint32_t* token_out);
+/* select_output_token for n sequences at once (the per-sequence routine of
+ * decode_select_token/native/tiles.rs:22-38 applied to each):
+ * tokens_out[i] = argmax_first of seqs[i]'s logits, lowest index on ties,
+ * in one launch over all rows.  A sequence whose last batched decode ran
+ * with vocab-sharded logits (rdet_tp_shard_logits) gets the token that
+ * decode's global argmax selected; select it before its next decode. */
+int32_t rdet_select_batch(rdet_ctx* ctx, rdet_seq* const* seqs, size_t n, uint32_t* tokens_out);
 
 /* decode_transition for a (ragged) batch: for each sequence, embed its token
  * at its own position, run every layer (appending to its KV cache) and
@@ -238,6 +245,18 @@ int32_t rdet_det_attention_decode_noalloc(const int32_t* q, const int32_t* k_cac
 int32_t rdet_nccl_unique_id(void* id_out, size_t len);
 int32_t rdet_tp_init(rdet_ctx* ctx, int32_t rank, int32_t world, const void* id, size_t len);
 int32_t rdet_tp_world(rdet_ctx* ctx); /* 1 when not sharded */
+/* Vocab-sharded selection for the tensor-parallel batched decode (the
+ * global argmax over a vocab-sharded lm_head; argmax_first,
+ * det_num/ops.rs:463-478).  With on != 0, rdet_decode on two or more
+ * sequences no longer all-gathers the logit rows: each rank finds the first
+ * maximum of its own vocab rows per sequence, the ranks exchange those
+ * (value, global index) pairs (8 bytes per row and chunk) and every rank
+ * reduces them to the same tokens, which rdet_select_batch returns.  The
+ * sequences' full logits are then not assembled on any rank: rdet_select,
+ * rdet_generate, and reading or committing RDET_BUF_LOGITS fail with
+ * RDET_E_STATE until their next prefill or unsharded decode.  on = 0
+ * restores the default (logits all-gathered).  Needs rdet_tp_init. */
+int32_t rdet_tp_shard_logits(rdet_ctx* ctx, int32_t on);
 
 /* NVLink reduction for the tensor-parallel batched decode (no counterpart in
  * the reference).  After rdet_tp_init, every rank calls rdet_tp_ipc_export,

@@ -35,10 +35,10 @@ FLAG_NO_TENSOR_CORES = 2
 SYMBOLS = [
     "rdet_open", "rdet_open_synthetic", "rdet_close", "rdet_get_model_info", "rdet_seq_new", "rdet_seq_free",
     "rdet_seq_position", "rdet_embed", "rdet_prefill", "rdet_prefill_begin", "rdet_prefill_range",
-    "rdet_prefill_finalize", "rdet_select", "rdet_decode", "rdet_decode_begin", "rdet_decode_range",
+    "rdet_prefill_finalize", "rdet_select", "rdet_select_batch", "rdet_decode", "rdet_decode_begin", "rdet_decode_range",
     "rdet_decode_finalize", "rdet_generate", "rdet_read", "rdet_commitment", "rdet_kv_prefix_commitments",
     "rdet_det_gemv", "rdet_det_linear",
-    "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_det_attention_prefill", "rdet_convert_to_wgt", "rdet_get_stream", "rdet_tensor_core_prefill", "rdet_nccl_unique_id", "rdet_tp_init", "rdet_tp_world", "rdet_tp_ipc_export", "rdet_tp_ipc_connect", "rdet_seq_kernels_per_step", "rdet_last_error",
+    "rdet_det_attention_decode", "rdet_det_attention_decode_noalloc", "rdet_det_attention_prefill", "rdet_convert_to_wgt", "rdet_get_stream", "rdet_tensor_core_prefill", "rdet_nccl_unique_id", "rdet_tp_init", "rdet_tp_world", "rdet_tp_shard_logits", "rdet_tp_ipc_export", "rdet_tp_ipc_connect", "rdet_seq_kernels_per_step", "rdet_last_error",
     "rdet_version",
 ]
 
@@ -86,6 +86,8 @@ def lib() -> C.CDLL:
         "rdet_prefill_range": [p, p, u32, u32],
         "rdet_prefill_finalize": [p, p],
         "rdet_select": [p, p, p],
+        "rdet_select_batch": [p, p, sz, p],
+        "rdet_tp_shard_logits": [p, i32],
         "rdet_decode": [p, p, p, sz],
         "rdet_decode_begin": [p, p, u32],
         "rdet_decode_range": [p, p, u32, u32],
@@ -180,6 +182,12 @@ class Model:
         opened the same model and passes the same id from nccl_unique_id()."""
         buf = C.create_string_buffer(bytes(uid), len(uid))
         _check(lib().rdet_tp_init(self._h, rank, world, buf, len(uid)))
+
+    def tp_shard_logits(self, on: bool = True) -> None:
+        """Vocab-sharded selection (rdet_tp_shard_logits): batched decodes end
+        with a global argmax over (value, index) pairs instead of gathering
+        the logit rows; take the tokens with select_batch."""
+        _check(lib().rdet_tp_shard_logits(self._h, 1 if on else 0))
 
     def tp_ipc_export(self, max_batch: int) -> bytes:
         """This rank's NVLink reduction buffers for batches of up to max_batch
@@ -335,6 +343,17 @@ def decode_batch(model: Model, seqs, tokens):
     arr = (C.c_void_p * len(seqs))(*[s._h for s in seqs])
     toks = np.ascontiguousarray(tokens, dtype=np.uint32)
     _check(lib().rdet_decode(model._h, arr, _ptr(toks), len(seqs)))
+
+
+def select_batch(model: Model, seqs) -> list[int]:
+    """select_output_token for every sequence in one launch (argmax_first of
+    each sequence's logits; after a vocab-sharded tensor-parallel decode,
+    the tokens its global argmax selected)."""
+    n = len(seqs)
+    arr = (C.c_void_p * max(n, 1))(*[s._h for s in seqs])
+    out = np.zeros(max(n, 1), dtype=np.uint32)
+    _check(lib().rdet_select_batch(model._h, arr, n, _ptr(out)))
+    return [int(v) for v in out[:n]]
 
 
 # ---- reference-named entry points ---------------------------------------------------

@@ -2061,9 +2061,15 @@ void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s) {
     // row is staged in a [GC][kAcVmx] shared array).  One CTA per
     // (sequence, query group) when those CTAs fit one wave: a second,
     // partly filled wave of half-size CTAs costs more than longer CTAs.
-    const int groups = a.Hq / std::max(1, std::min(4, Gq));
+    // With few query heads per GPU (tensor-parallel ranks) the one-CTA shape
+    // leaves SMs idle: split each window over the largest cluster that
+    // still fits one wave.
+    const int groups = std::max(1, a.Hq / std::max(1, std::min(4, Gq)));
+    const long ctas = (long)a.batch * groups;
+    int one_wave = 1;
+    while (one_wave < 4 && ctas * one_wave * 2 <= sm_count()) one_wave *= 2;
     int cl = wide4 ? (ac_smem(4, a.d, ac_rmax(a.window, a.cap, 4)) <= kAcMaxSmem ? 4 : 8)
-                   : ((long)a.batch * groups <= sm_count() ? 1 : RDET_AC_BATCH_CL);
+                   : (ctas <= sm_count() ? one_wave : RDET_AC_BATCH_CL);
     while (cl < CL && (a.d > kAcVmx * cl || ac_smem(1, a.d, ac_rmax(a.window, a.cap, cl)) > kAcMaxSmem)) cl *= 2;
     CL = cl < CL ? cl : CL;
   }
@@ -2571,6 +2577,56 @@ __global__ void argmax_final_kernel(const int32_t* part, int blocks, uint32_t* i
 void launch_argmax(const int32_t* x, int32_t n, int32_t* part, int32_t blocks, uint32_t* idx, cudaStream_t s) {
   launch_k(argmax_part_kernel, dim3(blocks), dim3(256), 0, s, x, n, part);
   launch_k(argmax_final_kernel, dim3(1), dim3(1), 0, s, part, blocks, idx);
+}
+
+// argmax_first of many rows at once.  Block (x, r) scans chunk x of row r
+// (row r at rows[r] when rows is given, else at base + r * ld) and writes its
+// first maximum as (value, idx0 + column) to part[(r * chunks + x) * 2].
+__global__ void argmax_rows_part_kernel(const int32_t* const* rows, const int32_t* base, int32_t n, size_t ld,
+                                        int32_t idx0, int32_t* part) {
+  pdl_entry();
+  __shared__ int32_t sv[32], si[32];
+  const int r = blockIdx.y, chunks = gridDim.x;
+  const int32_t* x = rows ? rows[r] : base + (size_t)r * ld;
+  const int j0 = (int)((int64_t)n * blockIdx.x / chunks), j1 = (int)((int64_t)n * (blockIdx.x + 1) / chunks);
+  int32_t bv = INT32_MIN, bi = INT32_MAX;
+  for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) better(bv, bi, x[j], idx0 + j);
+  for (int o = 16; o > 0; o >>= 1) {
+    int32_t v2 = __shfl_xor_sync(0xffffffffu, bv, o), i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+    better(bv, bi, v2, i2);
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) better(bv, bi, sv[w], si[w]);
+    part[((size_t)r * chunks + blockIdx.x) * 2] = bv;
+    part[((size_t)r * chunks + blockIdx.x) * 2 + 1] = bi;
+  }
+}
+// Row r's token from the pairs of `world` row blocks laid out
+// [world][B][chunks][2] (the vocab-sharded ranks' pairs after an all-gather;
+// world 1 for one GPU).  Comparing (value, index) keeps argmax_first's
+// lowest-index tie-break whatever the order of the pairs.
+__global__ void argmax_rows_final_kernel(const int32_t* part, int32_t world, int32_t B, int32_t chunks,
+                                         uint32_t* tokens) {
+  pdl_entry();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= B) return;
+  int32_t bv = INT32_MIN, bi = INT32_MAX;
+  for (int w = 0; w < world; ++w)
+    for (int x = 0; x < chunks; ++x) {
+      const int32_t* p = part + (((size_t)w * B + r) * chunks + x) * 2;
+      better(bv, bi, p[0], p[1]);
+    }
+  tokens[r] = (uint32_t)bi;
+}
+void launch_argmax_rows(const int32_t* const* rows, const int32_t* base, int32_t B, int32_t n, size_t ld,
+                        int32_t idx0, int32_t chunks, int32_t* part, cudaStream_t s) {
+  launch_k(argmax_rows_part_kernel, dim3(chunks, B), dim3(256), 0, s, rows, base, n, ld, idx0, part);
+}
+void launch_argmax_rows_final(const int32_t* part, int32_t world, int32_t B, int32_t chunks, uint32_t* tokens,
+                              cudaStream_t s) {
+  launch_k(argmax_rows_final_kernel, dim3((B + 127) / 128), dim3(128), 0, s, part, world, B, chunks, tokens);
 }
 __global__ void softcap_kernel(int32_t* x, int n, int32_t cap) {
   pdl_entry();

@@ -338,6 +338,12 @@ void launch_ple(const PleArgs& a, cudaStream_t s);
 // argmax_first over n values; result index written to *idx (u32).  `part`
 // holds at least 2*blocks ints of scratch.
 void launch_argmax(const int32_t* x, int32_t n, int32_t* part, int32_t blocks, uint32_t* idx, cudaStream_t s);
+// argmax_first of B rows: (value, idx0 + column) of each chunk's first max
+// into part [B][chunks][2]; then each row's token from [world][B][chunks][2]
+void launch_argmax_rows(const int32_t* const* rows, const int32_t* base, int32_t B, int32_t n, size_t ld,
+                        int32_t idx0, int32_t chunks, int32_t* part, cudaStream_t s);
+void launch_argmax_rows_final(const int32_t* part, int32_t world, int32_t B, int32_t chunks, uint32_t* tokens,
+                              cudaStream_t s);
 void launch_softcap(int32_t* x, int32_t n, int32_t cap, cudaStream_t s);
 
 // ---- misc ---------------------------------------------------------------------------

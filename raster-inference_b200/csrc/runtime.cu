@@ -479,6 +479,16 @@ struct TpState {
   std::vector<void*> ipc_opened;
   uint32_t seq = 0;            // reductions issued so far
   const int64_t* last = nullptr;  // the buffer holding the last reduction's local sums
+  // Vocab-sharded selection (rdet_tp_shard_logits): a batched decode ends
+  // with each row's first max over this rank's vocab rows as (value, global
+  // index) pairs, all-gathered [world][rows][chunks][2] and reduced to the
+  // tokens; the full logit rows are never assembled.
+  bool shard_logits = false;
+  int sel_rows = 0, sel_chunks = 0;
+  int32_t* lpairs = nullptr;   // [sel_rows][chunks][2] this rank's pairs
+  int32_t* gpairs = nullptr;   // [world][sel_rows][chunks][2]
+  uint32_t* tokens = nullptr;  // [sel_rows] the selected tokens of the last batch
+  uint64_t epoch = 0;          // sharded batched decodes so far
 };
 
 struct Seq;
@@ -532,6 +542,11 @@ struct Ctx {
   DecodeWs dw;
   int32_t* d_err = nullptr;
   int argblocks = 0;
+  // rdet_select_batch: row pointer table, chunk pairs and tokens for up to sel_rows rows
+  int sel_rows = 0;
+  int32_t** sel_tab = nullptr;
+  int32_t* sel_part = nullptr;
+  uint32_t* sel_tok = nullptr;
   Seq* prefill_owner = nullptr;  // sequence whose routine-granular prefill is in flight
   Seq* decode_owner = nullptr;
   std::vector<void*> live_seqs;  // rdet_seq handles still open on this context
@@ -607,6 +622,12 @@ struct Seq {
   int pos = 0;                   // tokens in the cache (position of the next token)
   bool prefilled = false;
   int32_t* logits = nullptr;     // [V]
+  // the last batched decode left this sequence's logits vocab-sharded over
+  // the tensor-parallel ranks: only its selected token is known, in row
+  // sel_row of that decode's tokens (valid while sel_epoch is current)
+  bool logits_sharded = false;
+  int sel_row = -1;
+  uint64_t sel_epoch = 0;
   uint32_t* d_token = nullptr;
   uint32_t* d_hist = nullptr;    // generated tokens (graph path)
   int32_t* d_step = nullptr;
@@ -1296,6 +1317,7 @@ static void prefill_finalize(Ctx& c, Seq& q) {
   q.pos = S;
   q.last_S = S;
   q.prefilled = true;
+  q.logits_sharded = false;
   q.last_was_prefill = true;
   q.prefill_next = -1;
   c.prefill_owner = nullptr;
@@ -1498,6 +1520,14 @@ static void decode_step_launch(Ctx& c, Seq& q) {
 
 static void select_launch(Ctx& c, Seq& q) {
   launch_argmax(q.logits, c.cfg.V, c.dw.argpart, c.argblocks, q.d_token, c.stream);
+}
+
+// The sequence's full logit row exists on this device.
+static void require_logits(const Seq& q) {
+  REQUIRE(q.prefilled, RDET_E_STATE, "no logits available (run prefill first)");
+  REQUIRE(!q.logits_sharded, RDET_E_STATE,
+          "the logits of this sequence are vocab-sharded over the tensor-parallel ranks "
+          "(rdet_tp_shard_logits): select its token with rdet_select_batch");
 }
 
 static void check_decode_ready(Ctx& c, Seq& q) {
@@ -2122,7 +2152,7 @@ static void tp_init(Ctx& c, int rank, int world, const ncclUniqueId& id) {
   NCK(nccl_api().commInitRank(&t.comm, world, id, rank));
 }
 
-static void decode_batch_tp(Ctx& c, Seq* const* seqs, const uint32_t* tokens, int B) {
+static void decode_batch_tp(Ctx& c, Seq* const* seqs, const uint32_t* tokens, int B, int row0) {
   const ModelCfg& m = c.cfg;
   PrefillWs& w = c.pw;
   cudaStream_t s = c.stream;
@@ -2154,14 +2184,42 @@ static void decode_batch_tp(Ctx& c, Seq* const* seqs, const uint32_t* tokens, in
   ol.y = c.tp.lgl;
   tp_linear(c, w.nrm, B, m.H, c.tp.lm, ol, carry.ready ? &carry : nullptr);
   if (m.has_softcap) launch_softcap(c.tp.lgl, B * c.tp.Vl, c.softcap, s);
-  NCK(nccl_api().allGather(c.tp.lgl, c.tp.lga, (size_t)B * c.tp.Vl, ncclInt32, c.tp.comm, s));
-  launch_gather_vocab(c.tp.lga, c.tp.world, B, c.tp.Vl, bw.logits_dst, s);
+  TpState& t = c.tp;
+  if (t.shard_logits) {
+    // global argmax over the vocab-sharded logits: each rank's first max per
+    // chunk of its rows as (value, global index), all-gathered (8 bytes per
+    // chunk and row), then reduced per row; the logit rows stay sharded
+    const int chunks = t.sel_chunks;
+    launch_argmax_rows(nullptr, t.lgl, B, t.Vl, (size_t)t.Vl, t.rank * t.Vl, chunks, t.lpairs, s);
+    NCK(nccl_api().allGather(t.lpairs, t.gpairs, (size_t)B * chunks * 2, ncclInt32, t.comm, s));
+    launch_argmax_rows_final(t.gpairs, t.world, B, chunks, t.tokens + row0, s);
+  } else {
+    NCK(nccl_api().allGather(t.lgl, t.lga, (size_t)B * t.Vl, ncclInt32, t.comm, s));
+    launch_gather_vocab(t.lga, t.world, B, t.Vl, bw.logits_dst, s);
+  }
   launch_add_i32_rows(bw.pos, B, 1, s);
   CK(cudaGetLastError());
   for (int i = 0; i < B; ++i) {
     seqs[i]->pos += 1;
     seqs[i]->last_was_prefill = false;
+    seqs[i]->logits_sharded = t.shard_logits;
+    seqs[i]->sel_row = row0 + i;
+    seqs[i]->sel_epoch = t.epoch;
   }
+}
+
+// Capacity of the vocab-sharded selection buffers for a decode of nseq rows.
+static void tp_select_buffers(Ctx& c, int nseq) {
+  TpState& t = c.tp;
+  const int B = std::min<int>(nseq, (int)c.max_prefill);
+  const int chunks = std::max(1, std::min(32, std::min(256 / std::max(1, B), t.Vl / 256)));
+  if (t.sel_rows >= nseq && t.sel_chunks >= chunks) return;
+  const int rows = std::max(nseq, 8);
+  t.sel_chunks = std::max(chunks, t.sel_chunks);
+  t.lpairs = c.dalloc_n<int32_t>((size_t)rows * t.sel_chunks * 2);
+  t.gpairs = c.dalloc_n<int32_t>((size_t)t.world * rows * t.sel_chunks * 2);
+  t.tokens = c.dalloc_n<uint32_t>((size_t)rows);
+  t.sel_rows = rows;
 }
 
 // Whether the batched path can run these sequences (distinct, and the
@@ -2584,11 +2642,70 @@ int32_t rdet_select(rdet_ctx* ctx, rdet_seq* seq, uint32_t* token_out) {
     Ctx& c = *ctx->c;
     Seq& q = *seq->s;
     CK(cudaSetDevice(c.device));
-    REQUIRE(q.prefilled, RDET_E_STATE, "select requires logits (run prefill first)");
+    require_logits(q);
     select_launch(c, q);
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(token_out, q.d_token, 4, cudaMemcpyDeviceToHost, c.stream));
     CK(cudaStreamSynchronize(c.stream));
+  });
+}
+
+int32_t rdet_select_batch(rdet_ctx* ctx, rdet_seq* const* seqs, size_t n, uint32_t* tokens_out) {
+  return guard([&] {
+    REQUIRE(ctx && (n == 0 || (seqs && tokens_out)), RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    CK(cudaSetDevice(c.device));
+    REQUIRE(n <= (1u << 20), RDET_E_RANGE, "at most 2^20 sequences per call");
+    std::vector<int> full;           // positions whose logit rows are on this device
+    std::vector<int> sharded;        // positions selected by the last vocab-sharded decode
+    for (size_t i = 0; i < n; ++i) {
+      REQUIRE(seqs[i] && seqs[i]->owner == ctx, RDET_E_INVALID, "sequence belongs to another context");
+      const Seq& q = *seqs[i]->s;
+      REQUIRE(q.prefilled, RDET_E_STATE, "no logits available (run prefill first)");
+      if (q.logits_sharded) {
+        REQUIRE(q.sel_epoch == c.tp.epoch && q.sel_row >= 0 && q.sel_row < c.tp.sel_rows, RDET_E_STATE,
+                "a later batched decode replaced this sequence's selected token: select before the next decode");
+        sharded.push_back((int)i);
+      } else {
+        full.push_back((int)i);
+      }
+    }
+    cudaStream_t s = c.stream;
+    const int nf = (int)full.size();
+    const int chunks = std::max(1, std::min(32, 256 / std::max(1, nf)));
+    if (nf > 0) {
+      if (c.sel_rows < nf) {
+        const int rows = std::max(nf, 64);
+        c.sel_tab = reinterpret_cast<int32_t**>(c.dalloc((size_t)rows * 8));
+        c.sel_part = c.dalloc_n<int32_t>((size_t)rows * 32 * 2);
+        c.sel_tok = c.dalloc_n<uint32_t>((size_t)rows);
+        c.sel_rows = rows;
+      }
+      std::vector<int32_t*> tab(nf);
+      for (int j = 0; j < nf; ++j) tab[j] = seqs[full[j]]->s->logits;
+      CK(cudaMemcpyAsync(c.sel_tab, tab.data(), (size_t)nf * 8, cudaMemcpyHostToDevice, s));
+      launch_argmax_rows(c.sel_tab, nullptr, nf, c.cfg.V, 0, 0, chunks, c.sel_part, s);
+      launch_argmax_rows_final(c.sel_part, 1, nf, chunks, c.sel_tok, s);
+      CK(cudaGetLastError());
+    }
+    std::vector<uint32_t> ftok(nf), stok;
+    if (nf > 0) CK(cudaMemcpyAsync(ftok.data(), c.sel_tok, (size_t)nf * 4, cudaMemcpyDeviceToHost, s));
+    if (!sharded.empty()) {
+      stok.resize(c.tp.sel_rows);
+      CK(cudaMemcpyAsync(stok.data(), c.tp.tokens, stok.size() * 4, cudaMemcpyDeviceToHost, s));
+    }
+    CK(cudaStreamSynchronize(s));
+    for (int j = 0; j < nf; ++j) tokens_out[full[j]] = ftok[j];
+    for (int i : sharded) tokens_out[i] = stok[seqs[i]->s->sel_row];
+  });
+}
+
+int32_t rdet_tp_shard_logits(rdet_ctx* ctx, int32_t on) {
+  return guard([&] {
+    REQUIRE(ctx, RDET_E_INVALID, "null argument");
+    Ctx& c = *ctx->c;
+    REQUIRE(c.tp.comm != nullptr, RDET_E_STATE, "rdet_tp_shard_logits needs rdet_tp_init first");
+    c.tp.shard_logits = on != 0;
   });
 }
 
@@ -2640,6 +2757,7 @@ int32_t rdet_decode_finalize(rdet_ctx* ctx, rdet_seq* seq) {
     CK(cudaGetLastError());
     CK(cudaStreamSynchronize(c.stream));
     check_err_flag(c, "decode");
+    q.logits_sharded = false;
     q.pos += 1;
     q.last_was_prefill = false;
     q.decode_next = -1;
@@ -2659,13 +2777,20 @@ int32_t rdet_decode(rdet_ctx* ctx, rdet_seq* const* seqs, const uint32_t* tokens
       check_token(c, tokens[i]);
     }
     std::vector<Seq*> batch(nseq);
-    for (size_t i = 0; i < nseq; ++i) batch[i] = seqs[i]->s.get();
+    for (size_t i = 0; i < nseq; ++i) {
+      batch[i] = seqs[i]->s.get();
+      batch[i]->logits_sharded = false;  // every path below but the sharded one writes the logits
+    }
     if (batch_supported(c, batch.data(), (int)nseq)) {
+      if (c.tp.comm && c.tp.shard_logits) {
+        tp_select_buffers(c, (int)nseq);
+        c.tp.epoch += 1;
+      }
       // chunks of at most max_prefill rows (the row workspaces' size)
       for (size_t i0 = 0; i0 < nseq; i0 += c.max_prefill) {
         const int B = (int)std::min<size_t>(c.max_prefill, nseq - i0);
         if (B >= 2) {
-          if (c.tp.comm) decode_batch_tp(c, batch.data() + i0, tokens + i0, B);
+          if (c.tp.comm) decode_batch_tp(c, batch.data() + i0, tokens + i0, B, (int)i0);
           else decode_batch(c, batch.data() + i0, tokens + i0, B);
           continue;
         }
@@ -2700,6 +2825,7 @@ int32_t rdet_generate(rdet_ctx* ctx, rdet_seq* seq, uint32_t n_tokens, uint32_t*
     check_decode_ready(c, q);
     REQUIRE(c.decode_owner == nullptr, RDET_E_STATE, "a routine-granular decode is in flight on this context");
     REQUIRE(q.pos + (int)n_tokens <= q.cap, RDET_E_RANGE, "generation would overflow the sequence KV cache");
+    require_logits(q);
     ensure_decode_graph(c, q);
     if (q.hist_cap < (int)n_tokens) {
       q.d_hist = static_cast<uint32_t*>(q.dalloc((size_t)std::max<uint32_t>(n_tokens, 1) * 4));
@@ -2757,7 +2883,7 @@ int32_t rdet_read(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t layer, in
         }
         break;
       case RDET_BUF_LOGITS:
-        REQUIRE(q.prefilled, RDET_E_STATE, "no logits available");
+        require_logits(q);
         v = d2h(c, q.logits, c.cfg.V);
         break;
       case RDET_BUF_LAYER_OUTPUT:
@@ -2808,7 +2934,7 @@ int32_t rdet_commitment(rdet_ctx* ctx, rdet_seq* seq, int32_t which, int32_t lay
         break;
       }
       case RDET_BUF_LOGITS: {
-        REQUIRE(q.prefilled, RDET_E_STATE, "no logits available");
+        require_logits(q);
         auto v = d2h(c, q.logits, c.cfg.V);
         Sha256 h;
         h.put("raster-det-num-act-vector-v1", 28);

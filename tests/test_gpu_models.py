@@ -192,8 +192,8 @@ def check_batched_equals_solo(cfg, width, lens, steps, seed):
         solo[i].prefill(ids)
     L = m.L
     for step in range(steps):
-        toks = [s.select() for s in batch]
-        assert toks == [s.select() for s in solo], step
+        toks = rdet.select_batch(m, batch)  # one launch over every row
+        assert toks == [s.select() for s in solo] == [s.select() for s in batch], step
         rdet.decode_batch(m, batch, toks)
         for s, t in zip(solo, toks):
             s.decode(t)

@@ -23,16 +23,20 @@ def tp_config():
                        layer_types=["sliding_attention", "full_attention", "sliding_attention", "sliding_attention"])
 
 
-def run_pair(d, lens, steps, rank, world, uid, device=0, exchange=None):
+def run_pair(d, lens, steps, rank, world, uid, device=0, exchange=None, shard_logits=False):
     """Decodes the same ragged batch on a sharded and an unsharded context of
     one device and compares them step by step.  exchange: a function that
     takes this rank's NVLink-reduction blob and returns all ranks' blobs in
-    rank order (the sharded context then reduces over NVLink, not NCCL)."""
+    rank order (the sharded context then reduces over NVLink, not NCCL).
+    shard_logits: the sharded context selects by the global argmax over the
+    ranks' (value, index) pairs and never assembles the logit rows."""
     sharded = rdet.Model.open(d, device=device, max_prefill=max(max(lens), len(lens)))
     plain = rdet.Model.open(d, device=device, max_prefill=max(max(lens), len(lens)))
     sharded.tp_init(rank, world, uid)
     if exchange is not None:
         sharded.tp_ipc_connect(exchange(sharded.tp_ipc_export(len(lens)), "blob"))
+    if shard_logits:
+        sharded.tp_shard_logits(True)
     assert sharded.tp_world == world and plain.tp_world == 1
     a = [sharded.new_sequence(n + steps + 4) for n in lens]
     b = [plain.new_sequence(n + steps + 4) for n in lens]
@@ -42,13 +46,18 @@ def run_pair(d, lens, steps, rank, world, uid, device=0, exchange=None):
         b[i].prefill(ids)
     for step in range(steps):
         toks = [s.select() for s in b]
-        assert toks == [s.select() for s in a], step
+        assert toks == rdet.select_batch(sharded, a), step
         rdet.decode_batch(sharded, a, toks)
         rdet.decode_batch(plain, b, toks)
         for i, (x, y) in enumerate(zip(a, b)):
-            assert np.array_equal(x.read(rdet.BUF_LOGITS), y.read(rdet.BUF_LOGITS)), (step, i)
+            if shard_logits:
+                with pytest.raises(rdet.RdetError, match="vocab-sharded"):
+                    x.read(rdet.BUF_LOGITS)
+            else:
+                assert np.array_equal(x.read(rdet.BUF_LOGITS), y.read(rdet.BUF_LOGITS)), (step, i)
             assert x.commitment(rdet.BUF_HIDDEN) == y.commitment(rdet.BUF_HIDDEN), (step, i)
             assert x.commitment(rdet.BUF_KV) == y.commitment(rdet.BUF_KV), (step, i)
+    assert rdet.select_batch(sharded, a) == [s.select() for s in b]
     if exchange is not None:
         # no rank frees its reduction buffers while another may still read them
         torch.cuda.synchronize(device)
@@ -69,6 +78,12 @@ def test_tp_world1_nvlink_reduction_matches_unsharded():
     run_pair(d, LENS, 3, 0, 1, rdet.nccl_unique_id(), exchange=lambda blob, tag: [blob])
 
 
+def test_tp_world1_sharded_logits_select_matches_unsharded():
+    # the global argmax over (value, index) pairs of the vocab rows
+    d = write_model(tp_config(), seed=65)
+    run_pair(d, LENS, 3, 0, 1, rdet.nccl_unique_id(), shard_logits=True)
+
+
 def test_tp_ipc_export_needs_tp_init():
     d = write_model(tp_config(), seed=64)
     m = rdet.Model.open(d, max_prefill=8)
@@ -83,7 +98,8 @@ root = sys.argv[1]
 sys.path[:0] = [os.path.join(root, "tests"), os.path.join(root, "tests", "golden"), os.path.join(root, "oracle"), root]
 import test_gpu_tp as T
 rank, world, uid, d = int(sys.argv[2]), int(sys.argv[3]), bytes.fromhex(sys.argv[4]), sys.argv[5]
-xdir = sys.argv[6] if len(sys.argv) > 6 else None
+xdir = sys.argv[6] if len(sys.argv) > 6 and sys.argv[6] != "-" else None
+shard = len(sys.argv) > 7 and sys.argv[7] == "shard"
 
 def exchange(blob, tag):
     # blobs through files in a shared folder; bounded wait for the other ranks
@@ -97,19 +113,19 @@ def exchange(blob, tag):
         time.sleep(0.05)
     raise RuntimeError("the other ranks' " + tag + " files did not arrive")
 
-T.run_pair(d, T.LENS, 3, rank, world, uid, device=rank, exchange=exchange if xdir else None)
+T.run_pair(d, T.LENS, 3, rank, world, uid, device=rank, exchange=exchange if xdir else None, shard_logits=shard)
 print("TP-OK", rank)
 """
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("nvlink", [False, True])
-def test_tp_two_gpus_match_unsharded(nvlink, tmp_path):
+@pytest.mark.parametrize("nvlink,shard", [(False, False), (True, False), (True, True)])
+def test_tp_two_gpus_match_unsharded(nvlink, shard, tmp_path):
     d = write_model(tp_config(), seed=62)
     uid = rdet.nccl_unique_id().hex()
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    extra = [str(tmp_path)] if nvlink else []
+    extra = [str(tmp_path) if nvlink else "-", "shard" if shard else "plain"]
     procs = [subprocess.Popen(["timeout", "-k", "10", "300", sys.executable, "-c", CHILD, root, str(r), "2", uid, d]
                               + extra, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True, env=env)
              for r in range(2)]

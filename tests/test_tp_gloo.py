@@ -8,7 +8,10 @@ K range; one all-reduce (int64 sum) completes it and requantize gives the
 replicated row; vocab rows are all-gathered before argmax_first.  This test
 replays that plan for one attention-output projection, one GELU MLP and the
 logits, each rank in its own process over gloo, and checks every result bit
-for bit against the unsharded computation of the oracle.  It also checks the
+for bit against the unsharded computation of the oracle.  It also replays the
+vocab-sharded selection (rdet_tp_shard_logits): each rank's first max per row
+as a (value, global index) pair, the pairs all-gathered and reduced, equal to
+argmax_first over the whole row, ties across the shards included, and the
 max-over-ranks step time that bench.py reports for N > 1."""
 import datetime
 import os
@@ -97,6 +100,21 @@ def _rank(rank, world, port):
         assert np.array_equal(logits, full)
         for s in range(S):
             assert O.argmax_first(list(logits[s])) == O.argmax_first(list(full[s]))
+        # vocab-sharded selection: pairs instead of rows, lowest index on ties
+        rows = np.array(full, dtype=np.int64)
+        top = int(rows.max()) + 1
+        rows[0, [3, vl + 5]] = top            # tie across the shard boundary: rank 0's index wins
+        rows[1, [vl + 7, vl + 2]] = top       # tie inside the last shard
+        rows[2, :] = -7                       # every value tied: index 0
+        rows = rows.astype(np.int32)
+        mine = rows[:, rank * vl:(rank + 1) * vl]
+        pairs = torch.tensor([[int(r.max()), rank * vl + int(np.argmax(r))] for r in mine], dtype=torch.int64)
+        got = [torch.empty_like(pairs) for _ in range(world)]
+        dist.all_gather(got, pairs)
+        for s in range(S):
+            cand = sorted((-int(g[s, 0]), int(g[s, 1])) for g in got)
+            assert cand[0][1] == O.argmax_first(list(rows[s]))
+        assert O.argmax_first(list(rows[0])) == 3 and O.argmax_first(list(rows[2])) == 0
         # bench.py's N > 1 timing: every rank takes the maximum of the ranks' times
         t = torch.tensor([1.5 + rank, 0.25 * (world - rank)], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
