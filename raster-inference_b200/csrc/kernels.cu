@@ -563,7 +563,7 @@ int stream_error_flag(bool reset) {
     int z = 0;
     cudaMemcpyToSymbol(g_stream_err, &z, sizeof(int));
   }
-  return v | tc_error_flag(reset) | tc_attn_error_flag(reset);
+  return v | tc_error_flag(reset) | tc_attn_error_flag(reset) | tc_attn_dec_error_flag(reset);
 }
 
 // Plans and launches the streamed GEMV; returns false when the launch does not
@@ -2056,6 +2056,7 @@ void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s) {
   const int Gq = a.group ? a.group : a.Hq / a.Hkv;
   const bool wide4 = a.batch > 1 && a.d > 256 && Gq % 4 == 0 && CL >= 8 &&
                      ac_smem(4, a.d, ac_rmax(a.window, a.cap, 8)) <= kAcMaxSmem && a.d <= kAcVmx * 8;
+  if (a.batch > 1 && launch_attn_decode_tc(a, sm_count(), s)) return;
   if (a.batch > 1) {
     // a CTA finalises d / CL output dims (at most kAcVmx: the first-max V
     // row is staged in a [GC][kAcVmx] shared array).  One CTA per

@@ -281,12 +281,26 @@ struct AttnDecodeArgs {
   // batched: the rows in launch order (longest context first, so that the
   // longest rows' clusters start in the first wave); null = row order
   const int32_t* row_order = nullptr;
+  // batched, tensor-core attention: each row's tensor maps of its caches
+  // ([layer][K, V], 128 bytes each; td_encode_cache_map) and the layer whose
+  // caches this launch reads; null: the CUDA-core kernel runs
+  const unsigned char* const* map_rows = nullptr;
+  int32_t map_layer = 0;
 };
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s);
 // Same computation in one kernel: one thread-block cluster per query head
 // splits the window across its CTAs and combines the exact softmax statistics
 // through distributed shared memory (no global scratch).
 void launch_attn_decode_cluster(const AttnDecodeArgs& a, cudaStream_t s);
+// Batched decode attention on the tensor cores (tc_attn_dec.cu): false when
+// the shape does not qualify (then the cluster kernel runs).
+bool launch_attn_decode_tc(const AttnDecodeArgs& a, int sms, cudaStream_t s);
+// The tensor map (128 bytes at out, 64-byte aligned) of one KV cache
+// [rows][d] i32 that launch_attn_decode_tc reads: 32 x 64 boxes, 128-byte
+// swizzle.  False when d is not a multiple of 128 or encoding fails.
+bool td_encode_cache_map(void* out, const int32_t* base, int rows, int d);
+int tc_attn_dec_error_flag(bool reset);
+void tc_attn_dec_init();
 // Whether launch_attn_decode_cluster runs the cluster kernel for this shape
 // (rotary: the fused prologue's rotary width, 0 when not fused).  When it
 // does not, it falls back to launch_attn_decode, which needs a.sc and does

@@ -575,6 +575,8 @@ struct Ctx {
     int32_t** vc = nullptr;
     int32_t** dec_out = nullptr;   // [rows] each sequence's per-layer outputs
     int32_t** logits_dst = nullptr;
+    const unsigned char** maps = nullptr;  // [rows] each sequence's cache tensor maps (Seq::d_maps)
+    bool maps_ok = false;          // every row of the current batch has them
     int32_t* logits = nullptr;     // [rows, V]
   } bw;
   TpState tp;
@@ -628,6 +630,11 @@ struct Seq {
   bool logits_sharded = false;
   int sel_row = -1;
   uint64_t sel_epoch = 0;
+  // tensor maps of the caches for the batched tensor-core attention:
+  // [layer][K, V], 128 bytes each (zero for layers without own caches or
+  // with head dims it does not take); maps_ok: every eligible one encoded
+  unsigned char* d_maps = nullptr;
+  bool maps_ok = false;
   uint32_t* d_token = nullptr;
   uint32_t* d_hist = nullptr;    // generated tokens (graph path)
   int32_t* d_step = nullptr;
@@ -1550,6 +1557,20 @@ static void seq_alloc(Ctx& c, Seq& q, int cap) {
     q.kc[l] = static_cast<int32_t*>(q.dalloc(n * 4));
     q.vc[l] = static_cast<int32_t*>(q.dalloc(n * 4));
   }
+  {
+    std::vector<unsigned char> maps((size_t)m.L * 256, 0);
+    bool ok = true;
+    for (int l = 0; l < m.L; ++l) {
+      const LayerCfg& lc = m.layers[l];
+      if (lc.donor >= 0 || lc.head_dim % 128 != 0) continue;
+      const int rows = lc.kv_heads * cap;
+      ok = ok && td_encode_cache_map(maps.data() + (size_t)l * 256, q.kc[l], rows, lc.head_dim) &&
+           td_encode_cache_map(maps.data() + (size_t)l * 256 + 128, q.vc[l], rows, lc.head_dim);
+    }
+    q.d_maps = static_cast<unsigned char*>(q.dalloc(maps.size()));
+    CK(cudaMemcpy(q.d_maps, maps.data(), maps.size(), cudaMemcpyHostToDevice));
+    q.maps_ok = ok;
+  }
   q.d_pos = static_cast<int32_t*>(q.dalloc(16));
   CK(cudaMemset(q.d_pos, 0, 16));
   q.logits = static_cast<int32_t*>(q.dalloc((size_t)m.V * 4));
@@ -1750,7 +1771,7 @@ static void batch_tables(Ctx& c, Seq* const* seqs, int B) {
   auto& bw = c.bw;
   if (bw.rows < B) {
     const int rows = std::max(B, 8);
-    const size_t ptrs = (size_t)rows * (3 + 2 * (size_t)m.L);
+    const size_t ptrs = (size_t)rows * (4 + 2 * (size_t)m.L);
     const size_t bytes = ptrs * 8 + (size_t)rows * 12 + (size_t)rows * m.V * 4 + 256;
     bw.mem = c.dalloc(bytes);
     auto* base = static_cast<unsigned char*>(bw.mem);
@@ -1759,14 +1780,16 @@ static void batch_tables(Ctx& c, Seq* const* seqs, int B) {
     bw.logits_dst = bw.dec_out + rows;
     bw.kc = bw.logits_dst + rows;
     bw.vc = bw.kc + (size_t)m.L * rows;
-    bw.ids = reinterpret_cast<uint32_t*>(bw.vc + (size_t)m.L * rows);
+    bw.maps = reinterpret_cast<const unsigned char**>(reinterpret_cast<uintptr_t>(bw.vc + (size_t)m.L * rows));
+    bw.ids = reinterpret_cast<uint32_t*>(reinterpret_cast<uintptr_t>(bw.maps + rows));
     bw.caps = reinterpret_cast<int32_t*>(bw.ids + rows);
     bw.order = bw.caps + rows;
     bw.logits = reinterpret_cast<int32_t*>((reinterpret_cast<uintptr_t>(bw.order + rows) + 255) & ~(uintptr_t)255);
     bw.rows = rows;
   }
   const int rows = bw.rows;
-  std::vector<int32_t*> host((size_t)rows * (3 + 2 * (size_t)m.L), nullptr);
+  std::vector<int32_t*> host((size_t)rows * (4 + 2 * (size_t)m.L), nullptr);
+  bw.maps_ok = true;
   std::vector<int32_t> caps(2 * (size_t)rows, 0);  // [caps | row order]
   for (int b = 0; b < B; ++b) {
     Seq& q = *seqs[b];
@@ -1778,6 +1801,8 @@ static void batch_tables(Ctx& c, Seq* const* seqs, int B) {
       host[(3 + (size_t)l) * rows + b] = q.kc[own];
       host[(3 + (size_t)m.L + l) * rows + b] = q.vc[own];
     }
+    host[(3 + 2 * (size_t)m.L) * rows + b] = reinterpret_cast<int32_t*>(q.d_maps);  // bw.maps[b]
+    bw.maps_ok = bw.maps_ok && q.maps_ok;
     caps[b] = q.cap;
   }
   // attention launch order: longest context first (ties by row)
@@ -1850,6 +1875,8 @@ static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32
   aa.kc_rows = bw.kc + (size_t)l * bw.rows;
   aa.vc_rows = bw.vc + (size_t)l * bw.rows;
   aa.row_order = bw.order;
+  aa.map_rows = bw.maps_ok ? bw.maps : nullptr;
+  aa.map_layer = lc.donor < 0 ? l : lc.donor;
   launch_attn_decode_cluster(aa, s);
   prefill_linear(c, w.comb, B, L.o, L.to, w.attn, kEpiPlain, nullptr);
   const bool ple = m.P > 0;
@@ -2025,6 +2052,8 @@ static const int32_t* decode_batch_layer_tp(Ctx& c, int B, int maxcap, int l, in
   aa.kc_rows = bw.kc + (size_t)l * bw.rows;
   aa.vc_rows = bw.vc + (size_t)l * bw.rows;
   aa.row_order = bw.order;
+  aa.map_rows = bw.maps_ok ? bw.maps : nullptr;
+  aa.map_layer = lc.donor < 0 ? l : lc.donor;
   launch_attn_decode_cluster(aa, s);
   tp_linear_sum(c, w.comb, B, Hql * d, T.o);
   const bool ple = m.P > 0;

@@ -109,7 +109,13 @@ def test_config5_ragged_batch_of_64(model, fx, cfg):
     for key, r in rec["sequences"].items():
         i = int(key)
         assert lens[i] == r["length"] and SEED + 100 + i == r["ids_seed"]
-        assert out[i] == r["tokens"], f"sequence {i}"
+        if out[i] != r["tokens"]:  # what went wrong, for the failure message
+            lg = seqs[i].read(rdet.BUF_LOGITS)
+            first0 = sum(1 for o in out if o and o[0] == 0)
+            bad = next(k for k, (a, b) in enumerate(zip(out[i], r["tokens"])) if a != b)
+            raise AssertionError(f"sequence {i}: first mismatch at token {bad}; final logits min {lg.min()} "
+                                 f"max {lg.max()} distinct {len(np.unique(lg))}; {first0} of {B} sequences "
+                                 f"selected token 0 after prefill")
         assert seqs[i].commitment(rdet.BUF_LOGITS) == r["final_logits"], f"sequence {i}"
         assert seqs[i].commitment(rdet.BUF_KV, own_cache_layers(cfg)) == r["final_kv_own_layers"], f"sequence {i}"
     for s in seqs:
