@@ -5,21 +5,21 @@
 //
 // One thread-block cluster per (sequence, group of GC query heads sharing a
 // KV head); CTA r of the cluster takes keys [n r / CL, n (r+1) / CL) of the
-// sequence's window.  The KV cache keeps its i32 row layout: each CTA copies
-// raw cache tiles into a shared-memory ring (16-byte asynchronous copies by
-// every thread) and converts them there into unsigned byte-limb planes (the
-// 64-byte swizzle layout the MMA descriptors read), so nothing else in the
-// library changes.
+// sequence's window.  The KV cache keeps its i32 row layout: tiled TMA
+// loads (a 2D tensor map per sequence and cache, 128-byte swizzle) bring raw
+// cache tiles into a shared-memory ring, and the CTA converts them there into
+// unsigned byte-limb planes (the 64-byte swizzle layout the MMA descriptors
+// read), so nothing else in the library changes.
 //
 // Scores.  With k_u = k + 2^31 and q_u = q + 2^31 (u32),
 //   sum k q = sum k_u q_u - 2^31 sum q_u - 2^31 sum k_u + 2^62 d  (wrapping i64)
 // and sum k_u q_u = sum_{a,b} 2^(8(a+b)) P_b[a], P_b[a] = sum_dim kbyte_b
-// qbyte_a.  The keys are the MMA's M = 128 rows (A = key limb plane b), the
-// B operand stacks the four query limbs of each of the GC heads (N = 16 rows,
-// row 4h + a), so one MMA per key limb writes P_b for all heads into 16 TMEM
-// columns: 64 columns per 128-key tile, double-buffered.  Each P is at most
-// 255^2 d: exact in the s32 accumulator for d <= 512.  The conversion thread
-// of a key row sums its k_u on the way.
+// qbyte_a.  The keys are the MMA's M = 128 rows (A = key limb plane b); the
+// B operand stacks the four query limbs of each of the GC heads (row 4h + a)
+// and one row of ones (row 16, N = 32), so one MMA per key limb writes P_b
+// for all heads and the key's limb-b byte sum, from which sum k_u follows:
+// 128 TMEM columns per 128-key tile, double-buffered.  Each entry is at most
+// 255^2 d: exact in the s32 accumulator for d <= 512.
 //
 // Softmax.  First max, exp terms, their sum, the ties-to-even division and
 // the residual on the CUDA cores, cluster-wide through distributed shared
@@ -32,13 +32,15 @@
 // 32 keys; per 128 dims 64 TMEM columns accumulate over the CTA's keys, each
 // entry at most 255^2 n for n keys: exact for n <= 33000.
 //
-// The pipeline is one ring of three raw tiles, two ahead of the tile being
-// converted (score tiles, then value tiles, so the first value tiles load
-// while the softmax runs), all threads converting a tile into one of two
-// plane buffers, and one thread issuing its MMAs; a plane buffer is
-// rewritten only after the MMAs that read it have committed.  Every mbarrier
-// wait is bounded: a wait that gives up sets the library's pipeline error
-// flag (the host raises an error).  No TMA or bulk copies are used.
+// Warp roles, coupled only by mbarriers: warp 8 issues the TMA loads into a
+// ring of three 32 KB slots (score tiles, then value tiles, so the first
+// value tiles load while the softmax runs), warps 0-7 convert each slot into
+// one of two plane buffers, warp 9 issues the MMAs of a plane buffer once all
+// converters have written it, and warps 10-13 drain the double-buffered score
+// accumulators as tiles complete.  The softmax and the cluster combine use
+// every warp.  Every mbarrier wait is bounded: a wait that gives up sets the
+// library's pipeline error flag (the host raises an error).  No load uses
+// cluster multicast.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -62,8 +64,13 @@ namespace {
 
 namespace cg = cooperative_groups;
 
-constexpr int kTdThreads = 256;
+// warps 0-7 convert raw tiles to limb planes, warp 8 issues the TMA loads,
+// warp 9 the MMAs, warps 10-13 drain the score accumulators; all of them
+// share the softmax and combine phases
+constexpr int kTdThreads = 448;
 constexpr int kTdWarps = kTdThreads / 32;
+constexpr int kTdConv = 256;  // converter threads
+constexpr int kTdProdWarp = 8, kTdMmaWarp = 9, kTdEpiWarp = 10;
 constexpr int kTdKeys = 128;                 // keys per score tile (MMA M)
 constexpr int kTdVKeys = 64;                 // keys per value tile
 constexpr int kTdBox = 64 * 128;             // one TMA box: 64 cache rows x 32 i32, 128-byte swizzle
@@ -170,7 +177,8 @@ __global__ void __launch_bounds__(kTdThreads, 1) attn_dec_tc_kernel(const TdArgs
   // planes_full[p]: every thread converted its part of plane buffer p;
   // mma_done[p]: the MMAs reading plane buffer p completed
   // full[s] / empty[s]: ring slot s loaded (TMA bytes) / converted by every thread
-  __shared__ __align__(8) uint64_t full[kTdSlots], empty[kTdSlots], planes_full[2], mma_done[2], acc_full[2], pv_full;
+  __shared__ __align__(8) uint64_t full[kTdSlots], empty[kTdSlots], planes_full[2], mma_done[2], acc_full[2],
+      acc_empty[2], pv_full;
   __shared__ uint32_t tmem_holder;
   __shared__ uint64_t qsum[4];
   __shared__ int32_t s_max[GC], s_idx[GC], g_max[GC], g_idx[GC], g_res[GC];
@@ -185,12 +193,13 @@ __global__ void __launch_bounds__(kTdThreads, 1) attn_dec_tc_kernel(const TdArgs
   if (tid == 0) {
     for (int i = 0; i < kTdSlots; ++i) {
       tcx::mbar_init(&full[i], 1);
-      tcx::mbar_init(&empty[i], kTdThreads);
+      tcx::mbar_init(&empty[i], kTdConv);
     }
     for (int i = 0; i < 2; ++i) {
-      tcx::mbar_init(&planes_full[i], kTdThreads);
+      tcx::mbar_init(&planes_full[i], kTdConv);
       tcx::mbar_init(&mma_done[i], 1);
       tcx::mbar_init(&acc_full[i], 1);
+      tcx::mbar_init(&acc_empty[i], 128);
     }
     tcx::mbar_init(&pv_full, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -217,19 +226,20 @@ __global__ void __launch_bounds__(kTdThreads, 1) attn_dec_tc_kernel(const TdArgs
   const int nq = ntile * ns;                                  // score stages
   const int nkb = (rows + kTdVKeys - 1) / kTdVKeys;
   const int total = nq + nkb * nd;                            // + value stages
-  const int crow = tid & 127, half = tid >> 7;  // a thread's row (key or dim) and half of the columns (dims or keys)
+  // a converter thread's row (key or dim) and half of the columns (dims or keys)
+  const int crow = tid & 127, half = (tid >> 7) & 1;
 
   auto wait = [&](uint64_t* bar, uint32_t parity) {
     if (!tcx::mbar_wait(bar, parity)) s_fail = 1;
   };
-  // Stage u -> slot u % kTdSlots by thread 0: four TMA boxes (score stage:
+  // Stage u -> slot u % kTdSlots by the producer: four TMA boxes (score stage:
   // keys [128 t, +128) x dims [64 s, +64); value stage: keys [64 kb, +64) x
   // dims [128 db, +128)), rows past the cache read as zero, rows past this
-  // CTA's keys are ignored.  Issued once every thread has converted the
-  // slot's previous stage.
+  // CTA's keys are ignored.  Issued once every converter thread has
+  // converted the slot's previous stage.
   const unsigned char* const maps = a.map_rows[brow] + (size_t)a.map_layer * 256;
   const int y0 = kvh * capr + start + lo;  // tensor row of this CTA's key 0
-  auto issue = [&](int u) {  // thread 0
+  auto issue = [&](int u) {  // producer lane
     const int sl = u % kTdSlots;
     if (u >= kTdSlots) wait(&empty[sl], ((u - kTdSlots) / kTdSlots) & 1);
     unsigned char* dst = ring + (size_t)sl * kTdSlot;
@@ -244,13 +254,6 @@ __global__ void __launch_bounds__(kTdThreads, 1) attn_dec_tc_kernel(const TdArgs
         td_tma2d(dst + b * kTdBox, maps + 128, db * 128 + b * 32, y0 + kb * kTdVKeys, &full[sl]);
     }
   };
-  if (tid == 0) {
-    // the maps were written through the generic proxy (a host copy, possibly
-    // into memory that held other maps before): acquire them for the TMA unit
-    asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(maps) : "memory");
-    asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(maps + 128) : "memory");
-    for (int u = 0; u < 2 && u < total; ++u) issue(u);
-  }
 
   // query planes: tile s (64 dims) = [32 rows][64 B]: row 4h + a = byte a of
   // q_u, row 16 = ones (its products are the key row sums), others zero
@@ -286,8 +289,8 @@ __global__ void __launch_bounds__(kTdThreads, 1) attn_dec_tc_kernel(const TdArgs
 #pragma unroll
   for (int h = 0; h < GC; ++h) { bm[h] = INT32_MIN; bi[h] = INT32_MAX; }
 
-  // epilogue of score tile t (TMEM columns 128 (t & 1) + 32 b + n): thread
-  // (lane row r, half) -> key t*128 + r, heads [half*GC/2, ...) (GC = 1: half 0)
+  // epilogue of score tile t (TMEM columns 128 (t & 1) + 32 b + n): epilogue
+  // thread of TMEM lane r -> key t*128 + r, every head
   auto score_epilogue = [&](int t) {
     wait(&acc_full[t & 1], (t >> 1) & 1);
     tcx::fence_after();
@@ -312,8 +315,7 @@ __global__ void __launch_bounds__(kTdThreads, 1) attn_dec_tc_kernel(const TdArgs
     const int j = t * kTdKeys + r;  // key index within this CTA
 #pragma unroll
     for (int h = 0; h < GC; ++h) {
-      const bool mine = GC == 1 ? half == 0 : ((h < GC / 2) == (half == 0));
-      if (mine && j < rows) {
+      if (j < rows) {
         const uint64_t x = acc[h] - (qsum[h] << 31) - (ksum << 31) + dcorr;
         const int32_t s = requantize((int64_t)x);
         sc[h * rmax + j] = s;
@@ -323,58 +325,73 @@ __global__ void __launch_bounds__(kTdThreads, 1) attn_dec_tc_kernel(const TdArgs
     tcx::fence_before();
   };
 
-  // ---- scores
-  for (int u = 0; u < nq; ++u) {
-    const int t = u / ns, s = u % ns, pb = u & 1;
-    if (tid == 0 && u + 2 < total) issue(u + 2);
-    wait(&full[u % kTdSlots], (u / kTdSlots) & 1);
-    if (u >= 2) wait(&mma_done[pb], ((u - 2) >> 1) & 1);
-    {
-      // key crow's dims 32*half .. +32: box (crow / 64, half), row crow % 64
-      const unsigned char* raw = ring + (size_t)(u % kTdSlots) * kTdSlot + ((crow >> 6) * 2 + half) * kTdBox;
-      const int br = crow & 63;
-      unsigned char* pl = planes + pb * kTdPlanes;
+  // ---- scores: the four roles run their own loops, coupled by mbarriers
+  if (tid < kTdConv) {
+    for (int u = 0; u < nq; ++u) {
+      const int pb = u & 1, s = u % ns;
+      wait(&full[u % kTdSlots], (u / kTdSlots) & 1);
+      if (u >= 2) wait(&mma_done[pb], ((u - 2) >> 1) & 1);
+      {
+        // key crow's dims 32*half .. +32: box (crow / 64, half), row crow % 64
+        const unsigned char* raw = ring + (size_t)(u % kTdSlots) * kTdSlot + ((crow >> 6) * 2 + half) * kTdBox;
+        const int br = crow & 63;
+        unsigned char* pl = planes + pb * kTdPlanes;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {  // 16-byte output chunk 2*half + c: dims 32*half + 16c ..
-        uint32_t o[4][4];
+        for (int c = 0; c < 2; ++c) {  // 16-byte output chunk 2*half + c: dims 32*half + 16c ..
+          uint32_t o[4][4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint4 w = *reinterpret_cast<const uint4*>(raw + sw128(br, 4 * c + k));
-          uint32_t q[4];
-          bytes_t4(w.x, w.y, w.z, w.w, q);
+          for (int k = 0; k < 4; ++k) {
+            const uint4 w = *reinterpret_cast<const uint4*>(raw + sw128(br, 4 * c + k));
+            uint32_t q[4];
+            bytes_t4(w.x, w.y, w.z, w.w, q);
 #pragma unroll
-          for (int b = 0; b < 4; ++b) o[b][k] = q[b];
+            for (int b = 0; b < 4; ++b) o[b][k] = q[b];
+          }
+#pragma unroll
+          for (int b = 0; b < 4; ++b)
+            *reinterpret_cast<uint4*>(pl + b * kTdPlane + sw64(crow, 2 * half + c)) =
+                make_uint4(o[b][0], o[b][1], o[b][2], o[b][3]);
         }
-#pragma unroll
-        for (int b = 0; b < 4; ++b)
-          *reinterpret_cast<uint4*>(pl + b * kTdPlane + sw64(crow, 2 * half + c)) =
-              make_uint4(o[b][0], o[b][1], o[b][2], o[b][3]);
       }
+      (void)s;
+      tcx::mbar_arrive(&empty[u % kTdSlots]);
+      td_fence_async();
+      tcx::mbar_arrive(&planes_full[pb]);
     }
-    tcx::mbar_arrive(&empty[u % kTdSlots]);
-    td_fence_async();
-    tcx::fence_before();
-    tcx::mbar_arrive(&planes_full[pb]);
-    if (tid == 32) {
-      wait(&planes_full[pb], (u >> 1) & 1);
-      tcx::fence_after();
-      const uint32_t pbase = td_su32(planes + pb * kTdPlanes), qbase = td_su32(qpl + s * 2048);
-      const uint32_t dcol = tmem + (uint32_t)(128 * (t & 1));
-#pragma unroll
-      for (int k = 0; k < 2; ++k)
-#pragma unroll
-        for (int b = 0; b < 4; ++b)
-          tcx::mma_i8(dcol + 32 * b, tcx::smem_desc_sw64(pbase + b * kTdPlane + 32 * k),
-                      tcx::smem_desc_sw64(qbase + 32 * k), kTdId32, (s > 0 || k > 0) ? 1u : 0u);
-      tcx::mma_commit(&mma_done[pb]);
-      if (s == ns - 1) tcx::mma_commit(&acc_full[t & 1]);
+  } else if (warp == kTdProdWarp) {
+    if (lane == 0) {
+      // the maps were written through the generic proxy (a host copy, possibly
+      // into memory that held other maps before): acquire them for the TMA unit
+      asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(maps) : "memory");
+      asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(maps + 128) : "memory");
+      // the score tiles and the first value tiles (these load during the
+      // softmax; every slot they reuse held a score tile)
+      for (int u = 0; u < total && u < nq + kTdSlots; ++u) issue(u);
     }
-    // the previous tile's scores once this tile's first stage is issued
-    // (the accumulator is double-buffered; tile t + 1 rewrites this one only
-    // after every thread converted its first stage, i.e. after this epilogue)
-    if (s == 0 && t > 0) score_epilogue(t - 1);
+  } else if (warp == kTdMmaWarp) {
+    if (lane == 0)
+      for (int u = 0; u < nq; ++u) {
+        const int t = u / ns, s = u % ns, pb = u & 1;
+        if (s == 0 && t >= 2) wait(&acc_empty[t & 1], ((t - 2) >> 1) & 1);  // tile t - 2 drained
+        wait(&planes_full[pb], (u >> 1) & 1);
+        tcx::fence_after();
+        const uint32_t pbase = td_su32(planes + pb * kTdPlanes), qbase = td_su32(qpl + s * 2048);
+        const uint32_t dcol = tmem + (uint32_t)(128 * (t & 1));
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+#pragma unroll
+          for (int b = 0; b < 4; ++b)
+            tcx::mma_i8(dcol + 32 * b, tcx::smem_desc_sw64(pbase + b * kTdPlane + 32 * k),
+                        tcx::smem_desc_sw64(qbase + 32 * k), kTdId32, (s > 0 || k > 0) ? 1u : 0u);
+        tcx::mma_commit(&mma_done[pb]);
+        if (s == ns - 1) tcx::mma_commit(&acc_full[t & 1]);
+      }
+  } else {
+    for (int t = 0; t < ntile; ++t) {
+      score_epilogue(t);
+      tcx::mbar_arrive(&acc_empty[t & 1]);
+    }
   }
-  if (ntile > 0) score_epilogue(ntile - 1);
   __syncthreads();
 
   // ---- first max: per head over this CTA, then over the cluster
@@ -499,63 +516,70 @@ __global__ void __launch_bounds__(kTdThreads, 1) attn_dec_tc_kernel(const TdArgs
   __syncthreads();
 
   // ---- weighted values: stage v = key block v / nd, dims 128 (v % nd)
-  for (int u = nq; u < total; ++u) {
-    const int v = u - nq, kb = v / nd, db = v % nd, pb = u & 1;
-    if (tid == 0 && u + 2 < total) issue(u + 2);
-    wait(&full[u % kTdSlots], (u / kTdSlots) & 1);
-    if (u >= 2) wait(&mma_done[pb], ((u - 2) >> 1) & 1);
-    {
-      // thread (dim crow, keys 32*half ..): dim crow of 32 key rows, in box
-      // crow / 32 at 16-byte chunk (crow % 32) / 4, word crow % 4
-      const unsigned char* raw = ring + (size_t)(u % kTdSlots) * kTdSlot + (crow >> 5) * kTdBox + (crow & 3) * 4;
-      const int ch = (crow & 31) >> 2;
-      unsigned char* pl = planes + pb * kTdPlanes;
-      auto val = [&](int j) { return *reinterpret_cast<const uint32_t*>(raw + sw128(j, ch)); };
+  if (tid < kTdConv) {
+    for (int u = nq; u < total; ++u) {
+      const int pb = u & 1;
+      wait(&full[u % kTdSlots], (u / kTdSlots) & 1);
+      if (u >= 2) wait(&mma_done[pb], ((u - 2) >> 1) & 1);
+      {
+        // thread (dim crow, keys 32*half ..): dim crow of 32 key rows, in box
+        // crow / 32 at 16-byte chunk (crow % 32) / 4, word crow % 4
+        const unsigned char* raw =
+            ring + (size_t)(u % kTdSlots) * kTdSlot + (crow >> 5) * kTdBox + (crow & 3) * 4;
+        const int ch = (crow & 31) >> 2;
+        unsigned char* pl = planes + pb * kTdPlanes;
+        auto val = [&](int j) { return *reinterpret_cast<const uint32_t*>(raw + sw128(j, ch)); };
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {  // chunk 2*half + c: keys 32*half + 16c ..
-        uint32_t o[4][4];
+        for (int c = 0; c < 2; ++c) {  // chunk 2*half + c: keys 32*half + 16c ..
+          uint32_t o[4][4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int j = 32 * half + 16 * c + 4 * k;
-          uint32_t q[4];
-          bytes_t4(val(j), val(j + 1), val(j + 2), val(j + 3), q);
+          for (int k = 0; k < 4; ++k) {
+            const int j = 32 * half + 16 * c + 4 * k;
+            uint32_t q[4];
+            bytes_t4(val(j), val(j + 1), val(j + 2), val(j + 3), q);
 #pragma unroll
-          for (int b = 0; b < 4; ++b) o[b][k] = q[b];
+            for (int b = 0; b < 4; ++b) o[b][k] = q[b];
+          }
+#pragma unroll
+          for (int b = 0; b < 4; ++b)
+            *reinterpret_cast<uint4*>(pl + b * kTdPlane + sw64(crow, 2 * half + c)) =
+                make_uint4(o[b][0], o[b][1], o[b][2], o[b][3]);
         }
-#pragma unroll
-        for (int b = 0; b < 4; ++b)
-          *reinterpret_cast<uint4*>(pl + b * kTdPlane + sw64(crow, 2 * half + c)) =
-              make_uint4(o[b][0], o[b][1], o[b][2], o[b][3]);
       }
+      tcx::mbar_arrive(&empty[u % kTdSlots]);
+      td_fence_async();
+      tcx::mbar_arrive(&planes_full[pb]);
     }
-    tcx::mbar_arrive(&empty[u % kTdSlots]);
-    td_fence_async();
-    tcx::fence_before();
-    tcx::mbar_arrive(&planes_full[pb]);
-    if (tid == 32) {
-      wait(&planes_full[pb], (u >> 1) & 1);
-      tcx::fence_after();
-      const uint32_t pbase = td_su32(planes + pb * kTdPlanes), wbase = td_su32(wpl + kb * 1024);
-      const uint32_t dcol = tmem + 256 + (uint32_t)(64 * db);
+  } else if (warp == kTdProdWarp) {
+    if (lane == 0)
+      for (int u = nq + kTdSlots; u < total; ++u) issue(u);
+  } else if (warp == kTdMmaWarp) {
+    if (lane == 0)
+      for (int u = nq; u < total; ++u) {
+        const int v = u - nq, kb = v / nd, db = v % nd, pb = u & 1;
+        wait(&planes_full[pb], (u >> 1) & 1);
+        tcx::fence_after();
+        const uint32_t pbase = td_su32(planes + pb * kTdPlanes), wbase = td_su32(wpl + kb * 1024);
+        const uint32_t dcol = tmem + 256 + (uint32_t)(64 * db);
 #pragma unroll
-      for (int k = 0; k < 2; ++k)
+        for (int k = 0; k < 2; ++k)
 #pragma unroll
-        for (int b = 0; b < 4; ++b)
-          tcx::mma_i8(dcol + 16 * b, tcx::smem_desc_sw64(pbase + b * kTdPlane + 32 * k),
-                      tcx::smem_desc_sw64(wbase + 32 * k), kTdId16, (kb > 0 || k > 0) ? 1u : 0u);
-      tcx::mma_commit(&mma_done[pb]);
-      if (u == total - 1) tcx::mma_commit(&pv_full);
-    }
+          for (int b = 0; b < 4; ++b)
+            tcx::mma_i8(dcol + 16 * b, tcx::smem_desc_sw64(pbase + b * kTdPlane + 32 * k),
+                        tcx::smem_desc_sw64(wbase + 32 * k), kTdId16, (kb > 0 || k > 0) ? 1u : 0u);
+        tcx::mma_commit(&mma_done[pb]);
+        if (u == total - 1) tcx::mma_commit(&pv_full);
+      }
   }
   // ---- partial weighted sums of this CTA: lane (dim within a 128-dim block)
   // (pacc overlays the ring: every stage was consumed, the residual row copied)
-  asm volatile("cp.async.wait_all;" ::: "memory");
-  __syncthreads();
-  if (total > nq) {
+  // (after the last value MMA every converter read and TMA copy is done, so
+  // pacc may overlay the ring)
+  if (total > nq && warp >= kTdEpiWarp) {
     wait(&pv_full, 0);
     tcx::fence_after();
     const int r = 32 * (warp & 3) + lane;
-    for (int db = warp >> 2; db < nd; db += 2) {
+    for (int db = 0; db < nd; ++db) {
       const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 256 + (uint32_t)(64 * db);
       uint64_t acc[GC];
 #pragma unroll
@@ -573,9 +597,10 @@ __global__ void __launch_bounds__(kTdThreads, 1) attn_dec_tc_kernel(const TdArgs
 #pragma unroll
       for (int h = 0; h < GC; ++h) pacc[h * d + 128 * db + r] = (int64_t)(acc[h] - ((uint64_t)s_wsum[h] << 31));
     }
-  } else {
+  } else if (total == nq) {
     for (int e = tid; e < GC * d; e += kTdThreads) pacc[e] = 0;
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   tcx::fence_before();
   cl.sync();
   // ---- combine: this CTA finalizes output dims [d0, d1)
@@ -601,7 +626,7 @@ __global__ void __launch_bounds__(kTdThreads, 1) attn_dec_tc_kernel(const TdArgs
       orow[(size_t)(qh0 + h) * d + dim] = requantize(v);
     }
   }
-  if (s_fail && tid == 32) {
+  if (s_fail && warp == kTdMmaWarp && lane == 0) {
     atomicExch(&g_tad_err, 1);
     // before the accumulator columns are released: one more bounded wait
     // for this thread's last MMAs
