@@ -409,6 +409,27 @@ def run_kernel_case(args):
         model.close()
         print(f"prefill: {args.ctx} tokens")
         return
+    if args.kernel_case == "batchattn":
+        # the batched decode attention alone at config-5 lengths: a narrow
+        # model with the E4B head geometry (sliding layer, full layer), 64
+        # ragged sequences, three batched steps (a few GB on the device)
+        small = {"text_config": dict(t, hidden_size=256, intermediate_size=512, num_hidden_layers=4,
+                                     num_kv_shared_layers=1, vocab_size=300, vocab_size_per_layer_input=300,
+                                     hidden_size_per_layer_input=32,
+                                     layer_types=["sliding_attention", "full_attention", "sliding_attention",
+                                                  "sliding_attention"])}
+        model = rdet.Model.synthetic(small, SEED, width=16, device=0, max_prefill=args.ctx)
+        lens = [128 + (x % 3969) for x in lcg_ids(args.batch, 1 << 30, SEED + 7)]
+        seqs = [model.new_sequence(n + 16) for n in lens]
+        for i, (sq, n) in enumerate(zip(seqs, lens)):
+            sq.prefill(lcg_ids(n, 300, SEED + 100 + i))
+        toks = rdet.select_batch(model, seqs)
+        for rep in range(3):
+            rdet.decode_batch(model, seqs, toks)
+            toks = rdet.select_batch(model, seqs)
+        model.close()
+        print(f"batched decode attention: {args.batch} sequences, 3 steps")
+        return
     if args.kernel_case == "batch":
         # one greedy step of the 64-sequence ragged batch
         # inside the NVTX range "batch", after two untimed steps, for a launch
@@ -901,7 +922,7 @@ def main():
     ap.add_argument("--config4-tokens", type=int, default=256, help="greedy tokens of the config-4 line (0: skip)")
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched ragged decode line (0: skip)")
     ap.add_argument("--batch-steps", type=int, default=128, help="greedy steps of the batched line (config 5: 128)")
-    ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc", "tcattn", "prefill", "convert", "batch"],
+    ap.add_argument("--kernel-case", choices=["gemv", "attn", "tc", "tcattn", "prefill", "convert", "batch", "batchattn"],
                     help="run a few launches of one kernel at E4B shapes for an ncu capture, then exit")
     ap.add_argument("--time-calls", type=int, default=0,
                     help="with --kernel-case attn: time this many back-to-back calls of each decode-attention entry "

@@ -328,33 +328,35 @@ __global__ void __launch_bounds__(kTdThreads, 1) attn_dec_tc_kernel(const TdArgs
   // ---- scores: the four roles run their own loops, coupled by mbarriers
   if (tid < kTdConv) {
     for (int u = 0; u < nq; ++u) {
-      const int pb = u & 1, s = u % ns;
+      const int pb = u & 1;
       wait(&full[u % kTdSlots], (u / kTdSlots) & 1);
-      if (u >= 2) wait(&mma_done[pb], ((u - 2) >> 1) & 1);
+      // key crow's dims 32*half .. +32: box (crow / 64, half), row crow % 64,
+      // into registers; the slot goes back to the producer at once
+      uint4 w[8];
       {
-        // key crow's dims 32*half .. +32: box (crow / 64, half), row crow % 64
         const unsigned char* raw = ring + (size_t)(u % kTdSlots) * kTdSlot + ((crow >> 6) * 2 + half) * kTdBox;
         const int br = crow & 63;
-        unsigned char* pl = planes + pb * kTdPlanes;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {  // 16-byte output chunk 2*half + c: dims 32*half + 16c ..
-          uint32_t o[4][4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint4 w = *reinterpret_cast<const uint4*>(raw + sw128(br, 4 * c + k));
-            uint32_t q[4];
-            bytes_t4(w.x, w.y, w.z, w.w, q);
-#pragma unroll
-            for (int b = 0; b < 4; ++b) o[b][k] = q[b];
-          }
-#pragma unroll
-          for (int b = 0; b < 4; ++b)
-            *reinterpret_cast<uint4*>(pl + b * kTdPlane + sw64(crow, 2 * half + c)) =
-                make_uint4(o[b][0], o[b][1], o[b][2], o[b][3]);
-        }
+        for (int i = 0; i < 8; ++i) w[i] = *reinterpret_cast<const uint4*>(raw + sw128(br, i));
       }
-      (void)s;
       tcx::mbar_arrive(&empty[u % kTdSlots]);
+      if (u >= 2) wait(&mma_done[pb], ((u - 2) >> 1) & 1);
+      unsigned char* pl = planes + pb * kTdPlanes;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {  // 16-byte output chunk 2*half + c: dims 32*half + 16c ..
+        uint32_t o[4][4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint32_t q[4];
+          bytes_t4(w[4 * c + k].x, w[4 * c + k].y, w[4 * c + k].z, w[4 * c + k].w, q);
+#pragma unroll
+          for (int b = 0; b < 4; ++b) o[b][k] = q[b];
+        }
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          *reinterpret_cast<uint4*>(pl + b * kTdPlane + sw64(crow, 2 * half + c)) =
+              make_uint4(o[b][0], o[b][1], o[b][2], o[b][3]);
+      }
       td_fence_async();
       tcx::mbar_arrive(&planes_full[pb]);
     }
@@ -520,33 +522,36 @@ __global__ void __launch_bounds__(kTdThreads, 1) attn_dec_tc_kernel(const TdArgs
     for (int u = nq; u < total; ++u) {
       const int pb = u & 1;
       wait(&full[u % kTdSlots], (u / kTdSlots) & 1);
-      if (u >= 2) wait(&mma_done[pb], ((u - 2) >> 1) & 1);
+      // dim crow of key rows 32*half .. +32 (box crow / 32, 16-byte chunk
+      // (crow % 32) / 4, word crow % 4) into registers; the slot goes back to
+      // the producer at once
+      uint32_t x[32];
       {
-        // thread (dim crow, keys 32*half ..): dim crow of 32 key rows, in box
-        // crow / 32 at 16-byte chunk (crow % 32) / 4, word crow % 4
         const unsigned char* raw =
             ring + (size_t)(u % kTdSlots) * kTdSlot + (crow >> 5) * kTdBox + (crow & 3) * 4;
         const int ch = (crow & 31) >> 2;
-        unsigned char* pl = planes + pb * kTdPlanes;
-        auto val = [&](int j) { return *reinterpret_cast<const uint32_t*>(raw + sw128(j, ch)); };
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {  // chunk 2*half + c: keys 32*half + 16c ..
-          uint32_t o[4][4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int j = 32 * half + 16 * c + 4 * k;
-            uint32_t q[4];
-            bytes_t4(val(j), val(j + 1), val(j + 2), val(j + 3), q);
-#pragma unroll
-            for (int b = 0; b < 4; ++b) o[b][k] = q[b];
-          }
-#pragma unroll
-          for (int b = 0; b < 4; ++b)
-            *reinterpret_cast<uint4*>(pl + b * kTdPlane + sw64(crow, 2 * half + c)) =
-                make_uint4(o[b][0], o[b][1], o[b][2], o[b][3]);
-        }
+        for (int j = 0; j < 32; ++j) x[j] = *reinterpret_cast<const uint32_t*>(raw + sw128(32 * half + j, ch));
       }
       tcx::mbar_arrive(&empty[u % kTdSlots]);
+      if (u >= 2) wait(&mma_done[pb], ((u - 2) >> 1) & 1);
+      unsigned char* pl = planes + pb * kTdPlanes;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {  // chunk 2*half + c: keys 32*half + 16c ..
+        uint32_t o[4][4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int j = 16 * c + 4 * k;
+          uint32_t q[4];
+          bytes_t4(x[j], x[j + 1], x[j + 2], x[j + 3], q);
+#pragma unroll
+          for (int b = 0; b < 4; ++b) o[b][k] = q[b];
+        }
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          *reinterpret_cast<uint4*>(pl + b * kTdPlane + sw64(crow, 2 * half + c)) =
+              make_uint4(o[b][0], o[b][1], o[b][2], o[b][3]);
+      }
       td_fence_async();
       tcx::mbar_arrive(&planes_full[pb]);
     }
