@@ -1160,7 +1160,12 @@ __global__ void row_norm_kernel(const RowNormArgs a, int S) {
 void launch_row_norm(const RowNormArgs& a, int32_t rows, cudaStream_t s) {
   const size_t smem = (size_t)a.n * 4;
   if (smem > 48 * 1024) cudaFuncSetAttribute(row_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch_k(row_norm_kernel, dim3(rows), dim3(256), smem, s, a, (int)rows);
+  // few rows (a batched decode step): one 16-byte piece per thread, so each
+  // row's dependent norm phases run as short as they can; many rows
+  // (prefill): 256 threads, several blocks per SM
+  int threads = 256;
+  if (rows < 2 * sm_count()) threads = std::max(256, std::min(1024, (a.n / 4 + 31) / 32 * 32));
+  launch_k(row_norm_kernel, dim3(rows), dim3(threads), smem, s, a, (int)rows);
 }
 
 // ---------------------------------------------------------------------------

@@ -1151,7 +1151,9 @@ bool tc_prepare_act(TcAct& a, const int32_t* X, int S, int K, void* mem, cudaStr
   a.tile4 = S > kTcM ? reinterpret_cast<uint32_t*>(a.rowsum + S) : nullptr;
   if (a.tile4 && cudaMemsetAsync(a.tile4, 0, ((size_t)(S + kT2Mrows - 1) / kT2Mrows) * 4, s) != cudaSuccess)
     return false;
-  tc_launch(tc_act_prep_kernel, dim3(S), dim3(256), 0, s, X, S, K, a.planes, a.rowsum, a.tile4);
+  // few long rows (a batched decode step): more threads per row
+  const int threads = (S < 2 * sm_count() && K >= 2048) ? 1024 : 256;
+  tc_launch(tc_act_prep_kernel, dim3(S), dim3(threads), 0, s, X, S, K, a.planes, a.rowsum, a.tile4);
   return encode_planes(a.map, a.planes, 4, S, K, kTcM) && encode_planes(a.map_t, a.planes, 4, S, K, kTsT);
 }
 
