@@ -1207,6 +1207,22 @@ __global__ void rope_table_kernel(const int64_t* inv_freq, int half, int32_t* cs
 void launch_rope_table(const int64_t* inv_freq, int half, int S, int32_t* cs, cudaStream_t s) {
   launch_k(rope_table_kernel, dim3(S), dim3(half < 128 ? (half + 31) / 32 * 32 : 128), 0, s, inv_freq, half, cs);
 }
+// The same factors for batch row r at its own position *pos_rows[r].
+__global__ void rope_rows_kernel(const int64_t* inv_freq, int half, const int32_t* const* pos_rows, int32_t* cs) {
+  pdl_entry();
+  const int r = blockIdx.x;
+  const uint32_t p = (uint32_t)*pos_rows[r];
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    int32_t c, sn;
+    sin_cos_acc(pos_angle(p, inv_freq[i]), &c, &sn);
+    reinterpret_cast<int2*>(cs)[(size_t)r * half + i] = make_int2(c, sn);
+  }
+}
+void launch_rope_rows(const int64_t* inv_freq, int half, int rows, const int32_t* const* pos_rows, int32_t* cs,
+                      cudaStream_t s) {
+  launch_k(rope_rows_kernel, dim3(rows), dim3(half < 128 ? (half + 31) / 32 * 32 : 128), 0, s, inv_freq, half,
+           pos_rows, cs);
+}
 
 __global__ void qkv_post_kernel(const QkvPostArgs a) {
   pdl_entry();

@@ -225,6 +225,9 @@ void launch_qkv_post(const QkvPostArgs& a, cudaStream_t s);
 // and pairs i in [0, half): the RoPE factors of a prompt, once per distinct
 // inverse-frequency table instead of once per (row, head, layer)
 void launch_rope_table(const int64_t* inv_freq, int half, int S, int32_t* cs, cudaStream_t s);
+// The same layout for batch rows at their own positions: row r at *pos_rows[r].
+void launch_rope_rows(const int64_t* inv_freq, int half, int rows, const int32_t* const* pos_rows, int32_t* cs,
+                      cudaStream_t s);
 
 // ---- attention -----------------------------------------------------------------
 struct AttnScratch {

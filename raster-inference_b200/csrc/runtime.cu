@@ -1537,6 +1537,20 @@ static void require_logits(const Seq& q) {
           "(rdet_tp_shard_logits): select its token with rdet_select_batch");
 }
 
+// RoPE factors of every batch row at its own position, once per distinct
+// frequency table, into the prefill's table buffer (rows <= max_prefill);
+// qkv_post then reads them instead of evaluating sin/cos in every head.
+static void batch_rope_tables(Ctx& c, int B) {
+  for (size_t t = 0; t < c.rope_list.size(); ++t)
+    launch_rope_rows(c.rope_list[t].first, c.rope_list[t].second, B, c.bw.pos,
+                     c.rope_cs + t * (size_t)c.max_prefill * c.rope_half_max * 2, c.stream);
+}
+static const int32_t* rope_table_of(const Ctx& c, const int64_t* inv_freq) {
+  for (size_t t = 0; t < c.rope_list.size(); ++t)
+    if (c.rope_list[t].first == inv_freq) return c.rope_cs + t * (size_t)c.max_prefill * c.rope_half_max * 2;
+  return nullptr;
+}
+
 static void check_decode_ready(Ctx& c, Seq& q) {
   REQUIRE(q.prefilled, RDET_E_STATE, "decode requires a prefilled sequence");
   REQUIRE(q.pos < q.cap, RDET_E_RANGE, "sequence KV cache is full");
@@ -1840,6 +1854,7 @@ static const int32_t* decode_batch_layer(Ctx& c, int B, int maxcap, int l, int32
   qa.S = B; qa.Hq = m.Hq; qa.Hkv = lc.kv_heads; qa.d = d; qa.rotary = lc.rotary; qa.inv_freq = L.inv_freq;
   qa.q_norm = L.q_norm; qa.k_norm = L.k_norm; qa.eps = c.eps; qa.q_out = w.qo;
   qa.pos_rows = bw.pos; qa.cap_rows = bw.caps;
+  qa.rope_cs = rope_table_of(c, L.inv_freq);
   // one tensor-core GEMM for q, k and v when their planes share a buffer
   // (rows [q | k | v] of w.hbuf, which the MLP overwrites later)
   const int nqkv = L.tqkv.nrows;
@@ -2036,6 +2051,7 @@ static const int32_t* decode_batch_layer_tp(Ctx& c, int B, int maxcap, int l, in
   qa.S = B; qa.Hq = Hql; qa.Hkv = lc.kv_heads; qa.d = d; qa.rotary = lc.rotary; qa.inv_freq = L.inv_freq;
   qa.q_in = w.q; qa.q_norm = L.q_norm; qa.k_norm = L.k_norm; qa.eps = c.eps; qa.q_out = w.qo;
   qa.pos_rows = bw.pos; qa.cap_rows = bw.caps;
+  qa.rope_cs = rope_table_of(c, L.inv_freq);
   if (lc.donor < 0) {
     prefill_linear(c, w.nrm, B, L.k, L.tk, w.kraw, kEpiPlain, nullptr, &nrm_planes);
     const int32_t* vsrc = w.kraw;  // k_eq_v: V is the raw K projection
@@ -2186,6 +2202,7 @@ static void decode_batch_tp(Ctx& c, Seq* const* seqs, const uint32_t* tokens, in
   PrefillWs& w = c.pw;
   cudaStream_t s = c.stream;
   batch_tables(c, seqs, B);
+  batch_rope_tables(c, B);
   tp_buffers(c, B);
   auto& bw = c.bw;
   int maxcap = 0;
@@ -2273,6 +2290,7 @@ static void decode_batch(Ctx& c, Seq* const* seqs, const uint32_t* tokens, int B
   PrefillWs& w = c.pw;
   cudaStream_t s = c.stream;
   batch_tables(c, seqs, B);
+  batch_rope_tables(c, B);
   auto& bw = c.bw;
   int maxcap = 0;
   for (int i = 0; i < B; ++i) maxcap = std::max(maxcap, seqs[i]->cap);
