@@ -674,13 +674,13 @@ cudaError_t td_launch(const AttnDecodeArgs& a, int CL, int rmax, cudaStream_t s)
   return cudaLaunchKernelEx(&cfg, attn_dec_tc_kernel<GC>, ta);
 }
 
+// RDET_TC_DECODE_ATTN=0 selects the CUDA-core kernel (read once per process)
 bool td_enabled() {
-  static int v = -1;
-  if (v < 0) {
+  static const bool on = [] {
     const char* e = std::getenv("RDET_TC_DECODE_ATTN");
-    v = (e && e[0] == '0') ? 0 : 1;
-  }
-  return v == 1;
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 }  // namespace
